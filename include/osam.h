@@ -1,0 +1,114 @@
+/* osam.h — C ABI of the ObjectSAM B200 convolution hot path.
+ *
+ * The reference hands every YOLOv8s-seg convolution to cuDNN through the C++ class ConvOp
+ * (reference src/conv.h:16-53, src/conv.cpp) and applies BatchNorm+SiLU, bias and SPPF pooling in
+ * separate passes (src/bn.cu, src/misc.cu).  This header is the plain-C boundary that replaces those
+ * calls: raw device pointers and sizes, an explicit CUDA stream, int status codes, no C++ or torch
+ * types.  A ConvOp-compatible C++ shim and the Python host layer sit on top of it.
+ *
+ * Conventions (same as the reference, src/conv.h:16-31, src/bn.cuh:9-21):
+ *   - activations are NHWC packed fp16 (__half), weights are KRSC fp16 (K, R, S, C);
+ *   - the transposed conv (ConvTranspose2d k=s=2) takes weights as (C_in, R, S, C_out), the layout
+ *     the reference keeps for it (src/model.h:24 "layout 2");
+ *   - accumulation is fp32;
+ *   - every pointer handed to a kernel is 16-byte aligned and every channel count/offset used by an
+ *     epilogue destination is a multiple of 8, except single-channel outputs (K = 1).
+ *   - No entry point allocates device memory; plan creation may (tensor-map scratch is host side).
+ * All functions return OSAM_OK (0) or a positive error code; osam_last_error() describes the last one.
+ */
+#ifndef OSAM_H_
+#define OSAM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* osam_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum {
+  OSAM_OK = 0,
+  OSAM_ERR_INVALID = 1,     /* bad argument / unsupported geometry */
+  OSAM_ERR_UNSUPPORTED = 2, /* valid for the reference, not implemented by this build */
+  OSAM_ERR_CUDA = 3,        /* CUDA runtime/driver error */
+  OSAM_ERR_TIMEOUT = 4,     /* a device-side wait ran out of its budget (kernel returned early) */
+  OSAM_ERR_NOMEM = 5
+};
+
+/* Conv geometry.  Replaces ConvGeom (reference src/conv.h:8-14); P = (H+2pad-R)/stride+1. */
+typedef struct osam_conv_geom {
+  int N, H, W, C; /* input */
+  int K, R, S;    /* output channels, kernel */
+  int stride, pad;
+} osam_conv_geom;
+
+/* One output destination of a fused epilogue.  Replaces Dest (reference src/bn.cuh:10-17):
+ * output channels [c0, c1) go to channels [choff, choff + c1 - c0) of an NHWC buffer with ctot
+ * channels; up = 2 writes each pixel to its 2×2 nearest-neighbour block of a 2P×2Q buffer. */
+typedef struct osam_dest {
+  void* p;
+  int ctot, choff, c0, c1, up;
+} osam_dest;
+
+#define OSAM_MAX_DEST 4
+
+enum {
+  OSAM_EPI_STORE = 0,  /* y = conv (+ beta·y): the plain ConvOp::fwd contract */
+  OSAM_EPI_BN_ACT = 1, /* a = act(scale·z + shift) (+ res) → dests: conv + bn_forward_apply (src/bn.cu:204-238) */
+  OSAM_EPI_BIAS = 2    /* y = z + bias → dests: conv + add_bias (src/misc.cu:116-134, src/model.cpp:403-407) */
+};
+
+/* Fused epilogue of a forward conv (the folded-BN / bias / residual / DestList store). */
+typedef struct osam_epilogue {
+  int kind;             /* OSAM_EPI_* */
+  const float* scale;   /* [K] BN_ACT: γ/√(var+eps) */
+  const float* shift;   /* [K] BN_ACT: β − μ·scale   (bn_eval_scale, src/bn.cu:277-284) */
+  const float* bias;    /* [K] BIAS */
+  const void* res;      /* BN_ACT: optional residual [N,P,Q,K] fp16 added after the activation */
+  int act;              /* BN_ACT: 1 = SiLU */
+  int round_z;          /* 1: round the fp32 accumulator to fp16 before the epilogue math, as the
+                           reference does by storing z in fp16 (src/model.cpp:388-400) */
+  int n_dest;
+  osam_dest dest[OSAM_MAX_DEST];
+} osam_epilogue;
+
+typedef struct osam_conv_plan osam_conv_plan;
+
+/* Plan for one conv geometry.  Replaces ConvOp::init + tune (src/conv.h:21-27): tile shapes are a
+ * static function of the geometry, so there is nothing to time.  transposed = 1 means
+ * ConvTranspose2d(C→K, kernel R=S=stride, pad 0) as in ConvOp::init(…, transposed=true). */
+int osam_conv_plan_create(const osam_conv_geom* g, int transposed, osam_conv_plan** out);
+int osam_conv_plan_destroy(osam_conv_plan* plan);
+/* Workspace bytes the caller must pass to fwd/dgrad/wgrad (ConvOp::tune's return value). */
+size_t osam_conv_workspace_size(const osam_conv_plan* plan);
+/* Output elements N·P·Q·K (ConvOp::out_elems, src/conv.h:33). */
+int64_t osam_conv_out_elems(const osam_conv_plan* plan);
+
+/* y = conv(x, w) (+ beta·y).  Replaces ConvOp::fwd (src/conv.h:29, src/conv.cpp:335-344). */
+int osam_conv_fwd(const osam_conv_plan* plan, const void* x, const void* w, void* y, float beta, void* ws,
+                  size_t ws_bytes, osam_stream_t stream);
+
+/* Conv fused with its epilogue (BN fold + SiLU + residual + multi-destination store, or bias).
+ * Replaces ConvOp::fwd followed by bn_eval_scale/bn_forward_apply (src/model.cpp:388-400) or by
+ * add_bias (src/model.cpp:405-406). */
+int osam_conv_fwd_fused(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep,
+                        void* ws, size_t ws_bytes, osam_stream_t stream);
+
+/* SPPF pooling: with cv1's output in channels [0,c) of cat (N×H×W×4c), writes the three chained
+ * 5×5/s1/p2 max-pools into slices 1..3.  Replaces sppf_pool_fwd (src/misc.cuh:6, src/misc.cu:149-153). */
+int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);
+
+/* Device error word shared by all kernels of this library on the current device: returns the first
+ * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises. */
+int osam_device_error(void);
+
+/* Human-readable description of the last error returned on this host thread. */
+const char* osam_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OSAM_H_ */

@@ -1,0 +1,400 @@
+// C ABI (include/osam.h): conv plans, TMA tensor-map encoding, argument validation and dispatch.
+// Replaces the cuDNN descriptor/plan machinery of ConvOp (reference src/conv.cpp:64-366): the tile shape
+// of a layer is a static function of its geometry, so "tuning" is a table lookup.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "conv_internal.h"
+
+namespace osam {
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_last_error[512] = "";
+
+void set_last_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(OSAM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------------ device error word
+static std::mutex g_err_mu;
+static int* g_err_word[64] = {};
+
+int* device_error_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (!g_err_word[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
+    g_err_word[dev] = p;
+  }
+  return g_err_word[dev];
+}
+
+// ------------------------------------------------------------------ tensor maps
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled_t encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+  });
+  return fn;
+}
+
+// fp16 tensor map: dims[0] innermost, strides in bytes for dims 1..rank-1.
+static int make_map(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_b,
+                    const uint32_t* box, int row_bytes) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (!fn) return fail(OSAM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) & 15) return fail(OSAM_ERR_INVALID, "operand not 16-byte aligned");
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; i++) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) {
+      gs[i] = strides_b[i];
+      if (strides_b[i] & 15) return fail(OSAM_ERR_INVALID, "tensor stride %llu not a multiple of 16 B",
+                                         (unsigned long long)strides_b[i]);
+    }
+  }
+  const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), gd, gs, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OSAM_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return OSAM_OK;
+}
+
+// ------------------------------------------------------------------ planning
+static int choose_bn(int gemm_n) {
+  static const int opts[] = {16, 32, 64, 128, 224, 256};
+  if (gemm_n <= 256)
+    for (int o : opts)
+      if (o >= gemm_n) return o;
+  if (gemm_n % 256 == 0) return 256;
+  return 128;
+}
+
+static long long cdivll(long long a, long long b) { return (a + b - 1) / b; }
+
+// 128-pixel spatial tile (tn images × th rows × tw cols) with the least padding; ties → wider rows.
+static void choose_tile(int N, int P, int Q, int* tn, int* th, int* tw) {
+  long long best = -1;
+  for (int lw = 7; lw >= 0; lw--)
+    for (int lh = 7 - lw; lh >= 0; lh--) {
+      const int w = 1 << lw, h = 1 << lh, n = 128 / (w * h);
+      const long long cost = cdivll(Q, w) * cdivll(P, h) * cdivll(N, n);
+      if (best < 0 || cost < best) {
+        best = cost;
+        *tn = n;
+        *th = h;
+        *tw = w;
+      }
+    }
+}
+
+static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p) {
+  std::memset(p, 0, sizeof(*p));
+  p->g = *g;
+  p->transposed = transposed;
+  if (g->N < 1 || g->H < 1 || g->W < 1 || g->C < 1 || g->K < 1 || g->R < 1 || g->S < 1 || g->stride < 1 || g->pad < 0)
+    return fail(OSAM_ERR_INVALID, "invalid conv geometry");
+  if (transposed) {
+    if (g->R != 2 || g->S != 2 || g->stride != 2 || g->pad != 0)
+      return fail(OSAM_ERR_UNSUPPORTED, "transposed conv: only kernel 2, stride 2, pad 0");
+    if (g->C % 32 || g->K % 8) return fail(OSAM_ERR_UNSUPPORTED, "transposed conv: C %% 32, K %% 8 required");
+    p->P = g->H;  // GEMM grid = input grid; the epilogue scatters to 2H × 2W
+    p->Q = g->W;
+    p->mode = A_GEMM;
+    p->BK = g->C % 64 == 0 ? 64 : 32;
+    p->gemm_n = 4 * g->K;
+    p->M = (long long)g->N * g->H * g->W;
+    p->nkc = g->C / p->BK;
+    p->nk = p->nkc;
+  } else {
+    p->P = (g->H + 2 * g->pad - g->R) / g->stride + 1;
+    p->Q = (g->W + 2 * g->pad - g->S) / g->stride + 1;
+    if (p->P < 1 || p->Q < 1) return fail(OSAM_ERR_INVALID, "empty conv output");
+    p->M = (long long)g->N * p->P * p->Q;
+    p->gemm_n = g->K;
+    if (g->R * g->S * g->C <= 32 && g->C % 32 != 0) {
+      p->mode = A_STEM;
+      p->BK = 32;
+      p->nkc = 1;
+      p->nk = 1;
+      if (g->K > 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C conv: K <= 64 required");
+    } else {
+      if (g->C % 32) return fail(OSAM_ERR_UNSUPPORTED, "conv input channels must be a multiple of 32 (C=%d)", g->C);
+      p->BK = g->C % 64 == 0 ? 64 : 32;
+      p->nkc = g->C / p->BK;
+      p->nk = g->R * g->S * p->nkc;
+      if (g->R == 1 && g->S == 1 && g->stride == 1 && g->pad == 0)
+        p->mode = A_GEMM;
+      else if (g->stride == 1)
+        p->mode = A_S1;
+      else if (g->stride == 2 && g->H % 2 == 0 && g->W % 2 == 0)
+        p->mode = A_S2;
+      else
+        return fail(OSAM_ERR_UNSUPPORTED, "conv stride %d with H=%d W=%d", g->stride, g->H, g->W);
+    }
+  }
+  p->BN = choose_bn(p->gemm_n);
+  if (p->mode == A_STEM && p->BN > 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C conv: K <= 64 required");
+  p->ntn = (int)cdivll(p->gemm_n, p->BN);
+  if (p->mode == A_S1 || p->mode == A_S2) {
+    choose_tile(g->N, p->P, p->Q, &p->tn, &p->th, &p->tw);
+    p->tiles_q = (int)cdivll(p->Q, p->tw);
+    p->tiles_p = (int)cdivll(p->P, p->th);
+    p->tiles_m = (int)(p->tiles_q * (long long)p->tiles_p * cdivll(g->N, p->tn));
+  } else {
+    p->tiles_m = (int)cdivll(p->M, 128);
+  }
+  if ((long long)p->tiles_m * p->ntn > 0x7fffffffLL) return fail(OSAM_ERR_UNSUPPORTED, "conv too large");
+  return OSAM_OK;
+}
+
+static int fill_dest(const osam_dest& s, int kout, DestDev* d, int transposed) {
+  if (!s.p) return fail(OSAM_ERR_INVALID, "destination pointer is NULL");
+  if (s.c0 < 0 || s.c1 <= s.c0 || s.c1 > kout) return fail(OSAM_ERR_INVALID, "destination channels [%d,%d)", s.c0, s.c1);
+  if (s.choff < 0 || s.choff + s.c1 - s.c0 > s.ctot) return fail(OSAM_ERR_INVALID, "destination channel offset");
+  if (s.up != 1 && s.up != 2) return fail(OSAM_ERR_INVALID, "destination up must be 1 or 2");
+  if (transposed && s.up != 1) return fail(OSAM_ERR_INVALID, "transposed conv: up must be 1");
+  d->p = static_cast<__half*>(s.p);
+  d->ctot = s.ctot;
+  d->choff = s.choff;
+  d->c0 = s.c0;
+  d->c1 = s.c1;
+  d->up = s.up;
+  d->vec = (s.ctot % 8 == 0 && s.choff % 8 == 0 && s.c0 % 8 == 0 && s.c1 % 8 == 0 &&
+            (reinterpret_cast<uintptr_t>(s.p) & 15) == 0);
+  return OSAM_OK;
+}
+
+int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
+                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready) {
+  if (!p || !x || !w) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
+  const osam_conv_geom& g = p->g;
+  *L = ConvLaunch{};
+  L->BK = p->BK;
+  L->BN = p->BN;
+  L->mode = p->mode;
+  L->grid = p->tiles_m * p->ntn;
+  ConvDev& d = L->d;
+  d.N = g.N; d.H = g.H; d.W = g.W; d.C = g.C; d.K = g.K;
+  d.P = p->P; d.Q = p->Q; d.R = g.R; d.S = g.S; d.stride = g.stride; d.pad = g.pad;
+  d.gemm_n = p->gemm_n;
+  d.tn = p->tn; d.th = p->th; d.tw = p->tw; d.tiles_q = p->tiles_q; d.tiles_p = p->tiles_p;
+  d.M = p->M;
+  d.ntn = p->ntn;
+  d.nkc = p->nkc;
+  d.nk = p->nk;
+  d.err = device_error_word();
+  if (!d.err) return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
+
+  // ---- epilogue
+  EpiDev& e = d.ep;
+  e.shuffle = p->transposed;
+  e.kout = g.K;
+  if (!ep) {
+    if (!y) return fail(OSAM_ERR_INVALID, "NULL output");
+    e.kind = OSAM_EPI_STORE;
+    e.beta = beta;
+    e.ndest = 1;
+    osam_dest o{y, g.K, 0, 0, g.K, 1};
+    int rc = fill_dest(o, g.K, &e.dest[0], p->transposed);
+    if (rc) return rc;
+  } else {
+    if (ep->kind < 0 || ep->kind > 2) return fail(OSAM_ERR_INVALID, "epilogue kind %d", ep->kind);
+    if (ep->n_dest < 1 || ep->n_dest > OSAM_MAX_DEST) return fail(OSAM_ERR_INVALID, "n_dest %d", ep->n_dest);
+    if (ep->kind == OSAM_EPI_BN_ACT && (!ep->scale || !ep->shift)) return fail(OSAM_ERR_INVALID, "BN epilogue needs scale/shift");
+    if (ep->kind == OSAM_EPI_BIAS && !ep->bias) return fail(OSAM_ERR_INVALID, "bias epilogue needs bias");
+    if (ep->res && p->transposed) return fail(OSAM_ERR_INVALID, "transposed conv: no residual");
+    if (ep->res && (reinterpret_cast<uintptr_t>(ep->res) & 15)) return fail(OSAM_ERR_INVALID, "residual not 16-byte aligned");
+    e.kind = ep->kind;
+    e.scale = ep->scale;
+    e.shift = ep->shift;
+    e.bias = ep->bias;
+    e.res = static_cast<const __half*>(ep->res);
+    e.act = ep->act;
+    e.round_z = ep->round_z;
+    e.beta = 0.f;
+    e.ndest = ep->n_dest;
+    for (int i = 0; i < ep->n_dest; i++) {
+      int rc = fill_dest(ep->dest[i], g.K, &e.dest[i], p->transposed);
+      if (rc) return rc;
+    }
+  }
+
+  // ---- operands
+  const int row_bytes = p->BK * 2;
+  if (p->mode == A_STEM) {
+    L->x = static_cast<const __half*>(x);
+    L->w = static_cast<const __half*>(w);
+    return OSAM_OK;
+  }
+  int rc;
+  if (p->mode == A_GEMM) {
+    const uint64_t dims[2] = {(uint64_t)g.C, (uint64_t)p->M};
+    const uint64_t str[1] = {(uint64_t)g.C * 2};
+    const uint32_t box[2] = {(uint32_t)p->BK, 128};
+    rc = make_map(&L->ta, x, 2, dims, str, box, row_bytes);
+  } else if (p->mode == A_S1) {
+    const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+    const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
+    const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)p->tw, (uint32_t)p->th, (uint32_t)p->tn};
+    rc = make_map(&L->ta, x, 4, dims, str, box, row_bytes);
+  } else {
+    const uint64_t dims[5] = {(uint64_t)2 * g.C, (uint64_t)g.W / 2, 2, (uint64_t)g.H / 2, (uint64_t)g.N};
+    const uint64_t str[4] = {(uint64_t)4 * g.C, (uint64_t)g.W * g.C * 2, (uint64_t)2 * g.W * g.C * 2,
+                             (uint64_t)g.H * g.W * g.C * 2};
+    const uint32_t box[5] = {(uint32_t)p->BK, (uint32_t)p->tw, 1, (uint32_t)p->th, (uint32_t)p->tn};
+    rc = make_map(&L->ta, x, 5, dims, str, box, row_bytes);
+  }
+  if (rc) return rc;
+
+  const void* wb = w;
+  if (p->transposed && !w_gemm_ready) {
+    const size_t need = (size_t)g.C * 4 * g.K * 2;
+    if (!ws || ws_bytes < need) return fail(OSAM_ERR_INVALID, "transposed conv needs %zu workspace bytes", need);
+    L->wt_src = static_cast<const __half*>(w);
+    L->wt_dst = static_cast<__half*>(ws);
+    wb = ws;
+  }
+  if (p->transposed) {
+    const uint64_t dims[2] = {(uint64_t)g.C, (uint64_t)4 * g.K};
+    const uint64_t str[1] = {(uint64_t)g.C * 2};
+    const uint32_t box[2] = {(uint32_t)p->BK, (uint32_t)p->BN};
+    rc = make_map(&L->tb, wb, 2, dims, str, box, row_bytes);
+  } else {
+    const uint64_t rsc = (uint64_t)g.R * g.S * g.C;
+    const uint64_t dims[2] = {rsc, (uint64_t)g.K};
+    const uint64_t str[1] = {rsc * 2};
+    const uint32_t box[2] = {(uint32_t)p->BK, (uint32_t)p->BN};
+    rc = make_map(&L->tb, wb, 2, dims, str, box, row_bytes);
+  }
+  return rc;
+}
+
+cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st) {
+  if (L.mode == A_STEM) return launch_conv_stem(L.x, L.w, L.d, L.BN, st);
+  if (L.wt_src) {
+    cudaError_t e = launch_convt_weight_relayout(L.wt_src, L.wt_dst, L.d.C, 4, L.d.K, st);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_conv_fprop(L, st);
+}
+
+}  // namespace osam
+
+using namespace osam;
+
+extern "C" {
+
+int osam_conv_plan_create(const osam_conv_geom* g, int transposed, osam_conv_plan** out) {
+  if (!g || !out) return fail(OSAM_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  osam_conv_plan* p = new (std::nothrow) osam_conv_plan;
+  if (!p) return fail(OSAM_ERR_NOMEM, "out of host memory");
+  int rc = plan_init(g, transposed, p);
+  if (rc) {
+    delete p;
+    return rc;
+  }
+  // Allocate the device error word now (plan time), never inside a launch that may be captured.
+  if (!device_error_word()) {
+    delete p;
+    return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
+  }
+  *out = p;
+  return OSAM_OK;
+}
+
+int osam_conv_plan_destroy(osam_conv_plan* p) {
+  delete p;
+  return OSAM_OK;
+}
+
+size_t osam_conv_workspace_size(const osam_conv_plan* p) {
+  if (!p || !p->transposed) return 0;
+  return ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
+}
+
+int64_t osam_conv_out_elems(const osam_conv_plan* p) {
+  if (!p) return 0;
+  if (p->transposed) return (int64_t)p->g.N * 2 * p->g.H * 2 * p->g.W * p->g.K;
+  return (int64_t)p->M * p->g.K;
+}
+
+int osam_conv_fwd(const osam_conv_plan* p, const void* x, const void* w, void* y, float beta, void* ws,
+                  size_t ws_bytes, osam_stream_t stream) {
+  ConvLaunch L;
+  int rc = conv_prepare(p, x, w, nullptr, beta, y, ws, ws_bytes, &L);
+  if (rc) return rc;
+  cudaError_t e = conv_launch(L, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_fwd launch");
+}
+
+int osam_conv_fwd_fused(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, void* ws,
+                        size_t ws_bytes, osam_stream_t stream) {
+  if (!ep) return fail(OSAM_ERR_INVALID, "NULL epilogue");
+  ConvLaunch L;
+  int rc = conv_prepare(p, x, w, ep, 0.f, nullptr, ws, ws_bytes, &L);
+  if (rc) return rc;
+  cudaError_t e = conv_launch(L, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_fwd_fused launch");
+}
+
+int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream) {
+  if (!cat || N < 1 || H < 1 || W < 1 || c < 32 || c % 32) return fail(OSAM_ERR_INVALID, "sppf arguments");
+  if (reinterpret_cast<uintptr_t>(cat) & 15) return fail(OSAM_ERR_INVALID, "sppf buffer not 16-byte aligned");
+  if ((size_t)2 * H * W * 32 * 2 > 200 * 1024) return fail(OSAM_ERR_UNSUPPORTED, "sppf map too large (%dx%d)", H, W);
+  cudaError_t e = launch_sppf(static_cast<__half*>(cat), N, H, W, c, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_sppf_fwd launch");
+}
+
+int osam_device_error(void) {
+  int* w = device_error_word();
+  if (!w) return fail(OSAM_ERR_CUDA, "no device error word");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "osam_device_error sync");
+  int v = 0;
+  e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "osam_device_error read");
+  if (v) {
+    cudaMemset(w, 0, sizeof(int));
+    set_last_error("device kernel reported error %d", v);
+  }
+  return v;
+}
+
+const char* osam_last_error(void) { return g_last_error; }
+
+}  // extern "C"

@@ -1,0 +1,250 @@
+// Forward convolution as an implicit GEMM on the sm_100a tensor cores.
+//
+//   GEMM M = output pixels (a 128-pixel tile: tn images × th rows × tw columns, or 128 consecutive rows
+//            of the [N·H·W, C] matrix for 1×1 convs), GEMM N = output channels (BN per CTA),
+//   GEMM K = taps × input channels, walked as (tap, BK-channel chunk) steps.
+//
+// One CTA = one output tile, 6 warps:
+//   warp 0      TMA producer: per K-step one A box (the input window of this tap, zero-filled halo)
+//               and one B box (the KRSC weight rows of this tap/chunk) into a STAGES-deep ring;
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instruction),
+//               fp32 accumulator in TMEM; tcgen05.commit frees ring slots and signals the epilogue;
+//   warps 2..5  epilogue: tcgen05.ld of the 128×BN accumulator, folded BN + SiLU (+ residual) or bias,
+//               fp16 conversion and the multi-destination store (channel slices, 2× nearest upsample)
+//               that replaces the reference's separate bn_forward_apply / add_bias passes.
+// The operand tiles are K-major with the TMA swizzle (128 B rows when BK = 64, 64 B rows when BK = 32)
+// that the UMMA shared-memory descriptor expects.  No multicast is used anywhere.
+#include "epilogue.cuh"
+
+namespace osam {
+
+template <int BK, int BN>
+struct FpropCfg {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // ≤ 128 output channels: two CTAs per SM (one's epilogue overlaps the other's main loop);
+  // wider tiles: one CTA per SM with a deeper ring.
+  static constexpr int RING_BUDGET = BN <= 128 ? 96 * 1024 : 190 * 1024;
+  static constexpr int STAGES_RAW = RING_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+  static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int ROW_BYTES = BK * 2;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 3 * BN * 4;
+};
+
+template <int BK, int BN, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const ConvDev d) {
+  using Cfg = FpropCfg<BK, BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = base + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accb = empty + STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accb + 1);
+  float* s_sc = reinterpret_cast<float*>(base + STAGES * Cfg::STAGE_BYTES + 256);
+  float* s_sh = s_sc + BN;
+  float* s_bi = s_sh + BN;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = blockIdx.x % d.ntn;
+  const int mt = blockIdx.x / d.ntn;
+  const int n0 = nt * BN;
+
+  long long m0 = 0;
+  int q0 = 0, p0 = 0, b0 = 0;
+  if (MODE == A_GEMM) {
+    m0 = (long long)mt * 128;
+  } else {
+    const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
+    const int tp = rest % d.tiles_p, tb_ = rest / d.tiles_p;
+    q0 = tq * d.tw;
+    p0 = tp * d.th;
+    b0 = tb_ * d.tn;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(accb, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&ta);
+    tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp >= 2) load_epilogue_consts(d.ep, d.gemm_n, n0, BN, threadIdx.x - 64, 128, s_sc, s_sh, s_bi);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < d.nk; kb++) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !mbar_wait(empty + s, ((kb / STAGES) - 1) & 1, d.err)) break;
+        mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
+        const int tap = kb / d.nkc, cc = (kb - tap * d.nkc) * BK;
+        uint8_t* a = sA + s * Cfg::A_BYTES;
+        uint8_t* b = sB + s * Cfg::B_BYTES;
+        if (MODE == A_GEMM) {
+          tma_load_2d(a, &ta, full + s, cc, (int)m0);
+        } else {
+          const int r = tap / d.S, c = tap - r * d.S;
+          if (MODE == A_S1) {
+            tma_load_4d(a, &ta, full + s, cc, q0 + c - d.pad, p0 + r - d.pad, b0);
+          } else {
+            const int dr = r - d.pad, dc = c - d.pad;
+            tma_load_5d(a, &ta, full + s, (dc & 1) * d.C + cc, q0 + (dc >> 1), dr & 1, p0 + (dr >> 1), b0);
+          }
+        }
+        tma_load_2d(b, &tb, full + s, tap * d.C + cc, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      bool ok = true;
+      for (int kb = 0; kb < d.nk; kb++) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(full + s, (kb / STAGES) & 1, d.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(sA + s * Cfg::A_BYTES), b = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++)
+          umma_f16(tmem, smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES), smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES),
+                   idesc, (kb | k) != 0);
+        umma_commit(empty + s);
+      }
+      if (ok) umma_commit(accb);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const EpiDev& e = d.ep;
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    bool valid;
+    long long pix;
+    int n, p, q;
+    if (MODE == A_GEMM) {
+      const long long m = m0 + row;
+      valid = m < d.M;
+      pix = m;
+      q = (int)(m % d.Q);
+      const long long t = m / d.Q;
+      p = (int)(t % d.P);
+      n = (int)(t / d.P);
+    } else {
+      const int thw = d.th * d.tw;
+      const int ni = row / thw, rr = row - ni * thw, i = rr / d.tw, j = rr - i * d.tw;
+      n = b0 + ni;
+      p = p0 + i;
+      q = q0 + j;
+      valid = n < d.N && p < d.P && q < d.Q;
+      pix = ((long long)n * d.P + p) * d.Q + q;
+    }
+    const bool ok = mbar_wait(accb, 0, d.err);
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int jc = 0; jc < BN / 16; jc++) {
+        __syncwarp();
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + jc * 16, v);
+        const int col0 = n0 + jc * 16;
+        if (!valid || col0 >= d.gemm_n) continue;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int col = col0 + h * 8;
+          if (col >= d.gemm_n) break;
+          const int cnt = d.gemm_n - col < 8 ? d.gemm_n - col : 8;
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) y[i] = v[h * 8 + i];
+          epilogue8(e, d.K, d.P, d.Q, y, cnt, col, jc * 16 + h * 8, s_sc, s_sh, s_bi, pix, n, p, q);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BK, int BN, int MODE>
+static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st) {
+  using Cfg = FpropCfg<BK, BN>;
+  static bool attr_set = false;  // per process; the attribute applies to every device
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv_fprop<BK, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  k_conv_fprop<BK, BN, MODE><<<L.grid, 192, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
+  return cudaGetLastError();
+}
+
+template <int BK, int BN>
+static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st) {
+  switch (L.mode) {
+    case A_GEMM: return launch_one<BK, BN, A_GEMM>(L, st);
+    case A_S1: return launch_one<BK, BN, A_S1>(L, st);
+    case A_S2: return launch_one<BK, BN, A_S2>(L, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int BK>
+static cudaError_t launch_bn(const ConvLaunch& L, cudaStream_t st) {
+  switch (L.BN) {
+    case 16: return launch_mode<BK, 16>(L, st);
+    case 32: return launch_mode<BK, 32>(L, st);
+    case 64: return launch_mode<BK, 64>(L, st);
+    case 128: return launch_mode<BK, 128>(L, st);
+    case 224: return launch_mode<BK, 224>(L, st);
+    case 256: return launch_mode<BK, 256>(L, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st) {
+  if (L.BK == 64) return launch_bn<64>(L, st);
+  if (L.BK == 32) return launch_bn<32>(L, st);
+  return cudaErrorInvalidValue;
+}
+
+// (C, RS, K) → (RS·K, C): transposed-conv weights into the K-major B operand of its GEMM.
+__global__ void k_convt_weight_relayout(const __half* __restrict__ src, __half* __restrict__ dst, int C, int RS,
+                                        int K) {
+  const long long n = (long long)C * RS * K;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const long long j = i / C;  // (rs, k) row of dst
+    dst[i] = src[(long long)c * RS * K + j];
+  }
+}
+
+cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st) {
+  const long long n = (long long)C * RS * K;
+  int grid = (int)((n + 255) / 256);
+  if (grid > 4096) grid = 4096;
+  k_convt_weight_relayout<<<grid, 256, 0, st>>>(src, dst, C, RS, K);
+  return cudaGetLastError();
+}
+
+}  // namespace osam

@@ -1,0 +1,91 @@
+// Internal (C++) interface between the C ABI / model runner and the conv kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/osam.h"
+
+namespace osam {
+
+// How the A (activation) tile of one K-step is fetched by TMA.
+enum AMode : int {
+  A_GEMM = 0,  // 1×1/s1/p0 conv or transposed conv: A is the [N·H·W, C] matrix itself (2-D map)
+  A_S1 = 1,    // stride-1 R×S conv: 4-D map (C, W, H, N); one shifted box per tap, halo = TMA zero fill
+  A_S2 = 2,    // stride-2 conv: 5-D map (2C, W/2, 2, H/2, N) — the parity-split view of NHWC — so a
+               // stride-2 gather becomes a dense box per tap
+  A_STEM = 3   // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
+};
+
+struct DestDev {
+  __half* p;
+  int ctot, choff, c0, c1, up;
+  int vec;  // 16-byte vector stores allowed
+};
+
+struct EpiDev {
+  int kind;  // OSAM_EPI_*
+  const float* scale;
+  const float* shift;
+  const float* bias;
+  const __half* res;
+  int act, round_z;
+  float beta;  // OSAM_EPI_STORE: y = conv + beta·y
+  int ndest;
+  DestDev dest[OSAM_MAX_DEST];
+  int shuffle;  // transposed conv: GEMM column j = (dy·2+dx)·kout + k → pixel (2p+dy, 2q+dx)
+  int kout;     // channels per (dy,dx) block for shuffle
+};
+
+struct ConvDev {
+  int N, H, W, C, K, P, Q, R, S, stride, pad;
+  int gemm_n;                 // GEMM N (= K, or 4·K for the transposed conv)
+  int tn, th, tw;             // spatial tile (tn images × th rows × tw cols = 128 pixels)
+  int tiles_q, tiles_p;       // spatial tiles along Q and P
+  long long M;                // N·P·Q (GEMM M) — for the transposed conv N·H·W
+  int ntn;                    // tiles along GEMM N
+  int nkc;                    // channel chunks per tap
+  int nk;                     // K iterations = taps · nkc
+  int* err;                   // device error word
+  EpiDev ep;
+};
+
+struct ConvLaunch {
+  int BK, BN, mode;
+  int grid;
+  CUtensorMap ta, tb;
+  ConvDev d;
+  // transposed conv: weights must be re-laid out (C,R,S,K) → (R·S·K, C) before the GEMM
+  const __half* wt_src = nullptr;
+  __half* wt_dst = nullptr;
+  // A_STEM: raw operand pointers (no tensor maps)
+  const __half* x = nullptr;
+  const __half* w = nullptr;
+};
+
+// Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
+int conv_prepare(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep, float beta,
+                 void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready = false);
+cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st);
+
+// kernels living in other translation units
+cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st);
+cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st);
+cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st);
+cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
+
+int* device_error_word();       // per-device error word (allocated on first use, before any capture)
+void set_last_error(const char* fmt, ...);
+
+}  // namespace osam
+
+struct osam_conv_plan {
+  osam_conv_geom g;
+  int transposed;
+  int P, Q;
+  int mode, BK, BN;
+  int tn, th, tw, tiles_q, tiles_p;
+  long long M;
+  int gemm_n, ntn, nkc, nk, tiles_m;
+};

@@ -1,0 +1,148 @@
+"""Parity of the sm_100a conv kernels (through the C ABI) with a plain PyTorch fp32 reference of the same op.
+
+Tolerance: fp16 outputs of an fp32-accumulated conv differ from the fp32 reference by the fp16 rounding
+of the output (≤ 2^-11 relative) plus accumulation-order noise, so every element must satisfy
+|y − ref| ≤ 2e-3·|ref| + 2e-3·max|ref|.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from objectsam_b200.conv import EPI_BIAS, EPI_BN_ACT, ConvGeom, ConvOp, DestSpec, sppf_pool_fwd
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def ref_conv(x, w, stride, pad):
+    """NHWC fp16 x, KRSC fp16 w → NHWC fp32 conv (TF32 off)."""
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    y = F.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(0, 3, 1, 2), stride=stride, padding=pad)
+    return y.permute(0, 2, 3, 1)
+
+
+def assert_close(y, ref, rel=2e-3):
+    y = y.float()
+    scale = ref.abs().max().item() + 1e-6
+    err = (y - ref).abs()
+    bound = rel * ref.abs() + rel * scale
+    bad = (err > bound).sum().item()
+    assert bad == 0, f"{bad} elements out of tolerance; max err {err.max().item():.3e} (scale {scale:.3e})"
+
+
+def rand_conv(N, H, W, C, K, R, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = (torch.rand(N, H, W, C, generator=g) * 2 - 1).half().to(DEV)
+    w = (torch.randn(K, R, R, C, generator=g) * (2.0 / (C * R * R)) ** 0.5).half().to(DEV)
+    return x, w
+
+
+# (N, H, W, C, K, R, stride): every kernel family — 3×3 s1/s2, 1×1, BK 32/64, BN 16..256, multi-N-tile, stem
+SHAPES = [
+    (2, 16, 16, 32, 32, 3, 1),
+    (2, 20, 20, 64, 64, 3, 1),
+    (3, 40, 40, 128, 128, 3, 1),
+    (2, 20, 20, 256, 224, 3, 1),
+    (1, 24, 36, 64, 256, 3, 1),
+    (2, 16, 16, 32, 64, 3, 2),
+    (2, 40, 40, 128, 256, 3, 2),
+    (1, 20, 20, 256, 512, 3, 2),
+    (2, 16, 16, 96, 64, 1, 1),
+    (2, 20, 20, 128, 1, 1, 1),
+    (2, 10, 10, 512, 512, 1, 1),
+    (1, 7, 9, 64, 32, 1, 1),
+    (2, 64, 64, 3, 32, 3, 2),
+    (1, 80, 80, 64, 64, 3, 1),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_fwd_matches_torch(cuda_lib, shape):
+    N, H, W, C, K, R, s = shape
+    x, w = rand_conv(N, H, W, C, K, R, seed=sum(shape))
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, s, R // 2))
+    y = torch.empty(op.out_shape(), dtype=torch.half, device=DEV)
+    op.fwd(x, w, y)
+    torch.cuda.synchronize()
+    assert_close(y, ref_conv(x, w, s, R // 2))
+
+
+def test_conv_fwd_beta_accumulates(cuda_lib):
+    x, w = rand_conv(2, 16, 16, 64, 64, 3, seed=7)
+    op = ConvOp().init(ConvGeom(2, 16, 16, 64, 64, 3, 3, 1, 1))
+    y0 = (torch.rand(2, 16, 16, 64, device=DEV) - 0.5).half()
+    y = y0.clone()
+    op.fwd(x, w, y, beta=1.0)
+    assert_close(y, ref_conv(x, w, 1, 1) + y0.float())
+
+
+def test_fused_bn_silu_residual_dests(cuda_lib):
+    """C2f-style epilogue: a = silu(scale·z + shift) + res → full buffer, a concat slice, and an upsampled slice."""
+    N, H, W, C, K = 2, 20, 20, 64, 128
+    x, w = rand_conv(N, H, W, C, K, 3, seed=11)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
+    shift = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    res = (torch.rand(N, H, W, K, generator=g) - 0.5).half().to(DEV)
+    out = torch.zeros(N, H, W, K, dtype=torch.half, device=DEV)
+    cat = torch.zeros(N, H, W, 3 * 64, dtype=torch.half, device=DEV)
+    up = torch.zeros(N, 2 * H, 2 * W, 96, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    op.fwd_fused(x, w, [DestSpec(out), DestSpec(cat, choff=64, c0=64, c1=128), DestSpec(up, choff=32, c0=0, c1=64, up=2)],
+                 kind=EPI_BN_ACT, scale=scale, shift=shift, res=res)
+    z = ref_conv(x, w, 1, 1).half().float()  # the reference stores z in fp16 before BN (round_z)
+    a = F.silu(z * scale + shift) + res.float()
+    assert_close(out, a)
+    assert_close(cat[..., 64:128], a[..., 64:128])
+    assert cat[..., :64].abs().max().item() == 0 and cat[..., 128:].abs().max().item() == 0
+    a_up = a[..., 0:64].repeat_interleave(2, dim=1).repeat_interleave(2, dim=2)
+    assert_close(up[..., 32:96], a_up)
+    assert up[..., :32].abs().max().item() == 0
+
+
+def test_fused_bias_head_k1(cuda_lib):
+    """Head 1×1 conv with bias and a single output channel (cls head, reference src/model.cpp:251)."""
+    N, H, W, C = 2, 40, 40, 128
+    x, w = rand_conv(N, H, W, C, 1, 1, seed=5)
+    bias = torch.tensor([0.25], device=DEV)
+    y = torch.empty(N, H, W, 1, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, 1, 1, 1, 1, 0))
+    op.fwd_fused(x, w, [DestSpec(y)], kind=EPI_BIAS, bias=bias)
+    assert_close(y, ref_conv(x, w, 1, 0).half().float() + 0.25)
+
+
+def test_conv_transpose_2x2(cuda_lib):
+    """proto.upsample: ConvTranspose2d(128→128, k=2, s=2) with weights in the reference's (C_in, R, S, C_out)."""
+    N, H, W, C, K = 2, 20, 20, 128, 128
+    g = torch.Generator(device="cpu").manual_seed(9)
+    x = (torch.rand(N, H, W, C, generator=g) * 2 - 1).half().to(DEV)
+    w_pt = (torch.randn(C, K, 2, 2, generator=g) * 0.1).half()  # PyTorch ConvTranspose2d weight
+    w = w_pt.permute(0, 2, 3, 1).contiguous().to(DEV)            # (C_in, kh, kw, C_out)
+    bias = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 2, 2, 2, 0), transposed=True)
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    y = torch.empty(op.out_shape(), dtype=torch.half, device=DEV)
+    op.fwd(x, w, y, ws=ws)
+    ref = F.conv_transpose2d(x.float().permute(0, 3, 1, 2), w_pt.float().to(DEV), stride=2).permute(0, 2, 3, 1)
+    assert_close(y, ref)
+    y2 = torch.empty_like(y)
+    op.fwd_fused(x, w, [DestSpec(y2)], kind=EPI_BIAS, bias=bias, ws=ws)
+    assert_close(y2, ref.half().float() + bias)
+
+
+def test_sppf_pool_exact(cuda_lib):
+    N, H, W, c = 3, 20, 20, 256
+    cat = torch.zeros(N, H, W, 4 * c, dtype=torch.half, device=DEV)
+    cat[..., :c] = torch.randn(N, H, W, c, device=DEV).half()
+    sppf_pool_fwd(cat, N, H, W, c)
+    x = cat[..., :c].permute(0, 3, 1, 2).float()
+    for k in range(1, 4):
+        x = F.max_pool2d(x, 5, 1, 2)
+        assert torch.equal(cat[..., k * c:(k + 1) * c].float(), x.permute(0, 2, 3, 1))
+
+
+def test_invalid_geometry_is_an_error(cuda_lib):
+    from objectsam_b200 import OsamError
+    with pytest.raises(OsamError):
+        ConvOp().init(ConvGeom(1, 16, 16, 48, 32, 3, 3, 1, 1))  # C % 32 != 0 and R·S·C > 32
