@@ -1,0 +1,107 @@
+"""CPU tests of the oracle (the checker) against the golden vectors and known answers."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fsow, postproc_ref, yolo_params, yolo_ref
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _golden_cases():
+    z = np.load(os.path.join(GOLDEN, "postproc_golden.npz"))
+    for ci in range(int(z["n_cases"])):
+        yield ci, {k[len(f"c{ci}_"):]: z[k] for k in z.files if k.startswith(f"c{ci}_")}
+
+
+@pytest.mark.parametrize("ci", range(4))
+def test_postproc_oracle_matches_reference_ref_detect(ci):
+    """The numpy restatement reproduces archive/tools/ref_detect.py exactly (scores, boxes, masks)."""
+    case = dict(_golden_cases())[ci]
+    o0 = case["o0"].astype(np.float32)
+    o1 = case["o1"].astype(np.float32)
+    S, cth, nth, mth, amin, mdet = case["cfg"]
+    xywh, conf, coefs = o0[:4].T, o0[4], o0[5:].T
+    det = postproc_ref.detect_one(xywh, conf, coefs, o1, int(S), conf_th=cth, nms_iou=nth, max_det=int(mdet),
+                                  area_min=int(amin), mask_iou=mth)
+    sel = det["sel"]
+    np.testing.assert_array_equal(det["score"][sel], case["score"])
+    np.testing.assert_array_equal(det["box"][sel], case["box"])
+    grid = np.unpackbits(case["grid"], axis=-1)[..., : int(case["grid_shape"][-1])].astype(bool)
+    np.testing.assert_array_equal(det["masks"][sel], grid.reshape(tuple(case["grid_shape"])))
+
+
+def test_nms_known_answer():
+    """Hand-checked case: strict '>' at the threshold, union>0 guard, stable tie order, max_det."""
+    boxes = np.array([[0, 0, 10, 10], [0, 0, 10, 10], [5, 0, 15, 10], [100, 100, 100, 110], [0, 0, 10, 7]],
+                     np.float32)
+    # 0 kept; 1 identical (IoU 1) suppressed; 2 IoU 50/150 kept; 3 zero-area box kept (union > 0 guard);
+    # 4 IoU with 0 = 70/100 rounds to exactly float32(0.7) and the test is strict '>', so it is kept.
+    assert np.float32(np.float32(70) / np.float32(100)) == np.float32(0.7)
+    assert postproc_ref.greedy_nms(boxes, 0.7, 10) == [0, 2, 3, 4]
+    assert postproc_ref.greedy_nms(boxes, 0.7, 2) == [0, 2]
+    conf = np.array([0.5, 0.9, 0.5, 0.2, 0.9], np.float32)
+    assert list(postproc_ref.nms_order(conf, 0.25)) == [1, 4, 0, 2]
+
+
+def test_dfl_decode_known_answer():
+    """A one-hot DFL distribution decodes to its bin; anchors are cell centres × stride."""
+    N, H, W = 1, 2, 2
+    box = [np.full((N, 64, H * 2 ** (2 - l), W * 2 ** (2 - l)), -30.0, np.float32) for l in range(3)]
+    for b in box:
+        b[:, 0 * 16 + 3] = 30.0   # left  = 3
+        b[:, 1 * 16 + 1] = 30.0   # top   = 1
+        b[:, 2 * 16 + 4] = 30.0   # right = 4
+        b[:, 3 * 16 + 2] = 30.0   # bottom= 2
+    cls = [np.zeros((N, 1) + b.shape[2:], np.float32) for b in box]
+    coef = [np.zeros((N, 32) + b.shape[2:], np.float32) for b in box]
+    xywh, conf, _ = postproc_ref.decode(box, cls, coef)
+    # first anchor of level 0: cell (0,0) → anchor (0.5, 0.5); x1=-2.5 y1=-0.5 x2=4.5 y2=2.5 → ×8
+    np.testing.assert_allclose(xywh[0, 0], [8 * 1.0, 8 * 1.0, 8 * 7.0, 8 * 3.0], atol=1e-4)
+    np.testing.assert_allclose(conf, 0.5)
+
+
+def test_fsow_roundtrip(tmp_path):
+    t = {"a.weight": np.arange(24, dtype=np.float32).reshape(2, 3, 4), "b": np.array([1, 2], np.int32),
+         "m": np.array([[1, 0]], np.uint8), "s": np.float32(3.5).reshape(())}
+    p = str(tmp_path / "x.fsow")
+    fsow.save(p, t)
+    r = fsow.load(p)
+    assert set(r) == set(t)
+    for k in t:
+        np.testing.assert_array_equal(r[k], t[k])
+        assert r[k].dtype == np.asarray(t[k]).dtype
+    with open(p, "r+b") as f:
+        f.write(b"XXXX")
+    with pytest.raises(ValueError):
+        fsow.load(p)
+
+
+def test_param_table_matches_yolov8s_seg():
+    shapes = yolo_params.param_shapes()
+    assert yolo_params.n_params() == 11790467  # 11.8 M (docs/SPEC.md:18-23)
+    assert shapes["model.22.cv2.0.2.weight"] == (64, 64, 1, 1)  # 4·reg_max box channels
+    assert shapes["model.22.proto.upsample.weight"] == (128, 128, 2, 2)
+    assert shapes["model.9.cv2.conv.weight"] == (512, 1024, 1, 1)
+    assert len([l for l in yolo_params.conv_layers()]) == 76  # 70 reference conv nodes + 6 unfused head convs
+
+
+def test_forward_flops_match_survey():
+    assert abs(yolo_ref.forward_flops(640) / 1e9 - 39.92) < 0.01
+    assert abs(yolo_ref.forward_flops(1024) / 1e9 - 102.18) < 0.01
+
+
+def test_oracle_forward_shapes_and_fp16_emulation_close_to_fp64():
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    w = yolo_params.make_weights(1, random_bn=True)
+    img = yolo_params.make_images(1, 128, 1)
+    o16 = yolo_ref.YoloSegRef(w, emulate_fp16=True).forward(img)
+    o64 = yolo_ref.YoloSegRef(w, emulate_fp16=False, dtype=torch.float64).forward(img)
+    assert tuple(o16["proto"].shape) == (1, 32, 32, 32)
+    assert [tuple(t.shape) for t in o16["box"]] == [(1, 64, 16, 16), (1, 64, 8, 8), (1, 64, 4, 4)]
+    for k in ("box", "cls", "coef"):
+        for a, b in zip(o16[k], o64[k]):
+            scale = b.abs().max().item()
+            assert (a.double() - b).abs().max().item() <= 2e-2 * scale + 1e-3
