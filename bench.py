@@ -1,0 +1,331 @@
+#!/usr/bin/env python
+"""YOLOv8s-seg nc=1 inference throughput on B200 — BASELINE config 2 (batch 64/GPU, 640×640, fp16 NHWC).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B] [--imgsz S]
+
+One process per GPU (torchrun for N > 1); images are sharded across ranks with no collective (weak
+scaling: every rank runs its own batch).  A step is one forward pass of the fused conv path over the
+rank's batch: stem → backbone → SPPF → neck → Segment head → proto, every conv one kernel with its
+folded-BN/SiLU/residual/concat epilogue.  Timing: W untimed warm-up steps, then K steps between a
+barrier + synchronize on both sides, CUDA events on the launching stream, max over ranks.  The inputs
+(157 MB per step) and activations (GBs) are larger than the 126 MB L2, so no flush is needed.
+
+Rank 0 prints one JSON line.  Besides the contract keys it carries:
+  roofline      dominant kernel (largest mean per-launch time, from per-node CUDA events over the timed
+                region) against the measured peaks in MEASURED_PEAKS.json;
+  e2e           the same metric through the C-ABI model with host buffers: pinned host → device input
+                copy, forward, device → host copy of the raw heads + proto, every step;
+  cpu_baseline  the CPU oracle (PyTorch forward of the same network, oracle/yolo_ref.py) on the host
+                cores, a bounded batch-1 sample.
+`--impl reference` runs the reference arm: the network's PyTorch CPU forward on the host cores (the
+reference has no CPU implementation of this path; its own code for it is the cuDNN build).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "YOLOv8s-seg 640 fp16 inference img/s"
+UNIT = "img/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--imgsz", type=int, default=640)
+    ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=d["hbm_gbs"], tflops=d["bf16_tflops"], tflops_sust=d["bf16_tflops_sustained"],
+                    src="measured")
+    return dict(hbm_gbs=6650.0, tflops=1590.0, tflops_sust=1400.0, src="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    rows.append(dict(sm=float(f[1]), smax=float(f[2]), power=float(f[3]), hw=f[5], hwt=f[6],
+                                     swt=f[7], swp=f[8]))
+                except ValueError:
+                    continue
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        load = [r for r in rows if r["power"] > 250] or rows
+        reasons = set()
+        for r in load:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("swp", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(load)}
+
+
+def cpu_forward_sample(imgsz: int, budget_s: float, seed: int = 0):
+    """PyTorch CPU forward of the network (oracle), batch-1 images until the budget is spent."""
+    import torch
+    from oracle import yolo_params, yolo_ref
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    w = yolo_params.make_weights(0)
+    m = yolo_ref.YoloSegRef(w, emulate_fp16=False)
+    img = yolo_params.make_images(1, imgsz, seed)
+    m.forward(img)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        m.forward(img)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return dict(value=n / dt, unit=UNIT, cores=torch.get_num_threads(), kind="port",
+                sample=f"{n} batch-1 {imgsz}x{imgsz} forwards of the PyTorch CPU restatement (fp32), {dt:.1f} s")
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the network's PyTorch CPU forward on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import yolo_params, yolo_ref
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    m = yolo_ref.YoloSegRef(yolo_params.make_weights(0), emulate_fp16=False)
+    img = yolo_params.make_images(1, args.imgsz, 0)
+    for _ in range(max(1, args.warmup)):
+        m.forward(img)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.forward(img)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"YOLOv8s-seg nc=1 forward, {args.imgsz}x{args.imgsz}, batch-1 sample per step",
+                       "imgsz": args.imgsz, "parallelism": "rank 0 only (host cores)"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{args.steps} timed batch-1 forwards of the PyTorch CPU restatement "
+                                       "(the reference implements this path only as its cuDNN build)"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    from objectsam_b200.model import Model
+    from oracle import yolo_params  # seeded synthetic weights/images only (the checker is not timed)
+
+    B, S = args.batch, args.imgsz
+    model = Model(B, S)
+    model.load(yolo_params.make_weights(0))
+    model.sync_weights()
+    imgs = torch.from_numpy(yolo_params.make_images(B, S, seed=rank)).half()
+    model.input().copy_(imgs.to(dev))
+    nodes = model.nodes()
+    n = len(nodes)
+    stream = torch.cuda.current_stream()
+
+    # ---- warm-up (eager + graph)
+    for _ in range(args.warmup):
+        model.forward()
+    model.forward(use_graph=True)
+    barrier()
+
+    # ---- timed region: K eager steps, a CUDA event before every node and after the last
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n + 1)] for _ in range(K)]
+    with ClockSampler(local) as clk:
+        barrier()
+        for k in range(K):
+            row = evs[k]
+            for i in range(n):
+                row[i].record(stream)
+                model.forward_nodes(i, 1)
+            row[n].record(stream)
+        barrier()
+    ms = evs[0][0].elapsed_time(evs[K - 1][n])
+    node_ms = [sum(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K)) / K for i in range(n)]
+    clocks = clk.summary()
+
+    # graph-replay timing of the same step (launch-overhead-free variant), informational
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    g0.record(stream)
+    for _ in range(K):
+        model.forward(use_graph=True)
+    g1.record(stream)
+    barrier()
+    graph_ms = g0.elapsed_time(g1)
+
+    t = torch.tensor([ms, graph_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, graph_ms = t.tolist()
+    value = world * B * K / (ms / 1e3)
+
+    # ---- e2e: host buffers through the C-ABI model, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        h_in = imgs.pin_memory()
+        outs = [model.head(k, l) for k in range(3) for l in range(3)] + [model.proto()]
+        h_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+        d_in = model.input()
+        for _ in range(2):
+            d_in.copy_(h_in, non_blocking=True)
+            model.forward(use_graph=True)
+            for h, d in zip(h_out, outs):
+                h.copy_(d, non_blocking=True)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            d_in.copy_(h_in, non_blocking=True)
+            model.forward(use_graph=True)
+            for h, d in zip(h_out, outs):
+                h.copy_(d, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * B * K / (te.item() / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
+               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in h_out)}
+
+    # ---- roofline of the dominant kernel
+    peaks = load_peaks()
+    top = max(range(n), key=lambda i: node_ms[i])
+    nd = nodes[top]
+    ridge = peaks["tflops_sust"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    bound = "tensor" if nd["flops"] / max(nd["bytes"], 1) > ridge else "hbm"
+    t_s = node_ms[top] / 1e3
+    if bound == "tensor":
+        ach, peak, unit_r = nd["flops"] / t_s / 1e12, peaks["tflops_sust"], "TFLOP/s"
+    else:
+        ach, peak, unit_r = nd["bytes"] / t_s / 1e9, peaks["hbm_gbs"], "GB/s"
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        try:
+            traffic = json.load(open(tf)).get(nd["name"], {}).get(f"b{B}_s{S}")
+        except (ValueError, OSError):
+            traffic = None
+    conv_flops = sum(x["flops"] for x in nodes)
+    roofline = {"bound": bound, "achieved": ach, "peak": peak, "unit": unit_r, "frac": ach / peak,
+                "traffic": traffic, "kernel": nd["name"], "kernel_ms": node_ms[top],
+                "peak_source": f"{peaks['src']} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
+                "algorithmic_flops": nd["flops"], "algorithmic_bytes": nd["bytes"],
+                "forward_conv_tflops": conv_flops / (ms / K / 1e3) / 1e12}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_forward_sample(S, args.cpu_sample_s)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+                "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
+                "config": {"workload": f"BASELINE config 2: YOLOv8s-seg nc=1 inference forward (heads + proto), "
+                                       f"batch {B}/GPU, {S}x{S} NHWC fp16, seeded U[0,1] images, He-normal weights",
+                           "global_batch": B * world, "imgsz": S, "parallelism": f"dp{world} (image shards, no collective)",
+                           "l2": "inputs+activations > 126 MB L2 (no flush needed)",
+                           "timing": "eager launches with a CUDA event per node over the timed region"},
+                "gpu_launches": K * n, "clocks": clocks, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "graph_ms_per_step": graph_ms / K,
+                "top_kernels": sorted(({"name": nodes[i]["name"], "ms": round(node_ms[i], 4),
+                                        "tflops": round(nodes[i]["flops"] / (node_ms[i] / 1e3) / 1e12, 1),
+                                        "gbs": round(nodes[i]["bytes"] / (node_ms[i] / 1e3) / 1e9, 0)}
+                                       for i in range(n)), key=lambda d: -d["ms"])[:12]}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -100,6 +100,48 @@ int osam_conv_fwd_fused(const osam_conv_plan* plan, const void* x, const void* w
  * 5×5/s1/p2 max-pools into slices 1..3.  Replaces sppf_pool_fwd (src/misc.cuh:6, src/misc.cu:149-153). */
 int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * YOLOv8s-seg (nc = 1) inference graph on the kernels above.  Replaces the reference's Model
+ * (src/model.h:97-140): build (src/model.cpp:168-347), Params::load + sync_weights (:49-62, :369),
+ * forward(false) (:383-414), input()/head()/proto() accessors.  Every conv node runs as one fused
+ * kernel (conv + folded eval-mode BN + SiLU + residual + concat/upsample routing, or conv + bias).
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct osam_model osam_model;
+
+/* A device tensor owned by the model: NHWC fp16, p = base of an (n, h, w, c) buffer. */
+typedef struct osam_tensor {
+  void* p;
+  int n, h, w, c;
+} osam_tensor;
+
+/* Build the graph and allocate all activations for `batch` images of imgsz×imgsz (imgsz % 32 == 0).
+ * reg_max: DFL bins of the box head (16 for YOLOv8s-seg).  Allocates device memory (setup time). */
+int osam_model_create(int batch, int imgsz, int reg_max, osam_model** out);
+int osam_model_destroy(osam_model* m);
+/* One parameter, PyTorch name and layout (e.g. "model.0.conv.weight" K×C×R×S), host fp32 — the
+ * reference's Params::load contract.  Unknown names are ignored (returns OSAM_OK), wrong shapes fail. */
+int osam_model_set_param(osam_model* m, const char* name, const float* data, const int64_t* shape, int ndim);
+/* Read every parameter from an FSOW file (reference src/fsow.h format). */
+int osam_model_load_fsow(osam_model* m, const char* path);
+/* Upload the parameters: fp16 KRSC weights and folded eval-mode BN (γ/√(var+eps), β−μ·scale), then
+ * encode every kernel's tensor maps.  All parameters must have been set. */
+int osam_model_sync_weights(osam_model* m, osam_stream_t stream);
+int osam_model_input(const osam_model* m, osam_tensor* t);                   /* NHWC fp16, C = 3 */
+int osam_model_head(const osam_model* m, int kind, int level, osam_tensor* t); /* kind 0 box, 1 cls, 2 coef */
+int osam_model_proto(const osam_model* m, osam_tensor* t);
+int osam_model_act(const osam_model* m, const char* name, osam_tensor* t);   /* any named activation */
+/* Inference forward pass: input → heads + proto.  use_graph = 1 records the launch sequence as a CUDA
+ * graph on the first call and replays it afterwards (the first call must not be inside a capture). */
+int osam_model_forward(osam_model* m, int use_graph, osam_stream_t stream);
+/* Kernels launched by one forward pass (one per graph node). */
+int osam_model_num_launches(const osam_model* m);
+/* Launch nodes [first, first+count) of the forward pass on `stream` (eager), e.g. to bracket one
+ * kernel with timing events.  Running every node in order equals osam_model_forward(m, 0, stream). */
+int osam_model_forward_nodes(osam_model* m, int first, int count, osam_stream_t stream);
+/* Geometry of node i: name (NUL-terminated, truncated to name_len), kind (0 conv+BN+SiLU, 1 head conv +
+ * bias, 2 transposed conv + bias, 3 SPPF pool) and the conv geometry (pool: N,H,W,C of the slice). */
+int osam_model_node_info(const osam_model* m, int i, char* name, int name_len, int* kind, osam_conv_geom* g);
+
 /* Device error word shared by all kernels of this library on the current device: returns the first
  * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises. */
 int osam_device_error(void);

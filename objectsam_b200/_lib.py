@@ -38,6 +38,11 @@ class Epilogue(ctypes.Structure):
                 ("act", c_int), ("round_z", c_int), ("n_dest", c_int), ("dest", Dest * MAX_DEST)]
 
 
+class Tensor(ctypes.Structure):
+    """osam_tensor — a device NHWC fp16 buffer owned by a model."""
+    _fields_ = [("p", c_void_p), ("n", c_int), ("h", c_int), ("w", c_int), ("c", c_int)]
+
+
 class OsamError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"osam error {code}: {msg}")
@@ -53,6 +58,19 @@ _SIGS = {
     "osam_conv_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_void_p]),
     "osam_conv_fwd_fused": (c_int, [c_void_p, c_void_p, c_void_p, POINTER(Epilogue), c_void_p, c_size_t, c_void_p]),
     "osam_sppf_fwd": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "osam_model_create": (c_int, [c_int, c_int, c_int, POINTER(c_void_p)]),
+    "osam_model_destroy": (c_int, [c_void_p]),
+    "osam_model_set_param": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, POINTER(c_int64), c_int]),
+    "osam_model_load_fsow": (c_int, [c_void_p, ctypes.c_char_p]),
+    "osam_model_sync_weights": (c_int, [c_void_p, c_void_p]),
+    "osam_model_input": (c_int, [c_void_p, POINTER(Tensor)]),
+    "osam_model_head": (c_int, [c_void_p, c_int, c_int, POINTER(Tensor)]),
+    "osam_model_proto": (c_int, [c_void_p, POINTER(Tensor)]),
+    "osam_model_act": (c_int, [c_void_p, ctypes.c_char_p, POINTER(Tensor)]),
+    "osam_model_forward": (c_int, [c_void_p, c_int, c_void_p]),
+    "osam_model_num_launches": (c_int, [c_void_p]),
+    "osam_model_forward_nodes": (c_int, [c_void_p, c_int, c_int, c_void_p]),
+    "osam_model_node_info": (c_int, [c_void_p, c_int, ctypes.c_char_p, c_int, POINTER(c_int), POINTER(ConvGeom)]),
     "osam_device_error": (c_int, []),
     "osam_last_error": (ctypes.c_char_p, []),
 }

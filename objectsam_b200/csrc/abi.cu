@@ -312,6 +312,11 @@ cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st) {
   return launch_conv_fprop(L, st);
 }
 
+cudaError_t conv_prime(const ConvLaunch& L) {
+  if (L.mode == A_STEM) return cudaSuccess;
+  return launch_conv_fprop(L, nullptr, true);
+}
+
 }  // namespace osam
 
 using namespace osam;

@@ -186,45 +186,48 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int BK, int BN, int MODE>
-static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st) {
+static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_only) {
   using Cfg = FpropCfg<BK, BN>;
-  static bool attr_set = false;  // per process; the attribute applies to every device
+  // The dynamic shared-memory opt-in is set once per process (one device per process) and, through
+  // conv_prime(), before any stream capture.
+  static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(k_conv_fprop<BK, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
+  if (prime_only) return cudaSuccess;
   k_conv_fprop<BK, BN, MODE><<<L.grid, 192, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
   return cudaGetLastError();
 }
 
 template <int BK, int BN>
-static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st) {
+static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime) {
   switch (L.mode) {
-    case A_GEMM: return launch_one<BK, BN, A_GEMM>(L, st);
-    case A_S1: return launch_one<BK, BN, A_S1>(L, st);
-    case A_S2: return launch_one<BK, BN, A_S2>(L, st);
+    case A_GEMM: return launch_one<BK, BN, A_GEMM>(L, st, prime);
+    case A_S1: return launch_one<BK, BN, A_S1>(L, st, prime);
+    case A_S2: return launch_one<BK, BN, A_S2>(L, st, prime);
   }
   return cudaErrorInvalidValue;
 }
 
 template <int BK>
-static cudaError_t launch_bn(const ConvLaunch& L, cudaStream_t st) {
+static cudaError_t launch_bn(const ConvLaunch& L, cudaStream_t st, bool prime) {
   switch (L.BN) {
-    case 16: return launch_mode<BK, 16>(L, st);
-    case 32: return launch_mode<BK, 32>(L, st);
-    case 64: return launch_mode<BK, 64>(L, st);
-    case 128: return launch_mode<BK, 128>(L, st);
-    case 224: return launch_mode<BK, 224>(L, st);
-    case 256: return launch_mode<BK, 256>(L, st);
+    case 16: return launch_mode<BK, 16>(L, st, prime);
+    case 32: return launch_mode<BK, 32>(L, st, prime);
+    case 64: return launch_mode<BK, 64>(L, st, prime);
+    case 128: return launch_mode<BK, 128>(L, st, prime);
+    case 224: return launch_mode<BK, 224>(L, st, prime);
+    case 256: return launch_mode<BK, 256>(L, st, prime);
   }
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st) {
-  if (L.BK == 64) return launch_bn<64>(L, st);
-  if (L.BK == 32) return launch_bn<32>(L, st);
+cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st, bool prime_only) {
+  if (L.BK == 64) return launch_bn<64>(L, st, prime_only);
+  if (L.BK == 32) return launch_bn<32>(L, st, prime_only);
   return cudaErrorInvalidValue;
 }
 

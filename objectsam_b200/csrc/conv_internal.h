@@ -68,9 +68,12 @@ struct ConvLaunch {
 int conv_prepare(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep, float beta,
                  void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready = false);
 cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st);
+// One-time per-kernel set-up (dynamic shared-memory opt-in) without launching: call before capturing.
+cudaError_t conv_prime(const ConvLaunch& L);
+cudaError_t sppf_prime();
 
 // kernels living in other translation units
-cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st);
+cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st, bool prime_only = false);
 cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st);
 cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st);
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);

@@ -1,0 +1,632 @@
+// YOLOv8s-seg (nc = 1) inference graph on the fused conv kernels (C ABI: osam_model_*).
+//
+// Same topology, parameter names and activation routing as the reference's Model (src/model.cpp:168-275):
+// concat is implicit — each producer's epilogue writes straight into its slices of the concat buffers
+// (with the 2× nearest upsample for the neck), C2f's cv1 writes both the concat buffer and the first
+// bottleneck input, and the three first convs of each head level share one K = 64+128+32 conv.
+// Differences by design: eval-mode BN is folded into each conv's epilogue (no z buffer, no apply pass),
+// head/upsample biases are applied in the epilogue, SPPF's three pools are one kernel, and the whole
+// forward can be replayed as one CUDA graph.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "conv_internal.h"
+
+namespace osam {
+int model_fail(int code, const char* fmt, ...);
+}
+
+namespace {
+using namespace osam;
+
+struct MAct {
+  std::string name;
+  int C = 0, H = 0, W = 0;
+  __half* p = nullptr;
+  size_t off = 0;  // byte offset in the activation arena
+};
+
+struct MDest {
+  MAct* a;
+  int choff, c0, c1, up;
+};
+
+enum NodeKind { N_CONVBN = 0, N_HEAD = 1, N_CONVT = 2, N_POOL = 3 };
+
+struct MNode {
+  NodeKind kind;
+  std::string name;
+  MAct* in = nullptr;
+  int K = 0, k = 1, s = 1;
+  std::vector<std::string> pre;  // parameter prefixes (three for a fused head conv)
+  std::vector<int> ks;           // output channels per prefix
+  std::vector<MDest> dests;
+  MAct* res = nullptr;
+  MAct* out = nullptr;
+  MAct* cat = nullptr;
+  int pc = 0;
+  osam_conv_plan plan{};
+  ConvLaunch L{};
+  size_t w_off = 0;  // fp16 weight arena offset (elements)
+  size_t f_off = 0;  // fp32 arena offset: scale[K] + shift[K] (CONVBN) or bias[K]
+};
+
+struct PInfo {
+  std::vector<int64_t> shape;
+  std::vector<float> host;
+  bool set = false;
+};
+
+__global__ void k_f32_to_f16(const float* __restrict__ s, __half* __restrict__ d, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    d[i] = __float2half_rn(s[i]);
+}
+// Eval-mode BN fold, same formula as the reference's k_eval_scale (src/bn.cu:277-284).
+__global__ void k_bn_fold(const float* __restrict__ gbmv, int C, float eps, float* __restrict__ scale,
+                          float* __restrict__ shift) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float g = gbmv[c], b = gbmv[C + c], rm = gbmv[2 * C + c], rv = gbmv[3 * C + c];
+  const float sc = g * rsqrtf(rv + eps);
+  scale[c] = sc;
+  shift[c] = b - rm * sc;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct osam_model {
+  int N = 0, S = 0, reg_max = 16;
+  float bn_eps = 1e-3f;
+  std::map<std::string, std::unique_ptr<MAct>> acts;
+  std::vector<std::unique_ptr<MNode>> nodes;
+  std::map<std::string, PInfo> params;
+  std::vector<std::string> porder;
+  MAct* in = nullptr;
+  MAct* head[3][3] = {};
+  MAct* proto = nullptr;
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  __half* w16 = nullptr;
+  size_t w16_n = 0;
+  float* f32 = nullptr;
+  size_t f32_n = 0;
+  bool synced = false;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+
+  // ------------------------------------------------------------------ graph construction
+  MAct* act(const std::string& n, int C, int H, int W) {
+    auto a = std::make_unique<MAct>();
+    a->name = n;
+    a->C = C;
+    a->H = H;
+    a->W = W;
+    MAct* p = a.get();
+    acts[n] = std::move(a);
+    return p;
+  }
+  void add_param(const std::string& name, std::vector<int64_t> shape) {
+    params[name].shape = std::move(shape);
+    porder.push_back(name);
+  }
+  void convbn(const std::string& name, MAct* in_, int K, int k, int s, std::vector<MDest> dests, MAct* res = nullptr,
+              std::vector<std::string> fused = {}, std::vector<int> fused_k = {}) {
+    auto nd = std::make_unique<MNode>();
+    nd->kind = N_CONVBN;
+    nd->name = name;
+    nd->in = in_;
+    nd->K = K;
+    nd->k = k;
+    nd->s = s;
+    nd->pre = fused.empty() ? std::vector<std::string>{name} : fused;
+    nd->ks = fused.empty() ? std::vector<int>{K} : fused_k;
+    for (size_t i = 0; i < nd->pre.size(); i++) {
+      const std::string& p = nd->pre[i];
+      add_param(p + ".conv.weight", {nd->ks[i], in_->C, k, k});
+      for (const char* b : {".bn.weight", ".bn.bias", ".bn.running_mean", ".bn.running_var"})
+        add_param(p + b, {nd->ks[i]});
+    }
+    for (auto& d : dests)
+      if (d.c1 == 0) d.c1 = K;
+    nd->dests = dests;
+    nd->res = res;
+    nodes.push_back(std::move(nd));
+  }
+  MAct* c2f(const std::string& name, MAct* x, int c2, int n, bool shortcut, std::vector<MDest> out) {
+    const int c = c2 / 2, H = x->H, W = x->W;
+    MAct* cat = act(name + ".cat", (2 + n) * c, H, W);
+    MAct* bin = act(name + ".m0.in", c, H, W);
+    convbn(name + ".cv1", x, 2 * c, 1, 1, {{cat, 0, 0, 2 * c, 1}, {bin, 0, c, 2 * c, 1}});
+    for (int j = 0; j < n; j++) {
+      const std::string mj = name + ".m." + std::to_string(j);
+      MAct* t = act(mj + ".t", c, H, W);
+      convbn(mj + ".cv1", bin, c, 3, 1, {{t, 0, 0, c, 1}});
+      std::vector<MDest> d = {{cat, (2 + j) * c, 0, c, 1}};
+      MAct* next = nullptr;
+      if (j + 1 < n) {
+        next = act(name + ".m" + std::to_string(j + 1) + ".in", c, H, W);
+        d.push_back({next, 0, 0, c, 1});
+      }
+      convbn(mj + ".cv2", t, c, 3, 1, d, shortcut ? bin : nullptr);
+      bin = next;
+    }
+    convbn(name + ".cv2", cat, c2, 1, 1, out);
+    return cat;
+  }
+  void head_conv(const std::string& name, MAct* x, int K, MAct* out) {
+    auto nd = std::make_unique<MNode>();
+    nd->kind = N_HEAD;
+    nd->name = name;
+    nd->in = x;
+    nd->K = K;
+    nd->out = out;
+    add_param(name + ".weight", {K, x->C, 1, 1});
+    add_param(name + ".bias", {K});
+    nodes.push_back(std::move(nd));
+  }
+
+  void build() {
+    auto M = [](int i) { return "model." + std::to_string(i); };
+    in = act("in", 3, S, S);
+    MAct* a0 = act("a0", 32, S / 2, S / 2);
+    convbn(M(0), in, 32, 3, 2, {{a0, 0, 0, 0, 1}});
+    MAct* a1 = act("a1", 64, S / 4, S / 4);
+    convbn(M(1), a0, 64, 3, 2, {{a1, 0, 0, 0, 1}});
+    MAct* a2 = act("a2", 64, S / 4, S / 4);
+    c2f(M(2), a1, 64, 1, true, {{a2, 0, 0, 0, 1}});
+    MAct* a3 = act("a3", 128, S / 8, S / 8);
+    convbn(M(3), a2, 128, 3, 2, {{a3, 0, 0, 0, 1}});
+    MAct* cat11 = act("cat11", 768, S / 16, S / 16);
+    MAct* cat14 = act("cat14", 384, S / 8, S / 8);
+    MAct* cat17 = act("cat17", 384, S / 16, S / 16);
+    MAct* cat20 = act("cat20", 768, S / 32, S / 32);
+    MAct* a4 = act("a4", 128, S / 8, S / 8);
+    c2f(M(4), a3, 128, 2, true, {{a4, 0, 0, 0, 1}, {cat14, 256, 0, 0, 1}});
+    MAct* a5 = act("a5", 256, S / 16, S / 16);
+    convbn(M(5), a4, 256, 3, 2, {{a5, 0, 0, 0, 1}});
+    MAct* a6 = act("a6", 256, S / 16, S / 16);
+    c2f(M(6), a5, 256, 2, true, {{a6, 0, 0, 0, 1}, {cat11, 512, 0, 0, 1}});
+    MAct* a7 = act("a7", 512, S / 32, S / 32);
+    convbn(M(7), a6, 512, 3, 2, {{a7, 0, 0, 0, 1}});
+    MAct* a8 = act("a8", 512, S / 32, S / 32);
+    c2f(M(8), a7, 512, 1, true, {{a8, 0, 0, 0, 1}});
+    MAct* sp = act(M(9) + ".cat", 1024, S / 32, S / 32);
+    convbn(M(9) + ".cv1", a8, 256, 1, 1, {{sp, 0, 0, 0, 1}});
+    {
+      auto nd = std::make_unique<MNode>();
+      nd->kind = N_POOL;
+      nd->name = M(9) + ".m";
+      nd->cat = sp;
+      nd->pc = 256;
+      nodes.push_back(std::move(nd));
+    }
+    convbn(M(9) + ".cv2", sp, 512, 1, 1, {{cat11, 0, 0, 0, 2}, {cat20, 256, 0, 0, 1}});
+    c2f(M(12), cat11, 256, 1, false, {{cat14, 0, 0, 0, 2}, {cat17, 128, 0, 0, 1}});
+    MAct* p3 = act("p3", 128, S / 8, S / 8);
+    c2f(M(15), cat14, 128, 1, false, {{p3, 0, 0, 0, 1}});
+    convbn(M(16), p3, 128, 3, 2, {{cat17, 0, 0, 0, 1}});
+    MAct* p4 = act("p4", 256, S / 16, S / 16);
+    c2f(M(18), cat17, 256, 1, false, {{p4, 0, 0, 0, 1}});
+    convbn(M(19), p4, 256, 3, 2, {{cat20, 0, 0, 0, 1}});
+    MAct* p5 = act("p5", 512, S / 32, S / 32);
+    c2f(M(21), cat20, 512, 1, false, {{p5, 0, 0, 0, 1}});
+    // Segment head: per level one fused 3×3 conv (box c2 | cls 128 | coef 32), then the three branches.
+    const int R4 = 4 * reg_max;
+    const int c2 = std::max(16, std::max(128 / 4, R4));
+    const int KH = c2 + 128 + 32;
+    MAct* P[3] = {p3, p4, p5};
+    const std::string hd = M(22);
+    for (int l = 0; l < 3; l++) {
+      const std::string L = std::to_string(l);
+      const int H = P[l]->H, W = P[l]->W;
+      MAct* hb = act("h" + L + ".b1", c2, H, W);
+      MAct* hc = act("h" + L + ".c1", 128, H, W);
+      MAct* hm = act("h" + L + ".m1", 32, H, W);
+      convbn(hd + ".h" + L + ".0", P[l], KH, 3, 1,
+             {{hb, 0, 0, c2, 1}, {hc, 0, c2, c2 + 128, 1}, {hm, 0, c2 + 128, KH, 1}}, nullptr,
+             {hd + ".cv2." + L + ".0", hd + ".cv3." + L + ".0", hd + ".cv4." + L + ".0"}, {c2, 128, 32});
+      MAct* hb2 = act("h" + L + ".b2", c2, H, W);
+      MAct* hc2 = act("h" + L + ".c2", 128, H, W);
+      MAct* hm2 = act("h" + L + ".m2", 32, H, W);
+      convbn(hd + ".cv2." + L + ".1", hb, c2, 3, 1, {{hb2, 0, 0, 0, 1}});
+      convbn(hd + ".cv3." + L + ".1", hc, 128, 3, 1, {{hc2, 0, 0, 0, 1}});
+      convbn(hd + ".cv4." + L + ".1", hm, 32, 3, 1, {{hm2, 0, 0, 0, 1}});
+      head[0][l] = act("out.box" + L, R4, H, W);
+      head[1][l] = act("out.cls" + L, 1, H, W);
+      head[2][l] = act("out.coef" + L, 32, H, W);
+      head_conv(hd + ".cv2." + L + ".2", hb2, R4, head[0][l]);
+      head_conv(hd + ".cv3." + L + ".2", hc2, 1, head[1][l]);
+      head_conv(hd + ".cv4." + L + ".2", hm2, 32, head[2][l]);
+    }
+    MAct* pr1 = act("proto.1", 128, S / 8, S / 8);
+    convbn(hd + ".proto.cv1", p3, 128, 3, 1, {{pr1, 0, 0, 0, 1}});
+    MAct* pru = act("proto.up", 128, S / 4, S / 4);
+    {
+      auto nd = std::make_unique<MNode>();
+      nd->kind = N_CONVT;
+      nd->name = hd + ".proto.upsample";
+      nd->in = pr1;
+      nd->out = pru;
+      nd->K = 128;
+      add_param(nd->name + ".weight", {128, 128, 2, 2});
+      add_param(nd->name + ".bias", {128});
+      nodes.push_back(std::move(nd));
+    }
+    MAct* pr2 = act("proto.2", 128, S / 4, S / 4);
+    convbn(hd + ".proto.cv2", pru, 128, 3, 1, {{pr2, 0, 0, 0, 1}});
+    proto = act("out.proto", 32, S / 4, S / 4);
+    convbn(hd + ".proto.cv3", pr2, 32, 1, 1, {{proto, 0, 0, 0, 1}});
+  }
+
+  int allocate() {
+    size_t off = 0;
+    for (auto& kv : acts) {
+      MAct* a = kv.second.get();
+      a->off = off;
+      off = align_up(off + (size_t)N * a->H * a->W * a->C * sizeof(__half), 1024);
+    }
+    arena_bytes = off;
+    cudaError_t e = cudaMalloc(&arena, arena_bytes);
+    if (e != cudaSuccess) return model_fail(OSAM_ERR_NOMEM, "activation arena (%zu B): %s", arena_bytes, cudaGetErrorString(e));
+    cudaMemset(arena, 0, arena_bytes);
+    for (auto& kv : acts) kv.second->p = reinterpret_cast<__half*>(arena + kv.second->off);
+    // weight / fp32 arenas
+    size_t w = 0, f = 0;
+    for (auto& nd : nodes) {
+      if (nd->kind == N_POOL) continue;
+      const int C = nd->in->C;
+      nd->w_off = w;
+      const size_t wn = nd->kind == N_CONVT ? (size_t)C * 4 * nd->K : (size_t)nd->K * nd->k * nd->k * C;
+      w = align_up(w + wn, 64);
+      nd->f_off = f;
+      f = align_up(f + (nd->kind == N_CONVBN ? 2 * (size_t)nd->K : (size_t)nd->K), 32);
+    }
+    w16_n = w;
+    f32_n = f;
+    if ((e = cudaMalloc(&w16, w16_n * sizeof(__half))) != cudaSuccess) return model_fail(OSAM_ERR_NOMEM, "weights");
+    if ((e = cudaMalloc(&f32, f32_n * sizeof(float))) != cudaSuccess) return model_fail(OSAM_ERR_NOMEM, "bn arena");
+    return OSAM_OK;
+  }
+
+  void release() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    exec = nullptr;
+    graph = nullptr;
+    cudaFree(arena);
+    cudaFree(w16);
+    cudaFree(f32);
+    arena = nullptr;
+    w16 = nullptr;
+    f32 = nullptr;
+  }
+
+  // ------------------------------------------------------------------ weights
+  int sync(cudaStream_t st) {
+    for (auto& n : porder)
+      if (!params[n].set) return model_fail(OSAM_ERR_INVALID, "parameter %s was not set", n.c_str());
+    std::vector<float> wst(w16_n, 0.f);  // fp32 staging of the fp16 weight arena
+    std::vector<float> bnst;             // [γ|β|μ|σ²] per CONVBN node, concatenated
+    std::vector<size_t> bn_at(nodes.size(), 0);
+    std::vector<float> fst(f32_n, 0.f);  // biases go straight into the fp32 arena
+    for (size_t ni = 0; ni < nodes.size(); ni++) {
+      MNode& nd = *nodes[ni];
+      if (nd.kind == N_POOL) continue;
+      const int C = nd.in->C, k = nd.k;
+      if (nd.kind == N_CONVBN) {
+        // KRSC: the fused head concatenates its prefixes along K
+        int k0 = 0;
+        bn_at[ni] = bnst.size();
+        bnst.resize(bnst.size() + 4 * (size_t)nd.K);
+        for (size_t pi = 0; pi < nd.pre.size(); pi++) {
+          const PInfo& W = params[nd.pre[pi] + ".conv.weight"];
+          const int Kp = nd.ks[pi];
+          for (int kk = 0; kk < Kp; kk++)
+            for (int r = 0; r < k; r++)
+              for (int s = 0; s < k; s++)
+                for (int c = 0; c < C; c++)
+                  wst[nd.w_off + (((size_t)(k0 + kk) * k + r) * k + s) * C + c] =
+                      W.host[(((size_t)kk * C + c) * k + r) * k + s];
+          const char* bnn[4] = {".bn.weight", ".bn.bias", ".bn.running_mean", ".bn.running_var"};
+          for (int q = 0; q < 4; q++) {
+            const PInfo& B = params[nd.pre[pi] + bnn[q]];
+            for (int kk = 0; kk < Kp; kk++) bnst[bn_at[ni] + (size_t)q * nd.K + k0 + kk] = B.host[kk];
+          }
+          k0 += Kp;
+        }
+      } else if (nd.kind == N_HEAD) {
+        const PInfo& W = params[nd.name + ".weight"];
+        for (int kk = 0; kk < nd.K; kk++)
+          for (int c = 0; c < C; c++) wst[nd.w_off + (size_t)kk * C + c] = W.host[(size_t)kk * C + c];
+        const PInfo& B = params[nd.name + ".bias"];
+        for (int kk = 0; kk < nd.K; kk++) fst[nd.f_off + kk] = B.host[kk];
+      } else {  // N_CONVT: PyTorch (C_in, C_out, 2, 2) → GEMM B rows ((dy·2+dx)·K + k), K-major over C_in
+        const PInfo& W = params[nd.name + ".weight"];
+        for (int c = 0; c < C; c++)
+          for (int kk = 0; kk < nd.K; kk++)
+            for (int dy = 0; dy < 2; dy++)
+              for (int dx = 0; dx < 2; dx++)
+                wst[nd.w_off + ((size_t)(dy * 2 + dx) * nd.K + kk) * C + c] =
+                    W.host[(((size_t)c * nd.K + kk) * 2 + dy) * 2 + dx];
+        const PInfo& B = params[nd.name + ".bias"];
+        for (int kk = 0; kk < nd.K; kk++) fst[nd.f_off + kk] = B.host[kk];
+      }
+    }
+    float* dw = nullptr;
+    float* dbn = nullptr;
+    cudaError_t e;
+    if ((e = cudaMalloc(&dw, wst.size() * sizeof(float))) != cudaSuccess) return model_fail(OSAM_ERR_NOMEM, "staging");
+    if ((e = cudaMalloc(&dbn, std::max<size_t>(bnst.size(), 1) * sizeof(float))) != cudaSuccess) {
+      cudaFree(dw);
+      return model_fail(OSAM_ERR_NOMEM, "staging");
+    }
+    cudaMemcpyAsync(dw, wst.data(), wst.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(dbn, bnst.data(), bnst.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(f32, fst.data(), fst.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    k_f32_to_f16<<<1024, 256, 0, st>>>(dw, w16, (long long)w16_n);
+    for (size_t ni = 0; ni < nodes.size(); ni++) {
+      MNode& nd = *nodes[ni];
+      if (nd.kind != N_CONVBN) continue;
+      k_bn_fold<<<(nd.K + 127) / 128, 128, 0, st>>>(dbn + bn_at[ni], nd.K, bn_eps, f32 + nd.f_off,
+                                                    f32 + nd.f_off + nd.K);
+    }
+    e = cudaStreamSynchronize(st);
+    cudaFree(dw);
+    cudaFree(dbn);
+    if (e != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
+    int rc = prepare_launches();
+    if (rc) return rc;
+    synced = true;
+    if (exec) {  // weights changed: the graph's kernel arguments are unchanged (same buffers), keep it
+    }
+    return OSAM_OK;
+  }
+
+  int prepare_launches() {
+    for (auto& ndp : nodes) {
+      MNode& nd = *ndp;
+      if (nd.kind == N_POOL) {
+        if (sppf_prime() != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "sppf setup");
+        continue;
+      }
+      osam_conv_geom g{N, nd.in->H, nd.in->W, nd.in->C, nd.K, nd.k, nd.k, nd.s, nd.k / 2};
+      if (nd.kind == N_HEAD) g = osam_conv_geom{N, nd.in->H, nd.in->W, nd.in->C, nd.K, 1, 1, 1, 0};
+      if (nd.kind == N_CONVT) g = osam_conv_geom{N, nd.in->H, nd.in->W, nd.in->C, nd.K, 2, 2, 2, 0};
+      osam_conv_plan* plan = nullptr;
+      int rc = osam_conv_plan_create(&g, nd.kind == N_CONVT, &plan);
+      if (rc) return model_fail(rc, "%s: %s", nd.name.c_str(), osam_last_error());
+      nd.plan = *plan;
+      osam_conv_plan_destroy(plan);
+      osam_epilogue ep{};
+      ep.round_z = 1;
+      if (nd.kind == N_CONVBN) {
+        ep.kind = OSAM_EPI_BN_ACT;
+        ep.scale = f32 + nd.f_off;
+        ep.shift = f32 + nd.f_off + nd.K;
+        ep.act = 1;
+        ep.res = nd.res ? nd.res->p : nullptr;
+        ep.n_dest = (int)nd.dests.size();
+        for (size_t i = 0; i < nd.dests.size(); i++) {
+          const MDest& d = nd.dests[i];
+          ep.dest[i] = osam_dest{d.a->p, d.a->C, d.choff, d.c0, d.c1, d.up};
+        }
+      } else {
+        ep.kind = OSAM_EPI_BIAS;
+        ep.bias = f32 + nd.f_off;
+        ep.n_dest = 1;
+        ep.dest[0] = osam_dest{nd.out->p, nd.out->C, 0, 0, nd.K, 1};
+      }
+      rc = conv_prepare(&nd.plan, nd.in->p, w16 + nd.w_off, &ep, 0.f, nullptr, nullptr, 0, &nd.L, true);
+      if (rc) return model_fail(rc, "%s: %s", nd.name.c_str(), osam_last_error());
+      if (conv_prime(nd.L) != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "%s: kernel setup", nd.name.c_str());
+    }
+    return OSAM_OK;
+  }
+
+  cudaError_t run(cudaStream_t st) {
+    for (auto& ndp : nodes) {
+      MNode& nd = *ndp;
+      cudaError_t e = nd.kind == N_POOL ? launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, st)
+                                        : conv_launch(nd.L, st);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+
+  int forward(int use_graph, cudaStream_t st) {
+    if (!synced) return model_fail(OSAM_ERR_INVALID, "forward before osam_model_sync_weights");
+    cudaError_t e;
+    if (!use_graph) {
+      e = run(st);
+      return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
+    }
+    if (!exec) {
+      if ((e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "begin capture: %s", cudaGetErrorString(e));
+      cudaError_t er = run(st);
+      e = cudaStreamEndCapture(st, &graph);
+      if (er != cudaSuccess || e != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "capture: %s", cudaGetErrorString(er != cudaSuccess ? er : e));
+      if ((e = cudaGraphInstantiate(&exec, graph, 0)) != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
+    }
+    e = cudaGraphLaunch(exec, st);
+    return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e));
+  }
+};
+
+namespace osam {
+int model_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  char buf[512];
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  set_last_error("%s", buf);
+  return code;
+}
+}  // namespace osam
+
+namespace {
+int fill_tensor(const osam_model* m, const MAct* a, osam_tensor* t) {
+  if (!a || !t) return model_fail(OSAM_ERR_INVALID, "no such tensor");
+  t->p = a->p;
+  t->n = m->N;
+  t->h = a->H;
+  t->w = a->W;
+  t->c = a->C;
+  return OSAM_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int osam_model_create(int batch, int imgsz, int reg_max, osam_model** out) {
+  if (!out || batch < 1 || imgsz < 32 || imgsz % 32 || reg_max < 1 || reg_max > 64)
+    return model_fail(OSAM_ERR_INVALID, "osam_model_create(batch=%d, imgsz=%d, reg_max=%d)", batch, imgsz, reg_max);
+  *out = nullptr;
+  auto m = std::make_unique<osam_model>();
+  m->N = batch;
+  m->S = imgsz;
+  m->reg_max = reg_max;
+  m->build();
+  int rc = m->allocate();
+  if (rc) {
+    m->release();
+    return rc;
+  }
+  if (!device_error_word()) {
+    m->release();
+    return model_fail(OSAM_ERR_CUDA, "device error word");
+  }
+  *out = m.release();
+  return OSAM_OK;
+}
+
+int osam_model_destroy(osam_model* m) {
+  if (m) {
+    m->release();
+    delete m;
+  }
+  return OSAM_OK;
+}
+
+int osam_model_set_param(osam_model* m, const char* name, const float* data, const int64_t* shape, int ndim) {
+  if (!m || !name || !data || (ndim && !shape)) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  auto it = m->params.find(name);
+  if (it == m->params.end()) return OSAM_OK;  // not a parameter of this graph (e.g. the DFL conv)
+  PInfo& p = it->second;
+  if ((int)p.shape.size() != ndim) return model_fail(OSAM_ERR_INVALID, "%s: rank %d, expected %zu", name, ndim, p.shape.size());
+  size_t n = 1;
+  for (int i = 0; i < ndim; i++) {
+    if (shape[i] != p.shape[i]) return model_fail(OSAM_ERR_INVALID, "%s: shape mismatch at dim %d", name, i);
+    n *= (size_t)shape[i];
+  }
+  p.host.assign(data, data + n);
+  p.set = true;
+  m->synced = false;
+  return OSAM_OK;
+}
+
+int osam_model_load_fsow(osam_model* m, const char* path) {
+  if (!m || !path) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  std::ifstream f(path, std::ios::binary);
+  if (!f.good()) return model_fail(OSAM_ERR_INVALID, "cannot open %s", path);
+  char magic[8];
+  f.read(magic, 8);
+  if (!f.good() || std::memcmp(magic, "FSOW0001", 8)) return model_fail(OSAM_ERR_INVALID, "%s: not an FSOW file", path);
+  uint32_t n = 0;
+  f.read(reinterpret_cast<char*>(&n), 4);
+  static const int isz[3] = {4, 4, 1};
+  for (uint32_t i = 0; i < n && f.good(); i++) {
+    uint16_t ln = 0;
+    f.read(reinterpret_cast<char*>(&ln), 2);
+    std::string name(ln, '\0');
+    f.read(&name[0], ln);
+    uint8_t nd = 0;
+    f.read(reinterpret_cast<char*>(&nd), 1);
+    std::vector<int64_t> shape(nd);
+    f.read(reinterpret_cast<char*>(shape.data()), 8 * nd);
+    uint8_t dt = 0;
+    f.read(reinterpret_cast<char*>(&dt), 1);
+    if (dt > 2) return model_fail(OSAM_ERR_INVALID, "%s: bad dtype", path);
+    size_t cnt = 1;
+    for (auto s : shape) cnt *= (size_t)s;
+    std::vector<char> buf(cnt * isz[dt]);
+    f.read(buf.data(), buf.size());
+    if (!f.good()) return model_fail(OSAM_ERR_INVALID, "%s: truncated", path);
+    if (dt != 0) continue;
+    int rc = osam_model_set_param(m, name.c_str(), reinterpret_cast<const float*>(buf.data()), shape.data(), nd);
+    if (rc) return rc;
+  }
+  return OSAM_OK;
+}
+
+int osam_model_sync_weights(osam_model* m, osam_stream_t stream) {
+  if (!m) return model_fail(OSAM_ERR_INVALID, "NULL model");
+  return m->sync(reinterpret_cast<cudaStream_t>(stream));
+}
+
+int osam_model_input(const osam_model* m, osam_tensor* t) { return m ? fill_tensor(m, m->in, t) : OSAM_ERR_INVALID; }
+
+int osam_model_head(const osam_model* m, int kind, int level, osam_tensor* t) {
+  if (!m || kind < 0 || kind > 2 || level < 0 || level > 2) return model_fail(OSAM_ERR_INVALID, "head(%d,%d)", kind, level);
+  return fill_tensor(m, m->head[kind][level], t);
+}
+
+int osam_model_proto(const osam_model* m, osam_tensor* t) { return m ? fill_tensor(m, m->proto, t) : OSAM_ERR_INVALID; }
+
+int osam_model_act(const osam_model* m, const char* name, osam_tensor* t) {
+  if (!m || !name) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  auto it = m->acts.find(name);
+  if (it == m->acts.end()) return model_fail(OSAM_ERR_INVALID, "no activation %s", name);
+  return fill_tensor(m, it->second.get(), t);
+}
+
+int osam_model_forward(osam_model* m, int use_graph, osam_stream_t stream) {
+  if (!m) return model_fail(OSAM_ERR_INVALID, "NULL model");
+  return m->forward(use_graph, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int osam_model_num_launches(const osam_model* m) { return m ? (int)m->nodes.size() : 0; }
+
+int osam_model_forward_nodes(osam_model* m, int first, int count, osam_stream_t stream) {
+  if (!m || first < 0 || count < 0 || first + count > (int)m->nodes.size())
+    return model_fail(OSAM_ERR_INVALID, "forward_nodes range");
+  if (!m->synced) return model_fail(OSAM_ERR_INVALID, "forward before osam_model_sync_weights");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int i = first; i < first + count; i++) {
+    MNode& nd = *m->nodes[i];
+    cudaError_t e = nd.kind == N_POOL ? launch_sppf(nd.cat->p, m->N, nd.cat->H, nd.cat->W, nd.pc, st)
+                                      : conv_launch(nd.L, st);
+    if (e != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "%s: %s", nd.name.c_str(), cudaGetErrorString(e));
+  }
+  return OSAM_OK;
+}
+
+int osam_model_node_info(const osam_model* m, int i, char* name, int name_len, int* kind, osam_conv_geom* g) {
+  if (!m || i < 0 || i >= (int)m->nodes.size()) return model_fail(OSAM_ERR_INVALID, "node index %d", i);
+  const MNode& nd = *m->nodes[i];
+  if (name && name_len > 0) {
+    std::strncpy(name, nd.name.c_str(), name_len - 1);
+    name[name_len - 1] = 0;
+  }
+  if (kind) *kind = (int)nd.kind;
+  if (g) {
+    if (nd.kind == N_POOL) *g = osam_conv_geom{m->N, nd.cat->H, nd.cat->W, nd.pc, nd.pc, 5, 5, 1, 2};
+    else *g = nd.plan.g;
+  }
+  return OSAM_OK;
+}
+
+}  // extern "C"

@@ -62,14 +62,20 @@ __global__ void __launch_bounds__(256) k_sppf(__half* __restrict__ cat, int H, i
   }
 }
 
-cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st) {
-  const size_t smem = size_t(2) * H * W * kSppfCG * sizeof(__half);
+cudaError_t sppf_prime() {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(k_sppf, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  return cudaSuccess;
+}
+
+cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st) {
+  const size_t smem = size_t(2) * H * W * kSppfCG * sizeof(__half);
+  cudaError_t e = sppf_prime();
+  if (e != cudaSuccess) return e;
   dim3 grid(c / kSppfCG, N);
   k_sppf<<<grid, 256, smem, st>>>(cat, H, W, c);
   return cudaGetLastError();

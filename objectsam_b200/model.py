@@ -1,0 +1,135 @@
+"""Host-side mirror of the reference's Model (src/model.h:97-140) for inference, over the C ABI.
+
+    m = Model(batch=64, imgsz=640)          # Model::build (graph + activation arena)
+    m.load(tensors) / m.load_fsow(path)     # Params::load (PyTorch names, OIHW fp32)
+    m.sync_weights()                        # fp16 KRSC copies + folded eval-mode BN
+    m.input().copy_(images_nhwc_fp16)       # Model::input()->p
+    m.forward()                             # Model::forward(false)
+    m.head(kind, lvl), m.proto()            # raw head tensors (box / cls / coef, proto), NHWC fp16
+
+Tensors returned by input()/head()/proto()/act() are torch CUDA views of the model's own buffers.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import Tensor, check, lib, stream_ptr
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ wrapper so torch can view a buffer owned by the library."""
+
+    def __init__(self, ptr: int, shape, owner):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self._owner = owner
+
+
+class Model:
+    BOX, CLS, COEF = 0, 1, 2
+
+    def __init__(self, batch: int, imgsz: int, reg_max: int = 16):
+        self.batch, self.imgsz, self.reg_max = batch, imgsz, reg_max
+        self._m = ctypes.c_void_p()
+        check(lib().osam_model_create(batch, imgsz, reg_max, ctypes.byref(self._m)))
+
+    def close(self) -> None:
+        if getattr(self, "_m", None):
+            lib().osam_model_destroy(self._m)
+            self._m = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------- parameters
+    def load(self, tensors: dict) -> None:
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32))
+            shape = (ctypes.c_int64 * a.ndim)(*a.shape)
+            check(lib().osam_model_set_param(self._m, name.encode(), a.ctypes.data, shape, a.ndim))
+
+    def load_fsow(self, path: str) -> None:
+        check(lib().osam_model_load_fsow(self._m, path.encode()))
+
+    def sync_weights(self, stream=None) -> None:
+        check(lib().osam_model_sync_weights(self._m, stream_ptr(stream)))
+
+    # ------------------------------------------------------------- tensors
+    def _view(self, t: Tensor):
+        import torch
+        return torch.as_tensor(_DeviceArray(t.p, (t.n, t.h, t.w, t.c), self), device="cuda")
+
+    def input(self):
+        t = Tensor()
+        check(lib().osam_model_input(self._m, ctypes.byref(t)))
+        return self._view(t)
+
+    def head(self, kind: int, lvl: int):
+        t = Tensor()
+        check(lib().osam_model_head(self._m, kind, lvl, ctypes.byref(t)))
+        return self._view(t)
+
+    def proto(self):
+        t = Tensor()
+        check(lib().osam_model_proto(self._m, ctypes.byref(t)))
+        return self._view(t)
+
+    def act(self, name: str):
+        t = Tensor()
+        check(lib().osam_model_act(self._m, name.encode(), ctypes.byref(t)))
+        return self._view(t)
+
+    def tensor_info(self, which: str, kind: int = 0, lvl: int = 0) -> Tensor:
+        t = Tensor()
+        if which == "input":
+            check(lib().osam_model_input(self._m, ctypes.byref(t)))
+        elif which == "head":
+            check(lib().osam_model_head(self._m, kind, lvl, ctypes.byref(t)))
+        else:
+            check(lib().osam_model_proto(self._m, ctypes.byref(t)))
+        return t
+
+    # ------------------------------------------------------------- execution
+    def forward(self, use_graph: bool = False, stream=None) -> None:
+        check(lib().osam_model_forward(self._m, int(use_graph), stream_ptr(stream)))
+
+    @property
+    def handle(self) -> int:
+        return self._m.value
+
+    def num_launches(self) -> int:
+        return lib().osam_model_num_launches(self._m)
+
+    def forward_nodes(self, first: int, count: int, stream=None) -> None:
+        check(lib().osam_model_forward_nodes(self._m, first, count, stream_ptr(stream)))
+
+    def nodes(self) -> list[dict]:
+        """Per node: name, kind (0 conv+BN+SiLU, 1 head conv, 2 transposed conv, 3 SPPF pool), geometry,
+        conv FLOPs (2·N·P·Q·K·C·R·S; the transposed conv counts H·W — the reference's formula,
+        src/model.cpp:483) and minimum HBM bytes (input + weights + every destination write)."""
+        from ._lib import ConvGeom
+        out = []
+        for i in range(self.num_launches()):
+            buf = ctypes.create_string_buffer(128)
+            kind = ctypes.c_int()
+            g = ConvGeom()
+            check(lib().osam_model_node_info(self._m, i, buf, 128, ctypes.byref(kind), ctypes.byref(g)))
+            k = kind.value
+            if k == 3:
+                flops = 0.0
+                nbytes = 2.0 * g.N * g.H * g.W * g.C * 4  # read slice 0, write slices 1..3
+            else:
+                pq = g.H * g.W if k == 2 else g.P() * g.Q()
+                kout = 4 * g.K if k == 2 else g.K
+                flops = 2.0 * g.N * pq * g.K * g.C * g.R * g.S
+                nbytes = 2.0 * (g.N * g.H * g.W * g.C + kout * g.R * g.S * g.C / (4 if k == 2 else 1)
+                                + g.N * pq * kout)
+            out.append(dict(index=i, name=buf.value.decode(), kind=k, N=g.N, H=g.H, W=g.W, C=g.C, K=g.K, R=g.R,
+                            S=g.S, stride=g.stride, flops=flops, bytes=nbytes))
+        return out

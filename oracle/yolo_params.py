@@ -77,9 +77,11 @@ def param_shapes():
     return shapes
 
 
-def make_weights(seed: int = 0, random_bn: bool = False) -> dict:
-    """Seeded weights: He-normal convs (std √(2/fan_in)), BN γ=1 β=0 μ=0 σ²=1 unless
-    random_bn, head/upsample biases U(-0.1, 0.1).  numpy PCG64 → identical on every machine."""
+def make_weights(seed: int = 0, random_bn: bool = False, gain: float = 1.0) -> dict:
+    """Seeded weights: He-normal convs (std gain·√(2/fan_in); gain 1 = BASELINE config 1), BN γ=1 β=0 μ=0
+    σ²=1 unless random_bn, head/upsample biases U(-0.1, 0.1).  numpy PCG64 → identical on every machine.
+    Parity tests use gain ≈ 1.2 so activations stay O(1) through the 70 convs (SiLU loses variance that
+    ReLU-calibrated He init does not restore)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     out = {}
     for name, shape in param_shapes().items():
@@ -88,7 +90,7 @@ def make_weights(seed: int = 0, random_bn: bool = False) -> dict:
                 fan_in = shape[0] * shape[2] * shape[3]
             else:
                 fan_in = shape[1] * shape[2] * shape[3]
-            out[name] = (rng.standard_normal(shape) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+            out[name] = (rng.standard_normal(shape) * (gain * np.sqrt(2.0 / fan_in))).astype(np.float32)
         elif name.endswith(".bias") and not name.endswith("bn.bias"):
             out[name] = rng.uniform(-0.1, 0.1, shape).astype(np.float32)
         elif name.endswith("bn.weight"):

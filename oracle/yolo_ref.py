@@ -25,8 +25,10 @@ BN_EPS = 1e-3
 
 
 class YoloSegRef:
-    def __init__(self, weights: dict, emulate_fp16: bool = True, dtype=torch.float32, device="cpu"):
+    def __init__(self, weights: dict, emulate_fp16: bool = True, dtype=torch.float32, device="cpu",
+                 calibrate: bool = False):
         self.fp16 = emulate_fp16
+        self.calibrate = calibrate
         self.dtype = dtype
         self.device = device
         self.w = {}
@@ -45,6 +47,9 @@ class YoloSegRef:
     def conv_bn(self, x, name, k, s, res=None, keep=None):
         w = self.w[f"{name}.conv.weight"]
         z = self._r(F.conv2d(x, w, stride=s, padding=k // 2))
+        if self.calibrate:  # running stats ← this batch's per-channel statistics (like a trained net)
+            self.w[f"{name}.bn.running_mean"] = z.mean((0, 2, 3))
+            self.w[f"{name}.bn.running_var"] = z.var((0, 2, 3), unbiased=False)
         g, b = self.w[f"{name}.bn.weight"], self.w[f"{name}.bn.bias"]
         rm, rv = self.w[f"{name}.bn.running_mean"], self.w[f"{name}.bn.running_var"]
         scale = (g.float() * torch.rsqrt(rv.float() + BN_EPS)).to(self.dtype)
@@ -122,6 +127,20 @@ class YoloSegRef:
         pr = self.conv_bn(up, "model.22.proto.cv2", 3, 1)
         out["proto"] = self.conv_bn(pr, "model.22.proto.cv3", 1, 1)
         return out
+
+
+def calibrated_weights(seed: int = 0, size: int = 128, n: int = 2) -> dict:
+    """Seeded test weights whose BN running statistics are set from a calibration batch, so every layer
+    sees normalised inputs and the activations stay O(1) through the network (random He-init weights with
+    identity BN shrink or blow up with depth).  γ ~ U(0.5, 1.5), β ~ U(-0.2, 0.2)."""
+    w = P.make_weights(seed, random_bn=True)
+    m = YoloSegRef(w, emulate_fp16=False, calibrate=True)
+    m.forward(P.make_images(n, size, seed + 7))
+    out = dict(w)
+    for k, v in m.w.items():
+        if "running" in k:
+            out[k] = v.detach().cpu().numpy().astype(np.float32)
+    return out
 
 
 def forward_flops(size: int = 640) -> float:

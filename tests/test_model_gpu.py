@@ -1,0 +1,89 @@
+"""Whole-network parity: the fused sm_100a forward (C ABI osam_model_*) vs the CPU oracle (oracle/yolo_ref.py,
+which emulates the reference's fp16 storage points).
+
+Tolerance (north star: max relative error 1e-2, MAE 1e-3), normalised by each tensor's scale:
+    max|y − ref| ≤ 1e-2·max|ref|   and   mean|y − ref| ≤ 1e-3·max|ref|.
+"""
+import numpy as np
+import pytest
+import torch
+
+from objectsam_b200.model import Model
+from oracle import yolo_params, yolo_ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(name, y_nhwc, ref_nchw, max_rel=1e-2, mae_rel=1e-3):
+    y = y_nhwc.float().cpu().permute(0, 3, 1, 2)
+    r = ref_nchw.float()
+    scale = r.abs().max().item() + 1e-6
+    d = (y - r).abs()
+    assert d.max().item() <= max_rel * scale, f"{name}: max err {d.max().item():.3e} vs scale {scale:.3e}"
+    assert d.mean().item() <= mae_rel * scale, f"{name}: mean err {d.mean().item():.3e} vs scale {scale:.3e}"
+
+
+def _run(weights, imgs, use_graph=False):
+    N, S = imgs.shape[0], imgs.shape[1]
+    m = Model(N, S)
+    m.load(weights)
+    m.sync_weights()
+    m.input().copy_(torch.from_numpy(imgs).half())
+    m.forward(use_graph=use_graph)
+    torch.cuda.synchronize()
+    return m
+
+
+@pytest.mark.parametrize("N,S,seed", [(2, 128, 3), (1, 256, 5)])
+def test_forward_matches_oracle_calibrated(cuda_lib, N, S, seed):
+    w = yolo_ref.calibrated_weights(seed, 128)
+    imgs = yolo_params.make_images(N, S, seed + 100)
+    m = _run(w, imgs)
+    ref = yolo_ref.YoloSegRef(w, emulate_fp16=True)
+    out = ref.forward(imgs)
+    for name in ("a0", "a1", "a2", "a3", "a4", "a5", "a6", "a7", "a8", "p3", "p4", "p5"):
+        _check(name, m.act(name), ref.acts[name])
+    for l in range(3):
+        _check(f"box{l}", m.head(0, l), out["box"][l])
+        _check(f"cls{l}", m.head(1, l), out["cls"][l])
+        _check(f"coef{l}", m.head(2, l), out["coef"][l])
+    _check("proto", m.proto(), out["proto"])
+
+
+def test_forward_baseline_config_640(cuda_lib):
+    """BASELINE config 1 weights (He-normal, identity BN) at 640×640."""
+    w = yolo_params.make_weights(0)
+    imgs = yolo_params.make_images(1, 640, 0)
+    m = _run(w, imgs)
+    out = yolo_ref.YoloSegRef(w, emulate_fp16=True).forward(imgs)
+    for l in range(3):
+        _check(f"box{l}", m.head(0, l), out["box"][l])
+        _check(f"cls{l}", m.head(1, l), out["cls"][l])
+        _check(f"coef{l}", m.head(2, l), out["coef"][l])
+    _check("proto", m.proto(), out["proto"])
+
+
+def test_graph_replay_is_bit_identical(cuda_lib):
+    w = yolo_ref.calibrated_weights(1, 128)
+    imgs = yolo_params.make_images(4, 160, 9)
+    m = _run(w, imgs)
+    eager = [m.head(k, l).clone() for k in range(3) for l in range(3)] + [m.proto().clone()]
+    m.forward(use_graph=True)
+    m.forward(use_graph=True)
+    torch.cuda.synchronize()
+    graph = [m.head(k, l) for k in range(3) for l in range(3)] + [m.proto()]
+    for a, b in zip(eager, graph):
+        assert torch.equal(a, b)
+    assert m.num_launches() == 70 + 1  # 70 conv nodes (reference count) + the SPPF pool
+
+
+def test_batch_rows_are_independent(cuda_lib):
+    """Image i of a batch gives the same result as image i alone (no cross-image leakage in the tiling)."""
+    w = yolo_ref.calibrated_weights(2, 128)
+    imgs = yolo_params.make_images(3, 96, 4)
+    mb = _run(w, imgs)
+    m1 = _run(w, imgs[1:2])
+    for k in range(3):
+        for l in range(3):
+            assert torch.equal(mb.head(k, l)[1:2], m1.head(k, l))
+    assert torch.equal(mb.proto()[1:2], m1.proto())
