@@ -103,6 +103,7 @@ struct osam_model {
   bool synced = false;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  cudaStream_t cap = nullptr;  // private stream the graph is recorded on (the legacy stream cannot capture)
 
   // ------------------------------------------------------------------ graph construction
   MAct* act(const std::string& n, int C, int H, int W) {
@@ -301,8 +302,10 @@ struct osam_model {
   void release() {
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
+    if (cap) cudaStreamDestroy(cap);
     exec = nullptr;
     graph = nullptr;
+    cap = nullptr;
     cudaFree(arena);
     cudaFree(w16);
     cudaFree(f32);
@@ -451,10 +454,13 @@ struct osam_model {
       return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
     }
     if (!exec) {
-      if ((e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+      // Record on the model's own stream; recording does not execute, so no ordering with `st` is needed.
+      if (!cap && (e = cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking)) != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "capture stream: %s", cudaGetErrorString(e));
+      if ((e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
         return model_fail(OSAM_ERR_CUDA, "begin capture: %s", cudaGetErrorString(e));
-      cudaError_t er = run(st);
-      e = cudaStreamEndCapture(st, &graph);
+      cudaError_t er = run(cap);
+      e = cudaStreamEndCapture(cap, &graph);
       if (er != cudaSuccess || e != cudaSuccess)
         return model_fail(OSAM_ERR_CUDA, "capture: %s", cudaGetErrorString(er != cudaSuccess ? er : e));
       if ((e = cudaGraphInstantiate(&exec, graph, 0)) != cudaSuccess)
