@@ -96,6 +96,22 @@ int osam_conv_fwd(const osam_conv_plan* plan, const void* x, const void* w, void
 int osam_conv_fwd_fused(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep,
                         void* ws, size_t ws_bytes, osam_stream_t stream);
 
+/* Transposed-conv forward that allocates nothing and takes no workspace: same result as
+ * osam_conv_fwd on a transposed plan, but the weights' re-laid-out copy goes to a fixed device array
+ * inside the library instead of a caller-provided workspace.  It has no counterpart in the reference
+ * (its ConvOp always receives a workspace from the caller).  It is meant for callers that cannot
+ * allocate device memory or hand out a workspace: a host that owns the whole device budget and gives
+ * a plugin only a stream, or a loop that must never reach the allocator because cudaMalloc can
+ * synchronise the device.
+ * Limit: C_in · 4 · C_out fp16 weights ≤ 256 KiB (C_in · C_out ≤ 32768, e.g. 128 → 128); larger plans
+ * return OSAM_ERR_INVALID.  Every GPU that loads the library holds the 256 KiB array until exit.
+ * The array is shared by all calls on a device and keeps the last call's contents: calls that overlap
+ * on the GPU (e.g. on two streams) race on it.  The first call on each device looks the array's device
+ * address up (cudaGetSymbolAddress) with that device current; make that first call before any stream
+ * capture begins.  Needs a transposed plan (OSAM_ERR_INVALID otherwise). */
+int osam_convt_fwd_static_scratch(const osam_conv_plan* plan, const void* x, const void* w, void* y, float beta,
+                                  osam_stream_t stream);
+
 /* SPPF pooling: with cv1's output in channels [0,c) of cat (N×H×W×4c), writes the three chained
  * 5×5/s1/p2 max-pools into slices 1..3.  Replaces sppf_pool_fwd (src/misc.cuh:6, src/misc.cu:149-153). */
 int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);

@@ -199,7 +199,7 @@ static int fill_dest(const osam_dest& s, int kout, DestDev* d, int transposed) {
 }
 
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
-                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready) {
+                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word) {
   if (!p || !x || !w) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
   *L = ConvLaunch{};
@@ -216,7 +216,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   d.ntn = p->ntn;
   d.nkc = p->nkc;
   d.nk = p->nk;
-  d.err = device_error_word();
+  d.err = err_word ? err_word : device_error_word();
   if (!d.err) return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
 
   // ---- epilogue
@@ -393,6 +393,7 @@ int osam_device_error(void) {
   int v = 0;
   e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "osam_device_error read");
+  if (!v) v = static_scratch_take_error();
   if (v) {
     cudaMemset(w, 0, sizeof(int));
     set_last_error("device kernel reported error %d", v);

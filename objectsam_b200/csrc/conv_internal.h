@@ -65,8 +65,10 @@ struct ConvLaunch {
 };
 
 // Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
+// err_word: device word the kernels report timeouts to (nullptr = the library's per-device word).
 int conv_prepare(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep, float beta,
-                 void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready = false);
+                 void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready = false,
+                 int* err_word = nullptr);
 cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st);
 // One-time per-kernel set-up (dynamic shared-memory opt-in) without launching: call before capturing.
 cudaError_t conv_prime(const ConvLaunch& L);
@@ -79,6 +81,7 @@ cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
 
 int* device_error_word();       // per-device error word (allocated on first use, before any capture)
+int static_scratch_take_error();  // error recorded by the static-scratch entry point's kernels (and clear it)
 void set_last_error(const char* fmt, ...);
 
 }  // namespace osam
