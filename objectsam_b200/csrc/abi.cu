@@ -166,6 +166,7 @@ static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p)
         return fail(OSAM_ERR_UNSUPPORTED, "conv stride %d with H=%d W=%d", g->stride, g->H, g->W);
     }
   }
+  if (p->gemm_n > 512) return fail(OSAM_ERR_UNSUPPORTED, "more than 512 GEMM output columns (%d)", p->gemm_n);
   p->BN = choose_bn(p->gemm_n);
   if (p->mode == A_STEM && p->BN > 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C conv: K <= 64 required");
   p->ntn = (int)cdivll(p->gemm_n, p->BN);
@@ -214,6 +215,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   d.tn = p->tn; d.th = p->th; d.tw = p->tw; d.tiles_q = p->tiles_q; d.tiles_p = p->tiles_p;
   d.M = p->M;
   d.ntn = p->ntn;
+  d.tiles_m = p->tiles_m;
   d.nkc = p->nkc;
   d.nk = p->nk;
   d.err = err_word ? err_word : device_error_word();

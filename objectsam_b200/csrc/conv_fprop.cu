@@ -1,36 +1,41 @@
 // Forward convolution as an implicit GEMM on the sm_100a tensor cores.
 //
 //   GEMM M = output pixels (a 128-pixel tile: tn images × th rows × tw columns, or 128 consecutive rows
-//            of the [N·H·W, C] matrix for 1×1 convs), GEMM N = output channels (BN per CTA),
+//            of the [N·H·W, C] matrix for 1×1 convs), GEMM N = output channels (BN per tile),
 //   GEMM K = taps × input channels, walked as (tap, BK-channel chunk) steps.
 //
-// One CTA = one output tile, 6 warps:
-//   warp 0      TMA producer: per K-step one A box (the input window of this tap, zero-filled halo)
-//               and one B box (the KRSC weight rows of this tap/chunk) into a STAGES-deep ring;
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instruction),
-//               fp32 accumulator in TMEM; tcgen05.commit frees ring slots and signals the epilogue;
+// Persistent kernel: each CTA walks the tile list (tile = blockIdx.x + i·gridDim.x, output-channel tile
+// fastest so neighbouring CTAs share their A windows in L2) with 6 warps:
+//   warp 0      TMA producer: per K-step one A box (the input window of this tap, halo = TMA zero fill)
+//               and one B box (KRSC weight rows) into a STAGES-deep ring; it runs ahead across tiles;
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16), accumulating into
+//               one of TWO TMEM buffers, so the MMAs of tile i+1 overlap the epilogue of tile i;
 //   warps 2..5  epilogue: tcgen05.ld of the 128×BN accumulator, folded BN + SiLU (+ residual) or bias,
 //               fp16 conversion and the multi-destination store (channel slices, 2× nearest upsample)
 //               that replaces the reference's separate bn_forward_apply / add_bias passes.
-// The operand tiles are K-major with the TMA swizzle (128 B rows when BK = 64, 64 B rows when BK = 32)
-// that the UMMA shared-memory descriptor expects.  No multicast is used anywhere.
+// Operand tiles are K-major with the TMA swizzle (128 B rows for BK = 64, 64 B rows for BK = 32) the UMMA
+// shared-memory descriptor expects.  No multicast anywhere.  Every wait is bounded (sm100.cuh).
 #include "epilogue.cuh"
 
 namespace osam {
+
+constexpr int kMaxGemmN = 512;  // per-column epilogue constants cached in shared memory
 
 template <int BK, int BN>
 struct FpropCfg {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // ≤ 128 output channels: two CTAs per SM (one's epilogue overlaps the other's main loop);
-  // wider tiles: one CTA per SM with a deeper ring.
+  // ≤ 128 output channels: two CTAs per SM (2 × 2 × 128 TMEM columns); wider tiles: one CTA per SM.
   static constexpr int RING_BUDGET = BN <= 128 ? 96 * 1024 : 190 * 1024;
   static constexpr int STAGES_RAW = RING_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
-  static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   static constexpr int ROW_BYTES = BK * 2;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 3 * BN * 4;
+  static constexpr int CONST_BYTES = 3 * kMaxGemmN * 4;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + CONST_BYTES;
+  static constexpr int CTAS_PER_SM = BN <= 128 ? 2 : 1;
 };
 
 template <int BK, int BN, int MODE>
@@ -44,35 +49,25 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sB = base + STAGES * Cfg::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accb = empty + STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA → epilogue)
+  uint64_t* acce = accf + 2;        // [2] accumulator drained (epilogue → MMA), 4 arrivals
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
   float* s_sc = reinterpret_cast<float*>(base + STAGES * Cfg::STAGE_BYTES + 256);
-  float* s_sh = s_sc + BN;
-  float* s_bi = s_sh + BN;
+  float* s_sh = s_sc + kMaxGemmN;
+  float* s_bi = s_sh + kMaxGemmN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = blockIdx.x % d.ntn;
-  const int mt = blockIdx.x / d.ntn;
-  const int n0 = nt * BN;
-
-  long long m0 = 0;
-  int q0 = 0, p0 = 0, b0 = 0;
-  if (MODE == A_GEMM) {
-    m0 = (long long)mt * 128;
-  } else {
-    const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-    const int tp = rest % d.tiles_p, tb_ = rest / d.tiles_p;
-    q0 = tq * d.tw;
-    p0 = tp * d.th;
-    b0 = tb_ * d.tn;
-  }
+  const int ntiles = d.tiles_m * d.ntn;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(accb, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 4);
+    }
     fence_barrier_init();
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
@@ -81,87 +76,119 @@ __global__ void __launch_bounds__(192, 1)
     tmem_alloc(tslot, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp >= 2) load_epilogue_consts(d.ep, d.gemm_n, n0, BN, threadIdx.x - 64, 128, s_sc, s_sh, s_bi);
+  if (warp >= 2) load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 128, s_sc, s_sh, s_bi);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      for (int kb = 0; kb < d.nk; kb++) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES && !mbar_wait(empty + s, ((kb / STAGES) - 1) & 1, d.err)) break;
-        mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
-        const int tap = kb / d.nkc, cc = (kb - tap * d.nkc) * BK;
-        uint8_t* a = sA + s * Cfg::A_BYTES;
-        uint8_t* b = sB + s * Cfg::B_BYTES;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
+        int q0 = 0, p0 = 0, b0 = 0, m0 = 0;
         if (MODE == A_GEMM) {
-          tma_load_2d(a, &ta, full + s, cc, (int)m0);
+          m0 = mt * 128;
         } else {
-          const int r = tap / d.S, c = tap - r * d.S;
-          if (MODE == A_S1) {
-            tma_load_4d(a, &ta, full + s, cc, q0 + c - d.pad, p0 + r - d.pad, b0);
-          } else {
-            const int dr = r - d.pad, dc = c - d.pad;
-            tma_load_5d(a, &ta, full + s, (dc & 1) * d.C + cc, q0 + (dc >> 1), dr & 1, p0 + (dr >> 1), b0);
-          }
+          const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
+          q0 = tq * d.tw;
+          p0 = (rest % d.tiles_p) * d.th;
+          b0 = (rest / d.tiles_p) * d.tn;
         }
-        tma_load_2d(b, &tb, full + s, tap * d.C + cc, n0);
+        for (int kb = 0; kb < d.nk; kb++, it++) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
+          const int tap = kb / d.nkc, cc = (kb - tap * d.nkc) * BK;
+          uint8_t* a = sA + s * Cfg::A_BYTES;
+          uint8_t* b = sB + s * Cfg::B_BYTES;
+          if (MODE == A_GEMM) {
+            tma_load_2d(a, &ta, full + s, cc, m0);
+          } else {
+            const int r = tap / d.S, c = tap - r * d.S;
+            if (MODE == A_S1) {
+              tma_load_4d(a, &ta, full + s, cc, q0 + c - d.pad, p0 + r - d.pad, b0);
+            } else {
+              const int dr = r - d.pad, dc = c - d.pad;
+              tma_load_5d(a, &ta, full + s, (dc & 1) * d.C + cc, q0 + (dc >> 1), dr & 1, p0 + (dr >> 1), b0);
+            }
+          }
+          tma_load_2d(b, &tb, full + s, tap * d.C + cc, n0);
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      uint32_t it = 0, lt = 0;
       bool ok = true;
-      for (int kb = 0; kb < d.nk; kb++) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(full + s, (kb / STAGES) & 1, d.err)) {
-          ok = false;
-          break;
-        }
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
+        const uint32_t buf = lt & 1;
+        if (lt >= 2 && !mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err)) break;
         tc_fence_after();
-        const uint32_t a = smem_u32(sA + s * Cfg::A_BYTES), b = smem_u32(sB + s * Cfg::B_BYTES);
+        const uint32_t dt = tmem + buf * Cfg::ACC_COLS;
+        for (int kb = 0; kb < d.nk; kb++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(full + s, (it / STAGES) & 1, d.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + s * Cfg::A_BYTES), b = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / 16; k++)
-          umma_f16(tmem, smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES), smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES),
-                   idesc, (kb | k) != 0);
-        umma_commit(empty + s);
+          for (int k = 0; k < BK / 16; k++)
+            umma_f16(dt, smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES), smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES),
+                     idesc, (kb | k) != 0);
+          umma_commit(empty + s);
+        }
+        if (ok) umma_commit(accf + buf);
       }
-      if (ok) umma_commit(accb);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const EpiDev& e = d.ep;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
-    bool valid;
-    long long pix;
-    int n, p, q;
-    if (MODE == A_GEMM) {
-      const long long m = m0 + row;
-      valid = m < d.M;
-      pix = m;
-      q = (int)(m % d.Q);
-      const long long t = m / d.Q;
-      p = (int)(t % d.P);
-      n = (int)(t / d.P);
-    } else {
-      const int thw = d.th * d.tw;
-      const int ni = row / thw, rr = row - ni * thw, i = rr / d.tw, j = rr - i * d.tw;
-      n = b0 + ni;
-      p = p0 + i;
-      q = q0 + j;
-      valid = n < d.N && p < d.P && q < d.Q;
-      pix = ((long long)n * d.P + p) * d.Q + q;
-    }
-    const bool ok = mbar_wait(accb, 0, d.err);
-    tc_fence_after();
-    if (ok) {
+    uint32_t lt = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+      const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
+      bool valid;
+      long long pix;
+      int n, p, q;
+      if (MODE == A_GEMM) {
+        const long long m = (long long)mt * 128 + row;
+        valid = m < d.M;
+        pix = m;
+        q = (int)(m % d.Q);
+        const long long tt = m / d.Q;
+        p = (int)(tt % d.P);
+        n = (int)(tt / d.P);
+      } else {
+        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
+        const int thw = d.th * d.tw;
+        const int ni = row / thw, rr = row - ni * thw, i = rr / d.tw, j = rr - i * d.tw;
+        n = (rest / d.tiles_p) * d.tn + ni;
+        p = (rest % d.tiles_p) * d.th + i;
+        q = tq * d.tw + j;
+        valid = n < d.N && p < d.P && q < d.Q;
+        pix = ((long long)n * d.P + p) * d.Q + q;
+      }
+      const uint32_t buf = lt & 1;
+      const bool ok = mbar_wait(accf + buf, (lt >> 1) & 1, d.err);
+      tc_fence_after();
+      if (!ok) break;
+      const uint32_t dt = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
       for (int jc = 0; jc < BN / 16; jc++) {
         __syncwarp();
         float v[16];
-        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + jc * 16, v);
+        tmem_ld16(dt + jc * 16, v);
         const int col0 = n0 + jc * 16;
         if (!valid || col0 >= d.gemm_n) continue;
 #pragma unroll
@@ -172,9 +199,12 @@ __global__ void __launch_bounds__(192, 1)
           float y[8];
 #pragma unroll
           for (int i = 0; i < 8; i++) y[i] = v[h * 8 + i];
-          epilogue8(e, d.K, d.P, d.Q, y, cnt, col, jc * 16 + h * 8, s_sc, s_sh, s_bi, pix, n, p, q);
+          epilogue8(e, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, pix, n, p, q);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce + buf);
     }
   }
   tc_fence_before();
@@ -198,7 +228,16 @@ static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_o
     attr_set = true;
   }
   if (prime_only) return cudaSuccess;
-  k_conv_fprop<BK, BN, MODE><<<L.grid, 192, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int cap = sms * Cfg::CTAS_PER_SM;
+  const int grid = L.grid < cap ? L.grid : cap;
+  k_conv_fprop<BK, BN, MODE><<<grid, 192, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
   return cudaGetLastError();
 }
 

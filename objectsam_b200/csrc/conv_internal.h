@@ -45,6 +45,7 @@ struct ConvDev {
   int tiles_q, tiles_p;       // spatial tiles along Q and P
   long long M;                // N·P·Q (GEMM M) — for the transposed conv N·H·W
   int ntn;                    // tiles along GEMM N
+  int tiles_m;                // tiles along GEMM M
   int nkc;                    // channel chunks per tap
   int nk;                     // K iterations = taps · nkc
   int* err;                   // device error word

@@ -7,7 +7,9 @@
 
 namespace osam {
 
-__device__ __forceinline__ float silu_f(float y) { return y * (1.f / (1.f + __expf(-y))); }
+// SiLU with the fast exponential and division the reference's fast-math build also uses
+// (CMakeLists.txt:11 --use_fast_math, src/bn.cu:35).
+__device__ __forceinline__ float silu_f(float y) { return __fdividef(y, 1.f + __expf(-y)); }
 
 // Store `cnt` (≤ 8) consecutive output channels starting at `k` of one output pixel to every destination
 // whose channel range holds them.  `pix` indexes the P×Q output grid; (n, p, q) locate it for the 2×
