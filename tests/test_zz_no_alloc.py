@@ -46,10 +46,10 @@ def test_static_scratch_matches_workspace_path_twice(cuda_lib):
 
 
 def test_static_scratch_rejects_oversize_plans(cuda_lib):
-    op = ConvOp().init(ConvGeom(1, 4, 4, 256, 256, 2, 2, 2, 0), transposed=True)  # 512 KiB of weights
-    x = torch.zeros(1, 4, 4, 256, dtype=torch.half, device=DEV)
-    w = torch.zeros(256, 2, 2, 256, dtype=torch.half, device=DEV)
-    y = torch.zeros(1, 8, 8, 256, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(1, 4, 4, 512, 128, 2, 2, 2, 0), transposed=True)  # 512 KiB of weights
+    x = torch.zeros(1, 4, 4, 512, dtype=torch.half, device=DEV)
+    w = torch.zeros(512, 2, 2, 128, dtype=torch.half, device=DEV)
+    y = torch.zeros(1, 8, 8, 128, dtype=torch.half, device=DEV)
     rc = _lib.lib().osam_convt_fwd_static_scratch(op._plan, x.data_ptr(), w.data_ptr(), y.data_ptr(), 0.0,
                                                   _lib.stream_ptr())
     assert rc == _lib.OSAM_ERR_INVALID
