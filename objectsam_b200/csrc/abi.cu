@@ -170,7 +170,26 @@ static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p)
   p->BN = choose_bn(p->gemm_n);
   if (p->mode == A_STEM && p->BN > 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C conv: K <= 64 required");
   p->ntn = (int)cdivll(p->gemm_n, p->BN);
-  if (p->mode == A_S1 || p->mode == A_S2) {
+  if (p->mode == A_STEM) {
+    // one image per tile, th × tw = 128 output pixels; the input window must fit 48 KiB of shared memory
+    long long best = -1;
+    for (int tw = 128; tw >= 16; tw /= 2) {
+      const int th = 128 / tw;
+      const long long wbytes = (long long)((th - 1) * g->stride + g->R) * ((tw - 1) * g->stride + g->S) * g->C * 2;
+      if (wbytes > 48 * 1024) continue;
+      const long long cost = cdivll(p->Q, tw) * cdivll(p->P, th);
+      if (best < 0 || cost < best) {
+        best = cost;
+        p->tw = tw;
+        p->th = th;
+      }
+    }
+    if (best < 0) return fail(OSAM_ERR_UNSUPPORTED, "small-C conv: input window too large");
+    p->tn = 1;
+    p->tiles_q = (int)cdivll(p->Q, p->tw);
+    p->tiles_p = (int)cdivll(p->P, p->th);
+    p->tiles_m = (int)(p->tiles_q * (long long)p->tiles_p * g->N);
+  } else if (p->mode == A_S1 || p->mode == A_S2) {
     choose_tile(g->N, p->P, p->Q, &p->tn, &p->th, &p->tw);
     p->tiles_q = (int)cdivll(p->Q, p->tw);
     p->tiles_p = (int)cdivll(p->P, p->th);
@@ -253,6 +272,17 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
       int rc = fill_dest(ep->dest[i], g.K, &e.dest[i], p->transposed);
       if (rc) return rc;
     }
+  }
+
+  // ---- warp-cooperative epilogue: every destination 8-channel aligned, tiles fully inside the GEMM N
+  {
+    bool coop = (p->gemm_n % p->BN == 0) && (p->BN % 16 == 0) && e.beta == 0.f;
+    for (int i = 0; i < e.ndest; i++) coop = coop && e.dest[i].vec;
+    if (e.shuffle) coop = coop && (e.kout % 32 == 0);
+    if (e.res) coop = coop && (g.K % 8 == 0);
+    if (p->mode == A_STEM) coop = coop && (p->BN == 32 || p->BN == 16 || p->BN == 64);
+    if (p->mode != A_STEM && p->mode != A_GEMM) coop = coop && (p->P < 65536 && p->Q < 65536);
+    e.coop = coop;
   }
 
   // ---- operands

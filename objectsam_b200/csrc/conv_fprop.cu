@@ -4,15 +4,17 @@
 //            of the [N·H·W, C] matrix for 1×1 convs), GEMM N = output channels (BN per tile),
 //   GEMM K = taps × input channels, walked as (tap, BK-channel chunk) steps.
 //
-// Persistent kernel: each CTA walks the tile list (tile = blockIdx.x + i·gridDim.x, output-channel tile
-// fastest so neighbouring CTAs share their A windows in L2) with 6 warps:
+// Persistent kernel, one CTA per SM: each CTA walks the tile list (tile = blockIdx.x + i·gridDim.x,
+// output-channel tile fastest so neighbouring CTAs share their A windows in L2) with 10 warps:
 //   warp 0      TMA producer: per K-step one A box (the input window of this tap, halo = TMA zero fill)
 //               and one B box (KRSC weight rows) into a STAGES-deep ring; it runs ahead across tiles;
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16), accumulating into
 //               one of TWO TMEM buffers, so the MMAs of tile i+1 overlap the epilogue of tile i;
-//   warps 2..5  epilogue: tcgen05.ld of the 128×BN accumulator, folded BN + SiLU (+ residual) or bias,
-//               fp16 conversion and the multi-destination store (channel slices, 2× nearest upsample)
-//               that replaces the reference's separate bn_forward_apply / add_bias passes.
+//   warps 2..9  epilogue: two warps per TMEM lane quadrant, each taking half of the tile's columns:
+//               tcgen05.ld, folded BN + SiLU (+ residual) or bias, fp16 conversion and the
+//               multi-destination store (channel slices, 2× nearest upsample) — written back through a
+//               per-warp shared-memory stage so that each store instruction covers whole pixel rows
+//               (epilogue.cuh).  This replaces the reference's separate bn_forward_apply / add_bias passes.
 // Operand tiles are K-major with the TMA swizzle (128 B rows for BK = 64, 64 B rows for BK = 32) the UMMA
 // shared-memory descriptor expects.  No multicast anywhere.  Every wait is bounded (sm100.cuh).
 #include "epilogue.cuh"
@@ -26,20 +28,23 @@ struct FpropCfg {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // ≤ 128 output channels: two CTAs per SM (2 × 2 × 128 TMEM columns); wider tiles: one CTA per SM.
-  static constexpr int RING_BUDGET = BN <= 128 ? 96 * 1024 : 190 * 1024;
+  // One CTA per SM: the ring takes what the stage/constant areas leave of the 227 KiB.
+  static constexpr int RING_BUDGET = 196 * 1024;
   static constexpr int STAGES_RAW = RING_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   static constexpr int ROW_BYTES = BK * 2;
   static constexpr int CONST_BYTES = 3 * kMaxGemmN * 4;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + CONST_BYTES;
-  static constexpr int CTAS_PER_SM = BN <= 128 ? 2 : 1;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int STAGE_OUT_BYTES = EPI_WARPS * 32 * 64;  // per-warp epilogue stage
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + CONST_BYTES + STAGE_OUT_BYTES;
+  static constexpr int CTAS_PER_SM = 1;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
 template <int BK, int BN, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const ConvDev d) {
   using Cfg = FpropCfg<BK, BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -50,11 +55,12 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA → epilogue)
-  uint64_t* acce = accf + 2;        // [2] accumulator drained (epilogue → MMA), 4 arrivals
+  uint64_t* acce = accf + 2;        // [2] accumulator drained (epilogue → MMA), one arrival per epilogue warp
   uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
   float* s_sc = reinterpret_cast<float*>(base + STAGES * Cfg::STAGE_BYTES + 256);
   float* s_sh = s_sc + kMaxGemmN;
   float* s_bi = s_sh + kMaxGemmN;
+  uint8_t* s_stage = reinterpret_cast<uint8_t*>(s_bi + kMaxGemmN);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = d.tiles_m * d.ntn;
@@ -66,7 +72,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(accf + b, 1);
-      mbar_init(acce + b, 4);
+      mbar_init(acce + b, Cfg::EPI_WARPS);
     }
     fence_barrier_init();
     tma_prefetch_desc(&ta);
@@ -76,7 +82,8 @@ __global__ void __launch_bounds__(192, 1)
     tmem_alloc(tslot, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp >= 2) load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 128, s_sc, s_sh, s_bi);
+  if (warp >= 2)
+    load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 32 * Cfg::EPI_WARPS, s_sc, s_sh, s_bi);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
@@ -151,10 +158,15 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    // ---------------------------------------------------------------- epilogue (warps 2..9)
     const EpiDev& e = d.ep;
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int ew = warp - 2;                 // 0..7
+    const int quad = warp & 3;               // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;                // which half of the tile's columns
     const int row = quad * 32 + lane;
+    const int cols = BN >= 32 ? BN / 2 : (half == 0 ? BN : 0);
+    const int cbeg = BN >= 32 ? half * (BN / 2) : 0;
+    uint8_t* stage = s_stage + ew * (32 * 64);
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
       const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
@@ -184,22 +196,53 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       if (!ok) break;
       const uint32_t dt = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(quad * 32) << 16);
+      if (e.coop) {
 #pragma unroll 1
-      for (int jc = 0; jc < BN / 16; jc++) {
-        __syncwarp();
-        float v[16];
-        tmem_ld16(dt + jc * 16, v);
-        const int col0 = n0 + jc * 16;
-        if (!valid || col0 >= d.gemm_n) continue;
+        for (int c = 0; c < cols;) {
+          __syncwarp();
+          const int col = n0 + cbeg + c;
+          if (cols - c >= 32) {
+            uint32_t r0[16], r1[16];
+            tmem_ld16_nowait(dt + cbeg + c, r0);
+            tmem_ld16_nowait(dt + cbeg + c + 16, r1);
+            tmem_wait_ld();
+            float v[32];
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int col = col0 + h * 8;
-          if (col >= d.gemm_n) break;
-          const int cnt = d.gemm_n - col < 8 ? d.gemm_n - col : 8;
-          float y[8];
+            for (int i = 0; i < 16; i++) {
+              v[i] = __uint_as_float(r0[i]);
+              v[16 + i] = __uint_as_float(r1[i]);
+            }
+            epilogue_warp<32>(e, d.K, d.P, d.Q, v, col, s_sc, s_sh, s_bi, valid, n, p, q, stage);
+            c += 32;
+          } else {
+            uint32_t r0[16];
+            tmem_ld16_nowait(dt + cbeg + c, r0);
+            tmem_wait_ld();
+            float v[16];
 #pragma unroll
-          for (int i = 0; i < 8; i++) y[i] = v[h * 8 + i];
-          epilogue8(e, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, pix, n, p, q);
+            for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r0[i]);
+            epilogue_warp<16>(e, d.K, d.P, d.Q, v, col, s_sc, s_sh, s_bi, valid, n, p, q, stage);
+            c += 16;
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < cols; c += 16) {
+          __syncwarp();
+          float v[16];
+          tmem_ld16(dt + cbeg + c, v);
+          const int col0 = n0 + cbeg + c;
+          if (!valid || col0 >= d.gemm_n) continue;
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const int col = col0 + h * 8;
+            if (col >= d.gemm_n) break;
+            const int cnt = d.gemm_n - col < 8 ? d.gemm_n - col : 8;
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) y[i] = v[h * 8 + i];
+            epilogue8(e, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, pix, n, p, q);
+          }
         }
       }
       tc_fence_before();
@@ -237,7 +280,7 @@ static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_o
   }
   const int cap = sms * Cfg::CTAS_PER_SM;
   const int grid = L.grid < cap ? L.grid : cap;
-  k_conv_fprop<BK, BN, MODE><<<grid, 192, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
+  k_conv_fprop<BK, BN, MODE><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
   return cudaGetLastError();
 }
 

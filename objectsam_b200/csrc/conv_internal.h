@@ -36,6 +36,7 @@ struct EpiDev {
   DestDev dest[OSAM_MAX_DEST];
   int shuffle;  // transposed conv: GEMM column j = (dy·2+dx)·kout + k → pixel (2p+dy, 2q+dx)
   int kout;     // channels per (dy,dx) block for shuffle
+  int coop;     // warp-cooperative coalesced epilogue allowed (see epilogue.cuh)
 };
 
 struct ConvDev {

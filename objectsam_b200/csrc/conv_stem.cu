@@ -1,15 +1,21 @@
 // Convolution with a tiny reduction (R·S·C ≤ 32, e.g. the 3×3/s2 RGB stem, C = 3) on the tensor cores.
 //
 // The reference runs this layer through cuDNN, which cannot use tensor cores at C = 3 (its own note,
-// src/misc.cu:194-196, measures 4.7 TFLOP/s for the wgrad of this layer).  Here the im2col row of each
-// output pixel (R·S·C taps, zero-padded to 32 fp16 = one 64-byte row) is gathered by its own thread
-// straight into the 64-byte-swizzled K-major layout the UMMA descriptor reads; one elected thread
-// issues two M=128 × N=BN × K=16 tcgen05 MMAs, and the same four warps run the fused epilogue.
-// The layer is HBM-bound (reads 6 B, writes 64 B per output pixel), so the CTA stays small and many
-// are resident per SM to hide the gather latency.
+// src/misc.cu:194-196, measures 4.7 TFLOP/s for the wgrad of this layer).  Here a CTA owns a th × tw
+// block of output pixels of one image (128 pixels):
+//   1. the block's input window ((th-1)·s+R rows × (tw-1)·s+S columns × C) is read with coalesced
+//      loads into shared memory (zero outside the image = the conv padding);
+//   2. each thread builds its pixel's im2col row (R·S·C taps zero-padded to 32 fp16 = one 64-byte row)
+//      from shared memory, straight into the 64-byte-swizzled K-major layout the UMMA reads;
+//   3. one elected thread issues two M=128 × N=BN × K=16 tcgen05 MMAs into TMEM;
+//   4. the four warps run the fused epilogue and store whole pixel rows through a per-warp stage.
+// The layer is HBM-bound (6 B in, 64 B out per output pixel); eight CTAs per SM overlap one CTA's loads
+// with another's epilogue.
 #include "epilogue.cuh"
 
 namespace osam {
+
+constexpr int kStemStage = 4 * 32 * 64;  // epilogue stage, 4 warps
 
 template <int BN>
 __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x, const __half* __restrict__ w,
@@ -17,11 +23,14 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
   constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : 128;
   __shared__ __align__(1024) uint8_t sA[128 * 64];
   __shared__ __align__(1024) uint8_t sB[BN * 64];
+  __shared__ __align__(16) uint8_t s_stage[kStemStage];
   __shared__ uint64_t bar;
   __shared__ uint32_t tslot;
   __shared__ float s_sc[BN], s_sh[BN], s_bi[BN];
+  extern __shared__ __half win[];  // input window, rows × cols × C
   const int tid = threadIdx.x, warp = tid >> 5;
   const int RSC = d.R * d.S * d.C;
+  const int WR = (d.th - 1) * d.stride + d.R, WC = (d.tw - 1) * d.stride + d.S, WCC = WC * d.C;
 
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -48,32 +57,38 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
   tc_fence_after();
   const uint32_t tmem = tslot;
   constexpr uint32_t idesc = idesc_f16_f32(128, BN);
-  const long long ntiles = (d.M + 127) / 128;
+  const int ntiles = d.tiles_m;
+  uint8_t* stage = s_stage + warp * (32 * 64);
   uint32_t phase = 0;
 
-  for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const long long m = tile * 128 + tid;
-    const bool valid = m < d.M;
-    const int q = (int)(m % d.Q);
-    const long long t = m / d.Q;
-    const int p = (int)(t % d.P), n = (int)(t / d.P);
-    // gather this pixel's im2col row
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int tq = tile % d.tiles_q, rest = tile / d.tiles_q;
+    const int tp = rest % d.tiles_p, n = rest / d.tiles_p;
+    const int q0 = tq * d.tw, p0 = tp * d.th;
+    const int ih0 = p0 * d.stride - d.pad, iw0 = q0 * d.stride - d.pad;
+    // 1. input window (coalesced along each row: consecutive threads → consecutive halves)
+    const __half* img = x + (long long)n * d.H * d.W * d.C;
+    for (int idx = tid; idx < WR * WCC; idx += 128) {
+      const int r = idx / WCC, rem = idx - r * WCC;
+      const int ih = ih0 + r, iw = iw0 + rem / d.C;
+      __half v = __float2half(0.f);
+      if (ih >= 0 && ih < d.H && iw >= 0 && iw < d.W) v = img[((long long)ih * d.W) * d.C + (long long)iw0 * d.C + rem];
+      win[idx] = v;
+    }
+    __syncthreads();
+    // 2. this thread's im2col row
+    const int i = tid / d.tw, j = tid - (tid / d.tw) * d.tw;
+    const int p = p0 + i, q = q0 + j;
+    const bool valid = p < d.P && q < d.Q;
     __align__(16) __half row[32];
 #pragma unroll
-    for (int i = 0; i < 32; i++) row[i] = __float2half(0.f);
-    if (valid) {
-      for (int r = 0; r < d.R; r++) {
-        const int ih = p * d.stride - d.pad + r;
-        if (ih < 0 || ih >= d.H) continue;
-        for (int s = 0; s < d.S; s++) {
-          const int iw = q * d.stride - d.pad + s;
-          if (iw < 0 || iw >= d.W) continue;
-          const __half* src = x + (((long long)n * d.H + ih) * d.W + iw) * d.C;
-          const int k0 = (r * d.S + s) * d.C;
-          for (int c = 0; c < d.C; c++) row[k0 + c] = src[c];
-        }
+    for (int k = 0; k < 32; k++) row[k] = __float2half(0.f);
+    for (int r = 0; r < d.R; r++)
+      for (int s = 0; s < d.S; s++) {
+        const __half* src = win + ((i * d.stride + r) * WC + (j * d.stride + s)) * d.C;
+        const int k0 = (r * d.S + s) * d.C;
+        for (int c = 0; c < d.C; c++) row[k0 + c] = src[c];
       }
-    }
     uint8_t* dst = sA + tid * 64;
 #pragma unroll
     for (int ch = 0; ch < 4; ch++)
@@ -82,33 +97,53 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // 3. MMA
     if (tid == 0) {
       const uint32_t a = smem_u32(sA), b = smem_u32(sB);
       umma_f16(tmem, smem_desc_kmajor(a, 64), smem_desc_kmajor(b, 64), idesc, 0);
       umma_f16(tmem, smem_desc_kmajor(a + 32, 64), smem_desc_kmajor(b + 32, 64), idesc, 1);
       umma_commit(&bar);
     }
-    bool ok = mbar_wait(&bar, phase, d.err);
+    const bool ok = mbar_wait(&bar, phase, d.err);
     phase ^= 1;
     if (!__syncthreads_and(ok)) break;
     tc_fence_after();
+    // 4. epilogue
+    const uint32_t dt = tmem + ((uint32_t)(warp * 32) << 16);
+    if (d.ep.coop) {
 #pragma unroll 1
-    for (int jc = 0; jc < BN / 16; jc++) {
-      __syncwarp();
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + jc * 16, v);
-      if (!valid) continue;
+      for (int c = 0; c < BN; c += 16) {
+        __syncwarp();
+        uint32_t r0[16];
+        tmem_ld16_nowait(dt + c, r0);
+        tmem_wait_ld();
+        float v[16];
 #pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int col = jc * 16 + h * 8;
-        if (col >= d.gemm_n) break;
-        const int cnt = d.gemm_n - col < 8 ? d.gemm_n - col : 8;
-        float y[8];
+        for (int t = 0; t < 16; t++) v[t] = __uint_as_float(r0[t]);
+        epilogue_warp<16>(d.ep, d.K, d.P, d.Q, v, c, s_sc, s_sh, s_bi, valid, n, p, q, stage);
+      }
+    } else {
+      const long long pix = ((long long)n * d.P + p) * d.Q + q;
+#pragma unroll 1
+      for (int jc = 0; jc < BN / 16; jc++) {
+        __syncwarp();
+        float v[16];
+        tmem_ld16(dt + jc * 16, v);
+        if (!valid) continue;
 #pragma unroll
-        for (int i = 0; i < 8; i++) y[i] = v[h * 8 + i];
-        epilogue8(d.ep, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, m, n, p, q);
+        for (int h = 0; h < 2; h++) {
+          const int col = jc * 16 + h * 8;
+          if (col >= d.gemm_n) break;
+          const int cnt = d.gemm_n - col < 8 ? d.gemm_n - col : 8;
+          float y[8];
+#pragma unroll
+          for (int t = 0; t < 8; t++) y[t] = v[h * 8 + t];
+          epilogue8(d.ep, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, pix, n, p, q);
+        }
       }
     }
+    tc_fence_before();
+    __syncthreads();  // TMEM and the window are reused by the next tile
   }
   tc_fence_before();
   __syncthreads();
@@ -118,17 +153,26 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
   }
 }
 
+size_t stem_window_bytes(const ConvDev& d) {
+  const int WR = (d.th - 1) * d.stride + d.R, WC = (d.tw - 1) * d.stride + d.S;
+  return (size_t)WR * WC * d.C * sizeof(__half);
+}
+
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st) {
-  const long long ntiles = (d.M + 127) / 128;
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
   const long long cap = (long long)sms * 8;
-  const int grid = (int)(ntiles < cap ? ntiles : cap);
+  const int grid = (int)(d.tiles_m < cap ? d.tiles_m : cap);
+  const size_t smem = stem_window_bytes(d);
   switch (BN) {
-    case 16: k_conv_stem<16><<<grid, 128, 0, st>>>(x, w, d); break;
-    case 32: k_conv_stem<32><<<grid, 128, 0, st>>>(x, w, d); break;
-    case 64: k_conv_stem<64><<<grid, 128, 0, st>>>(x, w, d); break;
+    case 16: k_conv_stem<16><<<grid, 128, smem, st>>>(x, w, d); break;
+    case 32: k_conv_stem<32><<<grid, 128, smem, st>>>(x, w, d); break;
+    case 64: k_conv_stem<64><<<grid, 128, smem, st>>>(x, w, d); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -53,7 +53,10 @@ SHAPES = [
     (2, 10, 10, 512, 512, 1, 1),
     (1, 7, 9, 64, 32, 1, 1),
     (2, 64, 64, 3, 32, 3, 2),
+    (1, 70, 90, 3, 32, 3, 2),
+    (2, 40, 36, 3, 16, 3, 1),
     (1, 80, 80, 64, 64, 3, 1),
+    (3, 33, 17, 64, 128, 3, 1),
 ]
 
 
@@ -99,6 +102,23 @@ def test_fused_bn_silu_residual_dests(cuda_lib):
     a_up = a[..., 0:64].repeat_interleave(2, dim=1).repeat_interleave(2, dim=2)
     assert_close(up[..., 32:96], a_up)
     assert up[..., :32].abs().max().item() == 0
+
+
+def test_fused_1x1_k512_upsample_dest(cuda_lib):
+    """SPPF.cv2-style node: 1×1 1024→512 with BN+SiLU to an upsampled concat slice and a plain slice."""
+    N, H, W, C, K = 2, 10, 10, 1024, 512
+    x, w = rand_conv(N, H, W, C, K, 1, seed=21)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
+    shift = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    cat_up = torch.zeros(N, 2 * H, 2 * W, 768, dtype=torch.half, device=DEV)
+    cat = torch.zeros(N, H, W, 768, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 1, 1, 1, 0))
+    op.fwd_fused(x, w, [DestSpec(cat_up, up=2), DestSpec(cat, choff=256)], kind=EPI_BN_ACT, scale=scale, shift=shift)
+    a = F.silu(ref_conv(x, w, 1, 0).half().float() * scale + shift)
+    assert_close(cat[..., 256:], a)
+    assert_close(cat_up[..., :512], a.repeat_interleave(2, dim=1).repeat_interleave(2, dim=2))
+    assert cat[..., :256].abs().max().item() == 0 and cat_up[..., 512:].abs().max().item() == 0
 
 
 def test_fused_bias_head_k1(cuda_lib):
