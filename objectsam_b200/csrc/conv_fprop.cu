@@ -4,13 +4,15 @@
 //            of the [N·H·W, C] matrix for 1×1 convs), GEMM N = output channels (BN per tile),
 //   GEMM K = taps × input channels, walked as (tap, BK-channel chunk) steps.
 //
-// Persistent kernel, one CTA per SM: each CTA walks the tile list (tile = blockIdx.x + i·gridDim.x,
-// output-channel tile fastest so neighbouring CTAs share their A windows in L2) with 10 warps:
+// Persistent kernel: each CTA walks the tile list (tile = blockIdx.x + i·gridDim.x, output-channel tile
+// fastest so neighbouring CTAs share their A windows in L2).  Two CTAs per SM with 6 warps each when
+// BN ≤ 128, one CTA with 10 warps for wider tiles:
 //   warp 0      TMA producer: per K-step one A box (the input window of this tap, halo = TMA zero fill)
 //               and one B box (KRSC weight rows) into a STAGES-deep ring; it runs ahead across tiles;
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16), accumulating into
 //               one of TWO TMEM buffers, so the MMAs of tile i+1 overlap the epilogue of tile i;
-//   warps 2..9  epilogue: two warps per TMEM lane quadrant, each taking half of the tile's columns:
+//   warps 2..   epilogue: one (BN ≤ 128) or two (wider, each taking half of the columns) warps per TMEM
+//               lane quadrant:
 //               tcgen05.ld, folded BN + SiLU (+ residual) or bias, fp16 conversion and the
 //               multi-destination store (channel slices, 2× nearest upsample) — written back through a
 //               per-warp shared-memory stage so that each store instruction covers whole pixel rows
@@ -28,23 +30,24 @@ struct FpropCfg {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // One CTA per SM: the ring takes what the stage/constant areas leave of the 227 KiB.
-  static constexpr int RING_BUDGET = 196 * 1024;
+  // ≤ 128 output channels: two CTAs per SM, each with 4 epilogue warps (two independent load/MMA
+  // pipelines hide TMA latency better); wider tiles: one CTA per SM with 8 epilogue warps.
+  static constexpr int CTAS_PER_SM = BN <= 128 ? 2 : 1;
+  static constexpr int EPI_WARPS = BN <= 128 ? 4 : 8;
+  static constexpr int RING_BUDGET = BN <= 128 ? 88 * 1024 : 196 * 1024;
   static constexpr int STAGES_RAW = RING_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   static constexpr int ROW_BYTES = BK * 2;
   static constexpr int CONST_BYTES = 3 * kMaxGemmN * 4;
-  static constexpr int EPI_WARPS = 8;
   static constexpr int STAGE_OUT_BYTES = EPI_WARPS * 32 * 64;  // per-warp epilogue stage
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + CONST_BYTES + STAGE_OUT_BYTES;
-  static constexpr int CTAS_PER_SM = 1;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
 template <int BK, int BN, int MODE>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::CTAS_PER_SM)
     k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const ConvDev d) {
   using Cfg = FpropCfg<BK, BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -158,14 +161,14 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..9)
+    // ---------------------------------------------------------------- epilogue (warps 2..)
     const EpiDev& e = d.ep;
-    const int ew = warp - 2;                 // 0..7
+    const int ew = warp - 2;                 // 0..EPI_WARPS-1
     const int quad = warp & 3;               // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;                // which half of the tile's columns
+    const int half = ew >> 2;                // which half of the tile's columns (8 epilogue warps)
     const int row = quad * 32 + lane;
-    const int cols = BN >= 32 ? BN / 2 : (half == 0 ? BN : 0);
-    const int cbeg = BN >= 32 ? half * (BN / 2) : 0;
+    const int cols = Cfg::EPI_WARPS == 4 ? BN : BN / 2;
+    const int cbeg = Cfg::EPI_WARPS == 4 ? 0 : half * (BN / 2);
     uint8_t* stage = s_stage + ew * (32 * 64);
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {

@@ -17,9 +17,12 @@ namespace osam {
 
 constexpr int kStemStage = 4 * 32 * 64;  // epilogue stage, 4 warps
 
-template <int BN>
+// FR/FS/FC/FSTR > 0: geometry fixed at compile time (the 3×3/s2/C=3 stem) so the im2col row stays in
+// registers; 0 = runtime geometry.
+template <int BN, int FR, int FS, int FC, int FSTR>
 __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x, const __half* __restrict__ w,
                                                    const ConvDev d) {
+  const int R = FR ? FR : d.R, S = FS ? FS : d.S, C = FC ? FC : d.C, STR = FSTR ? FSTR : d.stride;
   constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : 128;
   __shared__ __align__(1024) uint8_t sA[128 * 64];
   __shared__ __align__(1024) uint8_t sB[BN * 64];
@@ -29,8 +32,8 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
   __shared__ float s_sc[BN], s_sh[BN], s_bi[BN];
   extern __shared__ __half win[];  // input window, rows × cols × C
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int RSC = d.R * d.S * d.C;
-  const int WR = (d.th - 1) * d.stride + d.R, WC = (d.tw - 1) * d.stride + d.S, WCC = WC * d.C;
+  const int RSC = R * S * C;
+  const int WR = (d.th - 1) * STR + R, WC = (d.tw - 1) * STR + S, WCC = WC * C;
 
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -65,15 +68,19 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
     const int tq = tile % d.tiles_q, rest = tile / d.tiles_q;
     const int tp = rest % d.tiles_p, n = rest / d.tiles_p;
     const int q0 = tq * d.tw, p0 = tp * d.th;
-    const int ih0 = p0 * d.stride - d.pad, iw0 = q0 * d.stride - d.pad;
+    const int ih0 = p0 * STR - d.pad, iw0 = q0 * STR - d.pad;
     // 1. input window (coalesced along each row: consecutive threads → consecutive halves)
-    const __half* img = x + (long long)n * d.H * d.W * d.C;
-    for (int idx = tid; idx < WR * WCC; idx += 128) {
-      const int r = idx / WCC, rem = idx - r * WCC;
-      const int ih = ih0 + r, iw = iw0 + rem / d.C;
-      __half v = __float2half(0.f);
-      if (ih >= 0 && ih < d.H && iw >= 0 && iw < d.W) v = img[((long long)ih * d.W) * d.C + (long long)iw0 * d.C + rem];
-      win[idx] = v;
+    const __half* img = x + (long long)n * d.H * d.W * C;
+    for (int r = 0; r < WR; r++) {
+      const int ih = ih0 + r;
+      const bool row_in = ih >= 0 && ih < d.H;
+      const __half* src = img + ((long long)ih * d.W + iw0) * C;
+      for (int e = tid; e < WCC; e += 128) {
+        const int iw = iw0 + e / C;
+        __half v = __float2half(0.f);
+        if (row_in && iw >= 0 && iw < d.W) v = src[e];
+        win[r * WCC + e] = v;
+      }
     }
     __syncthreads();
     // 2. this thread's im2col row
@@ -83,12 +90,21 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
     __align__(16) __half row[32];
 #pragma unroll
     for (int k = 0; k < 32; k++) row[k] = __float2half(0.f);
-    for (int r = 0; r < d.R; r++)
-      for (int s = 0; s < d.S; s++) {
-        const __half* src = win + ((i * d.stride + r) * WC + (j * d.stride + s)) * d.C;
-        const int k0 = (r * d.S + s) * d.C;
-        for (int c = 0; c < d.C; c++) row[k0 + c] = src[c];
-      }
+    if (FR) {
+#pragma unroll
+      for (int r = 0; r < FR; r++)
+#pragma unroll
+        for (int s = 0; s < FS; s++)
+#pragma unroll
+          for (int c = 0; c < FC; c++) row[(r * FS + s) * FC + c] = win[((i * STR + r) * WC + (j * STR + s)) * FC + c];
+    } else {
+      for (int r = 0; r < R; r++)
+        for (int s = 0; s < S; s++) {
+          const __half* src = win + ((i * STR + r) * WC + (j * STR + s)) * C;
+          const int k0 = (r * S + s) * C;
+          for (int c = 0; c < C; c++) row[k0 + c] = src[c];
+        }
+    }
     uint8_t* dst = sA + tid * 64;
 #pragma unroll
     for (int ch = 0; ch < 4; ch++)
@@ -169,10 +185,15 @@ cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d,
   const long long cap = (long long)sms * 8;
   const int grid = (int)(d.tiles_m < cap ? d.tiles_m : cap);
   const size_t smem = stem_window_bytes(d);
+  const bool rgb = d.R == 3 && d.S == 3 && d.C == 3 && d.stride == 2;
+  if (rgb && BN == 32) {
+    k_conv_stem<32, 3, 3, 3, 2><<<grid, 128, smem, st>>>(x, w, d);
+    return cudaGetLastError();
+  }
   switch (BN) {
-    case 16: k_conv_stem<16><<<grid, 128, smem, st>>>(x, w, d); break;
-    case 32: k_conv_stem<32><<<grid, 128, smem, st>>>(x, w, d); break;
-    case 64: k_conv_stem<64><<<grid, 128, smem, st>>>(x, w, d); break;
+    case 16: k_conv_stem<16, 0, 0, 0, 0><<<grid, 128, smem, st>>>(x, w, d); break;
+    case 32: k_conv_stem<32, 0, 0, 0, 0><<<grid, 128, smem, st>>>(x, w, d); break;
+    case 64: k_conv_stem<64, 0, 0, 0, 0><<<grid, 128, smem, st>>>(x, w, d); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
