@@ -34,13 +34,13 @@ struct FpropCfg {
   // pipelines hide TMA latency better); wider tiles: one CTA per SM with 8 epilogue warps.
   static constexpr int CTAS_PER_SM = BN <= 128 ? 2 : 1;
   static constexpr int EPI_WARPS = BN <= 128 ? 4 : 8;
-  static constexpr int RING_BUDGET = BN <= 128 ? 88 * 1024 : 196 * 1024;
+  static constexpr int RING_BUDGET = BN <= 128 ? 96 * 1024 : 196 * 1024;
   static constexpr int STAGES_RAW = RING_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   static constexpr int ROW_BYTES = BK * 2;
-  static constexpr int CONST_BYTES = 3 * kMaxGemmN * 4;
+  static constexpr int CONST_BYTES = 2 * kMaxGemmN * 4;
   static constexpr int STAGE_OUT_BYTES = EPI_WARPS * 32 * 64;  // per-warp epilogue stage
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + CONST_BYTES + STAGE_OUT_BYTES;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
@@ -62,8 +62,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
   uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
   float* s_sc = reinterpret_cast<float*>(base + STAGES * Cfg::STAGE_BYTES + 256);
   float* s_sh = s_sc + kMaxGemmN;
-  float* s_bi = s_sh + kMaxGemmN;
-  uint8_t* s_stage = reinterpret_cast<uint8_t*>(s_bi + kMaxGemmN);
+  uint8_t* s_stage = reinterpret_cast<uint8_t*>(s_sh + kMaxGemmN);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = d.tiles_m * d.ntn;
@@ -86,7 +85,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
     tmem_relinquish();
   }
   if (warp >= 2)
-    load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 32 * Cfg::EPI_WARPS, s_sc, s_sh, s_bi);
+    load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 32 * Cfg::EPI_WARPS, s_sc, s_sh);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
@@ -215,7 +214,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
               v[i] = __uint_as_float(r0[i]);
               v[16 + i] = __uint_as_float(r1[i]);
             }
-            epilogue_warp<32>(e, d.K, d.P, d.Q, v, col, s_sc, s_sh, s_bi, valid, n, p, q, stage);
+            epilogue_warp<32>(e, d.K, d.P, d.Q, v, col, s_sc, s_sh, valid, n, p, q, stage);
             c += 32;
           } else {
             uint32_t r0[16];
@@ -224,7 +223,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
             float v[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r0[i]);
-            epilogue_warp<16>(e, d.K, d.P, d.Q, v, col, s_sc, s_sh, s_bi, valid, n, p, q, stage);
+            epilogue_warp<16>(e, d.K, d.P, d.Q, v, col, s_sc, s_sh, valid, n, p, q, stage);
             c += 16;
           }
         }
@@ -244,7 +243,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
             float y[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) y[i] = v[h * 8 + i];
-            epilogue8(e, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, pix, n, p, q);
+            epilogue8(e, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, pix, n, p, q);
           }
         }
       }

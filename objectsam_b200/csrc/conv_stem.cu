@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
   __shared__ __align__(16) uint8_t s_stage[kStemStage];
   __shared__ uint64_t bar;
   __shared__ uint32_t tslot;
-  __shared__ float s_sc[BN], s_sh[BN], s_bi[BN];
+  __shared__ float s_sc[BN], s_sh[BN];
   extern __shared__ __half win[];  // input window, rows × cols × C
   const int tid = threadIdx.x, warp = tid >> 5;
   const int RSC = R * S * C;
@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
     }
     *reinterpret_cast<uint4*>(sB + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)) = *reinterpret_cast<const uint4*>(v);
   }
-  load_epilogue_consts(d.ep, d.gemm_n, 0, BN, tid, 128, s_sc, s_sh, s_bi);
+  load_epilogue_consts(d.ep, d.gemm_n, 0, BN, tid, 128, s_sc, s_sh);
   fence_proxy_async_smem();
   __syncthreads();
   tc_fence_after();
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
         float v[16];
 #pragma unroll
         for (int t = 0; t < 16; t++) v[t] = __uint_as_float(r0[t]);
-        epilogue_warp<16>(d.ep, d.K, d.P, d.Q, v, c, s_sc, s_sh, s_bi, valid, n, p, q, stage);
+        epilogue_warp<16>(d.ep, d.K, d.P, d.Q, v, c, s_sc, s_sh, valid, n, p, q, stage);
       }
     } else {
       const long long pix = ((long long)n * d.P + p) * d.Q + q;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
           float y[8];
 #pragma unroll
           for (int t = 0; t < 8; t++) y[t] = v[h * 8 + t];
-          epilogue8(d.ep, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, s_bi, pix, n, p, q);
+          epilogue8(d.ep, d.K, d.P, d.Q, y, cnt, col, col, s_sc, s_sh, pix, n, p, q);
         }
       }
     }

@@ -48,9 +48,9 @@ __device__ __forceinline__ void store_dests(const EpiDev& e, long long pix, int 
 
 // Epilogue of 8 accumulator columns [col, col+8) (local columns [li, li+8) of the CTA's tile) of the
 // output pixel `pix` = (n, p, q) on the P×Q grid.  `cnt` columns are real (the rest are GEMM padding).
-// s_sc/s_sh/s_bi hold the tile's per-column scale, shift and bias.
+// s_sc/s_sh hold the per-column scale and shift (or bias).
 __device__ __forceinline__ void epilogue8(const EpiDev& e, int K, int P, int Q, float (&y)[8], int cnt, int col,
-                                          int li, const float* s_sc, const float* s_sh, const float* s_bi,
+                                          int li, const float* s_sc, const float* s_sh,
                                           long long pix, int n, int p, int q) {
   if (e.round_z) {
 #pragma unroll
@@ -86,7 +86,7 @@ __device__ __forceinline__ void epilogue8(const EpiDev& e, int K, int P, int Q, 
     }
   } else if (e.kind == OSAM_EPI_BIAS) {
 #pragma unroll
-    for (int i = 0; i < 8; i++) y[i] += s_bi[li + i];
+    for (int i = 0; i < 8; i++) y[i] += s_sh[li + i];
   } else if (e.beta != 0.f) {
     const DestDev& ds = e.dest[0];
     const __half* old = ds.p + opix * ds.ctot + ds.choff + k - ds.c0;
@@ -125,10 +125,10 @@ __device__ __forceinline__ void unpack8h(uint4 u, float* o) {
 }
 
 // v: this lane's W accumulator values of GEMM columns [col, col+W); (valid, n, p, q): this lane's output
-// pixel on the P×Q GEMM grid.  s_sc/s_sh/s_bi are indexed by GEMM column.
+// pixel on the P×Q GEMM grid.  s_sc/s_sh are indexed by GEMM column.
 template <int W>
 __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int Q, const float* v, int col,
-                                              const float* s_sc, const float* s_sh, const float* s_bi, bool valid,
+                                              const float* s_sc, const float* s_sh, bool valid,
                                               int n, int p, int q, uint8_t* stage) {
   constexpr int CPR = W / 8;     // 16-byte chunks per row
   constexpr int RPI = 32 / CPR;  // rows per cooperative instruction
@@ -153,7 +153,7 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
       const float t = s_sc[col + i] * z + s_sh[col + i];
       z = e.act ? silu_f(t) : t;
     } else if (e.kind == OSAM_EPI_BIAS) {
-      z += s_bi[col + i];
+      z += s_sh[col + i];
     }
     y[i] = z;
   }
@@ -215,16 +215,17 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
   __syncwarp();
 }
 
-// Per-column epilogue constants of the tile starting at GEMM column n0 (BN columns) into shared memory.
+// Per-column epilogue constants of the tile starting at GEMM column n0 (BN columns) into shared memory:
+// s_sc = BN scale (1 otherwise), s_sh = BN shift or the bias (0 otherwise).
 __device__ __forceinline__ void load_epilogue_consts(const EpiDev& e, int gemm_n, int n0, int BN, int tid,
-                                                     int nthreads, float* s_sc, float* s_sh, float* s_bi) {
+                                                     int nthreads, float* s_sc, float* s_sh) {
   for (int i = tid; i < BN; i += nthreads) {
     const int col = n0 + i;
     const bool ok = col < gemm_n;
     const int kc = e.shuffle ? col % e.kout : col;
-    s_sc[i] = (ok && e.scale) ? e.scale[kc] : 1.f;
-    s_sh[i] = (ok && e.shift) ? e.shift[kc] : 0.f;
-    s_bi[i] = (ok && e.bias) ? e.bias[kc] : 0.f;
+    const bool bn = e.kind == OSAM_EPI_BN_ACT, bias = e.kind == OSAM_EPI_BIAS;
+    s_sc[i] = (ok && bn && e.scale) ? e.scale[kc] : 1.f;
+    s_sh[i] = ok ? ((bn && e.shift) ? e.shift[kc] : ((bias && e.bias) ? e.bias[kc] : 0.f)) : 0.f;
   }
 }
 
