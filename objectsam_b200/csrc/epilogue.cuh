@@ -7,9 +7,23 @@
 
 namespace osam {
 
-// SiLU with the fast exponential and division the reference's fast-math build also uses
-// (CMakeLists.txt:11 --use_fast_math, src/bn.cu:35).
-__device__ __forceinline__ float silu_f(float y) { return __fdividef(y, 1.f + __expf(-y)); }
+// 1/d for d ≥ 1 on the FMA pipe: the classic exponent-flip initial estimate (magic-constant method,
+// ~12% max relative error) refined by three Newton–Raphson steps r ← r·(2 − d·r) (error squares each
+// step: ~1e-8).  Keeps the quarter-rate MUFU unit free for the exponential.
+__device__ __forceinline__ float rcp_nr(float d) {
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(d));
+  r = r * fmaf(-d, r, 2.f);
+  r = r * fmaf(-d, r, 2.f);
+  r = r * fmaf(-d, r, 2.f);
+  return r;
+}
+// SiLU y·σ(y) = y / (1 + e^{−y}): one MUFU exponential (the reference's fast-math build uses __expf too,
+// CMakeLists.txt:11, src/bn.cu:35) and the FMA-pipe reciprocal above.  y is clamped at −80 so 1 + e^{−y}
+// stays finite; silu(−80) ≈ −1e-33 rounds to −0 in fp16 either way.
+__device__ __forceinline__ float silu_f(float y) {
+  const float e = __expf(-fmaxf(y, -80.f));
+  return y * rcp_nr(1.f + e);
+}
 
 // Store `cnt` (≤ 8) consecutive output channels starting at `k` of one output pixel to every destination
 // whose channel range holds them.  `pix` indexes the P×Q output grid; (n, p, q) locate it for the 2×
@@ -124,50 +138,74 @@ __device__ __forceinline__ void unpack8h(uint4 u, float* o) {
   }
 }
 
-// v: this lane's W accumulator values of GEMM columns [col, col+W); (valid, n, p, q): this lane's output
-// pixel on the P×Q GEMM grid.  s_sc/s_sh are indexed by GEMM column.
+// v: this lane's W accumulator values of GEMM columns [col, col+W) (col % 16 == 0); (valid, n, p, q):
+// this lane's output pixel on the P×Q GEMM grid.  s_sc/s_sh are indexed by GEMM column.
+// The math runs as branch-free unrolled loops (the kind/act/round flags are hoisted), and the stores
+// use one shuffled 32-bit pixel index per row, so independent elements overlap in the pipelines.
 template <int W>
-__device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int Q, const float* v, int col,
-                                              const float* s_sc, const float* s_sh, bool valid,
-                                              int n, int p, int q, uint8_t* stage) {
+__device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int Q, float* v, int col,
+                                              const float* s_sc, const float* s_sh, bool valid, int n, int p,
+                                              int q, uint8_t* stage) {
   constexpr int CPR = W / 8;     // 16-byte chunks per row
   constexpr int RPI = 32 / CPR;  // rows per cooperative instruction
   const int lane = threadIdx.x & 31;
-  const int my_n = valid ? n : -1;
-  const int my_pq = (p << 16) | (q & 0xffff);
-  int k0 = col, dy = 0, dx = 0, OP = P, OQ = Q;
+  int k0 = col, OP = P, OQ = Q, op = p, oq = q;
   if (e.shuffle) {  // transposed conv: the pass lies in one (dy, dx) block (kout % 32 == 0)
     const int blk = col / e.kout;
     k0 = col - blk * e.kout;
-    dy = blk >> 1;
-    dx = blk & 1;
     OP = 2 * P;
     OQ = 2 * Q;
+    op = 2 * p + (blk >> 1);
+    oq = 2 * q + (blk & 1);
+  }
+  // this lane's output pixel (−1: outside the output) and its 2×-upsampled base pixel
+  const int my_o = valid ? (n * OP + op) * OQ + oq : -1;
+  const int my_u = (n * 2 * OP + 2 * op) * (2 * OQ) + 2 * oq;
+  const int my_r = (n * P + p) * Q + q;  // residual pixel (GEMM grid)
+
+  // ---- math (hoisted flags, branch-free loops)
+  if (e.round_z) {
+#pragma unroll
+    for (int i = 0; i < W; i++) v[i] = __half2float(__float2half_rn(v[i]));
   }
   float y[W];
+  if (e.kind == OSAM_EPI_BN_ACT) {
+    float sc[W], sh[W];
 #pragma unroll
-  for (int i = 0; i < W; i++) {
-    float z = v[i];
-    if (e.round_z) z = __half2float(__float2half_rn(z));
-    if (e.kind == OSAM_EPI_BN_ACT) {
-      const float t = s_sc[col + i] * z + s_sh[col + i];
-      z = e.act ? silu_f(t) : t;
-    } else if (e.kind == OSAM_EPI_BIAS) {
-      z += s_sh[col + i];
+    for (int i = 0; i < W; i += 4) {
+      *reinterpret_cast<float4*>(sc + i) = *reinterpret_cast<const float4*>(s_sc + col + i);
+      *reinterpret_cast<float4*>(sh + i) = *reinterpret_cast<const float4*>(s_sh + col + i);
     }
-    y[i] = z;
+    if (e.act) {
+#pragma unroll
+      for (int i = 0; i < W; i++) y[i] = silu_f(fmaf(sc[i], v[i], sh[i]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < W; i++) y[i] = fmaf(sc[i], v[i], sh[i]);
+    }
+  } else if (e.kind == OSAM_EPI_BIAS) {
+#pragma unroll
+    for (int i = 0; i < W; i += 4) {
+      const float4 b = *reinterpret_cast<const float4*>(s_sh + col + i);
+      y[i] = v[i] + b.x;
+      y[i + 1] = v[i + 1] + b.y;
+      y[i + 2] = v[i + 2] + b.z;
+      y[i + 3] = v[i + 3] + b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < W; i++) y[i] = v[i];
   }
+
+  // ---- residual: coalesced rows into the stage, then each lane reads its own row
   if (e.kind == OSAM_EPI_BN_ACT && e.res) {
+    const int my_rv = valid ? my_r : -1;
 #pragma unroll
     for (int it = 0; it < CPR; it++) {
       const int rr = it * RPI + lane / CPR, ch = lane % CPR;
-      const int rn = __shfl_sync(0xffffffffu, my_n, rr);
-      const int rpq = __shfl_sync(0xffffffffu, my_pq, rr);
+      const int rpix = __shfl_sync(0xffffffffu, my_rv, rr);
       uint4 val = make_uint4(0, 0, 0, 0);
-      if (rn >= 0) {
-        const long long rpix = ((long long)rn * P + (rpq >> 16)) * Q + (rpq & 0xffff);
-        val = *reinterpret_cast<const uint4*>(e.res + rpix * K + col + ch * 8);
-      }
+      if (rpix >= 0) val = *reinterpret_cast<const uint4*>(e.res + (long long)rpix * K + col + ch * 8);
       *reinterpret_cast<uint4*>(stage + stage_off(rr, ch)) = val;
     }
     __syncwarp();
@@ -180,35 +218,35 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
     }
     __syncwarp();
   }
+
+  // ---- fp16 rows into the stage, then whole pixel rows out
 #pragma unroll
   for (int ch = 0; ch < CPR; ch++) *reinterpret_cast<uint4*>(stage + stage_off(lane, ch)) = pack8h(y + ch * 8);
   __syncwarp();
+  const int nd = e.ndest;
 #pragma unroll
   for (int it = 0; it < CPR; it++) {
     const int rr = it * RPI + lane / CPR, ch = lane % CPR;
-    const int rn = __shfl_sync(0xffffffffu, my_n, rr);
-    const int rpq = __shfl_sync(0xffffffffu, my_pq, rr);
+    const int ro = __shfl_sync(0xffffffffu, my_o, rr);
+    const int ru = __shfl_sync(0xffffffffu, my_u, rr);
     const uint4 val = *reinterpret_cast<const uint4*>(stage + stage_off(rr, ch));
-    if (rn < 0) continue;
-    int op = rpq >> 16, oq = rpq & 0xffff;
-    if (e.shuffle) {
-      op = 2 * op + dy;
-      oq = 2 * oq + dx;
-    }
+    if (ro < 0) continue;
     const int k = k0 + ch * 8;
-#pragma unroll 1
-    for (int t = 0; t < e.ndest; t++) {
+#pragma unroll
+    for (int t = 0; t < OSAM_MAX_DEST; t++) {
+      if (t >= nd) break;
       const DestDev& ds = e.dest[t];
       if (k < ds.c0 || k >= ds.c1) continue;
-      __half* b = ds.p + ds.choff - ds.c0 + k;
+      __half* b = ds.p + (ds.choff - ds.c0 + k);
       if (ds.up == 1) {
-        *reinterpret_cast<uint4*>(b + (((long long)rn * OP + op) * OQ + oq) * ds.ctot) = val;
+        *reinterpret_cast<uint4*>(b + (long long)ro * ds.ctot) = val;
       } else {
-        const long long Q2 = 2LL * OQ, px = ((long long)rn * 2 * OP + 2 * op) * Q2 + 2 * oq;
-        *reinterpret_cast<uint4*>(b + px * ds.ctot) = val;
-        *reinterpret_cast<uint4*>(b + (px + 1) * ds.ctot) = val;
-        *reinterpret_cast<uint4*>(b + (px + Q2) * ds.ctot) = val;
-        *reinterpret_cast<uint4*>(b + (px + Q2 + 1) * ds.ctot) = val;
+        const long long c = ds.ctot, q2 = 2LL * OQ;
+        __half* u = b + (long long)ru * c;
+        *reinterpret_cast<uint4*>(u) = val;
+        *reinterpret_cast<uint4*>(u + c) = val;
+        *reinterpret_cast<uint4*>(u + q2 * c) = val;
+        *reinterpret_cast<uint4*>(u + (q2 + 1) * c) = val;
       }
     }
   }

@@ -411,7 +411,7 @@ struct osam_model {
       nd.plan = *plan;
       osam_conv_plan_destroy(plan);
       osam_epilogue ep{};
-      ep.round_z = 1;
+      ep.round_z = 0;  // keep z in fp32 into BN/SiLU (the reference rounds it to fp16 first: ≤ 1 ulp apart)
       if (nd.kind == N_CONVBN) {
         ep.kind = OSAM_EPI_BN_ACT;
         ep.scale = f32 + nd.f_off;
