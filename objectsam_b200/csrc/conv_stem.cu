@@ -29,7 +29,8 @@ __global__ void __launch_bounds__(128) k_conv_stem(const __half* __restrict__ x,
   __shared__ __align__(16) uint8_t s_stage[kStemStage];
   __shared__ uint64_t bar;
   __shared__ uint32_t tslot;
-  __shared__ float s_sc[BN], s_sh[BN];
+  __shared__ __align__(16) float s_sc[BN];
+  __shared__ __align__(16) float s_sh[BN];
   extern __shared__ __half win[];  // input window, rows × cols × C
   const int tid = threadIdx.x, warp = tid >> 5;
   const int RSC = R * S * C;

@@ -121,6 +121,21 @@ def test_fused_1x1_k512_upsample_dest(cuda_lib):
     assert cat[..., :256].abs().max().item() == 0 and cat_up[..., 512:].abs().max().item() == 0
 
 
+@pytest.mark.parametrize("shape", [(2, 64, 64, 3, 32, 3, 2), (1, 70, 90, 3, 32, 3, 2), (2, 40, 36, 3, 16, 3, 1)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_fused_stem_bn_silu(cuda_lib, shape):
+    """The C = 3 stem with its folded-BN + SiLU epilogue (model.0)."""
+    N, H, W, C, K, R, s = shape
+    x, w = rand_conv(N, H, W, C, K, R, seed=31)
+    g = torch.Generator(device="cpu").manual_seed(6)
+    scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
+    shift = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, s, R // 2))
+    y = torch.empty(op.out_shape(), dtype=torch.half, device=DEV)
+    op.fwd_fused(x, w, [DestSpec(y)], kind=EPI_BN_ACT, scale=scale, shift=shift, round_z=False)
+    assert_close(y, F.silu(ref_conv(x, w, s, R // 2) * scale + shift))
+
+
 def test_fused_bias_head_k1(cuda_lib):
     """Head 1×1 conv with bias and a single output channel (cls head, reference src/model.cpp:251)."""
     N, H, W, C = 2, 40, 40, 128
