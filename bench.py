@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ref-cudnn", action="store_true", help="skip timing the reference's cuDNN build")
     return ap.parse_args()
 
 
@@ -146,6 +147,26 @@ def cpu_forward_sample(imgsz: int, budget_s: float, seed: int = 0):
     dt = time.perf_counter() - t0
     return dict(value=n / dt, unit=UNIT, cores=torch.get_num_threads(), kind="port",
                 sample=f"{n} batch-1 {imgsz}x{imgsz} forwards of the PyTorch CPU restatement (fp32), {dt:.1f} s")
+
+
+def reference_cudnn(B: int, S: int, iters: int = 10):
+    """Times the reference's own cuDNN fp16 inference (oracle/_ref/ref_forward_fp16, built from its sources)
+    on this GPU with the same weights (BASELINE config 1 generator) and a seeded U[0,1] batch."""
+    binary = os.path.join(ROOT, "oracle", "_ref", "ref_forward_fp16")
+    if not os.path.exists(binary):
+        return {"unavailable": "oracle/_ref not built (make -C oracle)"}
+    from oracle import fsow, yolo_params
+    with tempfile.TemporaryDirectory() as td:
+        wp = os.path.join(td, "w.fsow")
+        fsow.save(wp, yolo_params.make_weights(0))
+        try:
+            out = subprocess.run([binary, wp, "-", "-", str(iters), str(B), str(S)], capture_output=True, text=True,
+                                 timeout=900, check=True).stdout
+            d = json.loads(out.strip().splitlines()[-1])
+            d["source"] = "reference src/{bn,misc}.cu + src/{conv,model}.cpp compiled for sm_100a (oracle/Makefile)"
+            return d
+        except (subprocess.SubprocessError, ValueError, IndexError) as e:
+            return {"unavailable": f"reference cuDNN run failed: {type(e).__name__}"}
 
 
 def run_reference(args, rank, world):
@@ -305,6 +326,13 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_forward_sample(S, args.cpu_sample_s)
+    ref_cudnn = None
+    if rank == 0 and world == 1 and not args.no_ref_cudnn:
+        model.close()  # release our activations before the reference allocates its own
+        torch.cuda.synchronize()
+        ref_cudnn = reference_cudnn(B, S)
+        if "img_per_s" in ref_cudnn:
+            ref_cudnn["speedup_ours_over_ref"] = value / ref_cudnn["img_per_s"]
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
@@ -316,7 +344,7 @@ def main():
                            "l2": "inputs+activations > 126 MB L2 (no flush needed)",
                            "timing": "eager launches with a CUDA event per node over the timed region"},
                 "gpu_launches": K * n, "clocks": clocks, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "graph_ms_per_step": graph_ms / K,
+                "graph_ms_per_step": graph_ms / K, "reference_cudnn": ref_cudnn,
                 "top_kernels": sorted(({"name": nodes[i]["name"], "ms": round(node_ms[i], 4),
                                         "tflops": round(nodes[i]["flops"] / (node_ms[i] / 1e3) / 1e12, 1),
                                         "gbs": round(nodes[i]["bytes"] / (node_ms[i] / 1e3) / 1e9, 0)}

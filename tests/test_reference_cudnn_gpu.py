@@ -1,0 +1,54 @@
+"""Parity with the reference's own cuDNN fp16 path (oracle/_ref/ref_forward_fp16, built from the reference
+sources by oracle/Makefile) on identical seeded weights and inputs.
+
+Tolerance (north star): max |ours − reference| ≤ 1e-2 · max|reference| per head tensor, and our error
+against the float64 network is no larger than 1.5× the reference fp16 path's own error against it (the
+two fp16 evaluations round differently; neither may drift further from the exact network than the other
+allows).  Skipped, with the reason, when the reference binaries were not built.
+"""
+import os
+import subprocess
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+from objectsam_b200.model import Model
+from oracle import fsow, yolo_params, yolo_ref
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF16 = os.path.join(ROOT, "oracle", "_ref", "ref_forward_fp16")
+
+
+@pytest.mark.skipif(not os.path.exists(REF16), reason="oracle/_ref not built (make -C oracle)")
+@pytest.mark.parametrize("seed,N,S", [(3, 2, 128), (0, 2, 256)])
+def test_matches_reference_cudnn_fp16(cuda_lib, seed, N, S):
+    w = yolo_ref.calibrated_weights(seed, 128)
+    imgs = yolo_params.make_images(N, S, seed + 100)
+    with tempfile.TemporaryDirectory() as td:
+        wp, ip, op = (os.path.join(td, n) for n in ("w.fsow", "x.fsow", "o.fsow"))
+        fsow.save(wp, w)
+        fsow.save(ip, {"images": imgs})
+        subprocess.run([REF16, wp, ip, op], check=True, timeout=600)
+        ref = fsow.load(op)
+    m = Model(N, S)
+    m.load(w)
+    m.sync_weights()
+    m.input().copy_(torch.from_numpy(imgs).half())
+    m.forward()
+    torch.cuda.synchronize()
+    o64 = yolo_ref.YoloSegRef(w, emulate_fp16=False, dtype=torch.float64).forward(imgs)
+    ours = {f"out.{k}{l}": m.head(i, l) for i, k in enumerate(("box", "cls", "coef")) for l in range(3)}
+    ours["out.proto"] = m.proto()
+    exact = {f"out.{k}{l}": o64[k][l] for k in ("box", "cls", "coef") for l in range(3)}
+    exact["out.proto"] = o64["proto"]
+    for name, y in ours.items():
+        y = y.double().cpu().numpy()
+        r = ref[name].astype(np.float64)
+        x = exact[name].permute(0, 2, 3, 1).numpy()
+        scale = np.abs(r).max() + 1e-6
+        assert np.abs(y - r).max() <= 1e-2 * scale, f"{name}: max |ours-ref| {np.abs(y - r).max():.3e} (scale {scale:.3e})"
+        e_ours, e_ref = np.abs(y - x), np.abs(r - x)
+        assert e_ours.mean() <= 1.5 * e_ref.mean() + 1e-4 * scale, f"{name}: mae {e_ours.mean():.3e} vs ref {e_ref.mean():.3e}"
