@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-cudnn", action="store_true", help="skip timing the reference's cuDNN build")
+    ap.add_argument("--nodes-out", default=None, help="write the per-node timing table (JSON) to this path")
     return ap.parse_args()
 
 
@@ -316,6 +317,9 @@ def main():
             traffic = json.load(open(tf)).get(nd["name"], {}).get(f"b{B}_s{S}")
         except (ValueError, OSError):
             traffic = None
+    if args.nodes_out and rank == 0:
+        with open(args.nodes_out, "w") as f:
+            json.dump([dict(nd_, ms=node_ms[i]) for i, nd_ in enumerate(nodes)], f, indent=0)
     conv_flops = sum(x["flops"] for x in nodes)
     roofline = {"bound": bound, "achieved": ach, "peak": peak, "unit": unit_r, "frac": ach / peak,
                 "traffic": traffic, "kernel": nd["name"], "kernel_ms": node_ms[top],

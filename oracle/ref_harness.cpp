@@ -86,6 +86,7 @@ int main(int argc, char** argv) {
     fsow_save(opath, out);
   }
 
+  if (getenv("OSAM_REF_PRINT_CONVS")) m.print_convs();  // the reference's per-conv tuned timings (to stdout)
   if (iters > 0) {
     cudaEvent_t e0, e1;
     CUDA_CHECK(cudaEventCreate(&e0));
