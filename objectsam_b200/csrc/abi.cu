@@ -133,7 +133,7 @@ static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p)
     if (g->C % 32 || g->K % 8) return fail(OSAM_ERR_UNSUPPORTED, "transposed conv: C %% 32, K %% 8 required");
     p->P = g->H;  // GEMM grid = input grid; the epilogue scatters to 2H × 2W
     p->Q = g->W;
-    p->mode = A_GEMM;
+    p->mode = A_S1;  // one "tap" (R = S = 1 view of the input), spatial tiles
     p->BK = g->C % 64 == 0 ? 64 : 32;
     p->gemm_n = 4 * g->K;
     p->M = (long long)g->N * g->H * g->W;
@@ -156,9 +156,7 @@ static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p)
       p->BK = g->C % 64 == 0 ? 64 : 32;
       p->nkc = g->C / p->BK;
       p->nk = g->R * g->S * p->nkc;
-      if (g->R == 1 && g->S == 1 && g->stride == 1 && g->pad == 0)
-        p->mode = A_GEMM;
-      else if (g->stride == 1)
+      if (g->stride == 1)
         p->mode = A_S1;
       else if (g->stride == 2 && g->H % 2 == 0 && g->W % 2 == 0)
         p->mode = A_S2;
@@ -230,6 +228,11 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   ConvDev& d = L->d;
   d.N = g.N; d.H = g.H; d.W = g.W; d.C = g.C; d.K = g.K;
   d.P = p->P; d.Q = p->Q; d.R = g.R; d.S = g.S; d.stride = g.stride; d.pad = g.pad;
+  if (p->transposed) {  // a single tap at offset 0 over the input grid
+    d.R = 1;
+    d.S = 1;
+    d.pad = 0;
+  }
   d.gemm_n = p->gemm_n;
   d.tn = p->tn; d.th = p->th; d.tw = p->tw; d.tiles_q = p->tiles_q; d.tiles_p = p->tiles_p;
   d.M = p->M;
@@ -283,6 +286,44 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     if (p->mode == A_STEM) coop = coop && (p->BN == 32 || p->BN == 16 || p->BN == 64);
     if (p->mode != A_STEM && p->mode != A_GEMM) coop = coop && (p->P < 65536 && p->Q < 65536);
     e.coop = coop;
+  }
+  // ---- TMA-store epilogue: spatial tiles, 32-column passes, destinations on 32-column boundaries
+  {
+    bool ts = e.coop && (p->mode == A_S1 || p->mode == A_S2) && p->BN % 32 == 0;
+    for (int i = 0; i < e.ndest && ts; i++) ts = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
+    if (e.shuffle) ts = ts && e.ndest == 1 && e.kout % 32 == 0;
+    e.tstore = 0;
+    if (ts) {
+      e.wtw = p->tw < 32 ? p->tw : 32;
+      e.wth = p->th < 32 / e.wtw ? p->th : 32 / e.wtw;
+      e.wtn = 32 / (e.wtw * e.wth);
+      const uint32_t box[4] = {32, (uint32_t)e.wtw, (uint32_t)e.wth, (uint32_t)e.wtn};
+      int rc = OSAM_OK;
+      for (int t = 0; t < e.ndest && rc == OSAM_OK; t++) {
+        const DestDev& ds = e.dest[t];
+        const uint64_t c = (uint64_t)ds.ctot;
+        const bool four = ds.up == 2 || e.shuffle;
+        const uint64_t OQ2 = 2ull * p->Q, OP2 = 2ull * p->P;
+        for (int v = 0; v < (four ? 4 : 1) && rc == OSAM_OK; v++) {
+          const int dy = v >> 1, dx = v & 1;
+          const __half* b = ds.p + (four ? ((uint64_t)dy * OQ2 + dx) * c : 0);
+          const uint64_t dims[4] = {c, (uint64_t)p->Q, (uint64_t)p->P, (uint64_t)g.N};
+          uint64_t str[3];
+          if (four) {
+            str[0] = 2 * c * 2;
+            str[1] = 2 * OQ2 * c * 2;
+            str[2] = OP2 * OQ2 * c * 2;
+          } else {
+            str[0] = c * 2;
+            str[1] = (uint64_t)p->Q * c * 2;
+            str[2] = (uint64_t)p->P * p->Q * c * 2;
+          }
+          rc = make_map(&L->sm.m[4 * t + v], b, 4, dims, str, box, 64);
+        }
+      }
+      if (rc != OSAM_OK) return rc;
+      e.tstore = 1;
+    }
   }
 
   // ---- operands

@@ -42,27 +42,28 @@ struct FpropCfg {
   static constexpr int ROW_BYTES = BK * 2;
   static constexpr int CONST_BYTES = 2 * kMaxGemmN * 4;
   static constexpr int STAGE_OUT_BYTES = EPI_WARPS * 32 * 64;  // per-warp epilogue stage
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + CONST_BYTES + STAGE_OUT_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGE_OUT_BYTES + CONST_BYTES + 256;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
 template <int BK, int BN, int MODE>
 __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::CTAS_PER_SM)
-    k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const ConvDev d) {
+    k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                 const __grid_constant__ StoreMaps sm, const ConvDev d) {
   using Cfg = FpropCfg<BK, BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
   uint8_t* sB = base + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint8_t* s_stage = base + STAGES * Cfg::STAGE_BYTES;  // 1024-aligned: the TMA store swizzle needs 512
+  float* s_sc = reinterpret_cast<float*>(s_stage + Cfg::STAGE_OUT_BYTES);
+  float* s_sh = s_sc + kMaxGemmN;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_sh + kMaxGemmN);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA → epilogue)
   uint64_t* acce = accf + 2;        // [2] accumulator drained (epilogue → MMA), one arrival per epilogue warp
   uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
-  float* s_sc = reinterpret_cast<float*>(base + STAGES * Cfg::STAGE_BYTES + 256);
-  float* s_sh = s_sc + kMaxGemmN;
-  uint8_t* s_stage = reinterpret_cast<uint8_t*>(s_sh + kMaxGemmN);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = d.tiles_m * d.ntn;
@@ -166,8 +167,11 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
     const int quad = warp & 3;               // TMEM lane quadrant this warp may access
     const int half = ew >> 2;                // which half of the tile's columns (8 epilogue warps)
     const int row = quad * 32 + lane;
-    const int cols = Cfg::EPI_WARPS == 4 ? BN : BN / 2;
-    const int cbeg = Cfg::EPI_WARPS == 4 ? 0 : half * (BN / 2);
+    // 8 epilogue warps: the first half takes the leading ceil32(BN/2) columns, the second the rest, so
+    // both halves are multiples of 32 for every BN % 32 == 0 (e.g. 224 → 128 + 96).
+    constexpr int SPLIT = ((BN / 2 + 31) / 32) * 32;
+    const int cols = Cfg::EPI_WARPS == 4 ? BN : (half == 0 ? SPLIT : BN - SPLIT);
+    const int cbeg = Cfg::EPI_WARPS == 4 ? 0 : half * SPLIT;
     uint8_t* stage = s_stage + ew * (32 * 64);
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
@@ -193,12 +197,36 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
         valid = n < d.N && p < d.P && q < d.Q;
         pix = ((long long)n * d.P + p) * d.Q + q;
       }
+      int bq = 0, bp = 0, bn = 0;  // origin of this warp's 32-row box (TMA-store epilogue)
+      if (MODE != A_GEMM) {
+        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
+        const int w0 = quad * 32, thw = d.th * d.tw;
+        bq = tq * d.tw + w0 % d.tw;
+        bp = (rest % d.tiles_p) * d.th + (w0 / d.tw) % d.th;
+        bn = (rest / d.tiles_p) * d.tn + w0 / thw;
+      }
       const uint32_t buf = lt & 1;
       const bool ok = mbar_wait(accf + buf, (lt >> 1) & 1, d.err);
       tc_fence_after();
       if (!ok) break;
       const uint32_t dt = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(quad * 32) << 16);
-      if (e.coop) {
+      if (e.tstore) {
+#pragma unroll 1
+        for (int c = 0; c < cols; c += 32) {
+          __syncwarp();
+          uint32_t r0[16], r1[16];
+          tmem_ld16_nowait(dt + cbeg + c, r0);
+          tmem_ld16_nowait(dt + cbeg + c + 16, r1);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            v[i] = __uint_as_float(r0[i]);
+            v[16 + i] = __uint_as_float(r1[i]);
+          }
+          epilogue_warp_tma(e, sm, d.K, d.P, d.Q, v, n0 + cbeg + c, s_sc, s_sh, valid, n, p, q, bq, bp, bn, stage);
+        }
+      } else if (e.coop) {
 #pragma unroll 1
         for (int c = 0; c < cols;) {
           __syncwarp();
@@ -252,6 +280,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
       if (lane == 0) mbar_arrive(acce + buf);
     }
   }
+  if (warp >= 2 && lane == 0) bulk_wait_group0();  // tensor stores complete before the CTA retires
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -282,7 +311,7 @@ static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_o
   }
   const int cap = sms * Cfg::CTAS_PER_SM;
   const int grid = L.grid < cap ? L.grid : cap;
-  k_conv_fprop<BK, BN, MODE><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.d);
+  k_conv_fprop<BK, BN, MODE><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.sm, L.d);
   return cudaGetLastError();
 }
 

@@ -37,6 +37,8 @@ struct EpiDev {
   int shuffle;  // transposed conv: GEMM column j = (dy·2+dx)·kout + k → pixel (2p+dy, 2q+dx)
   int kout;     // channels per (dy,dx) block for shuffle
   int coop;     // warp-cooperative coalesced epilogue allowed (see epilogue.cuh)
+  int tstore;   // warp rows leave through TMA tensor stores (StoreMaps); implies coop
+  int wtw, wth, wtn;  // a warp's 32 rows as a (wtn images × wth rows × wtw cols) box of the tile
 };
 
 struct ConvDev {
@@ -53,10 +55,18 @@ struct ConvDev {
   EpiDev ep;
 };
 
+// Output tensor maps of the TMA-store epilogue: index 4·dest + view; view 0 for plain destinations, views
+// (dy·2+dx) for 2×-upsampled destinations and for the transposed conv's pixel shuffle.
+constexpr int kMaxStoreMaps = 4 * OSAM_MAX_DEST;
+struct StoreMaps {
+  CUtensorMap m[kMaxStoreMaps];
+};
+
 struct ConvLaunch {
   int BK, BN, mode;
   int grid;
   CUtensorMap ta, tb;
+  StoreMaps sm;
   ConvDev d;
   // transposed conv: weights must be re-laid out (C,R,S,K) → (R·S·K, C) before the GEMM
   const __half* wt_src = nullptr;

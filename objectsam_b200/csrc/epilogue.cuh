@@ -253,6 +253,99 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
   __syncwarp();
 }
 
+// TMA-store variant (EpiDev::tstore): the warp's 32 rows form a box (wtn images × wth rows × wtw cols)
+// whose origin on the GEMM grid is (bq, bp, bn).  After the math, the rows go into the per-warp stage in
+// the 64-byte TMA swizzle and one lane issues a tensor store per destination (four for 2× upsampled
+// destinations and for the transposed conv's pixel shuffle, one per (dy, dx) view).  The tensor engine
+// clips rows outside the output, so partial tiles need no masking.  W = 32 (64-byte stage rows).
+__device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMaps& maps, int K, int P, int Q,
+                                                  float* v, int col, const float* s_sc, const float* s_sh,
+                                                  bool valid, int n, int p, int q, int bq, int bp, int bn,
+                                                  uint8_t* stage) {
+  constexpr int W = 32, CPR = 4, RPI = 8;
+  const int lane = threadIdx.x & 31;
+  if (e.round_z) {
+#pragma unroll
+    for (int i = 0; i < W; i++) v[i] = __half2float(__float2half_rn(v[i]));
+  }
+  float y[W];
+  if (e.kind == OSAM_EPI_BN_ACT) {
+    float sc[W], sh[W];
+#pragma unroll
+    for (int i = 0; i < W; i += 4) {
+      *reinterpret_cast<float4*>(sc + i) = *reinterpret_cast<const float4*>(s_sc + col + i);
+      *reinterpret_cast<float4*>(sh + i) = *reinterpret_cast<const float4*>(s_sh + col + i);
+    }
+    if (e.act) {
+#pragma unroll
+      for (int i = 0; i < W; i++) y[i] = silu_f(fmaf(sc[i], v[i], sh[i]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < W; i++) y[i] = fmaf(sc[i], v[i], sh[i]);
+    }
+  } else if (e.kind == OSAM_EPI_BIAS) {
+#pragma unroll
+    for (int i = 0; i < W; i += 4) {
+      const float4 b = *reinterpret_cast<const float4*>(s_sh + col + i);
+      y[i] = v[i] + b.x;
+      y[i + 1] = v[i + 1] + b.y;
+      y[i + 2] = v[i + 2] + b.z;
+      y[i + 3] = v[i + 3] + b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < W; i++) y[i] = v[i];
+  }
+  // the stage is free once the previous pass's tensor store has read it
+  if (lane == 0) bulk_wait_group_read0();
+  __syncwarp();
+  if (e.kind == OSAM_EPI_BN_ACT && e.res) {
+    const int my_rv = valid ? (n * P + p) * Q + q : -1;
+#pragma unroll
+    for (int it = 0; it < CPR; it++) {
+      const int rr = it * RPI + lane / CPR, ch = lane % CPR;
+      const int rpix = __shfl_sync(0xffffffffu, my_rv, rr);
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (rpix >= 0) val = *reinterpret_cast<const uint4*>(e.res + (long long)rpix * K + col + ch * 8);
+      *reinterpret_cast<uint4*>(stage + stage_off(rr, ch)) = val;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int ch = 0; ch < CPR; ch++) {
+      float r8[8];
+      unpack8h(*reinterpret_cast<const uint4*>(stage + stage_off(lane, ch)), r8);
+#pragma unroll
+      for (int i = 0; i < 8; i++) y[ch * 8 + i] += r8[i];
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int ch = 0; ch < CPR; ch++) *reinterpret_cast<uint4*>(stage + stage_off(lane, ch)) = pack8h(y + ch * 8);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (e.shuffle) {
+      const int blk = col / e.kout;
+      tma_store_4d(&maps.m[blk], stage, col - blk * e.kout, bq, bp, bn);
+    } else {
+#pragma unroll
+      for (int t = 0; t < OSAM_MAX_DEST; t++) {
+        if (t >= e.ndest) break;
+        const DestDev& ds = e.dest[t];
+        if (col < ds.c0 || col >= ds.c1) continue;
+        const int kk = ds.choff + col - ds.c0;
+        if (ds.up == 1) {
+          tma_store_4d(&maps.m[4 * t], stage, kk, bq, bp, bn);
+        } else {
+#pragma unroll
+          for (int vw = 0; vw < 4; vw++) tma_store_4d(&maps.m[4 * t + vw], stage, kk, bq, bp, bn);
+        }
+      }
+    }
+    bulk_commit_group();
+  }
+}
+
 // Per-column epilogue constants of the tile starting at GEMM column n0 (BN columns) into shared memory:
 // s_sc = BN scale (1 otherwise), s_sh = BN shift or the bias (0 otherwise).
 __device__ __forceinline__ void load_epilogue_consts(const EpiDev& e, int gemm_n, int n0, int BN, int tid,
