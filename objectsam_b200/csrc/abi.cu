@@ -85,7 +85,9 @@ static int make_map(CUtensorMap* tm, const void* base, int rank, const uint64_t*
                                          (unsigned long long)strides_b[i]);
     }
   }
-  const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), gd, gs, bx, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -331,6 +333,49 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   if (p->mode == A_STEM) {
     L->x = static_cast<const __half*>(x);
     L->w = static_cast<const __half*>(w);
+    // Pipelined RGB stem: 3×3/s2/p1, C = 3, K = 32, 2 × 64-pixel tiles, all destinations TMA-storable.
+    bool rgb = g.R == 3 && g.S == 3 && g.C == 3 && g.stride == 2 && g.pad == 1 && g.K == 32 && p->Q % 64 == 0 &&
+               p->P % 2 == 0 && e.coop && !e.res && !e.shuffle && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+               ((size_t)g.W * 3 * 2) % 16 == 0;
+    for (int i = 0; i < e.ndest && rgb; i++) rgb = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
+    if (rgb) {
+      d.th = 2;
+      d.tw = 64;
+      d.tn = 1;
+      d.tiles_q = p->Q / 64;
+      d.tiles_p = p->P / 2;
+      d.tiles_m = d.tiles_q * d.tiles_p * g.N;
+      const uint64_t dims[3] = {(uint64_t)g.W * 3, (uint64_t)g.H, (uint64_t)g.N};
+      const uint64_t str[2] = {(uint64_t)g.W * 3 * 2, (uint64_t)g.H * g.W * 3 * 2};
+      const uint32_t box[3] = {208, 5, 1};
+      int rc = make_map(&L->ta, x, 3, dims, str, box, 0);
+      if (rc) return rc;
+      const uint32_t sbox[4] = {32, 32, 1, 1};
+      for (int t = 0; t < e.ndest && rc == OSAM_OK; t++) {
+        const DestDev& ds = e.dest[t];
+        const uint64_t c = (uint64_t)ds.ctot;
+        const bool four = ds.up == 2;
+        const uint64_t OQ2 = 2ull * p->Q, OP2 = 2ull * p->P;
+        for (int v = 0; v < (four ? 4 : 1) && rc == OSAM_OK; v++) {
+          const __half* b = ds.p + (four ? ((uint64_t)(v >> 1) * OQ2 + (v & 1)) * c : 0);
+          const uint64_t sd[4] = {c, (uint64_t)p->Q, (uint64_t)p->P, (uint64_t)g.N};
+          uint64_t ss[3];
+          if (four) {
+            ss[0] = 2 * c * 2;
+            ss[1] = 2 * OQ2 * c * 2;
+            ss[2] = OP2 * OQ2 * c * 2;
+          } else {
+            ss[0] = c * 2;
+            ss[1] = (uint64_t)p->Q * c * 2;
+            ss[2] = (uint64_t)p->P * p->Q * c * 2;
+          }
+          rc = make_map(&L->sm.m[4 * t + v], b, 4, sd, ss, sbox, 64);
+        }
+      }
+      if (rc) return rc;
+      e.tstore = 1;
+      L->stem_rgb = 1;
+    }
     return OSAM_OK;
   }
   int rc;
@@ -377,7 +422,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
 }
 
 cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st) {
-  if (L.mode == A_STEM) return launch_conv_stem(L.x, L.w, L.d, L.BN, st);
+  if (L.mode == A_STEM) return L.stem_rgb ? launch_conv_stem_rgb(L, st) : launch_conv_stem(L.x, L.w, L.d, L.BN, st);
   if (L.wt_src) {
     cudaError_t e = launch_convt_weight_relayout(L.wt_src, L.wt_dst, L.d.C, 4, L.d.K, st);
     if (e != cudaSuccess) return e;

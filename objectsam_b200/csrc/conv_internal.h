@@ -74,6 +74,7 @@ struct ConvLaunch {
   // A_STEM: raw operand pointers (no tensor maps)
   const __half* x = nullptr;
   const __half* w = nullptr;
+  int stem_rgb = 0;  // pipelined RGB stem kernel (window tensor map in ta, TMA-store epilogue)
 };
 
 // Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
@@ -91,6 +92,7 @@ cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st, bool prime_o
 cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st);
 cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st);
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
+cudaError_t launch_conv_stem_rgb(const ConvLaunch& L, cudaStream_t st);
 
 int* device_error_word();       // per-device error word (allocated on first use, before any capture)
 int static_scratch_take_error();  // error recorded by the static-scratch entry point's kernels (and clear it)

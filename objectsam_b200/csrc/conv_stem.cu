@@ -201,3 +201,220 @@ cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d,
 }
 
 }  // namespace osam
+
+// ------------------------------------------------------------------------------------------------
+// Pipelined RGB stem (3×3, stride 2, pad 1, C = 3, K = 32): tiles of 2 output rows × 64 columns of one
+// image, persistent over the tile list, warp-specialised like the main conv kernel:
+//   warp 0       TMA: the tile's input window (5 rows × 387 fp16, i.e. 129 pixels × 3 channels) as two
+//                208-element boxes of the (W·C, H, N) view into a 6-slot ring; the out-of-range zero fill
+//                of the tensor engine supplies every conv pad (top/bottom rows, left/right columns);
+//   warps 2..5   im2col: each thread turns its pixel's 27 taps (from the window) into one 64-byte
+//                swizzled K-major row of the A tile (4-slot ring);
+//   warp 1       TMEM owner + MMA issuer: two K=16 UMMAs per tile into one of two accumulators;
+//   warps 6..9   epilogue: folded BN + SiLU and TMA tensor stores of whole 32-pixel row blocks.
+// The weights (32 × 27, zero-padded to 32 × 32) stay in shared memory for the whole kernel.
+namespace osam {
+
+constexpr int kS2Win = 6, kS2A = 4;
+constexpr int kS2Box = 208;                  // fp16 elements per window box row (416 B)
+constexpr int kS2BoxBytes = 2176;            // one box of 5 rows (2080 B), padded to 128 B
+constexpr int kS2WinBytes = 2 * kS2BoxBytes;  // two boxes per window
+constexpr int kS2Smem = 1024 + kS2A * 8192 + 2048 + 4 * 2048 + kS2Win * kS2WinBytes + 2 * 32 * 4 + 512;
+
+__global__ void __launch_bounds__(320, 1)
+    k_conv_stem_rgb(const __grid_constant__ CUtensorMap tw, const __grid_constant__ StoreMaps sm,
+                    const __half* __restrict__ w, const ConvDev d) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = base;                         // kS2A × 8 KiB, 1024-aligned
+  uint8_t* sB = sA + kS2A * 8192;             // 32 × 64 B
+  uint8_t* s_stage = sB + 2048;               // 4 epilogue warps × 2 KiB (1024-aligned)
+  uint8_t* s_win = s_stage + 4 * 2048;        // kS2Win windows
+  float* s_sc = reinterpret_cast<float*>(s_win + kS2Win * kS2WinBytes);
+  float* s_sh = s_sc + 32;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(s_sh + 32);
+  uint64_t* wempty = wfull + kS2Win;
+  uint64_t* afull = wempty + kS2Win;
+  uint64_t* aempty = afull + kS2A;
+  uint64_t* accf = aempty + kS2A;
+  uint64_t* acce = accf + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = d.tiles_m;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kS2Win; i++) {
+      mbar_init(wfull + i, 1);
+      mbar_init(wempty + i, 4);
+    }
+    for (int i = 0; i < kS2A; i++) {
+      mbar_init(afull + i, 4);
+      mbar_init(aempty + i, 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(accf + i, 1);
+      mbar_init(acce + i, 4);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tw);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 64);
+    tmem_relinquish();
+  }
+  // weights: row k = the 27 taps of output channel k (KRSC), zero-padded to 32, 64-byte swizzle
+  for (int i = threadIdx.x; i < 32 * 4; i += blockDim.x) {
+    const int r = i >> 2, ch = i & 3;
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int kk = ch * 8 + e;
+      v[e] = (r < d.K && kk < 27) ? w[r * 27 + kk] : __float2half(0.f);
+    }
+    *reinterpret_cast<uint4*>(sB + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)) = *reinterpret_cast<const uint4*>(v);
+  }
+  if (threadIdx.x < 32) load_epilogue_consts(d.ep, d.gemm_n, 0, 32, threadIdx.x, 32, s_sc, s_sh);
+  fence_proxy_async_smem();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- window producer
+    if (lane == 0) {
+      int lt = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+        const int s = lt % kS2Win;
+        if (lt >= kS2Win && !mbar_wait(wempty + s, ((lt / kS2Win) - 1) & 1, d.err)) break;
+        const int tq = t % d.tiles_q, rest = t / d.tiles_q, tp = rest % d.tiles_p, n = rest / d.tiles_p;
+        const int x0 = (2 * tq * 64 - 1) * 3;          // first element of the window row in the W·C row
+        const int xa = x0 >= 0 ? (x0 & ~7) : -((-x0 + 7) & ~7);  // aligned down to 8 elements (16 B)
+        const int ih0 = 2 * tp * 2 - 1;
+        mbar_arrive_expect_tx(wfull + s, 2 * 5 * kS2Box * 2);
+        uint8_t* dst = s_win + s * kS2WinBytes;
+        tma_load_3d(dst, &tw, wfull + s, xa, ih0, n);
+        tma_load_3d(dst + kS2BoxBytes, &tw, wfull + s, xa + kS2Box, ih0, n);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, 32);
+      int lt = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+        const int s = lt % kS2A;
+        const uint32_t buf = lt & 1;
+        if (lt >= 2 && !mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err)) break;
+        if (!mbar_wait(afull + s, (lt / kS2A) & 1, d.err)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(sA + s * 8192), b = smem_u32(sB);
+        umma_f16(tmem + buf * 32, smem_desc_kmajor(a, 64), smem_desc_kmajor(b, 64), idesc, 0);
+        umma_f16(tmem + buf * 32, smem_desc_kmajor(a + 32, 64), smem_desc_kmajor(b + 32, 64), idesc, 1);
+        umma_commit(aempty + s);
+        umma_commit(accf + buf);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- im2col (one A row per thread)
+    const int tid = threadIdx.x - 64;  // 0..127 = row of the A tile
+    const int i = tid >> 6, j = tid & 63;
+    int lt = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+      const int ws = lt % kS2Win, as = lt % kS2A;
+      if (!mbar_wait(wfull + ws, (lt / kS2Win) & 1, d.err)) break;
+      if (lt >= kS2A && !mbar_wait(aempty + as, ((lt / kS2A) - 1) & 1, d.err)) break;
+      const int tq = t % d.tiles_q;
+      const int x0 = (2 * tq * 64 - 1) * 3;
+      const int xa = x0 >= 0 ? (x0 & ~7) : -((-x0 + 7) & ~7);
+      const int off = x0 - xa;  // window element of input column iw0
+      const __half* win = reinterpret_cast<const __half*>(s_win + ws * kS2WinBytes);
+      const int iw_first = 2 * (tq * 64 + j) - 1;  // input column of tap s = 0
+      __align__(16) __half row[32];
+#pragma unroll
+      for (int r = 0; r < 3; r++) {
+        const int wr = 2 * i + r;  // window row (rows outside the image arrive as zeros)
+#pragma unroll
+        for (int s = 0; s < 3; s++) {
+          const bool col_in = iw_first + s >= 0 && iw_first + s < d.W;
+#pragma unroll
+          for (int c = 0; c < 3; c++) {
+            const int e = off + (2 * j + s) * 3 + c;  // element in the window row
+            const __half* src = e < kS2Box ? win + wr * kS2Box + e : win + kS2BoxBytes / 2 + wr * kS2Box + (e - kS2Box);
+            row[(r * 3 + s) * 3 + c] = col_in ? *src : __float2half(0.f);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 27; k < 32; k++) row[k] = __float2half(0.f);
+      uint8_t* dst = sA + as * 8192 + tid * 64;
+#pragma unroll
+      for (int ch = 0; ch < 4; ch++)
+        *reinterpret_cast<uint4*>(dst + ((ch ^ ((tid >> 1) & 3)) << 4)) = reinterpret_cast<const uint4*>(row)[ch];
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(afull + as);
+        mbar_arrive(wempty + ws);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 6..9)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    uint8_t* stage = s_stage + (warp - 6) * 2048;
+    int lt = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+      const int tq = t % d.tiles_q, rest = t / d.tiles_q, tp = rest % d.tiles_p, n = rest / d.tiles_p;
+      const int p = tp * 2 + (row >> 6), q = tq * 64 + (row & 63);
+      const bool valid = p < d.P && q < d.Q;
+      const int bq = tq * 64 + ((quad * 32) & 63), bp = tp * 2 + (quad >> 1);
+      const uint32_t buf = lt & 1;
+      const bool ok = mbar_wait(accf + buf, (lt >> 1) & 1, d.err);
+      tc_fence_after();
+      if (!ok) break;
+      uint32_t r0[16], r1[16];
+      const uint32_t dt = tmem + buf * 32 + ((uint32_t)(quad * 32) << 16);
+      tmem_ld16_nowait(dt, r0);
+      tmem_ld16_nowait(dt + 16, r1);
+      tmem_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        v[k] = __uint_as_float(r0[k]);
+        v[16 + k] = __uint_as_float(r1[k]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce + buf);  // accumulator registers are loaded: TMEM may be reused
+      epilogue_warp_tma(d.ep, sm, d.K, d.P, d.Q, v, 0, s_sc, s_sh, valid, n, p, q, bq, bp, n, stage);
+    }
+    if (lane == 0) bulk_wait_group0();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+cudaError_t launch_conv_stem_rgb(const ConvLaunch& L, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv_stem_rgb, cudaFuncAttributeMaxDynamicSharedMemorySize, kS2Smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int grid = L.d.tiles_m < sms ? L.d.tiles_m : sms;
+  k_conv_stem_rgb<<<grid, 320, kS2Smem, st>>>(L.ta, L.sm, L.w, L.d);
+  return cudaGetLastError();
+}
+
+}  // namespace osam

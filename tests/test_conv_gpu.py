@@ -53,6 +53,7 @@ SHAPES = [
     (2, 10, 10, 512, 512, 1, 1),
     (1, 7, 9, 64, 32, 1, 1),
     (2, 64, 64, 3, 32, 3, 2),
+    (2, 128, 256, 3, 32, 3, 2),
     (1, 70, 90, 3, 32, 3, 2),
     (2, 40, 36, 3, 16, 3, 1),
     (1, 80, 80, 64, 64, 3, 1),
@@ -121,7 +122,8 @@ def test_fused_1x1_k512_upsample_dest(cuda_lib):
     assert cat[..., :256].abs().max().item() == 0 and cat_up[..., 512:].abs().max().item() == 0
 
 
-@pytest.mark.parametrize("shape", [(2, 64, 64, 3, 32, 3, 2), (1, 70, 90, 3, 32, 3, 2), (2, 40, 36, 3, 16, 3, 1)],
+@pytest.mark.parametrize("shape", [(2, 64, 64, 3, 32, 3, 2), (2, 128, 256, 3, 32, 3, 2), (3, 256, 128, 3, 32, 3, 2),
+                                   (1, 70, 90, 3, 32, 3, 2), (2, 40, 36, 3, 16, 3, 1)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_fused_stem_bn_silu(cuda_lib, shape):
     """The C = 3 stem with its folded-BN + SiLU epilogue (model.0)."""
