@@ -221,7 +221,7 @@ constexpr int kS2BoxBytes = 2176;            // one box of 5 rows (2080 B), padd
 constexpr int kS2WinBytes = 2 * kS2BoxBytes;  // two boxes per window
 constexpr int kS2Smem = 1024 + kS2A * 8192 + 2048 + 4 * 2048 + kS2Win * kS2WinBytes + 2 * 32 * 4 + 512;
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(320, 2)
     k_conv_stem_rgb(const __grid_constant__ CUtensorMap tw, const __grid_constant__ StoreMaps sm,
                     const __half* __restrict__ w, const ConvDev d) {
   extern __shared__ uint8_t smem_raw[];
@@ -412,7 +412,7 @@ cudaError_t launch_conv_stem_rgb(const ConvLaunch& L, cudaStream_t st) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const int grid = L.d.tiles_m < sms ? L.d.tiles_m : sms;
+  const int grid = L.d.tiles_m < 2 * sms ? L.d.tiles_m : 2 * sms;  // two CTAs per SM
   k_conv_stem_rgb<<<grid, 320, kS2Smem, st>>>(L.ta, L.sm, L.w, L.d);
   return cudaGetLastError();
 }

@@ -268,33 +268,38 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMa
 #pragma unroll
     for (int i = 0; i < W; i++) v[i] = __half2float(__float2half_rn(v[i]));
   }
-  float y[W];
+  float* y = v;  // in place: keeps the live register set small
   if (e.kind == OSAM_EPI_BN_ACT) {
-    float sc[W], sh[W];
-#pragma unroll
-    for (int i = 0; i < W; i += 4) {
-      *reinterpret_cast<float4*>(sc + i) = *reinterpret_cast<const float4*>(s_sc + col + i);
-      *reinterpret_cast<float4*>(sh + i) = *reinterpret_cast<const float4*>(s_sh + col + i);
-    }
     if (e.act) {
 #pragma unroll
-      for (int i = 0; i < W; i++) y[i] = silu_f(fmaf(sc[i], v[i], sh[i]));
+      for (int i = 0; i < W; i += 4) {
+        const float4 sc = *reinterpret_cast<const float4*>(s_sc + col + i);
+        const float4 sh = *reinterpret_cast<const float4*>(s_sh + col + i);
+        y[i] = silu_f(fmaf(sc.x, v[i], sh.x));
+        y[i + 1] = silu_f(fmaf(sc.y, v[i + 1], sh.y));
+        y[i + 2] = silu_f(fmaf(sc.z, v[i + 2], sh.z));
+        y[i + 3] = silu_f(fmaf(sc.w, v[i + 3], sh.w));
+      }
     } else {
 #pragma unroll
-      for (int i = 0; i < W; i++) y[i] = fmaf(sc[i], v[i], sh[i]);
+      for (int i = 0; i < W; i += 4) {
+        const float4 sc = *reinterpret_cast<const float4*>(s_sc + col + i);
+        const float4 sh = *reinterpret_cast<const float4*>(s_sh + col + i);
+        y[i] = fmaf(sc.x, v[i], sh.x);
+        y[i + 1] = fmaf(sc.y, v[i + 1], sh.y);
+        y[i + 2] = fmaf(sc.z, v[i + 2], sh.z);
+        y[i + 3] = fmaf(sc.w, v[i + 3], sh.w);
+      }
     }
   } else if (e.kind == OSAM_EPI_BIAS) {
 #pragma unroll
     for (int i = 0; i < W; i += 4) {
       const float4 b = *reinterpret_cast<const float4*>(s_sh + col + i);
-      y[i] = v[i] + b.x;
-      y[i + 1] = v[i + 1] + b.y;
-      y[i + 2] = v[i + 2] + b.z;
-      y[i + 3] = v[i + 3] + b.w;
+      y[i] += b.x;
+      y[i + 1] += b.y;
+      y[i + 2] += b.z;
+      y[i + 3] += b.w;
     }
-  } else {
-#pragma unroll
-    for (int i = 0; i < W; i++) y[i] = v[i];
   }
   // the stage is free once the previous pass's tensor store has read it
   if (lane == 0) bulk_wait_group_read0();
