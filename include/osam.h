@@ -117,6 +117,36 @@ int osam_convt_fwd_static_scratch(const osam_conv_plan* plan, const void* x, con
 int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Inference post-process (the reference has it only in numpy: archive/tools/ref_detect.py:37-81).
+ * level_hw = {h0, w0, h1, w1, h2, w2} of the three head levels; anchors = Σ h·w, level-major, row-major.
+ * ------------------------------------------------------------------------------------------------ */
+
+/* DFL decode of the raw heads (NHWC fp16: box[l] 4·reg_max channels, cls[l] 1 channel) into xyxy boxes in
+ * input pixels (float [batch][anchors][4]) and conf = sigmoid(cls) (float [batch][anchors]).  Follows the
+ * reference's DFL decode (src/loss.cu:128-147) and the exported xywh → ref_detect xyxy conversion
+ * (archive/tools/ref_detect.py:44-45). */
+int osam_decode(const void* const* box, const void* const* cls, const int* level_hw, int batch, int imgsz,
+                int reg_max, float* xyxy, float* conf, osam_stream_t stream);
+
+/* Score threshold, stable descending sort and greedy NMS per image (archive/tools/ref_detect.py:41-60):
+ * conf > conf_th, strict IoU > iou_th suppression (only when the union is > 0), at most max_det kept.
+ * forced = 1 skips threshold and suppression and keeps the max_det highest scores.  Outputs per image:
+ * n_det[b], keep[b][max_det] (anchor indices in score order, −1 padded), det_box[b][max_det][4],
+ * det_score[b][max_det].  With coef (NHWC fp16 heads, 32 ch) and coef_g non-NULL, the kept anchors'
+ * mask coefficients are gathered into coef_g [batch][ceil128(max_det)][32] fp16 for osam_mask_assemble.
+ * Kept indices are bit-exact with the reference's loop for the same boxes and scores. */
+int osam_nms(const float* xyxy, const float* conf, int batch, int anchors, float conf_th, float iou_th, int max_det,
+             int forced, const void* const* coef, const int* level_hw, int* n_det, int* keep, float* det_box,
+             float* det_score, void* coef_g, osam_stream_t stream);
+
+/* Mask assembly (archive/tools/ref_detect.py:62-71) as a tensor-core GEMM per image:
+ * logits = coef_g[b] (ceil128(max_det) × 32) · proto[b] (32 × Hp·Wp, proto NHWC fp16), fused with
+ * mask = logit > 0 (≡ sigmoid > 0.5) ∩ the detection box scaled to the proto grid (g = Wp / imgsz).
+ * masks: u8 [batch][max_det][Hp·Wp], rows ≥ n_det[b] are zero. */
+int osam_mask_assemble(const void* coef_g, const void* proto, const float* det_box, const int* n_det, int batch,
+                       int proto_h, int proto_w, int imgsz, int max_det, unsigned char* masks, osam_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------
  * YOLOv8s-seg (nc = 1) inference graph on the kernels above.  Replaces the reference's Model
  * (src/model.h:97-140): build (src/model.cpp:168-347), Params::load + sync_weights (:49-62, :369),
  * forward(false) (:383-414), input()/head()/proto() accessors.  Every conv node runs as one fused

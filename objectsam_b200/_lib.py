@@ -59,6 +59,12 @@ _SIGS = {
     "osam_conv_fwd_fused": (c_int, [c_void_p, c_void_p, c_void_p, POINTER(Epilogue), c_void_p, c_size_t, c_void_p]),
     "osam_convt_fwd_static_scratch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
     "osam_sppf_fwd": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "osam_decode": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,
+                            c_void_p, c_void_p]),
+    "osam_nms": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_int, c_int, POINTER(c_void_p),
+                         POINTER(c_int), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "osam_mask_assemble": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                   c_void_p, c_void_p]),
     "osam_model_create": (c_int, [c_int, c_int, c_int, POINTER(c_void_p)]),
     "osam_model_destroy": (c_int, [c_void_p]),
     "osam_model_set_param": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, POINTER(c_int64), c_int]),
