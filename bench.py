@@ -4,9 +4,10 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B] [--imgsz S]
 
 One process per GPU (torchrun for N > 1); images are sharded across ranks with no collective (weak
-scaling: every rank runs its own batch).  A step is one forward pass of the fused conv path over the
-rank's batch: stem → backbone → SPPF → neck → Segment head → proto, every conv one kernel with its
-folded-BN/SiLU/residual/concat epilogue.  Timing: W untimed warm-up steps, then K steps between a
+scaling: every rank runs its own batch).  A step is the config-2 inference of the rank's batch: the
+forward pass of the fused conv path (stem → backbone → SPPF → neck → Segment head → proto, every conv
+one kernel with its folded-BN/SiLU/residual/concat epilogue), then DFL decode, conf > 0.25, NMS IoU 0.7,
+≤ 300 detections per image and the mask assembly (coef · proto > 0, cropped), masks bit-packed.  Timing: W untimed warm-up steps, then K steps between a
 barrier + synchronize on both sides, CUDA events on the launching stream, max over ranks.  The inputs
 (157 MB per step) and activations (GBs) are larger than the 126 MB L2, so no flush is needed.
 
@@ -129,8 +130,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(load)}
 
 
+def cpu_infer_one(m, img, imgsz):
+    """One CPU inference of the config-2 workload: PyTorch forward (oracle/yolo_ref.py) + the numpy
+    post-process of the reference (oracle/postproc_ref.py: conf 0.25, NMS 0.7, ≤ 300 dets, masks)."""
+    from oracle import postproc_ref
+    o = m.forward(img)
+    xywh, conf, coefs = postproc_ref.decode(o["box"], o["cls"], o["coef"])
+    return postproc_ref.detect_one(xywh[0], conf[0], coefs[0], o["proto"][0].numpy(), imgsz, 0.25, 0.7, 300)
+
+
 def cpu_forward_sample(imgsz: int, budget_s: float, seed: int = 0):
-    """PyTorch CPU forward of the network (oracle), batch-1 images until the budget is spent."""
+    """CPU inference (PyTorch forward + numpy post-process), batch-1 images until the budget is spent."""
     import torch
     from oracle import yolo_params, yolo_ref
     cores = os.cpu_count() or 1
@@ -138,16 +148,17 @@ def cpu_forward_sample(imgsz: int, budget_s: float, seed: int = 0):
     w = yolo_params.make_weights(0)
     m = yolo_ref.YoloSegRef(w, emulate_fp16=False)
     img = yolo_params.make_images(1, imgsz, seed)
-    m.forward(img)  # warm-up
+    cpu_infer_one(m, img, imgsz)  # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
-        m.forward(img)
+        cpu_infer_one(m, img, imgsz)
         n += 1
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
     return dict(value=n / dt, unit=UNIT, cores=torch.get_num_threads(), kind="port",
-                sample=f"{n} batch-1 {imgsz}x{imgsz} forwards of the PyTorch CPU restatement (fp32), {dt:.1f} s")
+                sample=f"{n} batch-1 {imgsz}x{imgsz} inferences (PyTorch CPU forward fp32 + numpy "
+                       f"decode/NMS/masks of ref_detect), {dt:.1f} s")
 
 
 def reference_cudnn(B: int, S: int, iters: int = 10):
@@ -181,21 +192,23 @@ def run_reference(args, rank, world):
     m = yolo_ref.YoloSegRef(yolo_params.make_weights(0), emulate_fp16=False)
     img = yolo_params.make_images(1, args.imgsz, 0)
     for _ in range(max(1, args.warmup)):
-        m.forward(img)
+        cpu_infer_one(m, img, args.imgsz)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        m.forward(img)
+        cpu_infer_one(m, img, args.imgsz)
     dt = time.perf_counter() - t0
     v = args.steps / dt
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"YOLOv8s-seg nc=1 forward, {args.imgsz}x{args.imgsz}, batch-1 sample per step",
+            "config": {"workload": f"YOLOv8s-seg nc=1 inference (forward + conf/NMS/masks), {args.imgsz}x{args.imgsz}, "
+                                   "batch-1 sample per step",
                        "imgsz": args.imgsz, "parallelism": "rank 0 only (host cores)"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{args.steps} timed batch-1 forwards of the PyTorch CPU restatement "
-                                       "(the reference implements this path only as its cuDNN build)"},
+                             "sample": f"{args.steps} timed batch-1 inferences: PyTorch CPU forward + the numpy "
+                                       "post-process of ref_detect (the reference implements the conv path only as "
+                                       "its cuDNN build)"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -219,6 +232,7 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    from objectsam_b200 import postproc
     from objectsam_b200.model import Model
     from oracle import yolo_params  # seeded synthetic weights/images only (the checker is not timed)
 
@@ -232,15 +246,39 @@ def main():
     n = len(nodes)
     stream = torch.cuda.current_stream()
 
+    box = [model.head(0, l) for l in range(3)]
+    cls = [model.head(1, l) for l in range(3)]
+    coef = [model.head(2, l) for l in range(3)]
+    proto = model.proto()
+
+    def post():
+        xyxy, conf = postproc.decode(box, cls, S)
+        det = postproc.nms(xyxy, conf, 0.25, 0.7, 300, coef=coef)
+        det["masks"] = postproc.mask_assemble(det["coef_g"], proto, det, S, packed=True)
+        return det
+
+    post_names = ["postproc.decode", "postproc.nms", "postproc.masks"]
+    nodes = nodes + [dict(index=n + i, name=nm, kind=4 + i, flops=0.0, bytes=0.0) for i, nm in enumerate(post_names)]
+    # algorithmic bytes of the post-process kernels: heads read / candidates / packed mask writes + proto reads
+    A = sum((S // s) ** 2 for s in (8, 16, 32))
+    nodes[n]["bytes"] = B * A * (64 + 1) * 2.0 + B * A * 5 * 4.0
+    nodes[n + 1]["bytes"] = B * A * 5 * 4.0 + B * 300 * (4 + 16 + 4 + 64)
+    Hp = S // 4
+    nodes[n + 2]["bytes"] = B * (384 * 64 + 300 * Hp * Hp / 8 + 3 * Hp * Hp * 64.0)
+    nodes[n + 2]["flops"] = 2.0 * B * 384 * 32 * Hp * Hp
+    n_all = len(nodes)
+
     # ---- warm-up (eager + graph)
     for _ in range(args.warmup):
         model.forward()
+        post()
     model.forward(use_graph=True)
+    post()
     barrier()
 
-    # ---- timed region: K eager steps, a CUDA event before every node and after the last
+    # ---- timed region: K eager steps, a CUDA event before every kernel and after the last
     K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n + 1)] for _ in range(K)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_all + 1)] for _ in range(K)]
     with ClockSampler(local) as clk:
         barrier()
         for k in range(K):
@@ -249,47 +287,58 @@ def main():
                 row[i].record(stream)
                 model.forward_nodes(i, 1)
             row[n].record(stream)
+            xyxy, conf = postproc.decode(box, cls, S)
+            row[n + 1].record(stream)
+            det = postproc.nms(xyxy, conf, 0.25, 0.7, 300, coef=coef)
+            row[n + 2].record(stream)
+            det["masks"] = postproc.mask_assemble(det["coef_g"], proto, det, S, packed=True)
+            row[n + 3].record(stream)
         barrier()
-    ms = evs[0][0].elapsed_time(evs[K - 1][n])
-    node_ms = [sum(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K)) / K for i in range(n)]
+    ms = evs[0][0].elapsed_time(evs[K - 1][n_all])
+    node_ms = [sum(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K)) / K for i in range(n_all)]
+    fwd_ms = sum(node_ms[:n])
     clocks = clk.summary()
+    n_det_mean = float(det["n_det"].float().mean().item())
 
-    # graph-replay timing of the same step (launch-overhead-free variant), informational
+    # graph-replay timing of the forward + the post-process launches, informational
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     g0.record(stream)
     for _ in range(K):
         model.forward(use_graph=True)
+        post()
     g1.record(stream)
     barrier()
     graph_ms = g0.elapsed_time(g1)
 
-    t = torch.tensor([ms, graph_ms], device=dev)
+    t = torch.tensor([ms, graph_ms, fwd_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, graph_ms = t.tolist()
+    ms, graph_ms, fwd_ms = t.tolist()
     value = world * B * K / (ms / 1e3)
 
     # ---- e2e: host buffers through the C-ABI model, copies inside the timed region
     e2e = None
     if not args.no_e2e:
         h_in = imgs.pin_memory()
-        outs = [model.head(k, l) for k in range(3) for l in range(3)] + [model.proto()]
-        h_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
         d_in = model.input()
-        for _ in range(2):
+        keys = ("n_det", "keep", "box", "score", "masks")
+        h_out = {k: torch.empty(det[k].shape, dtype=det[k].dtype, pin_memory=True) for k in keys}
+
+        def e2e_step():
             d_in.copy_(h_in, non_blocking=True)
             model.forward(use_graph=True)
-            for h, d in zip(h_out, outs):
-                h.copy_(d, non_blocking=True)
+            dd = post()
+            for k in keys:
+                h_out[k].copy_(dd[k], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(K):
-            d_in.copy_(h_in, non_blocking=True)
-            model.forward(use_graph=True)
-            for h, d in zip(h_out, outs):
-                h.copy_(d, non_blocking=True)
+            e2e_step()
         e1.record(stream)
         barrier()
         te = torch.tensor([e0.elapsed_time(e1)], device=dev)
@@ -297,11 +346,12 @@ def main():
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": world * B * K / (te.item() / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
-               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in h_out)}
+               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in h_out.values()),
+               "result": "detections (n_det, anchor ids, xyxy boxes, scores) + bit-packed 160x160 masks"}
 
     # ---- roofline of the dominant kernel
     peaks = load_peaks()
-    top = max(range(n), key=lambda i: node_ms[i])
+    top = max(range(n_all), key=lambda i: node_ms[i])
     nd = nodes[top]
     ridge = peaks["tflops_sust"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
     bound = "tensor" if nd["flops"] / max(nd["bytes"], 1) > ridge else "hbm"
@@ -320,39 +370,42 @@ def main():
     if args.nodes_out and rank == 0:
         with open(args.nodes_out, "w") as f:
             json.dump([dict(nd_, ms=node_ms[i]) for i, nd_ in enumerate(nodes)], f, indent=0)
-    conv_flops = sum(x["flops"] for x in nodes)
+    conv_flops = sum(x["flops"] for x in nodes[:n])
     roofline = {"bound": bound, "achieved": ach, "peak": peak, "unit": unit_r, "frac": ach / peak,
                 "traffic": traffic, "kernel": nd["name"], "kernel_ms": node_ms[top],
                 "peak_source": f"{peaks['src']} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
                 "algorithmic_flops": nd["flops"], "algorithmic_bytes": nd["bytes"],
-                "forward_conv_tflops": conv_flops / (ms / K / 1e3) / 1e12}
+                "forward_conv_tflops": conv_flops / (fwd_ms / K / 1e3) / 1e12}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_forward_sample(S, args.cpu_sample_s)
     ref_cudnn = None
     if rank == 0 and world == 1 and not args.no_ref_cudnn:
+        del box, cls, coef, proto, det
         model.close()  # release our activations before the reference allocates its own
         torch.cuda.synchronize()
         ref_cudnn = reference_cudnn(B, S)
         if "img_per_s" in ref_cudnn:
-            ref_cudnn["speedup_ours_over_ref"] = value / ref_cudnn["img_per_s"]
+            ref_cudnn["speedup_forward_only"] = (B * 1e3 / (fwd_ms / K)) / ref_cudnn["img_per_s"]
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
                 "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
-                "config": {"workload": f"BASELINE config 2: YOLOv8s-seg nc=1 inference forward (heads + proto), "
-                                       f"batch {B}/GPU, {S}x{S} NHWC fp16, seeded U[0,1] images, He-normal weights",
+                "config": {"workload": f"BASELINE config 2: YOLOv8s-seg nc=1 inference (forward + decode, conf 0.25, "
+                                       f"NMS 0.7, <=300 dets, masks), batch {B}/GPU, {S}x{S} NHWC fp16, seeded "
+                                       f"U[0,1] images, He-normal weights",
                            "global_batch": B * world, "imgsz": S, "parallelism": f"dp{world} (image shards, no collective)",
                            "l2": "inputs+activations > 126 MB L2 (no flush needed)",
                            "timing": "eager launches with a CUDA event per node over the timed region"},
-                "gpu_launches": K * n, "clocks": clocks, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": K * n_all, "clocks": clocks, "forward_only_img_per_s": world * B * 1e3 / (fwd_ms / K),
+                "detections_per_image": n_det_mean, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "graph_ms_per_step": graph_ms / K, "reference_cudnn": ref_cudnn,
                 "top_kernels": sorted(({"name": nodes[i]["name"], "ms": round(node_ms[i], 4),
                                         "tflops": round(nodes[i]["flops"] / (node_ms[i] / 1e3) / 1e12, 1),
                                         "gbs": round(nodes[i]["bytes"] / (node_ms[i] / 1e3) / 1e9, 0)}
-                                       for i in range(n)), key=lambda d: -d["ms"])[:12]}
+                                       for i in range(n_all)), key=lambda d: -d["ms"])[:12]}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

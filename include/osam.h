@@ -142,9 +142,11 @@ int osam_nms(const float* xyxy, const float* conf, int batch, int anchors, float
 /* Mask assembly (archive/tools/ref_detect.py:62-71) as a tensor-core GEMM per image:
  * logits = coef_g[b] (ceil128(max_det) × 32) · proto[b] (32 × Hp·Wp, proto NHWC fp16), fused with
  * mask = logit > 0 (≡ sigmoid > 0.5) ∩ the detection box scaled to the proto grid (g = Wp / imgsz).
- * masks: u8 [batch][max_det][Hp·Wp], rows ≥ n_det[b] are zero. */
+ * masks: packed = 0 → u8 [batch][max_det][Hp·Wp]; packed = 1 → u32 [batch][max_det][ceil(Hp·Wp/32)] with
+ * pixel 32·j + k in bit k of word j.  Rows ≥ n_det[b] are zero. */
 int osam_mask_assemble(const void* coef_g, const void* proto, const float* det_box, const int* n_det, int batch,
-                       int proto_h, int proto_w, int imgsz, int max_det, unsigned char* masks, osam_stream_t stream);
+                       int proto_h, int proto_w, int imgsz, int max_det, int packed, void* masks,
+                       osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------
  * YOLOv8s-seg (nc = 1) inference graph on the kernels above.  Replaces the reference's Model

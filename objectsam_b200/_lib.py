@@ -64,7 +64,7 @@ _SIGS = {
     "osam_nms": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_int, c_int, POINTER(c_void_p),
                          POINTER(c_int), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "osam_mask_assemble": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
-                                   c_void_p, c_void_p]),
+                                   c_int, c_void_p, c_void_p]),
     "osam_model_create": (c_int, [c_int, c_int, c_int, POINTER(c_void_p)]),
     "osam_model_destroy": (c_int, [c_void_p]),
     "osam_model_set_param": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, POINTER(c_int64), c_int]),

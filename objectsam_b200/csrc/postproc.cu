@@ -251,7 +251,8 @@ struct MaskArgs {
   const __half* proto;   // [B][Hp·Wp][32]
   const float* det_box;  // [B][max_det][4]
   const int* n_det;
-  uint8_t* masks;        // [B][max_det][Hp·Wp]
+  uint8_t* masks;        // [B][max_det][Hp·Wp] bytes, or packed bits [B][max_det][ceil32(Hp·Wp)/32] u32
+  int packed;            // 1: one bit per pixel (bit k of word j = pixel 32·j + k)
   int Hp, Wp, max_det, max_det_pad;
   float g;               // proto grid units per input pixel (Wp / S)
   int ptiles;            // pixel tiles of 256 per image
@@ -314,7 +315,10 @@ __global__ void __launch_bounds__(128) k_mask(const MaskArgs a) {
       const float4 o = reinterpret_cast<const float4*>(a.det_box)[(long long)b * a.max_det + det];
       bx = make_float4(__fmul_rn(o.x, a.g), __fmul_rn(o.y, a.g), __fmul_rn(o.z, a.g), __fmul_rn(o.w, a.g));
     }
+    const int nwords = (npix + 31) / 32;
     uint8_t* out = a.masks + ((long long)b * a.max_det + det) * npix + p0;
+    uint32_t* outw = reinterpret_cast<uint32_t*>(a.masks) + ((long long)b * a.max_det + det) * nwords + p0 / 32;
+    uint32_t bits = 0u;
 #pragma unroll 1
     for (int c = 0; c < 256; c += 16) {
       __syncwarp();
@@ -322,14 +326,22 @@ __global__ void __launch_bounds__(128) k_mask(const MaskArgs a) {
       tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
       if (det >= a.max_det || p0 + c >= npix) continue;
       uint32_t w4[4] = {0u, 0u, 0u, 0u};
+      uint32_t m16 = 0u;
 #pragma unroll
       for (int k = 0; k < 16; k++) {
         const int pix = p0 + c + k;
         const float yy = (float)(pix / a.Wp), xx = (float)(pix - (pix / a.Wp) * a.Wp);
-        const bool m = live && v[k] > 0.f && xx >= bx.x && xx < bx.z && yy >= bx.y && yy < bx.w;
+        const bool m = live && pix < npix && v[k] > 0.f && xx >= bx.x && xx < bx.z && yy >= bx.y && yy < bx.w;
         w4[k >> 2] |= (m ? 1u : 0u) << ((k & 3) * 8);
+        m16 |= (m ? 1u : 0u) << k;
       }
-      if (p0 + c + 16 <= npix && (npix & 15) == 0) {
+      if (a.packed) {
+        bits |= m16 << (c & 16);
+        if ((c & 16) || p0 + c + 16 >= npix) {
+          outw[c / 32] = bits;
+          bits = 0u;
+        }
+      } else if (p0 + c + 16 <= npix && (npix & 15) == 0) {
         *reinterpret_cast<uint4*>(out + c) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       } else {
         for (int k = 0; k < 16 && p0 + c + k < npix; k++) out[c + k] = (w4[k >> 2] >> ((k & 3) * 8)) & 0xff;
@@ -444,7 +456,8 @@ int osam_nms(const float* xyxy, const float* conf, int batch, int anchors, float
 }
 
 int osam_mask_assemble(const void* coef_g, const void* proto, const float* det_box, const int* n_det, int batch,
-                       int proto_h, int proto_w, int imgsz, int max_det, unsigned char* masks, osam_stream_t stream) {
+                       int proto_h, int proto_w, int imgsz, int max_det, int packed, void* masks,
+                       osam_stream_t stream) {
   if (!coef_g || !proto || !det_box || !n_det || !masks || batch < 1 || proto_h < 1 || proto_w < 1 || max_det < 1)
     return pp_fail(OSAM_ERR_INVALID, "osam_mask_assemble: invalid arguments");
   if ((reinterpret_cast<uintptr_t>(coef_g) | reinterpret_cast<uintptr_t>(proto)) & 15)
@@ -454,7 +467,8 @@ int osam_mask_assemble(const void* coef_g, const void* proto, const float* det_b
   a.proto = static_cast<const __half*>(proto);
   a.det_box = det_box;
   a.n_det = n_det;
-  a.masks = masks;
+  a.masks = static_cast<uint8_t*>(masks);
+  a.packed = packed;
   a.Hp = proto_h;
   a.Wp = proto_w;
   a.max_det = max_det;

@@ -55,25 +55,36 @@ def nms(xyxy, conf, conf_th: float = 0.25, iou_th: float = 0.7, max_det: int = 3
     return out
 
 
-def mask_assemble(coef_g, proto, det: dict, imgsz: int, stream=None):
-    """coef_g (B, ceil128(max_det), 32) fp16, proto (B, Hp, Wp, 32) fp16 → masks (B, max_det, Hp, Wp) u8."""
+def mask_assemble(coef_g, proto, det: dict, imgsz: int, packed: bool = False, stream=None):
+    """coef_g (B, ceil128(max_det), 32) fp16, proto (B, Hp, Wp, 32) fp16 → masks (B, max_det, Hp, Wp) u8, or
+    with packed=True (B, max_det, ceil(Hp·Wp/32)) int32 bit words (pixel 32·j + k = bit k of word j)."""
     B, Hp, Wp, _ = proto.shape
     max_det = det["keep"].shape[1]
-    masks = torch.empty(B, max_det, Hp, Wp, dtype=torch.uint8, device=proto.device)
+    if packed:
+        masks = torch.empty(B, max_det, (Hp * Wp + 31) // 32, dtype=torch.int32, device=proto.device)
+    else:
+        masks = torch.empty(B, max_det, Hp, Wp, dtype=torch.uint8, device=proto.device)
     check(lib().osam_mask_assemble(coef_g.data_ptr(), proto.data_ptr(), det["box"].data_ptr(),
-                                   det["n_det"].data_ptr(), B, Hp, Wp, imgsz, max_det, masks.data_ptr(),
-                                   stream_ptr(stream)))
+                                   det["n_det"].data_ptr(), B, Hp, Wp, imgsz, max_det, int(packed),
+                                   masks.data_ptr(), stream_ptr(stream)))
     return masks
 
 
+def unpack_masks(packed, Hp: int, Wp: int):
+    """Packed bit masks (…, words) → bool (…, Hp, Wp)."""
+    w = packed.to(torch.int64) & 0xFFFFFFFF
+    bits = ((w.unsqueeze(-1) >> torch.arange(32, device=w.device)) & 1).flatten(-2)
+    return bits[..., : Hp * Wp].reshape(*packed.shape[:-1], Hp, Wp).bool()
+
+
 def detect(model, conf_th: float = 0.25, iou_th: float = 0.7, max_det: int = 300, forced: bool = False,
-           stream=None) -> dict:
+           packed: bool = False, stream=None) -> dict:
     """Decode, NMS and masks on the model's current heads (after Model.forward)."""
     box = [model.head(0, l) for l in range(3)]
     cls = [model.head(1, l) for l in range(3)]
     coef = [model.head(2, l) for l in range(3)]
     xyxy, conf = decode(box, cls, model.imgsz, model.reg_max, stream)
     det = nms(xyxy, conf, conf_th, iou_th, max_det, forced, coef=coef, stream=stream)
-    det["masks"] = mask_assemble(det["coef_g"], model.proto(), det, model.imgsz, stream)
+    det["masks"] = mask_assemble(det["coef_g"], model.proto(), det, model.imgsz, packed, stream)
     det["xyxy"], det["conf"] = xyxy, conf
     return det

@@ -102,7 +102,9 @@ def test_masks_match_reference_golden(cuda_lib, ci):
     coef_g[0, :n] = torch.from_numpy(coefs[det["keep"][0, :n].cpu().numpy()]).half()
     proto = torch.from_numpy(o1).permute(1, 2, 0).contiguous()[None].half().to(DEV)
     masks = postproc.mask_assemble(coef_g.to(DEV), proto, det, S)
+    packed = postproc.mask_assemble(coef_g.to(DEV), proto, det, S, packed=True)
     torch.cuda.synchronize()
+    assert torch.equal(postproc.unpack_masks(packed, proto.shape[1], proto.shape[2]), masks.bool())
     grid = np.unpackbits(case["grid"], axis=-1)[..., : int(case["grid_shape"][-1])].astype(bool)
     grid = grid.reshape(tuple(case["grid_shape"]))
     got = masks[0, :n].cpu().numpy().astype(bool)
