@@ -296,7 +296,7 @@ def main():
         barrier()
     ms = evs[0][0].elapsed_time(evs[K - 1][n_all])
     node_ms = [sum(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K)) / K for i in range(n_all)]
-    fwd_ms = sum(node_ms[:n])
+    fwd_ms = sum(node_ms[:n]) * K  # forward kernels of all K steps (node_ms is per step)
     clocks = clk.summary()
     n_det_mean = float(det["n_det"].float().mean().item())
 

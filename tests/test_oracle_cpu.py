@@ -46,6 +46,36 @@ def test_nms_known_answer():
     assert list(postproc_ref.nms_order(conf, 0.25)) == [1, 4, 0, 2]
 
 
+@pytest.mark.parametrize("thr", [0.7, 0.5, 1 / 3, 0.45, 0.0, 1e-7, 0.999, -0.25])
+def test_exact_iou_threshold_identity(thr):
+    """The GPU NMS decides float32(inter / union) > thr without dividing: inter > union·m in double, m the
+    midpoint between thr and the next float up, ties going up when thr's last bit is 1.  Same answers as
+    the float32 division on random, near-threshold and small-integer (exact-fraction) operands."""
+    import struct
+    rng = np.random.Generator(np.random.PCG64(0))
+    t = np.float32(thr)
+    nx = np.nextafter(t, np.float32(np.inf))
+    mid = (float(t) + float(nx)) * 0.5
+    odd = struct.unpack("<I", struct.pack("<f", t))[0] & 1
+    u = (rng.random(100000) * 1e5 + 1e-3).astype(np.float32)
+    inter = (u.astype(np.float64) * float(t) * (1 + rng.integers(-40, 40, 100000) * 6e-8)).astype(np.float32)
+    a, b = rng.integers(1, 200, 50000).astype(np.float32), rng.integers(1, 200, 50000).astype(np.float32)
+    inter, u = np.concatenate([np.abs(inter), np.minimum(a, b)]), np.concatenate([u, np.maximum(a, b)])
+    ref = (inter / u).astype(np.float32) > t
+    p = u.astype(np.float64) * mid
+    got = (inter.astype(np.float64) > p) | ((inter.astype(np.float64) == p) & bool(odd))
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("kind", ["mixed", "grid", "dense", "sparse"])
+def test_greedy_nms_vec_matches_scalar(kind):
+    """The vectorised greedy NMS (used to check the GPU on thousands of candidates) keeps exactly the
+    boxes of the scalar restatement of ref_detect's loop."""
+    boxes = postproc_ref.stress_boxes(kind, 400, 5)
+    for thr, md in ((0.5, 300), (0.7, 40), (1 / 3, 1000)):
+        assert postproc_ref.greedy_nms_vec(boxes, thr, md) == postproc_ref.greedy_nms(boxes, thr, md)
+
+
 def test_dfl_decode_known_answer():
     """A one-hot DFL distribution decodes to its bin; anchors are cell centres × stride."""
     N, H, W = 1, 2, 2

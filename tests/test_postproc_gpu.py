@@ -141,3 +141,27 @@ def test_detect_pipeline_on_model_heads(cuda_lib):
         got = det["masks"][b, :n].cpu().numpy().astype(bool)
         near0 = np.abs(logits) < 1e-4 * (np.abs(logits).max() + 1e-12)
         assert ((got != ref_masks) & ~near0).sum() == 0
+
+
+@pytest.mark.parametrize("kind,thr,max_det", [("mixed", 0.5, 300), ("mixed", 0.7, 1000), ("grid", 0.5, 300),
+                                              ("grid", 0.7, 1000), ("dense", 0.45, 300), ("sparse", 0.7, 1000),
+                                              ("sparse", 1 / 3, 300), ("mixed", 0.2, 1000), ("grid", 0.3, 1000)])
+def test_nms_bit_exact_many_candidates(cuda_lib, kind, thr, max_det):
+    """8400 anchors, ~6300 above the threshold, tied scores: several 1024-candidate rounds and several
+    suppression-matrix blocks per round; kept anchors, scores and boxes identical to the greedy loop."""
+    A = 8400
+    rng = np.random.Generator(np.random.PCG64(11))
+    boxes = postproc_ref.stress_boxes(kind, A, 12)
+    conf = rng.random(A).astype(np.float32)
+    conf[rng.integers(0, A, 800)] = np.float32(0.625)  # ties resolve by anchor index
+    det = postproc.nms(torch.from_numpy(boxes)[None].to(DEV), torch.from_numpy(conf)[None].to(DEV), conf_th=0.25,
+                       iou_th=thr, max_det=max_det)
+    torch.cuda.synchronize()
+    idx = postproc_ref.nms_order(conf, 0.25)
+    anchors = idx[postproc_ref.greedy_nms_vec(boxes[idx], thr, max_det)]
+    n = int(det["n_det"][0])
+    assert n == len(anchors)
+    np.testing.assert_array_equal(det["keep"][0, :n].cpu().numpy(), anchors)
+    np.testing.assert_array_equal(det["score"][0, :n].cpu().numpy(), conf[anchors])
+    np.testing.assert_array_equal(det["box"][0, :n].cpu().numpy(), boxes[anchors])
+    assert (det["keep"][0, n:] == -1).all()
