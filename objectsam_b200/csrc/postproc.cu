@@ -118,6 +118,9 @@ struct NmsArgs {
   int max_det_pad;
   int mblk;            // survivors per suppression-matrix block (512, 256 or 128: what shared memory holds)
   // the IoU threshold as an exact test (see iou_gt)
+  float thr;           // iou_th
+  float thr_h;         // half the gap from iou_th to the next float (a power of two)
+  int thr_fast;        // iou_th finite in [1e-3, 1e3]: iou_gt's single-rounding pre-test applies
   double thr_mid;      // midpoint between iou_th and the next float above it
   int thr_odd;         // iou_th's last significand bit (a quotient exactly at thr_mid rounds up iff set)
   int thr_nonneg;      // iou_th ≥ 0: disjoint boxes (IoU 0) never pass
@@ -127,18 +130,28 @@ struct NmsArgs {
 
 // ref_detect's IoU test: RN(inter / union) > thr, with inter and union rounded as numpy's float32 ops round
 // them (b = candidate, c = kept box, ab / ac their areas, computed as (x2 − x1)·(y2 − y1)).  The rounded
-// quotient exceeds thr exactly when the real quotient exceeds the midpoint m between thr and the next
-// float, or equals m and round-to-even picks the upper neighbour (thr's last bit is 1); with union > 0 that
-// is inter > union·m, evaluated exactly in double (a 24-bit × 25-bit product).  No division is needed.
+// quotient exceeds thr exactly when the real quotient exceeds the midpoint m = thr + h between thr and the
+// next float, or equals m and round-to-even picks the upper neighbour (thr's last bit is 1); with union > 0
+// that is D = inter − union·thr > union·h.  D is first formed with one rounding (an FMA, relative error
+// ≤ 2⁻²⁴), which settles every pair farther than a factor 2 from the boundary; the rest are decided by
+// inter > union·m in double, where the 24-bit × 25-bit product is exact.  No division is needed.
+__device__ __forceinline__ bool iou_gt_exact(float inter, float u, const NmsArgs& a) {
+  if (inter == 0.f && a.thr_nonneg) return false;
+  if (!(u > 0.f) || a.thr_nan) return false;
+  const double p = __dmul_rn((double)u, a.thr_mid), in = (double)inter;
+  return in > p || (in == p && a.thr_odd);
+}
+
 __device__ __forceinline__ bool iou_gt(const float4 b, float ab, const float4 c, float ac, const NmsArgs& a) {
   const float iw = fmaxf(0.f, __fsub_rn(fminf(b.z, c.z), fmaxf(b.x, c.x)));
   const float ih = fmaxf(0.f, __fsub_rn(fminf(b.w, c.w), fmaxf(b.y, c.y)));
   const float inter = __fmul_rn(iw, ih);
-  if (inter == 0.f && a.thr_nonneg) return false;
   const float u = __fsub_rn(__fadd_rn(ab, ac), inter);
-  if (!(u > 0.f) || a.thr_nan) return false;
-  const double p = __dmul_rn((double)u, a.thr_mid), in = (double)inter;
-  return in > p || (in == p && a.thr_odd);
+  const float dd = __fmaf_rn(-u, a.thr, inter);
+  const float uh = __fmul_rn(u, a.thr_h);
+  const bool above = dd > 2.f * uh, below = dd < 0.5f * uh;
+  if (a.thr_fast && u >= 1e-20f && u <= 1e30f && (above || below)) return above;
+  return iou_gt_exact(inter, u, a);
 }
 
 __device__ __forceinline__ float box_area(const float4 b) { return __fmul_rn(__fsub_rn(b.z, b.x), __fsub_rn(b.w, b.y)); }
@@ -196,7 +209,7 @@ __device__ __forceinline__ int block_scan_excl(int v, int* tot, int* total) {
 //      block's suppression bit-matrix (row i: survivors j > i whose IoU with i passes), and warp 0 walks
 //      the block in order, keeping the first survivor not yet removed and OR-ing its row into the removed
 //      set — one step per kept box.  This keeps exactly the boxes of the sequential greedy loop.
-__global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
+__global__ void __launch_bounds__(kNmsThreads, 1) k_nms(const NmsArgs a) {
   extern __shared__ __align__(16) uint8_t nsm[];
   unsigned short* ord0 = reinterpret_cast<unsigned short*>(nsm);  // [A] candidate anchors
   unsigned short* ord1 = ord0 + a.A;                               // [A] radix ping-pong buffer
@@ -207,7 +220,8 @@ __global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
   // greedy phase
   float4* kept = reinterpret_cast<float4*>(ph);                     // [max_det]
   float* kept_area = reinterpret_cast<float*>(kept + a.max_det);    // [max_det]
-  float4* surv_box = reinterpret_cast<float4*>(kept_area + ((a.max_det + 3) & ~3));  // [kNmsThreads]
+  int* kept_src = reinterpret_cast<int*>(kept_area + ((a.max_det + 3) & ~3));  // [max_det] survivor slot
+  float4* surv_box = reinterpret_cast<float4*>(kept_src + ((a.max_det + 3) & ~3));  // [kNmsThreads]
   float* surv_area = reinterpret_cast<float*>(surv_box + kNmsThreads);                // [kNmsThreads]
   int* surv_an = reinterpret_cast<int*>(surv_area + kNmsThreads);                     // [kNmsThreads]
   uint32_t* mat = reinterpret_cast<uint32_t*>(surv_an + kNmsThreads);                 // [mblk][mblk / 32]
@@ -337,7 +351,14 @@ __global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
         bx = box[an];
         ab = box_area(bx);
       }
-      for (int k = 0; k < nk0 && alive; k++) alive = !iou_gt(bx, ab, kept[k], kept_area[k], a);
+      for (int k = 0; k < nk0 && alive; k += 4) {  // 4 independent tests per step (order-free: any one kills)
+        const int k1 = min(k + 1, nk0 - 1), k2 = min(k + 2, nk0 - 1), k3 = min(k + 3, nk0 - 1);
+        const bool s0 = iou_gt(bx, ab, kept[k], kept_area[k], a);
+        const bool s1 = iou_gt(bx, ab, kept[k1], kept_area[k1], a);
+        const bool s2 = iou_gt(bx, ab, kept[k2], kept_area[k2], a);
+        const bool s3 = iou_gt(bx, ab, kept[k3], kept_area[k3], a);
+        alive = !(s0 || s1 || s2 || s3);
+      }
       int ms;
       const int pos = block_scan_excl(alive ? 1 : 0, tot, &ms);
       if (alive) {
@@ -356,7 +377,14 @@ __global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
           if (!d) {
             const float4 me = surv_box[s0 + tid];
             const float ma = surv_area[s0 + tid];
-            for (int k = nk0; k < nkb && !d; k++) d = iou_gt(me, ma, kept[k], kept_area[k], a);
+            for (int k = nk0; k < nkb && !d; k += 4) {
+              const int k1 = min(k + 1, nkb - 1), k2 = min(k + 2, nkb - 1), k3 = min(k + 3, nkb - 1);
+              const bool s0 = iou_gt(me, ma, kept[k], kept_area[k], a);
+              const bool s1 = iou_gt(me, ma, kept[k1], kept_area[k1], a);
+              const bool s2 = iou_gt(me, ma, kept[k2], kept_area[k2], a);
+              const bool s3 = iou_gt(me, ma, kept[k3], kept_area[k3], a);
+              d = s0 || s1 || s2 || s3;
+            }
           }
           const unsigned dm = __ballot_sync(0xffffffffu, d);
           if (lane == 0) blk_dead[warp] = dm;
@@ -375,6 +403,7 @@ __global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
           const float ai = row ? surv_area[s0 + i] : 0.f;
           uint32_t bits = 0u;
           const int jend = min(32 * w + 32, nb);
+#pragma unroll 4
           for (int j = 32 * w; j < jend; j++) {
             const bool s = row && j > i && iou_gt(surv_box[s0 + j], surv_area[s0 + j], bi, ai, a);
             bits |= (s ? 1u : 0u) << (j - 32 * w);
@@ -390,13 +419,7 @@ __global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
             uint32_t live = ~__shfl_sync(0xffffffffu, removed, w);
             while (live != 0u && nk < a.max_det) {
               const int bit = __ffs(live) - 1, i = 32 * w + bit;
-              if (lane == 0) {
-                const int ai = surv_an[s0 + i];
-                kept[nk] = surv_box[s0 + i];
-                kept_area[nk] = surv_area[s0 + i];
-                a.keep[(long long)b * a.max_det + nk] = ai;
-                a.det_score[(long long)b * a.max_det + nk] = conf[ai];
-              }
+              if (lane == 0) kept_src[nk] = s0 + i;  // boxes and outputs are filled in after the walk
               nk++;
               if (lane >= w && lane < nwb) removed |= mat[i * mw + lane];
               const uint32_t above = bit == 31 ? 0u : (0xffffffffu << (bit + 1));
@@ -405,6 +428,15 @@ __global__ void __launch_bounds__(kNmsThreads) k_nms(const NmsArgs a) {
           }
           __syncwarp();
           if (lane == 0) nkept = nk;
+        }
+        __syncthreads();
+        const int nke = nkept;
+        for (int t = nkb + tid; t < nke; t += kNmsThreads) {
+          const int si = kept_src[t], ai = surv_an[si];
+          kept[t] = surv_box[si];
+          kept_area[t] = surv_area[si];
+          a.keep[(long long)b * a.max_det + t] = ai;
+          a.det_score[(long long)b * a.max_det + t] = conf[ai];
         }
         __syncthreads();
       }
@@ -707,7 +739,7 @@ static size_t nms_smem_sort_offset(int anchors) { return align16((size_t)anchors
 static size_t nms_smem_bytes(int anchors, int max_det, int mblk) {
   const size_t md4 = (size_t)((max_det + 3) & ~3);
   const size_t sort = (size_t)((anchors + 3) & ~3) * 4 + (size_t)kRadixBins * kNmsWarps * 4;
-  const size_t greedy = (size_t)max_det * 16 + md4 * 4 + (size_t)kNmsThreads * 24 + (size_t)mblk * (mblk / 32) * 4;
+  const size_t greedy = (size_t)max_det * 16 + md4 * 8 + (size_t)kNmsThreads * 24 + (size_t)mblk * (mblk / 32) * 4;
   return nms_smem_sort_offset(anchors) + std::max(sort, greedy);
 }
 
@@ -715,7 +747,10 @@ static size_t nms_smem_bytes(int anchors, int max_det, int mblk) {
 static void nms_threshold(float thr, NmsArgs& a) {
   a.thr_nan = thr != thr;
   a.thr_nonneg = thr >= 0.f;
+  a.thr = thr;
+  a.thr_fast = thr >= 1e-3f && thr <= 1e3f;
   const float nx = std::nextafter(thr, INFINITY);
+  a.thr_h = a.thr_fast ? (nx - thr) * 0.5f : 0.f;
   const double nxd = std::isinf(nx) && !std::isinf(thr) ? std::ldexp(1.0, 128) : (double)nx;
   a.thr_mid = ((double)thr + nxd) * 0.5;
   uint32_t bits;
