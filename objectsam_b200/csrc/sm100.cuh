@@ -51,13 +51,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps (up to `ns`) until the phase completes
+// instead of re-issuing the test, leaving the issue slots to the warps that have work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on a phase parity.  Returns false (and records kDevErrTimeout) when the budget runs out.
 static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-    for (int i = 0; i < 32; i++)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 8; i++)
+      if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (globaltimer() - t0 > kWaitBudgetNs) {
       if (err) atomicExch(err, kDevErrTimeout);
       return false;
