@@ -123,49 +123,6 @@ static void choose_tile(int N, int P, int Q, int* tn, int* th, int* tw) {
     }
 }
 
-// Halo-reuse tiling for a stride-1 R×S conv (conv_halo.cu): MT = 128·MH pixels of one image as th × tw
-// (tw a multiple of 8), the A and B ring depths that fit shared memory, and whether it beats the direct
-// path on TMA rows fetched (A: S boxes of (th + R − 1)·tw rows per chunk; B: R·S·BN rows per chunk).
-static void plan_halo(osam_conv_plan* p) {
-  const osam_conv_geom& g = p->g;
-  p->halo = 0;
-  if (p->transposed || p->mode != A_S1 || g.stride != 1 || (g.R == 1 && g.S == 1)) return;
-  if (p->BN != 32 && p->BN != 64 && p->BN != 128 && p->BN != 224 && p->BN != 256) return;
-  const int MT = p->BN <= 128 ? 256 : 128;
-  const size_t avail = kHaloSmemLimit - halo_fixed_smem_bytes();
-  const size_t b_bytes = (size_t)p->BN * p->BK * 2;
-  long long best = -1;
-  for (int tw : {32, 16, 8}) {
-    const int th = MT / tw;
-    if (th + g.R - 1 > 256) continue;
-    const size_t a_bytes = (size_t)(th + g.R - 1) * tw * p->BK * 2;
-    const size_t a_stride = (a_bytes + 1023) & ~size_t(1023);
-    int sa = 3;
-    if (3 * a_stride + (size_t)(g.R + 3) * b_bytes > avail) sa = 2;
-    if (sa * a_stride + 2 * b_bytes > avail) continue;
-    int sb = (int)((avail - sa * a_stride) / b_bytes);
-    if (sb > 8) sb = 8;
-    if (sb < 2) continue;
-    const long long tq = cdivll(p->Q, tw), tp = cdivll(p->P, th), tiles = tq * tp * g.N;
-    if ((double)g.N * p->P * p->Q < 0.75 * (double)tiles * MT) continue;  // too much padding
-    const long long rows = tiles * p->nkc * ((long long)g.S * (th + g.R - 1) * tw + (long long)g.R * g.S * p->BN);
-    if (best < 0 || rows < best) {
-      best = rows;
-      p->hth = th;
-      p->htw = tw;
-      p->htiles_q = (int)tq;
-      p->htiles_p = (int)tp;
-      p->htiles_m = (int)tiles;
-      p->hsa = sa;
-      p->hsb = sb;
-      p->ha_bytes = (int)a_bytes;
-      p->ha_stride = (int)a_stride;
-    }
-  }
-  const long long direct = (long long)p->tiles_m * p->nk * (128 + p->BN);
-  if (best > 0 && best * 10 < direct * 9) p->halo = 1;
-}
-
 static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p) {
   std::memset(p, 0, sizeof(*p));
   p->g = *g;
@@ -241,7 +198,6 @@ static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p)
     p->tiles_m = (int)cdivll(p->M, 128);
   }
   if ((long long)p->tiles_m * p->ntn > 0x7fffffffLL) return fail(OSAM_ERR_UNSUPPORTED, "conv too large");
-  plan_halo(p);
   return OSAM_OK;
 }
 
@@ -339,23 +295,9 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     for (int i = 0; i < e.ndest && ts; i++) ts = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
     if (e.shuffle) ts = ts && e.ndest == 1 && e.kout % 32 == 0;
     e.tstore = 0;
-    if (ts && p->halo && !e.shuffle) {  // halo-reuse kernel: one image per tile, th × tw pixels
-      L->mode = A_HALO;
-      d.tn = 1;
-      d.th = p->hth;
-      d.tw = p->htw;
-      d.tiles_q = p->htiles_q;
-      d.tiles_p = p->htiles_p;
-      d.tiles_m = p->htiles_m;
-      d.halo_sa = p->hsa;
-      d.halo_sb = p->hsb;
-      d.halo_a_bytes = p->ha_bytes;
-      d.halo_a_stride = p->ha_stride;
-      L->grid = d.tiles_m * p->ntn;
-    }
     if (ts) {
-      e.wtw = d.tw < 32 ? d.tw : 32;
-      e.wth = d.th < 32 / e.wtw ? d.th : 32 / e.wtw;
+      e.wtw = p->tw < 32 ? p->tw : 32;
+      e.wth = p->th < 32 / e.wtw ? p->th : 32 / e.wtw;
       e.wtn = 32 / (e.wtw * e.wth);
       const uint32_t box[4] = {32, (uint32_t)e.wtw, (uint32_t)e.wth, (uint32_t)e.wtn};
       int rc = OSAM_OK;
@@ -442,11 +384,6 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     const uint64_t str[1] = {(uint64_t)g.C * 2};
     const uint32_t box[2] = {(uint32_t)p->BK, 128};
     rc = make_map(&L->ta, x, 2, dims, str, box, row_bytes);
-  } else if (L->mode == A_HALO) {
-    const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
-    const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
-    const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)d.tw, (uint32_t)(d.th + g.R - 1), 1};
-    rc = make_map(&L->ta, x, 4, dims, str, box, row_bytes);
   } else if (p->mode == A_S1) {
     const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
     const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
@@ -490,13 +427,11 @@ cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st) {
     cudaError_t e = launch_convt_weight_relayout(L.wt_src, L.wt_dst, L.d.C, 4, L.d.K, st);
     if (e != cudaSuccess) return e;
   }
-  if (L.mode == A_HALO) return launch_conv_halo(L, st);
   return launch_conv_fprop(L, st);
 }
 
 cudaError_t conv_prime(const ConvLaunch& L) {
   if (L.mode == A_STEM) return cudaSuccess;
-  if (L.mode == A_HALO) return launch_conv_halo(L, nullptr, true);
   return launch_conv_fprop(L, nullptr, true);
 }
 

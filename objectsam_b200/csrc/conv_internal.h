@@ -15,13 +15,8 @@ enum AMode : int {
   A_S1 = 1,    // stride-1 R×S conv: 4-D map (C, W, H, N); one shifted box per tap, halo = TMA zero fill
   A_S2 = 2,    // stride-2 conv: 5-D map (2C, W/2, 2, H/2, N) — the parity-split view of NHWC — so a
                // stride-2 gather becomes a dense box per tap
-  A_STEM = 3,  // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
-  A_HALO = 4   // stride-1 R×S conv with halo reuse (conv_halo.cu): one (th + R − 1) × tw box per channel
-               // chunk and column shift, the row taps read from row offsets of it
+  A_STEM = 3   // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
 };
-
-// Dynamic shared memory a halo-conv CTA may use (the sm_100 opt-in limit per block).
-constexpr size_t kHaloSmemLimit = 227 * 1024;
 
 struct DestDev {
   __half* p;
@@ -56,9 +51,6 @@ struct ConvDev {
   int tiles_m;                // tiles along GEMM M
   int nkc;                    // channel chunks per tap
   int nk;                     // K iterations = taps · nkc
-  int halo_sa, halo_sb;       // A_HALO: A-ring and B-ring stages
-  int halo_a_bytes;           // A_HALO: bytes of one A box ((th + R − 1) · tw · BK · 2)
-  int halo_a_stride;          // A_HALO: A stage stride (a_bytes rounded up to 1024)
   int* err;                   // device error word
   EpiDev ep;
 };
@@ -97,8 +89,6 @@ cudaError_t sppf_prime();
 
 // kernels living in other translation units
 cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st, bool prime_only = false);
-cudaError_t launch_conv_halo(const ConvLaunch& L, cudaStream_t st, bool prime_only = false);
-size_t halo_fixed_smem_bytes();  // a halo CTA's shared memory besides its A and B rings
 cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st);
 cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st);
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
@@ -118,6 +108,4 @@ struct osam_conv_plan {
   int tn, th, tw, tiles_q, tiles_p;
   long long M;
   int gemm_n, ntn, nkc, nk, tiles_m;
-  // halo-reuse tiling (A_HALO), used when the epilogue allows TMA stores (decided per call)
-  int halo, hth, htw, htiles_q, htiles_p, htiles_m, hsa, hsb, ha_bytes, ha_stride;
 };
