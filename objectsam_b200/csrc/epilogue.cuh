@@ -25,6 +25,62 @@ __device__ __forceinline__ float silu_f(float y) {
   return y * rcp_nr(1.f + e);
 }
 
+// ---- packed pairs: sm_100's f32x2 FMA-pipe instructions take one issue slot for two fp32 values
+__device__ __forceinline__ uint64_t f2bits(float2 a) {
+  uint64_t u;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(u) : "f"(a.x), "f"(a.y));
+  return u;
+}
+__device__ __forceinline__ float2 f2from(uint64_t u) {
+  float2 a;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(u));
+  return a;
+}
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2bits(a)), "l"(f2bits(b)), "l"(f2bits(c)));
+  return f2from(d);
+}
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2bits(a)), "l"(f2bits(b)));
+  return f2from(d);
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// SiLU of two values, t·σ(t) with σ(t) = 1 / (1 + 2^(−t·log₂e)), on packed pairs: the exponent argument
+// is clamped at 115.4 (t ≥ −80, as silu_f), nd = −(1 + e) comes from one FMA, and 1/(1 + e) is the
+// exponent-flip estimate (rcp_nr's constant, the sign bit folded in: 0xFEF311C3 − bits(nd) =
+// 0x7EF311C3 − bits(−nd)) refined by the same three Newton–Raphson steps r ← r·(2 + nd·r).
+__device__ __forceinline__ float2 silu2(float2 t) {
+  constexpr float kNegLog2e = -1.4426950408889634f;
+  const float2 a = f2mul(t, make_float2(kNegLog2e, kNegLog2e));
+  const float2 e = make_float2(ex2_approx(fminf(a.x, 115.4f)), ex2_approx(fminf(a.y, 115.4f)));
+  const float2 nd = f2fma(e, make_float2(-1.f, -1.f), make_float2(-1.f, -1.f));
+  float2 r = make_float2(__uint_as_float(0xFEF311C3u - __float_as_uint(nd.x)),
+                         __uint_as_float(0xFEF311C3u - __float_as_uint(nd.y)));
+  const float2 two = make_float2(2.f, 2.f);
+  r = f2mul(r, f2fma(nd, r, two));
+  r = f2mul(r, f2fma(nd, r, two));
+  r = f2mul(r, f2fma(nd, r, two));
+  return f2mul(t, r);
+}
+
+// BN + SiLU of four consecutive columns: y = silu(sc·v + sh).
+__device__ __forceinline__ void bn_silu4(const float4 sc, const float4 sh, const float* v, float* y) {
+  const float2 t0 = f2fma(make_float2(sc.x, sc.y), make_float2(v[0], v[1]), make_float2(sh.x, sh.y));
+  const float2 t1 = f2fma(make_float2(sc.z, sc.w), make_float2(v[2], v[3]), make_float2(sh.z, sh.w));
+  const float2 y0 = silu2(t0), y1 = silu2(t1);
+  y[0] = y0.x;
+  y[1] = y0.y;
+  y[2] = y1.x;
+  y[3] = y1.y;
+}
+
 // Store `cnt` (≤ 8) consecutive output channels starting at `k` of one output pixel to every destination
 // whose channel range holds them.  `pix` indexes the P×Q output grid; (n, p, q) locate it for the 2×
 // upsampled destinations.
@@ -178,7 +234,9 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
     }
     if (e.act) {
 #pragma unroll
-      for (int i = 0; i < W; i++) y[i] = silu_f(fmaf(sc[i], v[i], sh[i]));
+      for (int i = 0; i < W; i += 4)
+        bn_silu4(make_float4(sc[i], sc[i + 1], sc[i + 2], sc[i + 3]), make_float4(sh[i], sh[i + 1], sh[i + 2], sh[i + 3]),
+                 v + i, y + i);
     } else {
 #pragma unroll
       for (int i = 0; i < W; i++) y[i] = fmaf(sc[i], v[i], sh[i]);
@@ -275,10 +333,7 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMa
       for (int i = 0; i < W; i += 4) {
         const float4 sc = *reinterpret_cast<const float4*>(s_sc + col + i);
         const float4 sh = *reinterpret_cast<const float4*>(s_sh + col + i);
-        y[i] = silu_f(fmaf(sc.x, v[i], sh.x));
-        y[i + 1] = silu_f(fmaf(sc.y, v[i + 1], sh.y));
-        y[i + 2] = silu_f(fmaf(sc.z, v[i + 2], sh.z));
-        y[i + 3] = silu_f(fmaf(sc.w, v[i + 3], sh.w));
+        bn_silu4(sc, sh, v + i, y + i);
       }
     } else {
 #pragma unroll

@@ -72,6 +72,53 @@ def test_conv_fwd_matches_torch(cuda_lib, shape):
     assert_close(y, ref_conv(x, w, s, R // 2))
 
 
+# Larger stride-1 grids at the network's sizes: full and ragged, BN 32..256, 3×3 and 5×5.
+LARGE_SHAPES = [
+    (2, 160, 160, 32, 32, 3),
+    (2, 80, 80, 64, 64, 3),
+    (2, 40, 40, 128, 128, 3),
+    (1, 80, 80, 128, 224, 3),
+    (2, 48, 48, 256, 256, 3),
+    (1, 50, 70, 64, 64, 3),
+    (1, 33, 100, 32, 128, 3),
+    (1, 64, 64, 64, 64, 5),
+]
+
+
+@pytest.mark.parametrize("shape", LARGE_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_large_s1_matches_torch(cuda_lib, shape):
+    N, H, W, C, K, R = shape
+    x, w = rand_conv(N, H, W, C, K, R, seed=sum(shape) + 1)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, 1, R // 2))
+    y = torch.full(op.out_shape(), 7.0, dtype=torch.half, device=DEV)
+    op.fwd(x, w, y)
+    torch.cuda.synchronize()
+    assert_close(y, ref_conv(x, w, 1, R // 2))
+
+
+def test_fused_residual_dests_large(cuda_lib):
+    """C2f epilogue at a multi-tile size: BN + SiLU + residual to a full buffer, a concat slice and a 2×
+    upsampled slice (each destination on 32-channel boundaries, so the TMA-store epilogue runs)."""
+    N, H, W, C, K = 2, 64, 64, 64, 128
+    x, w = rand_conv(N, H, W, C, K, 3, seed=12)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
+    shift = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    res = (torch.rand(N, H, W, K, generator=g) - 0.5).half().to(DEV)
+    out = torch.zeros(N, H, W, K, dtype=torch.half, device=DEV)
+    cat = torch.zeros(N, H, W, 3 * 64, dtype=torch.half, device=DEV)
+    up = torch.zeros(N, 2 * H, 2 * W, 96, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    op.fwd_fused(x, w, [DestSpec(out), DestSpec(cat, choff=64, c0=64, c1=128), DestSpec(up, choff=32, c0=0, c1=64, up=2)],
+                 kind=EPI_BN_ACT, scale=scale, shift=shift, res=res)
+    a = F.silu(ref_conv(x, w, 1, 1) * scale + shift) + res.float()
+    assert_close(out, a)
+    assert_close(cat[..., 64:128], a[..., 64:128])
+    assert cat[..., :64].abs().max().item() == 0 and cat[..., 128:].abs().max().item() == 0
+    assert_close(up[..., 32:96], a[..., 0:64].repeat_interleave(2, dim=1).repeat_interleave(2, dim=2))
+    assert up[..., :32].abs().max().item() == 0
+
+
 def test_conv_fwd_beta_accumulates(cuda_lib):
     x, w = rand_conv(2, 16, 16, 64, 64, 3, seed=7)
     op = ConvOp().init(ConvGeom(2, 16, 16, 64, 64, 3, 3, 1, 1))
