@@ -123,6 +123,39 @@ static void choose_tile(int N, int P, int Q, int* tn, int* th, int* tw) {
     }
 }
 
+// Window tiling for a narrow 3×3/s1/p1 conv (conv_win.cu): 128 positions of the row-flattened output
+// per tile, pitch = W + 2 rounded up to 32 (so every warp's 32 positions lie in one output row), and a
+// window of 128 + 2·pitch + 2 input positions in C/8 slabs of 16-byte rows (an odd row count per slab
+// keeps the slabs on different shared-memory banks); two or three windows and all nine weight taps must
+// fit in shared memory.
+static void plan_win(osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  p->win = 0;
+  if (p->transposed || g.stride != 1 || g.R != 3 || g.S != 3 || g.pad != 1) return;
+  if ((g.C != 32 && g.C != 64) || (g.K != 32 && g.K != 64)) return;
+  // measured on B200: the window wins for 32 input channels on grids ≥ 64 wide; at 64 channels, and on
+  // small grids (where rounding the pitch to 32 wastes a third of the tile), the TMA path is as fast or faster
+  if (g.C != 32 || g.W < 64) return;
+  const int wp = (g.W + 2 + 31) / 32 * 32, lw = (128 + 2 * wp + 2) | 1;
+  const size_t slab = (size_t)lw * 16, wbytes = (slab * (g.C / 8) + 1023) & ~size_t(1023);
+  int nwb = 3;
+  if (win_fixed_smem_bytes(g.C, g.K) + 3 * wbytes > kWinSmemLimit) nwb = 2;
+  if (win_fixed_smem_bytes(g.C, g.K) + nwb * wbytes > kWinSmemLimit) return;
+  const long long tpi = cdivll((long long)p->P * wp, 128), tiles = tpi * g.N;
+  if (tiles > 0x7fffffffLL) return;
+  // u / pitch by a multiply-high: exact while u · pitch < 2³² (u < (P + 3)·pitch)
+  if ((double)(p->P + 3) * wp * wp >= 4294967296.0) return;
+  p->win = 1;
+  p->win_nwb = nwb;
+  p->win_mul = (unsigned)((0x100000000ull + wp - 1) / wp);
+  p->win_wp = wp;
+  p->win_lw = lw;
+  p->win_slab = (int)slab;
+  p->win_wbytes = (int)wbytes;
+  p->win_tpi = (int)tpi;
+  p->win_tiles = (int)tiles;
+}
+
 static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p) {
   std::memset(p, 0, sizeof(*p));
   p->g = *g;
@@ -198,6 +231,7 @@ static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p)
     p->tiles_m = (int)cdivll(p->M, 128);
   }
   if ((long long)p->tiles_m * p->ntn > 0x7fffffffLL) return fail(OSAM_ERR_UNSUPPORTED, "conv too large");
+  plan_win(p);
   return OSAM_OK;
 }
 
@@ -289,15 +323,35 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     if (p->mode != A_STEM && p->mode != A_GEMM) coop = coop && (p->P < 65536 && p->Q < 65536);
     e.coop = coop;
   }
+  // ---- narrow 3×3 convs: one shared input window per tile (TMA-store epilogue, one output row per warp)
+  bool win = p->win && e.coop && !e.shuffle;
+  for (int i = 0; i < e.ndest && win; i++) win = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
+  if (win) {
+    L->mode = A_WIN;
+    d.tn = 1;
+    d.th = 1;
+    d.tw = 32;
+    d.win_nwb = p->win_nwb;
+    d.win_mul = p->win_mul;
+    L->x = static_cast<const __half*>(x);
+    d.win_wp = p->win_wp;
+    d.win_lw = p->win_lw;
+    d.win_slab = p->win_slab;
+    d.win_wbytes = p->win_wbytes;
+    d.win_tpi = p->win_tpi;
+    d.tiles_m = p->win_tiles;
+    d.ntn = 1;
+    L->grid = p->win_tiles;
+  }
   // ---- TMA-store epilogue: spatial tiles, 32-column passes, destinations on 32-column boundaries
   {
-    bool ts = e.coop && (p->mode == A_S1 || p->mode == A_S2) && p->BN % 32 == 0;
+    bool ts = e.coop && (L->mode == A_WIN || p->mode == A_S1 || p->mode == A_S2) && p->BN % 32 == 0;
     for (int i = 0; i < e.ndest && ts; i++) ts = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
     if (e.shuffle) ts = ts && e.ndest == 1 && e.kout % 32 == 0;
     e.tstore = 0;
     if (ts) {
-      e.wtw = p->tw < 32 ? p->tw : 32;
-      e.wth = p->th < 32 / e.wtw ? p->th : 32 / e.wtw;
+      e.wtw = d.tw < 32 ? d.tw : 32;
+      e.wth = d.th < 32 / e.wtw ? d.th : 32 / e.wtw;
       e.wtn = 32 / (e.wtw * e.wth);
       const uint32_t box[4] = {32, (uint32_t)e.wtw, (uint32_t)e.wth, (uint32_t)e.wtn};
       int rc = OSAM_OK;
@@ -427,11 +481,13 @@ cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st) {
     cudaError_t e = launch_convt_weight_relayout(L.wt_src, L.wt_dst, L.d.C, 4, L.d.K, st);
     if (e != cudaSuccess) return e;
   }
+  if (L.mode == A_WIN) return launch_conv_win(L, st);
   return launch_conv_fprop(L, st);
 }
 
 cudaError_t conv_prime(const ConvLaunch& L) {
   if (L.mode == A_STEM) return cudaSuccess;
+  if (L.mode == A_WIN) return launch_conv_win(L, nullptr, true);
   return launch_conv_fprop(L, nullptr, true);
 }
 

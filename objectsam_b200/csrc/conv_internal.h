@@ -15,8 +15,12 @@ enum AMode : int {
   A_S1 = 1,    // stride-1 R×S conv: 4-D map (C, W, H, N); one shifted box per tap, halo = TMA zero fill
   A_S2 = 2,    // stride-2 conv: 5-D map (2C, W/2, 2, H/2, N) — the parity-split view of NHWC — so a
                // stride-2 gather becomes a dense box per tap
-  A_STEM = 3   // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
+  A_STEM = 3,  // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
+  A_WIN = 4    // 3×3/s1/p1 with C, K ∈ {32, 64} (conv_win.cu): one shared input window per 128-position tile
 };
+
+// Dynamic shared memory a window-conv CTA may use (the sm_100 opt-in limit per block).
+constexpr size_t kWinSmemLimit = 227 * 1024;
 
 struct DestDev {
   __half* p;
@@ -51,6 +55,11 @@ struct ConvDev {
   int tiles_m;                // tiles along GEMM M
   int nkc;                    // channel chunks per tap
   int nk;                     // K iterations = taps · nkc
+  int win_wp, win_lw;         // A_WIN: row pitch W + 2 of the flattened space, window length (positions)
+  int win_slab, win_wbytes;   // A_WIN: bytes of one 8-channel slab of a window, of one window buffer
+  int win_tpi;                // A_WIN: 128-position tiles per image
+  int win_nwb;                // A_WIN: window buffers (2 or 3)
+  unsigned win_mul;           // A_WIN: ⌈2³²/pitch⌉ — u / pitch = umulhi(u, win_mul) for the sizes planned
   int* err;                   // device error word
   EpiDev ep;
 };
@@ -89,6 +98,8 @@ cudaError_t sppf_prime();
 
 // kernels living in other translation units
 cudaError_t launch_conv_fprop(const ConvLaunch& L, cudaStream_t st, bool prime_only = false);
+cudaError_t launch_conv_win(const ConvLaunch& L, cudaStream_t st, bool prime_only = false);
+size_t win_fixed_smem_bytes(int C, int K);  // a window-conv CTA's shared memory besides its windows
 cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st);
 cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st);
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
@@ -108,4 +119,7 @@ struct osam_conv_plan {
   int tn, th, tw, tiles_q, tiles_p;
   long long M;
   int gemm_n, ntn, nkc, nk, tiles_m;
+  // window tiling (A_WIN), used when the epilogue allows the coalesced warp stores (decided per call)
+  int win, win_wp, win_lw, win_slab, win_wbytes, win_tpi, win_tiles, win_nwb;
+  unsigned win_mul;
 };

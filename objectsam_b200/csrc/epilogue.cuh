@@ -316,10 +316,12 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
 // the 64-byte TMA swizzle and one lane issues a tensor store per destination (four for 2× upsampled
 // destinations and for the transposed conv's pixel shuffle, one per (dy, dx) view).  The tensor engine
 // clips rows outside the output, so partial tiles need no masking.  W = 32 (64-byte stage rows).
+// `rsm` (optional): this pass's residual rows already in shared memory (32 rows × 64 B, stage_off layout),
+// read instead of the global residual.
 __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMaps& maps, int K, int P, int Q,
                                                   float* v, int col, const float* s_sc, const float* s_sh,
                                                   bool valid, int n, int p, int q, int bq, int bp, int bn,
-                                                  uint8_t* stage) {
+                                                  uint8_t* stage, const uint8_t* rsm = nullptr) {
   constexpr int W = 32, CPR = 4, RPI = 8;
   const int lane = threadIdx.x & 31;
   if (e.round_z) {
@@ -359,7 +361,15 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMa
   // the stage is free once the previous pass's tensor store has read it
   if (lane == 0) bulk_wait_group_read0();
   __syncwarp();
-  if (e.kind == OSAM_EPI_BN_ACT && e.res) {
+  if (e.kind == OSAM_EPI_BN_ACT && e.res && rsm) {
+#pragma unroll
+    for (int ch = 0; ch < CPR; ch++) {
+      float r8[8];
+      unpack8h(*reinterpret_cast<const uint4*>(rsm + stage_off(lane, ch)), r8);
+#pragma unroll
+      for (int i = 0; i < 8; i++) y[ch * 8 + i] += r8[i];
+    }
+  } else if (e.kind == OSAM_EPI_BN_ACT && e.res) {
     const int my_rv = valid ? (n * P + p) * Q + q : -1;
 #pragma unroll
     for (int it = 0; it < CPR; it++) {

@@ -495,11 +495,6 @@ struct MaskArgs {
 
 constexpr int kMaskPix = 128;  // pixels per tile = UMMA N = TMEM columns
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // ⌈v⌉ clamped to [lo, hi]; NaN maps to `nan_to` (an empty range, as every comparison with NaN is false).
 __device__ __forceinline__ int ceil_clamp(float v, int lo, int hi, int nan_to) {

@@ -51,6 +51,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of a phase parity.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // try_wait with a suspend-time hint: a waiting thread sleeps (up to `ns`) until the phase completes
 // instead of re-issuing the test, leaving the issue slots to the warps that have work.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
@@ -183,6 +195,25 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, int row_byt
   d |= uint64_t(row_bytes == 128 ? 2 : 4) << 61;    // SWIZZLE_128B = 2, SWIZZLE_64B = 4
   return d;
 }
+
+// K-major operand without swizzle: core matrices of 8 rows × 16 B (8 fp16 of K), rows 16 B apart; `lbo` =
+// byte distance between the two 8-element K halves of a K=16 step, `sbo` = between 8-row groups.  Any
+// 16-byte-aligned start is valid, so an operand may begin at any row of such a layout.
+__device__ __forceinline__ uint64_t smem_desc_kmajor_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (saddr & 0x3FFFFu) >> 4;
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;  // descriptor version (sm_100); layout type 0 = no swizzle
+  return d;
+}
+
+// ------------------------------------------------------------------ cp.async (16-byte, zero-fill)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // 32 lanes × 16 consecutive fp32 columns; thread i of the warp receives lane (base_lane + i).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {

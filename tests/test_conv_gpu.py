@@ -119,6 +119,52 @@ def test_fused_residual_dests_large(cuda_lib):
     assert up[..., :32].abs().max().item() == 0
 
 
+# Narrow 3×3 convs (32 input channels, grids ≥ 64 wide) served from one shared input window per tile:
+# odd heights, ragged widths, K 32 and 64, a few rows only (the window wraps rows within a tile).
+WIN_SHAPES = [
+    (2, 7, 70, 32, 32),
+    (1, 33, 97, 32, 64),
+    (2, 40, 64, 32, 64),
+    (2, 24, 100, 32, 32),
+    (1, 200, 64, 32, 32),
+    (3, 5, 130, 32, 64),
+]
+
+
+@pytest.mark.parametrize("shape", WIN_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_window_matches_torch(cuda_lib, shape):
+    N, H, W, C, K = shape
+    x, w = rand_conv(N, H, W, C, K, 3, seed=sum(shape) + 2)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    y = torch.full(op.out_shape(), 7.0, dtype=torch.half, device=DEV)
+    op.fwd(x, w, y)
+    torch.cuda.synchronize()
+    assert_close(y, ref_conv(x, w, 1, 1))
+
+
+def test_conv_window_fused_residual_dests(cuda_lib):
+    """Bottleneck-style narrow conv: BN + SiLU + residual to a full buffer, a concat slice and a 2×
+    upsampled slice."""
+    N, H, W, C, K = 2, 48, 76, 32, 64
+    x, w = rand_conv(N, H, W, C, K, 3, seed=13)
+    g = torch.Generator(device="cpu").manual_seed(6)
+    scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
+    shift = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    res = (torch.rand(N, H, W, K, generator=g) - 0.5).half().to(DEV)
+    out = torch.zeros(N, H, W, K, dtype=torch.half, device=DEV)
+    cat = torch.zeros(N, H, W, 128, dtype=torch.half, device=DEV)
+    up = torch.zeros(N, 2 * H, 2 * W, 64, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    op.fwd_fused(x, w, [DestSpec(out), DestSpec(cat, choff=64, c0=0, c1=64), DestSpec(up, choff=32, c0=32, c1=64, up=2)],
+                 kind=EPI_BN_ACT, scale=scale, shift=shift, res=res)
+    a = F.silu(ref_conv(x, w, 1, 1) * scale + shift) + res.float()
+    assert_close(out, a)
+    assert_close(cat[..., 64:], a)
+    assert cat[..., :64].abs().max().item() == 0
+    assert_close(up[..., 32:64], a[..., 32:64].repeat_interleave(2, dim=1).repeat_interleave(2, dim=2))
+    assert up[..., :32].abs().max().item() == 0
+
+
 def test_conv_fwd_beta_accumulates(cuda_lib):
     x, w = rand_conv(2, 16, 16, 64, 64, 3, seed=7)
     op = ConvOp().init(ConvGeom(2, 16, 16, 64, 64, 3, 3, 1, 1))
