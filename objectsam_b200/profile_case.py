@@ -4,8 +4,8 @@ Used to point Nsight Compute at a single conv of the network on a realistic acti
 
     python -m objectsam_b200.profile_case --batch 32 --node model.22.proto.cv2 --repeat 3
 
-prints the node list and, per kernel name, how many launches the full forward makes, so that
-`ncu -k regex:<kernel> -s <that count> -c <repeat>` captures exactly the repeated node.
+wraps the repeated launches in the NVTX range "osam_profile", so that
+`ncu --nvtx --nvtx-include osam_profile/ -c <repeat> …` captures exactly the repeated node.
 """
 from __future__ import annotations
 
@@ -50,9 +50,11 @@ def main():
     m.forward()
     torch.cuda.synchronize()
     i = idx[a.node]
+    torch.cuda.nvtx.range_push("osam_profile")  # `ncu --nvtx --nvtx-include osam_profile/` captures only these
     for _ in range(a.repeat):
         m.forward_nodes(i, 1)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     print("launches per forward:", per_kernel, "| repeated node", a.node, "index", i)
 
 
