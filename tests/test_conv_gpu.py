@@ -82,6 +82,8 @@ LARGE_SHAPES = [
     (1, 50, 70, 64, 64, 3),
     (1, 33, 100, 32, 128, 3),
     (1, 64, 64, 64, 64, 5),
+    (1, 24, 16, 128, 128, 3),
+    (1, 40, 24, 64, 224, 3),
 ]
 
 
