@@ -90,6 +90,15 @@ int64_t osam_conv_out_elems(const osam_conv_plan* plan);
 int osam_conv_fwd(const osam_conv_plan* plan, const void* x, const void* w, void* y, float beta, void* ws,
                   size_t ws_bytes, osam_stream_t stream);
 
+/* dx = dgrad(dz, w) (+ beta·dx): the input gradient of the plan's forward conv, dz N×P×Q×K → dx N×H×W×C,
+ * beta 0 (overwrite) or 1 (accumulate, the reference's dgrad_accum).  Replaces ConvOp::dgrad (src/conv.h:30,
+ * src/conv.cpp:346-355).  Runs on the forward kernels over dz with re-laid-out weights written to the
+ * workspace (osam_conv_workspace_size, 256-byte aligned): one conv for stride 1, one per output-parity
+ * class for stride 2.  OSAM_ERR_UNSUPPORTED for transposed plans, non-square kernels, or output channels
+ * that the forward kernels cannot take as inputs (not a multiple of 32). */
+int osam_conv_dgrad(const osam_conv_plan* plan, const void* dz, const void* w, void* dx, float beta, void* ws,
+                    size_t ws_bytes, osam_stream_t stream);
+
 /* Conv fused with its epilogue (BN fold + SiLU + residual + multi-destination store, or bias).
  * Replaces ConvOp::fwd followed by bn_eval_scale/bn_forward_apply (src/model.cpp:388-400) or by
  * add_bias (src/model.cpp:405-406). */

@@ -78,6 +78,13 @@ class ConvOp:
         check(lib().osam_conv_fwd(self._plan, _ptr(x), _ptr(w), _ptr(y), float(beta), _ptr(ws), nbytes,
                                   stream_ptr(stream)))
 
+    def dgrad(self, dy, w, dx, ws=None, beta: float = 0.0, stream=None) -> None:
+        """dx = dgrad(dy, w) (+ beta·dx) — ConvOp::dgrad (src/conv.cpp:346-355).  `ws` must hold
+        workspace_size() bytes (a torch uint8 CUDA tensor, 256-byte aligned as torch allocates)."""
+        nbytes = 0 if ws is None else ws.numel() * ws.element_size()
+        check(lib().osam_conv_dgrad(self._plan, _ptr(dy), _ptr(w), _ptr(dx), float(beta), _ptr(ws), nbytes,
+                                    stream_ptr(stream)))
+
     def fwd_fused(self, x, w, dests: Sequence[DestSpec], kind: int = EPI_BN_ACT, scale=None, shift=None,
                   bias=None, res=None, act: bool = True, round_z: bool = True, ws=None, stream=None) -> None:
         ep = make_epilogue(self._g.K, dests, kind, scale, shift, bias, res, act, round_z)

@@ -156,6 +156,100 @@ static void plan_win(osam_conv_plan* p) {
   p->win_tiles = (int)tiles;
 }
 
+static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p);
+
+// Re-tile a plan for an output grid of P × Q (a dgrad sub-plan whose last taps read past dz: zero fill).
+static void plan_set_output(osam_conv_plan* p, int P, int Q) {
+  const osam_conv_geom& g = p->g;
+  p->P = P;
+  p->Q = Q;
+  p->M = (long long)g.N * P * Q;
+  if (p->mode == A_S1 || p->mode == A_S2) {
+    choose_tile(g.N, P, Q, &p->tn, &p->th, &p->tw);
+    p->tiles_q = (int)cdivll(Q, p->tw);
+    p->tiles_p = (int)cdivll(P, p->th);
+    p->tiles_m = (int)(p->tiles_q * (long long)p->tiles_p * cdivll(g.N, p->tn));
+  } else {
+    p->tiles_m = (int)cdivll(p->M, 128);
+  }
+  p->win = 0;
+}
+
+// Input gradient as forward convs over dz (ConvOp::dgrad, src/conv.cpp:346-355).
+//  stride 1: dx = conv(dz, Wd, pad' = R − 1 − pad) with Wd[c][r'][s'][k] = W[k][R−1−r'][S−1−s'][c];
+//  stride 2: output row h = 2i + ph only sees taps r ≡ ph + pad (mod 2), at dz row i + (ph + pad − r)/2 —
+//  for each parity class (ph, pw) a stride-1 conv over dz with those taps (ordered by dz offset) whose
+//  result lands on pixels (2i + ph, 2j + pw) of dx.
+static void plan_dgrad(osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  p->n_dg = 0;
+  if (p->transposed || g.R != g.S) return;
+  auto make = [&](int i, int R2, int S2, int pad2, int P, int Q, int par) -> bool {
+    osam_conv_geom sg{g.N, p->P, p->Q, g.K, g.C, R2, S2, 1, pad2};
+    osam_conv_plan* s = new (std::nothrow) osam_conv_plan;
+    if (!s) return false;
+    if (plan_init(&sg, 0, s) != OSAM_OK || s->mode == A_STEM) {
+      delete s;
+      return false;
+    }
+    plan_set_output(s, P, Q);
+    p->dg[i] = s;
+    p->dg_R[i] = R2;
+    p->dg_S[i] = S2;
+    p->dg_par[i] = par;
+    return true;
+  };
+  bool ok = true;
+  int n = 0;
+  if (g.stride == 1) {
+    ok = g.R <= 8 && make(0, g.R, g.S, g.R - 1 - g.pad, g.H, g.W, 0);
+    if (ok) {
+      for (int r = 0; r < g.R; r++) p->dg_rmap[0][r] = g.R - 1 - r;
+      for (int s = 0; s < g.S; s++) p->dg_smap[0][s] = g.S - 1 - s;
+      n = 1;
+    }
+  } else if (g.stride == 2 && g.H == 2 * p->P && g.W == 2 * p->Q && g.R <= 8) {
+    for (int ph = 0; ph < 2 && ok; ph++)
+      for (int pw = 0; pw < 2 && ok; pw++) {
+        // taps of each parity, in increasing dz offset (decreasing r)
+        int rt[8], st[8], nr = 0, ns = 0;
+        for (int r = g.R - 1; r >= 0; r--)
+          if (((ph + g.pad - r) % 2 + 2) % 2 == 0) rt[nr++] = r;
+        for (int s = g.S - 1; s >= 0; s--)
+          if (((pw + g.pad - s) % 2 + 2) % 2 == 0) st[ns++] = s;
+        if (nr == 0 || ns == 0) {
+          ok = false;
+          break;
+        }
+        const int orow = (ph + g.pad - rt[0]) / 2, ocol = (pw + g.pad - st[0]) / 2;
+        if (orow > 0 || ocol > 0 || orow != ocol) {
+          ok = false;
+          break;
+        }
+        const int i = ph * 2 + pw;
+        ok = make(i, nr, ns, -orow, p->P, p->Q, i + 1);
+        for (int r = 0; r < nr && ok; r++) p->dg_rmap[i][r] = rt[r];
+        for (int s = 0; s < ns && ok; s++) p->dg_smap[i][s] = st[s];
+        n += ok;
+      }
+  } else {
+    ok = false;
+  }
+  if (!ok) {
+    for (int i = 0; i < 4; i++) {
+      delete p->dg[i];
+      p->dg[i] = nullptr;
+    }
+    return;
+  }
+  long long off = 0;
+  for (int i = 0; i < n; i++) {
+    p->dg_woff[i] = off;
+    off += ((long long)g.C * p->dg_R[i] * p->dg_S[i] * g.K + 127) / 128 * 128;  // 256-byte aligned blocks
+  }
+  p->n_dg = n;
+}
+
 static int plan_init(const osam_conv_geom* g, int transposed, osam_conv_plan* p) {
   std::memset(p, 0, sizeof(*p));
   p->g = *g;
@@ -253,7 +347,7 @@ static int fill_dest(const osam_dest& s, int kout, DestDev* d, int transposed) {
 }
 
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
-                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word) {
+                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word, int par) {
   if (!p || !x || !w) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
   *L = ConvLaunch{};
@@ -283,6 +377,8 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   EpiDev& e = d.ep;
   e.shuffle = p->transposed;
   e.kout = g.K;
+  e.par = par;
+  if (par && p->mode == A_STEM) return fail(OSAM_ERR_UNSUPPORTED, "parity placement on the small-C path");
   if (!ep) {
     if (!y) return fail(OSAM_ERR_INVALID, "NULL output");
     e.kind = OSAM_EPI_STORE;
@@ -324,7 +420,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     e.coop = coop;
   }
   // ---- narrow 3×3 convs: one shared input window per tile (TMA-store epilogue, one output row per warp)
-  bool win = p->win && e.coop && !e.shuffle;
+  bool win = p->win && e.coop && !e.shuffle && !e.par;
   for (int i = 0; i < e.ndest && win; i++) win = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
   if (win) {
     L->mode = A_WIN;
@@ -348,6 +444,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     bool ts = e.coop && (L->mode == A_WIN || p->mode == A_S1 || p->mode == A_S2) && p->BN % 32 == 0;
     for (int i = 0; i < e.ndest && ts; i++) ts = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
     if (e.shuffle) ts = ts && e.ndest == 1 && e.kout % 32 == 0;
+    if (e.par) ts = ts && e.ndest == 1;
     e.tstore = 0;
     if (ts) {
       e.wtw = d.tw < 32 ? d.tw : 32;
@@ -358,7 +455,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
       for (int t = 0; t < e.ndest && rc == OSAM_OK; t++) {
         const DestDev& ds = e.dest[t];
         const uint64_t c = (uint64_t)ds.ctot;
-        const bool four = ds.up == 2 || e.shuffle;
+        const bool four = ds.up == 2 || e.shuffle || e.par;
         const uint64_t OQ2 = 2ull * p->Q, OP2 = 2ull * p->P;
         for (int v = 0; v < (four ? 4 : 1) && rc == OSAM_OK; v++) {
           const int dy = v >> 1, dx = v & 1;
@@ -512,18 +609,55 @@ int osam_conv_plan_create(const osam_conv_geom* g, int transposed, osam_conv_pla
     delete p;
     return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
   }
+  plan_dgrad(p);
   *out = p;
   return OSAM_OK;
 }
 
 int osam_conv_plan_destroy(osam_conv_plan* p) {
+  if (p)
+    for (int i = 0; i < 4; i++) delete p->dg[i];
   delete p;
   return OSAM_OK;
 }
 
+static size_t dgrad_workspace_bytes(const osam_conv_plan* p) {
+  size_t b = 0;
+  for (int i = 0; i < p->n_dg; i++)
+    b = (size_t)p->dg_woff[i] * 2 + (((size_t)p->g.C * p->dg_R[i] * p->dg_S[i] * p->g.K * 2 + 255) & ~size_t(255));
+  return b;
+}
+
+int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void* dx, float beta, void* ws,
+                    size_t ws_bytes, osam_stream_t stream) {
+  if (!p || !dz || !w || !dx) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
+  if (p->n_dg == 0) return fail(OSAM_ERR_UNSUPPORTED, "dgrad: geometry not supported (stride, kernel or channels)");
+  const size_t need = dgrad_workspace_bytes(p);
+  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return fail(OSAM_ERR_INVALID, "dgrad needs %zu workspace bytes (256-byte aligned)", need);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const osam_conv_geom& g = p->g;
+  __half* wsub = static_cast<__half*>(ws);
+  for (int i = 0; i < p->n_dg; i++) {
+    cudaError_t e = launch_dgrad_weights(static_cast<const __half*>(w), wsub + p->dg_woff[i], g.K, g.R, g.S, g.C,
+                                         p->dg_R[i], p->dg_S[i], p->dg_rmap[i], p->dg_smap[i], st);
+    if (e != cudaSuccess) return cuda_fail(e, "osam_conv_dgrad weight re-layout");
+  }
+  for (int i = 0; i < p->n_dg; i++) {
+    ConvLaunch L;
+    int rc = conv_prepare(p->dg[i], dz, wsub + p->dg_woff[i], nullptr, beta, dx, nullptr, 0, &L, false, nullptr,
+                          p->dg_par[i]);
+    if (rc) return rc;
+    cudaError_t e = conv_launch(L, st);
+    if (e != cudaSuccess) return cuda_fail(e, "osam_conv_dgrad launch");
+  }
+  return OSAM_OK;
+}
+
 size_t osam_conv_workspace_size(const osam_conv_plan* p) {
-  if (!p || !p->transposed) return 0;
-  return ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
+  if (!p) return 0;
+  if (p->transposed) return ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
+  return dgrad_workspace_bytes(p);
 }
 
 int64_t osam_conv_out_elems(const osam_conv_plan* p) {

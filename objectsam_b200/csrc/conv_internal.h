@@ -40,6 +40,8 @@ struct EpiDev {
   DestDev dest[OSAM_MAX_DEST];
   int shuffle;  // transposed conv: GEMM column j = (dy·2+dx)·kout + k → pixel (2p+dy, 2q+dx)
   int kout;     // channels per (dy,dx) block for shuffle
+  int par;      // 1..4: every column goes to pixel (2p + (par−1)/2, 2q + (par−1)%2) of a 2P × 2Q grid (the
+                // output-parity classes of a stride-2 dgrad); 0: none
   int coop;     // warp-cooperative coalesced epilogue allowed (see epilogue.cuh)
   int tstore;   // warp rows leave through TMA tensor stores (StoreMaps); implies coop
   int wtw, wth, wtn;  // a warp's 32 rows as a (wtn images × wth rows × wtw cols) box of the tile
@@ -90,7 +92,9 @@ struct ConvLaunch {
 // err_word: device word the kernels report timeouts to (nullptr = the library's per-device word).
 int conv_prepare(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep, float beta,
                  void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready = false,
-                 int* err_word = nullptr);
+                 int* err_word = nullptr, int par = 0);
+cudaError_t launch_dgrad_weights(const __half* w, __half* dst, int K, int R, int S, int C, int Rs, int Ss,
+                                 const int* rmap, const int* smap, cudaStream_t st);
 cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st);
 // One-time per-kernel set-up (dynamic shared-memory opt-in) without launching: call before capturing.
 cudaError_t conv_prime(const ConvLaunch& L);
@@ -119,6 +123,11 @@ struct osam_conv_plan {
   int tn, th, tw, tiles_q, tiles_p;
   long long M;
   int gemm_n, ntn, nkc, nk, tiles_m;
+  // dgrad: sub-plans over dz (1 for stride 1, the 4 output-parity classes for stride 2) with their weight
+  // re-layouts Wsub[c][r'][s'][k] = W[k][rmap[r']][smap[s']][c] packed in the caller's workspace
+  osam_conv_plan* dg[4];
+  int n_dg, dg_par[4], dg_R[4], dg_S[4], dg_rmap[4][8], dg_smap[4][8];
+  long long dg_woff[4];
   // window tiling (A_WIN), used when the epilogue allows the coalesced warp stores (decided per call)
   int win, win_wp, win_lw, win_slab, win_wbytes, win_tpi, win_tiles, win_nwb;
   unsigned win_mul;

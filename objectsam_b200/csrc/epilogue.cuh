@@ -128,9 +128,9 @@ __device__ __forceinline__ void epilogue8(const EpiDev& e, int K, int P, int Q, 
   }
   long long opix = pix;
   int op = p, oq = q, k = col, OP = P, OQ = Q;
-  if (e.shuffle) {  // transposed conv: column block (dy·2+dx) → output pixel (2p+dy, 2q+dx)
-    const int blk = col / e.kout;
-    k = col - blk * e.kout;
+  if (e.shuffle || e.par) {  // column block (dy·2+dx), or the fixed parity class → pixel (2p+dy, 2q+dx)
+    const int blk = e.par ? e.par - 1 : col / e.kout;
+    k = e.par ? col : col - blk * e.kout;
     op = 2 * p + (blk >> 1);
     oq = 2 * q + (blk & 1);
     OP = 2 * P;
@@ -206,9 +206,9 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
   constexpr int RPI = 32 / CPR;  // rows per cooperative instruction
   const int lane = threadIdx.x & 31;
   int k0 = col, OP = P, OQ = Q, op = p, oq = q;
-  if (e.shuffle) {  // transposed conv: the pass lies in one (dy, dx) block (kout % 32 == 0)
-    const int blk = col / e.kout;
-    k0 = col - blk * e.kout;
+  if (e.shuffle || e.par) {  // transposed conv: the pass lies in one (dy, dx) block (kout % 32 == 0)
+    const int blk = e.par ? e.par - 1 : col / e.kout;
+    k0 = e.par ? col : col - blk * e.kout;
     OP = 2 * P;
     OQ = 2 * Q;
     op = 2 * p + (blk >> 1);
@@ -394,9 +394,9 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMa
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if (e.shuffle) {
-      const int blk = col / e.kout;
-      tma_store_4d(&maps.m[blk], stage, col - blk * e.kout, bq, bp, bn);
+    if (e.shuffle || e.par) {
+      const int blk = e.par ? e.par - 1 : col / e.kout;
+      tma_store_4d(&maps.m[blk], stage, e.par ? col : col - blk * e.kout, bq, bp, bn);
     } else {
 #pragma unroll
       for (int t = 0; t < OSAM_MAX_DEST; t++) {

@@ -278,3 +278,59 @@ def test_invalid_geometry_is_an_error(cuda_lib):
     from objectsam_b200 import OsamError
     with pytest.raises(OsamError):
         ConvOp().init(ConvGeom(1, 16, 16, 48, 32, 3, 3, 1, 1))  # C % 32 != 0 and R·S·C > 32
+
+
+def ref_dgrad(dz, w, x_shape, stride, pad):
+    """NHWC fp16 dz, KRSC w → NHWC fp32 input gradient of conv2d (TF32 off)."""
+    torch.backends.cudnn.allow_tf32 = False
+    N, H, W, C = x_shape
+    dx = torch.nn.grad.conv2d_input((N, C, H, W), w.float().permute(0, 3, 1, 2), dz.float().permute(0, 3, 1, 2),
+                                    stride=stride, padding=pad)
+    return dx.permute(0, 2, 3, 1)
+
+
+# (N, H, W, C, K, R, stride): the network's dgrad shapes — 3×3 s1 and s2, 1×1, narrow and wide, ragged
+DGRAD_SHAPES = [
+    (2, 16, 16, 32, 32, 3, 1),
+    (2, 20, 20, 64, 128, 3, 1),
+    (1, 40, 24, 128, 64, 3, 1),
+    (2, 10, 10, 256, 256, 3, 1),
+    (2, 16, 16, 96, 64, 1, 1),
+    (1, 20, 20, 512, 256, 1, 1),
+    (2, 32, 32, 32, 64, 3, 2),
+    (2, 40, 40, 128, 256, 3, 2),
+    (1, 20, 28, 256, 512, 3, 2),
+    (1, 80, 80, 64, 128, 3, 2),
+]
+
+
+@pytest.mark.parametrize("shape", DGRAD_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_dgrad_matches_torch(cuda_lib, shape):
+    N, H, W, C, K, R, s = shape
+    x, w = rand_conv(N, H, W, C, K, R, seed=sum(shape) + 3)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, s, R // 2))
+    P, Q = op.geom().P(), op.geom().Q()
+    g = torch.Generator(device="cpu").manual_seed(9)
+    dz = (torch.rand(N, P, Q, K, generator=g) * 2 - 1).half().to(DEV)
+    ws = torch.empty(max(op.workspace_size(), 1), dtype=torch.uint8, device=DEV)
+    dx = torch.full((N, H, W, C), 3.0, dtype=torch.half, device=DEV)
+    op.dgrad(dz, w, dx, ws=ws)
+    torch.cuda.synchronize()
+    assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), s, R // 2))
+
+
+@pytest.mark.parametrize("stride", [1, 2])
+def test_conv_dgrad_beta_accumulates(cuda_lib, stride):
+    """beta = 1 adds the gradient to dx (the reference's dgrad_accum for inputs with several consumers)."""
+    N, H, W, C, K = 2, 24, 24, 64, 64
+    x, w = rand_conv(N, H, W, C, K, 3, seed=17)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, stride, 1))
+    P, Q = op.geom().P(), op.geom().Q()
+    g = torch.Generator(device="cpu").manual_seed(10)
+    dz = (torch.rand(N, P, Q, K, generator=g) - 0.5).half().to(DEV)
+    dx0 = (torch.rand(N, H, W, C, generator=g) - 0.5).half().to(DEV)
+    dx = dx0.clone()
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    op.dgrad(dz, w, dx, ws=ws, beta=1.0)
+    torch.cuda.synchronize()
+    assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), stride, 1) + dx0.float())
