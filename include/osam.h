@@ -99,6 +99,14 @@ int osam_conv_fwd(const osam_conv_plan* plan, const void* x, const void* w, void
 int osam_conv_dgrad(const osam_conv_plan* plan, const void* dz, const void* w, void* dx, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream);
 
+/* dw = wgrad(x, dz) (+ beta·dw): the weight gradient of the plan's forward conv, x N×H×W×C and
+ * dz N×P×Q×K → dw K×R×S×C fp16 (KRSC, like the reference's gw_act).  Replaces ConvOp::wgrad (src/conv.h:31,
+ * src/conv.cpp:357-366).  Accumulates in fp32 in the workspace (osam_conv_workspace_size, 256-byte
+ * aligned), which it zeroes itself.  OSAM_ERR_UNSUPPORTED for transposed plans and for channel counts that
+ * are not multiples of 32. */
+int osam_conv_wgrad(const osam_conv_plan* plan, const void* x, const void* dz, void* dw, float beta, void* ws,
+                    size_t ws_bytes, osam_stream_t stream);
+
 /* Conv fused with its epilogue (BN fold + SiLU + residual + multi-destination store, or bias).
  * Replaces ConvOp::fwd followed by bn_eval_scale/bn_forward_apply (src/model.cpp:388-400) or by
  * add_bias (src/model.cpp:405-406). */

@@ -58,6 +58,7 @@ _SIGS = {
     "osam_conv_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_void_p]),
     "osam_conv_fwd_fused": (c_int, [c_void_p, c_void_p, c_void_p, POINTER(Epilogue), c_void_p, c_size_t, c_void_p]),
     "osam_conv_dgrad": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_void_p]),
+    "osam_conv_wgrad": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_void_p]),
     "osam_convt_fwd_static_scratch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
     "osam_sppf_fwd": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "osam_decode": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,

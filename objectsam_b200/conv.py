@@ -85,6 +85,12 @@ class ConvOp:
         check(lib().osam_conv_dgrad(self._plan, _ptr(dy), _ptr(w), _ptr(dx), float(beta), _ptr(ws), nbytes,
                                     stream_ptr(stream)))
 
+    def wgrad(self, x, dy, dw, ws=None, beta: float = 0.0, stream=None) -> None:
+        """dw = wgrad(x, dy) (+ beta·dw), fp16 KRSC — ConvOp::wgrad (src/conv.cpp:357-366)."""
+        nbytes = 0 if ws is None else ws.numel() * ws.element_size()
+        check(lib().osam_conv_wgrad(self._plan, _ptr(x), _ptr(dy), _ptr(dw), float(beta), _ptr(ws), nbytes,
+                                    stream_ptr(stream)))
+
     def fwd_fused(self, x, w, dests: Sequence[DestSpec], kind: int = EPI_BN_ACT, scale=None, shift=None,
                   bias=None, res=None, act: bool = True, round_z: bool = True, ws=None, stream=None) -> None:
         ep = make_epilogue(self._g.K, dests, kind, scale, shift, bias, res, act, round_z)

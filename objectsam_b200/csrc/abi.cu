@@ -654,10 +654,83 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
   return OSAM_OK;
 }
 
+static size_t wgrad_workspace_bytes(const osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  return ((size_t)g.K * g.R * g.S * g.C * 4 + 255) & ~size_t(255);
+}
+
 size_t osam_conv_workspace_size(const osam_conv_plan* p) {
   if (!p) return 0;
   if (p->transposed) return ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
-  return dgrad_workspace_bytes(p);
+  return std::max(dgrad_workspace_bytes(p), wgrad_workspace_bytes(p));
+}
+
+int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float beta, void* ws,
+                    size_t ws_bytes, osam_stream_t stream) {
+  if (!p || !x || !dz || !dw) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
+  const osam_conv_geom& g = p->g;
+  if (p->transposed || (p->mode != A_S1 && p->mode != A_S2) || g.C % 32 || g.K % 32)
+    return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed, small-C or non-32-multiple channels");
+  const size_t need = wgrad_workspace_bytes(p);
+  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dz)) & 15)
+    return fail(OSAM_ERR_INVALID, "wgrad: operands must be 16-byte aligned");
+  WgradLaunch L{};
+  ConvDev& d = L.d;
+  d.N = g.N; d.H = g.H; d.W = g.W; d.C = g.C; d.K = g.K;
+  d.P = p->P; d.Q = p->Q; d.R = g.R; d.S = g.S; d.stride = g.stride; d.pad = g.pad;
+  d.tn = p->tn; d.th = p->th; d.tw = p->tw; d.tiles_q = p->tiles_q; d.tiles_p = p->tiles_p;
+  d.tiles_m = p->tiles_m;
+  d.err = device_error_word();
+  if (!d.err) return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
+  L.AB = g.K % 64 == 0 ? 64 : 32;
+  L.BB = g.C % 64 == 0 ? 64 : 32;
+  L.BN = g.C <= 32 ? 32 : (g.C <= 64 ? 64 : (g.C <= 128 ? 128 : 256));
+  if (L.BB == 32 && L.BN != 32) L.BB = 64;  // C = 96, 160, …: 64-channel boxes, the tail zero-filled
+  L.mode = p->mode;
+  L.acc = static_cast<float*>(ws);
+  L.dw = static_cast<__half*>(dw);
+  L.n_out = (long long)g.K * g.R * g.S * g.C;
+  L.beta = beta;
+  int rc = OSAM_OK;
+  {
+    const uint64_t dims[4] = {(uint64_t)g.K, (uint64_t)p->Q, (uint64_t)p->P, (uint64_t)g.N};
+    const uint64_t str[3] = {(uint64_t)g.K * 2, (uint64_t)p->Q * g.K * 2, (uint64_t)p->P * p->Q * g.K * 2};
+    const uint32_t box[4] = {(uint32_t)L.AB, (uint32_t)p->tw, (uint32_t)p->th, (uint32_t)p->tn};
+    rc = make_map(&L.tdz, dz, 4, dims, str, box, L.AB * 2);
+  }
+  if (rc == OSAM_OK && p->mode == A_S1) {
+    const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+    const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
+    const uint32_t box[4] = {(uint32_t)L.BB, (uint32_t)p->tw, (uint32_t)p->th, (uint32_t)p->tn};
+    rc = make_map(&L.tx, x, 4, dims, str, box, L.BB * 2);
+  } else if (rc == OSAM_OK) {
+    const uint64_t dims[5] = {(uint64_t)2 * g.C, (uint64_t)g.W / 2, 2, (uint64_t)g.H / 2, (uint64_t)g.N};
+    const uint64_t str[4] = {(uint64_t)4 * g.C, (uint64_t)g.W * g.C * 2, (uint64_t)2 * g.W * g.C * 2,
+                             (uint64_t)g.H * g.W * g.C * 2};
+    const uint32_t box[5] = {(uint32_t)L.BB, (uint32_t)p->tw, 1, (uint32_t)p->th, (uint32_t)p->tn};
+    rc = make_map(&L.tx, x, 5, dims, str, box, L.BB * 2);
+  }
+  if (rc) return rc;
+  // split the pixel tiles so that ≈ 2 CTAs per SM are launched
+  const long long nob = (long long)g.R * g.S * ((g.K + 127) / 128) * ((g.C + L.BN - 1) / L.BN);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  long long nsplit = (2LL * sms + nob - 1) / nob;
+  if (nsplit > p->tiles_m) nsplit = p->tiles_m;
+  if (nsplit < 1) nsplit = 1;
+  L.tiles_per_split = (int)((p->tiles_m + nsplit - 1) / nsplit);
+  L.nsplit = (int)((p->tiles_m + L.tiles_per_split - 1) / L.tiles_per_split);
+  if (nob * L.nsplit > 0x7fffffffLL) return fail(OSAM_ERR_UNSUPPORTED, "wgrad grid too large");
+  L.grid = (int)(nob * L.nsplit);
+  cudaError_t e = launch_conv_wgrad(L, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_wgrad launch");
 }
 
 int64_t osam_conv_out_elems(const osam_conv_plan* p) {

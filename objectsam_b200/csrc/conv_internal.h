@@ -88,6 +88,20 @@ struct ConvLaunch {
   int stem_rgb = 0;  // pipelined RGB stem kernel (window tensor map in ta, TMA-store epilogue)
 };
 
+// One weight-gradient launch (conv_wgrad.cu).
+struct WgradLaunch {
+  CUtensorMap tdz, tx;  // dz (K, Q, P, N) and x (forward A view) boxes of 128 tile pixels
+  ConvDev d;            // geometry and the forward plan's spatial tiling
+  float* acc;           // fp32 KRSC accumulator (workspace), zeroed by the launch
+  __half* dw;           // fp16 KRSC result
+  long long n_out;      // K·R·S·C
+  float beta;
+  int AB, BB, BN;       // dz / x box channels (32 or 64), GEMM N block
+  int mode;             // A_S1 or A_S2
+  int grid, nsplit, tiles_per_split;
+};
+cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st);
+
 // Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
 // err_word: device word the kernels report timeouts to (nullptr = the library's per-device word).
 int conv_prepare(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep, float beta,

@@ -1,0 +1,242 @@
+// Weight gradient of a conv on the sm_100a tensor cores (osam_conv_wgrad, replaces ConvOp::wgrad,
+// src/conv.cpp:357-366):  dW[k][r][s][c] = Σ_{n,p,q} dz[n][p][q][k] · x[n][p·st + r − pad][q·st + s − pad][c].
+//
+// For each tap (r, s) this is a GEMM  D[k][c] = Σ_pixels A[k][pixel] · B[c][pixel]  whose reduction runs
+// over the output pixels.  In NHWC both operands already have their M / N index contiguous, which is
+// the MN-major operand form of tcgen05: a TMA box of [pixels][64 channels] with the 128-byte swizzle
+// (32 channels: 64-byte swizzle) is exactly the MN-major canonical layout — rows of 64 channels, one row
+// per reduction index, LBO = distance between 64-channel blocks, SBO = distance between 8-row groups.
+// The pixel tiles are the forward conv's spatial tiles (tn images × th × tw = 128 output pixels): the dz
+// box is the tile itself, the x box is the same tile shifted by the tap (stride 2: the parity view of the
+// forward kernel), and TMA zero fill supplies the padding.
+//
+// Work split: CTA = (tap, 128-row block of K, BN-column block of C, range of pixel tiles).  Each CTA
+// accumulates its range in TMEM (M = 128, N = BN, K = 16 pixels per MMA, 8 MMAs per tile), then adds its
+// fp32 block into a zeroed fp32 workspace with vector atomics; a last pass writes dW in fp16 (+ beta·dW).
+// Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; warps 2–5: the final read-out.
+// No multicast.  Every wait is bounded (sm100.cuh).
+#include "conv_internal.h"
+#include "sm100.cuh"
+
+namespace osam {
+
+// MN-major operand descriptor: `row_bytes` = 128 (64 channels, SWIZZLE_128B) or 64 (32, SWIZZLE_64B).
+__device__ __forceinline__ uint64_t smem_desc_mnmajor(uint32_t saddr, int row_bytes, uint32_t block_bytes) {
+  uint64_t d = (saddr & 0x3FFFFu) >> 4;
+  d |= uint64_t((block_bytes >> 4) & 0x3FFFu) << 16;      // LBO: next block of 64 (32) M/N elements
+  d |= uint64_t(((8 * row_bytes) >> 4) & 0x3FFFu) << 32;  // SBO: next 8 reduction rows
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(row_bytes == 128 ? 2 : 4) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16, fp32 accumulator, both operands MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32_mn(int M, int N) {
+  return (1u << 4) | (1u << 15) | (1u << 16) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+template <int AB, int BB, int BN>
+struct WgCfg {
+  static constexpr int MBOX = 128 / AB;       // dz boxes per stage (M = 128 output channels)
+  static constexpr int NBOX = BN / BB;        // x boxes per stage
+  static constexpr int A_BOX = 128 * AB * 2;  // 128 pixels × AB channels
+  static constexpr int B_BOX = 128 * BB * 2;
+  static constexpr int STAGE_BYTES = MBOX * A_BOX + NBOX * B_BOX;
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 6 ? 6 : STAGES_RAW);
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int THREADS = 64 + 128;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+  static_assert(A_BOX % 1024 == 0 && B_BOX % 1024 == 0, "stage parts must stay 1024-byte aligned");
+};
+
+template <int AB, int BB, int BN, int MODE>
+__global__ void __launch_bounds__(WgCfg<AB, BB, BN>::THREADS, 1)
+    k_conv_wgrad(const __grid_constant__ CUtensorMap tdz, const __grid_constant__ CUtensorMap tx, const ConvDev d,
+                 float* __restrict__ acc, int nsplit, int tiles_per_split) {
+  using Cfg = WgCfg<AB, BB, BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int taps = d.R * d.S;
+  const int mblocks = (d.K + 127) / 128, nblocks = (d.C + BN - 1) / BN;
+  // CTA → (split, tap, m block, n block); neighbouring CTAs share their pixel range (L2 reuse of dz, x)
+  int rest = blockIdx.x;
+  const int nb = rest % nblocks;
+  rest /= nblocks;
+  const int mb = rest % mblocks;
+  rest /= mblocks;
+  const int tap = rest % taps;
+  const int split = rest / taps;
+  const int t0 = split * tiles_per_split, t1 = min(d.tiles_m, t0 + tiles_per_split);
+  const int r = tap / d.S, c = tap - r * d.S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tdz);
+    tma_prefetch_desc(&tx);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = t0; t < t1; t++, it++) {
+        const int s = it % STAGES;
+        if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) break;
+        const int tq = t % d.tiles_q, rr = t / d.tiles_q;
+        const int q0 = tq * d.tw, p0 = (rr % d.tiles_p) * d.th, b0 = (rr / d.tiles_p) * d.tn;
+        mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
+        uint8_t* a = base + s * Cfg::STAGE_BYTES;
+        uint8_t* b = a + Cfg::MBOX * Cfg::A_BOX;
+#pragma unroll
+        for (int j = 0; j < Cfg::MBOX; j++) tma_load_4d(a + j * Cfg::A_BOX, &tdz, full + s, mb * 128 + j * AB, q0, p0, b0);
+#pragma unroll
+        for (int j = 0; j < Cfg::NBOX; j++) {
+          const int cc = nb * BN + j * BB;
+          if (MODE == A_S1) {
+            tma_load_4d(b + j * Cfg::B_BOX, &tx, full + s, cc, q0 + c - d.pad, p0 + r - d.pad, b0);
+          } else {
+            const int dr = r - d.pad, dc = c - d.pad;
+            tma_load_5d(b + j * Cfg::B_BOX, &tx, full + s, (dc & 1) * d.C + cc, q0 + (dc >> 1), dr & 1,
+                        p0 + (dr >> 1), b0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32_mn(128, BN);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = t0; t < t1; t++, it++) {
+        const int s = it % STAGES;
+        if (!mbar_wait(full + s, (it / STAGES) & 1, d.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(base + s * Cfg::STAGE_BYTES), b = a + Cfg::MBOX * Cfg::A_BOX;
+#pragma unroll
+        for (int k = 0; k < 8; k++)  // 16 pixels (reduction rows) per MMA
+          umma_f16(tmem, smem_desc_mnmajor(a + k * 16 * AB * 2, AB * 2, Cfg::A_BOX),
+                   smem_desc_mnmajor(b + k * 16 * BB * 2, BB * 2, Cfg::B_BOX), idesc, (it | k) != 0);
+        umma_commit(empty + s);
+      }
+      if (ok && t1 > t0) umma_commit(accf);
+    }
+  } else {
+    // ---------------------------------------------------------------- read-out: fp32 block → atomics
+    const int quad = warp & 3;
+    const int k = mb * 128 + quad * 32 + lane;  // this lane's output channel
+    const bool ok = t1 > t0 && mbar_wait(accf, 0, d.err);
+    tc_fence_after();
+    if (ok) {
+      const uint32_t dt = tmem + ((uint32_t)(quad * 32) << 16);
+      float* row = acc + (((long long)k * d.R + r) * d.S + c) * d.C + nb * BN;
+#pragma unroll 1
+      for (int j = 0; j < BN; j += 16) {
+        __syncwarp();
+        float v[16];
+        tmem_ld16(dt + j, v);
+        if (k < d.K) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            if (nb * BN + j + i + 4 <= d.C)
+              atomicAdd(reinterpret_cast<float4*>(row + j + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// dw (fp16) = acc (fp32) + beta · dw
+__global__ void k_wgrad_finish(const float* __restrict__ acc, __half* __restrict__ dw, long long n, float beta) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    float v = acc[i];
+    if (beta != 0.f) v += beta * __half2float(dw[i]);
+    dw[i] = __float2half_rn(v);
+  }
+}
+
+template <int AB, int BB, int BN, int MODE>
+static cudaError_t wgrad_launch_one(const WgradLaunch& L, cudaStream_t st) {
+  using Cfg = WgCfg<AB, BB, BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv_wgrad<AB, BB, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  k_conv_wgrad<AB, BB, BN, MODE><<<L.grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.tdz, L.tx, L.d, L.acc, L.nsplit,
+                                                                              L.tiles_per_split);
+  return cudaGetLastError();
+}
+
+template <int AB, int BB, int BN>
+static cudaError_t wgrad_launch_mode(const WgradLaunch& L, cudaStream_t st) {
+  if (L.mode == A_S1) return wgrad_launch_one<AB, BB, BN, A_S1>(L, st);
+  if (L.mode == A_S2) return wgrad_launch_one<AB, BB, BN, A_S2>(L, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(L.acc, 0, (size_t)L.n_out * 4, st);
+  if (e != cudaSuccess) return e;
+  const int AB = L.AB, BB = L.BB, BN = L.BN;
+  if (AB == 64 && BB == 64) {
+    switch (BN) {
+      case 64: e = wgrad_launch_mode<64, 64, 64>(L, st); break;
+      case 128: e = wgrad_launch_mode<64, 64, 128>(L, st); break;
+      case 256: e = wgrad_launch_mode<64, 64, 256>(L, st); break;
+      default: return cudaErrorInvalidValue;
+    }
+  } else if (AB == 64 && BB == 32 && BN == 32) {
+    e = wgrad_launch_mode<64, 32, 32>(L, st);
+  } else if (AB == 32 && BB == 64) {
+    switch (BN) {
+      case 64: e = wgrad_launch_mode<32, 64, 64>(L, st); break;
+      case 128: e = wgrad_launch_mode<32, 64, 128>(L, st); break;
+      case 256: e = wgrad_launch_mode<32, 64, 256>(L, st); break;
+      default: return cudaErrorInvalidValue;
+    }
+  } else if (AB == 32 && BB == 32 && BN == 32) {
+    e = wgrad_launch_mode<32, 32, 32>(L, st);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  int grid = (int)((L.n_out + 255) / 256);
+  if (grid > 4096) grid = 4096;
+  k_wgrad_finish<<<grid, 256, 0, st>>>(L.acc, L.dw, L.n_out, L.beta);
+  return cudaGetLastError();
+}
+
+}  // namespace osam

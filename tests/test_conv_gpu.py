@@ -334,3 +334,41 @@ def test_conv_dgrad_beta_accumulates(cuda_lib, stride):
     op.dgrad(dz, w, dx, ws=ws, beta=1.0)
     torch.cuda.synchronize()
     assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), stride, 1) + dx0.float())
+
+
+def ref_wgrad(x, dz, w_shape, stride, pad):
+    """NHWC fp16 x and dz → KRSC fp32 weight gradient of conv2d (TF32 off)."""
+    torch.backends.cudnn.allow_tf32 = False
+    K, R, S, C = w_shape
+    dw = torch.nn.grad.conv2d_weight(x.float().permute(0, 3, 1, 2), (K, C, R, S), dz.float().permute(0, 3, 1, 2),
+                                     stride=stride, padding=pad)
+    return dw.permute(0, 2, 3, 1)
+
+
+@pytest.mark.parametrize("shape", DGRAD_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_wgrad_matches_torch(cuda_lib, shape):
+    N, H, W, C, K, R, s = shape
+    x, w = rand_conv(N, H, W, C, K, R, seed=sum(shape) + 4)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, s, R // 2))
+    P, Q = op.geom().P(), op.geom().Q()
+    g = torch.Generator(device="cpu").manual_seed(11)
+    dz = (torch.rand(N, P, Q, K, generator=g) * 2 - 1).half().to(DEV)
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    dw = torch.full((K, R, R, C), 5.0, dtype=torch.half, device=DEV)
+    op.wgrad(x, dz, dw, ws=ws)
+    torch.cuda.synchronize()
+    assert_close(dw, ref_wgrad(x, dz, (K, R, R, C), s, R // 2))
+
+
+def test_conv_wgrad_beta_accumulates(cuda_lib):
+    N, H, W, C, K = 2, 24, 24, 64, 128
+    x, w = rand_conv(N, H, W, C, K, 3, seed=19)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    g = torch.Generator(device="cpu").manual_seed(12)
+    dz = (torch.rand(N, H, W, K, generator=g) - 0.5).half().to(DEV)
+    dw0 = (torch.rand(K, 3, 3, C, generator=g) - 0.5).half().to(DEV)
+    dw = dw0.clone()
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    op.wgrad(x, dz, dw, ws=ws, beta=1.0)
+    torch.cuda.synchronize()
+    assert_close(dw, ref_wgrad(x, dz, (K, 3, 3, C), 1, 1) + dw0.float())
