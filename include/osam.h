@@ -134,6 +134,54 @@ int osam_convt_fwd_static_scratch(const osam_conv_plan* plan, const void* x, con
 int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Training-mode BatchNorm + SiLU and the head-conv bias passes (the reference's src/bn.cuh:23-47 and
+ * src/misc.cuh:13-17).  z, residuals and gradients are NHWC fp16 [N·H·W][C] with C a multiple of 8,
+ * C ≤ 2048; per-channel vectors are fp32.  Statistics reduce in fp32 per thread and CTA, then fp64.
+ * Workspaces: osam_bn_workspace_size(C) / osam_chan_sum_workspace_size(C) bytes, 16-byte aligned, ZERO-FILLED
+ * ONCE before first use (the reference's bn_init, src/bn.cuh:28); every call leaves it zeroed again.  One
+ * workspace serves calls issued in order on one stream; calls that may overlap need their own.
+ * ------------------------------------------------------------------------------------------------ */
+size_t osam_bn_workspace_size(int C);
+
+/* scale = γ/√(running_var + eps), shift = β − running_mean·scale.  Replaces bn_eval_scale (src/bn.cuh:36,
+ * src/bn.cu:277-284, :306-309). */
+int osam_bn_eval_scale(int C, const float* gamma, const float* beta, const float* run_mean, const float* run_var,
+                       float eps, float* scale, float* shift, osam_stream_t stream);
+
+/* Batch statistics of z: mean, istd = 1/√(var + eps) (biased var), scale = γ·istd, shift = β − mean·scale;
+ * with momentum > 0 also running_mean ← (1−m)·running_mean + m·mean and running_var ← (1−m)·running_var +
+ * m·var·M/(M−1).  Needs M = N·H·W ≥ 2.  Replaces bn_forward_stats (src/bn.cuh:30-34, src/bn.cu:311-322). */
+int osam_bn_forward_stats(const void* z, int N, int H, int W, int C, const float* gamma, const float* beta,
+                          float* run_mean, float* run_var, float momentum, float eps, float* mean, float* istd,
+                          float* scale, float* shift, void* ws, size_t ws_bytes, osam_stream_t stream);
+
+/* a = act(scale·z + shift) (+ res, [N·H·W][C]) → 1..4 destinations (c1 = 0 means C; channel offsets and
+ * ctot multiples of 8, buffers 16-byte aligned).  act = 1 is SiLU.  Replaces bn_forward_apply
+ * (src/bn.cuh:42-44, src/bn.cu:204-238, :324-327). */
+int osam_bn_forward_apply(const void* z, int N, int H, int W, int C, const float* scale, const float* shift,
+                          const void* res, const osam_dest* dests, int n_dest, int act, osam_stream_t stream);
+
+/* Backward of osam_bn_forward_apply ∘ stats.  grad_dests[i].p is the GRADIENT buffer of forward
+ * destination i (same ctot/choff/c0/c1/up); dA = their sum (2×2 sum for up = 2).  g = dA·silu'(y) (act),
+ * dβ = Σg, dγ = Σg·x̂ into gw_beta/gw_gamma (accum ? += : =), dz = scale·(g − Σg/M − x̂·Σg·x̂/M), and with
+ * res_grad non-null res_grad (res_accum ? += : =) dA.  Two passes: the sums, then dz.  Replaces bn_backward
+ * (src/bn.cuh:46-50, src/bn.cu:240-270, :329-344); its `sums` scratch lives in the workspace. */
+int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mean, const float* istd,
+                     const float* scale, const float* shift, const osam_dest* grad_dests, int n_dest, int act,
+                     void* dz, float* gw_gamma, float* gw_beta, int accum, void* res_grad, int res_accum, void* ws,
+                     size_t ws_bytes, osam_stream_t stream);
+
+/* out[c] (accum ? += : =) Σ_rows x[row][c] for x [M][C] fp16, any C ≤ 2048 (the bias gradient of the head
+ * convs).  Replaces chan_sum (src/misc.cuh:13-14, src/misc.cu:103-113, :168-172). */
+size_t osam_chan_sum_workspace_size(int C);
+int osam_chan_sum(const void* x, int64_t M, int C, float* out, int accum, void* ws, size_t ws_bytes,
+                  osam_stream_t stream);
+
+/* y[row][c] += bias[c] for y [M][C] fp16 (one fp16 rounding of the fp32 sum).  Replaces add_bias
+ * (src/misc.cuh:17, src/misc.cu:116-134, :174-177); the inference path fuses it into the conv epilogue. */
+int osam_add_bias(void* y, int64_t M, int C, const float* bias, osam_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Inference post-process (the reference has it only in numpy: archive/tools/ref_detect.py:37-81).
  * level_hw = {h0, w0, h1, w1, h2, w2} of the three head levels; anchors = Σ h·w, level-major, row-major.
  * ------------------------------------------------------------------------------------------------ */

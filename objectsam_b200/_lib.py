@@ -61,6 +61,20 @@ _SIGS = {
     "osam_conv_wgrad": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_void_p]),
     "osam_convt_fwd_static_scratch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
     "osam_sppf_fwd": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "osam_bn_workspace_size": (c_size_t, [c_int]),
+    "osam_bn_eval_scale": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+                                   c_void_p]),
+    "osam_bn_forward_stats": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_float, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                      c_void_p]),
+    "osam_bn_forward_apply": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                      POINTER(Dest), c_int, c_int, c_void_p]),
+    "osam_bn_backward": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                 POINTER(Dest), c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                 c_void_p, c_size_t, c_void_p]),
+    "osam_chan_sum_workspace_size": (c_size_t, [c_int]),
+    "osam_chan_sum": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "osam_add_bias": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "osam_decode": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,
                             c_void_p, c_void_p]),
     "osam_nms": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_int, c_int, POINTER(c_void_p),

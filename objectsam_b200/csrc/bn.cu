@@ -1,0 +1,714 @@
+// Training-mode BatchNorm + SiLU as standalone HBM passes, and the bias passes of the head convs.
+//
+// Replaces the reference's src/bn.cu (bn_forward_stats :311-322, bn_forward_apply :324-327,
+// bn_backward :329-344, bn_eval_scale :306-309) and src/misc.cu (chan_sum :168-172, add_bias :174-177).
+// The inference path never runs these: there BN is folded into the conv epilogue.  Training needs the
+// batch statistics of z before it can normalise z, and the backward needs two reductions over the whole
+// batch, so these stay separate passes over HBM.
+//
+// Layout: z, residuals, gradients are NHWC fp16 viewed as [M = N·H·W rows][C channels]; one thread owns
+// 8 channels (one 16-byte vector) of a row, V = C/8 consecutive threads cover a row, so a warp reads
+// 32·16 contiguous bytes.  Per-channel statistics are per-thread fp32 sums over the thread's rows, fp32
+// sums over the CTA's row lanes in shared memory, then fp64 atomics into a per-call workspace; the CTA
+// that arrives last turns the fp64 sums into the outputs and zeroes the workspace again for the next
+// call.  Every CTA owns one contiguous chunk of rows, and each pass that re-reads a chunk right after a
+// reduction over it (forward apply after statistics, backward apply after the gradient sums) walks the
+// chunk from its end: the rows a CTA read last are the ones the 126 MB L2 still holds.
+#include "conv_internal.h"
+#include "epilogue.cuh"
+#include "sm100.cuh"
+
+namespace osam {
+namespace {
+
+constexpr int kBnT = 256;            // threads per CTA
+constexpr int kBnMaxC = kBnT * 8;    // one 8-channel vector per thread per row at least
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// σ(y) = 1 / (1 + 2^(−y·log2 e)) on the MUFU unit; y is clamped at −80 so 1 + e^{−y} stays finite.
+__device__ __forceinline__ float sigmoid_fast(float y) {
+  return rcp_approx(1.f + ex2_approx(-kLog2e * fmaxf(y, -80.f)));
+}
+
+// Pixel index of the top-left of row `row`'s 2×2 block in the 2H×2W upsampled grid (nearest ×2).
+__device__ __forceinline__ long long up2_base(long long row, int H, int W) {
+  const long long hw = (long long)H * W;
+  const long long n = row / hw;
+  const int rem = int(row - n * hw), h = rem / W, w = rem - h * W;
+  return (n * 2 * H + 2 * h) * (2LL * W) + 2 * w;
+}
+
+struct GradDest {
+  const __half* g;  // gradient of the destination buffer (NHWC, ctot channels)
+  int ctot, choff, c0, c1, up;
+};
+
+// dA for channels c..c+7 of `row`: the sum of the gradients of every destination the forward wrote
+// that channel to, a 2×2 sum for the upsampled ones (reference gather8, src/bn.cu:46-66).
+__device__ __forceinline__ void gather_grad8(const GradDest* dl, int ndl, long long row, int c, int H, int W,
+                                             float (&dA)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; i++) dA[i] = 0.f;
+#pragma unroll
+  for (int k = 0; k < OSAM_MAX_DEST; k++) {
+    if (k >= ndl) break;
+    const GradDest& d = dl[k];
+    if (c < d.c0 || c >= d.c1) continue;
+    const int cc = d.choff + c - d.c0;
+    float t[8];
+    if (d.up == 1) {
+      ld8h(d.g + row * d.ctot + cc, t);
+#pragma unroll
+      for (int i = 0; i < 8; i++) dA[i] += t[i];
+    } else {
+      const long long b = up2_base(row, H, W), W2 = 2LL * W;
+      const long long q[4] = {b, b + 1, b + W2, b + W2 + 1};
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        ld8h(d.g + q[u] * d.ctot + cc, t);
+#pragma unroll
+        for (int i = 0; i < 8; i++) dA[i] += t[i];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void ld8f(const float* p, float (&o)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+  o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+// Per-channel parameters may sit anywhere in a parameter arena: 4-byte alignment only.
+__device__ __forceinline__ void ld8f_any(const float* p, float (&o)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; i++) o[i] = p[i];
+}
+
+enum RedMode : int { RED_STATS = 0, RED_BWD = 1, RED_SUM = 2 };
+
+struct RedArgs {
+  const __half* z;  // [M][C]
+  long long M;
+  int H, W, C;      // H, W: spatial size of z (for the upsampled gradient gather)
+  int rowlanes;     // rows processed side by side by one CTA (kBnT / (C/8))
+  long long rows;   // rows per CTA chunk
+  // RED_STATS
+  const float* gamma;
+  const float* beta;
+  float* run_mean;
+  float* run_var;
+  float mom, eps;
+  float* mean;
+  float* istd;
+  float* scale;
+  float* shift;
+  // RED_BWD (reads mean/istd/scale/shift)
+  GradDest dl[OSAM_MAX_DEST];
+  int ndl, act;
+  float* sums;      // [2C] Σg/M, Σg·x̂/M for the apply pass
+  float* gw_gamma;
+  float* gw_beta;
+  int accum;
+  // RED_SUM
+  float* out;
+  // all
+  double* acc;      // [2C] zero on entry, zero again on exit
+  unsigned* counter;
+};
+
+// Per-channel reductions over the rows of z (reference k_reduce<0|1>, src/bn.cu:112-202, and
+// chan_sum, src/misc.cu:103-113, :168-172):
+//   RED_STATS: Σ(z−K), Σ(z−K)² with K = running mean (shifted sums: no cancellation when |mean| ≫ std)
+//   RED_BWD:   Σg, Σg·x̂ with g = dA·silu'(y), y = scale·z + shift, x̂ = (z − mean)·istd
+//   RED_SUM:   Σz
+template <int MODE, int U>
+__global__ void __launch_bounds__(kBnT) k_bn_reduce(const RedArgs P) {
+  extern __shared__ float2 bn_red[];  // [rowlanes][C]
+  __shared__ unsigned s_last;
+  const int C = P.C, V = C >> 3, RL = P.rowlanes;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  const bool active = rl < RL;
+  const long long r0 = (long long)blockIdx.x * P.rows;
+  const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
+  float a[8], b[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) a[i] = b[i] = 0.f;
+  if (active) {
+    float k0[8], k1[8], k2[8], k3[8];
+    if (MODE == RED_STATS) ld8f_any(P.run_mean + c, k0);
+    if (MODE == RED_BWD) {
+      ld8f_any(P.scale + c, k0);
+      ld8f_any(P.shift + c, k1);
+      ld8f_any(P.mean + c, k2);
+      ld8f_any(P.istd + c, k3);
+    }
+    for (long long r = r0 + rl; r < r1; r += (long long)U * RL) {
+      float v[U][8], dA[U][8];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const long long rr = r + (long long)u * RL;
+        if (rr < r1) ld8h(P.z + rr * C + c, v[u]);
+      }
+      if (MODE == RED_BWD) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+          const long long rr = r + (long long)u * RL;
+          if (rr < r1) gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        if (r + (long long)u * RL >= r1) break;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (MODE == RED_STATS) {
+            const float d = v[u][i] - k0[i];
+            a[i] += d;
+            b[i] = fmaf(d, d, b[i]);
+          } else if (MODE == RED_BWD) {
+            float g = dA[u][i];
+            if (P.act) {
+              const float y = fmaf(k0[i], v[u][i], k1[i]), s = sigmoid_fast(y);
+              g *= s * fmaf(y, 1.f - s, 1.f);
+            }
+            a[i] += g;
+            b[i] = fmaf(g, (v[u][i] - k2[i]) * k3[i], b[i]);
+          } else {
+            a[i] += v[u][i];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) bn_red[rl * C + c + i] = make_float2(a[i], b[i]);
+  }
+  __syncthreads();
+  for (int ch = threadIdx.x; ch < C; ch += kBnT) {
+    float sa = 0.f, sb = 0.f;
+    for (int k = 0; k < RL; k++) {
+      const float2 t = bn_red[k * C + ch];
+      sa += t.x;
+      sb += t.y;
+    }
+    atomicAdd(&P.acc[ch], double(sa));
+    if (MODE != RED_SUM) atomicAdd(&P.acc[C + ch], double(sb));
+  }
+  // The last CTA to arrive finalises (threadfence reduction: every CTA's atomics are visible before its
+  // arrival on the counter).
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(P.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const double Md = double(P.M);
+  for (int ch = threadIdx.x; ch < C; ch += kBnT) {
+    const double sx = __ldcg(&P.acc[ch]);
+    const double sy = MODE != RED_SUM ? __ldcg(&P.acc[C + ch]) : 0.0;
+    P.acc[ch] = 0.0;
+    if (MODE != RED_SUM) P.acc[C + ch] = 0.0;
+    if (MODE == RED_STATS) {
+      // mean = K + E[z−K]; biased variance E[(z−K)²] − E[z−K]² (clamped at 0) for normalising; the
+      // running variance takes the unbiased M/(M−1) form (reference src/bn.cu:176-191).
+      const float K = P.run_mean[ch];
+      const float dm = float(sx / Md);
+      float var = float(sy / Md - double(dm) * double(dm));
+      var = var < 0.f ? 0.f : var;
+      const float m = K + dm, is = rsqrtf(var + P.eps);
+      P.mean[ch] = m;
+      P.istd[ch] = is;
+      const float sc = P.gamma[ch] * is;
+      P.scale[ch] = sc;
+      P.shift[ch] = P.beta[ch] - m * sc;
+      if (P.mom > 0.f) {
+        P.run_mean[ch] = (1.f - P.mom) * K + P.mom * m;
+        P.run_var[ch] = (1.f - P.mom) * P.run_var[ch] + P.mom * float(double(var) * Md / (Md - 1.0));
+      }
+    } else if (MODE == RED_BWD) {
+      P.sums[ch] = float(sx / Md);
+      P.sums[C + ch] = float(sy / Md);
+      if (P.accum) {
+        P.gw_beta[ch] += float(sx);
+        P.gw_gamma[ch] += float(sy);
+      } else {
+        P.gw_beta[ch] = float(sx);
+        P.gw_gamma[ch] = float(sy);
+      }
+    } else {
+      P.out[ch] = P.accum ? P.out[ch] + float(sx) : float(sx);
+    }
+  }
+  if (threadIdx.x == 0) *P.counter = 0u;
+}
+
+struct ApplyArgs {
+  const __half* z;
+  long long M;
+  int H, W, C, rowlanes;
+  long long rows;
+  const float* scale;
+  const float* shift;
+  const __half* res;  // [M][C] added after the activation, or null
+  DestDev dest[OSAM_MAX_DEST];
+  int ndest, act;
+};
+
+// a = act(scale·z + shift) (+ res) → every destination (reference k_apply, src/bn.cu:204-238).
+template <int U>
+__global__ void __launch_bounds__(kBnT) k_bn_apply(const ApplyArgs P) {
+  const int C = P.C, V = C >> 3, RL = P.rowlanes;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  if (rl >= RL) return;
+  const long long r0 = (long long)blockIdx.x * P.rows;
+  const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
+  float sc[8], sh[8];
+  ld8f_any(P.scale + c, sc);
+  ld8f_any(P.shift + c, sh);
+  for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
+    float v[U][8], rv[U][8];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const long long rr = r - (long long)u * RL;
+      if (rr >= r0) {
+        ld8h(P.z + rr * C + c, v[u]);
+        if (P.res) ld8h(P.res + rr * C + c, rv[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const long long rr = r - (long long)u * RL;
+      if (rr < r0) break;
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float y = fmaf(sc[i], v[u][i], sh[i]);
+        o[i] = P.act ? y * sigmoid_fast(y) : y;
+        if (P.res) o[i] += rv[u][i];
+      }
+#pragma unroll
+      for (int k = 0; k < OSAM_MAX_DEST; k++) {
+        if (k >= P.ndest) break;
+        const DestDev& d = P.dest[k];
+        if (c < d.c0 || c >= d.c1) continue;
+        const int cc = d.choff + c - d.c0;
+        if (d.up == 1) {
+          st8h(d.p + rr * d.ctot + cc, o);
+        } else {
+          const long long b = up2_base(rr, P.H, P.W), W2 = 2LL * P.W;
+          st8h(d.p + b * d.ctot + cc, o);
+          st8h(d.p + (b + 1) * d.ctot + cc, o);
+          st8h(d.p + (b + W2) * d.ctot + cc, o);
+          st8h(d.p + (b + W2 + 1) * d.ctot + cc, o);
+        }
+      }
+    }
+  }
+}
+
+struct BwdArgs {
+  const __half* z;
+  long long M;
+  int H, W, C, rowlanes;
+  long long rows;
+  const float* mean;
+  const float* istd;
+  const float* scale;
+  const float* shift;
+  const float* sums;  // [2C] from the reduction pass
+  GradDest dl[OSAM_MAX_DEST];
+  int ndl, act;
+  __half* dz;
+  __half* res_grad;
+  int res_accum;
+};
+
+// dz = scale·(g − mean(g) − x̂·mean(g·x̂)); res_grad (=|+=) dA (reference k_bwd_apply, src/bn.cu:240-270).
+template <int U>
+__global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
+  const int C = P.C, V = C >> 3, RL = P.rowlanes;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  if (rl >= RL) return;
+  const long long r0 = (long long)blockIdx.x * P.rows;
+  const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
+  float sc[8], sh[8], mu[8], is[8], m1[8], m2[8];
+  ld8f_any(P.scale + c, sc);
+  ld8f_any(P.shift + c, sh);
+  ld8f_any(P.mean + c, mu);
+  ld8f_any(P.istd + c, is);
+  ld8f(P.sums + c, m1);
+  ld8f(P.sums + C + c, m2);
+  for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
+    float v[U][8], dA[U][8];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const long long rr = r - (long long)u * RL;
+      if (rr >= r0) {
+        ld8h(P.z + rr * C + c, v[u]);
+        gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const long long rr = r - (long long)u * RL;
+      if (rr < r0) break;
+      const long long off = rr * C + c;
+      if (P.res_grad) {
+        float t[8];
+        if (P.res_accum) {
+          ld8h(P.res_grad + off, t);
+#pragma unroll
+          for (int i = 0; i < 8; i++) t[i] += dA[u][i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; i++) t[i] = dA[u][i];
+        }
+        st8h(P.res_grad + off, t);
+      }
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float g = dA[u][i];
+        if (P.act) {
+          const float y = fmaf(sc[i], v[u][i], sh[i]), s = sigmoid_fast(y);
+          g *= s * fmaf(y, 1.f - s, 1.f);
+        }
+        const float xh = (v[u][i] - mu[i]) * is[i];
+        o[i] = sc[i] * (g - m1[i] - xh * m2[i]);
+      }
+      st8h(P.dz + off, o);
+    }
+  }
+}
+
+// Σ over rows of x for channel counts that are not a multiple of 8 (the 1-channel class head): every
+// element goes to shared-memory channel sums, then to the fp64 accumulators; last CTA finalises.
+__global__ void __launch_bounds__(kBnT) k_chan_sum_any(const __half* __restrict__ x, long long n, int C,
+                                                        long long per_cta, float* out, int accum, double* acc,
+                                                        unsigned* counter) {
+  extern __shared__ float s_sum[];  // [C]
+  __shared__ unsigned s_last;
+  for (int ch = threadIdx.x; ch < C; ch += kBnT) s_sum[ch] = 0.f;
+  __syncthreads();
+  const long long e0 = (long long)blockIdx.x * per_cta;
+  const long long e1 = e0 + per_cta < n ? e0 + per_cta : n;
+  float run = 0.f;
+  int run_ch = -1;
+  for (long long e = e0 + threadIdx.x; e < e1; e += kBnT) {
+    const int ch = int(e % C);
+    const float v = __half2float(x[e]);
+    if (ch == run_ch) {
+      run += v;
+    } else {
+      if (run_ch >= 0) atomicAdd(&s_sum[run_ch], run);
+      run_ch = ch;
+      run = v;
+    }
+  }
+  if (run_ch >= 0) atomicAdd(&s_sum[run_ch], run);
+  __syncthreads();
+  for (int ch = threadIdx.x; ch < C; ch += kBnT) atomicAdd(&acc[ch], double(s_sum[ch]));
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int ch = threadIdx.x; ch < C; ch += kBnT) {
+    const double s = __ldcg(&acc[ch]);
+    acc[ch] = 0.0;
+    out[ch] = accum ? out[ch] + float(s) : float(s);
+  }
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
+// y += bias per channel, fp32 add then one fp16 rounding (reference k_add_bias8 / k_add_bias,
+// src/misc.cu:116-134).
+__global__ void __launch_bounds__(kBnT) k_add_bias8(__half* __restrict__ y, long long nvec, int C,
+                                                     const float* __restrict__ bias) {
+  const int V = C >> 3;
+  for (long long i = (long long)blockIdx.x * kBnT + threadIdx.x; i < nvec; i += (long long)gridDim.x * kBnT) {
+    const int c = int(i % V) * 8;
+    float v[8], b[8];
+    ld8h(y + i * 8, v);
+    ld8f_any(bias + c, b);
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] += b[k];
+    st8h(y + i * 8, v);
+  }
+}
+__global__ void __launch_bounds__(kBnT) k_add_bias1(__half* __restrict__ y, long long n, int C,
+                                                     const float* __restrict__ bias) {
+  for (long long i = (long long)blockIdx.x * kBnT + threadIdx.x; i < n; i += (long long)gridDim.x * kBnT)
+    y[i] = __float2half(__half2float(y[i]) + bias[i % C]);
+}
+
+// Eval-mode fold: scale = γ/√(var+eps), shift = β − μ·scale (reference k_eval_scale, src/bn.cu:277-284).
+__global__ void k_bn_eval_scale(int C, const float* g, const float* b, const float* rm, const float* rv, float eps,
+                                float* scale, float* shift) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float sc = g[c] * rsqrtf(rv[c] + eps);
+  scale[c] = sc;
+  shift[c] = b[c] - rm[c] * sc;
+}
+
+// ------------------------------------------------------------------ host side
+constexpr int kUStats = 4, kUBwd = 2, kUApply = 4, kUBwdApply = 2;
+
+int g_sms_cache[64] = {};
+int g_occ_cache[64][2] = {};
+
+// Resident CTAs per SM of the reduction kernel for `mode` (0: statistics / channel sums, 1: backward),
+// times the SM count: the grid that keeps every CTA of a pass resident at once.
+int resident_ctas(int mode) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 4;
+  if (!g_sms_cache[dev]) {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    g_sms_cache[dev] = sms > 0 ? sms : 148;
+  }
+  if (!g_occ_cache[dev][mode]) {
+    int occ = 0;
+    const size_t smem = size_t(kBnT) * 8 * sizeof(float2);
+    cudaError_t e = mode == 0
+        ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bn_reduce<RED_STATS, kUStats>, kBnT, smem)
+        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bn_reduce<RED_BWD, kUBwd>, kBnT, smem);
+    g_occ_cache[dev][mode] = (e == cudaSuccess && occ > 0) ? occ : 2;
+  }
+  return g_sms_cache[dev] * g_occ_cache[dev][mode];
+}
+
+struct Chunking {
+  int rowlanes, nblk;
+  long long rows;
+};
+// One contiguous chunk of rows per CTA, at most one resident wave, at least two row iterations per thread.
+Chunking chunking(long long M, int C, int mode) {
+  Chunking k;
+  k.rowlanes = kBnT / (C / 8);
+  const long long target = resident_ctas(mode);
+  long long rows = (M + target - 1) / target;
+  const long long min_rows = 2LL * k.rowlanes;
+  if (rows < min_rows) rows = min_rows;
+  k.rows = rows;
+  k.nblk = int((M + rows - 1) / rows);
+  return k;
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int bad(int code, const char* what) {
+  set_last_error("%s", what);
+  return code;
+}
+
+struct BnWs {
+  double* acc;
+  unsigned* counter;
+  float* sums;
+};
+size_t bn_ws_bytes(int C) { return ((size_t(C) * 24 + 16) + 255) / 256 * 256; }
+BnWs bn_ws(void* ws, int C) {
+  char* p = static_cast<char*>(ws);
+  BnWs w;
+  w.acc = reinterpret_cast<double*>(p);
+  w.counter = reinterpret_cast<unsigned*>(p + size_t(C) * 16);
+  w.sums = reinterpret_cast<float*>(p + size_t(C) * 16 + 16);
+  return w;
+}
+
+int check_shape(const void* z, int N, int H, int W, int C) {
+  if (!z || N < 1 || H < 1 || W < 1) return bad(OSAM_ERR_INVALID, "bn: empty tensor");
+  if (C < 8 || C % 8 || C > kBnMaxC) return bad(OSAM_ERR_INVALID, "bn: channels must be a multiple of 8 in [8, 2048]");
+  if (!al16(z)) return bad(OSAM_ERR_INVALID, "bn: tensor not 16-byte aligned");
+  if ((long long)N * H * W >= (1LL << 40)) return bad(OSAM_ERR_INVALID, "bn: tensor too large");
+  return OSAM_OK;
+}
+
+int launched(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("%s launch: %s", what, cudaGetErrorString(e));
+    return OSAM_ERR_CUDA;
+  }
+  return OSAM_OK;
+}
+
+}  // namespace
+}  // namespace osam
+
+using namespace osam;
+
+extern "C" {
+
+size_t osam_bn_workspace_size(int C) { return C > 0 ? bn_ws_bytes(C) : 0; }
+
+int osam_bn_eval_scale(int C, const float* gamma, const float* beta, const float* run_mean, const float* run_var,
+                       float eps, float* scale, float* shift, osam_stream_t stream) {
+  if (C < 1 || !gamma || !beta || !run_mean || !run_var || !scale || !shift)
+    return bad(OSAM_ERR_INVALID, "bn_eval_scale arguments");
+  k_bn_eval_scale<<<(C + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(C, gamma, beta, run_mean,
+                                                                                        run_var, eps, scale, shift);
+  return launched("osam_bn_eval_scale");
+}
+
+int osam_bn_forward_stats(const void* z, int N, int H, int W, int C, const float* gamma, const float* beta,
+                          float* run_mean, float* run_var, float momentum, float eps, float* mean, float* istd,
+                          float* scale, float* shift, void* ws, size_t ws_bytes, osam_stream_t stream) {
+  int rc = check_shape(z, N, H, W, C);
+  if (rc) return rc;
+  if (!gamma || !beta || !run_mean || !run_var || !mean || !istd || !scale || !shift)
+    return bad(OSAM_ERR_INVALID, "bn_forward_stats: null parameter");
+  const long long M = (long long)N * H * W;
+  if (M < 2) return bad(OSAM_ERR_INVALID, "bn_forward_stats: batch statistics need at least 2 values per channel");
+  if (!ws || ws_bytes < bn_ws_bytes(C) || !al16(ws)) return bad(OSAM_ERR_INVALID, "bn_forward_stats: workspace");
+  const Chunking k = chunking(M, C, 0);
+  const BnWs w = bn_ws(ws, C);
+  RedArgs P{};
+  P.z = static_cast<const __half*>(z);
+  P.M = M; P.H = H; P.W = W; P.C = C;
+  P.rowlanes = k.rowlanes; P.rows = k.rows;
+  P.gamma = gamma; P.beta = beta; P.run_mean = run_mean; P.run_var = run_var;
+  P.mom = momentum; P.eps = eps;
+  P.mean = mean; P.istd = istd; P.scale = scale; P.shift = shift;
+  P.acc = w.acc; P.counter = w.counter;
+  const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
+  k_bn_reduce<RED_STATS, kUStats><<<k.nblk, kBnT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  return launched("osam_bn_forward_stats");
+}
+
+int osam_bn_forward_apply(const void* z, int N, int H, int W, int C, const float* scale, const float* shift,
+                          const void* res, const osam_dest* dests, int n_dest, int act, osam_stream_t stream) {
+  int rc = check_shape(z, N, H, W, C);
+  if (rc) return rc;
+  if (!scale || !shift) return bad(OSAM_ERR_INVALID, "bn_forward_apply: null scale/shift");
+  if (n_dest < 1 || n_dest > OSAM_MAX_DEST || !dests) return bad(OSAM_ERR_INVALID, "bn_forward_apply: 1..4 dests");
+  if (res && !al16(res)) return bad(OSAM_ERR_INVALID, "bn_forward_apply: residual not 16-byte aligned");
+  const long long M = (long long)N * H * W;
+  const Chunking k = chunking(M, C, 0);
+  ApplyArgs P{};
+  P.z = static_cast<const __half*>(z);
+  P.M = M; P.H = H; P.W = W; P.C = C;
+  P.rowlanes = k.rowlanes; P.rows = k.rows;
+  P.scale = scale; P.shift = shift;
+  P.res = static_cast<const __half*>(res);
+  P.ndest = n_dest;
+  P.act = act ? 1 : 0;
+  for (int i = 0; i < n_dest; i++) {
+    const osam_dest& d = dests[i];
+    const int c1 = d.c1 > 0 ? d.c1 : C;
+    if (!d.p || !al16(d.p) || d.c0 < 0 || d.c0 % 8 || c1 % 8 || c1 > C || d.c0 >= c1 || d.choff < 0 ||
+        d.choff % 8 || d.ctot % 8 || d.choff + (c1 - d.c0) > d.ctot || (d.up != 1 && d.up != 2))
+      return bad(OSAM_ERR_INVALID, "bn_forward_apply: destination (16-byte aligned, channels multiple of 8)");
+    P.dest[i] = DestDev{static_cast<__half*>(d.p), d.ctot, d.choff, d.c0, c1, d.up, 1};
+  }
+  k_bn_apply<kUApply><<<k.nblk, kBnT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  return launched("osam_bn_forward_apply");
+}
+
+int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mean, const float* istd,
+                     const float* scale, const float* shift, const osam_dest* grad_dests, int n_dest, int act,
+                     void* dz, float* gw_gamma, float* gw_beta, int accum, void* res_grad, int res_accum, void* ws,
+                     size_t ws_bytes, osam_stream_t stream) {
+  int rc = check_shape(z, N, H, W, C);
+  if (rc) return rc;
+  if (!mean || !istd || !scale || !shift || !gw_gamma || !gw_beta)
+    return bad(OSAM_ERR_INVALID, "bn_backward: null parameter");
+  if (!dz || !al16(dz)) return bad(OSAM_ERR_INVALID, "bn_backward: dz missing or not 16-byte aligned");
+  if (res_grad && !al16(res_grad)) return bad(OSAM_ERR_INVALID, "bn_backward: res_grad not 16-byte aligned");
+  if (n_dest < 1 || n_dest > OSAM_MAX_DEST || !grad_dests) return bad(OSAM_ERR_INVALID, "bn_backward: 1..4 dests");
+  if (!ws || ws_bytes < bn_ws_bytes(C) || !al16(ws)) return bad(OSAM_ERR_INVALID, "bn_backward: workspace");
+  const long long M = (long long)N * H * W;
+  const Chunking k = chunking(M, C, 1);
+  const BnWs w = bn_ws(ws, C);
+  RedArgs P{};
+  BwdArgs B{};
+  for (int i = 0; i < n_dest; i++) {
+    const osam_dest& d = grad_dests[i];
+    const int c1 = d.c1 > 0 ? d.c1 : C;
+    if (!d.p || !al16(d.p) || d.c0 < 0 || d.c0 % 8 || c1 % 8 || c1 > C || d.c0 >= c1 || d.choff < 0 ||
+        d.choff % 8 || d.ctot % 8 || d.choff + (c1 - d.c0) > d.ctot || (d.up != 1 && d.up != 2))
+      return bad(OSAM_ERR_INVALID, "bn_backward: gradient destination (16-byte aligned, channels multiple of 8)");
+    P.dl[i] = B.dl[i] = GradDest{static_cast<const __half*>(d.p), d.ctot, d.choff, d.c0, c1, d.up};
+  }
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  P.z = B.z = static_cast<const __half*>(z);
+  P.M = B.M = M; P.H = B.H = H; P.W = B.W = W; P.C = B.C = C;
+  P.rowlanes = B.rowlanes = k.rowlanes; P.rows = B.rows = k.rows;
+  P.ndl = B.ndl = n_dest;
+  P.act = B.act = act ? 1 : 0;
+  P.mean = const_cast<float*>(mean);
+  P.istd = const_cast<float*>(istd);
+  P.scale = const_cast<float*>(scale);
+  P.shift = const_cast<float*>(shift);
+  B.mean = mean;
+  B.istd = istd;
+  B.scale = scale;
+  B.shift = shift;
+  P.sums = w.sums; B.sums = w.sums;
+  P.gw_gamma = gw_gamma; P.gw_beta = gw_beta; P.accum = accum ? 1 : 0;
+  P.acc = w.acc; P.counter = w.counter;
+  B.dz = static_cast<__half*>(dz);
+  B.res_grad = static_cast<__half*>(res_grad);
+  B.res_accum = res_accum ? 1 : 0;
+  const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
+  k_bn_reduce<RED_BWD, kUBwd><<<k.nblk, kBnT, smem, st>>>(P);
+  if ((rc = launched("osam_bn_backward (sums)"))) return rc;
+  k_bn_bwd_apply<kUBwdApply><<<k.nblk, kBnT, 0, st>>>(B);
+  return launched("osam_bn_backward (apply)");
+}
+
+size_t osam_chan_sum_workspace_size(int C) { return C > 0 ? ((size_t(C) * 8 + 16) + 255) / 256 * 256 : 0; }
+
+int osam_chan_sum(const void* x, int64_t M, int C, float* out, int accum, void* ws, size_t ws_bytes,
+                  osam_stream_t stream) {
+  if (!x || M < 1 || C < 1 || C > kBnMaxC || !out) return bad(OSAM_ERR_INVALID, "chan_sum arguments");
+  if (!ws || ws_bytes < osam_chan_sum_workspace_size(C) || !al16(ws))
+    return bad(OSAM_ERR_INVALID, "chan_sum: workspace");
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  double* acc = static_cast<double*>(ws);
+  unsigned* counter = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + size_t(C) * 8);
+  if (C % 8 == 0 && al16(x)) {
+    const Chunking k = chunking(M, C, 0);
+    RedArgs P{};
+    P.z = static_cast<const __half*>(x);
+    P.M = M; P.H = 1; P.W = 1; P.C = C;
+    P.rowlanes = k.rowlanes; P.rows = k.rows;
+    P.out = out; P.accum = accum ? 1 : 0;
+    P.acc = acc; P.counter = counter;
+    const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
+    k_bn_reduce<RED_SUM, kUStats><<<k.nblk, kBnT, smem, st>>>(P);
+  } else {
+    const long long n = (long long)M * C;
+    long long per = (n + resident_ctas(0) - 1) / resident_ctas(0);
+    if (per < 8LL * kBnT) per = 8LL * kBnT;
+    const int nblk = int((n + per - 1) / per);
+    k_chan_sum_any<<<nblk, kBnT, size_t(C) * sizeof(float), st>>>(static_cast<const __half*>(x), n, C, per, out,
+                                                                   accum ? 1 : 0, acc, counter);
+  }
+  return launched("osam_chan_sum");
+}
+
+int osam_add_bias(void* y, int64_t M, int C, const float* bias, osam_stream_t stream) {
+  if (!y || M < 1 || C < 1 || !bias) return bad(OSAM_ERR_INVALID, "add_bias arguments");
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long n = (long long)M * C;
+  const int grid = resident_ctas(0);
+  if (C % 8 == 0 && al16(y)) {
+    const long long nv = n / 8;
+    const int g = int(nv / kBnT + 1 < grid ? nv / kBnT + 1 : grid);
+    k_add_bias8<<<g, kBnT, 0, st>>>(static_cast<__half*>(y), nv, C, bias);
+  } else {
+    const int g = int(n / kBnT + 1 < grid ? n / kBnT + 1 : grid);
+    k_add_bias1<<<g, kBnT, 0, st>>>(static_cast<__half*>(y), n, C, bias);
+  }
+  return launched("osam_add_bias");
+}
+
+}  // extern "C"

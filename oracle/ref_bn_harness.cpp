@@ -1,0 +1,163 @@
+// Test infrastructure: runs the reference's own training-mode BN / bias / stem-wgrad kernels (built from its
+// sources src/bn.cu and src/misc.cu by oracle/Makefile into oracle/_ref/ref_bn) on inputs read from an FSOW
+// file, and writes their outputs to another, so the GPU tests can compare this build's kernels and the CPU
+// restatement (oracle/bn_ref.py) with the reference itself on identical inputs.
+//
+//   ref_bn <in.fsow> <out.fsow>
+//
+// Cases are named "c<i>.*".  c<i>.meta (int32) = {op, ...}:
+//   op 0  CONVBN training node: meta = {0, N, H, W, C, act, has_res, ndest, accum, res_accum,
+//         (ctot, choff, c0, c1, up) × ndest}; c<i>.f = {momentum, eps}; inputs z, gamma, beta, run_mean,
+//         run_var, [res], dest<k> (initial destination contents), grad<k> (destination gradients),
+//         gw_gamma0, gw_beta0, [res_grad0].  Runs bn_forward_stats → bn_forward_apply → bn_backward
+//         (src/model.cpp:388-400, :440-444) and writes mean, istd, scale, shift, run_mean, run_var,
+//         dest<k>, dz, gw_gamma, gw_beta, [res_grad].
+//   op 1  chan_sum: meta = {1, M, C, accum}; x (M, C), out0 (C) → out.
+//   op 2  add_bias: meta = {2, M, C}; y (M, C), bias (C) → y.
+//   op 3  wgrad_rgb_s2: meta = {3, N, H, W, K}; x (N, H, W, 3), dz (N, P, Q, K) → dw (K, 3, 3, 3) and
+//         ran (1 if the reference took its own kernel, 0 if it declined the shape).
+// Activations are converted to the reference's act_t (fp16) on upload; every value the tests send is
+// fp16-representable.
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "bn.cuh"
+#include "fsow.h"
+#include "misc.cuh"
+
+namespace {
+
+const HostTensor& need(const TensorMap& m, const std::string& k) {
+  auto it = m.find(k);
+  FSO_ASSERT(it != m.end(), "missing %s", k.c_str());
+  return it->second;
+}
+bool has(const TensorMap& m, const std::string& k) { return m.count(k) > 0; }
+
+act_t* up_act(const HostTensor& t) {
+  const int64_t n = t.numel();
+  std::vector<act_t> h(n);
+  for (int64_t i = 0; i < n; i++) h[i] = from_f<act_t>(t.f32()[i]);
+  act_t* d = dalloc<act_t>(n);
+  CUDA_CHECK(cudaMemcpy(d, h.data(), n * sizeof(act_t), cudaMemcpyHostToDevice));
+  return d;
+}
+float* up_f32(const HostTensor& t) {
+  float* d = dalloc<float>(t.numel());
+  CUDA_CHECK(cudaMemcpy(d, t.f32(), t.numel() * sizeof(float), cudaMemcpyHostToDevice));
+  return d;
+}
+HostTensor down_act(const act_t* d, const std::vector<int64_t>& shape) {
+  HostTensor t = HostTensor::make_f32(shape, nullptr);
+  const int64_t n = t.numel();
+  std::vector<act_t> h(n);
+  CUDA_CHECK(cudaMemcpy(h.data(), d, n * sizeof(act_t), cudaMemcpyDeviceToHost));
+  float* o = reinterpret_cast<float*>(t.data.data());
+  for (int64_t i = 0; i < n; i++) o[i] = to_f(h[i]);
+  return t;
+}
+HostTensor down_f32(const float* d, int64_t n) {
+  HostTensor t = HostTensor::make_f32({n}, nullptr);
+  CUDA_CHECK(cudaMemcpy(t.data.data(), d, n * sizeof(float), cudaMemcpyDeviceToHost));
+  return t;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  FSO_ASSERT(argc == 3, "usage: ref_bn <in.fsow> <out.fsow>");
+  const TensorMap in = fsow_load(argv[1]);
+  TensorMap out;
+  bn_init();
+  cudaStream_t st;
+  CUDA_CHECK(cudaStreamCreate(&st));
+  for (int ci = 0;; ci++) {
+    const std::string p = "c" + std::to_string(ci) + ".";
+    if (!has(in, p + "meta")) break;
+    const int32_t* m = need(in, p + "meta").i32();
+    const int op = m[0];
+    if (op == 0) {
+      const int N = m[1], H = m[2], W = m[3], C = m[4], act = m[5], has_res = m[6], nd = m[7];
+      const bool accum = m[8] != 0, res_accum = m[9] != 0;
+      const float* f = need(in, p + "f").f32();
+      BnShape s{N, H, W, C};
+      const int64_t M = s.M();
+      act_t* z = up_act(need(in, p + "z"));
+      float* gamma = up_f32(need(in, p + "gamma"));
+      float* beta = up_f32(need(in, p + "beta"));
+      float* rm = up_f32(need(in, p + "run_mean"));
+      float* rv = up_f32(need(in, p + "run_var"));
+      act_t* res = has_res ? up_act(need(in, p + "res")) : nullptr;
+      float *mean = dalloc<float>(C), *istd = dalloc<float>(C), *scale = dalloc<float>(C), *shift = dalloc<float>(C);
+      DestList fl, gl;
+      std::vector<std::vector<int64_t>> dshape;
+      for (int k = 0; k < nd; k++) {
+        const int* d = m + 10 + 5 * k;
+        const HostTensor& d0 = need(in, p + "dest" + std::to_string(k));
+        const HostTensor& g0 = need(in, p + "grad" + std::to_string(k));
+        Dest& a = fl.d[fl.n++];
+        a.p = up_act(d0);
+        a.ctot = d[0]; a.choff = d[1]; a.c0 = d[2]; a.c1 = d[3]; a.up = d[4];
+        Dest& b = gl.d[gl.n++];
+        b = a;
+        b.g = up_act(g0);
+        dshape.push_back(d0.shape);
+      }
+      bn_forward_stats(z, s, gamma, beta, rm, rv, f[0], f[1], mean, istd, scale, shift, st);
+      bn_forward_apply(z, s, scale, shift, res, fl, act != 0, st);
+      float* sums = dalloc<float>(2 * C);
+      act_t* dz = dalloc<act_t>(M * C);
+      float* gwg = up_f32(need(in, p + "gw_gamma0"));
+      float* gwb = up_f32(need(in, p + "gw_beta0"));
+      act_t* rg = nullptr;
+      if (has_res) rg = has(in, p + "res_grad0") ? up_act(need(in, p + "res_grad0")) : dalloc<act_t>(M * C);
+      bn_backward(z, s, gamma, mean, istd, scale, shift, gl, act != 0, sums, dz, gwg, gwb, accum, rg, res_accum, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "mean"] = down_f32(mean, C);
+      out[p + "istd"] = down_f32(istd, C);
+      out[p + "scale"] = down_f32(scale, C);
+      out[p + "shift"] = down_f32(shift, C);
+      out[p + "run_mean"] = down_f32(rm, C);
+      out[p + "run_var"] = down_f32(rv, C);
+      for (int k = 0; k < nd; k++) out[p + "dest" + std::to_string(k)] = down_act(fl.d[k].p, dshape[k]);
+      out[p + "dz"] = down_act(dz, {N, H, W, C});
+      out[p + "gw_gamma"] = down_f32(gwg, C);
+      out[p + "gw_beta"] = down_f32(gwb, C);
+      if (rg) out[p + "res_grad"] = down_act(rg, {N, H, W, C});
+    } else if (op == 1) {
+      const int64_t M = m[1];
+      const int C = m[2];
+      act_t* x = up_act(need(in, p + "x"));
+      float* o = up_f32(need(in, p + "out0"));
+      float* part = dalloc<float>(int64_t(chan_sum_blocks(M, C)) * C);
+      chan_sum(x, M, C, part, o, m[3] != 0, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "out"] = down_f32(o, C);
+    } else if (op == 2) {
+      const int64_t M = m[1];
+      const int C = m[2];
+      act_t* y = up_act(need(in, p + "y"));
+      float* b = up_f32(need(in, p + "bias"));
+      add_bias(y, M, C, b, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "y"] = down_act(y, {M, C});
+    } else if (op == 3) {
+      const int N = m[1], H = m[2], W = m[3], K = m[4];
+      act_t* x = up_act(need(in, p + "x"));
+      act_t* dz = up_act(need(in, p + "dz"));
+      float* tmp = dalloc<float>(int64_t(K) * 27);
+      act_t* dw = dalloc<act_t>(int64_t(K) * 27);
+      CUDA_CHECK(cudaMemset(dw, 0, size_t(K) * 27 * sizeof(act_t)));
+      const bool ran = wgrad_rgb_s2(x, dz, N, H, W, K, tmp, dw, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "dw"] = down_act(dw, {K, 3, 3, 3});
+      const float r = ran ? 1.f : 0.f;
+      out[p + "ran"] = HostTensor::make_f32({1}, &r);
+    } else {
+      FSO_ASSERT(false, "unknown op %d", op);
+    }
+  }
+  fsow_save(argv[2], out);
+  return 0;
+}

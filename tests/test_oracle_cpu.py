@@ -135,3 +135,69 @@ def test_oracle_forward_shapes_and_fp16_emulation_close_to_fp64():
         for a, b in zip(o16[k], o64[k]):
             scale = b.abs().max().item()
             assert (a.double() - b).abs().max().item() <= 2e-2 * scale + 1e-3
+
+
+# ---------------------------------------------------------------- training BN + SiLU restatement (oracle/bn_ref.py)
+@pytest.mark.parametrize("act,res", [(1, 1), (1, 0), (0, 0)])
+def test_bn_oracle_matches_torch_autograd(act, res):
+    """One conv+BN+SiLU node in training mode, two destinations (a concat slice and a 2× upsample of a channel
+    subset): the restatement's statistics, running-statistics update and backward (dz, dγ, dβ, residual
+    gradient) against torch batch_norm + SiLU autograd in fp64.  Tolerance 1e-4 relative to each tensor's
+    max: the restatement does its elementwise math in fp32 and rounds dz to fp16, as the reference does."""
+    from oracle import bn_ref
+    r = np.random.default_rng(3)
+    N, H, W, C, mom, eps = 2, 6, 5, 16, 0.03, 1e-3
+    f16 = lambda a: np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+    z = f16(1.5 + r.standard_normal((N, H, W, C)))
+    gamma, beta = r.uniform(0.5, 1.5, C).astype(np.float32), r.uniform(-0.5, 0.5, C).astype(np.float32)
+    rm0, rv0 = r.uniform(1, 2, C).astype(np.float32), r.uniform(0.5, 2, C).astype(np.float32)
+    resv = f16(r.uniform(-1, 1, z.shape)) if res else None
+    dests = [(32, 8, 0, 16, 1), (8, 0, 8, 16, 2)]
+    grads = [f16(r.standard_normal((N, H * up, W * up, ct)) * 0.1) for ct, _, _, _, up in dests]
+
+    st = bn_ref.bn_forward_stats(z, gamma, beta, rm0, rv0, mom, eps)
+    bw = bn_ref.bn_backward(z, st["mean"], st["istd"], st["scale"], st["shift"],
+                            [(g, choff, c0, c1, up) for g, (_, choff, c0, c1, up) in zip(grads, dests)], act,
+                            res_grad=np.zeros_like(z) if res else None)
+
+    d = torch.float64
+    zt = torch.tensor(z, dtype=d, requires_grad=True)
+    gt, bt = torch.tensor(gamma, dtype=d, requires_grad=True), torch.tensor(beta, dtype=d, requires_grad=True)
+    rm, rv = torch.tensor(rm0, dtype=d), torch.tensor(rv0, dtype=d)
+    y = torch.nn.functional.batch_norm(zt.permute(0, 3, 1, 2), rm, rv, gt, bt, training=True, momentum=mom,
+                                       eps=eps).permute(0, 2, 3, 1)
+    a = torch.nn.functional.silu(y) if act else y
+    rt = torch.tensor(resv, dtype=d, requires_grad=True) if res else None
+    if res:
+        a = a + rt
+    loss = 0
+    for g, (ct, choff, c0, c1, up) in zip(grads, dests):
+        s = a[..., c0:c1]
+        if up == 2:
+            s = s.repeat_interleave(2, 1).repeat_interleave(2, 2)
+        loss = loss + (s * torch.tensor(g[..., choff:choff + c1 - c0], dtype=d)).sum()
+    loss.backward()
+
+    def close(x, ref, tol=1e-4):
+        ref = np.asarray(ref, np.float64)
+        assert np.abs(np.asarray(x, np.float64) - ref).max() <= tol * (np.abs(ref).max() + 1e-12)
+
+    close(st["mean"], zt.detach().mean((0, 1, 2)).numpy(), 1e-6)
+    close(st["istd"], 1 / np.sqrt(zt.detach().var((0, 1, 2), unbiased=False).numpy() + eps), 1e-6)
+    close(st["run_mean"], rm.numpy(), 1e-6)
+    close(st["run_var"], rv.numpy(), 1e-6)
+    close(bw["dz"], zt.grad.numpy(), 2e-3)  # dz is rounded to fp16
+    close(bw["gw_gamma"], gt.grad.numpy())
+    close(bw["gw_beta"], bt.grad.numpy())
+    if res:
+        close(bw["res_grad"], rt.grad.numpy(), 1e-3)
+
+
+def test_chan_sum_and_add_bias_oracle():
+    from oracle import bn_ref
+    x = np.arange(12, dtype=np.float32).reshape(4, 3)
+    assert np.array_equal(bn_ref.chan_sum(x), np.array([18, 22, 26], np.float32))
+    assert np.array_equal(bn_ref.chan_sum(x, np.ones(3, np.float32), True), np.array([19, 23, 27], np.float32))
+    y = bn_ref.add_bias(np.full((2, 3), 2048, np.float32), np.array([0.5, 1.0, 1.5], np.float32))
+    # fp16 spacing at 2048 is 2: 2048.5 → 2048, 2049 ties to even → 2048, 2049.5 → 2050
+    assert np.array_equal(y, np.array([[2048, 2048, 2050]] * 2, np.float32))
