@@ -102,8 +102,9 @@ int osam_conv_dgrad(const osam_conv_plan* plan, const void* dz, const void* w, v
 /* dw = wgrad(x, dz) (+ beta·dw): the weight gradient of the plan's forward conv, x N×H×W×C and
  * dz N×P×Q×K → dw K×R×S×C fp16 (KRSC, like the reference's gw_act).  Replaces ConvOp::wgrad (src/conv.h:31,
  * src/conv.cpp:357-366).  Accumulates in fp32 in the workspace (osam_conv_workspace_size, 256-byte
- * aligned), which it zeroes itself.  OSAM_ERR_UNSUPPORTED for transposed plans and for channel counts that
- * are not multiples of 32. */
+ * aligned), which it zeroes itself.  Small-C plans (R·S·C ≤ 32, the RGB stem) take K = 32 or 64 and replace
+ * the reference's wgrad_rgb_s2 (src/misc.cu:193-273, src/model.cpp:421-422) for any size and stride.
+ * OSAM_ERR_UNSUPPORTED for transposed plans and for other channel counts that are not multiples of 32. */
 int osam_conv_wgrad(const osam_conv_plan* plan, const void* x, const void* dz, void* dw, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream);
 

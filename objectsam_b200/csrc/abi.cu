@@ -659,6 +659,57 @@ static size_t wgrad_workspace_bytes(const osam_conv_plan* p) {
   return ((size_t)g.K * g.R * g.S * g.C * 4 + 255) & ~size_t(255);
 }
 
+static int sm_count() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// Weight gradient of a small-C plan (R·S·C ≤ 32, the RGB stem): patch-gather tcgen05 kernel over runs of
+// 128 consecutive output pixels (conv_wgrad.cu), one CTA pair per SM.
+static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float beta, void* ws,
+                      size_t ws_bytes, osam_stream_t stream) {
+  const osam_conv_geom& g = p->g;
+  if (g.K != 32 && g.K != 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C wgrad: K must be 32 or 64 (K=%d)", g.K);
+  const size_t need = wgrad_workspace_bytes(p);
+  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need);
+  if ((reinterpret_cast<uintptr_t>(dz) & 15) || (reinterpret_cast<uintptr_t>(x) & 1))
+    return fail(OSAM_ERR_INVALID, "wgrad: dz must be 16-byte aligned, x 2-byte aligned");
+  if (p->M >= (1LL << 31) - 128) return fail(OSAM_ERR_UNSUPPORTED, "small-C wgrad: too many output pixels");
+  WgradLaunch L{};
+  ConvDev& d = L.d;
+  d.N = g.N; d.H = g.H; d.W = g.W; d.C = g.C; d.K = g.K;
+  d.P = p->P; d.Q = p->Q; d.R = g.R; d.S = g.S; d.stride = g.stride; d.pad = g.pad;
+  d.M = p->M;
+  d.err = device_error_word();
+  if (!d.err) return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
+  L.mode = A_STEM;
+  L.xp = static_cast<const __half*>(x);
+  L.acc = static_cast<float*>(ws);
+  L.dw = static_cast<__half*>(dw);
+  L.n_out = (long long)g.K * g.R * g.S * g.C;
+  L.beta = beta;
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)p->M};
+    const uint64_t str[1] = {(uint64_t)g.K * 2};
+    const uint32_t box[2] = {(uint32_t)g.K, 128};
+    const int rc = make_map(&L.tdz, dz, 2, dims, str, box, g.K * 2);
+    if (rc) return rc;
+  }
+  const long long tiles = (p->M + 127) / 128;
+  const long long ctas = std::min<long long>(tiles, 2LL * sm_count());
+  L.tiles_per_split = (int)((tiles + ctas - 1) / ctas);
+  L.grid = (int)((tiles + L.tiles_per_split - 1) / L.tiles_per_split);
+  cudaError_t e = launch_conv_wgrad(L, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_wgrad (small-C) launch");
+}
+
 size_t osam_conv_workspace_size(const osam_conv_plan* p) {
   if (!p) return 0;
   if (p->transposed) return ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
@@ -669,6 +720,7 @@ int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void
                     size_t ws_bytes, osam_stream_t stream) {
   if (!p || !x || !dz || !dw) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
+  if (!p->transposed && p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, beta, ws, ws_bytes, stream);
   if (p->transposed || (p->mode != A_S1 && p->mode != A_S2) || g.C % 32 || g.K % 32)
     return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed, small-C or non-32-multiple channels");
   const size_t need = wgrad_workspace_bytes(p);

@@ -97,7 +97,8 @@ struct WgradLaunch {
   long long n_out;      // K·R·S·C
   float beta;
   int AB, BB, BN;       // dz / x box channels (32 or 64), GEMM N block
-  int mode;             // A_S1 or A_S2
+  int mode;             // A_S1, A_S2, or A_STEM (R·S·C ≤ 32: patch gather, dz as one 2-D map)
+  const __half* xp;     // A_STEM: the input itself (gathered by the producer warps, no tensor map)
   int grid, nsplit, tiles_per_split;
 };
 cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st);

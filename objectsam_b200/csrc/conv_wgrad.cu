@@ -176,6 +176,172 @@ __global__ void __launch_bounds__(WgCfg<AB, BB, BN>::THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------------
+// Small-C input conv (R·S·C ≤ 32: the RGB stem, 3×3×3).  Replaces the reference's wgrad_rgb_s2
+// (src/misc.cu:193-273, a WMMA kernel because cuDNN cannot use tensor cores at C = 3).
+//   D[j][k] = Σ_pixels patch[pixel][j] · dz[pixel][k],   j = (r·S + s)·C + c,   dW[k][r][s][c] = D[j][k]
+// A = the im2col patch tile (M = patch column j, reduction = 128 output pixels), written by the producer
+// warps straight into the MN-major 64-byte-swizzled layout (a row of 32 patch columns per pixel); B = the
+// dz tile, 128 consecutive output pixels × K channels, one contiguous TMA box (MN-major: channels
+// contiguous).  M = 128 of which only the R·S·C ≤ 32 rows the patch fills are read back: the descriptor's
+// other three 32-row blocks point into the following shared memory and their products are discarded.
+// Warps 0–7: two groups of patch producers taking alternate tiles (one output pixel per thread); warp 8:
+// dz TMA; warp 9: TMEM owner + MMA issuer.  Warp 0 reads the 32×K fp32 block out and adds it into the
+// zeroed workspace.  HBM traffic: dz once, x ≈ (st·(Q−1)+S)/(st·Q)·(R/st) times (L1/L2 serve the overlap).
+template <int K>
+struct StemWgCfg {
+  static constexpr int A_BYTES = 128 * 64;     // 128 pixels × 32 patch columns (fp16)
+  static constexpr int B_BYTES = 128 * K * 2;  // 128 pixels × K dz channels
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 4;
+  static constexpr int SLACK = 3 * A_BYTES;    // the three discarded M blocks of the last stage's A
+  static constexpr int THREADS = 320;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + SLACK + 256;
+  static_assert(STAGES % 2 == 0, "the two producer groups own alternate stages");
+};
+
+template <int K>
+__global__ void __launch_bounds__(StemWgCfg<K>::THREADS, 1)
+    k_conv_wgrad_stem(const __grid_constant__ CUtensorMap tdz, const __half* __restrict__ x, const ConvDev d,
+                      float* __restrict__ acc, int tiles_per_cta) {
+  using Cfg = StemWgCfg<K>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_joff[32], s_jr[32], s_js[32];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + STAGES * Cfg::STAGE + Cfg::SLACK);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int RSC = d.R * d.S * d.C;
+  const long long tiles = (d.M + 127) / 128;
+  const long long t0 = (long long)blockIdx.x * tiles_per_cta;
+  const long long t1 = t0 + tiles_per_cta < tiles ? t0 + tiles_per_cta : tiles;
+  const int n_it = t1 > t0 ? int(t1 - t0) : 0;
+
+  if (threadIdx.x < 32) {
+    const int j = threadIdx.x;
+    if (j < RSC) {
+      const int rr = j / (d.S * d.C), ss = (j / d.C) % d.S, cc = j % d.C;
+      s_joff[j] = (rr * d.W + ss) * d.C + cc;
+      s_jr[j] = rr;
+      s_js[j] = ss;
+    } else {
+      s_joff[j] = 0;
+      s_jr[j] = -1;  // zero column
+      s_js[j] = 0;
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full + s, 128 + 1);  // the producer group's 128 threads + the dz TMA's expect_tx arrival
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tdz);
+  }
+  if (warp == 9) {
+    tmem_alloc(tslot, K);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp < 8) {
+    // ---------------------------------------------------------------- patch producers
+    const int grp = warp >> 2, row = threadIdx.x & 127;
+    const int PQ = d.P * d.Q;
+    for (int it = grp; it < n_it; it += 2) {
+      const int s = it % STAGES;
+      if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) break;
+      const long long pix = (t0 + it) * 128 + row;
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) pk[i] = 0u;
+      if (pix < d.M) {
+        const int n = int(pix / PQ), rem = int(pix - (long long)n * PQ), p = rem / d.Q, q = rem - p * d.Q;
+        const int y0 = p * d.stride - d.pad, x0 = q * d.stride - d.pad;
+        const long long b0 = ((long long)(n * d.H + y0) * d.W + x0) * d.C;  // index of patch (0, 0, 0); may be < 0
+        const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int jr = s_jr[j], js = s_js[j];
+          unsigned v = 0u;
+          if (jr >= 0 && (unsigned)(y0 + jr) < (unsigned)d.H && (unsigned)(x0 + js) < (unsigned)d.W)
+            v = __ldg(xs + b0 + s_joff[j]);
+          pk[j >> 1] |= v << ((j & 1) * 16);
+        }
+      }
+      uint8_t* a = base + s * Cfg::STAGE + row * 64;
+      const int sw = (row >> 1) & 3;
+#pragma unroll
+      for (int c = 0; c < 4; c++)
+        *reinterpret_cast<uint4*>(a + ((c ^ sw) << 4)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async_smem();
+      mbar_arrive(full + s);
+    }
+    if (warp == 0) {
+      // ---------------------------------------------------------------- read-out: lane j = patch column j
+      const bool ok = n_it > 0 && mbar_wait(accf, 0, d.err);
+      tc_fence_after();
+      if (ok) {
+#pragma unroll 1
+        for (int k0 = 0; k0 < K; k0 += 16) {
+          __syncwarp();
+          float v[16];
+          tmem_ld16(tmem + k0, v);
+          if (lane < RSC) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) atomicAdd(acc + (long long)(k0 + i) * RSC + lane, v[i]);
+          }
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ---------------------------------------------------------------- dz TMA
+    if (lane == 0) {
+      for (int it = 0; it < n_it; it++) {
+        const int s = it % STAGES;
+        if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) break;
+        mbar_arrive_expect_tx(full + s, Cfg::B_BYTES);
+        tma_load_2d(base + s * Cfg::STAGE + Cfg::A_BYTES, &tdz, full + s, 0, int((t0 + it) * 128));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32_mn(128, K);
+      bool ok = true;
+      for (int it = 0; it < n_it; it++) {
+        const int s = it % STAGES;
+        if (!mbar_wait(full + s, (it / STAGES) & 1, d.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(base + s * Cfg::STAGE), b = a + Cfg::A_BYTES;
+#pragma unroll
+        for (int k = 0; k < 8; k++)  // 16 pixels per MMA
+          umma_f16(tmem, smem_desc_mnmajor(a + k * 16 * 64, 64, Cfg::A_BYTES),
+                   smem_desc_mnmajor(b + k * 16 * K * 2, K * 2, Cfg::B_BYTES), idesc, (it | k) != 0);
+        umma_commit(empty + s);
+      }
+      if (ok && n_it > 0) umma_commit(accf);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, K);
+  }
+}
+
 // dw (fp16) = acc (fp32) + beta · dw
 __global__ void k_wgrad_finish(const float* __restrict__ acc, __half* __restrict__ dw, long long n, float beta) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -207,11 +373,29 @@ static cudaError_t wgrad_launch_mode(const WgradLaunch& L, cudaStream_t st) {
   return cudaErrorInvalidValue;
 }
 
+template <int K>
+static cudaError_t wgrad_stem_launch(const WgradLaunch& L, cudaStream_t st) {
+  using Cfg = StemWgCfg<K>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv_wgrad_stem<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  k_conv_wgrad_stem<K><<<L.grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.tdz, L.xp, L.d, L.acc, L.tiles_per_split);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(L.acc, 0, (size_t)L.n_out * 4, st);
   if (e != cudaSuccess) return e;
   const int AB = L.AB, BB = L.BB, BN = L.BN;
-  if (AB == 64 && BB == 64) {
+  if (L.mode == A_STEM) {
+    if (L.d.K == 32) e = wgrad_stem_launch<32>(L, st);
+    else if (L.d.K == 64) e = wgrad_stem_launch<64>(L, st);
+    else return cudaErrorInvalidValue;
+  } else if (AB == 64 && BB == 64) {
     switch (BN) {
       case 64: e = wgrad_launch_mode<64, 64, 64>(L, st); break;
       case 128: e = wgrad_launch_mode<64, 64, 128>(L, st); break;

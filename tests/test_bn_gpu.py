@@ -301,3 +301,26 @@ def test_chan_sum_and_add_bias_match_reference_kernels(cuda_lib):
             y = t16(ins[f"c{i}.y"])
             bn.add_bias(y, t32(ins[f"c{i}.bias"]))
             assert np.array_equal(y.float().cpu().numpy(), ref[f"c{i}.y"].reshape(M, C))
+
+
+@pytest.mark.skipif(not os.path.exists(REF_BN), reason="oracle/_ref/ref_bn not built (make -C oracle)")
+def test_stem_wgrad_matches_reference_kernel(cuda_lib):
+    """The stem's weight gradient (3×3/s2/p1, C = 3 → K = 32) against the reference's own WMMA kernel
+    wgrad_rgb_s2 (src/misc.cu:193-273) on identical inputs; both accumulate in fp32 and round to fp16."""
+    from objectsam_b200.conv import ConvGeom, ConvOp
+    N, H, W, K = 2, 256, 384, 32
+    r = np.random.default_rng(21)
+    x = fp16(r.uniform(0, 1, (N, H, W, 3)))
+    dz = fp16(r.uniform(-1, 1, (N, H // 2, W // 2, K)))
+    ins = {"c0.meta": np.array([3, N, H, W, K], np.int32), "c0.x": x, "c0.dz": dz}
+    with tempfile.TemporaryDirectory() as td:
+        fsow.save(os.path.join(td, "in.fsow"), ins)
+        subprocess.run([REF_BN, os.path.join(td, "in.fsow"), os.path.join(td, "out.fsow")], check=True, timeout=300)
+        ref = fsow.load(os.path.join(td, "out.fsow"))
+    assert ref["c0.ran"][0] == 1.0, "the reference declined the shape"
+    op = ConvOp().init(ConvGeom(N, H, W, 3, K, 3, 3, 2, 1))
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    dw = torch.empty(K, 3, 3, 3, dtype=torch.half, device=DEV)
+    op.wgrad(t16(x), t16(dz), dw, ws=ws)
+    torch.cuda.synchronize()
+    close_f16(dw.float().cpu().numpy(), ref["c0.dw"], "stem dw", rel=2e-3)

@@ -360,6 +360,28 @@ def test_conv_wgrad_matches_torch(cuda_lib, shape):
     assert_close(dw, ref_wgrad(x, dz, (K, R, R, C), s, R // 2))
 
 
+# small-C input convs (R·S·C ≤ 32): the RGB stem and odd sizes, both strides, K = 32 and 64
+STEM_WGRAD_SHAPES = [(2, 64, 64, 3, 32, 2), (1, 640, 640, 3, 32, 2), (3, 30, 46, 3, 64, 2), (2, 33, 17, 3, 32, 1),
+                     (1, 9, 7, 2, 32, 2)]
+
+
+@pytest.mark.parametrize("shape", STEM_WGRAD_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_conv_wgrad_small_c_matches_torch(cuda_lib, shape, beta):
+    N, H, W, C, K, s = shape
+    x, _ = rand_conv(N, H, W, C, K, 3, seed=sum(shape) + 9)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, s, 1))
+    P, Q = op.geom().P(), op.geom().Q()
+    g = torch.Generator(device="cpu").manual_seed(13)
+    dz = (torch.rand(N, P, Q, K, generator=g) * 2 - 1).half().to(DEV)
+    dw0 = (torch.rand(K, 3, 3, C, generator=g) - 0.5).half().to(DEV)
+    dw = dw0.clone()
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    op.wgrad(x, dz, dw, ws=ws, beta=beta)
+    torch.cuda.synchronize()
+    assert_close(dw, ref_wgrad(x, dz, (K, 3, 3, C), s, 1) + beta * dw0.float())
+
+
 def test_conv_wgrad_beta_accumulates(cuda_lib):
     N, H, W, C, K = 2, 24, 24, 64, 128
     x, w = rand_conv(N, H, W, C, K, 3, seed=19)
