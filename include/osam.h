@@ -183,6 +183,28 @@ int osam_chan_sum(const void* x, int64_t M, int C, float* out, int accum, void* 
 int osam_add_bias(void* y, int64_t M, int C, const float* bias, osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Training mask loss of the segment head (the mask part of SegLoss::run, src/loss.cuh:53-64,
+ * src/loss.cu:393-543, :613-619).  Inputs follow the reference's MaskArgs (src/loss.cu:393-408):
+ *   coef[l]    NHWC fp16 [batch][h_l][w_l][32] coefficient heads, level_hw = {h0, w0, h1, w1, h2, w2}
+ *              (anchors A = Σ h_l·w_l, level-major, row-major);
+ *   proto      NHWC fp16 [batch][proto_h][proto_w][32] (proto_w % 16 == 0, proto_h % 8 == 0);
+ *   npos[b], pos[b][A] (positive anchor ids of image b, first npos[b] entries), agt[b][A] (assigned gt of each
+ *   anchor), gt_box [batch][max_gt][4] xyxy input pixels, gt_mask [batch][max_gt][proto_h·proto_w/32] bits;
+ *   fg, scale: device floats (positive count of the batch, loss scale).
+ * For every positive i of image b and proto pixel p in its box scaled to the proto grid:
+ *   z = coef_i·proto_p, y = mask bit, loss_sum += bce(z, y)/(Hp·Wp·area_i)   (area normalised to the image)
+ *   g = (σ(z) − y)·box_gain·batch/max(fg,1)·scale/(Hp·Wp·area_i),  dproto_p += g·coef_i,  dcoef_i += g·proto_p.
+ * dproto is written for every pixel (zero outside all boxes); dcoef rows are written for the positive
+ * anchors only (the reference's detection-loss pass zeroes the others); *loss_sum is added to.
+ * Workspace: osam_mask_loss_workspace_size(batch, A) bytes, 256-byte aligned, ZERO-FILLED ONCE before first
+ * use; every call leaves it zeroed again. */
+size_t osam_mask_loss_workspace_size(int batch, int anchors);
+int osam_mask_loss(const void* const* coef, const int* level_hw, const void* proto, int batch, int proto_h, int proto_w,
+                   int imgsz, int max_gt, const int* npos, const int* pos, const int* agt, const float* gt_box,
+                   const uint32_t* gt_mask, const float* fg, const float* scale, float box_gain, void* dproto,
+                   void* const* dcoef, float* loss_sum, void* ws, size_t ws_bytes, osam_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Inference post-process (the reference has it only in numpy: archive/tools/ref_detect.py:37-81).
  * level_hw = {h0, w0, h1, w1, h2, w2} of the three head levels; anchors = Σ h·w, level-major, row-major.
  * ------------------------------------------------------------------------------------------------ */

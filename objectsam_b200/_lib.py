@@ -75,6 +75,10 @@ _SIGS = {
     "osam_chan_sum_workspace_size": (c_size_t, [c_int]),
     "osam_chan_sum": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "osam_add_bias": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "osam_mask_loss_workspace_size": (c_size_t, [c_int, c_int]),
+    "osam_mask_loss": (c_int, [POINTER(c_void_p), POINTER(c_int), c_void_p, c_int, c_int, c_int, c_int, c_int,
+                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float,
+                               c_void_p, POINTER(c_void_p), c_void_p, c_void_p, c_size_t, c_void_p]),
     "osam_decode": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,
                             c_void_p, c_void_p]),
     "osam_nms": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_int, c_int, POINTER(c_void_p),

@@ -1,7 +1,7 @@
-// Test infrastructure: runs the reference's own training-mode BN / bias / stem-wgrad kernels (built from its
-// sources src/bn.cu and src/misc.cu by oracle/Makefile into oracle/_ref/ref_bn) on inputs read from an FSOW
-// file, and writes their outputs to another, so the GPU tests can compare this build's kernels and the CPU
-// restatement (oracle/bn_ref.py) with the reference itself on identical inputs.
+// Test infrastructure: runs the reference's own training-mode BN / bias / stem-wgrad / loss kernels (built from
+// its sources src/bn.cu, src/misc.cu and src/loss.cu by oracle/Makefile into oracle/_ref/ref_bn) on inputs read
+// from an FSOW file, and writes their outputs to another, so the GPU tests can compare this build's kernels and
+// the CPU restatements (oracle/bn_ref.py, oracle/mask_loss_ref.py) with the reference itself on identical inputs.
 //
 //   ref_bn <in.fsow> <out.fsow>
 //
@@ -16,6 +16,9 @@
 //   op 2  add_bias: meta = {2, M, C}; y (M, C), bias (C) → y.
 //   op 3  wgrad_rgb_s2: meta = {3, N, H, W, K}; x (N, H, W, 3), dz (N, P, Q, K) → dw (K, 3, 3, 3) and
 //         ran (1 if the reference took its own kernel, 0 if it declined the shape).
+//   op 5  SegLoss::run (src/loss.cu:590-621): meta = {5, B, imgsz, G}; box<l>, cls<l>, coef<l> heads, proto,
+//         n_gt (int32 [B]), gt_box (B, G, 4), gt_mask (int32 [B, G, Hp·Wp/32]), scale (1) → dproto, dcoef<l>,
+//         items (16), agt (int32 [B, A]).
 // Activations are converted to the reference's act_t (fp16) on upload; every value the tests send is
 // fp16-representable.
 #include <cstdio>
@@ -24,6 +27,7 @@
 
 #include "bn.cuh"
 #include "fsow.h"
+#include "loss.cuh"
 #include "misc.cuh"
 
 namespace {
@@ -55,6 +59,19 @@ HostTensor down_act(const act_t* d, const std::vector<int64_t>& shape) {
   CUDA_CHECK(cudaMemcpy(h.data(), d, n * sizeof(act_t), cudaMemcpyDeviceToHost));
   float* o = reinterpret_cast<float*>(t.data.data());
   for (int64_t i = 0; i < n; i++) o[i] = to_f(h[i]);
+  return t;
+}
+int32_t* up_i32(const HostTensor& t) {
+  int32_t* d = dalloc<int32_t>(t.numel());
+  CUDA_CHECK(cudaMemcpy(d, t.i32(), t.numel() * sizeof(int32_t), cudaMemcpyHostToDevice));
+  return d;
+}
+HostTensor down_i32(const int32_t* d, const std::vector<int64_t>& shape) {
+  HostTensor t;
+  t.shape = shape;
+  t.dtype = 1;
+  t.data.resize(size_t(t.numel()) * 4);
+  CUDA_CHECK(cudaMemcpy(t.data.data(), d, t.data.size(), cudaMemcpyDeviceToHost));
   return t;
 }
 HostTensor down_f32(const float* d, int64_t n) {
@@ -154,6 +171,43 @@ int main(int argc, char** argv) {
       out[p + "dw"] = down_act(dw, {K, 3, 3, 3});
       const float r = ran ? 1.f : 0.f;
       out[p + "ran"] = HostTensor::make_f32({1}, &r);
+    } else if (op == 5) {
+      const int B = m[1], S = m[2], G = m[3];
+      LossCfg c;
+      c.B = B;
+      c.imgsz = S;
+      c.G = G;
+      for (int l = 0; l < 3; l++) c.lvl_h[l] = c.lvl_w[l] = S / c.stride[l];
+      c.Hp = c.Wp = S / 4;
+      SegLoss L;
+      L.init(c);
+      HeadIO io{};
+      std::vector<int64_t> cshape[3];
+      for (int l = 0; l < 3; l++) {
+        const std::string k = std::to_string(l);
+        const int h = c.lvl_h[l], w = c.lvl_w[l];
+        io.box[l] = up_act(need(in, p + "box" + k));
+        io.cls[l] = up_act(need(in, p + "cls" + k));
+        io.coef[l] = up_act(need(in, p + "coef" + k));
+        io.dbox[l] = dalloc<act_t>(int64_t(B) * h * w * 64);
+        io.dcls[l] = dalloc<act_t>(int64_t(B) * h * w);
+        io.dcoef[l] = dalloc<act_t>(int64_t(B) * h * w * 32);
+        cshape[l] = {B, h, w, 32};
+      }
+      io.proto = up_act(need(in, p + "proto"));
+      act_t* dproto = dalloc<act_t>(int64_t(B) * c.Hp * c.Wp * 32);
+      io.dproto = dproto;
+      GtBatch gt;
+      gt.n_gt = up_i32(need(in, p + "n_gt"));
+      gt.box = reinterpret_cast<float4*>(up_f32(need(in, p + "gt_box")));
+      gt.mask = reinterpret_cast<uint32_t*>(up_i32(need(in, p + "gt_mask")));
+      float* scale = up_f32(need(in, p + "scale"));
+      L.run(io, gt, scale, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "dproto"] = down_act(dproto, {B, c.Hp, c.Wp, 32});
+      for (int l = 0; l < 3; l++) out[p + "dcoef" + std::to_string(l)] = down_act(io.dcoef[l], cshape[l]);
+      out[p + "items"] = down_f32(L.items(), 16);
+      out[p + "agt"] = down_i32(L.assigned_gt(), {B, c.A()});
     } else {
       FSO_ASSERT(false, "unknown op %d", op);
     }

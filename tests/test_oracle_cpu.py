@@ -201,3 +201,52 @@ def test_chan_sum_and_add_bias_oracle():
     y = bn_ref.add_bias(np.full((2, 3), 2048, np.float32), np.array([0.5, 1.0, 1.5], np.float32))
     # fp16 spacing at 2048 is 2: 2048.5 → 2048, 2049 ties to even → 2048, 2049.5 → 2050
     assert np.array_equal(y, np.array([[2048, 2048, 2050]] * 2, np.float32))
+
+
+def test_mask_loss_oracle_matches_torch_autograd():
+    """The mask-loss restatement against torch autograd of Σ_pos Σ_crop BCE-with-logits(coef·proto, bit)·inv
+    (fp64): loss, and its gradients ·gk for proto and the positives' coefficients."""
+    from oracle import mask_loss_ref
+    r = np.random.default_rng(5)
+    B, S, G = 1, 128, 3
+    Hp = Wp = S // 4
+    lv = [(S // 8, S // 8), (S // 16, S // 16), (S // 32, S // 32)]
+    A = sum(h * w for h, w in lv)
+    coef = [r.uniform(-1, 1, (B, h, w, 32)).astype(np.float32) for h, w in lv]
+    proto = r.uniform(-1, 1, (B, Hp, Wp, 32)).astype(np.float32)
+    box = np.array([[[10, 12, 90, 70], [40, 40, 127, 120], [3, 50, 30, 126]]], np.float32)
+    bits = (r.random((B, G, Hp * Wp)) < 0.4).astype(np.uint32)
+    words = (bits.reshape(B, G, -1, 32) << np.arange(32, dtype=np.uint32)).sum(-1, dtype=np.uint64).astype(np.uint32)
+    words = words.view(np.int32)
+    sel = np.array([5, 77, 300, A - 1])
+    pos = np.zeros((B, A), np.int32)
+    pos[0, :4] = sel
+    agt = np.full((B, A), -1, np.int32)
+    agt[0, sel] = [0, 1, 2, 1]
+    npos = np.array([4], np.int32)
+    fg, scale, gain = 4.0, 8.0, 7.5
+    dp, dc, loss = mask_loss_ref.mask_loss(coef, proto, npos, pos, agt, box, words, fg, scale, S, gain)
+
+    pt = torch.tensor(proto, dtype=torch.float64, requires_grad=True)
+    cts = [torch.tensor(c, dtype=torch.float64, requires_grad=True) for c in coef]
+    tot = 0
+    for i, a in enumerate(sel):
+        j = agt[0, a]
+        x1, y1, x2, y2 = (box[0, j] / S).astype(np.float64)
+        inv = 1 / (Hp * Wp * (x2 - x1) * (y2 - y1))
+        px = torch.arange(Wp, dtype=torch.float64)
+        py = torch.arange(Hp, dtype=torch.float64)
+        m = ((px[None, :] >= x1 * Wp) & (px[None, :] < x2 * Wp) & (py[:, None] >= y1 * Hp) & (py[:, None] < y2 * Hp))
+        l, h, w = mask_loss_ref.anchor_of(lv, int(a))
+        z = pt[0] @ cts[l][0, h, w]
+        y = torch.tensor(bits[0, j].reshape(Hp, Wp), dtype=torch.float64)
+        bce = torch.nn.functional.binary_cross_entropy_with_logits(z, y, reduction="none")
+        tot = tot + (bce * m).sum() * inv
+    tot.backward()
+    gk = gain * B / fg * scale
+    assert abs(loss - tot.item()) <= 2e-6 * abs(tot.item())  # inv in fp32 in the restatement
+    assert np.abs(dp - pt.grad.numpy() * gk).max() <= 1e-5 * np.abs(dp).max()
+    for a in sel:
+        l, h, w = mask_loss_ref.anchor_of(lv, int(a))
+        want = cts[l].grad[0, h, w].numpy() * gk
+        assert np.abs(dc[(0, int(a))] - want).max() <= 1e-5 * np.abs(want).max()
