@@ -94,8 +94,10 @@ int osam_conv_fwd(const osam_conv_plan* plan, const void* x, const void* w, void
  * beta 0 (overwrite) or 1 (accumulate, the reference's dgrad_accum).  Replaces ConvOp::dgrad (src/conv.h:30,
  * src/conv.cpp:346-355).  Runs on the forward kernels over dz with re-laid-out weights written to the
  * workspace (osam_conv_workspace_size, 256-byte aligned): one conv for stride 1, one per output-parity
- * class for stride 2.  OSAM_ERR_UNSUPPORTED for transposed plans, non-square kernels, or output channels
- * that the forward kernels cannot take as inputs (not a multiple of 32). */
+ * class for stride 2.  Transposed plans (kernel = stride = 2, src/conv.cpp:351-353): dx is the stride-2 2×2
+ * conv of dy with the transposed conv's own (C_in, R, S, C_out) weights read as KRSC; no workspace.
+ * OSAM_ERR_UNSUPPORTED for non-square kernels or output channels that the forward kernels cannot take as
+ * inputs (not a multiple of 32). */
 int osam_conv_dgrad(const osam_conv_plan* plan, const void* dz, const void* w, void* dx, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream);
 
@@ -104,7 +106,9 @@ int osam_conv_dgrad(const osam_conv_plan* plan, const void* dz, const void* w, v
  * src/conv.cpp:357-366).  Accumulates in fp32 in the workspace (osam_conv_workspace_size, 256-byte
  * aligned), which it zeroes itself.  Small-C plans (R·S·C ≤ 32, the RGB stem) take K = 32 or 64 and replace
  * the reference's wgrad_rgb_s2 (src/misc.cu:193-273, src/model.cpp:421-422) for any size and stride.
- * OSAM_ERR_UNSUPPORTED for transposed plans and for other channel counts that are not multiples of 32. */
+ * Transposed plans (src/conv.cpp:362-364): dw[c][r][s][k] = Σ x[p][q][c]·dy[2p+r][2q+s][k] in the
+ * (C_in, R, S, C_out) layout, run as the weight gradient of that stride-2 conv.
+ * OSAM_ERR_UNSUPPORTED for other channel counts that are not multiples of 32. */
 int osam_conv_wgrad(const osam_conv_plan* plan, const void* x, const void* dz, void* dw, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream);
 
@@ -133,6 +137,14 @@ int osam_convt_fwd_static_scratch(const osam_conv_plan* plan, const void* x, con
 /* SPPF pooling: with cv1's output in channels [0,c) of cat (N×H×W×4c), writes the three chained
  * 5×5/s1/p2 max-pools into slices 1..3.  Replaces sppf_pool_fwd (src/misc.cuh:6, src/misc.cu:149-153). */
 int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);
+
+/* SPPF backward: with the forward's cat (N×H×W×4c, slices 0..3) and the gradients of all four slices in
+ * dcat, routes slice 3's gradient back through the three chained pools (each output position to the first
+ * maximum of its clipped 5×5 window, row-major, as PyTorch) and ADDS the result to dcat slice 0; slices 1–3
+ * of dcat are left as they are.  Needs no workspace (the reference's two fp32 scratch buffers stay on chip).
+ * Replaces sppf_pool_bwd (src/misc.cuh:9-10, src/misc.cu:48-73, :155-166).  c % 8 == 0;
+ * OSAM_ERR_UNSUPPORTED when H·W > 1937 (the per-CTA shared memory). */
+int osam_sppf_bwd(const void* cat, void* dcat, int N, int H, int W, int c, osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Training-mode BatchNorm + SiLU and the head-conv bias passes (the reference's src/bn.cuh:23-47 and

@@ -61,6 +61,7 @@ _SIGS = {
     "osam_conv_wgrad": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_void_p]),
     "osam_convt_fwd_static_scratch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
     "osam_sppf_fwd": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "osam_sppf_bwd": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "osam_bn_workspace_size": (c_size_t, [c_int]),
     "osam_bn_eval_scale": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                                    c_void_p]),

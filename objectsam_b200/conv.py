@@ -15,7 +15,7 @@ from typing import Optional, Sequence
 from . import _lib
 from ._lib import ConvGeom, Dest, Epilogue, check, lib, stream_ptr
 
-__all__ = ["ConvGeom", "ConvOp", "DestSpec", "sppf_pool_fwd", "EPI_STORE", "EPI_BN_ACT", "EPI_BIAS"]
+__all__ = ["ConvGeom", "ConvOp", "DestSpec", "sppf_pool_fwd", "sppf_pool_bwd", "EPI_STORE", "EPI_BN_ACT", "EPI_BIAS"]
 EPI_STORE, EPI_BN_ACT, EPI_BIAS = _lib.EPI_STORE, _lib.EPI_BN_ACT, _lib.EPI_BIAS
 
 
@@ -117,3 +117,9 @@ def make_epilogue(K: int, dests: Sequence[DestSpec], kind: int, scale=None, shif
 def sppf_pool_fwd(cat, N: int, H: int, W: int, c: int, stream=None) -> None:
     """Reference sppf_pool_fwd (src/misc.cuh:6): slices 1..3 of `cat` ← chained 5×5 max-pools of slice 0."""
     check(lib().osam_sppf_fwd(_ptr(cat), N, H, W, c, stream_ptr(stream)))
+
+
+def sppf_pool_bwd(cat, dcat, N: int, H: int, W: int, c: int, stream=None) -> None:
+    """Reference sppf_pool_bwd (src/misc.cuh:9): dcat slice 0 += the gradients of slices 1..3 routed back through
+    the chained pools (first maximum of each window).  The reference's fp32 scratch buffers are not needed."""
+    check(lib().osam_sppf_bwd(_ptr(cat), _ptr(dcat), N, H, W, c, stream_ptr(stream)))

@@ -183,7 +183,24 @@ static void plan_set_output(osam_conv_plan* p, int P, int Q) {
 static void plan_dgrad(osam_conv_plan* p) {
   const osam_conv_geom& g = p->g;
   p->n_dg = 0;
-  if (p->transposed || g.R != g.S) return;
+  p->dg_direct = 0;
+  if (p->transposed) {
+    if (g.R != g.stride || g.S != g.stride || g.stride != 2) return;
+    osam_conv_geom sg{g.N, 2 * g.H, 2 * g.W, g.K, g.C, 2, 2, 2, 0};
+    osam_conv_plan* s = new (std::nothrow) osam_conv_plan;
+    if (!s) return;
+    if (plan_init(&sg, 0, s) != OSAM_OK || s->mode != A_S2 || s->P != g.H || s->Q != g.W) {
+      delete s;
+      return;
+    }
+    p->dg[0] = s;
+    p->dg_R[0] = p->dg_S[0] = 2;
+    p->dg_woff[0] = 0;
+    p->dg_direct = 1;
+    p->n_dg = 1;
+    return;
+  }
+  if (g.R != g.S) return;
   auto make = [&](int i, int R2, int S2, int pad2, int P, int Q, int par) -> bool {
     osam_conv_geom sg{g.N, p->P, p->Q, g.K, g.C, R2, S2, 1, pad2};
     osam_conv_plan* s = new (std::nothrow) osam_conv_plan;
@@ -622,6 +639,7 @@ int osam_conv_plan_destroy(osam_conv_plan* p) {
 }
 
 static size_t dgrad_workspace_bytes(const osam_conv_plan* p) {
+  if (p->dg_direct) return 0;
   size_t b = 0;
   for (int i = 0; i < p->n_dg; i++)
     b = (size_t)p->dg_woff[i] * 2 + (((size_t)p->g.C * p->dg_R[i] * p->dg_S[i] * p->g.K * 2 + 255) & ~size_t(255));
@@ -633,9 +651,16 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
   if (!p || !dz || !w || !dx) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   if (p->n_dg == 0) return fail(OSAM_ERR_UNSUPPORTED, "dgrad: geometry not supported (stride, kernel or channels)");
   const size_t need = dgrad_workspace_bytes(p);
-  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255))
+  if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)))
     return fail(OSAM_ERR_INVALID, "dgrad needs %zu workspace bytes (256-byte aligned)", need);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->dg_direct) {  // transposed conv: a stride-2 2×2 forward conv over dy with the same weight array
+    ConvLaunch L;
+    int rc = conv_prepare(p->dg[0], dz, w, nullptr, beta, dx, nullptr, 0, &L);
+    if (rc) return rc;
+    cudaError_t e = conv_launch(L, st);
+    return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_dgrad (transposed) launch");
+  }
   const osam_conv_geom& g = p->g;
   __half* wsub = static_cast<__half*>(ws);
   for (int i = 0; i < p->n_dg; i++) {
@@ -712,7 +737,10 @@ static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, vo
 
 size_t osam_conv_workspace_size(const osam_conv_plan* p) {
   if (!p) return 0;
-  if (p->transposed) return ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
+  if (p->transposed) {
+    const size_t relayout = ((size_t)p->g.C * 4 * p->g.K * 2 + 255) & ~size_t(255);
+    return p->dg_direct ? std::max(relayout, wgrad_workspace_bytes(p->dg[0])) : relayout;
+  }
   return std::max(dgrad_workspace_bytes(p), wgrad_workspace_bytes(p));
 }
 
@@ -720,7 +748,13 @@ int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void
                     size_t ws_bytes, osam_stream_t stream) {
   if (!p || !x || !dz || !dw) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
-  if (!p->transposed && p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, beta, ws, ws_bytes, stream);
+  if (p->transposed) {
+    // dW[c][r][s][k] = Σ_{p,q} x[p][q][c]·dy[2p+r][2q+s][k]: the weight gradient of the stride-2 2×2 conv
+    // dg[0] (input dy, output x-shaped) with x in the role of its output gradient
+    if (!p->dg_direct) return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed conv other than kernel = stride = 2");
+    return osam_conv_wgrad(p->dg[0], dz, x, dw, beta, ws, ws_bytes, stream);
+  }
+  if (p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, beta, ws, ws_bytes, stream);
   if (p->transposed || (p->mode != A_S1 && p->mode != A_S2) || g.C % 32 || g.K % 32)
     return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed, small-C or non-32-multiple channels");
   const size_t need = wgrad_workspace_bytes(p);
@@ -816,6 +850,16 @@ int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream) {
   if ((size_t)2 * H * W * 32 * 2 > 200 * 1024) return fail(OSAM_ERR_UNSUPPORTED, "sppf map too large (%dx%d)", H, W);
   cudaError_t e = launch_sppf(static_cast<__half*>(cat), N, H, W, c, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_sppf_fwd launch");
+}
+
+int osam_sppf_bwd(const void* cat, void* dcat, int N, int H, int W, int c, osam_stream_t stream) {
+  if (!cat || !dcat || N < 1 || H < 1 || W < 1 || c < 8 || c % 8) return fail(OSAM_ERR_INVALID, "sppf_bwd arguments");
+  if ((reinterpret_cast<uintptr_t>(cat) | reinterpret_cast<uintptr_t>(dcat)) & 15)
+    return fail(OSAM_ERR_INVALID, "sppf_bwd buffers not 16-byte aligned");
+  if (sppf_bwd_smem_bytes(H, W) > 227 * 1024) return fail(OSAM_ERR_UNSUPPORTED, "sppf_bwd map too large (%dx%d)", H, W);
+  cudaError_t e = launch_sppf_bwd(static_cast<const __half*>(cat), static_cast<__half*>(dcat), N, H, W, c,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_sppf_bwd launch");
 }
 
 int osam_device_error(void) {

@@ -127,7 +127,7 @@ struct RedArgs {
 //   RED_BWD:   Σg, Σg·x̂ with g = dA·silu'(y), y = scale·z + shift, x̂ = (z − mean)·istd
 //   RED_SUM:   Σz
 template <int MODE, int U>
-__global__ void __launch_bounds__(kBnT) k_bn_reduce(const RedArgs P) {
+__global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(const RedArgs P) {
   extern __shared__ float2 bn_red[];  // [rowlanes][C]
   __shared__ unsigned s_last;
   const int C = P.C, V = C >> 3, RL = P.rowlanes;
@@ -139,20 +139,25 @@ __global__ void __launch_bounds__(kBnT) k_bn_reduce(const RedArgs P) {
 #pragma unroll
   for (int i = 0; i < 8; i++) a[i] = b[i] = 0.f;
   if (active) {
+    // RED_STATS: k0 = K.  RED_BWD: k0 = scale, k1 = shift, k2 = istd, k3 = −mean·istd (x̂ = z·k2 + k3).
     float k0[8], k1[8], k2[8], k3[8];
     if (MODE == RED_STATS) ld8f_any(P.run_mean + c, k0);
     if (MODE == RED_BWD) {
+      float mu[8];
       ld8f_any(P.scale + c, k0);
       ld8f_any(P.shift + c, k1);
-      ld8f_any(P.mean + c, k2);
-      ld8f_any(P.istd + c, k3);
+      ld8f_any(P.istd + c, k2);
+      ld8f_any(P.mean + c, mu);
+#pragma unroll
+      for (int i = 0; i < 8; i++) k3[i] = -mu[i] * k2[i];
     }
     for (long long r = r0 + rl; r < r1; r += (long long)U * RL) {
-      float v[U][8], dA[U][8];
+      uint4 zr[U];
+      float dA[U][8];
 #pragma unroll
       for (int u = 0; u < U; u++) {
         const long long rr = r + (long long)u * RL;
-        if (rr < r1) ld8h(P.z + rr * C + c, v[u]);
+        if (rr < r1) zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
       }
       if (MODE == RED_BWD) {
 #pragma unroll
@@ -164,22 +169,24 @@ __global__ void __launch_bounds__(kBnT) k_bn_reduce(const RedArgs P) {
 #pragma unroll
       for (int u = 0; u < U; u++) {
         if (r + (long long)u * RL >= r1) break;
+        float v[8];
+        unpack8h(zr[u], v);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           if (MODE == RED_STATS) {
-            const float d = v[u][i] - k0[i];
+            const float d = v[i] - k0[i];
             a[i] += d;
             b[i] = fmaf(d, d, b[i]);
           } else if (MODE == RED_BWD) {
             float g = dA[u][i];
             if (P.act) {
-              const float y = fmaf(k0[i], v[u][i], k1[i]), s = sigmoid_fast(y);
+              const float y = fmaf(k0[i], v[i], k1[i]), s = sigmoid_fast(y);
               g *= s * fmaf(y, 1.f - s, 1.f);
             }
             a[i] += g;
-            b[i] = fmaf(g, (v[u][i] - k2[i]) * k3[i], b[i]);
+            b[i] = fmaf(g, fmaf(v[i], k2[i], k3[i]), b[i]);
           } else {
-            a[i] += v[u][i];
+            a[i] += v[i];
           }
         }
       }
@@ -260,7 +267,7 @@ struct ApplyArgs {
 
 // a = act(scale·z + shift) (+ res) → every destination (reference k_apply, src/bn.cu:204-238).
 template <int U>
-__global__ void __launch_bounds__(kBnT) k_bn_apply(const ApplyArgs P) {
+__global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
   const int C = P.C, V = C >> 3, RL = P.rowlanes;
   const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
   if (rl >= RL) return;
@@ -270,27 +277,29 @@ __global__ void __launch_bounds__(kBnT) k_bn_apply(const ApplyArgs P) {
   ld8f_any(P.scale + c, sc);
   ld8f_any(P.shift + c, sh);
   for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
-    float v[U][8], rv[U][8];
+    uint4 zr[U], rr4[U];
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const long long rr = r - (long long)u * RL;
       if (rr >= r0) {
-        ld8h(P.z + rr * C + c, v[u]);
-        if (P.res) ld8h(P.res + rr * C + c, rv[u]);
+        zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
+        if (P.res) rr4[u] = *reinterpret_cast<const uint4*>(P.res + rr * C + c);
       }
     }
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const long long rr = r - (long long)u * RL;
       if (rr < r0) break;
-      float o[8];
+      float o[8], rv[8];
+      unpack8h(zr[u], o);
+      if (P.res) unpack8h(rr4[u], rv);
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        const float y = fmaf(sc[i], v[u][i], sh[i]);
+        const float y = fmaf(sc[i], o[i], sh[i]);
         o[i] = P.act ? y * sigmoid_fast(y) : y;
-        if (P.res) o[i] += rv[u][i];
+        if (P.res) o[i] += rv[i];
       }
-#pragma unroll
+#pragma unroll 1
       for (int k = 0; k < OSAM_MAX_DEST; k++) {
         if (k >= P.ndest) break;
         const DestDev& d = P.dest[k];
@@ -335,20 +344,30 @@ __global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
   if (rl >= RL) return;
   const long long r0 = (long long)blockIdx.x * P.rows;
   const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
-  float sc[8], sh[8], mu[8], is[8], m1[8], m2[8];
-  ld8f_any(P.scale + c, sc);
-  ld8f_any(P.shift + c, sh);
-  ld8f_any(P.mean + c, mu);
-  ld8f_any(P.istd + c, is);
-  ld8f(P.sums + c, m1);
-  ld8f(P.sums + C + c, m2);
+  // dz = scale·g + ka·z + kb with ka = −scale·istd·m2, kb = scale·(istd·m2·mean − m1)
+  float sc[8], sh[8], ka[8], kb[8];
+  {
+    float mu[8], is[8], m1[8], m2[8];
+    ld8f_any(P.scale + c, sc);
+    ld8f_any(P.shift + c, sh);
+    ld8f_any(P.mean + c, mu);
+    ld8f_any(P.istd + c, is);
+    ld8f(P.sums + c, m1);
+    ld8f(P.sums + C + c, m2);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      ka[i] = -sc[i] * is[i] * m2[i];
+      kb[i] = sc[i] * (is[i] * m2[i] * mu[i] - m1[i]);
+    }
+  }
   for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
-    float v[U][8], dA[U][8];
+    uint4 zr[U];
+    float dA[U][8];
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const long long rr = r - (long long)u * RL;
       if (rr >= r0) {
-        ld8h(P.z + rr * C + c, v[u]);
+        zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
         gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[u]);
       }
     }
@@ -369,18 +388,18 @@ __global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
         }
         st8h(P.res_grad + off, t);
       }
-      float o[8];
+      float v[8];
+      unpack8h(zr[u], v);
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         float g = dA[u][i];
         if (P.act) {
-          const float y = fmaf(sc[i], v[u][i], sh[i]), s = sigmoid_fast(y);
+          const float y = fmaf(sc[i], v[i], sh[i]), s = sigmoid_fast(y);
           g *= s * fmaf(y, 1.f - s, 1.f);
         }
-        const float xh = (v[u][i] - mu[i]) * is[i];
-        o[i] = sc[i] * (g - m1[i] - xh * m2[i]);
+        v[i] = fmaf(sc[i], g, fmaf(ka[i], v[i], kb[i]));
       }
-      st8h(P.dz + off, o);
+      st8h(P.dz + off, v);
     }
   }
 }
@@ -463,23 +482,34 @@ constexpr int kUStats = 4, kUBwd = 2, kUApply = 4, kUBwdApply = 2;
 int g_sms_cache[64] = {};
 int g_occ_cache[64][2] = {};
 
-// Resident CTAs per SM of the reduction kernel for `mode` (0: statistics / channel sums, 1: backward),
-// times the SM count: the grid that keeps every CTA of a pass resident at once.
+template <class K>
+int occupancy(K kernel, size_t smem) {
+  int occ = 0;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kBnT, smem) == cudaSuccess && occ > 0 ? occ : 1;
+}
+
+// CTAs that are resident at once for a pass pair — mode 0: statistics (or channel sums) and the forward
+// apply; mode 1: the backward sums and the backward apply — so that both kernels of a pair run as one wave
+// over the same row chunks.
 int resident_ctas(int mode) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 4;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 2;
   if (!g_sms_cache[dev]) {
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     g_sms_cache[dev] = sms > 0 ? sms : 148;
   }
   if (!g_occ_cache[dev][mode]) {
-    int occ = 0;
     const size_t smem = size_t(kBnT) * 8 * sizeof(float2);
-    cudaError_t e = mode == 0
-        ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bn_reduce<RED_STATS, kUStats>, kBnT, smem)
-        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bn_reduce<RED_BWD, kUBwd>, kBnT, smem);
-    g_occ_cache[dev][mode] = (e == cudaSuccess && occ > 0) ? occ : 2;
+    int a, b;
+    if (mode == 0) {
+      a = occupancy(k_bn_reduce<RED_STATS, kUStats>, smem);
+      b = occupancy(k_bn_apply<kUApply>, 0);
+    } else {
+      a = occupancy(k_bn_reduce<RED_BWD, kUBwd>, smem);
+      b = occupancy(k_bn_bwd_apply<kUBwdApply>, 0);
+    }
+    g_occ_cache[dev][mode] = a < b ? a : b;
   }
   return g_sms_cache[dev] * g_occ_cache[dev][mode];
 }

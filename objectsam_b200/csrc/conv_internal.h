@@ -121,6 +121,8 @@ cudaError_t launch_conv_win(const ConvLaunch& L, cudaStream_t st, bool prime_onl
 size_t win_fixed_smem_bytes(int C, int K);  // a window-conv CTA's shared memory besides its windows
 cudaError_t launch_convt_weight_relayout(const __half* src, __half* dst, int C, int RS, int K, cudaStream_t st);
 cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st);
+cudaError_t launch_sppf_bwd(const __half* cat, __half* dcat, int N, int H, int W, int c, cudaStream_t st);
+size_t sppf_bwd_smem_bytes(int H, int W);
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
 cudaError_t launch_conv_stem_rgb(const ConvLaunch& L, cudaStream_t st);
 
@@ -142,6 +144,10 @@ struct osam_conv_plan {
   // re-layouts Wsub[c][r'][s'][k] = W[k][rmap[r']][smap[s']][c] packed in the caller's workspace
   osam_conv_plan* dg[4];
   int n_dg, dg_par[4], dg_R[4], dg_S[4], dg_rmap[4][8], dg_smap[4][8];
+  // transposed conv (k = s = 2): dg[0] is the forward conv {N, 2H, 2W, C_out → C_in, 2×2, stride 2} whose
+  // KRSC weights are the transposed conv's own (C_in, R, S, C_out) array: dgrad runs it on dy as is, and
+  // wgrad is that conv's weight gradient with the operands' roles swapped.
+  int dg_direct;
   long long dg_woff[4];
   // window tiling (A_WIN), used when the epilogue allows the coalesced warp stores (decided per call)
   int win, win_wp, win_lw, win_slab, win_wbytes, win_tpi, win_tiles, win_nwb;

@@ -62,6 +62,105 @@ __global__ void __launch_bounds__(256) k_sppf(__half* __restrict__ cat, int H, i
   }
 }
 
+// SPPF backward (reference sppf_pool_bwd, src/misc.cu:48-73, :155-166): with the gradients of all four
+// slices in dcat, route slice 3's gradient through pool(slice 2), add slice 2's own gradient, route that
+// through pool(slice 1), add slice 1's, route through pool(slice 0) and add the result into dcat slice 0.
+// Each output position sends its gradient to the FIRST maximum of its clipped 5×5 window in row-major scan
+// order (strict >, the PyTorch rule).  One CTA per image × 8-channel group keeps slices 0–2, the argmax codes
+// and the fp32 gradients in shared memory; routing is a gather (each input position sums, in row-major order,
+// the gradients of the window positions whose argmax is itself), so the result is deterministic and no
+// fp32 scratch goes through HBM.
+constexpr int kSppfBwdCG = 8;
+
+size_t sppf_bwd_smem_bytes(int H, int W) { return (size_t)H * W * (3 * 16 + 2 * kSppfBwdCG * 4 + kSppfBwdCG); }
+
+__global__ void __launch_bounds__(256) k_sppf_bwd(const __half* __restrict__ cat, __half* __restrict__ dcat, int H,
+                                                  int W, int c) {
+  extern __shared__ uint4 sppfb_smem[];
+  const int HW = H * W;
+  const uint4* S = sppfb_smem;                                   // [3][HW] 8 fp16 values of slices 0..2
+  float* G = reinterpret_cast<float*>(sppfb_smem + 3 * HW);      // [HW][8] gradient of the pool output
+  float* Acc = G + HW * kSppfBwdCG;                              // [HW][8] gradient routed to the pool input
+  uint8_t* arg = reinterpret_cast<uint8_t*>(Acc + HW * kSppfBwdCG);  // [HW][8] argmax code (dy+2)·5 + (dx+2)
+  const int n = blockIdx.y, g0 = blockIdx.x * kSppfBwdCG;
+  const long long ctot = 4LL * c;
+  const __half* img = cat + (long long)n * HW * ctot;
+  __half* dimg = dcat + (long long)n * HW * ctot;
+  uint4* Sw = sppfb_smem;
+  for (int i = threadIdx.x; i < 3 * HW; i += blockDim.x) {
+    const int k = i / HW, px = i - k * HW;
+    Sw[i] = *reinterpret_cast<const uint4*>(img + px * ctot + k * c + g0);
+  }
+  for (int px = threadIdx.x; px < HW; px += blockDim.x) {
+    float v[8];
+    ld8h(dimg + px * ctot + 3 * c + g0, v);
+#pragma unroll
+    for (int k = 0; k < 8; k++) G[px * 8 + k] = v[k];
+  }
+  __syncthreads();
+  for (int L = 2; L >= 0; L--) {
+    const __half* SL = reinterpret_cast<const __half*>(S + L * HW);
+    for (int i = threadIdx.x; i < HW * 8; i += blockDim.x) {
+      const int o = i >> 3, ch = i & 7, h = o / W, w = o - h * W;
+      float best = -INFINITY;
+      int a = 255;
+      const int y0 = h - 2 < 0 ? 0 : h - 2, y1 = h + 2 >= H ? H - 1 : h + 2;
+      const int x0 = w - 2 < 0 ? 0 : w - 2, x1 = w + 2 >= W ? W - 1 : w + 2;
+      for (int y = y0; y <= y1; y++)
+        for (int x = x0; x <= x1; x++) {
+          const float v = __half2float(SL[(y * W + x) * 8 + ch]);
+          if (v > best) {
+            best = v;
+            a = (y - h + 2) * 5 + (x - w + 2);
+          }
+        }
+      arg[i] = (uint8_t)a;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < HW * 8; i += blockDim.x) {
+      const int p = i >> 3, ch = i & 7, h = p / W, w = p - h * W;
+      const int y0 = h - 2 < 0 ? 0 : h - 2, y1 = h + 2 >= H ? H - 1 : h + 2;
+      const int x0 = w - 2 < 0 ? 0 : w - 2, x1 = w + 2 >= W ? W - 1 : w + 2;
+      float acc = 0.f;
+      for (int y = y0; y <= y1; y++)
+        for (int x = x0; x <= x1; x++) {
+          const int o = y * W + x;
+          if (arg[o * 8 + ch] == (h - y + 2) * 5 + (w - x + 2)) acc += G[o * 8 + ch];
+        }
+      Acc[i] = acc;
+    }
+    __syncthreads();
+    if (L > 0) {
+      for (int px = threadIdx.x; px < HW; px += blockDim.x) {
+        float v[8];
+        ld8h(dimg + px * ctot + L * c + g0, v);
+#pragma unroll
+        for (int k = 0; k < 8; k++) G[px * 8 + k] = Acc[px * 8 + k] + v[k];
+      }
+      __syncthreads();
+    }
+  }
+  for (int px = threadIdx.x; px < HW; px += blockDim.x) {
+    float v[8];
+    __half* d = dimg + px * ctot + g0;
+    ld8h(d, v);
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] += Acc[px * 8 + k];
+    st8h(d, v);
+  }
+}
+
+cudaError_t launch_sppf_bwd(const __half* cat, __half* dcat, int N, int H, int W, int c, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_sppf_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  k_sppf_bwd<<<dim3(c / kSppfBwdCG, N), 256, sppf_bwd_smem_bytes(H, W), st>>>(cat, dcat, H, W, c);
+  return cudaGetLastError();
+}
+
 cudaError_t sppf_prime() {
   static bool attr = false;
   if (!attr) {

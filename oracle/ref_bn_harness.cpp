@@ -16,9 +16,15 @@
 //   op 2  add_bias: meta = {2, M, C}; y (M, C), bias (C) → y.
 //   op 3  wgrad_rgb_s2: meta = {3, N, H, W, K}; x (N, H, W, 3), dz (N, P, Q, K) → dw (K, 3, 3, 3) and
 //         ran (1 if the reference took its own kernel, 0 if it declined the shape).
+//   op 4  sppf_pool_bwd: meta = {4, N, H, W, c}; cat, dcat (N, H, W, 4c) → dcat.
 //   op 5  SegLoss::run (src/loss.cu:590-621): meta = {5, B, imgsz, G}; box<l>, cls<l>, coef<l> heads, proto,
 //         n_gt (int32 [B]), gt_box (B, G, 4), gt_mask (int32 [B, G, Hp·Wp/32]), scale (1) → dproto, dcoef<l>,
 //         items (16), agt (int32 [B, A]).
+// Timing ops (device time with CUDA events per call, L2 flushed by reading 256 MiB before each call; inputs
+// are seeded pseudo-random fp16 made on the host):
+//   op 10 BN passes of one conv+BN+SiLU node: meta = {10, N, H, W, C, iters} → ms = {stats, apply, backward,
+//         stats and apply back to back} (one plain destination, no residual).
+//   op 13 wgrad_rgb_s2: meta = {13, N, H, W, iters} → ms = {wgrad} (K = 32).
 // Activations are converted to the reference's act_t (fp16) on upload; every value the tests send is
 // fp16-representable.
 #include <cstdio>
@@ -73,6 +79,57 @@ HostTensor down_i32(const int32_t* d, const std::vector<int64_t>& shape) {
   t.data.resize(size_t(t.numel()) * 4);
   CUDA_CHECK(cudaMemcpy(t.data.data(), d, t.data.size(), cudaMemcpyDeviceToHost));
   return t;
+}
+act_t* rand_act(int64_t n, uint32_t seed, float lo, float hi) {
+  std::vector<act_t> h(n);
+  uint32_t x = seed * 2654435761u + 1u;
+  for (int64_t i = 0; i < n; i++) {
+    x = x * 1664525u + 1013904223u;
+    h[i] = from_f<act_t>(lo + (hi - lo) * float(x >> 8) * (1.f / 16777216.f));
+  }
+  act_t* d = dalloc<act_t>(n);
+  CUDA_CHECK(cudaMemcpy(d, h.data(), n * sizeof(act_t), cudaMemcpyHostToDevice));
+  return d;
+}
+float* const_f32(int64_t n, float v) {
+  std::vector<float> h(n, v);
+  float* d = dalloc<float>(n);
+  CUDA_CHECK(cudaMemcpy(d, h.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+  return d;
+}
+// Reads a buffer larger than L2 so that the timed call finds none of its inputs there (reads leave clean
+// lines: nothing is written back during the timed call).
+__global__ void k_flush_read(const uint4* p, size_t n, unsigned* sink) {
+  unsigned x = 0;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const uint4 v = p[i];
+    x ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (x == 0x9e3779b9u) *sink = x;
+}
+// Mean device time (ms) of fn over iters calls, each after an L2 flush.
+template <class F>
+float time_flushed(F fn, int iters, void* flush, size_t flush_bytes, cudaStream_t st) {
+  cudaEvent_t e0, e1;
+  CUDA_CHECK(cudaEventCreate(&e0));
+  CUDA_CHECK(cudaEventCreate(&e1));
+  fn();
+  fn();
+  float tot = 0.f;
+  for (int i = 0; i < iters; i++) {
+    k_flush_read<<<148 * 8, 256, 0, st>>>(static_cast<const uint4*>(flush), flush_bytes / 16,
+                                         reinterpret_cast<unsigned*>(static_cast<char*>(flush)));
+    CUDA_CHECK(cudaEventRecord(e0, st));
+    fn();
+    CUDA_CHECK(cudaEventRecord(e1, st));
+    CUDA_CHECK(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+    tot += ms;
+  }
+  CUDA_CHECK(cudaEventDestroy(e0));
+  CUDA_CHECK(cudaEventDestroy(e1));
+  return tot / iters;
 }
 HostTensor down_f32(const float* d, int64_t n) {
   HostTensor t = HostTensor::make_f32({n}, nullptr);
@@ -171,6 +228,16 @@ int main(int argc, char** argv) {
       out[p + "dw"] = down_act(dw, {K, 3, 3, 3});
       const float r = ran ? 1.f : 0.f;
       out[p + "ran"] = HostTensor::make_f32({1}, &r);
+    } else if (op == 4) {
+      const int N = m[1], H = m[2], W = m[3], c = m[4];
+      const int64_t n = int64_t(N) * H * W * c;
+      act_t* cat = up_act(need(in, p + "cat"));
+      act_t* dcat = up_act(need(in, p + "dcat"));
+      float* ta = dalloc<float>(n);
+      float* tb = dalloc<float>(n);
+      sppf_pool_bwd(cat, dcat, N, H, W, c, ta, tb, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "dcat"] = down_act(dcat, {N, H, W, 4 * c});
     } else if (op == 5) {
       const int B = m[1], S = m[2], G = m[3];
       LossCfg c;
@@ -208,6 +275,51 @@ int main(int argc, char** argv) {
       for (int l = 0; l < 3; l++) out[p + "dcoef" + std::to_string(l)] = down_act(io.dcoef[l], cshape[l]);
       out[p + "items"] = down_f32(L.items(), 16);
       out[p + "agt"] = down_i32(L.assigned_gt(), {B, c.A()});
+    } else if (op == 10 || op == 13) {
+      static void* flush = nullptr;
+      const size_t flush_bytes = size_t(256) << 20;
+      if (!flush) {
+        flush = DevMem::alloc(flush_bytes);
+        CUDA_CHECK(cudaMemset(flush, 1, flush_bytes));
+      }
+      std::vector<float> ms;
+      if (op == 10) {
+        const int N = m[1], H = m[2], W = m[3], C = m[4], iters = m[5];
+        BnShape s{N, H, W, C};
+        const int64_t M = s.M();
+        act_t* z = rand_act(M * C, 1, -2.f, 3.f);
+        float *gamma = const_f32(C, 1.f), *beta = const_f32(C, 0.f), *rm = const_f32(C, 0.f), *rv = const_f32(C, 1.f);
+        float *mean = dalloc<float>(C), *istd = dalloc<float>(C), *scale = dalloc<float>(C), *shift = dalloc<float>(C);
+        float *sums = dalloc<float>(2 * C), *gwg = dalloc<float>(C), *gwb = dalloc<float>(C);
+        DestList dl;
+        Dest& d = dl.d[dl.n++];
+        d.p = dalloc<act_t>(M * C);
+        d.g = rand_act(M * C, 2, -0.1f, 0.1f);
+        d.ctot = C; d.choff = 0; d.c0 = 0; d.c1 = C; d.up = 1;
+        act_t* dz = dalloc<act_t>(M * C);
+        ms.push_back(time_flushed([&] { bn_forward_stats(z, s, gamma, beta, rm, rv, 0.f, 1e-3f, mean, istd, scale,
+                                                          shift, st); }, iters, flush, flush_bytes, st));
+        ms.push_back(time_flushed([&] { bn_forward_apply(z, s, scale, shift, nullptr, dl, true, st); }, iters, flush,
+                                  flush_bytes, st));
+        ms.push_back(time_flushed([&] { bn_backward(z, s, gamma, mean, istd, scale, shift, dl, true, sums, dz, gwg, gwb,
+                                                     false, nullptr, false, st); }, iters, flush, flush_bytes, st));
+        ms.push_back(time_flushed([&] {
+          bn_forward_stats(z, s, gamma, beta, rm, rv, 0.f, 1e-3f, mean, istd, scale, shift, st);
+          bn_forward_apply(z, s, scale, shift, nullptr, dl, true, st);
+        }, iters, flush, flush_bytes, st));
+      } else {
+        const int N = m[1], H = m[2], W = m[3], iters = m[4];
+        const int P = (H + 1) / 2, Q = (W + 1) / 2;
+        act_t* x = rand_act(int64_t(N) * H * W * 3, 3, 0.f, 1.f);
+        act_t* dzz = rand_act(int64_t(N) * P * Q * 32, 4, -1.f, 1.f);
+        float* tmp = dalloc<float>(32 * 27);
+        act_t* dw = dalloc<act_t>(32 * 27);
+        bool ran = true;
+        ms.push_back(time_flushed([&] { ran = wgrad_rgb_s2(x, dzz, N, H, W, 32, tmp, dw, st); }, iters, flush,
+                                  flush_bytes, st));
+        if (!ran) ms[0] = -1.f;
+      }
+      out[p + "ms"] = HostTensor::make_f32({int64_t(ms.size())}, ms.data());
     } else {
       FSO_ASSERT(false, "unknown op %d", op);
     }

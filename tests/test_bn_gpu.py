@@ -324,3 +324,25 @@ def test_stem_wgrad_matches_reference_kernel(cuda_lib):
     op.wgrad(t16(x), t16(dz), dw, ws=ws)
     torch.cuda.synchronize()
     close_f16(dw.float().cpu().numpy(), ref["c0.dw"], "stem dw", rel=2e-3)
+
+
+@pytest.mark.skipif(not os.path.exists(REF_BN), reason="oracle/_ref/ref_bn not built (make -C oracle)")
+def test_sppf_bwd_matches_reference_kernel(cuda_lib):
+    """SPPF backward against the reference's own sppf_pool_bwd (src/misc.cu:155-166): its fp32 atomics add in
+    any order, so one fp16 rounding step of difference is allowed."""
+    from objectsam_b200.conv import sppf_pool_bwd, sppf_pool_fwd
+    N, H, W, c = 2, 20, 20, 128
+    r = np.random.default_rng(31)
+    cat = torch.zeros(N, H, W, 4 * c, dtype=torch.half, device=DEV)
+    cat[..., :c] = t16(r.standard_normal((N, H, W, c)))
+    sppf_pool_fwd(cat, N, H, W, c)
+    dcat = t16(fp16(r.standard_normal((N, H, W, 4 * c)) * 0.5))
+    ins = {"c0.meta": np.array([4, N, H, W, c], np.int32), "c0.cat": cat.float().cpu().numpy(),
+           "c0.dcat": dcat.float().cpu().numpy()}
+    with tempfile.TemporaryDirectory() as td:
+        fsow.save(os.path.join(td, "in.fsow"), ins)
+        subprocess.run([REF_BN, os.path.join(td, "in.fsow"), os.path.join(td, "out.fsow")], check=True, timeout=300)
+        ref = fsow.load(os.path.join(td, "out.fsow"))
+    sppf_pool_bwd(cat, dcat, N, H, W, c)
+    torch.cuda.synchronize()
+    close_f16(dcat.float().cpu().numpy(), ref["c0.dcat"], "sppf dcat", rel=1e-3)

@@ -8,7 +8,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from objectsam_b200.conv import EPI_BIAS, EPI_BN_ACT, ConvGeom, ConvOp, DestSpec, sppf_pool_fwd
+from objectsam_b200.conv import EPI_BIAS, EPI_BN_ACT, ConvGeom, ConvOp, DestSpec, sppf_pool_bwd, sppf_pool_fwd
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -261,6 +261,56 @@ def test_conv_transpose_2x2(cuda_lib):
     y2 = torch.empty_like(y)
     op.fwd_fused(x, w, [DestSpec(y2)], kind=EPI_BIAS, bias=bias, ws=ws)
     assert_close(y2, ref.half().float() + bias)
+
+
+CONVT_SHAPES = [(2, 20, 20, 128, 128), (1, 80, 80, 128, 128), (3, 9, 13, 64, 32)]
+
+
+@pytest.mark.parametrize("shape", CONVT_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_conv_transpose_2x2_dgrad_wgrad(cuda_lib, shape, beta):
+    """Input and weight gradients of ConvTranspose2d(k = s = 2) (reference ConvOp::dgrad/wgrad on its transposed
+    descriptor, src/conv.cpp:351-353, :362-364) against torch autograd in fp32, weights in (C_in, R, S, C_out)."""
+    N, H, W, C, K = shape
+    g = torch.Generator(device="cpu").manual_seed(sum(shape))
+    x = (torch.rand(N, H, W, C, generator=g) * 2 - 1).half().to(DEV)
+    w_pt = (torch.randn(C, K, 2, 2, generator=g) * 0.1).half()
+    w = w_pt.permute(0, 2, 3, 1).contiguous().to(DEV)
+    dy = (torch.rand(N, 2 * H, 2 * W, K, generator=g) * 2 - 1).half().to(DEV)
+    dx0 = (torch.rand(N, H, W, C, generator=g) - 0.5).half().to(DEV)
+    dw0 = (torch.rand(C, 2, 2, K, generator=g) - 0.5).half().to(DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 2, 2, 2, 0), transposed=True)
+    ws = torch.empty(max(op.workspace_size(), 256), dtype=torch.uint8, device=DEV)
+    dx, dw = dx0.clone(), dw0.clone()
+    op.dgrad(dy, w, dx, ws=ws, beta=beta)
+    op.wgrad(x, dy, dw, ws=ws, beta=beta)
+    torch.cuda.synchronize()
+    xt = x.float().permute(0, 3, 1, 2).requires_grad_(True)
+    wt = w_pt.float().to(DEV).requires_grad_(True)
+    F.conv_transpose2d(xt, wt, stride=2).backward(dy.float().permute(0, 3, 1, 2))
+    assert_close(dx, xt.grad.permute(0, 2, 3, 1) + beta * dx0.float())
+    assert_close(dw, wt.grad.permute(0, 2, 3, 1) + beta * dw0.float())
+
+
+SPPF_BWD_SHAPES = [(3, 20, 20, 256, False), (2, 9, 11, 64, False), (2, 20, 20, 64, True), (1, 40, 40, 32, False)]
+
+
+@pytest.mark.parametrize("shape", SPPF_BWD_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_sppf_bwd_matches_oracle_bit_exact(cuda_lib, shape):
+    """SPPF backward against the restatement (same fp32 summation order: bit-exact), ties included."""
+    import numpy as np
+    from oracle import sppf_ref
+    N, H, W, c, ties = shape
+    r = np.random.default_rng(H * W + c)
+    x = r.integers(-2, 3, (N, H, W, c)) if ties else r.standard_normal((N, H, W, c))
+    cat = torch.zeros(N, H, W, 4 * c, dtype=torch.half, device=DEV)
+    cat[..., :c] = torch.from_numpy(x.astype(np.float32)).half().to(DEV)
+    sppf_pool_fwd(cat, N, H, W, c)
+    dcat = torch.from_numpy((r.standard_normal((N, H, W, 4 * c)) * 0.5).astype(np.float32)).half().to(DEV)
+    want = sppf_ref.sppf_bwd(cat.float().cpu().numpy(), dcat.float().cpu().numpy(), c)
+    sppf_pool_bwd(cat, dcat, N, H, W, c)
+    torch.cuda.synchronize()
+    assert np.array_equal(dcat.float().cpu().numpy(), want)
 
 
 def test_sppf_pool_exact(cuda_lib):

@@ -250,3 +250,30 @@ def test_mask_loss_oracle_matches_torch_autograd():
         l, h, w = mask_loss_ref.anchor_of(lv, int(a))
         want = cts[l].grad[0, h, w].numpy() * gk
         assert np.abs(dc[(0, int(a))] - want).max() <= 1e-5 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("ties", [False, True])
+def test_sppf_oracle_matches_torch_autograd(ties):
+    """The SPPF restatement (forward chain and first-max backward) against torch max_pool2d autograd; with
+    ties (values from a handful of integers) torch's CPU max-pool also takes the first maximum of the window
+    in row-major order, so the routing must agree exactly."""
+    from oracle import sppf_ref
+    r = np.random.default_rng(2)
+    N, H, W, c = 2, 9, 11, 8
+    x = (r.integers(-2, 3, (N, H, W, c)) if ties else r.standard_normal((N, H, W, c))).astype(np.float32)
+    cat = np.zeros((N, H, W, 4 * c), np.float32)
+    cat[..., :c] = x
+    for k in range(1, 4):
+        cat[..., k * c:(k + 1) * c] = sppf_ref.pool5_fwd(cat[..., (k - 1) * c:k * c])
+    dcat = (r.integers(-8, 9, (N, H, W, 4 * c)) / 8).astype(np.float32)  # exact in fp16 and in fp32 sums
+    got = sppf_ref.sppf_bwd(cat, dcat, c)
+    xt = torch.tensor(x, dtype=torch.float64).permute(0, 3, 1, 2).requires_grad_(True)
+    s1 = torch.nn.functional.max_pool2d(xt, 5, 1, 2)
+    s2 = torch.nn.functional.max_pool2d(s1, 5, 1, 2)
+    s3 = torch.nn.functional.max_pool2d(s2, 5, 1, 2)
+    assert np.array_equal(s3.detach().permute(0, 2, 3, 1).numpy(), cat[..., 3 * c:])
+    g = lambda k: torch.tensor(dcat[..., k * c:(k + 1) * c], dtype=torch.float64).permute(0, 3, 1, 2)
+    ((s1 * g(1)).sum() + (s2 * g(2)).sum() + (s3 * g(3)).sum()).backward()
+    want = dcat[..., :c] + xt.grad.permute(0, 2, 3, 1).numpy()
+    assert np.array_equal(got[..., :c], want.astype(np.float16).astype(np.float32))
+    assert np.array_equal(got[..., c:], dcat[..., c:])
