@@ -290,6 +290,29 @@ int osam_model_forward_nodes(osam_model* m, int first, int count, osam_stream_t 
  * bias, 2 transposed conv + bias, 3 SPPF pool) and the conv geometry (pool: N,H,W,C of the slice). */
 int osam_model_node_info(const osam_model* m, int i, char* name, int name_len, int* kind, osam_conv_geom* g);
 
+/* ---- training (the reference's Model::forward(true) / Model::backward, src/model.cpp:383-470) ----
+ * osam_model_train_init allocates the activation gradients, the per-node z buffers and BN state, and the fp32
+ * parameter-gradient arena; it takes γ, β and the running statistics from the parameters last synced.
+ * osam_model_forward_train: conv → z (fp16), batch statistics (running statistics updated with `momentum`),
+ * BN + SiLU (+ residual) → destinations; the heads and proto come out as in inference.
+ * The caller then writes the gradients of the heads and of proto (osam_model_act_grad on "out.box<l>",
+ * "out.cls<l>", "out.coef<l>", "out.proto") and runs osam_model_backward_nodes over [first, first + count)
+ * in DECREASING node order; osam_model_backward_nodes(m, 0, osam_model_num_launches(m), s) is the whole
+ * backward.  Per node: BN backward (dz, dγ, dβ, residual gradient), weight gradient, input gradient
+ * (accumulated where an activation feeds several nodes); heads and the transposed conv: bias gradient,
+ * weight gradient, input gradient; SPPF: its backward.  Parameter gradients (fp32) sit in one arena with
+ * the nodes in REVERSE order, so the gradients of nodes [first, n) are one contiguous range that a
+ * data-parallel all-reduce can send while nodes before `first` are still computing.  They are written,
+ * not accumulated. */
+int osam_model_train_init(osam_model* m, osam_stream_t stream);
+int osam_model_forward_train(osam_model* m, float momentum, osam_stream_t stream);
+int osam_model_backward_nodes(osam_model* m, int first, int count, osam_stream_t stream);
+int osam_model_act_grad(const osam_model* m, const char* name, osam_tensor* t); /* gradient of an activation */
+int osam_model_grad_arena(const osam_model* m, float** p, int64_t* n);        /* fp32 parameter gradients */
+int osam_model_node_grad_range(const osam_model* m, int i, int64_t* off, int64_t* n); /* node i's slice */
+/* One parameter's gradient in its PyTorch name and layout (host fp32, n ≥ its element count); synchronous. */
+int osam_model_get_grad(osam_model* m, const char* name, float* out, int64_t n);
+
 /* Device error word shared by all kernels of this library on the current device: returns the first
  * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises. */
 int osam_device_error(void);

@@ -99,6 +99,13 @@ _SIGS = {
     "osam_model_num_launches": (c_int, [c_void_p]),
     "osam_model_forward_nodes": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "osam_model_node_info": (c_int, [c_void_p, c_int, ctypes.c_char_p, c_int, POINTER(c_int), POINTER(ConvGeom)]),
+    "osam_model_train_init": (c_int, [c_void_p, c_void_p]),
+    "osam_model_forward_train": (c_int, [c_void_p, c_float, c_void_p]),
+    "osam_model_backward_nodes": (c_int, [c_void_p, c_int, c_int, c_void_p]),
+    "osam_model_act_grad": (c_int, [c_void_p, ctypes.c_char_p, POINTER(Tensor)]),
+    "osam_model_grad_arena": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_int64)]),
+    "osam_model_node_grad_range": (c_int, [c_void_p, c_int, POINTER(c_int64), POINTER(c_int64)]),
+    "osam_model_get_grad": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, c_int64]),
     "osam_device_error": (c_int, []),
     "osam_last_error": (ctypes.c_char_p, []),
 }

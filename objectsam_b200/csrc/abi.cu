@@ -218,7 +218,36 @@ static void plan_dgrad(osam_conv_plan* p) {
   };
   bool ok = true;
   int n = 0;
-  if (g.stride == 1) {
+  p->dg_chunk = 0;
+  if (g.stride == 1 && g.C > 512) {
+    // the sub-conv's GEMM N is C: split it into equal 32-aligned slices of at most 512 channels
+    int nc = (g.C + 511) / 512;
+    while (nc <= 4 && (g.C % nc || (g.C / nc) % 32)) nc++;
+    ok = nc <= 4 && g.R <= 8;
+    const int chunk = ok ? g.C / nc : 0;
+    for (int i = 0; i < nc && ok; i++) {
+      osam_conv_geom sg{g.N, p->P, p->Q, g.K, chunk, g.R, g.S, 1, g.R - 1 - g.pad};
+      osam_conv_plan* s = new (std::nothrow) osam_conv_plan;
+      if (!s || plan_init(&sg, 0, s) != OSAM_OK || s->mode == A_STEM) {
+        delete s;
+        ok = false;
+        break;
+      }
+      plan_set_output(s, g.H, g.W);
+      p->dg[i] = s;
+      p->dg_R[i] = g.R;
+      p->dg_S[i] = g.S;
+      p->dg_par[i] = 0;
+      for (int r = 0; r < g.R; r++) p->dg_rmap[i][r] = g.R - 1 - r;
+      for (int s2 = 0; s2 < g.S; s2++) p->dg_smap[i][s2] = g.S - 1 - s2;
+    }
+    if (ok) {
+      p->dg_chunk = chunk;
+      for (int i = 0; i < nc; i++) p->dg_woff[i] = 0;  // one re-laid-out set; slice i starts at c = chunk·i
+      p->n_dg = nc;
+      return;
+    }
+  } else if (g.stride == 1) {
     ok = g.R <= 8 && make(0, g.R, g.S, g.R - 1 - g.pad, g.H, g.W, 0);
     if (ok) {
       for (int r = 0; r < g.R; r++) p->dg_rmap[0][r] = g.R - 1 - r;
@@ -364,7 +393,8 @@ static int fill_dest(const osam_dest& s, int kout, DestDev* d, int transposed) {
 }
 
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
-                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word, int par) {
+                 void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word, int par, int y_ctot,
+                 int y_choff) {
   if (!p || !x || !w) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
   *L = ConvLaunch{};
@@ -401,7 +431,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     e.kind = OSAM_EPI_STORE;
     e.beta = beta;
     e.ndest = 1;
-    osam_dest o{y, g.K, 0, 0, g.K, 1};
+    osam_dest o{y, y_ctot > 0 ? y_ctot : g.K, y_ctot > 0 ? y_choff : 0, 0, g.K, 1};
     int rc = fill_dest(o, g.K, &e.dest[0], p->transposed);
     if (rc) return rc;
   } else {
@@ -640,6 +670,7 @@ int osam_conv_plan_destroy(osam_conv_plan* p) {
 
 static size_t dgrad_workspace_bytes(const osam_conv_plan* p) {
   if (p->dg_direct) return 0;
+  if (p->dg_chunk) return ((size_t)p->g.C * p->g.R * p->g.S * p->g.K * 2 + 255) & ~size_t(255);
   size_t b = 0;
   for (int i = 0; i < p->n_dg; i++)
     b = (size_t)p->dg_woff[i] * 2 + (((size_t)p->g.C * p->dg_R[i] * p->dg_S[i] * p->g.K * 2 + 255) & ~size_t(255));
@@ -649,6 +680,14 @@ static size_t dgrad_workspace_bytes(const osam_conv_plan* p) {
 int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void* dx, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream) {
   if (!p || !dz || !w || !dx) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
+  const osam_conv_geom& g1 = p->g;
+  if (!p->transposed && g1.K == 1 && g1.R == 1 && g1.S == 1 && g1.stride == 1 && g1.pad == 0 && g1.C % 8 == 0) {
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dx)) & 15)
+      return fail(OSAM_ERR_INVALID, "dgrad: w and dx must be 16-byte aligned");
+    cudaError_t e = launch_dgrad_k1(static_cast<const __half*>(dz), static_cast<const __half*>(w),
+                                    static_cast<__half*>(dx), p->M, g1.C, beta, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_dgrad (K = 1) launch");
+  }
   if (p->n_dg == 0) return fail(OSAM_ERR_UNSUPPORTED, "dgrad: geometry not supported (stride, kernel or channels)");
   const size_t need = dgrad_workspace_bytes(p);
   if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)))
@@ -663,6 +702,21 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
   }
   const osam_conv_geom& g = p->g;
   __half* wsub = static_cast<__half*>(ws);
+  if (p->dg_chunk) {  // one weight re-layout, then one sub-conv per slice of dx's channels
+    cudaError_t e = launch_dgrad_weights(static_cast<const __half*>(w), wsub, g.K, g.R, g.S, g.C, g.R, g.S,
+                                         p->dg_rmap[0], p->dg_smap[0], st);
+    if (e != cudaSuccess) return cuda_fail(e, "osam_conv_dgrad weight re-layout");
+    for (int i = 0; i < p->n_dg; i++) {
+      ConvLaunch L;
+      const int c0 = p->dg_chunk * i;
+      int rc = conv_prepare(p->dg[i], dz, wsub + (size_t)c0 * g.R * g.S * g.K, nullptr, beta, dx, nullptr, 0, &L, false,
+                            nullptr, 0, g.C, c0);
+      if (rc) return rc;
+      e = conv_launch(L, st);
+      if (e != cudaSuccess) return cuda_fail(e, "osam_conv_dgrad launch");
+    }
+    return OSAM_OK;
+  }
   for (int i = 0; i < p->n_dg; i++) {
     cudaError_t e = launch_dgrad_weights(static_cast<const __half*>(w), wsub + p->dg_woff[i], g.K, g.R, g.S, g.C,
                                          p->dg_R[i], p->dg_S[i], p->dg_rmap[i], p->dg_smap[i], st);
@@ -755,6 +809,15 @@ int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void
     return osam_conv_wgrad(p->dg[0], dz, x, dw, beta, ws, ws_bytes, stream);
   }
   if (p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, beta, ws, ws_bytes, stream);
+  if (g.K == 1 && g.R == 1 && g.S == 1 && g.stride == 1 && g.pad == 0 && g.C % 8 == 0) {
+    const size_t need1 = wgrad_workspace_bytes(p);
+    if (!ws || ws_bytes < need1 || (reinterpret_cast<uintptr_t>(ws) & 255))
+      return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need1);
+    if (reinterpret_cast<uintptr_t>(x) & 15) return fail(OSAM_ERR_INVALID, "wgrad: x must be 16-byte aligned");
+    cudaError_t e = launch_wgrad_k1(static_cast<const __half*>(x), static_cast<const __half*>(dz), static_cast<float*>(ws),
+                                    static_cast<__half*>(dw), p->M, g.C, beta, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_wgrad (K = 1) launch");
+  }
   if (p->transposed || (p->mode != A_S1 && p->mode != A_S2) || g.C % 32 || g.K % 32)
     return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed, small-C or non-32-multiple channels");
   const size_t need = wgrad_workspace_bytes(p);

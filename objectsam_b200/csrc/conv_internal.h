@@ -102,12 +102,18 @@ struct WgradLaunch {
   int grid, nsplit, tiles_per_split;
 };
 cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st);
+// 1×1 conv with one output channel: dx = dy ⊗ w (+ beta·dx); dw = Σ dy·x (fp32 acc[C] scratch, + beta·dw)
+cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long long npix, int C, float beta,
+                            cudaStream_t st);
+cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, long long npix, int C,
+                            float beta, cudaStream_t st);
 
 // Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
 // err_word: device word the kernels report timeouts to (nullptr = the library's per-device word).
+// y_ctot / y_choff (plain store only): y is a slice [y_choff, y_choff + K) of a tensor with y_ctot channels.
 int conv_prepare(const osam_conv_plan* plan, const void* x, const void* w, const osam_epilogue* ep, float beta,
                  void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready = false,
-                 int* err_word = nullptr, int par = 0);
+                 int* err_word = nullptr, int par = 0, int y_ctot = 0, int y_choff = 0);
 cudaError_t launch_dgrad_weights(const __half* w, __half* dst, int K, int R, int S, int C, int Rs, int Ss,
                                  const int* rmap, const int* smap, cudaStream_t st);
 cudaError_t conv_launch(const ConvLaunch& L, cudaStream_t st);
@@ -148,6 +154,9 @@ struct osam_conv_plan {
   // KRSC weights are the transposed conv's own (C_in, R, S, C_out) array: dgrad runs it on dy as is, and
   // wgrad is that conv's weight gradient with the operands' roles swapped.
   int dg_direct;
+  // stride-1 convs with more than 512 input channels: the dgrad's output channels in dg_n_chunk slices of
+  // dg_chunk channels (sub-plan i writes dx channels [dg_chunk·i, dg_chunk·(i+1)) of one re-laid-out set)
+  int dg_chunk;
   long long dg_woff[4];
   // window tiling (A_WIN), used when the epilogue allows the coalesced warp stores (decided per call)
   int win, win_wp, win_lw, win_slab, win_wbytes, win_tpi, win_tiles, win_nwb;

@@ -373,6 +373,52 @@ static cudaError_t wgrad_launch_mode(const WgradLaunch& L, cudaStream_t st) {
   return cudaErrorInvalidValue;
 }
 
+// ------------------------------------------------------------------------------------------------------
+// 1×1 convs with one output channel (the class heads, 128 → 1): both gradients are outer products / channel
+// sums, HBM-bound, with no GEMM to give the tensor cores.
+//   dgrad: dx[pixel][c] = dy[pixel]·w[c] (+ beta·dx)      wgrad: dw[c] = Σ_pixel dy[pixel]·x[pixel][c]
+__global__ void __launch_bounds__(256) k_dgrad_k1(const __half* __restrict__ dy, const __half* __restrict__ w,
+                                                  __half* __restrict__ dx, long long npix, int C, float beta) {
+  const int V = C / 8;
+  const long long n = npix * V;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+    const long long pix = i / V;
+    const int c = int(i - pix * V) * 8;
+    const float g = __half2float(dy[pix]);
+    float wv[8], o[8];
+    ld8h(w + c, wv);
+    if (beta != 0.f) ld8h(dx + pix * C + c, o);
+#pragma unroll
+    for (int k = 0; k < 8; k++) o[k] = beta != 0.f ? fmaf(g, wv[k], beta * o[k]) : g * wv[k];
+    st8h(dx + pix * C + c, o);
+  }
+}
+__global__ void __launch_bounds__(256) k_wgrad_k1(const __half* __restrict__ x, const __half* __restrict__ dy,
+                                                  float* __restrict__ acc, long long npix, int C, long long rows) {
+  extern __shared__ float k1_red[];  // [256 / V][C]
+  const int V = C / 8, RL = 256 / V;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  const long long r0 = blockIdx.x * rows, r1 = r0 + rows < npix ? r0 + rows : npix;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (rl < RL) {
+    for (long long r = r0 + rl; r < r1; r += RL) {
+      float xv[8];
+      ld8h(x + r * C + c, xv);
+      const float g = __half2float(dy[r]);
+#pragma unroll
+      for (int k = 0; k < 8; k++) a[k] = fmaf(g, xv[k], a[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) k1_red[rl * C + c + k] = a[k];
+  }
+  __syncthreads();
+  for (int ch = threadIdx.x; ch < C; ch += 256) {
+    float t = 0.f;
+    for (int q = 0; q < RL; q++) t += k1_red[q * C + ch];
+    atomicAdd(acc + ch, t);
+  }
+}
+
 template <int K>
 static cudaError_t wgrad_stem_launch(const WgradLaunch& L, cudaStream_t st) {
   using Cfg = StemWgCfg<K>;
@@ -420,6 +466,33 @@ cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
   int grid = (int)((L.n_out + 255) / 256);
   if (grid > 4096) grid = 4096;
   k_wgrad_finish<<<grid, 256, 0, st>>>(L.acc, L.dw, L.n_out, L.beta);
+  return cudaGetLastError();
+}
+
+}  // namespace osam
+
+namespace osam {
+
+cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long long npix, int C, float beta,
+                            cudaStream_t st) {
+  const long long n = npix * (C / 8);
+  long long grid = (n + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  k_dgrad_k1<<<(unsigned)grid, 256, 0, st>>>(dy, w, dx, npix, C, beta);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, long long npix, int C,
+                            float beta, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(acc, 0, (size_t)C * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  const int RL = 256 / (C / 8);
+  long long rows = (npix + 148 * 4 - 1) / (148 * 4);
+  if (rows < 4LL * RL) rows = 4LL * RL;
+  const long long grid = (npix + rows - 1) / rows;
+  k_wgrad_k1<<<(unsigned)grid, 256, (size_t)RL * C * sizeof(float), st>>>(x, dy, acc, npix, C, rows);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  k_wgrad_finish<<<(C + 255) / 256, 256, 0, st>>>(acc, dw, C, beta);
   return cudaGetLastError();
 }
 

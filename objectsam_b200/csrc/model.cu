@@ -31,7 +31,8 @@ struct MAct {
   std::string name;
   int C = 0, H = 0, W = 0;
   __half* p = nullptr;
-  size_t off = 0;  // byte offset in the activation arena
+  size_t off = 0;     // byte offset in the activation arena
+  __half* g = nullptr;  // training: gradient buffer (same shape), none for the input image
 };
 
 struct MDest {
@@ -57,6 +58,11 @@ struct MNode {
   ConvLaunch L{};
   size_t w_off = 0;  // fp16 weight arena offset (elements)
   size_t f_off = 0;  // fp32 arena offset: scale[K] + shift[K] (CONVBN) or bias[K]
+  // training
+  __half* z = nullptr;       // CONVBN: conv output before BN (fp16, as the reference stores it)
+  size_t t_off = 0;          // CONVBN: fp32 train arena: γ, β, running μ, running σ², mean, istd, scale, shift
+  size_t g_off = 0, g_w = 0;  // fp32 parameter-gradient arena: weights (g_w elements) then γ, β or the bias
+  bool res_accum = false, dgrad_accum = false;
 };
 
 struct PInfo {
@@ -82,6 +88,11 @@ __global__ void k_bn_fold(const float* __restrict__ gbmv, int C, float eps, floa
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+__global__ void k_f16_to_f32(const __half* __restrict__ s, float* __restrict__ d, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    d[i] = __half2float(s[i]);
+}
+
 }  // namespace
 
 struct osam_model {
@@ -104,6 +115,20 @@ struct osam_model {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   cudaStream_t cap = nullptr;  // private stream the graph is recorded on (the legacy stream cannot capture)
+  // training (osam_model_train_init)
+  bool train = false;
+  uint8_t* garena = nullptr;   // activation gradients
+  __half* zarena = nullptr;    // z of every CONVBN node
+  float* tarena = nullptr;     // BN parameters and batch statistics
+  float* grad32 = nullptr;     // parameter gradients, nodes in reverse order (contiguous DP buckets)
+  size_t grad32_n = 0;
+  __half* dz = nullptr;        // one node's dz (fp16), reused
+  __half* gw16 = nullptr;      // one node's fp16 weight gradient, reused
+  __half* wconvt = nullptr;    // transposed conv weights in the reference's (C_in, R, S, C_out) layout
+  void* ws = nullptr;          // conv workspace (max over nodes)
+  size_t ws_bytes = 0;
+  void* bnws = nullptr;        // zero-filled BN / channel-sum accumulators
+  size_t bnws_bytes = 0;
 
   // ------------------------------------------------------------------ graph construction
   MAct* act(const std::string& n, int C, int H, int W) {
@@ -299,7 +324,31 @@ struct osam_model {
     return OSAM_OK;
   }
 
+  static void free_subplans(osam_conv_plan& p) {
+    for (int i = 0; i < 4; i++) {
+      delete p.dg[i];
+      p.dg[i] = nullptr;
+    }
+  }
+
   void release() {
+    for (auto& nd : nodes) free_subplans(nd->plan);
+    cudaFree(garena);
+    cudaFree(zarena);
+    cudaFree(tarena);
+    cudaFree(grad32);
+    cudaFree(dz);
+    cudaFree(gw16);
+    cudaFree(wconvt);
+    cudaFree(ws);
+    cudaFree(bnws);
+    garena = nullptr;
+    zarena = nullptr;
+    tarena = nullptr;
+    grad32 = nullptr;
+    dz = gw16 = wconvt = nullptr;
+    ws = bnws = nullptr;
+    train = false;
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
     if (cap) cudaStreamDestroy(cap);
@@ -408,7 +457,9 @@ struct osam_model {
       osam_conv_plan* plan = nullptr;
       int rc = osam_conv_plan_create(&g, nd.kind == N_CONVT, &plan);
       if (rc) return model_fail(rc, "%s: %s", nd.name.c_str(), osam_last_error());
-      nd.plan = *plan;
+      free_subplans(nd.plan);
+      nd.plan = *plan;  // the node owns the plan's gradient sub-plans from here on
+      for (int i = 0; i < 4; i++) plan->dg[i] = nullptr;
       osam_conv_plan_destroy(plan);
       osam_epilogue ep{};
       ep.round_z = 0;  // keep z in fp32 into BN/SiLU (the reference rounds it to fp16 first: ≤ 1 ulp apart)
@@ -444,6 +495,254 @@ struct osam_model {
       if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+  }
+
+  // ------------------------------------------------------------------ training (reference Model::forward(true)
+  // and Model::backward, src/model.cpp:383-470): conv → z, batch statistics, apply; then in reverse order BN
+  // backward, weight gradient, input gradient (accumulating where an activation has several consumers).
+  int train_init(cudaStream_t st) {
+    if (!synced) return model_fail(OSAM_ERR_INVALID, "train_init before osam_model_sync_weights");
+    if (train) return OSAM_OK;
+    cudaError_t e;
+    // activation gradients (all but the input image)
+    size_t goff = 0;
+    std::vector<std::pair<MAct*, size_t>> gat;
+    for (auto& kv : acts) {
+      MAct* a = kv.second.get();
+      if (a == in) continue;
+      gat.push_back({a, goff});
+      goff = align_up(goff + (size_t)N * a->H * a->W * a->C * sizeof(__half), 1024);
+    }
+    if ((e = cudaMalloc(&garena, goff)) != cudaSuccess) return model_fail(OSAM_ERR_NOMEM, "gradient arena");
+    cudaMemsetAsync(garena, 0, goff, st);
+    for (auto& ga : gat) ga.first->g = reinterpret_cast<__half*>(garena + ga.second);
+    // z buffers, BN state, parameter gradients (reverse node order), scratch sizes
+    size_t zn = 0, tn = 0, dzn = 0, gwn = 0, wsb = 256, bnb = 256;
+    for (auto& nd : nodes)
+      if (nd->kind == N_CONVBN) {
+        const size_t n = (size_t)N * nd->plan.P * nd->plan.Q * nd->K;
+        nd->t_off = tn;
+        tn = align_up(tn + 8 * (size_t)nd->K, 32);
+        dzn = std::max(dzn, n);
+        zn = align_up(zn + n, 512);
+      }
+    size_t gn = 0;
+    for (int i = (int)nodes.size() - 1; i >= 0; i--) {
+      MNode& nd = *nodes[i];
+      if (nd.kind == N_POOL) continue;
+      const int C = nd.in->C;
+      nd.g_w = nd.kind == N_CONVT ? (size_t)C * 4 * nd.K : (size_t)nd.K * nd.k * nd.k * C;
+      nd.g_off = gn;
+      gn = align_up(gn + nd.g_w + (nd.kind == N_CONVBN ? 2 * (size_t)nd.K : (size_t)nd.K), 64);
+      gwn = std::max(gwn, nd.g_w);
+      wsb = std::max(wsb, osam_conv_workspace_size(&nd.plan));
+      bnb = std::max(bnb, std::max(osam_bn_workspace_size(nd.K), osam_chan_sum_workspace_size(nd.K)));
+    }
+    grad32_n = gn;
+    if ((e = cudaMalloc(&zarena, std::max<size_t>(zn, 1) * sizeof(__half))) != cudaSuccess ||
+        (e = cudaMalloc(&tarena, std::max<size_t>(tn, 1) * sizeof(float))) != cudaSuccess ||
+        (e = cudaMalloc(&grad32, std::max<size_t>(gn, 1) * sizeof(float))) != cudaSuccess ||
+        (e = cudaMalloc(&dz, std::max<size_t>(dzn, 1) * sizeof(__half))) != cudaSuccess ||
+        (e = cudaMalloc(&gw16, std::max<size_t>(gwn, 1) * sizeof(__half))) != cudaSuccess ||
+        (e = cudaMalloc(&ws, wsb)) != cudaSuccess || (e = cudaMalloc(&bnws, bnb)) != cudaSuccess)
+      return model_fail(OSAM_ERR_NOMEM, "training buffers: %s", cudaGetErrorString(e));
+    ws_bytes = wsb;
+    bnws_bytes = bnb;
+    cudaMemsetAsync(bnws, 0, bnb, st);
+    cudaMemsetAsync(grad32, 0, std::max<size_t>(gn, 1) * sizeof(float), st);
+    size_t zo = 0;
+    std::vector<float> th(std::max<size_t>(tn, 1), 0.f);
+    for (auto& ndp : nodes) {
+      MNode& nd = *ndp;
+      if (nd.kind != N_CONVBN) continue;
+      nd.z = zarena + zo;
+      zo = align_up(zo + (size_t)N * nd.plan.P * nd.plan.Q * nd.K, 512);
+      int k0 = 0;
+      const char* bnn[4] = {".bn.weight", ".bn.bias", ".bn.running_mean", ".bn.running_var"};
+      for (size_t pi = 0; pi < nd.pre.size(); pi++) {
+        for (int q = 0; q < 4; q++) {
+          const PInfo& B = params[nd.pre[pi] + bnn[q]];
+          for (int kk = 0; kk < nd.ks[pi]; kk++) th[nd.t_off + (size_t)q * nd.K + k0 + kk] = B.host[kk];
+        }
+        k0 += nd.ks[pi];
+      }
+    }
+    cudaMemcpyAsync(tarena, th.data(), th.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    // the transposed conv's weights in the reference's (C_in, R, S, C_out) layout for its gradients
+    for (auto& ndp : nodes)
+      if (ndp->kind == N_CONVT) {
+        MNode& nd = *ndp;
+        const int C = nd.in->C;
+        std::vector<__half> h((size_t)C * 4 * nd.K);
+        const PInfo& W = params[nd.name + ".weight"];  // PyTorch (C_in, C_out, 2, 2)
+        for (int c = 0; c < C; c++)
+          for (int dy = 0; dy < 2; dy++)
+            for (int dx = 0; dx < 2; dx++)
+              for (int kk = 0; kk < nd.K; kk++)
+                h[(((size_t)c * 2 + dy) * 2 + dx) * nd.K + kk] =
+                    __float2half_rn(W.host[(((size_t)c * nd.K + kk) * 2 + dy) * 2 + dx]);
+        if ((e = cudaMalloc(&wconvt, h.size() * sizeof(__half))) != cudaSuccess)
+          return model_fail(OSAM_ERR_NOMEM, "transposed-conv weights");
+        cudaMemcpy(wconvt, h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice);
+      }
+    // which gradient writes overwrite and which accumulate (reference src/model.cpp:352-366)
+    std::map<const MAct*, bool> written;
+    for (int l = 0; l < 3; l++)
+      for (int k = 0; k < 3; k++) written[head[k][l]] = true;
+    written[proto] = true;
+    for (int i = (int)nodes.size() - 1; i >= 0; i--) {
+      MNode& nd = *nodes[i];
+      if (nd.kind == N_POOL) continue;
+      if (nd.kind == N_CONVBN) {
+        for (auto& d : nd.dests)
+          if (!written.count(d.a)) return model_fail(OSAM_ERR_INVALID, "%s: gradient of %s not ready", nd.name.c_str(),
+                                                     d.a->name.c_str());
+        if (nd.res) {
+          nd.res_accum = written.count(nd.res) > 0;
+          written[nd.res] = true;
+        }
+      } else if (!written.count(nd.out)) {
+        return model_fail(OSAM_ERR_INVALID, "%s: output gradient not ready", nd.name.c_str());
+      }
+      if (nd.in != in) {
+        nd.dgrad_accum = written.count(nd.in) > 0;
+        written[nd.in] = true;
+      }
+    }
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "train_init: %s", cudaGetErrorString(e));
+    train = true;
+    return OSAM_OK;
+  }
+
+  int forward_train(float momentum, cudaStream_t st) {
+    if (!train) return model_fail(OSAM_ERR_INVALID, "forward_train before osam_model_train_init");
+    for (auto& ndp : nodes) {
+      MNode& nd = *ndp;
+      int rc = OSAM_OK;
+      if (nd.kind == N_CONVBN) {
+        const int P = nd.plan.P, Q = nd.plan.Q, K = nd.K;
+        float* T = tarena + nd.t_off;
+        rc = osam_conv_fwd(&nd.plan, nd.in->p, w16 + nd.w_off, nd.z, 0.f, ws, ws_bytes, st);
+        if (!rc)
+          rc = osam_bn_forward_stats(nd.z, N, P, Q, K, T, T + K, T + 2 * K, T + 3 * K, momentum, bn_eps, T + 4 * K,
+                                     T + 5 * K, T + 6 * K, T + 7 * K, bnws, bnws_bytes, st);
+        osam_dest d[OSAM_MAX_DEST];
+        for (size_t i = 0; i < nd.dests.size(); i++)
+          d[i] = osam_dest{nd.dests[i].a->p, nd.dests[i].a->C, nd.dests[i].choff, nd.dests[i].c0, nd.dests[i].c1,
+                           nd.dests[i].up};
+        if (!rc)
+          rc = osam_bn_forward_apply(nd.z, N, P, Q, K, T + 6 * K, T + 7 * K, nd.res ? nd.res->p : nullptr, d,
+                                     (int)nd.dests.size(), 1, st);
+      } else if (nd.kind == N_POOL) {
+        if (launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, st) != cudaSuccess) rc = OSAM_ERR_CUDA;
+      } else {
+        if (conv_launch(nd.L, st) != cudaSuccess) rc = OSAM_ERR_CUDA;
+      }
+      if (rc) return model_fail(rc, "%s (train forward): %s", nd.name.c_str(), osam_last_error());
+    }
+    return OSAM_OK;
+  }
+
+  int wgrad_to_arena(MNode& nd, const __half* x, const __half* dy, cudaStream_t st) {
+    int rc = osam_conv_wgrad(&nd.plan, x, dy, gw16, 0.f, ws, ws_bytes, st);
+    if (rc) return rc;
+    k_f16_to_f32<<<(unsigned)std::min<size_t>((nd.g_w + 255) / 256, 4096), 256, 0, st>>>(gw16, grad32 + nd.g_off,
+                                                                                       (long long)nd.g_w);
+    return cudaGetLastError() == cudaSuccess ? OSAM_OK : OSAM_ERR_CUDA;
+  }
+
+  int backward_nodes(int first, int count, cudaStream_t st) {
+    if (!train) return model_fail(OSAM_ERR_INVALID, "backward before osam_model_train_init");
+    for (int i = first + count - 1; i >= first; i--) {
+      MNode& nd = *nodes[i];
+      int rc = OSAM_OK;
+      if (nd.kind == N_CONVBN) {
+        const int P = nd.plan.P, Q = nd.plan.Q, K = nd.K;
+        float* T = tarena + nd.t_off;
+        osam_dest gd[OSAM_MAX_DEST];
+        for (size_t k = 0; k < nd.dests.size(); k++)
+          gd[k] = osam_dest{nd.dests[k].a->g, nd.dests[k].a->C, nd.dests[k].choff, nd.dests[k].c0, nd.dests[k].c1,
+                            nd.dests[k].up};
+        float* gg = grad32 + nd.g_off + nd.g_w;
+        rc = osam_bn_backward(nd.z, N, P, Q, K, T + 4 * K, T + 5 * K, T + 6 * K, T + 7 * K, gd, (int)nd.dests.size(), 1,
+                              dz, gg, gg + K, 0, nd.res ? nd.res->g : nullptr, nd.res_accum ? 1 : 0, bnws, bnws_bytes,
+                              st);
+        if (!rc) rc = wgrad_to_arena(nd, nd.in->p, dz, st);
+        if (!rc && nd.in != in)
+          rc = osam_conv_dgrad(&nd.plan, dz, w16 + nd.w_off, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
+      } else if (nd.kind == N_POOL) {
+        rc = osam_sppf_bwd(nd.cat->p, nd.cat->g, N, nd.cat->H, nd.cat->W, nd.pc, st);
+      } else {
+        const long long M = (long long)N * nd.out->H * nd.out->W;
+        rc = osam_chan_sum(nd.out->g, M, nd.K, grad32 + nd.g_off + nd.g_w, 0, bnws, bnws_bytes, st);
+        if (!rc) rc = wgrad_to_arena(nd, nd.in->p, nd.out->g, st);
+        const __half* w = nd.kind == N_CONVT ? wconvt : w16 + nd.w_off;
+        if (!rc && nd.in != in)
+          rc = osam_conv_dgrad(&nd.plan, nd.out->g, w, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
+      }
+      if (rc) return model_fail(rc, "%s (backward): %s", nd.name.c_str(), osam_last_error());
+    }
+    return OSAM_OK;
+  }
+
+  // Gradient of one parameter in its PyTorch name and layout (host fp32), read back after a backward.
+  int get_grad(const std::string& name, float* out, size_t n) {
+    if (!train) return model_fail(OSAM_ERR_INVALID, "no gradients before osam_model_train_init");
+    auto it = params.find(name);
+    if (it == params.end()) return model_fail(OSAM_ERR_INVALID, "no parameter %s", name.c_str());
+    size_t cnt = 1;
+    for (auto v : it->second.shape) cnt *= (size_t)v;
+    if (n < cnt) return model_fail(OSAM_ERR_INVALID, "%s: %zu values needed", name.c_str(), cnt);
+    for (auto& ndp : nodes) {
+      MNode& nd = *ndp;
+      if (nd.kind == N_POOL) continue;
+      const int C = nd.in->C, k = nd.k;
+      std::vector<float> g(nd.g_w + (nd.kind == N_CONVBN ? 2 * (size_t)nd.K : (size_t)nd.K));
+      auto fetch = [&]() {
+        cudaMemcpy(g.data(), grad32 + nd.g_off, g.size() * sizeof(float), cudaMemcpyDeviceToHost);
+      };
+      if (nd.kind == N_CONVBN) {
+        int k0 = 0;
+        for (size_t pi = 0; pi < nd.pre.size(); pi++) {
+          const std::string& pf = nd.pre[pi];
+          const int Kp = nd.ks[pi];
+          if (name == pf + ".conv.weight") {
+            fetch();
+            for (int kk = 0; kk < Kp; kk++)
+              for (int c = 0; c < C; c++)
+                for (int r = 0; r < k; r++)
+                  for (int s2 = 0; s2 < k; s2++)
+                    out[(((size_t)kk * C + c) * k + r) * k + s2] = g[(((size_t)(k0 + kk) * k + r) * k + s2) * C + c];
+            return OSAM_OK;
+          }
+          if (name == pf + ".bn.weight" || name == pf + ".bn.bias") {
+            fetch();
+            const size_t base = nd.g_w + (name == pf + ".bn.bias" ? (size_t)nd.K : 0);
+            for (int kk = 0; kk < Kp; kk++) out[kk] = g[base + k0 + kk];
+            return OSAM_OK;
+          }
+          k0 += Kp;
+        }
+      } else if (name == nd.name + ".weight") {
+        fetch();
+        if (nd.kind == N_HEAD) {
+          for (size_t q = 0; q < nd.g_w; q++) out[q] = g[q];  // (K, 1, 1, C) = (K, C, 1, 1)
+        } else {  // (C_in, 2, 2, C_out) → PyTorch (C_in, C_out, 2, 2)
+          for (int c = 0; c < C; c++)
+            for (int dy = 0; dy < 2; dy++)
+              for (int dx = 0; dx < 2; dx++)
+                for (int kk = 0; kk < nd.K; kk++)
+                  out[(((size_t)c * nd.K + kk) * 2 + dy) * 2 + dx] = g[(((size_t)c * 2 + dy) * 2 + dx) * nd.K + kk];
+        }
+        return OSAM_OK;
+      } else if (name == nd.name + ".bias") {
+        fetch();
+        for (int kk = 0; kk < nd.K; kk++) out[kk] = g[nd.g_w + kk];
+        return OSAM_OK;
+      }
+    }
+    return model_fail(OSAM_ERR_INVALID, "%s has no gradient (running statistics are not trained)", name.c_str());
   }
 
   int forward(int use_graph, cudaStream_t st) {
@@ -618,6 +917,53 @@ int osam_model_forward_nodes(osam_model* m, int first, int count, osam_stream_t 
     if (e != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "%s: %s", nd.name.c_str(), cudaGetErrorString(e));
   }
   return OSAM_OK;
+}
+
+int osam_model_train_init(osam_model* m, osam_stream_t stream) {
+  if (!m) return model_fail(OSAM_ERR_INVALID, "NULL model");
+  return m->train_init(reinterpret_cast<cudaStream_t>(stream));
+}
+
+int osam_model_forward_train(osam_model* m, float momentum, osam_stream_t stream) {
+  if (!m) return model_fail(OSAM_ERR_INVALID, "NULL model");
+  return m->forward_train(momentum, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int osam_model_backward_nodes(osam_model* m, int first, int count, osam_stream_t stream) {
+  if (!m || first < 0 || count < 0 || first + count > (int)m->nodes.size())
+    return model_fail(OSAM_ERR_INVALID, "backward_nodes range");
+  return m->backward_nodes(first, count, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int osam_model_act_grad(const osam_model* m, const char* name, osam_tensor* t) {
+  if (!m || !name || !t) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  if (!m->train) return model_fail(OSAM_ERR_INVALID, "no gradients before osam_model_train_init");
+  auto it = m->acts.find(name);
+  if (it == m->acts.end() || !it->second->g) return model_fail(OSAM_ERR_INVALID, "no gradient for %s", name);
+  int rc = fill_tensor(m, it->second.get(), t);
+  t->p = it->second->g;
+  return rc;
+}
+
+int osam_model_grad_arena(const osam_model* m, float** p, int64_t* n) {
+  if (!m || !p || !n) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  if (!m->train) return model_fail(OSAM_ERR_INVALID, "no gradients before osam_model_train_init");
+  *p = m->grad32;
+  *n = (int64_t)m->grad32_n;
+  return OSAM_OK;
+}
+
+int osam_model_node_grad_range(const osam_model* m, int i, int64_t* off, int64_t* n) {
+  if (!m || i < 0 || i >= (int)m->nodes.size() || !off || !n) return model_fail(OSAM_ERR_INVALID, "node index %d", i);
+  const MNode& nd = *m->nodes[i];
+  *off = (int64_t)nd.g_off;
+  *n = nd.kind == N_POOL ? 0 : (int64_t)(nd.g_w + (nd.kind == N_CONVBN ? 2 * (size_t)nd.K : (size_t)nd.K));
+  return OSAM_OK;
+}
+
+int osam_model_get_grad(osam_model* m, const char* name, float* out, int64_t n) {
+  if (!m || !name || !out || n < 0) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  return m->get_grad(name, out, (size_t)n);
 }
 
 int osam_model_node_info(const osam_model* m, int i, char* name, int name_len, int* kind, osam_conv_geom* g) {

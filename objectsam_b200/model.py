@@ -22,8 +22,8 @@ from ._lib import Tensor, check, lib, stream_ptr
 class _DeviceArray:
     """__cuda_array_interface__ wrapper so torch can view a buffer owned by the library."""
 
-    def __init__(self, ptr: int, shape, owner):
-        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f2", "data": (ptr, False),
+    def __init__(self, ptr: int, shape, owner, typestr: str = "<f2"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
                                          "version": 3, "strides": None}
         self._owner = owner
 
@@ -108,6 +108,44 @@ class Model:
 
     def forward_nodes(self, first: int, count: int, stream=None) -> None:
         check(lib().osam_model_forward_nodes(self._m, first, count, stream_ptr(stream)))
+
+    # ------------------------------------------------------------- training (Model::forward(true), backward)
+    def train_init(self, stream=None) -> None:
+        """Allocate gradients, z buffers and BN state (after sync_weights)."""
+        check(lib().osam_model_train_init(self._m, stream_ptr(stream)))
+
+    def forward_train(self, momentum: float = 0.03, stream=None) -> None:
+        check(lib().osam_model_forward_train(self._m, float(momentum), stream_ptr(stream)))
+
+    def backward_nodes(self, first: int, count: int, stream=None) -> None:
+        """Backward of nodes [first, first + count), last node first."""
+        check(lib().osam_model_backward_nodes(self._m, first, count, stream_ptr(stream)))
+
+    def backward(self, stream=None) -> None:
+        self.backward_nodes(0, self.num_launches(), stream)
+
+    def act_grad(self, name: str):
+        """Gradient buffer of an activation ("out.box0", "out.proto", …) as a torch NHWC fp16 view."""
+        t = Tensor()
+        check(lib().osam_model_act_grad(self._m, name.encode(), ctypes.byref(t)))
+        return self._view(t)
+
+    def grad_arena(self):
+        """All parameter gradients (fp32, nodes in reverse order) as one torch view."""
+        import torch
+        p, n = ctypes.c_void_p(), ctypes.c_int64()
+        check(lib().osam_model_grad_arena(self._m, ctypes.byref(p), ctypes.byref(n)))
+        return torch.as_tensor(_DeviceArray(p.value, (n.value,), self, "<f4"), device="cuda")
+
+    def node_grad_range(self, i: int) -> tuple[int, int]:
+        off, n = ctypes.c_int64(), ctypes.c_int64()
+        check(lib().osam_model_node_grad_range(self._m, i, ctypes.byref(off), ctypes.byref(n)))
+        return off.value, n.value
+
+    def get_grad(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(int(np.prod(shape)), np.float32)
+        check(lib().osam_model_get_grad(self._m, name.encode(), out.ctypes.data, out.size))
+        return out.reshape(shape)
 
     def nodes(self) -> list[dict]:
         """Per node: name, kind (0 conv+BN+SiLU, 1 head conv, 2 transposed conv, 3 SPPF pool), geometry,

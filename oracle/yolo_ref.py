@@ -26,9 +26,10 @@ BN_EPS = 1e-3
 
 class YoloSegRef:
     def __init__(self, weights: dict, emulate_fp16: bool = True, dtype=torch.float32, device="cpu",
-                 calibrate: bool = False):
+                 calibrate: bool = False, train: bool = False):
         self.fp16 = emulate_fp16
         self.calibrate = calibrate
+        self.train = train  # BN on batch statistics, autograd on (reference Model::forward(true), src/bn.cu:112-202)
         self.dtype = dtype
         self.device = device
         self.w = {}
@@ -37,6 +38,8 @@ class YoloSegRef:
             if self.fp16 and (k.endswith("conv.weight") or (t.ndim == 4)):
                 t = t.half().float()
             self.w[k] = t.to(dtype)
+            if train and not k.endswith(("running_mean", "running_var")):
+                self.w[k].requires_grad_(True)
         self.acts = {}
 
     # -------------------------------------------------------------- helpers
@@ -51,9 +54,14 @@ class YoloSegRef:
             self.w[f"{name}.bn.running_mean"] = z.mean((0, 2, 3))
             self.w[f"{name}.bn.running_var"] = z.var((0, 2, 3), unbiased=False)
         g, b = self.w[f"{name}.bn.weight"], self.w[f"{name}.bn.bias"]
-        rm, rv = self.w[f"{name}.bn.running_mean"], self.w[f"{name}.bn.running_var"]
-        scale = (g.float() * torch.rsqrt(rv.float() + BN_EPS)).to(self.dtype)
-        shift = (b.float() - rm.float() * scale.float()).to(self.dtype)
+        if self.train:  # batch statistics, biased variance (the normalisation the reference's stats pass feeds)
+            mu, var = z.mean((0, 2, 3)), z.var((0, 2, 3), unbiased=False)
+            scale = g * torch.rsqrt(var + BN_EPS)
+            shift = b - mu * scale
+        else:
+            rm, rv = self.w[f"{name}.bn.running_mean"], self.w[f"{name}.bn.running_var"]
+            scale = (g.float() * torch.rsqrt(rv.float() + BN_EPS)).to(self.dtype)
+            shift = (b.float() - rm.float() * scale.float()).to(self.dtype)
         y = z * scale.view(1, -1, 1, 1) + shift.view(1, -1, 1, 1)
         y = y * torch.sigmoid(y)
         if res is not None:
@@ -87,10 +95,14 @@ class YoloSegRef:
         return F.interpolate(x, scale_factor=2, mode="nearest")
 
     # -------------------------------------------------------------- network
-    @torch.no_grad()
     def forward(self, img_nhwc) -> dict:
         """img_nhwc: (N, S, S, 3) float array/tensor in [0,1].  Returns NCHW tensors:
-        box[l] (N,64,H,W), cls[l] (N,1,H,W), coef[l] (N,32,H,W), proto (N,32,S/4,S/4)."""
+        box[l] (N,64,H,W), cls[l] (N,1,H,W), coef[l] (N,32,H,W), proto (N,32,S/4,S/4).
+        In training mode the graph is kept for autograd (the parameters in self.w require grad)."""
+        with torch.set_grad_enabled(self.train):
+            return self._forward(img_nhwc)
+
+    def _forward(self, img_nhwc) -> dict:
         x = torch.as_tensor(np.asarray(img_nhwc), dtype=torch.float32).to(self.device)
         x = self._r(x.to(self.dtype).permute(0, 3, 1, 2).contiguous())
         self.acts = {}

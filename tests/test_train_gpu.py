@@ -1,0 +1,103 @@
+"""Training pass of the whole network (reference Model::forward(true) + Model::backward, src/model.cpp:383-470)
+through the C ABI: batch-statistics BN forward, then the backward of every node from given head gradients,
+against torch autograd of the CPU restatement in training mode (oracle/yolo_ref.py, fp16 storage emulated).
+
+Tolerances, against fp64 autograd: a head's max error ≤ 2× the error that the reference's fp16 storage
+points alone cause (the fp32 restatement with fp16 rounding where the reference stores fp16) + 1e-2·max;
+each parameter gradient's relL2 = ‖ours − ref‖/‖ref‖ ≤ max(2× that of the fp16-storage restatement, 1e-2).
+"""
+import numpy as np
+import pytest
+import torch
+
+from objectsam_b200.model import Model
+from oracle import yolo_params, yolo_ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _setup(N, S, seed):
+    w = yolo_ref.calibrated_weights(seed, S)
+    imgs = yolo_params.make_images(N, S, seed + 1)
+    m = Model(N, S)
+    m.load(w)
+    m.sync_weights()
+    m.train_init()
+    m.input().copy_(torch.from_numpy(imgs).half())
+    return m, w, imgs
+
+
+def _head_grads(m, S, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    grads = {}
+    names = [f"out.{k}{l}" for k in ("box", "cls", "coef") for l in range(3)] + ["out.proto"]
+    for n in names:
+        t = m.act_grad(n)
+        r = (torch.randn(t.shape, generator=g) * 0.05).half()
+        t.copy_(r.to(DEV))
+        grads[n] = r.float()
+    return grads
+
+
+def _oracle(w, imgs, G, fp16):
+    """Outputs and parameter gradients of the CPU restatement in training mode: fp64 exact, or fp32 with the
+    reference's fp16 storage points emulated."""
+    ref = yolo_ref.YoloSegRef(w, emulate_fp16=fp16, dtype=torch.float32 if fp16 else torch.float64, train=True)
+    out = ref.forward(imgs)
+    d = torch.float32 if fp16 else torch.float64
+    loss = sum((out[k][l] * G[f"out.{k}{l}"].to(d).permute(0, 3, 1, 2)).sum() for k in ("box", "cls", "coef")
+               for l in range(3))
+    loss = loss + (out["proto"] * G["out.proto"].to(d).permute(0, 3, 1, 2)).sum()
+    loss.backward()
+    grads = {n: t.grad.double().numpy() for n, t in ref.w.items() if t.grad is not None}
+    return {k: ([t.detach().double() for t in v] if isinstance(v, list) else v.detach().double())
+            for k, v in out.items()}, grads
+
+
+@pytest.mark.parametrize("N,S", [(2, 256)])
+def test_train_pass_matches_autograd(cuda_lib, N, S):
+    """Against fp64 autograd; the allowed error is twice what the reference's fp16 storage alone causes
+    (the same network in fp32 with fp16 rounding at the reference's storage points), or 1e-2."""
+    m, w, imgs = _setup(N, S, 3)
+    m.forward_train(0.03)
+    G = _head_grads(m, S, 9)
+    m.backward()
+    torch.cuda.synchronize()
+    o64, g64 = _oracle(w, imgs, G, fp16=False)
+    o16, g16 = _oracle(w, imgs, G, fp16=True)
+    for key, kind in (("box", 0), ("cls", 1), ("coef", 2)):
+        for l in range(3):
+            y = m.head(kind, l).double().cpu().permute(0, 3, 1, 2)
+            r, r16 = o64[key][l], o16[key][l]
+            e, e16 = (y - r).abs().max().item(), (r16 - r).abs().max().item()
+            assert e <= 2 * e16 + 1e-2 * r.abs().max().item(), f"{key}{l}: max err {e:.3e} (fp16 storage {e16:.3e})"
+    worst, checked = [], 0
+    for name, want in g64.items():
+        got = m.get_grad(name, want.shape).astype(np.float64)
+        nrm = np.linalg.norm(want) + 1e-30
+        rel, rel16 = np.linalg.norm(got - want) / nrm, np.linalg.norm(g16[name] - want) / nrm
+        worst.append((rel, rel16, name))
+        checked += 1
+        assert rel <= max(2 * rel16, 1e-2), f"{name}: relL2 {rel:.3e} (fp16 storage {rel16:.3e})"
+    assert checked > 150, f"only {checked} parameter gradients compared"
+    worst.sort(reverse=True)
+    print(f"{checked} parameter gradients; worst relL2 {worst[0][0]:.3e} ({worst[0][2]}, fp16 storage "
+          f"{worst[0][1]:.3e})")
+
+
+def test_train_backward_in_buckets_equals_whole(cuda_lib):
+    """Backward run as consecutive node ranges (last first, as the data-parallel buckets run it) gives the
+    gradients of one whole backward (up to the order of the weight gradients' fp32 atomics)."""
+    m, w, imgs = _setup(2, 128, 5)
+    m.forward_train(0.0)
+    _head_grads(m, 128, 4)
+    m.backward()
+    whole = m.grad_arena().clone()
+    n = m.num_launches()
+    cuts = [n, 50, 31, 7, 0]
+    for hi, lo in zip(cuts, cuts[1:]):
+        m.backward_nodes(lo, hi - lo)
+    torch.cuda.synchronize()
+    again = m.grad_arena()
+    assert torch.norm(again - whole) <= 1e-5 * torch.norm(whole)
