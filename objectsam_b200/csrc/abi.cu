@@ -751,8 +751,8 @@ static int sm_count() {
 
 // Weight gradient of a small-C plan (R·S·C ≤ 32, the RGB stem): patch-gather tcgen05 kernel over runs of
 // 128 consecutive output pixels (conv_wgrad.cu), one CTA pair per SM.
-static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float beta, void* ws,
-                      size_t ws_bytes, osam_stream_t stream) {
+static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
+                      void* ws, size_t ws_bytes, osam_stream_t stream) {
   const osam_conv_geom& g = p->g;
   if (g.K != 32 && g.K != 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C wgrad: K must be 32 or 64 (K=%d)", g.K);
   const size_t need = wgrad_workspace_bytes(p);
@@ -772,6 +772,7 @@ static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, vo
   L.xp = static_cast<const __half*>(x);
   L.acc = static_cast<float*>(ws);
   L.dw = static_cast<__half*>(dw);
+  L.dw32 = dw32;
   L.n_out = (long long)g.K * g.R * g.S * g.C;
   L.beta = beta;
   {
@@ -798,24 +799,45 @@ size_t osam_conv_workspace_size(const osam_conv_plan* p) {
   return std::max(dgrad_workspace_bytes(p), wgrad_workspace_bytes(p));
 }
 
+static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
+                      void* ws, size_t ws_bytes, osam_stream_t stream);
+
 int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream) {
-  if (!p || !x || !dz || !dw) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
+  if (!dw) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
+  return wgrad_impl(p, x, dz, dw, nullptr, beta, ws, ws_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace osam {
+int conv_wgrad_f32(const osam_conv_plan* p, const void* x, const void* dz, float* dw32, float beta, void* ws,
+                   size_t ws_bytes, cudaStream_t st) {
+  if (!dw32) return fail(OSAM_ERR_INVALID, "NULL fp32 weight-gradient output");
+  return wgrad_impl(p, x, dz, nullptr, dw32, beta, ws, ws_bytes, reinterpret_cast<osam_stream_t>(st));
+}
+}  // namespace osam
+
+extern "C" {
+
+static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
+                      void* ws, size_t ws_bytes, osam_stream_t stream) {
+  if (!p || !x || !dz || (!dw && !dw32)) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
   if (p->transposed) {
     // dW[c][r][s][k] = Σ_{p,q} x[p][q][c]·dy[2p+r][2q+s][k]: the weight gradient of the stride-2 2×2 conv
     // dg[0] (input dy, output x-shaped) with x in the role of its output gradient
     if (!p->dg_direct) return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed conv other than kernel = stride = 2");
-    return osam_conv_wgrad(p->dg[0], dz, x, dw, beta, ws, ws_bytes, stream);
+    return wgrad_impl(p->dg[0], dz, x, dw, dw32, beta, ws, ws_bytes, stream);
   }
-  if (p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, beta, ws, ws_bytes, stream);
+  if (p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, dw32, beta, ws, ws_bytes, stream);
   if (g.K == 1 && g.R == 1 && g.S == 1 && g.stride == 1 && g.pad == 0 && g.C % 8 == 0) {
     const size_t need1 = wgrad_workspace_bytes(p);
     if (!ws || ws_bytes < need1 || (reinterpret_cast<uintptr_t>(ws) & 255))
       return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need1);
     if (reinterpret_cast<uintptr_t>(x) & 15) return fail(OSAM_ERR_INVALID, "wgrad: x must be 16-byte aligned");
     cudaError_t e = launch_wgrad_k1(static_cast<const __half*>(x), static_cast<const __half*>(dz), static_cast<float*>(ws),
-                                    static_cast<__half*>(dw), p->M, g.C, beta, reinterpret_cast<cudaStream_t>(stream));
+                                    static_cast<__half*>(dw), dw32, p->M, g.C, beta, reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_wgrad (K = 1) launch");
   }
   if (p->transposed || (p->mode != A_S1 && p->mode != A_S2) || g.C % 32 || g.K % 32)
@@ -840,6 +862,7 @@ int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void
   L.mode = p->mode;
   L.acc = static_cast<float*>(ws);
   L.dw = static_cast<__half*>(dw);
+  L.dw32 = dw32;
   L.n_out = (long long)g.K * g.R * g.S * g.C;
   L.beta = beta;
   int rc = OSAM_OK;

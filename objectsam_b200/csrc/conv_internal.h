@@ -94,6 +94,7 @@ struct WgradLaunch {
   ConvDev d;            // geometry and the forward plan's spatial tiling
   float* acc;           // fp32 KRSC accumulator (workspace), zeroed by the launch
   __half* dw;           // fp16 KRSC result
+  float* dw32;          // or, when non-null, the fp32 result (dw unused)
   long long n_out;      // K·R·S·C
   float beta;
   int AB, BB, BN;       // dz / x box channels (32 or 64), GEMM N block
@@ -105,8 +106,11 @@ cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st);
 // 1×1 conv with one output channel: dx = dy ⊗ w (+ beta·dx); dw = Σ dy·x (fp32 acc[C] scratch, + beta·dw)
 cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long long npix, int C, float beta,
                             cudaStream_t st);
-cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, long long npix, int C,
-                            float beta, cudaStream_t st);
+cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, float* dw32, long long npix,
+                            int C, float beta, cudaStream_t st);
+// osam_conv_wgrad with the result in fp32 (dw32, + beta·dw32) instead of fp16: the training path's gradient arena.
+int conv_wgrad_f32(const osam_conv_plan* plan, const void* x, const void* dz, float* dw32, float beta, void* ws,
+                   size_t ws_bytes, cudaStream_t st);
 
 // Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
 // err_word: device word the kernels report timeouts to (nullptr = the library's per-device word).

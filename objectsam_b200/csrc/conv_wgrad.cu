@@ -342,12 +342,17 @@ __global__ void __launch_bounds__(StemWgCfg<K>::THREADS, 1)
   }
 }
 
-// dw (fp16) = acc (fp32) + beta · dw
-__global__ void k_wgrad_finish(const float* __restrict__ acc, __half* __restrict__ dw, long long n, float beta) {
+// dw (fp16) = acc (fp32) + beta · dw, or dw32 (fp32) = acc + beta · dw32
+__global__ void k_wgrad_finish(const float* __restrict__ acc, __half* __restrict__ dw, float* __restrict__ dw32,
+                               long long n, float beta) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     float v = acc[i];
-    if (beta != 0.f) v += beta * __half2float(dw[i]);
-    dw[i] = __float2half_rn(v);
+    if (dw32) {
+      dw32[i] = beta != 0.f ? v + beta * dw32[i] : v;
+    } else {
+      if (beta != 0.f) v += beta * __half2float(dw[i]);
+      dw[i] = __float2half_rn(v);
+    }
   }
 }
 
@@ -465,7 +470,7 @@ cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   int grid = (int)((L.n_out + 255) / 256);
   if (grid > 4096) grid = 4096;
-  k_wgrad_finish<<<grid, 256, 0, st>>>(L.acc, L.dw, L.n_out, L.beta);
+  k_wgrad_finish<<<grid, 256, 0, st>>>(L.acc, L.dw, L.dw32, L.n_out, L.beta);
   return cudaGetLastError();
 }
 
@@ -482,8 +487,8 @@ cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long 
   return cudaGetLastError();
 }
 
-cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, long long npix, int C,
-                            float beta, cudaStream_t st) {
+cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, float* dw32, long long npix,
+                            int C, float beta, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(acc, 0, (size_t)C * sizeof(float), st);
   if (e != cudaSuccess) return e;
   const int RL = 256 / (C / 8);
@@ -492,7 +497,7 @@ cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __hal
   const long long grid = (npix + rows - 1) / rows;
   k_wgrad_k1<<<(unsigned)grid, 256, (size_t)RL * C * sizeof(float), st>>>(x, dy, acc, npix, C, rows);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  k_wgrad_finish<<<(C + 255) / 256, 256, 0, st>>>(acc, dw, C, beta);
+  k_wgrad_finish<<<(C + 255) / 256, 256, 0, st>>>(acc, dw, dw32, C, beta);
   return cudaGetLastError();
 }
 

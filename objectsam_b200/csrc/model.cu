@@ -129,6 +129,13 @@ struct osam_model {
   size_t ws_bytes = 0;
   void* bnws = nullptr;        // zero-filled BN / channel-sum accumulators
   size_t bnws_bytes = 0;
+  // backward: weight gradients run on a side stream, overlapping the next node's BN backward and input
+  // gradient on the caller's stream (the reference's wgrad_side, src/model.cpp:416-428); two dz buffers
+  // alternate so a node's BN backward never overwrites the dz a pending weight gradient still reads
+  __half* dz2 = nullptr;
+  void* ws_side = nullptr;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_dz[2] = {}, ev_wg[2] = {}, ev_fork = nullptr, ev_join = nullptr;
 
   // ------------------------------------------------------------------ graph construction
   MAct* act(const std::string& n, int C, int H, int W) {
@@ -342,6 +349,20 @@ struct osam_model {
     cudaFree(wconvt);
     cudaFree(ws);
     cudaFree(bnws);
+    cudaFree(dz2);
+    cudaFree(ws_side);
+    for (int i = 0; i < 2; i++) {
+      if (ev_dz[i]) cudaEventDestroy(ev_dz[i]);
+      if (ev_wg[i]) cudaEventDestroy(ev_wg[i]);
+      ev_dz[i] = ev_wg[i] = nullptr;
+    }
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (ev_join) cudaEventDestroy(ev_join);
+    if (side) cudaStreamDestroy(side);
+    ev_fork = ev_join = nullptr;
+    side = nullptr;
+    dz2 = nullptr;
+    ws_side = nullptr;
     garena = nullptr;
     zarena = nullptr;
     tarena = nullptr;
@@ -544,8 +565,20 @@ struct osam_model {
         (e = cudaMalloc(&grad32, std::max<size_t>(gn, 1) * sizeof(float))) != cudaSuccess ||
         (e = cudaMalloc(&dz, std::max<size_t>(dzn, 1) * sizeof(__half))) != cudaSuccess ||
         (e = cudaMalloc(&gw16, std::max<size_t>(gwn, 1) * sizeof(__half))) != cudaSuccess ||
-        (e = cudaMalloc(&ws, wsb)) != cudaSuccess || (e = cudaMalloc(&bnws, bnb)) != cudaSuccess)
+        (e = cudaMalloc(&ws, wsb)) != cudaSuccess || (e = cudaMalloc(&bnws, bnb)) != cudaSuccess ||
+        (e = cudaMalloc(&dz2, std::max<size_t>(dzn, 1) * sizeof(__half))) != cudaSuccess ||
+        (e = cudaMalloc(&ws_side, wsb)) != cudaSuccess)
       return model_fail(OSAM_ERR_NOMEM, "training buffers: %s", cudaGetErrorString(e));
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    if ((e = cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, lo)) != cudaSuccess)
+      return model_fail(OSAM_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
+    for (int i = 0; i < 2; i++) {
+      cudaEventCreateWithFlags(&ev_dz[i], cudaEventDisableTiming);
+      cudaEventCreateWithFlags(&ev_wg[i], cudaEventDisableTiming);
+    }
+    cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming);
     ws_bytes = wsb;
     bnws_bytes = bnb;
     cudaMemsetAsync(bnws, 0, bnb, st);
@@ -644,45 +677,61 @@ struct osam_model {
     return OSAM_OK;
   }
 
-  int wgrad_to_arena(MNode& nd, const __half* x, const __half* dy, cudaStream_t st) {
-    int rc = osam_conv_wgrad(&nd.plan, x, dy, gw16, 0.f, ws, ws_bytes, st);
-    if (rc) return rc;
-    k_f16_to_f32<<<(unsigned)std::min<size_t>((nd.g_w + 255) / 256, 4096), 256, 0, st>>>(gw16, grad32 + nd.g_off,
-                                                                                       (long long)nd.g_w);
-    return cudaGetLastError() == cudaSuccess ? OSAM_OK : OSAM_ERR_CUDA;
-  }
-
   int backward_nodes(int first, int count, cudaStream_t st) {
     if (!train) return model_fail(OSAM_ERR_INVALID, "backward before osam_model_train_init");
+    // the side stream starts after everything issued so far on the caller's stream
+    cudaEventRecord(ev_fork, st);
+    cudaStreamWaitEvent(side, ev_fork, 0);
+    bool busy[2] = {false, false};
+    int buf = 0;
     for (int i = first + count - 1; i >= first; i--) {
       MNode& nd = *nodes[i];
       int rc = OSAM_OK;
       if (nd.kind == N_CONVBN) {
         const int P = nd.plan.P, Q = nd.plan.Q, K = nd.K;
         float* T = tarena + nd.t_off;
+        __half* d = buf ? dz2 : dz;
+        if (busy[buf]) cudaStreamWaitEvent(st, ev_wg[buf], 0);  // its last weight gradient has read it
         osam_dest gd[OSAM_MAX_DEST];
         for (size_t k = 0; k < nd.dests.size(); k++)
           gd[k] = osam_dest{nd.dests[k].a->g, nd.dests[k].a->C, nd.dests[k].choff, nd.dests[k].c0, nd.dests[k].c1,
                             nd.dests[k].up};
         float* gg = grad32 + nd.g_off + nd.g_w;
         rc = osam_bn_backward(nd.z, N, P, Q, K, T + 4 * K, T + 5 * K, T + 6 * K, T + 7 * K, gd, (int)nd.dests.size(), 1,
-                              dz, gg, gg + K, 0, nd.res ? nd.res->g : nullptr, nd.res_accum ? 1 : 0, bnws, bnws_bytes,
+                              d, gg, gg + K, 0, nd.res ? nd.res->g : nullptr, nd.res_accum ? 1 : 0, bnws, bnws_bytes,
                               st);
-        if (!rc) rc = wgrad_to_arena(nd, nd.in->p, dz, st);
+        if (!rc) {
+          cudaEventRecord(ev_dz[buf], st);
+          cudaStreamWaitEvent(side, ev_dz[buf], 0);
+          rc = conv_wgrad_f32(&nd.plan, nd.in->p, d, grad32 + nd.g_off, 0.f, ws_side, ws_bytes, side);
+          cudaEventRecord(ev_wg[buf], side);
+          busy[buf] = true;
+        }
         if (!rc && nd.in != in)
-          rc = osam_conv_dgrad(&nd.plan, dz, w16 + nd.w_off, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
+          rc = osam_conv_dgrad(&nd.plan, d, w16 + nd.w_off, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
+        buf ^= 1;
       } else if (nd.kind == N_POOL) {
         rc = osam_sppf_bwd(nd.cat->p, nd.cat->g, N, nd.cat->H, nd.cat->W, nd.pc, st);
       } else {
+        // the head gradients are set by the caller before the backward and never change during it
         const long long M = (long long)N * nd.out->H * nd.out->W;
-        rc = osam_chan_sum(nd.out->g, M, nd.K, grad32 + nd.g_off + nd.g_w, 0, bnws, bnws_bytes, st);
-        if (!rc) rc = wgrad_to_arena(nd, nd.in->p, nd.out->g, st);
+        cudaEventRecord(ev_fork, st);
+        cudaStreamWaitEvent(side, ev_fork, 0);
+        rc = conv_wgrad_f32(&nd.plan, nd.in->p, nd.out->g, grad32 + nd.g_off, 0.f, ws_side, ws_bytes, side);
+        if (!rc) rc = osam_chan_sum(nd.out->g, M, nd.K, grad32 + nd.g_off + nd.g_w, 0, bnws, bnws_bytes, st);
         const __half* w = nd.kind == N_CONVT ? wconvt : w16 + nd.w_off;
         if (!rc && nd.in != in)
           rc = osam_conv_dgrad(&nd.plan, nd.out->g, w, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
       }
-      if (rc) return model_fail(rc, "%s (backward): %s", nd.name.c_str(), osam_last_error());
+      if (rc) {
+        cudaEventRecord(ev_join, side);
+        cudaStreamWaitEvent(st, ev_join, 0);
+        return model_fail(rc, "%s (backward): %s", nd.name.c_str(), osam_last_error());
+      }
     }
+    // every weight gradient of the range is complete when the caller's stream passes this point
+    cudaEventRecord(ev_join, side);
+    cudaStreamWaitEvent(st, ev_join, 0);
     return OSAM_OK;
   }
 

@@ -6,15 +6,21 @@ Tolerances, against fp64 autograd: a head's max error ≤ 2× the error that the
 points alone cause (the fp32 restatement with fp16 rounding where the reference stores fp16) + 1e-2·max;
 each parameter gradient's relL2 = ‖ours − ref‖/‖ref‖ ≤ max(2× that of the fp16-storage restatement, 1e-2).
 """
+import os
+import subprocess
+import tempfile
+
 import numpy as np
 import pytest
 import torch
 
 from objectsam_b200.model import Model
-from oracle import yolo_params, yolo_ref
+from oracle import fsow, yolo_params, yolo_ref
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_TRAIN = os.path.join(ROOT, "oracle", "_ref", "ref_train")
 
 
 def _setup(N, S, seed):
@@ -101,3 +107,43 @@ def test_train_backward_in_buckets_equals_whole(cuda_lib):
     torch.cuda.synchronize()
     again = m.grad_arena()
     assert torch.norm(again - whole) <= 1e-5 * torch.norm(whole)
+
+
+@pytest.mark.skipif(not os.path.exists(REF_TRAIN), reason="oracle/_ref/ref_train not built (make -C oracle)")
+def test_train_pass_matches_reference_cudnn(cuda_lib):
+    """The same weights, images and head gradients through the reference's own training pass (its cuDNN fp16
+    build: Model::forward(true) + backward); both are measured against fp64 autograd and this build's error
+    may be at most twice the reference's (or 1e-2) on every head and every parameter gradient."""
+    N, S = 2, 256
+    m, w, imgs = _setup(N, S, 3)
+    m.forward_train(0.03)
+    G = _head_grads(m, S, 9)
+    m.backward()
+    torch.cuda.synchronize()
+    ins = {"images": imgs.astype(np.float32)}
+    ins.update({f"grad.{k}": v.numpy() for k, v in G.items()})
+    with tempfile.TemporaryDirectory() as td:
+        fsow.save(os.path.join(td, "w.fsow"), w)
+        fsow.save(os.path.join(td, "in.fsow"), ins)
+        subprocess.run([REF_TRAIN, os.path.join(td, "w.fsow"), os.path.join(td, "in.fsow"), os.path.join(td, "o.fsow")],
+                       check=True, timeout=600)
+        ref = fsow.load(os.path.join(td, "o.fsow"))
+    o64, g64 = _oracle(w, imgs, G, fp16=False)
+    for key, kind in (("box", 0), ("cls", 1), ("coef", 2)):
+        for l in range(3):
+            y = m.head(kind, l).double().cpu().permute(0, 3, 1, 2)
+            rr = torch.from_numpy(ref[f"out.{key}{l}"]).double().permute(0, 3, 1, 2)
+            r = o64[key][l]
+            e, eref = (y - r).abs().max().item(), (rr - r).abs().max().item()
+            assert e <= 2 * eref + 1e-2 * r.abs().max().item(), f"{key}{l}: max err {e:.3e}, reference {eref:.3e}"
+    worst = []
+    for name, want in g64.items():
+        got = m.get_grad(name, want.shape).astype(np.float64)
+        theirs = ref["grad." + name].astype(np.float64)
+        nrm = np.linalg.norm(want) + 1e-30
+        rel, rref = np.linalg.norm(got - want) / nrm, np.linalg.norm(theirs - want) / nrm
+        worst.append((rel / max(rref, 1e-12), rel, rref, name))
+        assert rel <= max(2 * rref, 1e-2), f"{name}: relL2 {rel:.3e}, reference {rref:.3e}"
+    worst.sort(reverse=True)
+    print(f"{len(worst)} gradients; largest ratio to the reference's error {worst[0][0]:.2f} ({worst[0][3]}: "
+          f"{worst[0][1]:.3e} vs {worst[0][2]:.3e})")
