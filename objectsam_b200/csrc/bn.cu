@@ -126,7 +126,8 @@ struct RedArgs {
 //   RED_STATS: Σ(z−K), Σ(z−K)² with K = running mean (shifted sums: no cancellation when |mean| ≫ std)
 //   RED_BWD:   Σg, Σg·x̂ with g = dA·silu'(y), y = scale·z + shift, x̂ = (z − mean)·istd
 //   RED_SUM:   Σz
-template <int MODE, int U>
+// SIMPLE (RED_BWD): one destination, not upsampled, all channels — dA is one 16-byte load per row, kept raw.
+template <int MODE, int U, bool SIMPLE = false>
 __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(const RedArgs P) {
   extern __shared__ float2 bn_red[];  // [rowlanes][C]
   __shared__ unsigned s_last;
@@ -152,18 +153,21 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
       for (int i = 0; i < 8; i++) k3[i] = -mu[i] * k2[i];
     }
     for (long long r = r0 + rl; r < r1; r += (long long)U * RL) {
-      uint4 zr[U];
-      float dA[U][8];
+      uint4 zr[U], gr[SIMPLE ? U : 1];
+      float dA[SIMPLE ? 1 : U][8];
 #pragma unroll
       for (int u = 0; u < U; u++) {
         const long long rr = r + (long long)u * RL;
-        if (rr < r1) zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
+        if (rr < r1) {
+          zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
+          if (SIMPLE) gr[u] = *reinterpret_cast<const uint4*>(P.dl[0].g + rr * P.dl[0].ctot + P.dl[0].choff + c);
+        }
       }
-      if (MODE == RED_BWD) {
+      if (MODE == RED_BWD && !SIMPLE) {
 #pragma unroll
         for (int u = 0; u < U; u++) {
           const long long rr = r + (long long)u * RL;
-          if (rr < r1) gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[u]);
+          if (rr < r1) gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[SIMPLE ? 0 : u]);
         }
       }
 #pragma unroll
@@ -171,6 +175,7 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
         if (r + (long long)u * RL >= r1) break;
         float v[8];
         unpack8h(zr[u], v);
+        if (SIMPLE) unpack8h(gr[u], dA[0]);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           if (MODE == RED_STATS) {
@@ -178,7 +183,7 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
             a[i] += d;
             b[i] = fmaf(d, d, b[i]);
           } else if (MODE == RED_BWD) {
-            float g = dA[u][i];
+            float g = dA[SIMPLE ? 0 : u][i];
             if (P.act) {
               const float y = fmaf(k0[i], v[i], k1[i]), s = sigmoid_fast(y);
               g *= s * fmaf(y, 1.f - s, 1.f);
@@ -337,8 +342,8 @@ struct BwdArgs {
 };
 
 // dz = scale·(g − mean(g) − x̂·mean(g·x̂)); res_grad (=|+=) dA (reference k_bwd_apply, src/bn.cu:240-270).
-template <int U>
-__global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
+template <int U, bool SIMPLE = false>
+__global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
   const int C = P.C, V = C >> 3, RL = P.rowlanes;
   const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
   if (rl >= RL) return;
@@ -361,14 +366,17 @@ __global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
     }
   }
   for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
-    uint4 zr[U];
-    float dA[U][8];
+    uint4 zr[U], gr[SIMPLE ? U : 1];
+    float dAf[SIMPLE ? 1 : U][8];
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const long long rr = r - (long long)u * RL;
       if (rr >= r0) {
         zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
-        gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[u]);
+        if (SIMPLE)
+          gr[u] = *reinterpret_cast<const uint4*>(P.dl[0].g + rr * P.dl[0].ctot + P.dl[0].choff + c);
+        else
+          gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dAf[SIMPLE ? 0 : u]);
       }
     }
 #pragma unroll
@@ -376,15 +384,17 @@ __global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
       const long long rr = r - (long long)u * RL;
       if (rr < r0) break;
       const long long off = rr * C + c;
+      float (&dA)[8] = dAf[SIMPLE ? 0 : u];
+      if (SIMPLE) unpack8h(gr[u], dA);
       if (P.res_grad) {
         float t[8];
         if (P.res_accum) {
           ld8h(P.res_grad + off, t);
 #pragma unroll
-          for (int i = 0; i < 8; i++) t[i] += dA[u][i];
+          for (int i = 0; i < 8; i++) t[i] += dA[i];
         } else {
 #pragma unroll
-          for (int i = 0; i < 8; i++) t[i] = dA[u][i];
+          for (int i = 0; i < 8; i++) t[i] = dA[i];
         }
         st8h(P.res_grad + off, t);
       }
@@ -392,7 +402,7 @@ __global__ void __launch_bounds__(kBnT) k_bn_bwd_apply(const BwdArgs P) {
       unpack8h(zr[u], v);
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        float g = dA[u][i];
+        float g = dA[i];
         if (P.act) {
           const float y = fmaf(sc[i], v[i], sh[i]), s = sigmoid_fast(y);
           g *= s * fmaf(y, 1.f - s, 1.f);
@@ -477,10 +487,10 @@ __global__ void k_bn_eval_scale(int C, const float* g, const float* b, const flo
 }
 
 // ------------------------------------------------------------------ host side
-constexpr int kUStats = 4, kUBwd = 2, kUApply = 4, kUBwdApply = 2;
+constexpr int kUStats = 4, kUBwd = 2, kUApply = 4, kUBwdApply = 2, kUBwdSimple = 4;
 
 int g_sms_cache[64] = {};
-int g_occ_cache[64][2] = {};
+int g_occ_cache[64][3] = {};
 
 template <class K>
 int occupancy(K kernel, size_t smem) {
@@ -489,8 +499,8 @@ int occupancy(K kernel, size_t smem) {
 }
 
 // CTAs that are resident at once for a pass pair — mode 0: statistics (or channel sums) and the forward
-// apply; mode 1: the backward sums and the backward apply — so that both kernels of a pair run as one wave
-// over the same row chunks.
+// apply; mode 1: the backward sums and the backward apply; mode 2: the same for a single plain destination —
+// so that both kernels of a pair run as one wave over the same row chunks.
 int resident_ctas(int mode) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 2;
@@ -505,9 +515,12 @@ int resident_ctas(int mode) {
     if (mode == 0) {
       a = occupancy(k_bn_reduce<RED_STATS, kUStats>, smem);
       b = occupancy(k_bn_apply<kUApply>, 0);
-    } else {
+    } else if (mode == 1) {
       a = occupancy(k_bn_reduce<RED_BWD, kUBwd>, smem);
       b = occupancy(k_bn_bwd_apply<kUBwdApply>, 0);
+    } else {
+      a = occupancy(k_bn_reduce<RED_BWD, kUBwdSimple, true>, smem);
+      b = occupancy(k_bn_bwd_apply<kUBwdSimple, true>, 0);
     }
     g_occ_cache[dev][mode] = a < b ? a : b;
   }
@@ -655,7 +668,9 @@ int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mea
   if (n_dest < 1 || n_dest > OSAM_MAX_DEST || !grad_dests) return bad(OSAM_ERR_INVALID, "bn_backward: 1..4 dests");
   if (!ws || ws_bytes < bn_ws_bytes(C) || !al16(ws)) return bad(OSAM_ERR_INVALID, "bn_backward: workspace");
   const long long M = (long long)N * H * W;
-  const Chunking k = chunking(M, C, 1);
+  const bool simple = n_dest == 1 && grad_dests[0].up == 1 && grad_dests[0].c0 == 0 &&
+                      (grad_dests[0].c1 == 0 || grad_dests[0].c1 == C);
+  const Chunking k = chunking(M, C, simple ? 2 : 1);
   const BnWs w = bn_ws(ws, C);
   RedArgs P{};
   BwdArgs B{};
@@ -688,6 +703,12 @@ int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mea
   B.res_grad = static_cast<__half*>(res_grad);
   B.res_accum = res_accum ? 1 : 0;
   const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
+  if (simple) {
+    k_bn_reduce<RED_BWD, kUBwdSimple, true><<<k.nblk, kBnT, smem, st>>>(P);
+    if ((rc = launched("osam_bn_backward (sums)"))) return rc;
+    k_bn_bwd_apply<kUBwdSimple, true><<<k.nblk, kBnT, 0, st>>>(B);
+    return launched("osam_bn_backward (apply)");
+  }
   k_bn_reduce<RED_BWD, kUBwd><<<k.nblk, kBnT, smem, st>>>(P);
   if ((rc = launched("osam_bn_backward (sums)"))) return rc;
   k_bn_bwd_apply<kUBwdApply><<<k.nblk, kBnT, 0, st>>>(B);
