@@ -679,6 +679,45 @@ static size_t dgrad_workspace_bytes(const osam_conv_plan* p) {
 
 int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void* dx, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream) {
+  return conv_dgrad_ex(p, dz, w, dx, beta, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // extern "C"
+
+namespace osam {
+size_t dgrad_prelaid_bytes(const osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  if (!p || p->dg_direct || p->n_dg == 0) return 0;
+  if (p->dg_chunk) return ((size_t)g.C * g.R * g.S * g.K * 2 + 255) & ~size_t(255);
+  return dgrad_workspace_bytes(p);
+}
+
+int dgrad_jobs(const osam_conv_plan* p, const __half* w, __half* prelaid, DgradJob* out) {
+  if (!p || p->dg_direct || p->n_dg == 0) return 0;
+  const osam_conv_geom& g = p->g;
+  const int n = p->dg_chunk ? 1 : p->n_dg;
+  for (int i = 0; i < n; i++) {
+    DgradJob& j = out[i];
+    j.w = w;
+    j.dst = prelaid + p->dg_woff[i];
+    j.K = g.K;
+    j.R = g.R;
+    j.S = g.S;
+    j.C = g.C;
+    j.Rs = p->dg_chunk ? g.R : p->dg_R[i];
+    j.Ss = p->dg_chunk ? g.S : p->dg_S[i];
+    for (int q = 0; q < 8; q++) {
+      j.r[q] = q < j.Rs ? p->dg_rmap[i][q] : 0;
+      j.s[q] = q < j.Ss ? p->dg_smap[i][q] : 0;
+    }
+    j.n = (long long)g.C * j.Rs * j.Ss * g.K;
+  }
+  return n;
+}
+
+int conv_dgrad_ex(const osam_conv_plan* p, const void* dz, const void* w, void* dx, float beta, void* ws,
+                  size_t ws_bytes, cudaStream_t st_in, const __half* prelaid) {
+  const osam_stream_t stream = reinterpret_cast<osam_stream_t>(st_in);
   if (!p || !dz || !w || !dx) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g1 = p->g;
   if (!p->transposed && g1.K == 1 && g1.R == 1 && g1.S == 1 && g1.stride == 1 && g1.pad == 0 && g1.C % 8 == 0) {
@@ -689,7 +728,7 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
     return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_dgrad (K = 1) launch");
   }
   if (p->n_dg == 0) return fail(OSAM_ERR_UNSUPPORTED, "dgrad: geometry not supported (stride, kernel or channels)");
-  const size_t need = dgrad_workspace_bytes(p);
+  const size_t need = prelaid ? 0 : dgrad_workspace_bytes(p);
   if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)))
     return fail(OSAM_ERR_INVALID, "dgrad needs %zu workspace bytes (256-byte aligned)", need);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -701,10 +740,11 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
     return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_dgrad (transposed) launch");
   }
   const osam_conv_geom& g = p->g;
-  __half* wsub = static_cast<__half*>(ws);
+  __half* wsub = prelaid ? const_cast<__half*>(prelaid) : static_cast<__half*>(ws);
   if (p->dg_chunk) {  // one weight re-layout, then one sub-conv per slice of dx's channels
-    cudaError_t e = launch_dgrad_weights(static_cast<const __half*>(w), wsub, g.K, g.R, g.S, g.C, g.R, g.S,
-                                         p->dg_rmap[0], p->dg_smap[0], st);
+    cudaError_t e = prelaid ? cudaSuccess
+                            : launch_dgrad_weights(static_cast<const __half*>(w), wsub, g.K, g.R, g.S, g.C, g.R, g.S,
+                                                   p->dg_rmap[0], p->dg_smap[0], st);
     if (e != cudaSuccess) return cuda_fail(e, "osam_conv_dgrad weight re-layout");
     for (int i = 0; i < p->n_dg; i++) {
       ConvLaunch L;
@@ -717,7 +757,7 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
     }
     return OSAM_OK;
   }
-  for (int i = 0; i < p->n_dg; i++) {
+  for (int i = 0; i < p->n_dg && !prelaid; i++) {
     cudaError_t e = launch_dgrad_weights(static_cast<const __half*>(w), wsub + p->dg_woff[i], g.K, g.R, g.S, g.C,
                                          p->dg_R[i], p->dg_S[i], p->dg_rmap[i], p->dg_smap[i], st);
     if (e != cudaSuccess) return cuda_fail(e, "osam_conv_dgrad weight re-layout");
@@ -732,6 +772,10 @@ int osam_conv_dgrad(const osam_conv_plan* p, const void* dz, const void* w, void
   }
   return OSAM_OK;
 }
+
+}  // namespace osam
+
+extern "C" {
 
 static size_t wgrad_workspace_bytes(const osam_conv_plan* p) {
   const osam_conv_geom& g = p->g;
@@ -752,11 +796,11 @@ static int sm_count() {
 // Weight gradient of a small-C plan (R·S·C ≤ 32, the RGB stem): patch-gather tcgen05 kernel over runs of
 // 128 consecutive output pixels (conv_wgrad.cu), one CTA pair per SM.
 static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
-                      void* ws, size_t ws_bytes, osam_stream_t stream) {
+                      void* ws, size_t ws_bytes, osam_stream_t stream, bool direct) {
   const osam_conv_geom& g = p->g;
   if (g.K != 32 && g.K != 64) return fail(OSAM_ERR_UNSUPPORTED, "small-C wgrad: K must be 32 or 64 (K=%d)", g.K);
   const size_t need = wgrad_workspace_bytes(p);
-  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255))
+  if (!direct && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)))
     return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need);
   if ((reinterpret_cast<uintptr_t>(dz) & 15) || (reinterpret_cast<uintptr_t>(x) & 1))
     return fail(OSAM_ERR_INVALID, "wgrad: dz must be 16-byte aligned, x 2-byte aligned");
@@ -770,7 +814,8 @@ static int wgrad_stem(const osam_conv_plan* p, const void* x, const void* dz, vo
   if (!d.err) return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
   L.mode = A_STEM;
   L.xp = static_cast<const __half*>(x);
-  L.acc = static_cast<float*>(ws);
+  L.direct = direct;
+  L.acc = direct ? dw32 : static_cast<float*>(ws);
   L.dw = static_cast<__half*>(dw);
   L.dw32 = dw32;
   L.n_out = (long long)g.K * g.R * g.S * g.C;
@@ -800,7 +845,7 @@ size_t osam_conv_workspace_size(const osam_conv_plan* p) {
 }
 
 static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
-                      void* ws, size_t ws_bytes, osam_stream_t stream);
+                      void* ws, size_t ws_bytes, osam_stream_t stream, bool direct = false);
 
 int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float beta, void* ws,
                     size_t ws_bytes, osam_stream_t stream) {
@@ -812,38 +857,40 @@ int osam_conv_wgrad(const osam_conv_plan* p, const void* x, const void* dz, void
 
 namespace osam {
 int conv_wgrad_f32(const osam_conv_plan* p, const void* x, const void* dz, float* dw32, float beta, void* ws,
-                   size_t ws_bytes, cudaStream_t st) {
+                   size_t ws_bytes, cudaStream_t st, bool direct) {
   if (!dw32) return fail(OSAM_ERR_INVALID, "NULL fp32 weight-gradient output");
-  return wgrad_impl(p, x, dz, nullptr, dw32, beta, ws, ws_bytes, reinterpret_cast<osam_stream_t>(st));
+  if (direct && beta != 0.f) return fail(OSAM_ERR_INVALID, "direct weight gradient with beta");
+  return wgrad_impl(p, x, dz, nullptr, dw32, beta, ws, ws_bytes, reinterpret_cast<osam_stream_t>(st), direct);
 }
 }  // namespace osam
 
 extern "C" {
 
 static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
-                      void* ws, size_t ws_bytes, osam_stream_t stream) {
+                      void* ws, size_t ws_bytes, osam_stream_t stream, bool direct) {
   if (!p || !x || !dz || (!dw && !dw32)) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
   if (p->transposed) {
     // dW[c][r][s][k] = Σ_{p,q} x[p][q][c]·dy[2p+r][2q+s][k]: the weight gradient of the stride-2 2×2 conv
     // dg[0] (input dy, output x-shaped) with x in the role of its output gradient
     if (!p->dg_direct) return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed conv other than kernel = stride = 2");
-    return wgrad_impl(p->dg[0], dz, x, dw, dw32, beta, ws, ws_bytes, stream);
+    return wgrad_impl(p->dg[0], dz, x, dw, dw32, beta, ws, ws_bytes, stream, direct);
   }
-  if (p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, dw32, beta, ws, ws_bytes, stream);
+  if (p->mode == A_STEM) return wgrad_stem(p, x, dz, dw, dw32, beta, ws, ws_bytes, stream, direct);
   if (g.K == 1 && g.R == 1 && g.S == 1 && g.stride == 1 && g.pad == 0 && g.C % 8 == 0) {
     const size_t need1 = wgrad_workspace_bytes(p);
-    if (!ws || ws_bytes < need1 || (reinterpret_cast<uintptr_t>(ws) & 255))
+    if (!direct && (!ws || ws_bytes < need1 || (reinterpret_cast<uintptr_t>(ws) & 255)))
       return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need1);
     if (reinterpret_cast<uintptr_t>(x) & 15) return fail(OSAM_ERR_INVALID, "wgrad: x must be 16-byte aligned");
     cudaError_t e = launch_wgrad_k1(static_cast<const __half*>(x), static_cast<const __half*>(dz), static_cast<float*>(ws),
-                                    static_cast<__half*>(dw), dw32, p->M, g.C, beta, reinterpret_cast<cudaStream_t>(stream));
+                                    static_cast<__half*>(dw), dw32, p->M, g.C, beta, direct,
+                                    reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_wgrad (K = 1) launch");
   }
   if (p->transposed || (p->mode != A_S1 && p->mode != A_S2) || g.C % 32 || g.K % 32)
     return fail(OSAM_ERR_UNSUPPORTED, "wgrad: transposed, small-C or non-32-multiple channels");
   const size_t need = wgrad_workspace_bytes(p);
-  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255))
+  if (!direct && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)))
     return fail(OSAM_ERR_INVALID, "wgrad needs %zu workspace bytes (256-byte aligned)", need);
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dz)) & 15)
     return fail(OSAM_ERR_INVALID, "wgrad: operands must be 16-byte aligned");
@@ -860,7 +907,8 @@ static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, vo
   L.BN = g.C <= 32 ? 32 : (g.C <= 64 ? 64 : (g.C <= 128 ? 128 : 256));
   if (L.BB == 32 && L.BN != 32) L.BB = 64;  // C = 96, 160, …: 64-channel boxes, the tail zero-filled
   L.mode = p->mode;
-  L.acc = static_cast<float*>(ws);
+  L.direct = direct;
+  L.acc = direct ? dw32 : static_cast<float*>(ws);
   L.dw = static_cast<__half*>(dw);
   L.dw32 = dw32;
   L.n_out = (long long)g.K * g.R * g.S * g.C;

@@ -95,6 +95,7 @@ struct WgradLaunch {
   float* acc;           // fp32 KRSC accumulator (workspace), zeroed by the launch
   __half* dw;           // fp16 KRSC result
   float* dw32;          // or, when non-null, the fp32 result (dw unused)
+  bool direct;          // dw32 is zero already: the kernels add into it (acc = dw32, no zeroing, no finish pass)
   long long n_out;      // K·R·S·C
   float beta;
   int AB, BB, BN;       // dz / x box channels (32 or 64), GEMM N block
@@ -107,10 +108,27 @@ cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st);
 cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long long npix, int C, float beta,
                             cudaStream_t st);
 cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, float* dw32, long long npix,
-                            int C, float beta, cudaStream_t st);
+                            int C, float beta, bool direct, cudaStream_t st);
 // osam_conv_wgrad with the result in fp32 (dw32, + beta·dw32) instead of fp16: the training path's gradient arena.
+// direct = true: dw32 has been zeroed by the caller and the kernels add into it (no workspace, no extra passes).
 int conv_wgrad_f32(const osam_conv_plan* plan, const void* x, const void* dz, float* dw32, float beta, void* ws,
-                   size_t ws_bytes, cudaStream_t st);
+                   size_t ws_bytes, cudaStream_t st, bool direct = false);
+// osam_conv_dgrad with the sub-convs' re-laid-out weights already in `prelaid` (dgrad_prelaid_bytes(plan) bytes,
+// written by launch_dgrad_weights_batched); prelaid = nullptr re-lays them out into ws first.
+int conv_dgrad_ex(const osam_conv_plan* plan, const void* dz, const void* w, void* dx, float beta, void* ws,
+                  size_t ws_bytes, cudaStream_t st, const __half* prelaid);
+size_t dgrad_prelaid_bytes(const osam_conv_plan* plan);
+struct DgradJob {
+  const __half* w;
+  __half* dst;
+  int K, R, S, C, Rs, Ss;
+  int r[8], s[8];
+  long long n;
+};
+// All of a model's dgrad weight re-layouts (jobs in device memory) in one launch.
+cudaError_t launch_dgrad_weights_batched(const DgradJob* jobs, int njobs, cudaStream_t st);
+// The jobs that produce `prelaid` for one plan from its KRSC weights (at most 4; returns the count).
+int dgrad_jobs(const osam_conv_plan* plan, const __half* w, __half* prelaid, DgradJob* out);
 
 // Fills `L` (tensor maps, tiling, epilogue) for one call.  Returns an OSAM_* code.
 // err_word: device word the kernels report timeouts to (nullptr = the library's per-device word).

@@ -439,7 +439,7 @@ static cudaError_t wgrad_stem_launch(const WgradLaunch& L, cudaStream_t st) {
 }
 
 cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(L.acc, 0, (size_t)L.n_out * 4, st);
+  cudaError_t e = L.direct ? cudaSuccess : cudaMemsetAsync(L.acc, 0, (size_t)L.n_out * 4, st);
   if (e != cudaSuccess) return e;
   const int AB = L.AB, BB = L.BB, BN = L.BN;
   if (L.mode == A_STEM) {
@@ -467,7 +467,7 @@ cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
   } else {
     return cudaErrorInvalidValue;
   }
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || L.direct) return e;
   int grid = (int)((L.n_out + 255) / 256);
   if (grid > 4096) grid = 4096;
   k_wgrad_finish<<<grid, 256, 0, st>>>(L.acc, L.dw, L.dw32, L.n_out, L.beta);
@@ -488,15 +488,16 @@ cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long 
 }
 
 cudaError_t launch_wgrad_k1(const __half* x, const __half* dy, float* acc, __half* dw, float* dw32, long long npix,
-                            int C, float beta, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(acc, 0, (size_t)C * sizeof(float), st);
+                            int C, float beta, bool direct, cudaStream_t st) {
+  if (direct) acc = dw32;
+  cudaError_t e = direct ? cudaSuccess : cudaMemsetAsync(acc, 0, (size_t)C * sizeof(float), st);
   if (e != cudaSuccess) return e;
   const int RL = 256 / (C / 8);
   long long rows = (npix + 148 * 4 - 1) / (148 * 4);
   if (rows < 4LL * RL) rows = 4LL * RL;
   const long long grid = (npix + rows - 1) / rows;
   k_wgrad_k1<<<(unsigned)grid, 256, (size_t)RL * C * sizeof(float), st>>>(x, dy, acc, npix, C, rows);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = cudaGetLastError()) != cudaSuccess || direct) return e;
   k_wgrad_finish<<<(C + 255) / 256, 256, 0, st>>>(acc, dw, dw32, C, beta);
   return cudaGetLastError();
 }

@@ -36,4 +36,23 @@ cudaError_t launch_dgrad_weights(const __half* w, __half* dst, int K, int R, int
   return cudaGetLastError();
 }
 
+__global__ void k_dgrad_weights_batched(const DgradJob* __restrict__ jobs) {
+  const DgradJob& j = jobs[blockIdx.y];
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < j.n; i += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(i % j.K);
+    long long t = i / j.K;
+    const int s2 = (int)(t % j.Ss);
+    t /= j.Ss;
+    const int r2 = (int)(t % j.Rs);
+    const int c = (int)(t / j.Rs);
+    j.dst[i] = j.w[(((long long)k * j.R + j.r[r2]) * j.S + j.s[s2]) * j.C + c];
+  }
+}
+
+cudaError_t launch_dgrad_weights_batched(const DgradJob* jobs, int njobs, cudaStream_t st) {
+  if (njobs <= 0) return cudaSuccess;
+  k_dgrad_weights_batched<<<dim3(64, njobs), 256, 0, st>>>(jobs);
+  return cudaGetLastError();
+}
+
 }  // namespace osam

@@ -62,6 +62,7 @@ struct MNode {
   __half* z = nullptr;       // CONVBN: conv output before BN (fp16, as the reference stores it)
   size_t t_off = 0;          // CONVBN: fp32 train arena: γ, β, running μ, running σ², mean, istd, scale, shift
   size_t g_off = 0, g_w = 0;  // fp32 parameter-gradient arena: weights (g_w elements) then γ, β or the bias
+  __half* pre_w = nullptr;     // this node's re-laid-out dgrad weights (nullptr: none needed)
   bool res_accum = false, dgrad_accum = false;
 };
 
@@ -134,6 +135,10 @@ struct osam_model {
   // alternate so a node's BN backward never overwrites the dz a pending weight gradient still reads
   __half* dz2 = nullptr;
   void* ws_side = nullptr;
+  // the input-gradient convs' re-laid-out weights, all nodes, refreshed by one batched launch per step
+  __half* prelaid = nullptr;
+  DgradJob* jobs = nullptr;
+  int njobs = 0;
   cudaStream_t side = nullptr;
   cudaEvent_t ev_dz[2] = {}, ev_wg[2] = {}, ev_fork = nullptr, ev_join = nullptr;
 
@@ -351,6 +356,11 @@ struct osam_model {
     cudaFree(bnws);
     cudaFree(dz2);
     cudaFree(ws_side);
+    cudaFree(prelaid);
+    cudaFree(jobs);
+    prelaid = nullptr;
+    jobs = nullptr;
+    njobs = 0;
     for (int i = 0; i < 2; i++) {
       if (ev_dz[i]) cudaEventDestroy(ev_dz[i]);
       if (ev_wg[i]) cudaEventDestroy(ev_wg[i]);
@@ -579,6 +589,34 @@ struct osam_model {
     }
     cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming);
     cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming);
+    {
+      size_t pb = 0;
+      std::vector<size_t> poff(nodes.size(), 0);
+      for (size_t i = 0; i < nodes.size(); i++) {
+        MNode& nd = *nodes[i];
+        if (nd.kind == N_POOL || nd.kind == N_CONVT) continue;
+        const size_t b = dgrad_prelaid_bytes(&nd.plan);
+        poff[i] = pb;
+        pb += b;
+      }
+      if (pb && (e = cudaMalloc(&prelaid, pb)) != cudaSuccess)
+        return model_fail(OSAM_ERR_NOMEM, "dgrad weights: %s", cudaGetErrorString(e));
+      std::vector<DgradJob> jh;
+      for (size_t i = 0; i < nodes.size(); i++) {
+        MNode& nd = *nodes[i];
+        if (nd.kind == N_POOL || nd.kind == N_CONVT || !dgrad_prelaid_bytes(&nd.plan)) continue;
+        nd.pre_w = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(prelaid) + poff[i]);
+        DgradJob j[4];
+        const int nj = dgrad_jobs(&nd.plan, w16 + nd.w_off, nd.pre_w, j);
+        for (int q = 0; q < nj; q++) jh.push_back(j[q]);
+      }
+      njobs = (int)jh.size();
+      if (njobs) {
+        if ((e = cudaMalloc(&jobs, jh.size() * sizeof(DgradJob))) != cudaSuccess)
+          return model_fail(OSAM_ERR_NOMEM, "dgrad jobs");
+        cudaMemcpy(jobs, jh.data(), jh.size() * sizeof(DgradJob), cudaMemcpyHostToDevice);
+      }
+    }
     ws_bytes = wsb;
     bnws_bytes = bnb;
     cudaMemsetAsync(bnws, 0, bnb, st);
@@ -674,11 +712,25 @@ struct osam_model {
       }
       if (rc) return model_fail(rc, "%s (train forward): %s", nd.name.c_str(), osam_last_error());
     }
+    // this step's weights, re-laid out once for every input-gradient conv of the coming backward
+    if (launch_dgrad_weights_batched(jobs, njobs, st) != cudaSuccess)
+      return model_fail(OSAM_ERR_CUDA, "dgrad weight re-layout");
     return OSAM_OK;
   }
 
   int backward_nodes(int first, int count, cudaStream_t st) {
     if (!train) return model_fail(OSAM_ERR_INVALID, "backward before osam_model_train_init");
+    // the weight gradients of the range are accumulated straight into the arena: zero it first
+    {
+      size_t lo = grad32_n, hi = 0;
+      for (int i = first; i < first + count; i++) {
+        const MNode& nd = *nodes[i];
+        if (nd.kind == N_POOL) continue;
+        lo = std::min(lo, nd.g_off);
+        hi = std::max(hi, nd.g_off + nd.g_w);
+      }
+      if (hi > lo) cudaMemsetAsync(grad32 + lo, 0, (hi - lo) * sizeof(float), st);
+    }
     // the side stream starts after everything issued so far on the caller's stream
     cudaEventRecord(ev_fork, st);
     cudaStreamWaitEvent(side, ev_fork, 0);
@@ -703,12 +755,13 @@ struct osam_model {
         if (!rc) {
           cudaEventRecord(ev_dz[buf], st);
           cudaStreamWaitEvent(side, ev_dz[buf], 0);
-          rc = conv_wgrad_f32(&nd.plan, nd.in->p, d, grad32 + nd.g_off, 0.f, ws_side, ws_bytes, side);
+          rc = conv_wgrad_f32(&nd.plan, nd.in->p, d, grad32 + nd.g_off, 0.f, ws_side, ws_bytes, side, true);
           cudaEventRecord(ev_wg[buf], side);
           busy[buf] = true;
         }
         if (!rc && nd.in != in)
-          rc = osam_conv_dgrad(&nd.plan, d, w16 + nd.w_off, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
+          rc = conv_dgrad_ex(&nd.plan, d, w16 + nd.w_off, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st,
+                             nd.pre_w);
         buf ^= 1;
       } else if (nd.kind == N_POOL) {
         rc = osam_sppf_bwd(nd.cat->p, nd.cat->g, N, nd.cat->H, nd.cat->W, nd.pc, st);
@@ -717,11 +770,11 @@ struct osam_model {
         const long long M = (long long)N * nd.out->H * nd.out->W;
         cudaEventRecord(ev_fork, st);
         cudaStreamWaitEvent(side, ev_fork, 0);
-        rc = conv_wgrad_f32(&nd.plan, nd.in->p, nd.out->g, grad32 + nd.g_off, 0.f, ws_side, ws_bytes, side);
+        rc = conv_wgrad_f32(&nd.plan, nd.in->p, nd.out->g, grad32 + nd.g_off, 0.f, ws_side, ws_bytes, side, true);
         if (!rc) rc = osam_chan_sum(nd.out->g, M, nd.K, grad32 + nd.g_off + nd.g_w, 0, bnws, bnws_bytes, st);
         const __half* w = nd.kind == N_CONVT ? wconvt : w16 + nd.w_off;
         if (!rc && nd.in != in)
-          rc = osam_conv_dgrad(&nd.plan, nd.out->g, w, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st);
+          rc = conv_dgrad_ex(&nd.plan, nd.out->g, w, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st, nd.pre_w);
       }
       if (rc) {
         cudaEventRecord(ev_join, side);
