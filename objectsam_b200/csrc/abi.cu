@@ -392,6 +392,51 @@ static int fill_dest(const osam_dest& s, int kout, DestDev* d, int transposed) {
   return OSAM_OK;
 }
 
+// Planner switches, read at every plan preparation (never in graph replays); the tests force each form.
+static int env_switch(const char* name) {
+  const char* v = getenv(name);
+  return (v && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
+}
+
+// CTA pairs with 2-SM UMMAs for the per-tap kernel (conv_fprop.cu; OSAM_FPROP_PAIR=0|1 forces it).
+// Measured on B200 at the network's shapes (batch 64): 3–4 % faster for the stride-2 convs with ≥ 128
+// output channels and ≥ 600 tiles; slower or even elsewhere (1×1: 5–40 %, small grids: 2–5 %).  A pair
+// sums every output in the same order as a single CTA (same K sequence), so the choice may depend on N.
+static int choose_pair(const osam_conv_plan* p, int mode) {
+  if (mode != A_GEMM && mode != A_S1 && mode != A_S2) return 0;
+  if ((p->BN / 2) * p->BK * 2 % 1024 != 0) return 0;  // each CTA's half of B must fill whole 1 KB atoms
+  const int f = env_switch("OSAM_FPROP_PAIR");
+  if (f >= 0) return f;
+  return mode == A_S2 && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
+}
+
+// Column-shifted windows (A_W3) for a 3×3/s1/p1 conv; tiles of th × tw = 128 pixels of one image, tw ∈
+// {8, 16}, whichever pads the image less.  Chosen from the per-image padding alone (the window form sums
+// in another order than the per-tap form, so a layer must take the same form at every batch size):
+// ≤ 5 % padding, or ≤ 25 % when C ≤ 64 or more than 128 output channels (measured on B200: at 40 × 40,
+// 20 % padding, the windows win by 6–20 % there and lose 3 % at 128 → 128).  OSAM_FPROP_W3=0|1 forces
+// it (1: whenever the geometry allows).  Returns tw, or 0.
+static int choose_w3(const osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  if (p->transposed || p->mode != A_S1 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1) return 0;
+  const int f = env_switch("OSAM_FPROP_W3");
+  if (f == 0) return 0;
+  int best_tw = 0;
+  long long best = 0;
+  for (int tw = 8; tw <= 16; tw *= 2) {
+    const long long tiles = cdivll(p->Q, tw) * cdivll(p->P, 128 / tw);  // per image
+    if (best_tw == 0 || tiles < best) {
+      best = tiles;
+      best_tw = tw;
+    }
+  }
+  if (f == 1) return best_tw;
+  const long long padded = best * 128 * 100, area = (long long)p->P * p->Q;
+  if (padded <= area * 105) return best_tw;
+  if (padded <= area * 125 && (g.C <= 64 || p->BN > 128)) return best_tw;
+  return 0;
+}
+
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
                  void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word, int par, int y_ctot,
                  int y_choff) {
@@ -401,6 +446,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   L->BK = p->BK;
   L->BN = p->BN;
   L->mode = p->mode;
+  L->pair = 0;
   L->grid = p->tiles_m * p->ntn;
   ConvDev& d = L->d;
   d.N = g.N; d.H = g.H; d.W = g.W; d.C = g.C; d.K = g.K;
@@ -485,6 +531,19 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     d.tiles_m = p->win_tiles;
     d.ntn = 1;
     L->grid = p->win_tiles;
+  }
+  if (L->mode == A_S1) {
+    const int tw = choose_w3(p);
+    if (tw) {
+      L->mode = A_W3;
+      d.tn = 1;
+      d.tw = tw;
+      d.th = 128 / tw;
+      d.tiles_q = (int)cdivll(p->Q, d.tw);
+      d.tiles_p = (int)cdivll(p->P, d.th);
+      d.tiles_m = (int)((long long)d.tiles_q * d.tiles_p * g.N);
+      L->grid = d.tiles_m * p->ntn;
+    }
   }
   // ---- TMA-store epilogue: spatial tiles, 32-column passes, destinations on 32-column boundaries
   {
@@ -577,6 +636,8 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     return OSAM_OK;
   }
   int rc;
+  L->pair = choose_pair(p, L->mode);
+  const uint32_t b_rows = (uint32_t)(L->pair ? p->BN / 2 : p->BN);  // weight rows per CTA
   if (p->mode == A_GEMM) {
     const uint64_t dims[2] = {(uint64_t)g.C, (uint64_t)p->M};
     const uint64_t str[1] = {(uint64_t)g.C * 2};
@@ -585,7 +646,10 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   } else if (p->mode == A_S1) {
     const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
     const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
-    const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)p->tw, (uint32_t)p->th, (uint32_t)p->tn};
+    // A_W3: one (th + 2) × tw window per box; else the th × tw × tn tile of one tap
+    const bool w3 = L->mode == A_W3;
+    const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)(w3 ? d.tw : p->tw), (uint32_t)(w3 ? d.th + 2 : p->th),
+                             (uint32_t)(w3 ? 1 : p->tn)};
     rc = make_map(&L->ta, x, 4, dims, str, box, row_bytes);
   } else {
     const uint64_t dims[5] = {(uint64_t)2 * g.C, (uint64_t)g.W / 2, 2, (uint64_t)g.H / 2, (uint64_t)g.N};
@@ -607,13 +671,13 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   if (p->transposed) {
     const uint64_t dims[2] = {(uint64_t)g.C, (uint64_t)4 * g.K};
     const uint64_t str[1] = {(uint64_t)g.C * 2};
-    const uint32_t box[2] = {(uint32_t)p->BK, (uint32_t)p->BN};
+    const uint32_t box[2] = {(uint32_t)p->BK, b_rows};
     rc = make_map(&L->tb, wb, 2, dims, str, box, row_bytes);
   } else {
     const uint64_t rsc = (uint64_t)g.R * g.S * g.C;
     const uint64_t dims[2] = {rsc, (uint64_t)g.K};
     const uint64_t str[1] = {rsc * 2};
-    const uint32_t box[2] = {(uint32_t)p->BK, (uint32_t)p->BN};
+    const uint32_t box[2] = {(uint32_t)p->BK, b_rows};
     rc = make_map(&L->tb, wb, 2, dims, str, box, row_bytes);
   }
   return rc;

@@ -19,54 +19,81 @@
 //               (epilogue.cuh).  This replaces the reference's separate bn_forward_apply / add_bias passes.
 // Operand tiles are K-major with the TMA swizzle (128 B rows for BK = 64, 64 B rows for BK = 32) the UMMA
 // shared-memory descriptor expects.  No multicast anywhere.  Every wait is bounded (sm100.cuh).
+//
+// A_W3 (3×3, stride 1, pad 1; tiles of th = 128/tw rows × tw ∈ {8, 16} columns of one image): per BK-channel
+// chunk the producer loads three column-shifted input windows (th + 2 rows × tw columns, shifts −1, 0, +1)
+// instead of nine tap boxes; tap (r, c) reads window c from row r·tw on, a whole number of swizzle atoms,
+// so its UMMA descriptor is the plain K-major one.  The windows have their own ring; a window is released
+// after its three taps.  A third of the A boxes and ~40 % of the A bytes of the per-tap form.
+//
+// PAIR (CTA pairs on two SMs, cluster of 2): a work unit is two 128-pixel M tiles × BN channels, one
+// tile per CTA, computed by 2-SM UMMAs (M = 256) that the leader CTA (rank 0) issues.  Each CTA stages
+// its own A tile and HALF of the B (weight) rows.  Both producers' loads count on the leader's full
+// barrier (the leader expects both CTAs' bytes); the leader's commits arrive on both CTAs' empty and
+// accumulator barriers; both CTAs' epilogue warps arrive on the leader's drained barrier.
 #include "epilogue.cuh"
 
 namespace osam {
 
 constexpr int kMaxGemmN = 512;  // per-column epilogue constants cached in shared memory
 
-template <int BK, int BN>
+template <int BK, int BN, bool PAIR = false, bool W3 = false>
 struct FpropCfg {
-  static constexpr int A_BYTES = 128 * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_BYTES = W3 ? 0 : 128 * BK * 2;  // per-tap A box in the joint ring (not with W3)
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // weight rows staged by this CTA
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static_assert(B_BYTES % 1024 == 0, "weight stages must keep the ring 1024-byte aligned");
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // ≤ 128 output channels: two CTAs per SM, each with 4 epilogue warps (two independent load/MMA
   // pipelines hide TMA latency better); wider tiles: one CTA per SM with 8 epilogue warps.
   static constexpr int CTAS_PER_SM = BN <= 128 ? 2 : 1;
   static constexpr int EPI_WARPS = BN <= 128 ? 4 : 8;
   static constexpr int RING_BUDGET = BN <= 128 ? 96 * 1024 : 196 * 1024;
-  static constexpr int STAGES_RAW = RING_BUDGET / STAGE_BYTES;
+  // A_W3 window ring: windows of up to 160 rows (tw = 16: 10 × 16), 2 or 3 of them
+  static constexpr int WIN_ROWS = 160;
+  static constexpr int WIN_BYTES = W3 ? WIN_ROWS * BK * 2 : 0;
+  static constexpr int A_STAGES = W3 ? (CTAS_PER_SM == 2 ? 2 : 3) : 0;
+  static constexpr int STAGES_RAW = (RING_BUDGET - A_STAGES * WIN_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   static constexpr int ROW_BYTES = BK * 2;
   static constexpr int CONST_BYTES = 2 * kMaxGemmN * 4;
   static constexpr int STAGE_OUT_BYTES = EPI_WARPS * 32 * 64;  // per-warp epilogue stage
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGE_OUT_BYTES + CONST_BYTES + 256;
+  static constexpr int SMEM_BYTES =
+      1024 + A_STAGES * WIN_BYTES + STAGES * STAGE_BYTES + STAGE_OUT_BYTES + CONST_BYTES + 256;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
-template <int BK, int BN, int MODE>
-__global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::CTAS_PER_SM)
+template <int BK, int BN, int MODE, bool PAIR = false>
+__global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
+                                  FpropCfg<BK, BN, PAIR, MODE == A_W3>::CTAS_PER_SM)
     k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                  const __grid_constant__ StoreMaps sm, const ConvDev d) {
-  using Cfg = FpropCfg<BK, BN>;
+  constexpr bool W3 = MODE == A_W3;
+  using Cfg = FpropCfg<BK, BN, PAIR, W3>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = base;
-  uint8_t* sB = base + STAGES * Cfg::A_BYTES;
-  uint8_t* s_stage = base + STAGES * Cfg::STAGE_BYTES;  // 1024-aligned: the TMA store swizzle needs 512
+  uint8_t* sA = base;  // per-tap A boxes, or (A_W3) the window ring
+  uint8_t* sB = base + (W3 ? Cfg::A_STAGES * Cfg::WIN_BYTES : STAGES * Cfg::A_BYTES);
+  uint8_t* s_stage = sB + STAGES * Cfg::B_BYTES;  // 1024-aligned: the TMA store swizzle needs 512
   float* s_sc = reinterpret_cast<float*>(s_stage + Cfg::STAGE_OUT_BYTES);
   float* s_sh = s_sc + kMaxGemmN;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_sh + kMaxGemmN);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA → epilogue)
   uint64_t* acce = accf + 2;        // [2] accumulator drained (epilogue → MMA), one arrival per epilogue warp
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
+  uint64_t* afull = acce + 2;       // A_W3: [A_STAGES] window landed
+  uint64_t* aempty = afull + Cfg::A_STAGES;  // A_W3: [A_STAGES] window's three taps consumed
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(aempty + Cfg::A_STAGES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ntiles = d.tiles_m * d.ntn;
+  // PAIR: units of two M tiles (this CTA's is 2·unit + rank), walked by cluster; else single tiles by CTA.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+  const int ntiles = PAIR ? ((d.tiles_m + 1) >> 1) * d.ntn : d.tiles_m * d.ntn;
+  const int t_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int t_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -75,29 +102,79 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(accf + b, 1);
-      mbar_init(acce + b, Cfg::EPI_WARPS);
+      mbar_init(acce + b, (PAIR ? 2 : 1) * Cfg::EPI_WARPS);
+    }
+    for (int s = 0; s < Cfg::A_STAGES; s++) {
+      mbar_init(afull + s, 1);
+      mbar_init(aempty + s, 1);
     }
     fence_barrier_init();
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
   }
   if (warp == 1) {
-    tmem_alloc(tslot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tslot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tslot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp >= 2)
     load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 32 * Cfg::EPI_WARPS, s_sc, s_sh);
-  __syncthreads();
+  // PAIR: both CTAs' barriers are initialised before either CTA signals the other's
+  if (PAIR) {
+    __syncwarp();  // the cluster barrier is warp-aligned
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
+    if constexpr (W3) {
+      if (lane == 0) {
+        uint32_t it = 0, ait = 0;
+        bool ok = true;
+        const int tw = d.tw, th = d.th;
+        for (int t = t_first; t < ntiles && ok; t += t_step) {
+          const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
+          const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
+          const int q0 = tq * tw, p0 = (rest % d.tiles_p) * th, b0 = rest / d.tiles_p;
+          for (int cc = 0; cc < d.C && ok; cc += BK) {
+            for (int c = 0; c < 3 && ok; c++, ait++) {
+              const int ws = ait % Cfg::A_STAGES;
+              if (ait >= (uint32_t)Cfg::A_STAGES && !mbar_wait(aempty + ws, ((ait / Cfg::A_STAGES) - 1) & 1, d.err)) {
+                ok = false;
+                break;
+              }
+              // window c: rows p0−1 … p0+th, columns q0+c−1 … q0+c−2+tw (zero fill outside the image)
+              mbar_arrive_expect_tx(afull + ws, (uint32_t)((th + 2) * tw * BK * 2));
+              tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, p0 - 1, b0);
+              for (int r = 0; r < 3; r++, it++) {
+                const int s = it % STAGES;
+                if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) {
+                  ok = false;
+                  break;
+                }
+                mbar_arrive_expect_tx(full + s, Cfg::B_BYTES);
+                tma_load_2d(sB + s * Cfg::B_BYTES, &tb, full + s, (r * 3 + c) * d.C + cc, n0);
+              }
+            }
+          }
+        }
+      }
+    } else if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
+      for (int t = t_first; t < ntiles && ok; t += t_step) {
+        // PAIR: the peer's tile of a last unit with an odd tile count lies past the end: its boxes read
+        // the zero fill (TMA out-of-range), its epilogue stores nothing
+        const int nt = t % d.ntn, mt = PAIR ? (t / d.ntn) * 2 + (int)rank : t / d.ntn;
+        const int n0 = nt * BN + (int)rank * Cfg::B_ROWS;
         int q0 = 0, p0 = 0, b0 = 0, m0 = 0;
         if (MODE == A_GEMM) {
           m0 = mt * 128;
@@ -113,34 +190,112 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
-          const int tap = kb / d.nkc, cc = (kb - tap * d.nkc) * BK;
+          const int tap = kb / d.nkc, cc = (kb - tap * d.nkc) * BK;  // taps outer, channel chunks inner
           uint8_t* a = sA + s * Cfg::A_BYTES;
           uint8_t* b = sB + s * Cfg::B_BYTES;
+          int ca[5] = {cc, 0, 0, 0, 0};  // A box coordinates
           if (MODE == A_GEMM) {
-            tma_load_2d(a, &ta, full + s, cc, m0);
+            ca[1] = m0;
           } else {
             const int r = tap / d.S, c = tap - r * d.S;
             if (MODE == A_S1) {
-              tma_load_4d(a, &ta, full + s, cc, q0 + c - d.pad, p0 + r - d.pad, b0);
+              ca[1] = q0 + c - d.pad;
+              ca[2] = p0 + r - d.pad;
+              ca[3] = b0;
             } else {
               const int dr = r - d.pad, dc = c - d.pad;
-              tma_load_5d(a, &ta, full + s, (dc & 1) * d.C + cc, q0 + (dc >> 1), dr & 1, p0 + (dr >> 1), b0);
+              ca[0] = (dc & 1) * d.C + cc;
+              ca[1] = q0 + (dc >> 1);
+              ca[2] = dr & 1;
+              ca[3] = p0 + (dr >> 1);
+              ca[4] = b0;
             }
           }
-          tma_load_2d(b, &tb, full + s, tap * d.C + cc, n0);
+          if (PAIR) {
+            const uint32_t fb = mapa_shared(full + s, 0);  // the leader's full barrier counts both CTAs
+            if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * Cfg::STAGE_BYTES);
+            if (MODE == A_GEMM)
+              tma_load_2d_cg2(a, &ta, fb, ca[0], ca[1]);
+            else if (MODE == A_S1)
+              tma_load_4d_cg2(a, &ta, fb, ca[0], ca[1], ca[2], ca[3]);
+            else
+              tma_load_5d_cg2(a, &ta, fb, ca[0], ca[1], ca[2], ca[3], ca[4]);
+            tma_load_2d_cg2(b, &tb, fb, tap * d.C + cc, n0);
+          } else {
+            mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
+            if (MODE == A_GEMM)
+              tma_load_2d(a, &ta, full + s, ca[0], ca[1]);
+            else if (MODE == A_S1)
+              tma_load_4d(a, &ta, full + s, ca[0], ca[1], ca[2], ca[3]);
+            else
+              tma_load_5d(a, &ta, full + s, ca[0], ca[1], ca[2], ca[3], ca[4]);
+            tma_load_2d(b, &tb, full + s, tap * d.C + cc, n0);
+          }
         }
+      }
+      // PAIR: the leader's last commits arrive on this CTA's empty barriers; wait for them so that
+      // none lands after the CTA has retired
+      if (PAIR && ok) {
+        for (uint32_t j = it > (uint32_t)STAGES ? it - STAGES : 0; j < it; j++)
+          if (!mbar_wait(empty + j % STAGES, (j / STAGES) & 1, d.err)) break;
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+    if constexpr (W3) {
+      if (lane == 0) {
+        constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+        const uint32_t tap_rows_bytes = (uint32_t)(d.tw * Cfg::ROW_BYTES);  // one window row of tw pixels
+        uint32_t it = 0, ait = 0, lt = 0;
+        bool ok = true;
+        for (int t = t_first; t < ntiles && ok; t += t_step, lt++) {
+          const uint32_t buf = lt & 1;
+          if (lt >= 2 && !mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err)) break;
+          tc_fence_after();
+          const uint32_t dt = tmem + buf * Cfg::ACC_COLS;
+          uint32_t acc = 0;
+          for (int cc = 0; cc < d.C && ok; cc += BK) {
+            for (int c = 0; c < 3 && ok; c++, ait++) {
+              const int ws = ait % Cfg::A_STAGES;
+              if (!mbar_wait(afull + ws, (ait / Cfg::A_STAGES) & 1, d.err)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t wa = smem_u32(sA + ws * Cfg::WIN_BYTES);
+              for (int r = 0; r < 3; r++, it++) {
+                const int s = it % STAGES;
+                if (!mbar_wait(full + s, (it / STAGES) & 1, d.err)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                const uint32_t a = wa + r * tap_rows_bytes, b = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++) {
+                  umma_f16(dt, smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES),
+                           smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES), idesc, acc);
+                  acc = 1;
+                }
+                umma_commit(empty + s);
+              }
+              umma_commit(aempty + ws);  // after the window's three taps (or what of them was issued)
+            }
+          }
+          if (ok) umma_commit(accf + buf);
+        }
+      }
+    } else if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 256 : 128, BN);
       uint32_t it = 0, lt = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
+      for (int t = t_first; t < ntiles && ok; t += t_step, lt++) {
         const uint32_t buf = lt & 1;
-        if (lt >= 2 && !mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err)) break;
+        if (lt >= 2) {
+          const bool drained = PAIR ? mbar_wait_cluster(acce + buf, ((lt >> 1) - 1) & 1, d.err)
+                                    : mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err);
+          if (!drained) break;
+        }
         tc_fence_after();
         const uint32_t dt = tmem + buf * Cfg::ACC_COLS;
         for (int kb = 0; kb < d.nk; kb++, it++) {
@@ -152,12 +307,25 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
           tc_fence_after();
           const uint32_t a = smem_u32(sA + s * Cfg::A_BYTES), b = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; k++)
-            umma_f16(dt, smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES), smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES),
-                     idesc, (kb | k) != 0);
-          umma_commit(empty + s);
+          for (int k = 0; k < BK / 16; k++) {
+            const uint64_t da = smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES);
+            const uint64_t db = smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES);
+            if (PAIR)
+              umma_f16_pair(dt, da, db, idesc, (kb | k) != 0);
+            else
+              umma_f16(dt, da, db, idesc, (kb | k) != 0);
+          }
+          if (PAIR)
+            umma_commit_pair(empty + s);
+          else
+            umma_commit(empty + s);
         }
-        if (ok) umma_commit(accf + buf);
+        if (ok) {
+          if (PAIR)
+            umma_commit_pair(accf + buf);
+          else
+            umma_commit(accf + buf);
+        }
       }
     }
   } else {
@@ -173,9 +341,18 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
     const int cols = Cfg::EPI_WARPS == 4 ? BN : (half == 0 ? SPLIT : BN - SPLIT);
     const int cbeg = Cfg::EPI_WARPS == 4 ? 0 : half * SPLIT;
     uint8_t* stage = s_stage + ew * (32 * 64);
+    const uint32_t acce_leader = PAIR ? mapa_shared(acce, 0) : 0;  // drained barriers live in the leader
     uint32_t lt = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
-      const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
+    for (int t = t_first; t < ntiles; t += t_step, lt++) {
+      const int nt = t % d.ntn, mt = PAIR ? (t / d.ntn) * 2 + (int)rank : t / d.ntn, n0 = nt * BN;
+      if (PAIR && mt >= d.tiles_m) {  // the peer's tile of an odd last unit: nothing to store
+        const uint32_t buf = lt & 1;
+        if (!mbar_wait(accf + buf, (lt >> 1) & 1, d.err)) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
+        continue;
+      }
       bool valid;
       long long pix;
       int n, p, q;
@@ -277,50 +454,93 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN>::THREADS, FpropCfg<BK, BN>::C
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acce + buf);
+      if (lane == 0) {
+        if (PAIR)
+          mbar_arrive_cluster(acce_leader + buf * 8);
+        else
+          mbar_arrive(acce + buf);
+      }
     }
   }
   if (warp >= 2 && lane == 0) bulk_wait_group0();  // tensor stores complete before the CTA retires
   tc_fence_before();
-  __syncthreads();
+  // PAIR: neither CTA frees its TMEM or retires while the other may still signal it
+  if (PAIR) {
+    __syncwarp();  // lanes 1–31 of the producer and MMA warps wait here for lane 0
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
 }
 
-template <int BK, int BN, int MODE>
+template <int BK, int BN, int MODE, bool PAIR>
 static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_only) {
-  using Cfg = FpropCfg<BK, BN>;
+  using Cfg = FpropCfg<BK, BN, PAIR, MODE == A_W3>;
+  auto kern = k_conv_fprop<BK, BN, MODE, PAIR>;
   // The dynamic shared-memory opt-in is set once per process (one device per process) and, through
   // conv_prime(), before any stream capture.
   static bool attr_set = false;
+  static int slots = 0;  // CTAs (PAIR: clusters) that run at once
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv_fprop<BK, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  if (prime_only) return cudaSuccess;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
+    int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
+    slots = sms * Cfg::CTAS_PER_SM;
+    // PAIR: one cluster per two CTA slots.  (The occupancy query for a cluster launch reports one CTA per
+    // SM for the ≤ 128-wide configurations, yet two co-reside in practice: measured.  Clusters beyond
+    // what fits simply wait; nothing depends on their co-residence.)
+    if (PAIR) slots /= 2;
+    attr_set = true;
   }
-  const int cap = sms * Cfg::CTAS_PER_SM;
-  const int grid = L.grid < cap ? L.grid : cap;
-  k_conv_fprop<BK, BN, MODE><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.sm, L.d);
-  return cudaGetLastError();
+  if (prime_only) return cudaSuccess;
+  if (!PAIR) {
+    const int grid = L.grid < slots ? L.grid : slots;
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.sm, L.d);
+    return cudaGetLastError();
+  }
+  const int units = ((L.d.tiles_m + 1) / 2) * L.d.ntn;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (units < slots ? units : slots));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, L.ta, L.tb, L.sm, L.d);
 }
 
 template <int BK, int BN>
 static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime) {
+  // CTA pairs need each CTA's half of the weight rows to keep 1024-byte stages (BN/2 rows of BK)
+  constexpr bool kPairOk = (BN / 2) * BK * 2 % 1024 == 0;
+  if (kPairOk && L.pair) {
+    switch (L.mode) {
+      case A_GEMM: return launch_one<BK, BN, A_GEMM, kPairOk>(L, st, prime);
+      case A_S1: return launch_one<BK, BN, A_S1, kPairOk>(L, st, prime);
+      case A_S2: return launch_one<BK, BN, A_S2, kPairOk>(L, st, prime);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (L.mode) {
-    case A_GEMM: return launch_one<BK, BN, A_GEMM>(L, st, prime);
-    case A_S1: return launch_one<BK, BN, A_S1>(L, st, prime);
-    case A_S2: return launch_one<BK, BN, A_S2>(L, st, prime);
+    case A_GEMM: return launch_one<BK, BN, A_GEMM, false>(L, st, prime);
+    case A_S1: return launch_one<BK, BN, A_S1, false>(L, st, prime);
+    case A_S2: return launch_one<BK, BN, A_S2, false>(L, st, prime);
+    case A_W3: return launch_one<BK, BN, A_W3, false>(L, st, prime);
   }
   return cudaErrorInvalidValue;
 }

@@ -16,7 +16,9 @@ enum AMode : int {
   A_S2 = 2,    // stride-2 conv: 5-D map (2C, W/2, 2, H/2, N) — the parity-split view of NHWC — so a
                // stride-2 gather becomes a dense box per tap
   A_STEM = 3,  // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
-  A_WIN = 4    // 3×3/s1/p1 with C, K ∈ {32, 64} (conv_win.cu): one shared input window per 128-position tile
+  A_WIN = 4,   // 3×3/s1/p1 with C, K ∈ {32, 64} (conv_win.cu): one shared input window per 128-position tile
+  A_W3 = 5     // 3×3/s1/p1 (conv_fprop.cu): tiles of th × tw = 128 pixels of one image; per channel chunk three
+               // column-shifted input windows of (th + 2) × tw pixels, each serving its column's three taps
 };
 
 // Dynamic shared memory a window-conv CTA may use (the sm_100 opt-in limit per block).
@@ -75,6 +77,7 @@ struct StoreMaps {
 
 struct ConvLaunch {
   int BK, BN, mode;
+  int pair;  // conv_fprop: CTA pairs with 2-SM UMMAs (the weight map's box is then BN/2 rows)
   int grid;
   CUtensorMap ta, tb;
   StoreMaps sm;

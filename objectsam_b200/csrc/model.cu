@@ -89,11 +89,6 @@ __global__ void k_bn_fold(const float* __restrict__ gbmv, int C, float eps, floa
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__global__ void k_f16_to_f32(const __half* __restrict__ s, float* __restrict__ d, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-    d[i] = __half2float(s[i]);
-}
-
 }  // namespace
 
 struct osam_model {

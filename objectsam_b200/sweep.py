@@ -1,6 +1,7 @@
 """Per-layer sweep: forward, dgrad and wgrad of every conv of the network, one by one.
 
-    python -m objectsam_b200.sweep --batch 128 [--reps 10] [--ref oracle/_ref/ref_forward_fp16] [--json out]
+    python -m objectsam_b200.sweep --batch 128 [--reps 10] [--ops fwd,dgrad,wgrad] [--ref oracle/_ref/ref_forward_fp16]
+                                   [--json out]
 
 Each op runs on seeded U[-1,1] NHWC fp16 tensors of the layer's shape (He-normal weights) and is timed
 with CUDA events over `reps` launches after two warm-up launches; TFLOP/s use the reference's FLOP
@@ -47,7 +48,9 @@ def main():
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--ref", default=None, help="reference cuDNN harness binary (oracle/_ref/ref_forward_fp16)")
     ap.add_argument("--json", default=None, help="write the table as JSON")
+    ap.add_argument("--ops", default="fwd,dgrad,wgrad", help="comma list of the passes to time")
     a = ap.parse_args()
+    ops = set(a.ops.split(","))
     import torch
 
     from objectsam_b200.conv import ConvGeom, ConvOp
@@ -89,15 +92,16 @@ def main():
         ws = torch.empty(max(op.workspace_size(), 256), dtype=torch.uint8, device=dev)
         flops = 2.0 * N * (H * W if tr else oshape[1] * oshape[2]) * K * C * R * R
         row = {"name": n["name"], "N": N, "H": H, "W": W, "C": C, "K": K, "R": R, "stride": s, "gflop": flops / 1e9}
-        row["fwd_ms"] = timed(lambda: op.fwd(x, w, y, ws=ws))
-        if not tr and n["index"] > 0:  # the stem has no input gradient (need_grad = false, src/model.cpp:177)
+        if "fwd" in ops:
+            row["fwd_ms"] = timed(lambda: op.fwd(x, w, y, ws=ws))
+        if not tr and n["index"] > 0 and "dgrad" in ops:  # the stem has no input gradient (need_grad = false, src/model.cpp:177)
             dx = torch.empty_like(x)
             try:
                 row["dgrad_ms"] = timed(lambda: op.dgrad(y, w, dx, ws=ws))
             except RuntimeError as e:
                 row["dgrad_ms"] = None
                 row["dgrad_note"] = str(e)[:80]
-        if not tr:
+        if not tr and "wgrad" in ops:
             dw = torch.empty(w_shape, dtype=torch.half, device=dev)
             try:
                 row["wgrad_ms"] = timed(lambda: op.wgrad(x, y, dw, ws=ws))

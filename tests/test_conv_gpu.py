@@ -72,6 +72,96 @@ def test_conv_fwd_matches_torch(cuda_lib, shape):
     assert_close(y, ref_conv(x, w, s, R // 2))
 
 
+# The three forms of the tensor-map kernel, each forced for every size: single CTAs with one A box per
+# tap ("tap"), CTA pairs with 2-SM UMMAs (M = 256 over two SMs, each staging its tile and half of the
+# weight rows: "pair"), and column-shifted input windows for 3×3/s1/p1 ("w3", 128-pixel tiles of one
+# image, ragged grids zero-filled).  3×3 s1/s2 and 1×1, BK 32/64, BN 32..256, several N tiles, odd tile
+# counts (the last pair's second tile is empty), every epilogue store form.
+FORMS = {"tap": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "0"},
+         "pair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "0"},
+         "w3": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "1"}}
+FORM_SHAPES = [
+    (3, 40, 40, 128, 128, 3, 1),
+    (2, 20, 20, 64, 64, 3, 1),
+    (3, 33, 17, 64, 128, 3, 1),
+    (2, 20, 20, 64, 384, 3, 1),
+    (2, 20, 20, 256, 224, 3, 1),
+    (1, 24, 36, 64, 256, 3, 1),
+    (2, 32, 48, 32, 32, 3, 1),
+    (1, 50, 70, 64, 64, 3, 1),
+    (2, 16, 16, 32, 64, 3, 2),
+    (2, 40, 40, 128, 256, 3, 2),
+    (1, 20, 20, 256, 512, 3, 2),
+    (2, 16, 16, 96, 64, 1, 1),
+    (1, 7, 9, 64, 64, 1, 1),
+    (3, 30, 30, 64, 384, 1, 1),
+    (2, 10, 10, 512, 512, 1, 1),
+]
+
+
+def set_form(monkeypatch, form):
+    for k, v in FORMS[form].items():
+        monkeypatch.setenv(k, v)
+
+
+@pytest.mark.parametrize("form", list(FORMS))
+@pytest.mark.parametrize("shape", FORM_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_fwd_forms(cuda_lib, monkeypatch, shape, form):
+    set_form(monkeypatch, form)
+    N, H, W, C, K, R, s = shape
+    x, w = rand_conv(N, H, W, C, K, R, seed=sum(shape) + 5)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, s, R // 2))
+    y = torch.full(op.out_shape(), 3.0, dtype=torch.half, device=DEV)
+    op.fwd(x, w, y)
+    assert_close(y, ref_conv(x, w, s, R // 2))
+    y0 = (torch.rand(op.out_shape(), device=DEV) - 0.5).half()  # beta = 1: the per-element epilogue
+    y = y0.clone()
+    op.fwd(x, w, y, beta=1.0)
+    assert_close(y, ref_conv(x, w, s, R // 2) + y0.float())
+
+
+@pytest.mark.parametrize("form", list(FORMS))
+def test_fused_residual_dests_forms(cuda_lib, monkeypatch, form):
+    """The multi-destination BN + SiLU + residual epilogue (TMA stores) with every kernel form."""
+    set_form(monkeypatch, form)
+    N, H, W, C, K = 3, 24, 40, 64, 128
+    x, w = rand_conv(N, H, W, C, K, 3, seed=13)
+    g = torch.Generator(device="cpu").manual_seed(9)
+    scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
+    shift = (torch.rand(K, generator=g) - 0.5).to(DEV)
+    res = (torch.rand(N, H, W, K, generator=g) - 0.5).half().to(DEV)
+    out = torch.zeros(N, H, W, K, dtype=torch.half, device=DEV)
+    cat = torch.zeros(N, H, W, 3 * 64, dtype=torch.half, device=DEV)
+    up = torch.zeros(N, 2 * H, 2 * W, 96, dtype=torch.half, device=DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    op.fwd_fused(x, w, [DestSpec(out), DestSpec(cat, choff=64, c0=64, c1=128), DestSpec(up, choff=32, c0=0, c1=64, up=2)],
+                 kind=EPI_BN_ACT, scale=scale, shift=shift, res=res)
+    a = F.silu(ref_conv(x, w, 1, 1).half().float() * scale + shift) + res.float()
+    assert_close(out, a)
+    assert_close(cat[..., 64:128], a[..., 64:128])
+    assert cat[..., :64].abs().max().item() == 0 and cat[..., 128:].abs().max().item() == 0
+    assert_close(up[..., 32:96], a[..., 0:64].repeat_interleave(2, dim=1).repeat_interleave(2, dim=2))
+    assert up[..., :32].abs().max().item() == 0
+
+
+@pytest.mark.parametrize("form", list(FORMS))
+@pytest.mark.parametrize("shape", [(2, 20, 20, 64, 64), (1, 33, 40, 128, 128), (2, 16, 24, 256, 128)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_conv_dgrad_forms(cuda_lib, monkeypatch, shape, form):
+    """Stride-1 3×3 input gradients run as forward convs over dz: every kernel form."""
+    set_form(monkeypatch, form)
+    N, H, W, C, K = shape
+    x, w = rand_conv(N, H, W, C, K, 3, seed=sum(shape))
+    g = torch.Generator(device="cpu").manual_seed(2)
+    dz = (torch.rand(N, H, W, K, generator=g) * 2 - 1).half().to(DEV)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, 1, 1))
+    ws = torch.empty(max(op.workspace_size(), 1), dtype=torch.uint8, device=DEV)
+    dx = torch.full((N, H, W, C), 3.0, dtype=torch.half, device=DEV)
+    op.dgrad(dz, w, dx, ws=ws)
+    torch.cuda.synchronize()
+    assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), 1, 1))
+
+
 # Larger stride-1 grids at the network's sizes: full and ragged, BN 32..256, 3×3 and 5×5.
 LARGE_SHAPES = [
     (2, 160, 160, 32, 32, 3),
