@@ -361,7 +361,10 @@ def main():
                         stage[(i + 1) % 2].copy_(h_in, non_blocking=True)
                         ev_in[(i + 1) % 2].record(copy_in)
                 stream.wait_event(ev_in[s])
-                d_in.copy_(stage[s], non_blocking=True)
+                # staged input → model input as an elementwise kernel (×1, exact), not a memcpy: a
+                # device-to-device memcpy runs on a copy engine and can queue behind the next step's
+                # host → device copy on that engine, which serialises the copies with the compute
+                torch.mul(stage[s], 1, out=d_in)
                 ev_used[s].record(stream)
                 model.forward(use_graph=True)
                 dd = post()

@@ -494,6 +494,7 @@ struct MaskArgs {
 };
 
 constexpr int kMaskPix = 128;  // pixels per tile = UMMA N = TMEM columns
+constexpr int kMaskBufs = 4;   // prototype tile ring: tiles t+1 … t+3 stream in while tile t is computed
 
 
 // ⌈v⌉ clamped to [lo, hi]; NaN maps to `nan_to` (an empty range, as every comparison with NaN is false).
@@ -504,15 +505,16 @@ __device__ __forceinline__ int ceil_clamp(float v, int lo, int hi, int nan_to) {
 }
 
 // One CTA = 128 detections (one per thread) × a run of `tiles_per_cta` consecutive 128-pixel tiles of one
-// image.  Per tile: two K=16 UMMAs (M=128, N=128) of coef · proto into TMEM while the next tile's prototypes
-// stream into the other shared buffer (cp.async), then each thread turns its detection's 128 logits into
+// image.  Per tile: two K=16 UMMAs (M=128, N=128) of coef · proto into TMEM while the next three tiles'
+// prototypes stream into a four-deep shared ring (cp.async; one tile in flight left the load latency
+// exposed at every tile), then each thread turns its detection's 128 logits into
 // bits: (logit > 0) ∧ inside the cropped box.  The crop x ≥ x1·g ∧ x < x2·g is tested on integers (for an
 // integer x and a float b, x ≥ b ⟺ x ≥ ⌈b⌉ and x < b ⟺ x < ⌈b⌉), one image row per 16-pixel chunk when
-// Wp % 16 == 0.  Detection tiles with no live detection only write zeros.  ≤ 128 TMEM columns and ~25 KB
+// Wp % 16 == 0.  Detection tiles with no live detection only write zeros.  ≤ 128 TMEM columns and ~41 KB
 // of shared memory per CTA, so four CTAs share an SM.
 __global__ void __launch_bounds__(128, 4) k_mask(const MaskArgs a) {
   __shared__ __align__(1024) uint8_t sA[128 * 64];
-  __shared__ __align__(1024) uint8_t sB[2][kMaskPix * 64];
+  __shared__ __align__(1024) uint8_t sB[kMaskBufs][kMaskPix * 64];
   __shared__ uint64_t bar;
   __shared__ uint32_t tslot;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -565,8 +567,12 @@ __global__ void __launch_bounds__(128, 4) k_mask(const MaskArgs a) {
                  pimg + (long long)(in ? pix : 0) * 32 + ch * 8, in ? 16u : 0u);
     }
   };
-  load_b(t_begin, 0);
-  cp_async_commit();
+  // prologue: tiles t_begin … t_begin + kMaskBufs − 2, one commit group each (empty groups past the end
+  // keep the count uniform: at tile i, group i is complete once at most kMaskBufs − 2 are pending)
+  for (int j = 0; j < kMaskBufs - 1; j++) {
+    if (t_begin + j < t_end) load_b(t_begin + j, j);
+    cp_async_commit();
+  }
 
   // crop rectangle on the proto grid as integer half-open ranges [xlo, xhi) × [ylo, yhi)
   const bool live = det < ndet;
@@ -584,20 +590,20 @@ __global__ void __launch_bounds__(128, 4) k_mask(const MaskArgs a) {
   bool fail = false;
 #pragma unroll 1
   for (int t = t_begin, i = 0; t < t_end; t++, i++) {
-    cp_async_wait_all();
+    cp_async_wait_n<kMaskBufs - 2>();
     fence_proxy_async_smem();
     if (__syncthreads_or(fail)) break;  // B(t) visible; the previous tile's TMEM reads are done
     tc_fence_after();
     const uint32_t tmem = tslot + trow;
     if (tid == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(128, kMaskPix);
-      const uint32_t sa = smem_u32(sA), sb = smem_u32(sB[i & 1]);
+      const uint32_t sa = smem_u32(sA), sb = smem_u32(sB[i % kMaskBufs]);
       umma_f16(tslot, smem_desc_kmajor(sa, 64), smem_desc_kmajor(sb, 64), idesc, 0);
       umma_f16(tslot, smem_desc_kmajor(sa + 32, 64), smem_desc_kmajor(sb + 32, 64), idesc, 1);
       umma_commit(&bar);
     }
-    // the other buffer was last read by tile t−1's UMMAs, whose commit every thread has waited for
-    if (t + 1 < t_end) load_b(t + 1, (i + 1) & 1);
+    // buffer (i − 1) mod kMaskBufs was last read by tile t−1's UMMAs, whose commit every thread has waited for
+    if (t + kMaskBufs - 1 < t_end) load_b(t + kMaskBufs - 1, (i + kMaskBufs - 1) % kMaskBufs);
     cp_async_commit();
     fail = !mbar_wait(&bar, i & 1, a.err);
     tc_fence_after();
