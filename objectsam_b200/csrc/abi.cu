@@ -410,12 +410,12 @@ static int choose_pair(const osam_conv_plan* p, int mode) {
   return mode == A_S2 && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
 }
 
-// Column-shifted windows (A_W3) for a 3×3/s1/p1 conv; tiles of th × tw = 128 pixels of one image, tw ∈
-// {8, 16}, whichever pads the image less.  Chosen from the per-image padding alone (the window form sums
-// in another order than the per-tap form, so a layer must take the same form at every batch size):
-// ≤ 5 % padding, or ≤ 25 % when C ≤ 64 or more than 128 output channels (measured on B200: at 40 × 40,
-// 20 % padding, the windows win by 6–20 % there and lose 3 % at 128 → 128).  OSAM_FPROP_W3=0|1 forces
-// it (1: whenever the geometry allows).  Returns tw, or 0.
+// Column-shifted windows (A_W3) for a 3×3/s1/p1 conv; tiles of 16 rows × 8 columns of one image.  Chosen
+// from the per-image padding alone (the window form sums in another order than the per-tap form, so a
+// layer must take the same form at every batch size): ≤ 5 % padding, or ≤ 25 % when C ≤ 64 or more than
+// 128 output channels (measured on B200: at 40 × 40, 20 % padding, the windows win by 6–20 % there and
+// lose 3 % at 128 → 128).  OSAM_FPROP_W3=0|1 forces it (1: whenever the geometry allows).  Returns the
+// tile width, or 0.
 static int choose_w3(const osam_conv_plan* p) {
   const osam_conv_geom& g = p->g;
   if (p->transposed || p->mode != A_S1 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1) return 0;
@@ -423,7 +423,7 @@ static int choose_w3(const osam_conv_plan* p) {
   if (f == 0) return 0;
   int best_tw = 0;
   long long best = 0;
-  for (int tw = 8; tw <= 16; tw *= 2) {
+  for (int tw = 8; tw <= 8; tw *= 2) {  // the kernel's window ring is sized for tw = 8 (18 × 8 windows)
     const long long tiles = cdivll(p->Q, tw) * cdivll(p->P, 128 / tw);  // per image
     if (best_tw == 0 || tiles < best) {
       best = tiles;
@@ -513,7 +513,9 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     e.coop = coop;
   }
   // ---- narrow 3×3 convs: one shared input window per tile (TMA-store epilogue, one output row per warp)
-  bool win = p->win && e.coop && !e.shuffle && !e.par;
+  // the window form of the tensor-map kernel (A_W3) is faster than conv_win.cu where both apply (measured:
+  // 160² 32 → 32 0.117 vs 0.143 ms, 80² 0.033 vs 0.037 ms at batch 64)
+  bool win = p->win && e.coop && !e.shuffle && !e.par && env_switch("OSAM_FPROP_WIN") != 0 && !choose_w3(p);
   for (int i = 0; i < e.ndest && win; i++) win = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
   if (win) {
     L->mode = A_WIN;

@@ -20,7 +20,7 @@
 // Operand tiles are K-major with the TMA swizzle (128 B rows for BK = 64, 64 B rows for BK = 32) the UMMA
 // shared-memory descriptor expects.  No multicast anywhere.  Every wait is bounded (sm100.cuh).
 //
-// A_W3 (3×3, stride 1, pad 1; tiles of th = 128/tw rows × tw ∈ {8, 16} columns of one image): per BK-channel
+// A_W3 (3×3, stride 1, pad 1; tiles of 16 rows × 8 columns of one image): per BK-channel
 // chunk the producer loads three column-shifted input windows (th + 2 rows × tw columns, shifts −1, 0, +1)
 // instead of nine tap boxes; tap (r, c) reads window c from row r·tw on, a whole number of swizzle atoms,
 // so its UMMA descriptor is the plain K-major one.  The windows have their own ring; a window is released
@@ -46,13 +46,19 @@ struct FpropCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // ≤ 128 output channels: two CTAs per SM, each with 4 epilogue warps (two independent load/MMA
   // pipelines hide TMA latency better); wider tiles: one CTA per SM with 8 epilogue warps.
-  static constexpr int CTAS_PER_SM = BN <= 128 ? 2 : 1;
-  static constexpr int EPI_WARPS = BN <= 128 ? 4 : 8;
-  static constexpr int RING_BUDGET = BN <= 128 ? 96 * 1024 : 196 * 1024;
-  // A_W3 window ring: windows of up to 160 rows (tw = 16: 10 × 16), 2 or 3 of them
-  static constexpr int WIN_ROWS = 160;
+  // (one CTA per SM for the 128-wide window form, 8 epilogue warps and a 196 KB ring: measured 30 % slower)
+  static constexpr bool ONE_CTA = BN > 128;
+  static constexpr int CTAS_PER_SM = ONE_CTA ? 1 : 2;
+  static constexpr int EPI_WARPS = ONE_CTA ? 8 : 4;
+  static constexpr int RING_BUDGET = ONE_CTA ? 196 * 1024 : 96 * 1024;
+  // A_W3 window ring: windows of 18 × 8 pixel rows; as many as fit (2…4) beside five weight stages (the
+  // window loads are the latency-critical ones — a window feeds only three taps — but fewer than five
+  // weight stages cost more than a deeper window ring gains: measured with 3, 5 and 7)
+  static constexpr int W3_MIN_B = 5;
+  static constexpr int WIN_ROWS = 144;
   static constexpr int WIN_BYTES = W3 ? WIN_ROWS * BK * 2 : 0;
-  static constexpr int A_STAGES = W3 ? (CTAS_PER_SM == 2 ? 2 : 3) : 0;
+  static constexpr int A_FIT = W3 ? (RING_BUDGET - W3_MIN_B * B_BYTES) / WIN_BYTES : 0;
+  static constexpr int A_STAGES = W3 ? (A_FIT < 2 ? 2 : (A_FIT > 4 ? 4 : A_FIT)) : 0;
   static constexpr int STAGES_RAW = (RING_BUDGET - A_STAGES * WIN_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
