@@ -127,8 +127,6 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
       tmem_relinquish();
     }
   }
-  if (warp >= 2)
-    load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 32 * Cfg::EPI_WARPS, s_sc, s_sh);
   // PAIR: both CTAs' barriers are initialised before either CTA signals the other's
   if (PAIR) {
     __syncwarp();  // the cluster barrier is warp-aligned
@@ -138,9 +136,14 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
   }
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  // Programmatic dependent launch: the set-up above (barriers, TMEM, tensor-map prefetch) overlapped the
+  // previous kernel's tail; the producer and the epilogue — the only threads touching global memory —
+  // wait for that kernel below, and the next conv may begin its own set-up now.
+  grid_dep_launch();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) grid_dep_wait();
     if constexpr (W3) {
       if (lane == 0) {
         uint32_t it = 0, ait = 0;
@@ -336,6 +339,9 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..)
+    grid_dep_wait();
+    load_epilogue_consts(d.ep, d.gemm_n, 0, d.gemm_n, threadIdx.x - 64, 32 * Cfg::EPI_WARPS, s_sc, s_sh);
+    named_bar_sync(1, 32 * Cfg::EPI_WARPS);
     const EpiDev& e = d.ep;
     const int ew = warp - 2;                 // 0..EPI_WARPS-1
     const int quad = warp & 3;               // TMEM lane quadrant this warp may access
@@ -509,24 +515,27 @@ static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_o
     attr_set = true;
   }
   if (prime_only) return cudaSuccess;
-  if (!PAIR) {
-    const int grid = L.grid < slots ? L.grid : slots;
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.ta, L.tb, L.sm, L.d);
-    return cudaGetLastError();
-  }
-  const int units = ((L.d.tiles_m + 1) / 2) * L.d.ntn;
+  // programmatic dependent launch (the kernel waits for its predecessor itself: grid_dep_wait)
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = 2;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(2 * (units < slots ? units : slots));
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = st;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  if (!PAIR) {
+    cfg.gridDim = dim3(L.grid < slots ? L.grid : slots);
+  } else {
+    const int units = ((L.d.tiles_m + 1) / 2) * L.d.ntn;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = 2;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    cfg.gridDim = dim3(2 * (units < slots ? units : slots));
+  }
   return cudaLaunchKernelEx(&cfg, kern, L.ta, L.tb, L.sm, L.d);
 }
 

@@ -92,6 +92,13 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with the programmatic-serialization attribute may start while the previous kernel of
+// its stream is still running; each thread that reads or writes what that kernel touches first waits for
+// its completion (and the visibility of its writes).  `launch_dependents` lets the next such kernel start.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ CTA pairs (clusters of two)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
