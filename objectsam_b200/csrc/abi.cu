@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "conv_internal.h"
 
@@ -410,31 +411,40 @@ static int choose_pair(const osam_conv_plan* p, int mode) {
   return mode == A_S2 && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
 }
 
-// Column-shifted windows (A_W3) for a 3×3/s1/p1 conv; tiles of 16 rows × 8 columns of one image.  Chosen
-// from the per-image padding alone (the window form sums in another order than the per-tap form, so a
-// layer must take the same form at every batch size): ≤ 5 % padding, or ≤ 25 % when C ≤ 64 or more than
-// 128 output channels (measured on B200: at 40 × 40, 20 % padding, the windows win by 6–20 % there and
-// lose 3 % at 128 → 128).  OSAM_FPROP_W3=0|1 forces it (1: whenever the geometry allows).  Returns the
-// tile width, or 0.
-static int choose_w3(const osam_conv_plan* p) {
+// Column-shifted windows (A_W3) for a 3×3/s1/p1 conv.  Whether a layer takes the window form is decided
+// from its grid alone (the window form sums in another order than the per-tap form, so a layer must take
+// the same form at every batch size): the best spatial block th × tw (th·tw ∈ {128, 64, 32}, tw ∈
+// {4, 8, 16}) pads the image by ≤ 5 %, or by ≤ 25 % when C ≤ 64 or the conv has more than 128 output
+// channels (measured on B200).  The tile — th rows × tw columns × ni images, th·tw·ni = 128, tw·ni ∈
+// {8, 16} — is then the one with the fewest tiles for this batch.  OSAM_FPROP_W3=0|1 forces the form (1:
+// whenever the geometry allows).  Returns false when the window form is not taken.
+struct W3Tile {
+  int th, tw, ni;
+};
+static bool choose_w3(const osam_conv_plan* p, W3Tile* out) {
   const osam_conv_geom& g = p->g;
-  if (p->transposed || p->mode != A_S1 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1) return 0;
+  if (p->transposed || p->mode != A_S1 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1) return false;
   const int f = env_switch("OSAM_FPROP_W3");
-  if (f == 0) return 0;
-  int best_tw = 0;
-  long long best = 0;
-  for (int tw = 8; tw <= 8; tw *= 2) {  // the kernel's window ring is sized for tw = 8 (18 × 8 windows)
-    const long long tiles = cdivll(p->Q, tw) * cdivll(p->P, 128 / tw);  // per image
-    if (best_tw == 0 || tiles < best) {
+  if (f == 0) return false;
+  static const W3Tile opts[] = {{16, 8, 1}, {8, 16, 1}, {8, 8, 2}, {16, 4, 2}, {8, 4, 4}};
+  long long best_sp = -1;  // padded pixels of the best spatial block, per image
+  for (const W3Tile& o : opts) {
+    const long long sp = cdivll(p->Q, o.tw) * o.tw * cdivll(p->P, o.th) * o.th;
+    if (best_sp < 0 || sp < best_sp) best_sp = sp;
+  }
+  const long long area = (long long)p->P * p->Q;
+  const bool take = f == 1 || best_sp * 100 <= area * 105 ||
+                    (best_sp * 100 <= area * 125 && (g.C <= 64 || p->BN > 128));
+  if (!take) return false;
+  long long best = -1;
+  for (const W3Tile& o : opts) {
+    const long long tiles = cdivll(p->Q, o.tw) * cdivll(p->P, o.th) * cdivll(g.N, o.ni);
+    if (best < 0 || tiles < best) {
       best = tiles;
-      best_tw = tw;
+      *out = o;
     }
   }
-  if (f == 1) return best_tw;
-  const long long padded = best * 128 * 100, area = (long long)p->P * p->Q;
-  if (padded <= area * 105) return best_tw;
-  if (padded <= area * 125 && (g.C <= 64 || p->BN > 128)) return best_tw;
-  return 0;
+  return true;
 }
 
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
@@ -515,7 +525,8 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   // ---- narrow 3×3 convs: one shared input window per tile (TMA-store epilogue, one output row per warp)
   // the window form of the tensor-map kernel (A_W3) is faster than conv_win.cu where both apply (measured:
   // 160² 32 → 32 0.117 vs 0.143 ms, 80² 0.033 vs 0.037 ms at batch 64)
-  bool win = p->win && e.coop && !e.shuffle && !e.par && env_switch("OSAM_FPROP_WIN") != 0 && !choose_w3(p);
+  W3Tile w3t{};
+  bool win = p->win && e.coop && !e.shuffle && !e.par && env_switch("OSAM_FPROP_WIN") != 0 && !choose_w3(p, &w3t);
   for (int i = 0; i < e.ndest && win; i++) win = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
   if (win) {
     L->mode = A_WIN;
@@ -535,15 +546,14 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     L->grid = p->win_tiles;
   }
   if (L->mode == A_S1) {
-    const int tw = choose_w3(p);
-    if (tw) {
+    if (choose_w3(p, &w3t)) {
       L->mode = A_W3;
-      d.tn = 1;
-      d.tw = tw;
-      d.th = 128 / tw;
+      d.tn = w3t.ni;
+      d.tw = w3t.tw;
+      d.th = w3t.th;
       d.tiles_q = (int)cdivll(p->Q, d.tw);
       d.tiles_p = (int)cdivll(p->P, d.th);
-      d.tiles_m = (int)((long long)d.tiles_q * d.tiles_p * g.N);
+      d.tiles_m = (int)((long long)d.tiles_q * d.tiles_p * cdivll(g.N, d.tn));
       L->grid = d.tiles_m * p->ntn;
     }
   }
@@ -555,10 +565,17 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     if (e.par) ts = ts && e.ndest == 1;
     e.tstore = 0;
     if (ts) {
+      // A_W3: (C, Q, N, P) views (a warp's rows run row, image, column): box {32, tw, ni, 32 / (ni·tw)}
+      const bool w3 = L->mode == A_W3;
       e.wtw = d.tw < 32 ? d.tw : 32;
       e.wth = d.th < 32 / e.wtw ? d.th : 32 / e.wtw;
       e.wtn = 32 / (e.wtw * e.wth);
-      const uint32_t box[4] = {32, (uint32_t)e.wtw, (uint32_t)e.wth, (uint32_t)e.wtn};
+      if (w3) {
+        e.wtw = d.tw;
+        e.wtn = d.tn;
+        e.wth = 32 / (d.tw * d.tn);
+      }
+      const uint32_t box[4] = {32, (uint32_t)e.wtw, (uint32_t)(w3 ? e.wtn : e.wth), (uint32_t)(w3 ? e.wth : e.wtn)};
       int rc = OSAM_OK;
       for (int t = 0; t < e.ndest && rc == OSAM_OK; t++) {
         const DestDev& ds = e.dest[t];
@@ -568,7 +585,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
         for (int v = 0; v < (four ? 4 : 1) && rc == OSAM_OK; v++) {
           const int dy = v >> 1, dx = v & 1;
           const __half* b = ds.p + (four ? ((uint64_t)dy * OQ2 + dx) * c : 0);
-          const uint64_t dims[4] = {c, (uint64_t)p->Q, (uint64_t)p->P, (uint64_t)g.N};
+          uint64_t dims[4] = {c, (uint64_t)p->Q, (uint64_t)p->P, (uint64_t)g.N};
           uint64_t str[3];
           if (four) {
             str[0] = 2 * c * 2;
@@ -578,6 +595,10 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
             str[0] = c * 2;
             str[1] = (uint64_t)p->Q * c * 2;
             str[2] = (uint64_t)p->P * p->Q * c * 2;
+          }
+          if (w3) {  // (C, Q, N, P)
+            std::swap(dims[2], dims[3]);
+            std::swap(str[1], str[2]);
           }
           rc = make_map(&L->sm.m[4 * t + v], b, 4, dims, str, box, 64);
         }
@@ -648,11 +669,15 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   } else if (p->mode == A_S1) {
     const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
     const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
-    // A_W3: one (th + 2) × tw window per box; else the th × tw × tn tile of one tap
-    const bool w3 = L->mode == A_W3;
-    const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)(w3 ? d.tw : p->tw), (uint32_t)(w3 ? d.th + 2 : p->th),
-                             (uint32_t)(w3 ? 1 : p->tn)};
-    rc = make_map(&L->ta, x, 4, dims, str, box, row_bytes);
+    if (L->mode == A_W3) {  // one (th + 2)-row × ni-image × tw-column window per box, a (C, W, N, H) view
+      const uint64_t wdims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.N, (uint64_t)g.H};
+      const uint64_t wstr[3] = {str[0], str[2], str[1]};
+      const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)d.tw, (uint32_t)d.tn, (uint32_t)(d.th + 2)};
+      rc = make_map(&L->ta, x, 4, wdims, wstr, box, row_bytes);
+    } else {  // the th × tw × tn tile of one tap
+      const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)p->tw, (uint32_t)p->th, (uint32_t)p->tn};
+      rc = make_map(&L->ta, x, 4, dims, str, box, row_bytes);
+    }
   } else {
     const uint64_t dims[5] = {(uint64_t)2 * g.C, (uint64_t)g.W / 2, 2, (uint64_t)g.H / 2, (uint64_t)g.N};
     const uint64_t str[4] = {(uint64_t)4 * g.C, (uint64_t)g.W * g.C * 2, (uint64_t)2 * g.W * g.C * 2,

@@ -20,10 +20,12 @@
 // Operand tiles are K-major with the TMA swizzle (128 B rows for BK = 64, 64 B rows for BK = 32) the UMMA
 // shared-memory descriptor expects.  No multicast anywhere.  Every wait is bounded (sm100.cuh).
 //
-// A_W3 (3×3, stride 1, pad 1; tiles of 16 rows × 8 columns of one image): per BK-channel
-// chunk the producer loads three column-shifted input windows (th + 2 rows × tw columns, shifts −1, 0, +1)
-// instead of nine tap boxes; tap (r, c) reads window c from row r·tw on, a whole number of swizzle atoms,
-// so its UMMA descriptor is the plain K-major one.  The windows have their own ring; a window is released
+// A_W3 (3×3, stride 1, pad 1; tiles of th rows × tw columns × ni images, th·tw·ni = 128, tw·ni ∈ {8, 16}):
+// per BK-channel chunk the producer loads three column-shifted input windows ((th + 2) rows × ni images ×
+// tw columns, shifts −1, 0, +1; a (C, W, N, H) view so a window's pixel rows run (row, image, column))
+// instead of nine tap boxes.  The tile's GEMM rows run in the same (row, image, column) order, so tap
+// (r, c) reads window c from pixel row r·ni·tw on — a whole number of swizzle atoms — and its UMMA
+// descriptor is the plain K-major one.  The windows have their own ring; a window is released
 // after its three taps.  A third of the A boxes and ~40 % of the A bytes of the per-tap form.
 //
 // PAIR (CTA pairs on two SMs, cluster of 2): a work unit is two 128-pixel M tiles × BN channels, one
@@ -51,11 +53,11 @@ struct FpropCfg {
   static constexpr int CTAS_PER_SM = ONE_CTA ? 1 : 2;
   static constexpr int EPI_WARPS = ONE_CTA ? 8 : 4;
   static constexpr int RING_BUDGET = ONE_CTA ? 196 * 1024 : 96 * 1024;
-  // A_W3 window ring: windows of 18 × 8 pixel rows; as many as fit (2…4) beside five weight stages (the
-  // window loads are the latency-critical ones — a window feeds only three taps — but fewer than five
-  // weight stages cost more than a deeper window ring gains: measured with 3, 5 and 7)
+  // A_W3 window ring: windows of (th + 2)·ni·tw ≤ 160 pixel rows; as many as fit (2…4) beside five weight
+  // stages (the window loads are the latency-critical ones — a window feeds only three taps — but fewer
+  // than five weight stages cost more than a deeper window ring gains: measured with 3, 5 and 7)
   static constexpr int W3_MIN_B = 5;
-  static constexpr int WIN_ROWS = 144;
+  static constexpr int WIN_ROWS = 160;
   static constexpr int WIN_BYTES = W3 ? WIN_ROWS * BK * 2 : 0;
   static constexpr int A_FIT = W3 ? (RING_BUDGET - W3_MIN_B * B_BYTES) / WIN_BYTES : 0;
   static constexpr int A_STAGES = W3 ? (A_FIT < 2 ? 2 : (A_FIT > 4 ? 4 : A_FIT)) : 0;
@@ -148,11 +150,11 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
       if (lane == 0) {
         uint32_t it = 0, ait = 0;
         bool ok = true;
-        const int tw = d.tw, th = d.th;
+        const int tw = d.tw, th = d.th, ni = d.tn;
         for (int t = t_first; t < ntiles && ok; t += t_step) {
           const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
           const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-          const int q0 = tq * tw, p0 = (rest % d.tiles_p) * th, b0 = rest / d.tiles_p;
+          const int q0 = tq * tw, p0 = (rest % d.tiles_p) * th, b0 = (rest / d.tiles_p) * ni;
           for (int cc = 0; cc < d.C && ok; cc += BK) {
             for (int c = 0; c < 3 && ok; c++, ait++) {
               const int ws = ait % Cfg::A_STAGES;
@@ -160,9 +162,10 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
                 ok = false;
                 break;
               }
-              // window c: rows p0−1 … p0+th, columns q0+c−1 … q0+c−2+tw (zero fill outside the image)
-              mbar_arrive_expect_tx(afull + ws, (uint32_t)((th + 2) * tw * BK * 2));
-              tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, p0 - 1, b0);
+              // window c: rows p0−1 … p0+th, images b0 … b0+ni−1, columns q0+c−1 … q0+c−2+tw (zero fill
+              // outside the batch and the image); the map's dimensions are (C, W, N, H)
+              mbar_arrive_expect_tx(afull + ws, (uint32_t)((th + 2) * ni * tw * BK * 2));
+              tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, b0, p0 - 1);
               for (int r = 0; r < 3; r++, it++) {
                 const int s = it % STAGES;
                 if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) {
@@ -254,7 +257,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
     if constexpr (W3) {
       if (lane == 0) {
         constexpr uint32_t idesc = idesc_f16_f32(128, BN);
-        const uint32_t tap_rows_bytes = (uint32_t)(d.tw * Cfg::ROW_BYTES);  // one window row of tw pixels
+        const uint32_t tap_rows_bytes = (uint32_t)(d.tn * d.tw * Cfg::ROW_BYTES);  // one window row: ni·tw pixels
         uint32_t it = 0, ait = 0, lt = 0;
         bool ok = true;
         for (int t = t_first; t < ntiles && ok; t += t_step, lt++) {
@@ -376,6 +379,14 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
         const long long tt = m / d.Q;
         p = (int)(tt % d.P);
         n = (int)(tt / d.P);
+      } else if (W3) {  // GEMM rows in (row, image, column) order
+        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q, nw = d.tn * d.tw;
+        const int i = row / nw, rr = row - i * nw, ni = rr / d.tw, j = rr - ni * d.tw;
+        n = (rest / d.tiles_p) * d.tn + ni;
+        p = (rest % d.tiles_p) * d.th + i;
+        q = tq * d.tw + j;
+        valid = n < d.N && p < d.P && q < d.Q;
+        pix = ((long long)n * d.P + p) * d.Q + q;
       } else {
         const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
         const int thw = d.th * d.tw;
@@ -387,7 +398,14 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
         pix = ((long long)n * d.P + p) * d.Q + q;
       }
       int bq = 0, bp = 0, bn = 0;  // origin of this warp's 32-row box (TMA-store epilogue)
-      if (MODE != A_GEMM) {
+      if (W3) {
+        // the store maps are (C, Q, N, P) views, so their 3rd and 4th coordinates are image and row:
+        // passed in the (bp, bn) slots.  A warp's 32 rows are 32 / (ni·tw) whole tile rows.
+        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
+        bq = tq * d.tw;
+        bp = (rest / d.tiles_p) * d.tn;
+        bn = (rest % d.tiles_p) * d.th + (quad * 32) / (d.tn * d.tw);
+      } else if (MODE != A_GEMM) {
         const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
         const int w0 = quad * 32, thw = d.th * d.tw;
         bq = tq * d.tw + w0 % d.tw;

@@ -96,6 +96,10 @@ FORM_SHAPES = [
     (1, 7, 9, 64, 64, 1, 1),
     (3, 30, 30, 64, 384, 1, 1),
     (2, 10, 10, 512, 512, 1, 1),
+    (8, 8, 8, 64, 64, 3, 1),      # window form: 8 × 8 × 2-image tiles
+    (4, 20, 20, 32, 64, 3, 1),    # window form: 8 × 4 × 4-image tiles, ragged rows
+    (6, 40, 40, 128, 128, 3, 1),
+    (5, 12, 20, 64, 128, 3, 1),   # odd batch: the last tile's second image is zero fill
 ]
 
 
@@ -121,10 +125,13 @@ def test_conv_fwd_forms(cuda_lib, monkeypatch, shape, form):
 
 
 @pytest.mark.parametrize("form", list(FORMS))
-def test_fused_residual_dests_forms(cuda_lib, monkeypatch, form):
-    """The multi-destination BN + SiLU + residual epilogue (TMA stores) with every kernel form."""
+@pytest.mark.parametrize("nhw", [(3, 24, 40), (4, 8, 8)], ids=lambda s: "x".join(map(str, s)))
+def test_fused_residual_dests_forms(cuda_lib, monkeypatch, form, nhw):
+    """The multi-destination BN + SiLU + residual epilogue (TMA stores) with every kernel form (the 8 × 8
+    grid takes two-image window tiles)."""
     set_form(monkeypatch, form)
-    N, H, W, C, K = 3, 24, 40, 64, 128
+    N, H, W = nhw
+    C, K = 64, 128
     x, w = rand_conv(N, H, W, C, K, 3, seed=13)
     g = torch.Generator(device="cpu").manual_seed(9)
     scale = (torch.rand(K, generator=g) + 0.5).to(DEV)
