@@ -136,6 +136,16 @@ struct osam_model {
   int njobs = 0;
   cudaStream_t side = nullptr;
   cudaEvent_t ev_dz[2] = {}, ev_wg[2] = {}, ev_fork = nullptr, ev_join = nullptr;
+  // forward on several streams: nodes that do not depend on each other (the neck's PAN path, the three
+  // head levels and their branches, the proto chain) overlap, so small layers fill the SMs that a big one
+  // leaves idle in its last wave.  Stream 0 is the caller's; the schedule is fixed at the first forward.
+  static constexpr int kFwdStreams = 3;
+  cudaStream_t fwd_st[kFwdStreams - 1] = {};
+  std::vector<int> node_order;               // launch order: topological, longest remaining path first
+  std::vector<int> node_stream;              // per node: 0 … kFwdStreams − 1
+  std::vector<std::vector<int>> node_waits;  // per node: producers on other streams (latest per stream)
+  std::vector<cudaEvent_t> node_ev;          // per node: recorded after it when another stream waits on it
+  cudaEvent_t ev_fwd_start = nullptr, ev_fwd_end[kFwdStreams - 1] = {};
 
   // ------------------------------------------------------------------ graph construction
   MAct* act(const std::string& n, int C, int H, int W) {
@@ -364,6 +374,20 @@ struct osam_model {
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
     if (side) cudaStreamDestroy(side);
+    for (cudaEvent_t ev : node_ev)
+      if (ev) cudaEventDestroy(ev);
+    node_ev.clear();
+    node_order.clear();
+    node_stream.clear();
+    node_waits.clear();
+    for (int k = 0; k < kFwdStreams - 1; k++) {
+      if (fwd_st[k]) cudaStreamDestroy(fwd_st[k]);
+      if (ev_fwd_end[k]) cudaEventDestroy(ev_fwd_end[k]);
+      fwd_st[k] = nullptr;
+      ev_fwd_end[k] = nullptr;
+    }
+    if (ev_fwd_start) cudaEventDestroy(ev_fwd_start);
+    ev_fwd_start = nullptr;
     ev_fork = ev_join = nullptr;
     side = nullptr;
     dz2 = nullptr;
@@ -513,12 +537,135 @@ struct osam_model {
     return OSAM_OK;
   }
 
+  // Dependency DAG of the forward (a node depends on every earlier writer of an activation it reads;
+  // concat buffers are written by several nodes into disjoint channel slices).  Nodes are launched in a
+  // topological order that puts the longest remaining chain (by FLOPs) first — so the proto branch starts
+  // as soon as its input exists — and assigned greedily to kFwdStreams streams: a node continues the
+  // stream whose last node is its latest producer, else takes the stream idle longest.
+  cudaError_t plan_streams() {
+    if (!node_stream.empty()) return cudaSuccess;
+    const int n = (int)nodes.size();
+    std::map<const MAct*, std::vector<int>> writers;
+    std::vector<std::vector<const MAct*>> rd(n);
+    for (int i = 0; i < n; i++) {
+      const MNode& nd = *nodes[i];
+      if (nd.kind == N_POOL) {
+        rd[i].push_back(nd.cat);
+        writers[nd.cat].push_back(i);
+        continue;
+      }
+      rd[i].push_back(nd.in);
+      if (nd.res) rd[i].push_back(nd.res);
+      if (nd.kind == N_CONVBN)
+        for (const MDest& d : nd.dests) writers[d.a].push_back(i);
+      else
+        writers[nd.out].push_back(i);
+    }
+    std::vector<std::vector<int>> dep(n), succ(n);
+    for (int i = 0; i < n; i++) {
+      for (const MAct* a : rd[i]) {
+        auto it = writers.find(a);
+        if (it == writers.end()) continue;
+        for (int w : it->second)
+          if (w < i) dep[i].push_back(w);
+      }
+      std::sort(dep[i].begin(), dep[i].end());
+      dep[i].erase(std::unique(dep[i].begin(), dep[i].end()), dep[i].end());
+      for (int w : dep[i]) succ[w].push_back(i);
+    }
+    std::vector<double> bottom(n, 0.0);  // FLOPs of the longest chain from a node to the end
+    for (int i = n - 1; i >= 0; i--) {
+      const MNode& nd = *nodes[i];
+      double c = 1.0;
+      if (nd.kind != N_POOL)
+        c = 2.0 * (double)nd.plan.M * nd.plan.gemm_n * nd.plan.g.R * nd.plan.g.S * nd.plan.g.C;
+      double m = 0.0;
+      for (int sx : succ[i]) m = std::max(m, bottom[sx]);
+      bottom[i] = c + m;
+    }
+    node_order.clear();
+    std::vector<int> pending(n);
+    std::vector<char> ready(n, 0);
+    for (int i = 0; i < n; i++) {
+      pending[i] = (int)dep[i].size();
+      ready[i] = pending[i] == 0;
+    }
+    for (int step = 0; step < n; step++) {
+      int pick = -1;
+      for (int i = 0; i < n; i++)
+        if (ready[i] == 1 && (pick < 0 || bottom[i] > bottom[pick])) pick = i;
+      ready[pick] = 2;
+      node_order.push_back(pick);
+      for (int sx : succ[pick])
+        if (--pending[sx] == 0) ready[sx] = 1;
+    }
+    node_stream.assign(n, 0);
+    node_waits.assign(n, {});
+    std::vector<char> signal(n, 0);
+    int tail[kFwdStreams];
+    for (int k = 0; k < kFwdStreams; k++) tail[k] = -1;
+    std::vector<int> pos(n);
+    for (int q = 0; q < n; q++) pos[node_order[q]] = q;
+    for (int q = 0; q < n; q++) {
+      const int i = node_order[q];
+      const std::vector<int>& deps = dep[i];  // launched earlier, all of them
+      int st = -1;
+      int best = -1;  // the latest-launched producer that is still the tail of its stream
+      for (int w : deps)
+        if (tail[node_stream[w]] == pos[w] && (best < 0 || pos[w] > pos[best])) best = w;
+      if (best >= 0) st = node_stream[best];
+      if (st < 0) {
+        st = 0;
+        for (int k = 1; k < kFwdStreams; k++)
+          if (tail[k] < tail[st]) st = k;
+      }
+      node_stream[i] = st;
+      int latest[kFwdStreams];  // per other stream, the producer launched last there
+      for (int k = 0; k < kFwdStreams; k++) latest[k] = -1;
+      for (int w : deps) {
+        const int ks = node_stream[w];
+        if (ks != st && (latest[ks] < 0 || pos[w] > pos[latest[ks]])) latest[ks] = w;
+      }
+      for (int k = 0; k < kFwdStreams; k++)
+        if (latest[k] >= 0) {
+          node_waits[i].push_back(latest[k]);
+          signal[latest[k]] = 1;
+        }
+      tail[st] = q;
+    }
+    cudaError_t e;
+    node_ev.assign(n, nullptr);
+    for (int i = 0; i < n; i++)
+      if (signal[i] && (e = cudaEventCreateWithFlags(&node_ev[i], cudaEventDisableTiming)) != cudaSuccess) return e;
+    for (int k = 0; k < kFwdStreams - 1; k++) {
+      if ((e = cudaStreamCreateWithFlags(&fwd_st[k], cudaStreamNonBlocking)) != cudaSuccess) return e;
+      if ((e = cudaEventCreateWithFlags(&ev_fwd_end[k], cudaEventDisableTiming)) != cudaSuccess) return e;
+    }
+    return cudaEventCreateWithFlags(&ev_fwd_start, cudaEventDisableTiming);
+  }
+
   cudaError_t run(cudaStream_t st) {
-    for (auto& ndp : nodes) {
-      MNode& nd = *ndp;
-      cudaError_t e = nd.kind == N_POOL ? launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, st)
-                                        : conv_launch(nd.L, st);
+    cudaError_t e = plan_streams();
+    if (e != cudaSuccess) return e;
+    cudaStream_t ss[kFwdStreams] = {st};
+    for (int k = 1; k < kFwdStreams; k++) ss[k] = fwd_st[k - 1];
+    // fork: the internal streams start after the caller's stream has reached this point
+    if ((e = cudaEventRecord(ev_fwd_start, st)) != cudaSuccess) return e;
+    for (int k = 1; k < kFwdStreams; k++)
+      if ((e = cudaStreamWaitEvent(ss[k], ev_fwd_start, 0)) != cudaSuccess) return e;
+    for (int i : node_order) {
+      MNode& nd = *nodes[i];
+      cudaStream_t s = ss[node_stream[i]];
+      for (int w : node_waits[i])
+        if ((e = cudaStreamWaitEvent(s, node_ev[w], 0)) != cudaSuccess) return e;
+      e = nd.kind == N_POOL ? launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, s) : conv_launch(nd.L, s);
       if (e != cudaSuccess) return e;
+      if (node_ev[i] && (e = cudaEventRecord(node_ev[i], s)) != cudaSuccess) return e;
+    }
+    // join: the caller's stream continues after every node
+    for (int k = 1; k < kFwdStreams; k++) {
+      if ((e = cudaEventRecord(ev_fwd_end[k - 1], ss[k])) != cudaSuccess) return e;
+      if ((e = cudaStreamWaitEvent(st, ev_fwd_end[k - 1], 0)) != cudaSuccess) return e;
     }
     return cudaSuccess;
   }
@@ -849,6 +996,8 @@ struct osam_model {
       e = run(st);
       return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
     }
+    if ((e = plan_streams()) != cudaSuccess)  // streams and events exist before any capture begins
+      return model_fail(OSAM_ERR_CUDA, "forward streams: %s", cudaGetErrorString(e));
     if (!exec) {
       // Record on the model's own stream; recording does not execute, so no ordering with `st` is needed.
       if (!cap && (e = cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking)) != cudaSuccess)
