@@ -399,16 +399,18 @@ static int env_switch(const char* name) {
   return (v && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
 }
 
-// CTA pairs with 2-SM UMMAs for the per-tap kernel (conv_fprop.cu; OSAM_FPROP_PAIR=0|1 forces it).
-// Measured on B200 at the network's shapes (batch 64): 3–4 % faster for the stride-2 convs with ≥ 128
-// output channels and ≥ 600 tiles; slower or even elsewhere (1×1: 5–40 %, small grids: 2–5 %).  A pair
-// sums every output in the same order as a single CTA (same K sequence), so the choice may depend on N.
+// CTA pairs with 2-SM UMMAs (conv_fprop.cu; OSAM_FPROP_PAIR=0|1 forces it).  Measured on B200 at the
+// network's shapes (batch 64): with ≥ 128 output channels and ≥ 600 tiles, 3–4 % faster for the stride-2
+// convs and 4–11 % for the window form (proto.cv2 0.417 → 0.372 ms: with the windows, the weight stream
+// is most of what the SM loads, and a pair loads half of it); slower for 1×1 convs, 64-wide tiles and
+// small grids.  A pair sums every output in the same order as a single CTA (same K sequence), so the
+// choice may depend on N.
 static int choose_pair(const osam_conv_plan* p, int mode) {
-  if (mode != A_GEMM && mode != A_S1 && mode != A_S2) return 0;
+  if (mode != A_GEMM && mode != A_S1 && mode != A_S2 && mode != A_W3) return 0;
   if ((p->BN / 2) * p->BK * 2 % 1024 != 0) return 0;  // each CTA's half of B must fill whole 1 KB atoms
   const int f = env_switch("OSAM_FPROP_PAIR");
   if (f >= 0) return f;
-  return mode == A_S2 && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
+  return (mode == A_S2 || mode == A_W3) && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
 }
 
 // Column-shifted windows (A_W3) for a 3×3/s1/p1 conv.  Whether a layer takes the window form is decided

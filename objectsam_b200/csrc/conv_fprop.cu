@@ -151,8 +151,12 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
         uint32_t it = 0, ait = 0;
         bool ok = true;
         const int tw = d.tw, th = d.th, ni = d.tn;
+        const uint32_t wbytes = (uint32_t)((th + 2) * ni * tw * BK * 2);
         for (int t = t_first; t < ntiles && ok; t += t_step) {
-          const int nt = t % d.ntn, mt = t / d.ntn, n0 = nt * BN;
+          // PAIR: this CTA's tile of the unit (past the end for the peer of an odd last unit: zero fill),
+          // its half of the weight rows; every load counts on the leader's barriers
+          const int nt = t % d.ntn, mt = PAIR ? (t / d.ntn) * 2 + (int)rank : t / d.ntn;
+          const int n0 = nt * BN + (int)rank * Cfg::B_ROWS;
           const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
           const int q0 = tq * tw, p0 = (rest % d.tiles_p) * th, b0 = (rest / d.tiles_p) * ni;
           for (int cc = 0; cc < d.C && ok; cc += BK) {
@@ -164,19 +168,36 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
               }
               // window c: rows p0−1 … p0+th, images b0 … b0+ni−1, columns q0+c−1 … q0+c−2+tw (zero fill
               // outside the batch and the image); the map's dimensions are (C, W, N, H)
-              mbar_arrive_expect_tx(afull + ws, (uint32_t)((th + 2) * ni * tw * BK * 2));
-              tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, b0, p0 - 1);
+              if (PAIR) {
+                if (rank == 0) mbar_arrive_expect_tx(afull + ws, 2 * wbytes);
+                tma_load_4d_cg2(sA + ws * Cfg::WIN_BYTES, &ta, mapa_shared(afull + ws, 0), cc, q0 + c - 1, b0, p0 - 1);
+              } else {
+                mbar_arrive_expect_tx(afull + ws, wbytes);
+                tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, b0, p0 - 1);
+              }
               for (int r = 0; r < 3; r++, it++) {
                 const int s = it % STAGES;
                 if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) {
                   ok = false;
                   break;
                 }
-                mbar_arrive_expect_tx(full + s, Cfg::B_BYTES);
-                tma_load_2d(sB + s * Cfg::B_BYTES, &tb, full + s, (r * 3 + c) * d.C + cc, n0);
+                if (PAIR) {
+                  if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * Cfg::B_BYTES);
+                  tma_load_2d_cg2(sB + s * Cfg::B_BYTES, &tb, mapa_shared(full + s, 0), (r * 3 + c) * d.C + cc, n0);
+                } else {
+                  mbar_arrive_expect_tx(full + s, Cfg::B_BYTES);
+                  tma_load_2d(sB + s * Cfg::B_BYTES, &tb, full + s, (r * 3 + c) * d.C + cc, n0);
+                }
               }
             }
           }
+        }
+        // PAIR: the leader's last commits arrive on this CTA's barriers; wait for them before retiring
+        if (PAIR && ok) {
+          for (uint32_t j = it > (uint32_t)STAGES ? it - STAGES : 0; j < it; j++)
+            if (!mbar_wait(empty + j % STAGES, (j / STAGES) & 1, d.err)) break;
+          for (uint32_t j = ait > (uint32_t)Cfg::A_STAGES ? ait - Cfg::A_STAGES : 0; j < ait; j++)
+            if (!mbar_wait(aempty + j % Cfg::A_STAGES, (j / Cfg::A_STAGES) & 1, d.err)) break;
         }
       }
     } else if (lane == 0) {
@@ -255,14 +276,18 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if constexpr (W3) {
-      if (lane == 0) {
-        constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      if (lane == 0 && rank == 0) {
+        constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 256 : 128, BN);
         const uint32_t tap_rows_bytes = (uint32_t)(d.tn * d.tw * Cfg::ROW_BYTES);  // one window row: ni·tw pixels
         uint32_t it = 0, ait = 0, lt = 0;
         bool ok = true;
         for (int t = t_first; t < ntiles && ok; t += t_step, lt++) {
           const uint32_t buf = lt & 1;
-          if (lt >= 2 && !mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err)) break;
+          if (lt >= 2) {
+            const bool drained = PAIR ? mbar_wait_cluster(acce + buf, ((lt >> 1) - 1) & 1, d.err)
+                                      : mbar_wait(acce + buf, ((lt >> 1) - 1) & 1, d.err);
+            if (!drained) break;
+          }
           tc_fence_after();
           const uint32_t dt = tmem + buf * Cfg::ACC_COLS;
           uint32_t acc = 0;
@@ -285,16 +310,32 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
                 const uint32_t a = wa + r * tap_rows_bytes, b = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
                 for (int k = 0; k < BK / 16; k++) {
-                  umma_f16(dt, smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES),
-                           smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES), idesc, acc);
+                  const uint64_t da = smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES);
+                  const uint64_t db = smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES);
+                  if (PAIR)
+                    umma_f16_pair(dt, da, db, idesc, acc);
+                  else
+                    umma_f16(dt, da, db, idesc, acc);
                   acc = 1;
                 }
-                umma_commit(empty + s);
+                if (PAIR)
+                  umma_commit_pair(empty + s);
+                else
+                  umma_commit(empty + s);
               }
-              umma_commit(aempty + ws);  // after the window's three taps (or what of them was issued)
+              // after the window's three taps (or what of them was issued)
+              if (PAIR)
+                umma_commit_pair(aempty + ws);
+              else
+                umma_commit(aempty + ws);
             }
           }
-          if (ok) umma_commit(accf + buf);
+          if (ok) {
+            if (PAIR)
+              umma_commit_pair(accf + buf);
+            else
+              umma_commit(accf + buf);
+          }
         }
       }
     } else if (lane == 0 && rank == 0) {
@@ -566,6 +607,7 @@ static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime)
       case A_GEMM: return launch_one<BK, BN, A_GEMM, kPairOk>(L, st, prime);
       case A_S1: return launch_one<BK, BN, A_S1, kPairOk>(L, st, prime);
       case A_S2: return launch_one<BK, BN, A_S2, kPairOk>(L, st, prime);
+      case A_W3: return launch_one<BK, BN, A_W3, kPairOk>(L, st, prime);
     }
     return cudaErrorInvalidValue;
   }
