@@ -662,6 +662,22 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   }
   int rc;
   L->pair = choose_pair(p, L->mode);
+  // Narrow window-form layers keep all nine weight taps in shared memory (A_W3R): one channel chunk, one
+  // N tile, BN ≤ 64; the 64 × 64 taps (72 KB) fit beside the windows only as a CTA pair's halves.
+  // Measured on B200 (batch 64): 32 → 32 at 160² 0.106 → 0.065 ms, at 80² 0.030 → 0.019 ms; 64 → 64 at
+  // 80² 4–5 % faster; on small grids the once-per-CTA weight load does not pay (−4 %), hence the tile
+  // thresholds.  OSAM_FPROP_W3R=0|1 forces it (1: whenever the geometry allows).
+  const int w3r_env = env_switch("OSAM_FPROP_W3R");
+  const long long w3_tiles = (long long)d.tiles_m * p->ntn;
+  if (L->mode == A_W3 && w3r_env != 0 && p->ntn == 1 && g.C == p->BK && (p->BN == 32 || p->BN == 64) &&
+      (w3r_env == 1 || w3_tiles >= (p->BN == 32 ? 600 : 1600))) {
+    bool fits = p->BN == 32 || p->BK == 32 || L->pair;
+    if (!fits && env_switch("OSAM_FPROP_PAIR") != 0) {
+      L->pair = 1;
+      fits = true;
+    }
+    if (fits) L->mode = A_W3R;
+  }
   const uint32_t b_rows = (uint32_t)(L->pair ? p->BN / 2 : p->BN);  // weight rows per CTA
   if (p->mode == A_GEMM) {
     const uint64_t dims[2] = {(uint64_t)g.C, (uint64_t)p->M};
@@ -671,7 +687,8 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   } else if (p->mode == A_S1) {
     const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
     const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2, (uint64_t)g.H * g.W * g.C * 2};
-    if (L->mode == A_W3) {  // one (th + 2)-row × ni-image × tw-column window per box, a (C, W, N, H) view
+    if (L->mode == A_W3 || L->mode == A_W3R) {  // one (th + 2)-row × ni-image × tw-column window per box,
+                                                // a (C, W, N, H) view
       const uint64_t wdims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.N, (uint64_t)g.H};
       const uint64_t wstr[3] = {str[0], str[2], str[1]};
       const uint32_t box[4] = {(uint32_t)p->BK, (uint32_t)d.tw, (uint32_t)d.tn, (uint32_t)(d.th + 2)};

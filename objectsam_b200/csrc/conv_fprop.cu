@@ -28,6 +28,9 @@
 // descriptor is the plain K-major one.  The windows have their own ring; a window is released
 // after its three taps.  A third of the A boxes and ~40 % of the A bytes of the per-tap form.
 //
+// A_W3R: the window form for narrow layers (C = BK, one N tile, BN ≤ 64): the nine weight taps are loaded
+// once per CTA and stay in shared memory; per tile only the three windows stream.
+//
 // PAIR (CTA pairs on two SMs, cluster of 2): a work unit is two 128-pixel M tiles × BN channels, one
 // tile per CTA, computed by 2-SM UMMAs (M = 256) that the leader CTA (rank 0) issues.  Each CTA stages
 // its own A tile and HALF of the B (weight) rows.  Both producers' loads count on the leader's full
@@ -39,7 +42,7 @@ namespace osam {
 
 constexpr int kMaxGemmN = 512;  // per-column epilogue constants cached in shared memory
 
-template <int BK, int BN, bool PAIR = false, bool W3 = false>
+template <int BK, int BN, bool PAIR = false, bool W3 = false, bool RESB = false>
 struct FpropCfg {
   static constexpr int A_BYTES = W3 ? 0 : 128 * BK * 2;  // per-tap A box in the joint ring (not with W3)
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // weight rows staged by this CTA
@@ -59,10 +62,11 @@ struct FpropCfg {
   static constexpr int W3_MIN_B = 5;
   static constexpr int WIN_ROWS = 160;
   static constexpr int WIN_BYTES = W3 ? WIN_ROWS * BK * 2 : 0;
-  static constexpr int A_FIT = W3 ? (RING_BUDGET - W3_MIN_B * B_BYTES) / WIN_BYTES : 0;
+  static constexpr int A_FIT = W3 ? (RING_BUDGET - (RESB ? 9 : W3_MIN_B) * B_BYTES) / WIN_BYTES : 0;
   static constexpr int A_STAGES = W3 ? (A_FIT < 2 ? 2 : (A_FIT > 4 ? 4 : A_FIT)) : 0;
   static constexpr int STAGES_RAW = (RING_BUDGET - A_STAGES * WIN_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+  // RESB: the nine weight taps, loaded once (full[0] counts them)
+  static constexpr int STAGES = RESB ? 9 : (STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW));
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   static constexpr int ROW_BYTES = BK * 2;
@@ -74,12 +78,13 @@ struct FpropCfg {
 };
 
 template <int BK, int BN, int MODE, bool PAIR = false>
-__global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
-                                  FpropCfg<BK, BN, PAIR, MODE == A_W3>::CTAS_PER_SM)
+__global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE == A_W3R, MODE == A_W3R>::THREADS,
+                                  FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE == A_W3R, MODE == A_W3R>::CTAS_PER_SM)
     k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                  const __grid_constant__ StoreMaps sm, const ConvDev d) {
-  constexpr bool W3 = MODE == A_W3;
-  using Cfg = FpropCfg<BK, BN, PAIR, W3>;
+  constexpr bool W3 = MODE == A_W3 || MODE == A_W3R;
+  constexpr bool RESB = MODE == A_W3R;
+  using Cfg = FpropCfg<BK, BN, PAIR, W3, RESB>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -152,6 +157,17 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
         bool ok = true;
         const int tw = d.tw, th = d.th, ni = d.tn;
         const uint32_t wbytes = (uint32_t)((th + 2) * ni * tw * BK * 2);
+        if (RESB) {  // the nine weight taps (this CTA's rows), once; full[0] counts them
+          const int nb = (int)rank * Cfg::B_ROWS;
+          if (PAIR) {
+            if (rank == 0) mbar_arrive_expect_tx(full, 2 * 9 * Cfg::B_BYTES);
+            for (int tap = 0; tap < 9; tap++)
+              tma_load_2d_cg2(sB + tap * Cfg::B_BYTES, &tb, mapa_shared(full, 0), tap * d.C, nb);
+          } else {
+            mbar_arrive_expect_tx(full, 9 * Cfg::B_BYTES);
+            for (int tap = 0; tap < 9; tap++) tma_load_2d(sB + tap * Cfg::B_BYTES, &tb, full, tap * d.C, nb);
+          }
+        }
         for (int t = t_first; t < ntiles && ok; t += t_step) {
           // PAIR: this CTA's tile of the unit (past the end for the peer of an odd last unit: zero fill),
           // its half of the weight rows; every load counts on the leader's barriers
@@ -175,7 +191,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
                 mbar_arrive_expect_tx(afull + ws, wbytes);
                 tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, b0, p0 - 1);
               }
-              for (int r = 0; r < 3; r++, it++) {
+              for (int r = 0; r < 3 && !RESB; r++, it++) {
                 const int s = it % STAGES;
                 if (it >= STAGES && !mbar_wait(empty + s, ((it / STAGES) - 1) & 1, d.err)) {
                   ok = false;
@@ -280,7 +296,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
         constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 256 : 128, BN);
         const uint32_t tap_rows_bytes = (uint32_t)(d.tn * d.tw * Cfg::ROW_BYTES);  // one window row: ni·tw pixels
         uint32_t it = 0, ait = 0, lt = 0;
-        bool ok = true;
+        bool ok = !RESB || mbar_wait(full, 0, d.err);  // RESB: the resident weights have landed
         for (int t = t_first; t < ntiles && ok; t += t_step, lt++) {
           const uint32_t buf = lt & 1;
           if (lt >= 2) {
@@ -301,8 +317,8 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
               tc_fence_after();
               const uint32_t wa = smem_u32(sA + ws * Cfg::WIN_BYTES);
               for (int r = 0; r < 3; r++, it++) {
-                const int s = it % STAGES;
-                if (!mbar_wait(full + s, (it / STAGES) & 1, d.err)) {
+                const int s = RESB ? r * 3 + c : (int)(it % STAGES);  // RESB: the tap's resident weights
+                if (!RESB && !mbar_wait(full + s, (it / STAGES) & 1, d.err)) {
                   ok = false;
                   break;
                 }
@@ -318,10 +334,12 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
                     umma_f16(dt, da, db, idesc, acc);
                   acc = 1;
                 }
-                if (PAIR)
-                  umma_commit_pair(empty + s);
-                else
-                  umma_commit(empty + s);
+                if (!RESB) {
+                  if (PAIR)
+                    umma_commit_pair(empty + s);
+                  else
+                    umma_commit(empty + s);
+                }
               }
               // after the window's three taps (or what of them was issued)
               if (PAIR)
@@ -553,7 +571,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3>::THREADS,
 
 template <int BK, int BN, int MODE, bool PAIR>
 static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_only) {
-  using Cfg = FpropCfg<BK, BN, PAIR, MODE == A_W3>;
+  using Cfg = FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE == A_W3R, MODE == A_W3R>;
   auto kern = k_conv_fprop<BK, BN, MODE, PAIR>;
   // The dynamic shared-memory opt-in is set once per process (one device per process) and, through
   // conv_prime(), before any stream capture.
@@ -608,6 +626,9 @@ static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime)
       case A_S1: return launch_one<BK, BN, A_S1, kPairOk>(L, st, prime);
       case A_S2: return launch_one<BK, BN, A_S2, kPairOk>(L, st, prime);
       case A_W3: return launch_one<BK, BN, A_W3, kPairOk>(L, st, prime);
+      case A_W3R:
+        if constexpr (BN == 32 || BN == 64) return launch_one<BK, BN, A_W3R, kPairOk>(L, st, prime);
+        break;
     }
     return cudaErrorInvalidValue;
   }
@@ -616,6 +637,9 @@ static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime)
     case A_S1: return launch_one<BK, BN, A_S1, false>(L, st, prime);
     case A_S2: return launch_one<BK, BN, A_S2, false>(L, st, prime);
     case A_W3: return launch_one<BK, BN, A_W3, false>(L, st, prime);
+    case A_W3R:
+      if constexpr (BN == 32 || BN == 64) return launch_one<BK, BN, A_W3R, false>(L, st, prime);
+      break;
   }
   return cudaErrorInvalidValue;
 }

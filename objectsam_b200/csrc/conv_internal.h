@@ -17,8 +17,9 @@ enum AMode : int {
                // stride-2 gather becomes a dense box per tap
   A_STEM = 3,  // R·S·C ≤ 32 (RGB stem): per-thread im2col gather into shared memory, no TMA
   A_WIN = 4,   // 3×3/s1/p1 with C, K ∈ {32, 64} (conv_win.cu): one shared input window per 128-position tile
-  A_W3 = 5     // 3×3/s1/p1 (conv_fprop.cu): tiles of th × tw = 128 pixels of one image; per channel chunk three
-               // column-shifted input windows of (th + 2) × tw pixels, each serving its column's three taps
+  A_W3 = 5,    // 3×3/s1/p1 (conv_fprop.cu): 128-pixel tiles (rows × images × columns); per channel chunk three
+               // column-shifted input windows, each serving its column's three taps
+  A_W3R = 6    // A_W3 with all nine weight taps resident in shared memory (C = BK, one N tile, BN ≤ 64)
 };
 
 // Dynamic shared memory a window-conv CTA may use (the sm_100 opt-in limit per block).

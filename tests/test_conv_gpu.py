@@ -75,12 +75,15 @@ def test_conv_fwd_matches_torch(cuda_lib, shape):
 # The forms of the tensor-map kernel, each forced for every size: single CTAs with one A box per tap
 # ("tap"), CTA pairs with 2-SM UMMAs (M = 256 over two SMs, each staging its tile and half of the weight
 # rows: "pair"), column-shifted input windows for 3×3/s1/p1 ("w3", 128-pixel tiles, ragged grids
-# zero-filled) and both at once ("w3pair").  3×3 s1/s2 and 1×1, BK 32/64, BN 32..256, several N tiles,
-# odd tile counts (the last pair's second tile is empty), every epilogue store form.
+# zero-filled), both at once ("w3pair"), the window form with all nine weight taps resident for the narrow
+# layers ("w3res") and with them always streamed ("w3stream").  3×3 s1/s2 and 1×1, BK 32/64, BN 32..256,
+# several N tiles, odd tile counts (the last pair's second tile is empty), every epilogue store form.
 FORMS = {"tap": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "0"},
          "pair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "0"},
          "w3": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "1"},
-         "w3pair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "1"}}
+         "w3pair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "1"},
+         "w3stream": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "1", "OSAM_FPROP_W3R": "0"},
+         "w3res": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "1", "OSAM_FPROP_W3R": "1"}}
 FORM_SHAPES = [
     (3, 40, 40, 128, 128, 3, 1),
     (2, 20, 20, 64, 64, 3, 1),
