@@ -406,11 +406,11 @@ static int env_switch(const char* name) {
 // small grids.  A pair sums every output in the same order as a single CTA (same K sequence), so the
 // choice may depend on N.
 static int choose_pair(const osam_conv_plan* p, int mode) {
-  if (mode != A_GEMM && mode != A_S1 && mode != A_S2 && mode != A_W3) return 0;
+  if (mode != A_GEMM && mode != A_S1 && mode != A_S2 && mode != A_W3 && mode != A_W3S2) return 0;
   if ((p->BN / 2) * p->BK * 2 % 1024 != 0) return 0;  // each CTA's half of B must fill whole 1 KB atoms
   const int f = env_switch("OSAM_FPROP_PAIR");
   if (f >= 0) return f;
-  return (mode == A_S2 || mode == A_W3) && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
+  return (mode == A_S2 || mode == A_W3 || mode == A_W3S2) && p->BN >= 128 && (long long)p->tiles_m * p->ntn >= 600;
 }
 
 // Column-shifted windows (A_W3) for a 3×3/s1/p1 conv.  Whether a layer takes the window form is decided
@@ -447,6 +447,19 @@ static bool choose_w3(const osam_conv_plan* p, W3Tile* out) {
     }
   }
   return true;
+}
+
+// Stride-2 window form (A_W3S2) for a 3×3/s2/p1 conv whose output grid tiles into 16 × 8 blocks exactly,
+// by default only where the weights can stay resident (one channel chunk, BN ≤ 64: model.1, 0.173 →
+// 0.106 ms at batch 64; streamed, the 64 → 128 conv measured 1 % slower than the per-tap form).
+// OSAM_FPROP_W3S2=0|1 forces it (1: any grid, ragged tiles zero-filled).
+static bool choose_w3s2(const osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  if (p->transposed || p->mode != A_S2 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 2) return false;
+  if (p->BN != 32 && p->BN != 64 && p->BN != 128) return false;  // the instantiated widths
+  const int f = env_switch("OSAM_FPROP_W3S2");
+  if (f >= 0) return f == 1;
+  return p->P % 16 == 0 && p->Q % 8 == 0 && g.C == p->BK && p->ntn == 1 && p->BN <= 64;
 }
 
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
@@ -558,6 +571,15 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
       d.tiles_m = (int)((long long)d.tiles_q * d.tiles_p * cdivll(g.N, d.tn));
       L->grid = d.tiles_m * p->ntn;
     }
+  } else if (L->mode == A_S2 && choose_w3s2(p)) {
+    L->mode = A_W3S2;
+    d.tn = 1;
+    d.tw = 8;
+    d.th = 16;
+    d.tiles_q = (int)cdivll(p->Q, 8);
+    d.tiles_p = (int)cdivll(p->P, 16);
+    d.tiles_m = (int)((long long)d.tiles_q * d.tiles_p * g.N);
+    L->grid = d.tiles_m * p->ntn;
   }
   // ---- TMA-store epilogue: spatial tiles, 32-column passes, destinations on 32-column boundaries
   {
@@ -568,7 +590,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     e.tstore = 0;
     if (ts) {
       // A_W3: (C, Q, N, P) views (a warp's rows run row, image, column): box {32, tw, ni, 32 / (ni·tw)}
-      const bool w3 = L->mode == A_W3;
+      const bool w3 = mode_window(L->mode);
       e.wtw = d.tw < 32 ? d.tw : 32;
       e.wth = d.th < 32 / e.wtw ? d.th : 32 / e.wtw;
       e.wtn = 32 / (e.wtw * e.wth);
@@ -667,16 +689,20 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
   // Measured on B200 (batch 64): 32 → 32 at 160² 0.106 → 0.065 ms, at 80² 0.030 → 0.019 ms; 64 → 64 at
   // 80² 4–5 % faster; on small grids the once-per-CTA weight load does not pay (−4 %), hence the tile
   // thresholds.  OSAM_FPROP_W3R=0|1 forces it (1: whenever the geometry allows).
+  // The stride-2 window form takes resident weights under the same conditions (A_W3S2R).
   const int w3r_env = env_switch("OSAM_FPROP_W3R");
   const long long w3_tiles = (long long)d.tiles_m * p->ntn;
-  if (L->mode == A_W3 && w3r_env != 0 && p->ntn == 1 && g.C == p->BK && (p->BN == 32 || p->BN == 64) &&
-      (w3r_env == 1 || w3_tiles >= (p->BN == 32 ? 600 : 1600))) {
-    bool fits = p->BN == 32 || p->BK == 32 || L->pair;
-    if (!fits && env_switch("OSAM_FPROP_PAIR") != 0) {
+  if ((L->mode == A_W3 || L->mode == A_W3S2) && w3r_env != 0 && p->ntn == 1 && g.C == p->BK &&
+      (p->BN == 32 || p->BN == 64) && (w3r_env == 1 || w3_tiles >= (p->BN == 32 ? 600 : 1600))) {
+    // the nine taps (this CTA's rows) and two windows within the 96 KB ring of a two-CTA-per-SM kernel
+    const long long win = (L->mode == A_W3S2 ? 272 : 160) * 2LL * p->BK;
+    auto fits = [&](int pair) { return 9LL * (pair ? p->BN / 2 : p->BN) * 2 * p->BK + 2 * win <= 96 * 1024; };
+    bool ok = fits(L->pair);
+    if (!ok && !L->pair && env_switch("OSAM_FPROP_PAIR") != 0 && fits(1)) {
       L->pair = 1;
-      fits = true;
+      ok = true;
     }
-    if (fits) L->mode = A_W3R;
+    if (ok) L->mode = L->mode == A_W3 ? A_W3R : A_W3S2R;
   }
   const uint32_t b_rows = (uint32_t)(L->pair ? p->BN / 2 : p->BN);  // weight rows per CTA
   if (p->mode == A_GEMM) {
@@ -701,7 +727,10 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     const uint64_t dims[5] = {(uint64_t)2 * g.C, (uint64_t)g.W / 2, 2, (uint64_t)g.H / 2, (uint64_t)g.N};
     const uint64_t str[4] = {(uint64_t)4 * g.C, (uint64_t)g.W * g.C * 2, (uint64_t)2 * g.W * g.C * 2,
                              (uint64_t)g.H * g.W * g.C * 2};
-    const uint32_t box[5] = {(uint32_t)p->BK, (uint32_t)p->tw, 1, (uint32_t)p->th, (uint32_t)p->tn};
+    // stride-2 window form: 8 columns × both row parities × 17 row pairs of one image per box
+    const bool s2w = mode_s2_window(L->mode);
+    const uint32_t box[5] = {(uint32_t)p->BK, (uint32_t)(s2w ? 8 : p->tw), s2w ? 2u : 1u,
+                             (uint32_t)(s2w ? 17 : p->th), (uint32_t)(s2w ? 1 : p->tn)};
     rc = make_map(&L->ta, x, 5, dims, str, box, row_bytes);
   }
   if (rc) return rc;

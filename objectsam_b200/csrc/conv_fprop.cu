@@ -31,6 +31,12 @@
 // A_W3R: the window form for narrow layers (C = BK, one N tile, BN ≤ 64): the nine weight taps are loaded
 // once per CTA and stay in shared memory; per tile only the three windows stream.
 //
+// A_W3S2 / A_W3S2R: the window form of a 3×3 / stride-2 / pad-1 conv on 16 × 8 output tiles.  Through the
+// parity view (2C, W/2, 2, H/2, N) a column tap dc ∈ {−1, 0, 1} is one box of 17 row pairs × both row
+// parities × 8 columns (channel half dc & 1, column offset dc >> 1): pixel rows run (row pair, parity,
+// column), so output row i of row tap r starts at pixel row 16·i + 8·(r + 1) — 8-row core groups 16 rows
+// apart (SBO = 16 rows), each a whole swizzle atom.
+//
 // PAIR (CTA pairs on two SMs, cluster of 2): a work unit is two 128-pixel M tiles × BN channels, one
 // tile per CTA, computed by 2-SM UMMAs (M = 256) that the leader CTA (rank 0) issues.  Each CTA stages
 // its own A tile and HALF of the B (weight) rows.  Both producers' loads count on the leader's full
@@ -42,8 +48,9 @@ namespace osam {
 
 constexpr int kMaxGemmN = 512;  // per-column epilogue constants cached in shared memory
 
-template <int BK, int BN, bool PAIR = false, bool W3 = false, bool RESB = false>
+template <int BK, int BN, bool PAIR, int MODE>
 struct FpropCfg {
+  static constexpr bool W3 = mode_window(MODE), RESB = mode_resident(MODE), S2W = mode_s2_window(MODE);
   static constexpr int A_BYTES = W3 ? 0 : 128 * BK * 2;  // per-tap A box in the joint ring (not with W3)
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // weight rows staged by this CTA
   static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -60,7 +67,7 @@ struct FpropCfg {
   // stages (the window loads are the latency-critical ones — a window feeds only three taps — but fewer
   // than five weight stages cost more than a deeper window ring gains: measured with 3, 5 and 7)
   static constexpr int W3_MIN_B = 5;
-  static constexpr int WIN_ROWS = 160;
+  static constexpr int WIN_ROWS = S2W ? 272 : 160;  // 17 row pairs × 2 parities × 8, or (th + 2)·ni·tw
   static constexpr int WIN_BYTES = W3 ? WIN_ROWS * BK * 2 : 0;
   static constexpr int A_FIT = W3 ? (RING_BUDGET - (RESB ? 9 : W3_MIN_B) * B_BYTES) / WIN_BYTES : 0;
   static constexpr int A_STAGES = W3 ? (A_FIT < 2 ? 2 : (A_FIT > 4 ? 4 : A_FIT)) : 0;
@@ -78,13 +85,11 @@ struct FpropCfg {
 };
 
 template <int BK, int BN, int MODE, bool PAIR = false>
-__global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE == A_W3R, MODE == A_W3R>::THREADS,
-                                  FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE == A_W3R, MODE == A_W3R>::CTAS_PER_SM)
+__global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCfg<BK, BN, PAIR, MODE>::CTAS_PER_SM)
     k_conv_fprop(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                  const __grid_constant__ StoreMaps sm, const ConvDev d) {
-  constexpr bool W3 = MODE == A_W3 || MODE == A_W3R;
-  constexpr bool RESB = MODE == A_W3R;
-  using Cfg = FpropCfg<BK, BN, PAIR, W3, RESB>;
+  using Cfg = FpropCfg<BK, BN, PAIR, MODE>;
+  constexpr bool W3 = Cfg::W3, RESB = Cfg::RESB, S2W = Cfg::S2W;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -156,7 +161,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE ==
         uint32_t it = 0, ait = 0;
         bool ok = true;
         const int tw = d.tw, th = d.th, ni = d.tn;
-        const uint32_t wbytes = (uint32_t)((th + 2) * ni * tw * BK * 2);
+        const uint32_t wbytes = (uint32_t)((S2W ? 2 * (th + 1) : th + 2) * ni * tw * BK * 2);
         if (RESB) {  // the nine weight taps (this CTA's rows), once; full[0] counts them
           const int nb = (int)rank * Cfg::B_ROWS;
           if (PAIR) {
@@ -184,12 +189,23 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE ==
               }
               // window c: rows p0−1 … p0+th, images b0 … b0+ni−1, columns q0+c−1 … q0+c−2+tw (zero fill
               // outside the batch and the image); the map's dimensions are (C, W, N, H)
+              // stride 2 (parity view): channel half dc & 1, column offset dc >> 1, both row parities, row
+              // pairs p0−1 … p0+th−1
+              const int dc = c - 1;
+              uint8_t* wdst = sA + ws * Cfg::WIN_BYTES;
               if (PAIR) {
                 if (rank == 0) mbar_arrive_expect_tx(afull + ws, 2 * wbytes);
-                tma_load_4d_cg2(sA + ws * Cfg::WIN_BYTES, &ta, mapa_shared(afull + ws, 0), cc, q0 + c - 1, b0, p0 - 1);
+                const uint32_t fb = mapa_shared(afull + ws, 0);
+                if (S2W)
+                  tma_load_5d_cg2(wdst, &ta, fb, (dc & 1) * d.C + cc, q0 + (dc >> 1), 0, p0 - 1, b0);
+                else
+                  tma_load_4d_cg2(wdst, &ta, fb, cc, q0 + c - 1, b0, p0 - 1);
               } else {
                 mbar_arrive_expect_tx(afull + ws, wbytes);
-                tma_load_4d(sA + ws * Cfg::WIN_BYTES, &ta, afull + ws, cc, q0 + c - 1, b0, p0 - 1);
+                if (S2W)
+                  tma_load_5d(wdst, &ta, afull + ws, (dc & 1) * d.C + cc, q0 + (dc >> 1), 0, p0 - 1, b0);
+                else
+                  tma_load_4d(wdst, &ta, afull + ws, cc, q0 + c - 1, b0, p0 - 1);
               }
               for (int r = 0; r < 3 && !RESB; r++, it++) {
                 const int s = it % STAGES;
@@ -294,7 +310,10 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE ==
     if constexpr (W3) {
       if (lane == 0 && rank == 0) {
         constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 256 : 128, BN);
-        const uint32_t tap_rows_bytes = (uint32_t)(d.tn * d.tw * Cfg::ROW_BYTES);  // one window row: ni·tw pixels
+        // row tap r starts at window pixel row r·ni·tw (stride 1) or 8·(r + 1) (stride 2, SBO 16 rows)
+        const uint32_t tap_rows_bytes = (uint32_t)((S2W ? 8 : d.tn * d.tw) * Cfg::ROW_BYTES);
+        const uint32_t tap_base_bytes = S2W ? 8u * Cfg::ROW_BYTES : 0u;
+        constexpr uint32_t a_sbo = (S2W ? 16 : 8) * Cfg::ROW_BYTES;
         uint32_t it = 0, ait = 0, lt = 0;
         bool ok = !RESB || mbar_wait(full, 0, d.err);  // RESB: the resident weights have landed
         for (int t = t_first; t < ntiles && ok; t += t_step, lt++) {
@@ -323,10 +342,10 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE ==
                   break;
                 }
                 tc_fence_after();
-                const uint32_t a = wa + r * tap_rows_bytes, b = smem_u32(sB + s * Cfg::B_BYTES);
+                const uint32_t a = wa + tap_base_bytes + r * tap_rows_bytes, b = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
                 for (int k = 0; k < BK / 16; k++) {
-                  const uint64_t da = smem_desc_kmajor(a + k * 32, Cfg::ROW_BYTES);
+                  const uint64_t da = smem_desc_kmajor_sbo(a + k * 32, Cfg::ROW_BYTES, a_sbo);
                   const uint64_t db = smem_desc_kmajor(b + k * 32, Cfg::ROW_BYTES);
                   if (PAIR)
                     umma_f16_pair(dt, da, db, idesc, acc);
@@ -571,7 +590,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE ==
 
 template <int BK, int BN, int MODE, bool PAIR>
 static cudaError_t launch_one(const ConvLaunch& L, cudaStream_t st, bool prime_only) {
-  using Cfg = FpropCfg<BK, BN, PAIR, MODE == A_W3 || MODE == A_W3R, MODE == A_W3R>;
+  using Cfg = FpropCfg<BK, BN, PAIR, MODE>;
   auto kern = k_conv_fprop<BK, BN, MODE, PAIR>;
   // The dynamic shared-memory opt-in is set once per process (one device per process) and, through
   // conv_prime(), before any stream capture.
@@ -629,6 +648,12 @@ static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime)
       case A_W3R:
         if constexpr (BN == 32 || BN == 64) return launch_one<BK, BN, A_W3R, kPairOk>(L, st, prime);
         break;
+      case A_W3S2:
+        if constexpr (BN == 32 || BN == 64 || BN == 128) return launch_one<BK, BN, A_W3S2, kPairOk>(L, st, prime);
+        break;
+      case A_W3S2R:
+        if constexpr (BN == 32 || BN == 64) return launch_one<BK, BN, A_W3S2R, kPairOk>(L, st, prime);
+        break;
     }
     return cudaErrorInvalidValue;
   }
@@ -639,6 +664,12 @@ static cudaError_t launch_mode(const ConvLaunch& L, cudaStream_t st, bool prime)
     case A_W3: return launch_one<BK, BN, A_W3, false>(L, st, prime);
     case A_W3R:
       if constexpr (BN == 32 || BN == 64) return launch_one<BK, BN, A_W3R, false>(L, st, prime);
+      break;
+    case A_W3S2:
+      if constexpr (BN == 32 || BN == 64 || BN == 128) return launch_one<BK, BN, A_W3S2, false>(L, st, prime);
+      break;
+    case A_W3S2R:
+      if constexpr (BN == 32 || BN == 64) return launch_one<BK, BN, A_W3S2R, false>(L, st, prime);
       break;
   }
   return cudaErrorInvalidValue;

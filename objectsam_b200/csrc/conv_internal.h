@@ -19,8 +19,13 @@ enum AMode : int {
   A_WIN = 4,   // 3×3/s1/p1 with C, K ∈ {32, 64} (conv_win.cu): one shared input window per 128-position tile
   A_W3 = 5,    // 3×3/s1/p1 (conv_fprop.cu): 128-pixel tiles (rows × images × columns); per channel chunk three
                // column-shifted input windows, each serving its column's three taps
-  A_W3R = 6    // A_W3 with all nine weight taps resident in shared memory (C = BK, one N tile, BN ≤ 64)
+  A_W3R = 6,   // A_W3 with all nine weight taps resident in shared memory (C = BK, one N tile, BN ≤ 64)
+  A_W3S2 = 7,  // 3×3/s2/p1 window form: three column windows of the parity view per chunk (16 × 8 tiles)
+  A_W3S2R = 8  // A_W3S2 with the weight taps resident
 };
+constexpr bool mode_window(int m) { return m == A_W3 || m == A_W3R || m == A_W3S2 || m == A_W3S2R; }
+constexpr bool mode_resident(int m) { return m == A_W3R || m == A_W3S2R; }
+constexpr bool mode_s2_window(int m) { return m == A_W3S2 || m == A_W3S2R; }
 
 // Dynamic shared memory a window-conv CTA may use (the sm_100 opt-in limit per block).
 constexpr size_t kWinSmemLimit = 227 * 1024;

@@ -312,6 +312,17 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, int row_byt
   return d;
 }
 
+// As smem_desc_kmajor with an explicit stride between 8-row core groups (a multiple of 8·row_bytes):
+// operands whose consecutive 8-row groups are not adjacent in the tile (the stride-2 window form).
+__device__ __forceinline__ uint64_t smem_desc_kmajor_sbo(uint32_t saddr, int row_bytes, uint32_t sbo) {
+  uint64_t d = (saddr & 0x3FFFFu) >> 4;
+  d |= uint64_t(1) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(row_bytes == 128 ? 2 : 4) << 61;
+  return d;
+}
+
 // K-major operand without swizzle: core matrices of 8 rows × 16 B (8 fp16 of K), rows 16 B apart; `lbo` =
 // byte distance between the two 8-element K halves of a K=16 step, `sbo` = between 8-row groups.  Any
 // 16-byte-aligned start is valid, so an operand may begin at any row of such a layout.

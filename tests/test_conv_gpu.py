@@ -76,14 +76,18 @@ def test_conv_fwd_matches_torch(cuda_lib, shape):
 # ("tap"), CTA pairs with 2-SM UMMAs (M = 256 over two SMs, each staging its tile and half of the weight
 # rows: "pair"), column-shifted input windows for 3×3/s1/p1 ("w3", 128-pixel tiles, ragged grids
 # zero-filled), both at once ("w3pair"), the window form with all nine weight taps resident for the narrow
-# layers ("w3res") and with them always streamed ("w3stream").  3×3 s1/s2 and 1×1, BK 32/64, BN 32..256,
+# layers ("w3res") and with them always streamed ("w3stream"), and the stride-2 window form streamed,
+# resident and paired ("s2win", "s2winres", "s2winpair").  3×3 s1/s2 and 1×1, BK 32/64, BN 32..256,
 # several N tiles, odd tile counts (the last pair's second tile is empty), every epilogue store form.
 FORMS = {"tap": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "0"},
          "pair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "0"},
          "w3": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "1"},
          "w3pair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "1"},
          "w3stream": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3": "1", "OSAM_FPROP_W3R": "0"},
-         "w3res": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "1", "OSAM_FPROP_W3R": "1"}}
+         "w3res": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3": "1", "OSAM_FPROP_W3R": "1"},
+         "s2win": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3S2": "1", "OSAM_FPROP_W3R": "0"},
+         "s2winres": {"OSAM_FPROP_PAIR": "0", "OSAM_FPROP_W3S2": "1", "OSAM_FPROP_W3R": "1"},
+         "s2winpair": {"OSAM_FPROP_PAIR": "1", "OSAM_FPROP_W3S2": "1", "OSAM_FPROP_W3R": "0"}}
 FORM_SHAPES = [
     (3, 40, 40, 128, 128, 3, 1),
     (2, 20, 20, 64, 64, 3, 1),
@@ -96,6 +100,8 @@ FORM_SHAPES = [
     (2, 16, 16, 32, 64, 3, 2),
     (2, 40, 40, 128, 256, 3, 2),
     (1, 20, 20, 256, 512, 3, 2),
+    (2, 64, 32, 64, 128, 3, 2),   # stride-2 window form: 32 × 16 output, exact 16 × 8 tiles
+    (3, 36, 20, 32, 64, 3, 2),    # ragged stride-2 windows (18 × 10 output)
     (2, 16, 16, 96, 64, 1, 1),
     (1, 7, 9, 64, 64, 1, 1),
     (3, 30, 30, 64, 384, 1, 1),
