@@ -279,7 +279,10 @@ int osam_model_head(const osam_model* m, int kind, int level, osam_tensor* t); /
 int osam_model_proto(const osam_model* m, osam_tensor* t);
 int osam_model_act(const osam_model* m, const char* name, osam_tensor* t);   /* any named activation */
 /* Inference forward pass: input → heads + proto.  use_graph = 1 records the launch sequence as a CUDA
- * graph on the first call and replays it afterwards (the first call must not be inside a capture). */
+ * graph on the first call and replays it afterwards (the first call must not be inside a capture).
+ * Independent nodes run on the model's own streams forked from `stream` and joined back into it: work
+ * queued on `stream` after the call sees the whole forward complete.  The first call creates those
+ * streams and events. */
 int osam_model_forward(osam_model* m, int use_graph, osam_stream_t stream);
 /* Kernels launched by one forward pass (one per graph node). */
 int osam_model_num_launches(const osam_model* m);
