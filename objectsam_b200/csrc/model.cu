@@ -349,6 +349,11 @@ struct osam_model {
   }
 
   void release() {
+    // the instantiated graph refers to the forward's streams' events: destroy it first
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    exec = nullptr;
+    graph = nullptr;
     for (auto& nd : nodes) free_subplans(nd->plan);
     cudaFree(garena);
     cudaFree(zarena);
