@@ -13,7 +13,8 @@
  *   - accumulation is fp32;
  *   - every pointer handed to a kernel is 16-byte aligned and every channel count/offset used by an
  *     epilogue destination is a multiple of 8, except single-channel outputs (K = 1).
- *   - No entry point allocates device memory; plan creation may (tensor-map scratch is host side).
+ *   - No conv, BN, pooling or post-process entry point allocates device memory, plan creation included;
+ *     only osam_model_create / osam_model_train_init / osam_model_sync_weights allocate (the model's arenas).
  * All functions return OSAM_OK (0) or a positive error code; osam_last_error() describes the last one.
  */
 #ifndef OSAM_H_
@@ -317,8 +318,19 @@ int osam_model_node_grad_range(const osam_model* m, int i, int64_t* off, int64_t
 int osam_model_get_grad(osam_model* m, const char* name, float* out, int64_t n);
 
 /* Device error word shared by all kernels of this library on the current device: returns the first
- * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises. */
+ * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises.
+ * Launches are asynchronous, so a kernel whose bounded wait ran out (OSAM_ERR_TIMEOUT: it returned early
+ * and its output is incomplete) is seen here, not in the status of the call that launched it; callers
+ * check it at a point where they synchronise anyway.  The word is a static device variable of the
+ * library: nothing is allocated for it.  No counterpart in the reference (cuDNN has no device-side
+ * status; its kernels cannot time out). */
 int osam_device_error(void);
+
+/* Self-test of the bounded device waits: launches one thread that waits on an mbarrier nothing arrives
+ * at, with a budget of budget_ns (at most 5 s); the wait runs out, records OSAM_ERR_TIMEOUT in the device
+ * error word and the kernel returns, leaving the context usable.  For tests; no counterpart in the
+ * reference. */
+int osam_selftest_wait_timeout(unsigned long long budget_ns, osam_stream_t stream);
 
 /* Human-readable description of the last error returned on this host thread. */
 const char* osam_last_error(void);

@@ -8,6 +8,7 @@
 #include <utility>
 
 #include "conv_internal.h"
+#include "sm100.cuh"
 
 namespace osam {
 
@@ -34,6 +35,10 @@ static int cuda_fail(cudaError_t e, const char* what) {
 }
 
 // ------------------------------------------------------------------ device error word
+// A file-scope device variable: every device that loads the library has one, zero-initialised at module
+// load, so nothing is ever allocated for it.  Host code cannot use the symbol as an address; its device
+// address is looked up (cudaGetSymbolAddress) once per device, at plan or model creation, and cached.
+static __device__ int g_dev_err_word;
 static std::mutex g_err_mu;
 static int* g_err_word[64] = {};
 
@@ -42,12 +47,20 @@ int* device_error_word() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lk(g_err_mu);
   if (!g_err_word[dev]) {
-    int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
-    g_err_word[dev] = p;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_dev_err_word) != cudaSuccess || !p) return nullptr;
+    g_err_word[dev] = static_cast<int*>(p);
   }
   return g_err_word[dev];
+}
+
+// Self-test of the bounded wait: one thread waits on an mbarrier that nothing arrives at, with the given
+// budget, so the wait runs out, records kDevErrTimeout in the error word and the kernel returns.
+__global__ void k_selftest_wait(unsigned long long budget_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  mbar_wait_for(&bar, 0, err, budget_ns);
 }
 
 // ------------------------------------------------------------------ tensor maps
@@ -1143,12 +1156,21 @@ int osam_device_error(void) {
   int v = 0;
   e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "osam_device_error read");
-  if (!v) v = static_scratch_take_error();
-  if (v) {
-    cudaMemset(w, 0, sizeof(int));
-    set_last_error("device kernel reported error %d", v);
-  }
+  if (v && (e = cudaMemset(w, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "osam_device_error clear");
+  // the static-scratch entry point's kernels report to their own word: read and clear it on every call
+  const int vs = static_scratch_take_error();
+  if (!v) v = vs;
+  if (v) set_last_error("device kernel reported error %d", v);
   return v;
+}
+
+int osam_selftest_wait_timeout(unsigned long long budget_ns, osam_stream_t stream) {
+  if (budget_ns == 0 || budget_ns > 5000000000ull) return fail(OSAM_ERR_INVALID, "budget must be in (0, 5 s]");
+  int* w = device_error_word();
+  if (!w) return fail(OSAM_ERR_CUDA, "no device error word");
+  k_selftest_wait<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(budget_ns, w);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_selftest_wait_timeout launch");
 }
 
 const char* osam_last_error(void) { return g_last_error; }

@@ -13,7 +13,7 @@
 // Its device address is looked up once per device, with that device current, by cudaGetSymbolAddress;
 // the first call of the entry point on a device does that lookup.  No path here calls cudaMalloc,
 // cudaFree or any allocating library routine — timeouts of these launches go to a static error word
-// of this file, not to the library's lazily allocated one.
+// of this file, which osam_device_error() reads and clears together with the library's own word.
 #include <mutex>
 
 #include "conv_internal.h"

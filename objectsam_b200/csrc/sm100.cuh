@@ -92,6 +92,22 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// The same bounded wait with the budget as an argument (for the self-test kernel that lets a wait run
+// out on purpose; the pipelines use mbar_wait and its fixed budget).
+static __device__ __noinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err,
+                                                 unsigned long long budget_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 8; i++)
+      if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (globaltimer() - t0 > budget_ns) {
+      if (err) atomicExch(err, kDevErrTimeout);
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ programmatic dependent launch
 // A kernel launched with the programmatic-serialization attribute may start while the previous kernel of
 // its stream is still running; each thread that reads or writes what that kernel touches first waits for

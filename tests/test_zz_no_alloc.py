@@ -4,7 +4,8 @@ Callers that cannot allocate device memory or provide a workspace (a plugin host
 budget and only hands out a stream; a loop that must never reach cudaMalloc, which can synchronise the
 device) use this entry point; its weight-relayout scratch is a fixed 256 KiB device array inside the
 library.  Checked through the C ABI against the workspace path (osam_conv_fwd with a caller workspace)
-on two calls in a row with different inputs, with the conv tests' tolerance.  This file sorts last so a
+and against torch's fp32 conv_transpose2d, on two calls in a row with different inputs, with the conv
+tests' tolerance.  This file sorts last so a
 run that stops at the first failure has already run every other test; it also passes alone.
 """
 import pytest
@@ -42,6 +43,10 @@ def test_static_scratch_matches_workspace_path_twice(cuda_lib):
         torch.cuda.synchronize()
         assert not torch.isnan(y).any()
         _assert_close(y, y_ref)
+        # and against torch's fp32 transposed conv of the same fp16 operands (weights (C_in, R, S, C_out))
+        y32 = torch.nn.functional.conv_transpose2d(x.float().permute(0, 3, 1, 2), w.float().permute(0, 3, 1, 2),
+                                                   stride=2).permute(0, 2, 3, 1)
+        _assert_close(y, y32)
     assert _lib.device_error() == 0
 
 
