@@ -7,6 +7,9 @@ Tolerances (north star: max relative error 1e-2, mean absolute error 1e-3):
   - BN-calibrated weights (activations O(10–100): two fp16 evaluations of the 60-layer chain drift apart
     by several fp16 ulps): both measured against the float64 network, our max error ≤ max(1e-2·scale,
     1.5 × the reference's) and our mean error ≤ 1.5 × the reference's + 1e-4·scale.
+The BASELINE batches themselves (config 2: 64 × 640², config 5: 32 × 1024²) run at full size here, and the
+first and last image of the batch are compared with the reference run on those two images: a tiling or
+addressing fault that only shows at full batch would show here.
 Skipped, with the reason, when the reference binaries were not built.
 """
 import os
@@ -23,29 +26,51 @@ from oracle import fsow, yolo_params, yolo_ref
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF16 = os.path.join(ROOT, "oracle", "_ref", "ref_forward_fp16")
+KEYS = [f"out.{k}{l}" for k in ("box", "cls", "coef") for l in range(3)] + ["out.proto"]
 
 
-@pytest.mark.skipif(not os.path.exists(REF16), reason="oracle/_ref not built (make -C oracle)")
-@pytest.mark.parametrize("weights,seed,N,S", [("baseline", 0, 1, 640), ("calibrated", 3, 2, 128),
-                                              ("calibrated", 0, 2, 256)])
-def test_matches_reference_cudnn_fp16(cuda_lib, weights, seed, N, S):
-    w = yolo_params.make_weights(seed) if weights == "baseline" else yolo_ref.calibrated_weights(seed, 128)
-    imgs = yolo_params.make_images(N, S, seed + 100)
+def run_reference(w, imgs):
     with tempfile.TemporaryDirectory() as td:
         wp, ip, op = (os.path.join(td, n) for n in ("w.fsow", "x.fsow", "o.fsow"))
         fsow.save(wp, w)
-        fsow.save(ip, {"images": imgs})
-        subprocess.run([REF16, wp, ip, op], check=True, timeout=600)
-        ref = fsow.load(op)
+        fsow.save(ip, {"images": np.ascontiguousarray(imgs, dtype=np.float32)})
+        subprocess.run([REF16, wp, ip, op], check=True, timeout=600, capture_output=True)
+        return fsow.load(op)
+
+
+def model_outputs(m):
+    ours = {f"out.{k}{l}": m.head(i, l) for i, k in enumerate(("box", "cls", "coef")) for l in range(3)}
+    ours["out.proto"] = m.proto()
+    return ours
+
+
+def check_direct(name, y, r):
+    scale = np.abs(r).max() + 1e-6
+    d = np.abs(y - r)
+    assert d.max() <= 1e-2 * scale, f"{name}: max |ours-ref| {d.max():.3e} (scale {scale:.3e})"
+    assert d.mean() <= 1e-3, f"{name}: mean |ours-ref| {d.mean():.3e}"
+    return d.max() / scale, d.mean()
+
+
+@pytest.mark.skipif(not os.path.exists(REF16), reason="oracle/_ref not built (make -C oracle)")
+@pytest.mark.parametrize("weights,seed,N,S", [("baseline", 0, 1, 640), ("baseline", 1, 1, 1024),
+                                              ("calibrated", 3, 2, 128), ("calibrated", 0, 2, 256)])
+def test_matches_reference_cudnn_fp16(cuda_lib, weights, seed, N, S):
+    w = yolo_params.make_weights(seed) if weights == "baseline" else yolo_ref.calibrated_weights(seed, 128)
+    imgs = yolo_params.make_images(N, S, seed + 100)
+    ref = run_reference(w, imgs)
     m = Model(N, S)
     m.load(w)
     m.sync_weights()
     m.input().copy_(torch.from_numpy(imgs).half())
     m.forward()
     torch.cuda.synchronize()
+    ours = model_outputs(m)
+    if weights == "baseline":
+        for name, y in ours.items():
+            check_direct(name, y.double().cpu().numpy(), ref[name].astype(np.float64))
+        return
     o64 = yolo_ref.YoloSegRef(w, emulate_fp16=False, dtype=torch.float64).forward(imgs)
-    ours = {f"out.{k}{l}": m.head(i, l) for i, k in enumerate(("box", "cls", "coef")) for l in range(3)}
-    ours["out.proto"] = m.proto()
     exact = {f"out.{k}{l}": o64[k][l] for k in ("box", "cls", "coef") for l in range(3)}
     exact["out.proto"] = o64["proto"]
     for name, y in ours.items():
@@ -53,13 +78,29 @@ def test_matches_reference_cudnn_fp16(cuda_lib, weights, seed, N, S):
         r = ref[name].astype(np.float64)
         x = exact[name].permute(0, 2, 3, 1).numpy()
         scale = np.abs(r).max() + 1e-6
-        d = np.abs(y - r)
-        if weights == "baseline":
-            assert d.max() <= 1e-2 * scale, f"{name}: max |ours-ref| {d.max():.3e} (scale {scale:.3e})"
-            assert d.mean() <= 1e-3, f"{name}: mean |ours-ref| {d.mean():.3e}"
-        else:
-            e_ours, e_ref = np.abs(y - x), np.abs(r - x)
-            assert e_ours.max() <= max(1e-2 * scale, 1.5 * e_ref.max()), \
-                f"{name}: max err vs fp64 {e_ours.max():.3e}, reference {e_ref.max():.3e}"
-            assert e_ours.mean() <= 1.5 * e_ref.mean() + 1e-4 * scale, \
-                f"{name}: mae vs fp64 {e_ours.mean():.3e}, reference {e_ref.mean():.3e}"
+        e_ours, e_ref = np.abs(y - x), np.abs(r - x)
+        assert e_ours.max() <= max(1e-2 * scale, 1.5 * e_ref.max()), \
+            f"{name}: max err vs fp64 {e_ours.max():.3e}, reference {e_ref.max():.3e}"
+        assert e_ours.mean() <= 1.5 * e_ref.mean() + 1e-4 * scale, \
+            f"{name}: mae vs fp64 {e_ours.mean():.3e}, reference {e_ref.mean():.3e}"
+
+
+@pytest.mark.skipif(not os.path.exists(REF16), reason="oracle/_ref not built (make -C oracle)")
+@pytest.mark.parametrize("B,S", [(64, 640), (32, 1024)])
+def test_full_baseline_batch_first_and_last_image(cuda_lib, B, S):
+    """BASELINE configs 2 and 5 at their own batch: the batch bench.py times (same weights and image
+    generator), through the model's CUDA graph; images 0 and B-1 against the reference run on them."""
+    w = yolo_params.make_weights(0)
+    imgs = yolo_params.make_images(B, S, 0)
+    m = Model(B, S)
+    m.load(w)
+    m.sync_weights()
+    m.input().copy_(torch.from_numpy(imgs).half())
+    m.forward(use_graph=True)
+    torch.cuda.synchronize()
+    pick = [0, B - 1]
+    ours = {k: v[pick].double().cpu().numpy() for k, v in model_outputs(m).items()}
+    m.close()
+    ref = run_reference(w, imgs[pick])
+    for name in KEYS:
+        check_direct(name, ours[name], ref[name].astype(np.float64))
