@@ -37,7 +37,7 @@ def _sources():
     out = []
     for dirpath, _, files in os.walk(CSRC):
         for f in sorted(files):
-            if f.endswith((".cu", ".cpp")) and not dirpath.endswith("shim"):
+            if f.endswith((".cu", ".cpp")):
                 out.append(os.path.join(dirpath, f))
     return sorted(out)
 
@@ -74,7 +74,7 @@ def build(verbose: bool = False, jobs: int | None = None) -> str:
     with ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(s, newest_header, verbose), srcs))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lcuda"] * 0
+        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs
         if verbose:
             print(" ".join(cmd), flush=True)
         res = subprocess.run(cmd, capture_output=True, text=True)
