@@ -148,6 +148,15 @@ struct osam_model {
   cudaEvent_t ev_fwd_start = nullptr, ev_fwd_end[kFwdStreams - 1] = {};
 
   // ------------------------------------------------------------------ graph construction
+  // The network is data (kLayers below, one row per model.<i> module) lowered in two steps:
+  //   1. expand(): each module becomes primitive tensors (Prim) — convs, channel slices, 2× upsamples,
+  //      concats, the SPPF pool chain — with explicit producers;
+  //   2. lower(): concats, slices and upsamples vanish.  A compute primitive's output is routed to every
+  //      place that reads it: its own buffer only when some primitive reads it directly, and otherwise (or
+  //      besides) the channel range of each concat that contains it, 2× upsampled on the way when an
+  //      upsample sits in between — the epilogue's destination list (osam_dest).
+  // Every compute primitive becomes one node (one kernel launch), in primitive order.
+
   MAct* act(const std::string& n, int C, int H, int W) {
     auto a = std::make_unique<MAct>();
     a->name = n;
@@ -162,153 +171,283 @@ struct osam_model {
     params[name].shape = std::move(shape);
     porder.push_back(name);
   }
-  void convbn(const std::string& name, MAct* in_, int K, int k, int s, std::vector<MDest> dests, MAct* res = nullptr,
-              std::vector<std::string> fused = {}, std::vector<int> fused_k = {}) {
-    auto nd = std::make_unique<MNode>();
-    nd->kind = N_CONVBN;
-    nd->name = name;
-    nd->in = in_;
-    nd->K = K;
-    nd->k = k;
-    nd->s = s;
-    nd->pre = fused.empty() ? std::vector<std::string>{name} : fused;
-    nd->ks = fused.empty() ? std::vector<int>{K} : fused_k;
-    for (size_t i = 0; i < nd->pre.size(); i++) {
-      const std::string& p = nd->pre[i];
-      add_param(p + ".conv.weight", {nd->ks[i], in_->C, k, k});
-      for (const char* b : {".bn.weight", ".bn.bias", ".bn.running_mean", ".bn.running_var"})
-        add_param(p + b, {nd->ks[i]});
-    }
-    for (auto& d : dests)
-      if (d.c1 == 0) d.c1 = K;
-    nd->dests = dests;
-    nd->res = res;
-    nodes.push_back(std::move(nd));
+
+  enum PrimOp { P_INPUT, P_CONV, P_HEAD, P_CONVT, P_POOLCAT, P_SLICE, P_UP2, P_CAT };
+  struct Prim {
+    PrimOp op;
+    std::string name;              // tensor name when it is given a buffer of its own
+    std::vector<int> src;          // producers (P_CAT: in channel order)
+    int C = 0, H = 0, W = 0;       // output shape
+    int k = 1, s = 1, res = -1;    // P_CONV: kernel, stride, residual primitive (added after the SiLU)
+    int c0 = 0;                    // P_SLICE: first channel taken from its producer
+    std::string param;             // P_CONV / P_HEAD / P_CONVT: parameter prefix
+    std::vector<std::string> branch;  // P_CONV: prefixes of convs fused along K (one per branch)
+    std::vector<int> branch_k;
+    bool output = false;           // a model output (head or proto): always has its own buffer
+    MAct* buf = nullptr;
+  };
+  std::vector<Prim> prims;
+
+  int prim(Prim p) {
+    prims.push_back(std::move(p));
+    return (int)prims.size() - 1;
   }
-  MAct* c2f(const std::string& name, MAct* x, int c2, int n, bool shortcut, std::vector<MDest> out) {
-    const int c = c2 / 2, H = x->H, W = x->W;
-    MAct* cat = act(name + ".cat", (2 + n) * c, H, W);
-    MAct* bin = act(name + ".m0.in", c, H, W);
-    convbn(name + ".cv1", x, 2 * c, 1, 1, {{cat, 0, 0, 2 * c, 1}, {bin, 0, c, 2 * c, 1}});
+  int conv(const std::string& pre, int x, int K, int k, int s, int res = -1) {
+    Prim p{P_CONV, pre, {x}};
+    p.C = K;
+    p.H = (prims[x].H + 2 * (k / 2) - k) / s + 1;
+    p.W = (prims[x].W + 2 * (k / 2) - k) / s + 1;
+    p.k = k;
+    p.s = s;
+    p.res = res;
+    p.param = pre;
+    return prim(p);
+  }
+  int slice(int x, int c0, int c1, const std::string& name) {
+    Prim p{P_SLICE, name, {x}};
+    p.C = c1 - c0;
+    p.H = prims[x].H;
+    p.W = prims[x].W;
+    p.c0 = c0;
+    return prim(p);
+  }
+  int concat(const std::vector<int>& xs, const std::string& name) {
+    Prim p{P_CAT, name, xs};
+    for (int x : xs) p.C += prims[x].C;
+    p.H = prims[xs[0]].H;
+    p.W = prims[xs[0]].W;
+    return prim(p);
+  }
+  int up2(int x) {
+    Prim p{P_UP2, prims[x].name + ".up", {x}};
+    p.C = prims[x].C;
+    p.H = 2 * prims[x].H;
+    p.W = 2 * prims[x].W;
+    return prim(p);
+  }
+
+  // YOLOv8-seg: the rows of Ultralytics' yolov8-seg model description at full width and depth; the "s"
+  // variant scales channels by 0.5 (at most 1024 before scaling, multiples of 8) and repeats by 1/3.
+  enum Mod { M_CONV, M_C2F, M_SPPF, M_UP, M_CAT, M_SEGMENT };
+  struct Row {
+    Mod m;
+    int from[3];  // producer rows, -1 = the row before; unused entries 0
+    int nfrom;
+    int repeats, ch, k, s;
+    bool shortcut;
+  };
+  static constexpr Row kLayers[23] = {
+      {M_CONV, {-1}, 1, 1, 64, 3, 2, false},       // 0   P1/2
+      {M_CONV, {-1}, 1, 1, 128, 3, 2, false},      // 1   P2/4
+      {M_C2F, {-1}, 1, 3, 128, 0, 0, true},        // 2
+      {M_CONV, {-1}, 1, 1, 256, 3, 2, false},      // 3   P3/8
+      {M_C2F, {-1}, 1, 6, 256, 0, 0, true},        // 4
+      {M_CONV, {-1}, 1, 1, 512, 3, 2, false},      // 5   P4/16
+      {M_C2F, {-1}, 1, 6, 512, 0, 0, true},        // 6
+      {M_CONV, {-1}, 1, 1, 1024, 3, 2, false},     // 7   P5/32
+      {M_C2F, {-1}, 1, 3, 1024, 0, 0, true},       // 8
+      {M_SPPF, {-1}, 1, 1, 1024, 5, 1, false},     // 9
+      {M_UP, {-1}, 1, 1, 0, 0, 0, false},          // 10
+      {M_CAT, {-1, 6}, 2, 1, 0, 0, 0, false},      // 11
+      {M_C2F, {-1}, 1, 3, 512, 0, 0, false},       // 12
+      {M_UP, {-1}, 1, 1, 0, 0, 0, false},          // 13
+      {M_CAT, {-1, 4}, 2, 1, 0, 0, 0, false},      // 14
+      {M_C2F, {-1}, 1, 3, 256, 0, 0, false},       // 15  P3 out
+      {M_CONV, {-1}, 1, 1, 256, 3, 2, false},      // 16
+      {M_CAT, {-1, 12}, 2, 1, 0, 0, 0, false},     // 17
+      {M_C2F, {-1}, 1, 3, 512, 0, 0, false},       // 18  P4 out
+      {M_CONV, {-1}, 1, 1, 512, 3, 2, false},      // 19
+      {M_CAT, {-1, 9}, 2, 1, 0, 0, 0, false},      // 20
+      {M_C2F, {-1}, 1, 3, 1024, 0, 0, false},      // 21  P5 out
+      {M_SEGMENT, {15, 18, 21}, 3, 1, 256, 0, 0, false},  // 22  Segment(nc = 1, nm = 32, npr = 256)
+  };
+  static int width(int c) { return (std::min(c, 1024) / 2 + 7) / 8 * 8; }
+  static int depth(int n) { return std::max((int)std::lround(n * 0.33), 1); }
+
+  // C2f: cv1 (1×1, 2c) split in halves; n bottlenecks (3×3, 3×3, + input if shortcut) chained from the
+  // second half; cv2 (1×1) over the concat of both halves and every bottleneck output.
+  int expand_c2f(const std::string& pre, const std::string& tn, int x, int c2, int n, bool shortcut) {
+    const int c = c2 / 2;
+    const int y = conv(pre + ".cv1", x, 2 * c, 1, 1);
+    std::vector<int> parts = {y};
+    int b = slice(y, c, 2 * c, tn + ".b0");
     for (int j = 0; j < n; j++) {
-      const std::string mj = name + ".m." + std::to_string(j);
-      MAct* t = act(mj + ".t", c, H, W);
-      convbn(mj + ".cv1", bin, c, 3, 1, {{t, 0, 0, c, 1}});
-      std::vector<MDest> d = {{cat, (2 + j) * c, 0, c, 1}};
-      MAct* next = nullptr;
-      if (j + 1 < n) {
-        next = act(name + ".m" + std::to_string(j + 1) + ".in", c, H, W);
-        d.push_back({next, 0, 0, c, 1});
-      }
-      convbn(mj + ".cv2", t, c, 3, 1, d, shortcut ? bin : nullptr);
-      bin = next;
+      const std::string mj = pre + ".m." + std::to_string(j);
+      const int t = conv(mj + ".cv1", b, c, 3, 1);
+      prims[t].name = tn + ".t" + std::to_string(j);
+      b = conv(mj + ".cv2", t, c, 3, 1, shortcut ? b : -1);
+      prims[b].name = tn + ".b" + std::to_string(j + 1);
+      parts.push_back(b);
     }
-    convbn(name + ".cv2", cat, c2, 1, 1, out);
-    return cat;
+    return conv(pre + ".cv2", concat(parts, tn + ".cat"), c2, 1, 1);
   }
-  void head_conv(const std::string& name, MAct* x, int K, MAct* out) {
-    auto nd = std::make_unique<MNode>();
-    nd->kind = N_HEAD;
-    nd->name = name;
-    nd->in = x;
-    nd->K = K;
-    nd->out = out;
-    add_param(name + ".weight", {K, x->C, 1, 1});
-    add_param(name + ".bias", {K});
-    nodes.push_back(std::move(nd));
+  // SPPF: cv1 (1×1, c/2) → three chained 5×5 max-pools, concatenated with cv1's output → cv2 (1×1).  The
+  // pool chain is one kernel that reads channels [0, c/2) of the concat and writes the other three slices.
+  int expand_sppf(const std::string& pre, const std::string& tn, int x, int c2) {
+    const int ch = prims[x].C / 2;
+    const int a = conv(pre + ".cv1", x, ch, 1, 1);
+    Prim p{P_POOLCAT, tn + ".cat", {a}};
+    p.C = 4 * ch;
+    p.H = prims[a].H;
+    p.W = prims[a].W;
+    p.param = pre + ".m";
+    return conv(pre + ".cv2", prim(p), c2, 1, 1);
+  }
+  // Segment head: per level three branches (box 4·reg_max, class nc, mask coefficients nm), each
+  // Conv3×3 → Conv3×3 → Conv2d 1×1 + bias; the three branch stems read the same input with the same
+  // geometry, so they run as ONE conv whose output channels are the branches side by side.  Proto:
+  // Conv3×3 → ConvTranspose 2×2/s2 + bias → Conv3×3 → Conv1×1 (nm channels) on P3.
+  void expand_segment(const std::string& pre, const int lv[3], int npr) {
+    const int nm = 32, ch0 = prims[lv[0]].C;
+    // Ultralytics' branch widths: box max(16, ch0/4, 4·reg_max), class max(ch0, min(nc, 100)) with nc = 1,
+    // mask coefficients max(ch0/4, nm)
+    const int cb = std::max({16, ch0 / 4, 4 * reg_max}), cc = std::max(ch0, 1), cm = std::max(ch0 / 4, nm);
+    const int widths[3] = {cb, cc, cm}, outs[3] = {4 * reg_max, 1, nm};
+    const char* branch[3] = {".cv2.", ".cv3.", ".cv4."};
+    const char* kind[3] = {"box", "cls", "coef"};
+    for (int l = 0; l < 3; l++) {
+      const std::string L = std::to_string(l);
+      const int stem = conv(pre + ".h" + L + ".0", lv[l], cb + cc + cm, 3, 1);
+      prims[stem].name = "h" + L + ".stem";
+      int c0 = 0;
+      for (int b = 0; b < 3; b++) {
+        prims[stem].branch.push_back(pre + branch[b] + L + ".0");
+        prims[stem].branch_k.push_back(widths[b]);
+        const int sb = slice(stem, c0, c0 + widths[b], "h" + L + "." + kind[b] + ".1");
+        c0 += widths[b];
+        const int mid = conv(pre + branch[b] + L + ".1", sb, widths[b], 3, 1);
+        prims[mid].name = "h" + L + "." + kind[b] + ".2";
+        Prim h{P_HEAD, std::string("out.") + kind[b] + L, {mid}};
+        h.C = outs[b];
+        h.H = prims[mid].H;
+        h.W = prims[mid].W;
+        h.param = pre + branch[b] + L + ".2";
+        h.output = true;
+        head_prim[b][l] = prim(h);
+      }
+    }
+    const int p1 = conv(pre + ".proto.cv1", lv[0], npr, 3, 1);
+    prims[p1].name = "proto.1";
+    Prim u{P_CONVT, "proto.up", {p1}};
+    u.C = npr;
+    u.H = 2 * prims[p1].H;
+    u.W = 2 * prims[p1].W;
+    u.param = pre + ".proto.upsample";
+    const int pu = prim(u);
+    const int p2 = conv(pre + ".proto.cv2", pu, npr, 3, 1);
+    prims[p2].name = "proto.2";
+    proto_prim = conv(pre + ".proto.cv3", p2, nm, 1, 1);
+    prims[proto_prim].name = "out.proto";
+    prims[proto_prim].output = true;
+  }
+  int head_prim[3][3] = {}, proto_prim = -1;
+
+  void expand() {
+    Prim x{P_INPUT, "in"};
+    x.C = 3;
+    x.H = x.W = S;
+    int row_out[23];
+    row_out[0] = -1;
+    int cur = prim(x);
+    for (int i = 0; i < 23; i++) {
+      const Row& r = kLayers[i];
+      int src[3];
+      for (int j = 0; j < r.nfrom; j++) src[j] = r.from[j] < 0 ? (i == 0 ? cur : row_out[i - 1]) : row_out[r.from[j]];
+      const std::string pre = "model." + std::to_string(i), tn = "L" + std::to_string(i);
+      int out = -1;
+      switch (r.m) {
+        case M_CONV: out = conv(pre, src[0], width(r.ch), r.k, r.s); break;
+        case M_C2F: out = expand_c2f(pre, tn, src[0], width(r.ch), depth(r.repeats), r.shortcut); break;
+        case M_SPPF: out = expand_sppf(pre, tn, src[0], width(r.ch)); break;
+        case M_UP: out = up2(src[0]); break;
+        case M_CAT: out = concat(std::vector<int>(src, src + r.nfrom), tn); break;
+        case M_SEGMENT: expand_segment(pre, src, width(r.ch)); break;
+      }
+      if (out >= 0 && prims[out].op != P_CAT && prims[out].op != P_UP2) prims[out].name = tn;
+      row_out[i] = out;
+    }
+  }
+
+  // Destinations of a producer's channels: they sit at channels [c0, c1) of primitive p, starting at the
+  // producer's channel pc; followed through the slices, upsamples and concats that read p.
+  void route(int p, int c0, int c1, int pc, int up, std::vector<MDest>& out) {
+    for (int q = 0; q < (int)prims.size(); q++) {
+      const Prim& Q = prims[q];
+      for (size_t j = 0; j < Q.src.size(); j++) {
+        if (Q.src[j] != p) continue;
+        if (Q.op == P_CAT) {
+          int off = 0;
+          for (size_t t = 0; t < j; t++) off += prims[Q.src[t]].C;
+          route(q, off + c0, off + c1, pc, up, out);
+        } else if (Q.op == P_POOLCAT) {
+          route(q, c0, c1, pc, up, out);
+        } else if (Q.op == P_UP2) {
+          route(q, c0, c1, pc, up * 2, out);
+        } else if (Q.op == P_SLICE) {
+          const int a = std::max(c0, Q.c0), b = std::min(c1, Q.c0 + Q.C);
+          if (a < b) route(q, a - Q.c0, b - Q.c0, pc + (a - c0), up, out);
+        }
+      }
+    }
+    if (prims[p].buf) out.push_back(MDest{prims[p].buf, c0, pc, pc + (c1 - c0), up});
   }
 
   void build() {
-    auto M = [](int i) { return "model." + std::to_string(i); };
-    in = act("in", 3, S, S);
-    MAct* a0 = act("a0", 32, S / 2, S / 2);
-    convbn(M(0), in, 32, 3, 2, {{a0, 0, 0, 0, 1}});
-    MAct* a1 = act("a1", 64, S / 4, S / 4);
-    convbn(M(1), a0, 64, 3, 2, {{a1, 0, 0, 0, 1}});
-    MAct* a2 = act("a2", 64, S / 4, S / 4);
-    c2f(M(2), a1, 64, 1, true, {{a2, 0, 0, 0, 1}});
-    MAct* a3 = act("a3", 128, S / 8, S / 8);
-    convbn(M(3), a2, 128, 3, 2, {{a3, 0, 0, 0, 1}});
-    MAct* cat11 = act("cat11", 768, S / 16, S / 16);
-    MAct* cat14 = act("cat14", 384, S / 8, S / 8);
-    MAct* cat17 = act("cat17", 384, S / 16, S / 16);
-    MAct* cat20 = act("cat20", 768, S / 32, S / 32);
-    MAct* a4 = act("a4", 128, S / 8, S / 8);
-    c2f(M(4), a3, 128, 2, true, {{a4, 0, 0, 0, 1}, {cat14, 256, 0, 0, 1}});
-    MAct* a5 = act("a5", 256, S / 16, S / 16);
-    convbn(M(5), a4, 256, 3, 2, {{a5, 0, 0, 0, 1}});
-    MAct* a6 = act("a6", 256, S / 16, S / 16);
-    c2f(M(6), a5, 256, 2, true, {{a6, 0, 0, 0, 1}, {cat11, 512, 0, 0, 1}});
-    MAct* a7 = act("a7", 512, S / 32, S / 32);
-    convbn(M(7), a6, 512, 3, 2, {{a7, 0, 0, 0, 1}});
-    MAct* a8 = act("a8", 512, S / 32, S / 32);
-    c2f(M(8), a7, 512, 1, true, {{a8, 0, 0, 0, 1}});
-    MAct* sp = act(M(9) + ".cat", 1024, S / 32, S / 32);
-    convbn(M(9) + ".cv1", a8, 256, 1, 1, {{sp, 0, 0, 0, 1}});
-    {
+    prims.clear();
+    expand();
+    // buffers: the input, every concat (and the SPPF pool concat), the model outputs, and every other
+    // primitive that a compute primitive reads as its input or residual
+    std::vector<char> read_direct(prims.size(), 0);
+    for (const Prim& p : prims) {
+      if (p.op == P_CONV || p.op == P_HEAD || p.op == P_CONVT) read_direct[p.src[0]] = 1;
+      if (p.res >= 0) read_direct[p.res] = 1;
+    }
+    for (int i = 0; i < (int)prims.size(); i++) {
+      Prim& p = prims[i];
+      if (p.op == P_INPUT || p.op == P_CAT || p.op == P_POOLCAT || p.output || read_direct[i])
+        p.buf = act(p.name, p.C, p.H, p.W);
+    }
+    in = prims[0].buf;
+    for (int b = 0; b < 3; b++)
+      for (int l = 0; l < 3; l++) head[b][l] = prims[head_prim[b][l]].buf;
+    proto = prims[proto_prim].buf;
+    // nodes, in primitive order
+    for (int i = 0; i < (int)prims.size(); i++) {
+      const Prim& p = prims[i];
       auto nd = std::make_unique<MNode>();
-      nd->kind = N_POOL;
-      nd->name = M(9) + ".m";
-      nd->cat = sp;
-      nd->pc = 256;
+      nd->name = p.param;
+      if (p.op == P_CONV) {
+        nd->kind = N_CONVBN;
+        nd->in = prims[p.src[0]].buf;
+        nd->K = p.C;
+        nd->k = p.k;
+        nd->s = p.s;
+        nd->pre = p.branch.empty() ? std::vector<std::string>{p.param} : p.branch;
+        nd->ks = p.branch.empty() ? std::vector<int>{p.C} : p.branch_k;
+        for (size_t b = 0; b < nd->pre.size(); b++) {
+          add_param(nd->pre[b] + ".conv.weight", {nd->ks[b], nd->in->C, p.k, p.k});
+          for (const char* t : {".bn.weight", ".bn.bias", ".bn.running_mean", ".bn.running_var"})
+            add_param(nd->pre[b] + t, {nd->ks[b]});
+        }
+        route(i, 0, p.C, 0, 1, nd->dests);
+        nd->res = p.res >= 0 ? prims[p.res].buf : nullptr;
+      } else if (p.op == P_HEAD || p.op == P_CONVT) {
+        nd->kind = p.op == P_HEAD ? N_HEAD : N_CONVT;
+        nd->in = prims[p.src[0]].buf;
+        nd->out = p.buf;
+        nd->K = p.C;
+        if (p.op == P_HEAD) add_param(p.param + ".weight", {p.C, nd->in->C, 1, 1});
+        else add_param(p.param + ".weight", {nd->in->C, p.C, 2, 2});
+        add_param(p.param + ".bias", {p.C});
+      } else if (p.op == P_POOLCAT) {
+        nd->kind = N_POOL;
+        nd->cat = p.buf;
+        nd->pc = prims[p.src[0]].C;
+      } else {
+        continue;
+      }
       nodes.push_back(std::move(nd));
     }
-    convbn(M(9) + ".cv2", sp, 512, 1, 1, {{cat11, 0, 0, 0, 2}, {cat20, 256, 0, 0, 1}});
-    c2f(M(12), cat11, 256, 1, false, {{cat14, 0, 0, 0, 2}, {cat17, 128, 0, 0, 1}});
-    MAct* p3 = act("p3", 128, S / 8, S / 8);
-    c2f(M(15), cat14, 128, 1, false, {{p3, 0, 0, 0, 1}});
-    convbn(M(16), p3, 128, 3, 2, {{cat17, 0, 0, 0, 1}});
-    MAct* p4 = act("p4", 256, S / 16, S / 16);
-    c2f(M(18), cat17, 256, 1, false, {{p4, 0, 0, 0, 1}});
-    convbn(M(19), p4, 256, 3, 2, {{cat20, 0, 0, 0, 1}});
-    MAct* p5 = act("p5", 512, S / 32, S / 32);
-    c2f(M(21), cat20, 512, 1, false, {{p5, 0, 0, 0, 1}});
-    // Segment head: per level one fused 3×3 conv (box c2 | cls 128 | coef 32), then the three branches.
-    const int R4 = 4 * reg_max;
-    const int c2 = std::max(16, std::max(128 / 4, R4));
-    const int KH = c2 + 128 + 32;
-    MAct* P[3] = {p3, p4, p5};
-    const std::string hd = M(22);
-    for (int l = 0; l < 3; l++) {
-      const std::string L = std::to_string(l);
-      const int H = P[l]->H, W = P[l]->W;
-      MAct* hb = act("h" + L + ".b1", c2, H, W);
-      MAct* hc = act("h" + L + ".c1", 128, H, W);
-      MAct* hm = act("h" + L + ".m1", 32, H, W);
-      convbn(hd + ".h" + L + ".0", P[l], KH, 3, 1,
-             {{hb, 0, 0, c2, 1}, {hc, 0, c2, c2 + 128, 1}, {hm, 0, c2 + 128, KH, 1}}, nullptr,
-             {hd + ".cv2." + L + ".0", hd + ".cv3." + L + ".0", hd + ".cv4." + L + ".0"}, {c2, 128, 32});
-      MAct* hb2 = act("h" + L + ".b2", c2, H, W);
-      MAct* hc2 = act("h" + L + ".c2", 128, H, W);
-      MAct* hm2 = act("h" + L + ".m2", 32, H, W);
-      convbn(hd + ".cv2." + L + ".1", hb, c2, 3, 1, {{hb2, 0, 0, 0, 1}});
-      convbn(hd + ".cv3." + L + ".1", hc, 128, 3, 1, {{hc2, 0, 0, 0, 1}});
-      convbn(hd + ".cv4." + L + ".1", hm, 32, 3, 1, {{hm2, 0, 0, 0, 1}});
-      head[0][l] = act("out.box" + L, R4, H, W);
-      head[1][l] = act("out.cls" + L, 1, H, W);
-      head[2][l] = act("out.coef" + L, 32, H, W);
-      head_conv(hd + ".cv2." + L + ".2", hb2, R4, head[0][l]);
-      head_conv(hd + ".cv3." + L + ".2", hc2, 1, head[1][l]);
-      head_conv(hd + ".cv4." + L + ".2", hm2, 32, head[2][l]);
-    }
-    MAct* pr1 = act("proto.1", 128, S / 8, S / 8);
-    convbn(hd + ".proto.cv1", p3, 128, 3, 1, {{pr1, 0, 0, 0, 1}});
-    MAct* pru = act("proto.up", 128, S / 4, S / 4);
-    {
-      auto nd = std::make_unique<MNode>();
-      nd->kind = N_CONVT;
-      nd->name = hd + ".proto.upsample";
-      nd->in = pr1;
-      nd->out = pru;
-      nd->K = 128;
-      add_param(nd->name + ".weight", {128, 128, 2, 2});
-      add_param(nd->name + ".bias", {128});
-      nodes.push_back(std::move(nd));
-    }
-    MAct* pr2 = act("proto.2", 128, S / 4, S / 4);
-    convbn(hd + ".proto.cv2", pru, 128, 3, 1, {{pr2, 0, 0, 0, 1}});
-    proto = act("out.proto", 32, S / 4, S / 4);
-    convbn(hd + ".proto.cv3", pr2, 32, 1, 1, {{proto, 0, 0, 0, 1}});
   }
 
   int allocate() {
@@ -675,6 +814,43 @@ struct osam_model {
     return cudaSuccess;
   }
 
+  int plan_gradient_modes() {
+    // Gradient write modes.  An activation read by several nodes (as input or as residual) receives one
+    // gradient contribution per read.  The backward visits nodes last to first, so the read in the LAST
+    // reading node writes (beta 0) and every earlier read accumulates (beta 1); inside one node the
+    // residual's gradient is written before the input gradient.  Every buffer a node writes must receive a
+    // gradient: from a later reader, or from the caller (the heads and proto).
+    std::map<const MAct*, int> last_reader;
+    for (int i = 0; i < (int)nodes.size(); i++) {
+      const MNode& nd = *nodes[i];
+      if (nd.kind == N_POOL) continue;
+      last_reader[nd.in] = i;
+      if (nd.res) last_reader[nd.res] = i;
+    }
+    auto gets_grad = [&](const MAct* a, int i) {
+      if (a == proto) return true;
+      for (int l = 0; l < 3; l++)
+        for (int k = 0; k < 3; k++)
+          if (a == head[k][l]) return true;
+      auto it = last_reader.find(a);
+      return it != last_reader.end() && it->second > i;
+    };
+    for (int i = 0; i < (int)nodes.size(); i++) {
+      MNode& nd = *nodes[i];
+      if (nd.kind == N_POOL) continue;
+      if (nd.kind == N_CONVBN) {
+        for (auto& d : nd.dests)
+          if (!gets_grad(d.a, i))
+            return model_fail(OSAM_ERR_INVALID, "%s: nothing reads %s", nd.name.c_str(), d.a->name.c_str());
+      } else if (!gets_grad(nd.out, i)) {
+        return model_fail(OSAM_ERR_INVALID, "%s: nothing reads its output", nd.name.c_str());
+      }
+      if (nd.res) nd.res_accum = last_reader[nd.res] != i;
+      if (nd.in != in) nd.dgrad_accum = last_reader[nd.in] != i || nd.res == nd.in;
+    }
+    return OSAM_OK;
+  }
+
   // ------------------------------------------------------------------ training (reference Model::forward(true)
   // and Model::backward, src/model.cpp:383-470): conv → z, batch statistics, apply; then in reverse order BN
   // backward, weight gradient, input gradient (accumulating where an activation has several consumers).
@@ -803,30 +979,7 @@ struct osam_model {
           return model_fail(OSAM_ERR_NOMEM, "transposed-conv weights");
         cudaMemcpy(wconvt, h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice);
       }
-    // which gradient writes overwrite and which accumulate (reference src/model.cpp:352-366)
-    std::map<const MAct*, bool> written;
-    for (int l = 0; l < 3; l++)
-      for (int k = 0; k < 3; k++) written[head[k][l]] = true;
-    written[proto] = true;
-    for (int i = (int)nodes.size() - 1; i >= 0; i--) {
-      MNode& nd = *nodes[i];
-      if (nd.kind == N_POOL) continue;
-      if (nd.kind == N_CONVBN) {
-        for (auto& d : nd.dests)
-          if (!written.count(d.a)) return model_fail(OSAM_ERR_INVALID, "%s: gradient of %s not ready", nd.name.c_str(),
-                                                     d.a->name.c_str());
-        if (nd.res) {
-          nd.res_accum = written.count(nd.res) > 0;
-          written[nd.res] = true;
-        }
-      } else if (!written.count(nd.out)) {
-        return model_fail(OSAM_ERR_INVALID, "%s: output gradient not ready", nd.name.c_str());
-      }
-      if (nd.in != in) {
-        nd.dgrad_accum = written.count(nd.in) > 0;
-        written[nd.in] = true;
-      }
-    }
+    if (int rc = plan_gradient_modes()) return rc;
     e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "train_init: %s", cudaGetErrorString(e));
     train = true;

@@ -57,8 +57,12 @@ def test_forward_matches_oracle_calibrated(cuda_lib, N, S, seed):
     out = ref.forward(imgs)
     ref64 = yolo_ref.YoloSegRef(w, emulate_fp16=False, dtype=torch.float64)
     o64 = ref64.forward(imgs)
-    for name in ("a0", "a1", "a2", "a3", "a4", "a5", "a6", "a7", "a8", "p3", "p4", "p5"):
-        _check(name, m.act(name), ref.acts[name], ref64.acts[name])
+    # the model's tensors are named by layer (L<i> = the output of model.<i>); the oracle keeps the same
+    # tensors under the reference's names
+    keep = {"L0": "a0", "L1": "a1", "L2": "a2", "L3": "a3", "L4": "a4", "L5": "a5", "L6": "a6", "L7": "a7",
+            "L8": "a8", "L15": "p3", "L18": "p4", "L21": "p5"}
+    for name, oracle_name in keep.items():
+        _check(name, m.act(name), ref.acts[oracle_name], ref64.acts[oracle_name])
     for l in range(3):
         for key, kind in (("box", 0), ("cls", 1), ("coef", 2)):
             _check(f"{key}{l}", m.head(kind, l), out[key][l], o64[key][l])
