@@ -421,6 +421,100 @@ def main():
     barrier()
     fwd_graph_ms = f0.elapsed_time(f1) / K
 
+    # ---- e2e: host buffers through the C-ABI model, every step's copies inside the timed region.  Steps are
+    # pipelined the way a streaming user runs them: step i+1's pinned-host → device input copy (copy stream,
+    # into one of two staging buffers) and step i's device → host copy of its detections and masks (a second
+    # copy stream) overlap the compute of the neighbouring steps; the compute stream moves each staged input
+    # into the model's input buffer (device → device) before its forward.
+    e2e = None
+    if not args.no_e2e:
+        h_in = imgs.pin_memory()  # allocated after the affinity above: NUMA-local to this GPU
+        d_in = model.input()
+        keys = ("n_det", "keep", "box", "score", "masks")
+        copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        stage = [torch.empty_like(d_in) for _ in range(2)]
+        # two result slots on the device (step i writes slot i % 2 while slot (i-1) % 2 drains to the host)
+        # and two on the host: nothing is allocated inside the timed loop
+        A_ = sum(t.shape[1] * t.shape[2] for t in box)
+        slots = []
+        for _ in range(2):
+            dd = {k: torch.empty_like(det[k]) for k in ("n_det", "keep", "box", "score", "coef_g", "masks")}
+            dd["xyxy"] = torch.empty(B, A_, 4, dtype=torch.float32, device=dev)
+            dd["conf"] = torch.empty(B, A_, dtype=torch.float32, device=dev)
+            slots.append(dd)
+        h_out = [{k: torch.empty(det[k].shape, dtype=det[k].dtype, pin_memory=True) for k in keys} for _ in range(2)]
+
+        def post_into(dd):
+            postproc.decode(box, cls, S, out=(dd["xyxy"], dd["conf"]))
+            postproc.nms(dd["xyxy"], dd["conf"], 0.25, 0.7, 300, coef=coef, out=dd)
+            postproc.mask_assemble(dd["coef_g"], proto, dd, S, packed=True, out=dd["masks"])
+
+        def e2e_run(steps):
+            ev_in = [torch.cuda.Event() for _ in range(2)]
+            ev_used = [torch.cuda.Event() for _ in range(2)]
+            ev_out = [torch.cuda.Event() for _ in range(2)]
+            copy_in.wait_stream(stream)
+            copy_out.wait_stream(stream)
+            with torch.cuda.stream(copy_in):
+                stage[0].copy_(h_in, non_blocking=True)
+                ev_in[0].record(copy_in)
+            for i in range(steps):
+                s = i % 2
+                if i + 1 < steps:  # stage the next step's input while this one computes
+                    with torch.cuda.stream(copy_in):
+                        if i >= 1:
+                            copy_in.wait_event(ev_used[(i + 1) % 2])
+                        stage[(i + 1) % 2].copy_(h_in, non_blocking=True)
+                        ev_in[(i + 1) % 2].record(copy_in)
+                stream.wait_event(ev_in[s])
+                # staged input → model input as an elementwise kernel (×1, exact), not a memcpy: a
+                # device-to-device memcpy runs on a copy engine and can queue behind the next step's
+                # host → device copy on that engine, which serialises the copies with the compute
+                torch.mul(stage[s], 1, out=d_in)
+                ev_used[s].record(stream)
+                model.forward(use_graph=True)
+                if i >= 2:
+                    stream.wait_event(ev_out[s])  # slot s's results of step i-2 have reached the host
+                post_into(slots[s])
+                done = torch.cuda.Event()
+                done.record(stream)
+                with torch.cuda.stream(copy_out):
+                    copy_out.wait_event(done)
+                    for k in keys:
+                        h_out[s][k].copy_(slots[s][k], non_blocking=True)
+                    ev_out[s].record(copy_out)
+            stream.wait_stream(copy_out)
+
+        e2e_run(3)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        e2e_run(K)
+        e1.record(stream)
+        barrier()
+        te = e0.elapsed_time(e1)
+        # this rank's host → device copy rate alone (the same pinned buffer, K copies back to back)
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        with torch.cuda.stream(copy_in):
+            h0.record(copy_in)
+            for i in range(K):
+                stage[i % 2].copy_(h_in, non_blocking=True)
+            h1.record(copy_in)
+        barrier()
+        h2d_gbs = h_in.numel() * h_in.element_size() * K / (h0.elapsed_time(h1) / 1e3) / 1e9
+        te_max, = all_max([te])
+        h2d_min = -all_max([-h2d_gbs])[0]
+        e2e = {"value": world * B * K / (te_max / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
+               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in h_out[0].values()),
+               "h2d_gbs_per_rank_min": h2d_min,
+               "h2d_bound_img_per_s": world * B * h2d_min * 1e9 / (h_in.numel() * h_in.element_size()),
+               "cpu_affinity": f"{len(cpus)} CPUs near the GPU (NVML)" if cpus else "default",
+               "result": "detections (n_det, anchor ids, xyxy boxes, scores) + bit-packed masks",
+               "pipelining": "double-buffered: step i+1's H2D and step i's D2H on two copy streams overlap the "
+                             "compute; two preallocated result slots; all K steps' copies inside the timed region"}
+
     # ---- per-kernel durations (roofline, per-node table)
     st = {}
 
@@ -440,85 +534,6 @@ def main():
 
     ms, fwd_graph_ms_max, fwd_kernels_ms = all_max([ms, fwd_graph_ms, fwd_kernels_ms])
     value = world * B * K / (ms / 1e3)
-
-    # ---- e2e: host buffers through the C-ABI model, every step's copies inside the timed region.  Steps are
-    # pipelined the way a streaming user runs them: step i+1's pinned-host → device input copy (copy stream,
-    # into one of two staging buffers) and step i's device → host copy of its detections and masks (a second
-    # copy stream) overlap the compute of the neighbouring steps; the compute stream moves each staged input
-    # into the model's input buffer (device → device) before its forward.
-    e2e = None
-    if not args.no_e2e:
-        h_in = imgs.pin_memory()  # allocated after the affinity above: NUMA-local to this GPU
-        d_in = model.input()
-        keys = ("n_det", "keep", "box", "score", "masks")
-        h_out = {k: torch.empty(det[k].shape, dtype=det[k].dtype, pin_memory=True) for k in keys}
-        copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-        stage = [torch.empty_like(d_in) for _ in range(2)]
-
-        def e2e_run(steps):
-            ev_in = [torch.cuda.Event() for _ in range(2)]
-            ev_used = [torch.cuda.Event() for _ in range(2)]
-            copy_in.wait_stream(stream)
-            with torch.cuda.stream(copy_in):
-                stage[0].copy_(h_in, non_blocking=True)
-                ev_in[0].record(copy_in)
-            keep_alive = []
-            for i in range(steps):
-                s = i % 2
-                if i + 1 < steps:  # stage the next step's input while this one computes
-                    with torch.cuda.stream(copy_in):
-                        if i >= 1:
-                            copy_in.wait_event(ev_used[(i + 1) % 2])
-                        stage[(i + 1) % 2].copy_(h_in, non_blocking=True)
-                        ev_in[(i + 1) % 2].record(copy_in)
-                stream.wait_event(ev_in[s])
-                # staged input → model input as an elementwise kernel (×1, exact), not a memcpy: a
-                # device-to-device memcpy runs on a copy engine and can queue behind the next step's
-                # host → device copy on that engine, which serialises the copies with the compute
-                torch.mul(stage[s], 1, out=d_in)
-                ev_used[s].record(stream)
-                model.forward(use_graph=True)
-                dd = post()
-                done = torch.cuda.Event()
-                done.record(stream)
-                with torch.cuda.stream(copy_out):
-                    copy_out.wait_event(done)
-                    for k in keys:
-                        h_out[k].copy_(dd[k], non_blocking=True)
-                keep_alive.append(dd)  # the device results stay allocated until their copies ran
-            stream.wait_stream(copy_out)
-            return keep_alive
-
-        e2e_run(2)
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        kept = e2e_run(K)
-        e1.record(stream)
-        barrier()
-        del kept
-        te = e0.elapsed_time(e1)
-        # this rank's host → device copy rate alone (the same pinned buffer, K copies back to back)
-        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        with torch.cuda.stream(copy_in):
-            h0.record(copy_in)
-            for i in range(K):
-                stage[i % 2].copy_(h_in, non_blocking=True)
-            h1.record(copy_in)
-        barrier()
-        h2d_gbs = h_in.numel() * h_in.element_size() * K / (h0.elapsed_time(h1) / 1e3) / 1e9
-        te_max, = all_max([te])
-        h2d_min = -all_max([-h2d_gbs])[0]
-        e2e = {"value": world * B * K / (te_max / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
-               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in h_out.values()),
-               "h2d_gbs_per_rank_min": h2d_min,
-               "h2d_bound_img_per_s": world * B * h2d_min * 1e9 / (h_in.numel() * h_in.element_size()),
-               "cpu_affinity": f"{len(cpus)} CPUs near the GPU (NVML)" if cpus else "default",
-               "result": "detections (n_det, anchor ids, xyxy boxes, scores) + bit-packed masks",
-               "pipelining": "double-buffered: step i+1's H2D and step i's D2H on two copy streams overlap the "
-                             "compute; all K steps' copies inside the timed region"}
 
     # ---- roofline of the dominant kernel (timed in a sub-second pass: the burst peak applies)
     peaks = load_peaks()

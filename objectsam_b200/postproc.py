@@ -23,31 +23,38 @@ def _level_hw(ts):
     return (ctypes.c_int * 6)(*[v for t in ts for v in (t.shape[1], t.shape[2])])
 
 
-def decode(box, cls, imgsz: int, reg_max: int = 16, stream=None):
-    """box[l] (B,H,W,4·reg_max), cls[l] (B,H,W,1) fp16 → xyxy (B,A,4) float32 px, conf (B,A) float32."""
+def decode(box, cls, imgsz: int, reg_max: int = 16, stream=None, out=None):
+    """box[l] (B,H,W,4·reg_max), cls[l] (B,H,W,1) fp16 → xyxy (B,A,4) float32 px, conf (B,A) float32.
+    out=(xyxy, conf) writes into existing tensors instead of allocating."""
     B = box[0].shape[0]
     A = sum(t.shape[1] * t.shape[2] for t in box)
-    xyxy = torch.empty(B, A, 4, dtype=torch.float32, device=box[0].device)
-    conf = torch.empty(B, A, dtype=torch.float32, device=box[0].device)
+    if out is not None:
+        xyxy, conf = out
+    else:
+        xyxy = torch.empty(B, A, 4, dtype=torch.float32, device=box[0].device)
+        conf = torch.empty(B, A, dtype=torch.float32, device=box[0].device)
     check(lib().osam_decode(_ptrs(box), _ptrs(cls), _level_hw(box), B, imgsz, reg_max, xyxy.data_ptr(),
                             conf.data_ptr(), stream_ptr(stream)))
     return xyxy, conf
 
 
 def nms(xyxy, conf, conf_th: float = 0.25, iou_th: float = 0.7, max_det: int = 300, forced: bool = False,
-        coef=None, stream=None) -> dict:
+        coef=None, stream=None, out=None) -> dict:
     """Per image: n_det, keep (anchor ids, −1 padded), box (xyxy), score; with coef heads also coef_g, the
-    kept anchors' mask coefficients laid out for mask_assemble."""
+    kept anchors' mask coefficients laid out for mask_assemble.  out= a dict of that form from an earlier
+    call with the same shapes: written in place instead of allocated."""
     B, A = conf.shape
     dev = conf.device
-    out = dict(n_det=torch.empty(B, dtype=torch.int32, device=dev),
-               keep=torch.empty(B, max_det, dtype=torch.int32, device=dev),
-               box=torch.empty(B, max_det, 4, dtype=torch.float32, device=dev),
-               score=torch.empty(B, max_det, dtype=torch.float32, device=dev))
     pad = (max_det + 127) // 128 * 128
+    if out is None:
+        out = dict(n_det=torch.empty(B, dtype=torch.int32, device=dev),
+                   keep=torch.empty(B, max_det, dtype=torch.int32, device=dev),
+                   box=torch.empty(B, max_det, 4, dtype=torch.float32, device=dev),
+                   score=torch.empty(B, max_det, dtype=torch.float32, device=dev))
     coef_p, hw, cg = None, None, None
     if coef is not None:
-        out["coef_g"] = torch.empty(B, pad, 32, dtype=torch.float16, device=dev)
+        if "coef_g" not in out:
+            out["coef_g"] = torch.empty(B, pad, 32, dtype=torch.float16, device=dev)
         coef_p, hw, cg = _ptrs(coef), _level_hw(coef), out["coef_g"].data_ptr()
     check(lib().osam_nms(xyxy.data_ptr(), conf.data_ptr(), B, A, float(conf_th), float(iou_th), max_det,
                          int(forced), coef_p, hw, out["n_det"].data_ptr(), out["keep"].data_ptr(),
@@ -55,12 +62,15 @@ def nms(xyxy, conf, conf_th: float = 0.25, iou_th: float = 0.7, max_det: int = 3
     return out
 
 
-def mask_assemble(coef_g, proto, det: dict, imgsz: int, packed: bool = False, stream=None):
+def mask_assemble(coef_g, proto, det: dict, imgsz: int, packed: bool = False, stream=None, out=None):
     """coef_g (B, ceil128(max_det), 32) fp16, proto (B, Hp, Wp, 32) fp16 → masks (B, max_det, Hp, Wp) u8, or
-    with packed=True (B, max_det, ceil(Hp·Wp/32)) int32 bit words (pixel 32·j + k = bit k of word j)."""
+    with packed=True (B, max_det, ceil(Hp·Wp/32)) int32 bit words (pixel 32·j + k = bit k of word j).
+    out= an existing tensor of that shape and type to write into."""
     B, Hp, Wp, _ = proto.shape
     max_det = det["keep"].shape[1]
-    if packed:
+    if out is not None:
+        masks = out
+    elif packed:
         masks = torch.empty(B, max_det, (Hp * Wp + 31) // 32, dtype=torch.int32, device=proto.device)
     else:
         masks = torch.empty(B, max_det, Hp, Wp, dtype=torch.uint8, device=proto.device)
