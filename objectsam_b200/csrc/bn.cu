@@ -35,46 +35,51 @@ __device__ __forceinline__ float sigmoid_fast(float y) {
   return rcp_approx(1.f + ex2_approx(-kLog2e * fmaxf(y, -80.f)));
 }
 
-// Pixel index of the top-left of row `row`'s 2×2 block in the 2H×2W upsampled grid (nearest ×2).
-__device__ __forceinline__ long long up2_base(long long row, int H, int W) {
-  const long long hw = (long long)H * W;
-  const long long n = row / hw;
-  const int rem = int(row - n * hw), h = rem / W, w = rem - h * W;
-  return (n * 2 * H + 2 * h) * (2LL * W) + 2 * w;
+// Row r = n·H·W + h·W + w of an H×W map lands, in the 2H×2W map that its nearest 2× upsample fills, on
+// the 2×2 block whose top-left pixel is 2·(2·(n·H + h)·W + w); with nh = r / W that is 4·nh·W + 2·(r − nh·W).
+__device__ __forceinline__ long long up2_corner(long long r, int W) {
+  const long long nh = r / W;
+  return 4 * nh * W + 2 * (r - nh * W);
 }
 
-struct GradDest {
-  const __half* g;  // gradient of the destination buffer (NHWC, ctot channels)
-  int ctot, choff, c0, c1, up;
+// A destination the forward wrote to, read back as a gradient source.  `g` is offset so that channel c
+// of the producing conv sits at g[pixel·ctot + c] (g = buffer + choff − c0); it holds channels
+// [c_lo, c_hi) of the producer, 2×2-upsampled when up = 2.
+struct GradSrc {
+  const __half* g;
+  int ctot, c_lo, c_hi, up;
 };
 
-// dA for channels c..c+7 of `row`: the sum of the gradients of every destination the forward wrote
-// that channel to, a 2×2 sum for the upsampled ones (reference gather8, src/bn.cu:46-66).
-__device__ __forceinline__ void gather_grad8(const GradDest* dl, int ndl, long long row, int c, int H, int W,
-                                             float (&dA)[8]) {
+// dA for channels c..c+7 of row r: the sum over every gradient source that holds those channels; an
+// upsampled source contributes the four pixels of its 2×2 block.
+__device__ __forceinline__ void dest_grad_sum8(const GradSrc* srcs, int n, long long r, int c, int W,
+                                               float (&dA)[8]) {
 #pragma unroll
   for (int i = 0; i < 8; i++) dA[i] = 0.f;
+  long long corner = -1;
 #pragma unroll
   for (int k = 0; k < OSAM_MAX_DEST; k++) {
-    if (k >= ndl) break;
-    const GradDest& d = dl[k];
-    if (c < d.c0 || c >= d.c1) continue;
-    const int cc = d.choff + c - d.c0;
+    if (k >= n) break;
+    const GradSrc sk = srcs[k];
+    if (c < sk.c_lo || c >= sk.c_hi) continue;
+    const __half* base = sk.g + c;
+    const long long pitch = sk.ctot;
     float t[8];
-    if (d.up == 1) {
-      ld8h(d.g + row * d.ctot + cc, t);
+    if (sk.up == 1) {
+      ld8h(base + r * pitch, t);
 #pragma unroll
       for (int i = 0; i < 8; i++) dA[i] += t[i];
-    } else {
-      const long long b = up2_base(row, H, W), W2 = 2LL * W;
-      const long long q[4] = {b, b + 1, b + W2, b + W2 + 1};
+      continue;
+    }
+    if (corner < 0) corner = up2_corner(r, W);
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
-        ld8h(d.g + q[u] * d.ctot + cc, t);
+    for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+      for (int dx = 0; dx < 2; dx++) {
+        ld8h(base + (corner + dy * 2LL * W + dx) * pitch, t);
 #pragma unroll
         for (int i = 0; i < 8; i++) dA[i] += t[i];
       }
-    }
   }
 }
 
@@ -91,34 +96,53 @@ __device__ __forceinline__ void ld8f_any(const float* p, float (&o)[8]) {
 
 enum RedMode : int { RED_STATS = 0, RED_BWD = 1, RED_SUM = 2 };
 
-struct RedArgs {
-  const __half* z;  // [M][C]
-  long long M;
-  int H, W, C;      // H, W: spatial size of z (for the upsampled gradient gather)
-  int rowlanes;     // rows processed side by side by one CTA (kBnT / (C/8))
-  long long rows;   // rows per CTA chunk
-  // RED_STATS
+// The rows a pass walks: z as [M][C] (W = the map's width, for upsampled destinations); each CTA owns
+// `chunk` consecutive rows and processes `lanes` of them side by side (kBnT / (C/8) threads per row).
+struct Rows {
+  const __half* z;
+  long long M, chunk;
+  int W, C, lanes;
+};
+// Cross-CTA reduction state: fp64 sums [2C] and an arrival count, zero between calls.
+struct Accum {
+  double* acc;
+  unsigned* arrivals;
+};
+// RED_STATS: batch statistics in, the normalisation and the running statistics out.
+struct StatsIO {
   const float* gamma;
   const float* beta;
+  float momentum, eps;
   float* run_mean;
   float* run_var;
-  float mom, eps;
   float* mean;
   float* istd;
   float* scale;
   float* shift;
-  // RED_BWD (reads mean/istd/scale/shift)
-  GradDest dl[OSAM_MAX_DEST];
-  int ndl, act;
-  float* sums;      // [2C] Σg/M, Σg·x̂/M for the apply pass
-  float* gw_gamma;
-  float* gw_beta;
-  int accum;
-  // RED_SUM
+};
+// RED_BWD: what the forward used, where the gradients come from, where the sums go.
+struct BwdIO {
+  const float* mean;
+  const float* istd;
+  const float* scale;
+  const float* shift;
+  GradSrc src[OSAM_MAX_DEST];
+  int nsrc, silu, accum;
+  float* gmean;  // [2C] Σg/M, Σg·x̂/M for the apply pass
+  float* d_gamma;
+  float* d_beta;
+};
+// RED_SUM: per-channel sums (=|+=) into out.
+struct SumIO {
   float* out;
-  // all
-  double* acc;      // [2C] zero on entry, zero again on exit
-  unsigned* counter;
+  int accum;
+};
+struct RedArgs {
+  Rows rows;
+  Accum red;
+  StatsIO st;
+  BwdIO bw;
+  SumIO sum;
 };
 
 // Per-channel reductions over the rows of z (reference k_reduce<0|1>, src/bn.cu:112-202, and
@@ -131,24 +155,25 @@ template <int MODE, int U, bool SIMPLE = false>
 __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(const RedArgs P) {
   extern __shared__ float2 bn_red[];  // [rowlanes][C]
   __shared__ unsigned s_last;
-  const int C = P.C, V = C >> 3, RL = P.rowlanes;
+  const Rows R = P.rows;
+  const int C = R.C, V = C >> 3, RL = R.lanes;
   const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
   const bool active = rl < RL;
-  const long long r0 = (long long)blockIdx.x * P.rows;
-  const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
+  const long long r0 = (long long)blockIdx.x * R.chunk;
+  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
   float a[8], b[8];
 #pragma unroll
   for (int i = 0; i < 8; i++) a[i] = b[i] = 0.f;
   if (active) {
     // RED_STATS: k0 = K.  RED_BWD: k0 = scale, k1 = shift, k2 = istd, k3 = −mean·istd (x̂ = z·k2 + k3).
     float k0[8], k1[8], k2[8], k3[8];
-    if (MODE == RED_STATS) ld8f_any(P.run_mean + c, k0);
+    if (MODE == RED_STATS) ld8f_any(P.st.run_mean + c, k0);
     if (MODE == RED_BWD) {
       float mu[8];
-      ld8f_any(P.scale + c, k0);
-      ld8f_any(P.shift + c, k1);
-      ld8f_any(P.istd + c, k2);
-      ld8f_any(P.mean + c, mu);
+      ld8f_any(P.bw.scale + c, k0);
+      ld8f_any(P.bw.shift + c, k1);
+      ld8f_any(P.bw.istd + c, k2);
+      ld8f_any(P.bw.mean + c, mu);
 #pragma unroll
       for (int i = 0; i < 8; i++) k3[i] = -mu[i] * k2[i];
     }
@@ -159,15 +184,15 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
       for (int u = 0; u < U; u++) {
         const long long rr = r + (long long)u * RL;
         if (rr < r1) {
-          zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
-          if (SIMPLE) gr[u] = *reinterpret_cast<const uint4*>(P.dl[0].g + rr * P.dl[0].ctot + P.dl[0].choff + c);
+          zr[u] = *reinterpret_cast<const uint4*>(R.z + rr * C + c);
+          if (SIMPLE) gr[u] = *reinterpret_cast<const uint4*>(P.bw.src[0].g + rr * P.bw.src[0].ctot + c);
         }
       }
       if (MODE == RED_BWD && !SIMPLE) {
 #pragma unroll
         for (int u = 0; u < U; u++) {
           const long long rr = r + (long long)u * RL;
-          if (rr < r1) gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dA[SIMPLE ? 0 : u]);
+          if (rr < r1) dest_grad_sum8(P.bw.src, P.bw.nsrc, rr, c, R.W, dA[SIMPLE ? 0 : u]);
         }
       }
 #pragma unroll
@@ -184,7 +209,7 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
             b[i] = fmaf(d, d, b[i]);
           } else if (MODE == RED_BWD) {
             float g = dA[SIMPLE ? 0 : u][i];
-            if (P.act) {
+            if (P.bw.silu) {
               const float y = fmaf(k0[i], v[i], k1[i]), s = sigmoid_fast(y);
               g *= s * fmaf(y, 1.f - s, 1.f);
             }
@@ -207,77 +232,72 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
       sa += t.x;
       sb += t.y;
     }
-    atomicAdd(&P.acc[ch], double(sa));
-    if (MODE != RED_SUM) atomicAdd(&P.acc[C + ch], double(sb));
+    atomicAdd(&P.red.acc[ch], double(sa));
+    if (MODE != RED_SUM) atomicAdd(&P.red.acc[C + ch], double(sb));
   }
   // The last CTA to arrive finalises (threadfence reduction: every CTA's atomics are visible before its
   // arrival on the counter).
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(P.counter, 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) s_last = atomicAdd(P.red.arrivals, 1u) == gridDim.x - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const double Md = double(P.M);
+  const double Md = double(R.M);
   for (int ch = threadIdx.x; ch < C; ch += kBnT) {
-    const double sx = __ldcg(&P.acc[ch]);
-    const double sy = MODE != RED_SUM ? __ldcg(&P.acc[C + ch]) : 0.0;
-    P.acc[ch] = 0.0;
-    if (MODE != RED_SUM) P.acc[C + ch] = 0.0;
+    const double sx = __ldcg(&P.red.acc[ch]);
+    const double sy = MODE != RED_SUM ? __ldcg(&P.red.acc[C + ch]) : 0.0;
+    P.red.acc[ch] = 0.0;
+    if (MODE != RED_SUM) P.red.acc[C + ch] = 0.0;
     if (MODE == RED_STATS) {
       // mean = K + E[z−K]; biased variance E[(z−K)²] − E[z−K]² (clamped at 0) for normalising; the
       // running variance takes the unbiased M/(M−1) form (reference src/bn.cu:176-191).
-      const float K = P.run_mean[ch];
+      const StatsIO S = P.st;
+      const float K = S.run_mean[ch];
       const float dm = float(sx / Md);
       float var = float(sy / Md - double(dm) * double(dm));
       var = var < 0.f ? 0.f : var;
-      const float m = K + dm, is = rsqrtf(var + P.eps);
-      P.mean[ch] = m;
-      P.istd[ch] = is;
-      const float sc = P.gamma[ch] * is;
-      P.scale[ch] = sc;
-      P.shift[ch] = P.beta[ch] - m * sc;
-      if (P.mom > 0.f) {
-        P.run_mean[ch] = (1.f - P.mom) * K + P.mom * m;
-        P.run_var[ch] = (1.f - P.mom) * P.run_var[ch] + P.mom * float(double(var) * Md / (Md - 1.0));
+      const float m = K + dm, is = rsqrtf(var + S.eps);
+      S.mean[ch] = m;
+      S.istd[ch] = is;
+      const float sc = S.gamma[ch] * is;
+      S.scale[ch] = sc;
+      S.shift[ch] = S.beta[ch] - m * sc;
+      if (S.momentum > 0.f) {
+        S.run_mean[ch] = (1.f - S.momentum) * K + S.momentum * m;
+        S.run_var[ch] = (1.f - S.momentum) * S.run_var[ch] + S.momentum * float(double(var) * Md / (Md - 1.0));
       }
     } else if (MODE == RED_BWD) {
-      P.sums[ch] = float(sx / Md);
-      P.sums[C + ch] = float(sy / Md);
-      if (P.accum) {
-        P.gw_beta[ch] += float(sx);
-        P.gw_gamma[ch] += float(sy);
-      } else {
-        P.gw_beta[ch] = float(sx);
-        P.gw_gamma[ch] = float(sy);
-      }
+      const BwdIO G = P.bw;
+      G.gmean[ch] = float(sx / Md);
+      G.gmean[C + ch] = float(sy / Md);
+      G.d_beta[ch] = G.accum ? G.d_beta[ch] + float(sx) : float(sx);
+      G.d_gamma[ch] = G.accum ? G.d_gamma[ch] + float(sy) : float(sy);
     } else {
-      P.out[ch] = P.accum ? P.out[ch] + float(sx) : float(sx);
+      P.sum.out[ch] = P.sum.accum ? P.sum.out[ch] + float(sx) : float(sx);
     }
   }
-  if (threadIdx.x == 0) *P.counter = 0u;
+  if (threadIdx.x == 0) *P.red.arrivals = 0u;
 }
 
 struct ApplyArgs {
-  const __half* z;
-  long long M;
-  int H, W, C, rowlanes;
-  long long rows;
+  Rows rows;
   const float* scale;
   const float* shift;
   const __half* res;  // [M][C] added after the activation, or null
   DestDev dest[OSAM_MAX_DEST];
-  int ndest, act;
+  int ndest, silu;
 };
 
 // a = act(scale·z + shift) (+ res) → every destination (reference k_apply, src/bn.cu:204-238).
 template <int U>
 __global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
-  const int C = P.C, V = C >> 3, RL = P.rowlanes;
+  const Rows R = P.rows;
+  const int C = R.C, V = C >> 3, RL = R.lanes;
   const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
   if (rl >= RL) return;
-  const long long r0 = (long long)blockIdx.x * P.rows;
-  const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
+  const long long r0 = (long long)blockIdx.x * R.chunk;
+  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
   float sc[8], sh[8];
   ld8f_any(P.scale + c, sc);
   ld8f_any(P.shift + c, sh);
@@ -287,7 +307,7 @@ __global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
     for (int u = 0; u < U; u++) {
       const long long rr = r - (long long)u * RL;
       if (rr >= r0) {
-        zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
+        zr[u] = *reinterpret_cast<const uint4*>(R.z + rr * C + c);
         if (P.res) rr4[u] = *reinterpret_cast<const uint4*>(P.res + rr * C + c);
       }
     }
@@ -301,7 +321,7 @@ __global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         const float y = fmaf(sc[i], o[i], sh[i]);
-        o[i] = P.act ? y * sigmoid_fast(y) : y;
+        o[i] = P.silu ? y * sigmoid_fast(y) : y;
         if (P.res) o[i] += rv[i];
       }
 #pragma unroll 1
@@ -313,11 +333,11 @@ __global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
         if (d.up == 1) {
           st8h(d.p + rr * d.ctot + cc, o);
         } else {
-          const long long b = up2_base(rr, P.H, P.W), W2 = 2LL * P.W;
-          st8h(d.p + b * d.ctot + cc, o);
-          st8h(d.p + (b + 1) * d.ctot + cc, o);
-          st8h(d.p + (b + W2) * d.ctot + cc, o);
-          st8h(d.p + (b + W2 + 1) * d.ctot + cc, o);
+          const long long q = up2_corner(rr, R.W);
+#pragma unroll
+          for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+            for (int dx = 0; dx < 2; dx++) st8h(d.p + (q + dy * 2LL * R.W + dx) * d.ctot + cc, o);
         }
       }
     }
@@ -325,17 +345,14 @@ __global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
 }
 
 struct BwdArgs {
-  const __half* z;
-  long long M;
-  int H, W, C, rowlanes;
-  long long rows;
+  Rows rows;
   const float* mean;
   const float* istd;
   const float* scale;
   const float* shift;
-  const float* sums;  // [2C] from the reduction pass
-  GradDest dl[OSAM_MAX_DEST];
-  int ndl, act;
+  const float* gmean;  // [2C] from the reduction pass
+  GradSrc src[OSAM_MAX_DEST];
+  int nsrc, silu;
   __half* dz;
   __half* res_grad;
   int res_accum;
@@ -344,11 +361,12 @@ struct BwdArgs {
 // dz = scale·(g − mean(g) − x̂·mean(g·x̂)); res_grad (=|+=) dA (reference k_bwd_apply, src/bn.cu:240-270).
 template <int U, bool SIMPLE = false>
 __global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
-  const int C = P.C, V = C >> 3, RL = P.rowlanes;
+  const Rows R = P.rows;
+  const int C = R.C, V = C >> 3, RL = R.lanes;
   const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
   if (rl >= RL) return;
-  const long long r0 = (long long)blockIdx.x * P.rows;
-  const long long r1 = r0 + P.rows < P.M ? r0 + P.rows : P.M;
+  const long long r0 = (long long)blockIdx.x * R.chunk;
+  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
   // dz = scale·g + ka·z + kb with ka = −scale·istd·m2, kb = scale·(istd·m2·mean − m1)
   float sc[8], sh[8], ka[8], kb[8];
   {
@@ -357,8 +375,8 @@ __global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
     ld8f_any(P.shift + c, sh);
     ld8f_any(P.mean + c, mu);
     ld8f_any(P.istd + c, is);
-    ld8f(P.sums + c, m1);
-    ld8f(P.sums + C + c, m2);
+    ld8f(P.gmean + c, m1);
+    ld8f(P.gmean + C + c, m2);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       ka[i] = -sc[i] * is[i] * m2[i];
@@ -372,11 +390,11 @@ __global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
     for (int u = 0; u < U; u++) {
       const long long rr = r - (long long)u * RL;
       if (rr >= r0) {
-        zr[u] = *reinterpret_cast<const uint4*>(P.z + rr * C + c);
+        zr[u] = *reinterpret_cast<const uint4*>(R.z + rr * C + c);
         if (SIMPLE)
-          gr[u] = *reinterpret_cast<const uint4*>(P.dl[0].g + rr * P.dl[0].ctot + P.dl[0].choff + c);
+          gr[u] = *reinterpret_cast<const uint4*>(P.src[0].g + rr * P.src[0].ctot + c);
         else
-          gather_grad8(P.dl, P.ndl, rr, c, P.H, P.W, dAf[SIMPLE ? 0 : u]);
+          dest_grad_sum8(P.src, P.nsrc, rr, c, R.W, dAf[SIMPLE ? 0 : u]);
       }
     }
 #pragma unroll
@@ -403,7 +421,7 @@ __global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         float g = dA[i];
-        if (P.act) {
+        if (P.silu) {
           const float y = fmaf(sc[i], v[i], sh[i]), s = sigmoid_fast(y);
           g *= s * fmaf(y, 1.f - s, 1.f);
         }
@@ -614,13 +632,9 @@ int osam_bn_forward_stats(const void* z, int N, int H, int W, int C, const float
   const Chunking k = chunking(M, C, 0);
   const BnWs w = bn_ws(ws, C);
   RedArgs P{};
-  P.z = static_cast<const __half*>(z);
-  P.M = M; P.H = H; P.W = W; P.C = C;
-  P.rowlanes = k.rowlanes; P.rows = k.rows;
-  P.gamma = gamma; P.beta = beta; P.run_mean = run_mean; P.run_var = run_var;
-  P.mom = momentum; P.eps = eps;
-  P.mean = mean; P.istd = istd; P.scale = scale; P.shift = shift;
-  P.acc = w.acc; P.counter = w.counter;
+  P.rows = Rows{static_cast<const __half*>(z), M, k.rows, W, C, k.rowlanes};
+  P.red = Accum{w.acc, w.counter};
+  P.st = StatsIO{gamma, beta, momentum, eps, run_mean, run_var, mean, istd, scale, shift};
   const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
   k_bn_reduce<RED_STATS, kUStats><<<k.nblk, kBnT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
   return launched("osam_bn_forward_stats");
@@ -636,13 +650,12 @@ int osam_bn_forward_apply(const void* z, int N, int H, int W, int C, const float
   const long long M = (long long)N * H * W;
   const Chunking k = chunking(M, C, 0);
   ApplyArgs P{};
-  P.z = static_cast<const __half*>(z);
-  P.M = M; P.H = H; P.W = W; P.C = C;
-  P.rowlanes = k.rowlanes; P.rows = k.rows;
-  P.scale = scale; P.shift = shift;
+  P.rows = Rows{static_cast<const __half*>(z), M, k.rows, W, C, k.rowlanes};
+  P.scale = scale;
+  P.shift = shift;
   P.res = static_cast<const __half*>(res);
   P.ndest = n_dest;
-  P.act = act ? 1 : 0;
+  P.silu = act ? 1 : 0;
   for (int i = 0; i < n_dest; i++) {
     const osam_dest& d = dests[i];
     const int c1 = d.c1 > 0 ? d.c1 : C;
@@ -680,25 +693,22 @@ int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mea
     if (!d.p || !al16(d.p) || d.c0 < 0 || d.c0 % 8 || c1 % 8 || c1 > C || d.c0 >= c1 || d.choff < 0 ||
         d.choff % 8 || d.ctot % 8 || d.choff + (c1 - d.c0) > d.ctot || (d.up != 1 && d.up != 2))
       return bad(OSAM_ERR_INVALID, "bn_backward: gradient destination (16-byte aligned, channels multiple of 8)");
-    P.dl[i] = B.dl[i] = GradDest{static_cast<const __half*>(d.p), d.ctot, d.choff, d.c0, c1, d.up};
+    P.bw.src[i] = B.src[i] = GradSrc{static_cast<const __half*>(d.p) + d.choff - d.c0, d.ctot, d.c0, c1, d.up};
   }
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  P.z = B.z = static_cast<const __half*>(z);
-  P.M = B.M = M; P.H = B.H = H; P.W = B.W = W; P.C = B.C = C;
-  P.rowlanes = B.rowlanes = k.rowlanes; P.rows = B.rows = k.rows;
-  P.ndl = B.ndl = n_dest;
-  P.act = B.act = act ? 1 : 0;
-  P.mean = const_cast<float*>(mean);
-  P.istd = const_cast<float*>(istd);
-  P.scale = const_cast<float*>(scale);
-  P.shift = const_cast<float*>(shift);
-  B.mean = mean;
-  B.istd = istd;
-  B.scale = scale;
-  B.shift = shift;
-  P.sums = w.sums; B.sums = w.sums;
-  P.gw_gamma = gw_gamma; P.gw_beta = gw_beta; P.accum = accum ? 1 : 0;
-  P.acc = w.acc; P.counter = w.counter;
+  P.rows = B.rows = Rows{static_cast<const __half*>(z), M, k.rows, W, C, k.rowlanes};
+  P.red = Accum{w.acc, w.counter};
+  P.bw.nsrc = B.nsrc = n_dest;
+  P.bw.silu = B.silu = act ? 1 : 0;
+  P.bw.mean = B.mean = mean;
+  P.bw.istd = B.istd = istd;
+  P.bw.scale = B.scale = scale;
+  P.bw.shift = B.shift = shift;
+  P.bw.gmean = w.sums;
+  B.gmean = w.sums;
+  P.bw.d_gamma = gw_gamma;
+  P.bw.d_beta = gw_beta;
+  P.bw.accum = accum ? 1 : 0;
   B.dz = static_cast<__half*>(dz);
   B.res_grad = static_cast<__half*>(res_grad);
   B.res_accum = res_accum ? 1 : 0;
@@ -728,11 +738,9 @@ int osam_chan_sum(const void* x, int64_t M, int C, float* out, int accum, void* 
   if (C % 8 == 0 && al16(x)) {
     const Chunking k = chunking(M, C, 0);
     RedArgs P{};
-    P.z = static_cast<const __half*>(x);
-    P.M = M; P.H = 1; P.W = 1; P.C = C;
-    P.rowlanes = k.rowlanes; P.rows = k.rows;
-    P.out = out; P.accum = accum ? 1 : 0;
-    P.acc = acc; P.counter = counter;
+    P.rows = Rows{static_cast<const __half*>(x), M, k.rows, 1, C, k.rowlanes};
+    P.red = Accum{acc, counter};
+    P.sum = SumIO{out, accum ? 1 : 0};
     const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
     k_bn_reduce<RED_SUM, kUStats><<<k.nblk, kBnT, smem, st>>>(P);
   } else {

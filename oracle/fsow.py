@@ -1,8 +1,12 @@
 """FSOW tensor-bundle files (test infrastructure).
 
-Format (reference src/fsow.h:28-67, pytools/fsow.py:1-44): b"FSOW0001", u32 count, then per tensor
-u16 name length, utf-8 name, u8 ndim, ndim × i64 shape, u8 dtype (0 f32, 1 i32, 2 u8), raw little-endian
-data.  Weights keep PyTorch names and layouts (OIHW).
+The reference's exchange format for weights and tensors (reference src/fsow.h:28-67): the 8-byte tag
+b"FSOW0001", a little-endian u32 record count, then one record per tensor —
+    u16 name length | utf-8 name | u8 rank | rank x i64 extents | u8 element code | raw little-endian data
+with element codes 0 = float32, 1 = int32, 2 = uint8.  Weights keep PyTorch names and layouts (OIHW).
+
+This module parses a whole file from one buffer with a cursor, and builds each record in memory before
+the file is written (atomically: temp file, then rename), so a half-written bundle is never seen.
 """
 from __future__ import annotations
 
@@ -11,47 +15,75 @@ import struct
 
 import numpy as np
 
-MAGIC = b"FSOW0001"
-_CODE = {np.dtype(np.float32): 0, np.dtype(np.int32): 1, np.dtype(np.uint8): 2}
-_DTYPE = {0: np.float32, 1: np.int32, 2: np.uint8}
+TAG = b"FSOW0001"
+CODES = (np.dtype("<f4"), np.dtype("<i4"), np.dtype("u1"))  # element code = index
+
+
+def _code(dtype) -> int:
+    for i, d in enumerate(CODES):
+        if np.dtype(dtype).newbyteorder("<") == d:
+            return i
+    return -1
+
+
+def encode(name: str, arr) -> bytes:
+    """One record.  Element types other than the three the format knows are stored as float32."""
+    a = np.asarray(arr)
+    if _code(a.dtype) < 0:
+        a = a.astype(np.float32)
+    code = _code(a.dtype)
+    raw = np.ascontiguousarray(a, dtype=CODES[code])
+    key = name.encode("utf-8")
+    head = struct.pack(f"<H{len(key)}sB{raw.ndim}qB", len(key), key, raw.ndim, *raw.shape, code)
+    return head + raw.tobytes()
 
 
 def save(path: str, tensors: dict) -> None:
-    """Write atomically (temp file + rename), like fsow_save (src/fsow.h:53-67)."""
-    tmp = path + ".tmp"
+    body = b"".join(encode(k, tensors[k]) for k in sorted(tensors))
+    tmp = f"{path}.partial"
     with open(tmp, "wb") as f:
-        f.write(MAGIC)
-        f.write(struct.pack("<I", len(tensors)))
-        for name, arr in sorted(tensors.items()):
-            a = np.ascontiguousarray(arr)
-            if a.dtype not in _CODE:
-                a = a.astype(np.float32)
-            nb = name.encode()
-            f.write(struct.pack("<H", len(nb)))
-            f.write(nb)
-            f.write(struct.pack("<B", a.ndim))
-            f.write(struct.pack(f"<{a.ndim}q", *a.shape))
-            f.write(struct.pack("<B", _CODE[a.dtype]))
-            f.write(a.astype(a.dtype.newbyteorder("<"), copy=False).tobytes())
+        f.write(TAG + struct.pack("<I", len(tensors)) + body)
     os.replace(tmp, path)
 
 
+class _Cursor:
+    def __init__(self, buf: bytes, where: str):
+        self.buf, self.at, self.where = memoryview(buf), 0, where
+
+    def take(self, fmt: str):
+        size = struct.calcsize(fmt)
+        if self.at + size > len(self.buf):
+            raise ValueError(f"{self.where}: truncated at byte {self.at}")
+        vals = struct.unpack_from(fmt, self.buf, self.at)
+        self.at += size
+        return vals
+
+    def raw(self, n: int) -> memoryview:
+        if self.at + n > len(self.buf):
+            raise ValueError(f"{self.where}: truncated at byte {self.at}")
+        out = self.buf[self.at:self.at + n]
+        self.at += n
+        return out
+
+
 def load(path: str) -> dict:
-    out = {}
     with open(path, "rb") as f:
-        if f.read(8) != MAGIC:
-            raise ValueError(f"{path}: not an FSOW file")
-        (n,) = struct.unpack("<I", f.read(4))
-        for _ in range(n):
-            (ln,) = struct.unpack("<H", f.read(2))
-            name = f.read(ln).decode()
-            (nd,) = struct.unpack("<B", f.read(1))
-            shape = struct.unpack(f"<{nd}q", f.read(8 * nd)) if nd else ()
-            (code,) = struct.unpack("<B", f.read(1))
-            dt = np.dtype(_DTYPE[code])
-            cnt = int(np.prod(shape)) if nd else 1
-            buf = f.read(cnt * dt.itemsize)
-            if len(buf) != cnt * dt.itemsize:
-                raise ValueError(f"{path}: truncated at {name}")
-            out[name] = np.frombuffer(buf, dt.newbyteorder("<")).astype(dt).reshape(shape)
-    return out
+        data = f.read()
+    if data[:8] != TAG:
+        raise ValueError(f"{path}: not an FSOW file")
+    cur = _Cursor(data, path)
+    cur.at = 8
+    (count,) = cur.take("<I")
+    tensors = {}
+    for _ in range(count):
+        (klen,) = cur.take("<H")
+        name = bytes(cur.raw(klen)).decode("utf-8")
+        (rank,) = cur.take("<B")
+        shape = cur.take(f"<{rank}q")
+        (code,) = cur.take("<B")
+        if code >= len(CODES):
+            raise ValueError(f"{path}: {name} has unknown element code {code}")
+        dt = CODES[code]
+        n = int(np.prod(shape, dtype=np.int64))
+        tensors[name] = np.frombuffer(cur.raw(n * dt.itemsize), dt).astype(dt.newbyteorder("=")).reshape(shape)
+    return tensors
