@@ -321,10 +321,18 @@ int osam_model_get_grad(osam_model* m, const char* name, float* out, int64_t n);
  * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises.
  * Launches are asynchronous, so a kernel whose bounded wait ran out (OSAM_ERR_TIMEOUT: it returned early
  * and its output is incomplete) is seen here, not in the status of the call that launched it; callers
- * check it at a point where they synchronise anyway.  The word is a static device variable of the
- * library: nothing is allocated for it.  No counterpart in the reference (cuDNN has no device-side
- * status; its kernels cannot time out). */
+ * check it at a point where they synchronise anyway, or poll osam_device_error_peek.  The word is one int
+ * of host-mapped pinned memory allocated at the first plan or model creation (a static device variable
+ * before that); no launch allocates.  No counterpart in the reference (cuDNN has no device-side status;
+ * its kernels cannot time out). */
 int osam_device_error(void);
+
+/* The error word as it stands, read from host-mapped memory without synchronising anything and without
+ * clearing it: non-zero once a kernel that has already finished recorded a failure.  Cheap enough to call
+ * before every launch (the ConvOp shim does, and aborts like the reference's FSO_ASSERT).  Covers kernels
+ * launched after the first plan or model creation, which allocates the mapped word (pinned host memory,
+ * once per process); returns 0 before that.  No counterpart in the reference. */
+int osam_device_error_peek(void);
 
 /* Self-test of the bounded device waits: launches one thread that waits on an mbarrier nothing arrives
  * at, with a budget of budget_ns (at most 5 s); the wait runs out, records OSAM_ERR_TIMEOUT in the device

@@ -107,6 +107,7 @@ _SIGS = {
     "osam_model_node_grad_range": (c_int, [c_void_p, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "osam_model_get_grad": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, c_int64]),
     "osam_device_error": (c_int, []),
+    "osam_device_error_peek": (c_int, []),
     "osam_selftest_wait_timeout": (c_int, [ctypes.c_ulonglong, c_void_p]),
     "osam_last_error": (ctypes.c_char_p, []),
 }

@@ -35,23 +35,45 @@ static int cuda_fail(cudaError_t e, const char* what) {
 }
 
 // ------------------------------------------------------------------ device error word
-// A file-scope device variable: every device that loads the library has one, zero-initialised at module
-// load, so nothing is ever allocated for it.  Host code cannot use the symbol as an address; its device
-// address is looked up (cudaGetSymbolAddress) once per device, at plan or model creation, and cached.
+// Kernels record a failed bounded wait in an error word.  At the first plan or model creation the word
+// becomes one int of pinned, host-mapped memory shared by every device (allocated once per process,
+// never inside a launch), so the host can read it at any time without synchronising
+// (osam_device_error_peek).  Before that — post-process or BN entry points used without any plan — the
+// kernels report to a file-scope device variable, which needs no allocation at all.
 static __device__ int g_dev_err_word;
 static std::mutex g_err_mu;
-static int* g_err_word[64] = {};
+static int* g_err_static[64] = {};       // device address of g_dev_err_word, per device
+static volatile int* g_err_host = nullptr;  // host view of the mapped word
+static int* g_err_mapped = nullptr;         // device view of the mapped word
+
+int error_word_init() {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (g_err_mapped) return OSAM_OK;
+  int* h = nullptr;
+  cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&h), 64, cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) return fail(OSAM_ERR_CUDA, "error word: cudaHostAlloc: %s", cudaGetErrorString(e));
+  *h = 0;
+  void* d = nullptr;
+  if ((e = cudaHostGetDevicePointer(&d, h, 0)) != cudaSuccess || d != h) {
+    cudaFreeHost(h);
+    return fail(OSAM_ERR_CUDA, "error word: no unified device address for mapped host memory");
+  }
+  g_err_host = h;
+  g_err_mapped = h;
+  return OSAM_OK;
+}
 
 int* device_error_word() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lk(g_err_mu);
-  if (!g_err_word[dev]) {
+  if (g_err_mapped) return g_err_mapped;
+  if (!g_err_static[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_dev_err_word) != cudaSuccess || !p) return nullptr;
-    g_err_word[dev] = static_cast<int*>(p);
+    g_err_static[dev] = static_cast<int*>(p);
   }
-  return g_err_word[dev];
+  return g_err_static[dev];
 }
 
 // Self-test of the bounded wait: one thread waits on an mbarrier that nothing arrives at, with the given
@@ -803,10 +825,10 @@ int osam_conv_plan_create(const osam_conv_geom* g, int transposed, osam_conv_pla
     delete p;
     return rc;
   }
-  // Allocate the device error word now (plan time), never inside a launch that may be captured.
-  if (!device_error_word()) {
+  // the host-mapped error word exists from the first plan on (allocated here, never inside a launch)
+  if ((rc = error_word_init()) != OSAM_OK || !device_error_word()) {
     delete p;
-    return fail(OSAM_ERR_CUDA, "cannot allocate the device error word");
+    return rc ? rc : fail(OSAM_ERR_CUDA, "no device error word");
   }
   plan_dgrad(p);
   *out = p;
@@ -1149,17 +1171,38 @@ int osam_sppf_bwd(const void* cat, void* dcat, int N, int H, int W, int c, osam_
 }
 
 int osam_device_error(void) {
-  int* w = device_error_word();
-  if (!w) return fail(OSAM_ERR_CUDA, "no device error word");
+  if (!device_error_word()) return fail(OSAM_ERR_CUDA, "no device error word");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_fail(e, "osam_device_error sync");
   int v = 0;
-  e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "osam_device_error read");
-  if (v && (e = cudaMemset(w, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "osam_device_error clear");
-  // the static-scratch entry point's kernels report to their own word: read and clear it on every call
+  if (g_err_host) {
+    v = *g_err_host;
+    *g_err_host = 0;
+  }
+  // the device variable (kernels launched before the mapped word existed) and the static-scratch entry
+  // point's own word: read and clear them on every call
+  int* w = nullptr;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    w = dev >= 0 && dev < 64 ? g_err_static[dev] : nullptr;
+  }
+  if (w) {
+    int vd = 0;
+    if ((e = cudaMemcpy(&vd, w, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+      return cuda_fail(e, "osam_device_error read");
+    if (vd && (e = cudaMemset(w, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "osam_device_error clear");
+    if (!v) v = vd;
+  }
   const int vs = static_scratch_take_error();
   if (!v) v = vs;
+  if (v) set_last_error("device kernel reported error %d", v);
+  return v;
+}
+
+int osam_device_error_peek(void) {
+  const int v = g_err_host ? *g_err_host : 0;
   if (v) set_last_error("device kernel reported error %d", v);
   return v;
 }

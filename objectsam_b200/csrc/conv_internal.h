@@ -163,7 +163,8 @@ size_t sppf_bwd_smem_bytes(int H, int W);
 cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d, int BN, cudaStream_t st);
 cudaError_t launch_conv_stem_rgb(const ConvLaunch& L, cudaStream_t st);
 
-int* device_error_word();       // per-device error word (a static device variable; address cached per device)
+int* device_error_word();       // the error word kernels report to (host-mapped after error_word_init)
+int error_word_init();           // allocates the host-mapped error word once per process (plan/model creation)
 int static_scratch_take_error();  // error recorded by the static-scratch entry point's kernels (and clear it)
 void set_last_error(const char* fmt, ...);
 

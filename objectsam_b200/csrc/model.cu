@@ -1214,9 +1214,9 @@ int osam_model_create(int batch, int imgsz, int reg_max, osam_model** out) {
     m->release();
     return rc;
   }
-  if (!device_error_word()) {
+  if ((rc = error_word_init()) != OSAM_OK || !device_error_word()) {
     m->release();
-    return model_fail(OSAM_ERR_CUDA, "device error word");
+    return rc ? rc : model_fail(OSAM_ERR_CUDA, "device error word");
   }
   *out = m.release();
   return OSAM_OK;

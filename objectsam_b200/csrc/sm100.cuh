@@ -12,6 +12,14 @@ namespace osam {
 // Error codes written to the device error word (mirrored by OSAM_ERR_* in include/osam.h).
 constexpr int kDevErrTimeout = 4;
 
+// Records an error code in the error word: a plain store made visible system-wide (the word may be
+// host-mapped memory, read by the host while kernels run; any non-zero code marks the failure).
+__device__ __forceinline__ void record_error(int* err, int code) {
+  if (!err) return;
+  *reinterpret_cast<volatile int*>(err) = code;
+  __threadfence_system();
+}
+
 // Budget for one mbarrier wait.  The longest single conv at the largest supported batch runs for a
 // few milliseconds; 2 s only triggers when a producer/consumer is truly lost.
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;
@@ -86,7 +94,7 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     for (int i = 0; i < 8; i++)
       if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (globaltimer() - t0 > kWaitBudgetNs) {
-      if (err) atomicExch(err, kDevErrTimeout);
+      record_error(err, kDevErrTimeout);
       return false;
     }
   }
@@ -102,7 +110,7 @@ static __device__ __noinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity
     for (int i = 0; i < 8; i++)
       if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (globaltimer() - t0 > budget_ns) {
-      if (err) atomicExch(err, kDevErrTimeout);
+      record_error(err, kDevErrTimeout);
       return false;
     }
   }
@@ -155,7 +163,7 @@ static __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t
     for (int i = 0; i < 8; i++)
       if (mbar_try_wait_sleep_cluster(bar, parity, 100000u)) return true;
     if (globaltimer() - t0 > kWaitBudgetNs) {
-      if (err) atomicExch(err, kDevErrTimeout);
+      record_error(err, kDevErrTimeout);
       return false;
     }
   }

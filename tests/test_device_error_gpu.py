@@ -28,6 +28,21 @@ def test_bounded_wait_runs_out_and_reports_timeout(cuda_lib):
     assert x.sum().item() == 1024.0
 
 
+def test_timeout_visible_without_synchronising(cuda_lib):
+    """After the first plan exists the word is host-mapped: a finished kernel's timeout is visible to
+    osam_device_error_peek() (no device synchronisation, no clearing) — what the ConvOp shim polls."""
+    from objectsam_b200.conv import ConvGeom, ConvOp
+    ConvOp().init(ConvGeom(1, 8, 8, 32, 32, 3, 3, 1, 1))  # plan creation sets up the mapped word
+    assert _lib.device_error() == 0
+    assert _lib.lib().osam_device_error_peek() == 0
+    _lib.check(_lib.lib().osam_selftest_wait_timeout(10_000_000, _lib.stream_ptr()))
+    torch.cuda.synchronize()
+    assert _lib.lib().osam_device_error_peek() == _lib.OSAM_ERR_TIMEOUT
+    assert _lib.lib().osam_device_error_peek() == _lib.OSAM_ERR_TIMEOUT  # peek does not clear
+    assert _lib.device_error() == _lib.OSAM_ERR_TIMEOUT
+    assert _lib.lib().osam_device_error_peek() == 0
+
+
 def test_selftest_rejects_bad_budget(cuda_lib):
     assert _lib.lib().osam_selftest_wait_timeout(0, _lib.stream_ptr()) == _lib.OSAM_ERR_INVALID
     assert _lib.lib().osam_selftest_wait_timeout(10_000_000_000, _lib.stream_ptr()) == _lib.OSAM_ERR_INVALID
