@@ -317,6 +317,34 @@ int osam_model_node_grad_range(const osam_model* m, int i, int64_t* off, int64_t
 /* One parameter's gradient in its PyTorch name and layout (host fp32, n ≥ its element count); synchronous. */
 int osam_model_get_grad(osam_model* m, const char* name, float* out, int64_t n);
 
+/* ---- data-parallel training: the gradient exchange (SURVEY's multi-GPU plan for the reference's
+ * src/train.cpp:209-232 step; the reference itself trains on one GPU).  One process per GPU holds a model
+ * after osam_model_train_init; osam_dp_backward runs the model's whole backward in buckets of about
+ * bucket_bytes of fp32 gradients (last node first) and all-reduces each bucket's gradients (ncclAvg: the sum
+ * over ranks ÷ world) on a communication stream while the earlier nodes' backward continues; the caller's
+ * stream waits for the exchange at the end, so an optimizer step enqueued after it reads averaged gradients
+ * (the order src/optim.cu:170-175 needs).  NCCL is loaded at run time (the libnccl.so.2 already in the
+ * process, else the system one).
+ *   osam_dp_unique_id   rank 0 makes a communicator id (NCCL's 128-byte unique id); every rank needs it
+ *   osam_dp_create      a new NON-BLOCKING communicator (world, rank, id); init_timeout_ms bounds the wait
+ *                       for the other ranks (OSAM_ERR_TIMEOUT).  world = 1: no communicator, the backward
+ *                       runs unbucketed-equivalent and nothing is exchanged.
+ *   osam_dp_create_from_comm  over the caller's ncclComm_t (not destroyed by osam_dp_destroy)
+ *   osam_dp_wait        host guard after a step: polls the exchange's completion and ncclCommGetAsyncError;
+ *                       on an NCCL error, or when timeout_ms passes first (a peer died or stopped), aborts
+ *                       the communicator (ncclCommAbort) and returns an error instead of hanging.
+ * No counterpart in the reference. */
+typedef struct osam_dp osam_dp;
+int osam_dp_unique_id(unsigned char id[128]);
+int osam_dp_create(osam_model* m, int world, int rank, const unsigned char id[128], size_t bucket_bytes,
+                   int init_timeout_ms, osam_dp** out);
+int osam_dp_create_from_comm(osam_model* m, void* nccl_comm, size_t bucket_bytes, osam_dp** out);
+int osam_dp_num_buckets(const osam_dp* dp);
+int osam_dp_bucket(const osam_dp* dp, int i, int* first, int* count, int64_t* off, int64_t* n);
+int osam_dp_backward(osam_dp* dp, osam_stream_t stream);
+int osam_dp_wait(osam_dp* dp, int timeout_ms);
+int osam_dp_destroy(osam_dp* dp);
+
 /* Device error word shared by all kernels of this library on the current device: returns the first
  * error code recorded by a kernel since the last call (0 if none) and clears it.  Synchronises.
  * Launches are asynchronous, so a kernel whose bounded wait ran out (OSAM_ERR_TIMEOUT: it returned early

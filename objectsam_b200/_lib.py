@@ -106,6 +106,14 @@ _SIGS = {
     "osam_model_grad_arena": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_int64)]),
     "osam_model_node_grad_range": (c_int, [c_void_p, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "osam_model_get_grad": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, c_int64]),
+    "osam_dp_unique_id": (c_int, [ctypes.c_char_p]),
+    "osam_dp_create": (c_int, [c_void_p, c_int, c_int, ctypes.c_char_p, c_size_t, c_int, POINTER(c_void_p)]),
+    "osam_dp_create_from_comm": (c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_void_p)]),
+    "osam_dp_num_buckets": (c_int, [c_void_p]),
+    "osam_dp_bucket": (c_int, [c_void_p, c_int, POINTER(c_int), POINTER(c_int), POINTER(c_int64), POINTER(c_int64)]),
+    "osam_dp_backward": (c_int, [c_void_p, c_void_p]),
+    "osam_dp_wait": (c_int, [c_void_p, c_int]),
+    "osam_dp_destroy": (c_int, [c_void_p]),
     "osam_device_error": (c_int, []),
     "osam_device_error_peek": (c_int, []),
     "osam_selftest_wait_timeout": (c_int, [ctypes.c_ulonglong, c_void_p]),

@@ -70,7 +70,9 @@ struct FpropCfg {
   static constexpr int WIN_ROWS = S2W ? 272 : 160;  // 17 row pairs × 2 parities × 8, or (th + 2)·ni·tw
   static constexpr int WIN_BYTES = W3 ? WIN_ROWS * BK * 2 : 0;
   static constexpr int A_FIT = W3 ? (RING_BUDGET - (RESB ? 9 : W3_MIN_B) * B_BYTES) / WIN_BYTES : 0;
-  static constexpr int A_STAGES = W3 ? (A_FIT < 2 ? 2 : (A_FIT > 4 ? 4 : A_FIT)) : 0;
+  // resident-weight forms stream only windows: a deeper window ring (up to 8) keeps more loads in flight
+  static constexpr int A_MAX = RESB ? 8 : 4;
+  static constexpr int A_STAGES = W3 ? (A_FIT < 2 ? 2 : (A_FIT > A_MAX ? A_MAX : A_FIT)) : 0;
   static constexpr int STAGES_RAW = (RING_BUDGET - A_STAGES * WIN_BYTES) / STAGE_BYTES;
   // RESB: the nine weight taps, loaded once (full[0] counts them)
   static constexpr int STAGES = RESB ? 9 : (STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW));
@@ -491,6 +493,11 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
         bn = (rest / d.tiles_p) * d.tn + w0 / thw;
       }
       const uint32_t buf = lt & 1;
+      // the residual of the first 32 columns is loaded before the accumulator is ready; each later pass's
+      // at the start of that pass, ahead of its TMEM load and math
+      const bool pre_res = e.tstore && e.kind == OSAM_EPI_BN_ACT && e.res != nullptr;
+      uint4 rcur[4];
+      if (pre_res) residual_rows(e, valid ? pix : -1LL, d.K, n0 + cbeg, rcur);
       const bool ok = mbar_wait(accf + buf, (lt >> 1) & 1, d.err);
       tc_fence_after();
       if (!ok) break;
@@ -499,6 +506,7 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
 #pragma unroll 1
         for (int c = 0; c < cols; c += 32) {
           __syncwarp();
+          if (pre_res && c > 0) residual_rows(e, valid ? pix : -1LL, d.K, n0 + cbeg + c, rcur);
           uint32_t r0[16], r1[16];
           tmem_ld16_nowait(dt + cbeg + c, r0);
           tmem_ld16_nowait(dt + cbeg + c + 16, r1);
@@ -509,7 +517,8 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
             v[i] = __uint_as_float(r0[i]);
             v[16 + i] = __uint_as_float(r1[i]);
           }
-          epilogue_warp_tma(e, sm, d.K, d.P, d.Q, v, n0 + cbeg + c, s_sc, s_sh, valid, n, p, q, bq, bp, bn, stage);
+          epilogue_warp_tma(e, sm, d.K, d.P, d.Q, v, n0 + cbeg + c, s_sc, s_sh, valid, n, p, q, bq, bp, bn, stage,
+                            nullptr, pre_res ? rcur : nullptr);
         }
       } else if (e.coop) {
 #pragma unroll 1

@@ -208,15 +208,22 @@ cudaError_t launch_conv_stem(const __half* x, const __half* w, const ConvDev& d,
 //   warp 0       TMA: the tile's input window (5 rows × 387 fp16, i.e. 129 pixels × 3 channels) as two
 //                208-element boxes of the (W·C, H, N) view into a 6-slot ring; the out-of-range zero fill
 //                of the tensor engine supplies every conv pad (top/bottom rows, left/right columns);
-//   warps 2..5   im2col: each thread turns its pixel's 27 taps (from the window) into one 64-byte
-//                swizzled K-major row of the A tile (4-slot ring);
+//   warps 2..5   im2col: each thread builds its pixel's 64-byte swizzled K-major row of the A tile
+//                (4-slot ring) from three aligned 20-byte runs of the window, one per kernel row;
 //   warp 1       TMEM owner + MMA issuer: two K=16 UMMAs per tile into one of two accumulators;
 //   warps 6..9   epilogue: folded BN + SiLU and TMA tensor stores of whole 32-pixel row blocks.
-// The weights (32 × 27, zero-padded to 32 × 32) stay in shared memory for the whole kernel.
+// K layout of a row: kernel row r occupies k = 10r … 10r+9.  For output column q the nine taps of row r
+// (input columns 2q−1 … 2q+1, three channels each) are the nine consecutive halves that start at element
+// 6q − 3 of the input row; the run of TEN halves that starts one element earlier (at 6q − 4, always even)
+// is 4-byte aligned in the window, so it is read as five 32-bit words.  Its first half belongs to the
+// previous pixel and meets a zero weight (k = 10r), as do k = 30, 31.  The weights (32 × 27, laid out
+// this way) stay in shared memory for the whole kernel.
 namespace osam {
 
 constexpr int kS2Win = 6, kS2A = 4;
 constexpr int kS2Box = 208;                  // fp16 elements per window box row (416 B)
+constexpr int kS2Box1 = 200;                 // the second box starts 200 elements in (overlapping the first by 8,
+                                             // so no ten-element run straddles the two)
 constexpr int kS2BoxBytes = 2176;            // one box of 5 rows (2080 B), padded to 128 B
 constexpr int kS2WinBytes = 2 * kS2BoxBytes;  // two boxes per window
 constexpr int kS2Smem = 1024 + kS2A * 8192 + 2048 + 4 * 2048 + kS2Win * kS2WinBytes + 2 * 32 * 4 + 512;
@@ -262,14 +269,14 @@ __global__ void __launch_bounds__(320, 2)
     tmem_alloc(tslot, 64);
     tmem_relinquish();
   }
-  // weights: row k = the 27 taps of output channel k (KRSC), zero-padded to 32, 64-byte swizzle
+  // weights: row k = the 27 taps of output channel k (KRSC) at k = 10r + 1 + 3s + c, 64-byte swizzle
   for (int i = threadIdx.x; i < 32 * 4; i += blockDim.x) {
     const int r = i >> 2, ch = i & 3;
     __align__(16) __half v[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) {
-      const int kk = ch * 8 + e;
-      v[e] = (r < d.K && kk < 27) ? w[r * 27 + kk] : __float2half(0.f);
+      const int kk = ch * 8 + e, kr = kk / 10, t = kk - kr * 10;
+      v[e] = (r < d.K && kr < 3 && t > 0) ? w[r * 27 + kr * 9 + (t - 1)] : __float2half(0.f);
     }
     *reinterpret_cast<uint4*>(sB + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)) = *reinterpret_cast<const uint4*>(v);
   }
@@ -293,7 +300,7 @@ __global__ void __launch_bounds__(320, 2)
         mbar_arrive_expect_tx(wfull + s, 2 * 5 * kS2Box * 2);
         uint8_t* dst = s_win + s * kS2WinBytes;
         tma_load_3d(dst, &tw, wfull + s, xa, ih0, n);
-        tma_load_3d(dst + kS2BoxBytes, &tw, wfull + s, xa + kS2Box, ih0, n);
+        tma_load_3d(dst + kS2BoxBytes, &tw, wfull + s, xa + kS2Box1, ih0, n);
       }
     }
   } else if (warp == 1) {
@@ -318,38 +325,30 @@ __global__ void __launch_bounds__(320, 2)
     // ---------------------------------------------------------------- im2col (one A row per thread)
     const int tid = threadIdx.x - 64;  // 0..127 = row of the A tile
     const int i = tid >> 6, j = tid & 63;
+    // the ten-half run of kernel row r starts at window element 6j + 4 (the window starts 4 elements before
+    // the run of the tile's first column: xa = 6·q0 − 8 rounded as the producer rounds it); a run ending
+    // past element 208 is read from the second box, which starts at element 200
+    const int e0 = 6 * j + 4;
+    const int run_off = e0 + 10 <= kS2Box ? e0 * 2 : kS2BoxBytes + (e0 - kS2Box1) * 2;  // bytes into a window row
     int lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
       const int ws = lt % kS2Win, as = lt % kS2A;
       if (!mbar_wait(wfull + ws, (lt / kS2Win) & 1, d.err)) break;
       if (lt >= kS2A && !mbar_wait(aempty + as, ((lt / kS2A) - 1) & 1, d.err)) break;
-      const int tq = t % d.tiles_q;
-      const int x0 = (2 * tq * 64 - 1) * 3;
-      const int xa = x0 >= 0 ? (x0 & ~7) : -((-x0 + 7) & ~7);
-      const int off = x0 - xa;  // window element of input column iw0
-      const __half* win = reinterpret_cast<const __half*>(s_win + ws * kS2WinBytes);
-      const int iw_first = 2 * (tq * 64 + j) - 1;  // input column of tap s = 0
-      __align__(16) __half row[32];
+      const uint8_t* win = s_win + ws * kS2WinBytes + run_off;
+      uint32_t row[16];
 #pragma unroll
       for (int r = 0; r < 3; r++) {
-        const int wr = 2 * i + r;  // window row (rows outside the image arrive as zeros)
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(win + (2 * i + r) * (kS2Box * 2));
 #pragma unroll
-        for (int s = 0; s < 3; s++) {
-          const bool col_in = iw_first + s >= 0 && iw_first + s < d.W;
-#pragma unroll
-          for (int c = 0; c < 3; c++) {
-            const int e = off + (2 * j + s) * 3 + c;  // element in the window row
-            const __half* src = e < kS2Box ? win + wr * kS2Box + e : win + kS2BoxBytes / 2 + wr * kS2Box + (e - kS2Box);
-            row[(r * 3 + s) * 3 + c] = col_in ? *src : __float2half(0.f);
-          }
-        }
+        for (int u = 0; u < 5; u++) row[5 * r + u] = src[u];
       }
-#pragma unroll
-      for (int k = 27; k < 32; k++) row[k] = __float2half(0.f);
+      row[15] = 0u;
       uint8_t* dst = sA + as * 8192 + tid * 64;
 #pragma unroll
       for (int ch = 0; ch < 4; ch++)
-        *reinterpret_cast<uint4*>(dst + ((ch ^ ((tid >> 1) & 3)) << 4)) = reinterpret_cast<const uint4*>(row)[ch];
+        *reinterpret_cast<uint4*>(dst + ((ch ^ ((tid >> 1) & 3)) << 4)) =
+            make_uint4(row[4 * ch], row[4 * ch + 1], row[4 * ch + 2], row[4 * ch + 3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {

@@ -317,11 +317,13 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
 // destinations and for the transposed conv's pixel shuffle, one per (dy, dx) view).  The tensor engine
 // clips rows outside the output, so partial tiles need no masking.  W = 32 (64-byte stage rows).
 // `rsm` (optional): this pass's residual rows already in shared memory (32 rows × 64 B, stage_off layout),
-// read instead of the global residual.
+// read instead of the global residual.  `rreg` (optional): this pass's residual rows already in registers,
+// loaded by residual_rows (below) before the accumulator was ready.
 __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMaps& maps, int K, int P, int Q,
                                                   float* v, int col, const float* s_sc, const float* s_sh,
                                                   bool valid, int n, int p, int q, int bq, int bp, int bn,
-                                                  uint8_t* stage, const uint8_t* rsm = nullptr) {
+                                                  uint8_t* stage, const uint8_t* rsm = nullptr,
+                                                  const uint4* rreg = nullptr) {
   constexpr int W = 32, CPR = 4, RPI = 8;
   const int lane = threadIdx.x & 31;
   if (e.round_z) {
@@ -374,9 +376,13 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMa
 #pragma unroll
     for (int it = 0; it < CPR; it++) {
       const int rr = it * RPI + lane / CPR, ch = lane % CPR;
-      const int rpix = __shfl_sync(0xffffffffu, my_rv, rr);
       uint4 val = make_uint4(0, 0, 0, 0);
-      if (rpix >= 0) val = *reinterpret_cast<const uint4*>(e.res + (long long)rpix * K + col + ch * 8);
+      if (rreg) {
+        val = rreg[it];
+      } else {
+        const int rpix = __shfl_sync(0xffffffffu, my_rv, rr);
+        if (rpix >= 0) val = *reinterpret_cast<const uint4*>(e.res + (long long)rpix * K + col + ch * 8);
+      }
       *reinterpret_cast<uint4*>(stage + stage_off(rr, ch)) = val;
     }
     __syncwarp();
@@ -413,6 +419,19 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiDev& e, const StoreMa
       }
     }
     bulk_commit_group();
+  }
+}
+
+// The residual of a warp's 32 rows × 32 channels from column `col` on, in the coalesced order
+// epilogue_warp_tma stages it (lane l holds row 8·it + l/4, channels 8·(l%4)…+7 in rv[it]); `my_pix` is
+// this lane's own row's pixel, −1 outside the output.  Issued before the accumulator is ready, so the
+// loads overlap the MMAs instead of stalling the epilogue.
+__device__ __forceinline__ void residual_rows(const EpiDev& e, long long my_pix, int K, int col, uint4 (&rv)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const long long rpix = __shfl_sync(0xffffffffu, my_pix, it * 8 + lane / 4);
+    rv[it] = rpix >= 0 ? *reinterpret_cast<const uint4*>(e.res + rpix * K + col + (lane % 4) * 8) : make_uint4(0, 0, 0, 0);
   }
 }
 

@@ -2,6 +2,11 @@
 averaged with an all-reduce (NCCL over NVLink on the GPUs, gloo on CPU), bucket by bucket, while the backward
 of the earlier layers is still running.
 
+Two forms: DataParallel drives the exchange from Python with torch.distributed (any backend, gloo on CPU);
+NcclDataParallel runs it inside the library (osam_dp_*: buckets, NCCL all-reduce with ncclAvg on a
+communication stream, non-blocking communicator with a host-side abort guard) — the path a C++ trainer
+calls directly.
+
 This is the gradient exchange of the reference's multi-GPU plan (ncclAllReduce, sum then ÷ world, over the
 fp32 gradient arenas, bucketed in reverse layer order on a communication stream after each bucket's
 weight-gradient work; it must finish before the optimizer step).  The model's fp32 gradient arena keeps the
@@ -97,3 +102,65 @@ class DataParallel:
             view.mul_(1.0 / self.world)
         if self.cuda and self.world > 1:
             (stream if stream is not None else torch.cuda.current_stream(self.arena.device)).wait_stream(self.comm)
+
+
+class NcclDataParallel:
+    """The library's own data-parallel exchange (include/osam.h osam_dp_*) for one process per GPU.
+
+    The NCCL communicator id is made by rank 0 and passed to the other ranks through the torch.distributed
+    group (any backend); the communicator itself belongs to the library.  backward() runs the model's whole
+    backward with the bucketed, overlapped all-reduce (average) on the current stream; wait(timeout_ms)
+    guards a step: it raises (after aborting the communicator) if the exchange fails or does not finish in
+    time."""
+
+    def __init__(self, model, bucket_mb: float = 4.0, group=None, init_timeout_ms: int = 120000):
+        import ctypes
+        from ._lib import check, lib
+        self.m = model
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        uid = ctypes.create_string_buffer(128)
+        if self.world > 1:
+            if self.rank == 0:
+                check(lib().osam_dp_unique_id(uid))
+            box = [bytes(uid.raw)]
+            dist.broadcast_object_list(box, src=0, group=group)
+            uid = ctypes.create_string_buffer(box[0], 128)
+        self._dp = ctypes.c_void_p()
+        check(lib().osam_dp_create(model._m, self.world, self.rank, uid, int(bucket_mb * (1 << 20)),
+                                   init_timeout_ms, ctypes.byref(self._dp)))
+
+    @property
+    def num_buckets(self) -> int:
+        from ._lib import lib
+        return lib().osam_dp_num_buckets(self._dp)
+
+    def buckets(self) -> list[Bucket]:
+        import ctypes
+        from ._lib import check, lib
+        out = []
+        for i in range(self.num_buckets):
+            f, c, o, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+            check(lib().osam_dp_bucket(self._dp, i, ctypes.byref(f), ctypes.byref(c), ctypes.byref(o), ctypes.byref(n)))
+            out.append(Bucket(f.value, c.value, o.value, n.value))
+        return out
+
+    def backward(self, stream=None) -> None:
+        from ._lib import check, lib, stream_ptr
+        check(lib().osam_dp_backward(self._dp, stream_ptr(stream)))
+
+    def wait(self, timeout_ms: int = 60000) -> None:
+        from ._lib import check, lib
+        check(lib().osam_dp_wait(self._dp, timeout_ms))
+
+    def close(self) -> None:
+        from ._lib import lib
+        if getattr(self, "_dp", None):
+            lib().osam_dp_destroy(self._dp)
+            self._dp = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

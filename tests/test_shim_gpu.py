@@ -56,13 +56,29 @@ def test_reference_forward_on_shim_matches_cudnn(cuda_lib, weights, seed, N, S):
             op = os.path.join(td, b + ".fsow")
             _run(b, wp, ip, op)
             outs[b] = fsow.load(op)
+    if weights == "baseline":  # logits O(0.1): directly against the cuDNN build
+        for k in KEYS:
+            r = outs["ref_forward_fp16"][k].astype(np.float64)
+            y = outs["shim_forward_fp16"][k].astype(np.float64)
+            scale = np.abs(r).max() + 1e-6
+            d = np.abs(y - r)
+            assert d.max() <= 1e-2 * scale, f"{k}: max |shim-cudnn| {d.max():.3e} (scale {scale:.3e})"
+            assert d.mean() <= 1e-3, f"{k}: mean |shim-cudnn| {d.mean():.3e}"
+        return
+    # BN-calibrated weights (activations O(10-100)): two fp16 evaluations of the 60-conv chain drift apart
+    # by several ulps, so both builds are measured against the float64 network (the bar of the native
+    # model's reference-parity test)
+    o64 = yolo_ref.YoloSegRef(w, emulate_fp16=False, dtype=torch.float64).forward(imgs)
+    exact = {f"out.{k}{l}": o64[k][l] for k in ("box", "cls", "coef") for l in range(3)}
+    exact["out.proto"] = o64["proto"]
     for k in KEYS:
+        x = exact[k].permute(0, 2, 3, 1).numpy()
         r = outs["ref_forward_fp16"][k].astype(np.float64)
         y = outs["shim_forward_fp16"][k].astype(np.float64)
         scale = np.abs(r).max() + 1e-6
-        d = np.abs(y - r)
-        assert d.max() <= 1e-2 * scale, f"{k}: max |shim-cudnn| {d.max():.3e} (scale {scale:.3e})"
-        assert d.mean() <= 1e-3 * max(1.0, scale), f"{k}: mean |shim-cudnn| {d.mean():.3e}"
+        e_s, e_c = np.abs(y - x), np.abs(r - x)
+        assert e_s.max() <= max(1e-2 * scale, 1.5 * e_c.max()), f"{k}: max err shim {e_s.max():.3e}, cudnn {e_c.max():.3e}"
+        assert e_s.mean() <= 1.5 * e_c.mean() + 1e-4 * scale, f"{k}: mae shim {e_s.mean():.3e}, cudnn {e_c.mean():.3e}"
 
 
 @needs_bins
