@@ -66,6 +66,18 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-cudnn", action="store_true", help="skip timing the reference's cuDNN build")
     ap.add_argument("--nodes-out", default=None, help="write the per-node timing table (JSON) to this path")
+    ap.add_argument("--no-train", action="store_true", help="skip the training-step leg")
+    ap.add_argument("--train-batch", type=int, default=16, help="training leg: images per GPU (BASELINE config 4)")
+    ap.add_argument("--bucket-mb", type=float, default=4.0, help="training leg: gradient bucket size")
+    ap.add_argument("--mode", choices=["step", "sweep", "train-passes", "node"], default="step",
+                    help="step: the bench line (default); sweep: per-layer fwd/dgrad/wgrad table (config 3); "
+                         "train-passes: BN / stem-wgrad / mask-loss passes against the reference's kernels; "
+                         "node: one node of the forward repeated (an ncu target)")
+    ap.add_argument("--reps", type=int, default=10, help="sweep / train-passes: timed repetitions")
+    ap.add_argument("--ops", default="fwd,dgrad,wgrad", help="sweep: passes to time")
+    ap.add_argument("--json", default=None, help="sweep / train-passes: write the table as JSON")
+    ap.add_argument("--node", default="model.22.proto.cv2", help="node mode: the node to repeat")
+    ap.add_argument("--repeat", type=int, default=1, help="node mode: repetitions inside the NVTX range")
     return ap.parse_args()
 
 
@@ -309,11 +321,380 @@ def time_kernels(model, n, post_fns, K):
     return ms, how
 
 
+# ----------------------------------------------------------------------------------------------------------
+# Other modes (BASELINE config 3 sweep, training-pass table, single-node repeat for ncu)
+
+def _reference_conv_table(batch: int, imgsz: int) -> dict:
+    """{layer: (fwd_ms, dgrad_ms, wgrad_ms)}: the reference cuDNN build's own tuned per-conv timings
+    (oracle/_ref/ref_forward_fp16 with OSAM_REF_PRINT_CONVS) on the same batch and size."""
+    import re
+    binary = os.path.join(ROOT, "oracle", "_ref", "ref_forward_fp16")
+    if not os.path.exists(binary):
+        return {}
+    from oracle import fsow, yolo_params
+    with tempfile.TemporaryDirectory() as td:
+        wp = os.path.join(td, "w.fsow")
+        fsow.save(wp, yolo_params.make_weights(0))
+        env = dict(child_env(), OSAM_REF_PRINT_CONVS="1")
+        out = subprocess.run([binary, wp, "-", "-", "0", str(batch), str(imgsz)], capture_output=True, text=True,
+                             env=env, timeout=900).stdout
+    tab = {}
+    for line in out.splitlines():
+        m = re.match(r"^(\S+)\s+\d+\s+\d+\s+\d+\s+\d+\s+\d+\s+\d+\s+\|\s+([\d.]+)\s+([\d.]+)\s+([\d.]+)", line)
+        if m:
+            tab[m.group(1)] = tuple(float(m.group(i)) for i in (2, 3, 4))
+    return tab
+
+
+def mode_sweep(args):
+    """forward, input gradient and weight gradient of every conv of the network, one by
+    one, on seeded U[-1,1] NHWC fp16 tensors of the layer's shape (He-normal weights); CUDA events over
+    `reps` launches after two warm-up launches; TFLOP/s with the reference's FLOP formula 2·N·P·Q·K·C·R·S
+    (src/model.cpp:483; the transposed conv counts H·W) and the fraction of the measured burst peak; beside
+    them the reference cuDNN build's own tuned times for the same layers.
+
+        python bench.py --mode sweep --batch 128 [--reps 10] [--ops fwd,dgrad,wgrad] [--json out]"""
+    import torch
+    from objectsam_b200.conv import ConvGeom, ConvOp
+    from objectsam_b200.model import Model
+    from oracle import yolo_params  # seeded synthetic weights only: the layer geometry comes from the model
+    ops = set(args.ops.split(","))
+    dev = "cuda"
+    peak = load_peaks()["tflops"]
+    m = Model(args.batch, args.imgsz)
+    m.load(yolo_params.make_weights(0))
+    m.sync_weights()
+    nodes = [n for n in m.nodes() if n["kind"] in (0, 1, 2)]  # convs, head convs, the transposed conv
+    m.close()
+    torch.cuda.empty_cache()
+    g = torch.Generator(device="cpu").manual_seed(0)
+    rows = []
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.reps
+
+    for n in nodes:
+        N, H, W, C, K, R, st = n["N"], n["H"], n["W"], n["C"], n["K"], n["R"], n["stride"]
+        tr = n["kind"] == 2
+        op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, st, 0 if tr else R // 2), transposed=tr)
+        oshape = op.out_shape()
+        x = (torch.rand(N, H, W, C, generator=g) * 2 - 1).half().to(dev)
+        w_shape = (C, R, R, K) if tr else (K, R, R, C)
+        w = (torch.randn(*w_shape, generator=g) * (2.0 / (C * R * R)) ** 0.5).half().to(dev)
+        y = torch.empty(oshape, dtype=torch.half, device=dev)
+        ws = torch.empty(max(op.workspace_size(), 256), dtype=torch.uint8, device=dev)
+        flops = 2.0 * N * (H * W if tr else oshape[1] * oshape[2]) * K * C * R * R
+        row = {"name": n["name"], "N": N, "H": H, "W": W, "C": C, "K": K, "R": R, "stride": st, "gflop": flops / 1e9}
+        if "fwd" in ops:
+            row["fwd_ms"] = timed(lambda: op.fwd(x, w, y, ws=ws))
+        if not tr and n["index"] > 0 and "dgrad" in ops:  # the stem has no input gradient (src/model.cpp:177)
+            dx = torch.empty_like(x)
+            try:
+                row["dgrad_ms"] = timed(lambda: op.dgrad(y, w, dx, ws=ws))
+            except RuntimeError as e:
+                row["dgrad_ms"], row["dgrad_note"] = None, str(e)[:80]
+        if not tr and "wgrad" in ops:
+            dw = torch.empty(w_shape, dtype=torch.half, device=dev)
+            try:
+                row["wgrad_ms"] = timed(lambda: op.wgrad(x, y, dw, ws=ws))
+            except RuntimeError as e:
+                row["wgrad_ms"], row["wgrad_note"] = None, str(e)[:80]
+        for k in ("fwd", "dgrad", "wgrad"):
+            t = row.get(k + "_ms")
+            if t:
+                row[k + "_tflops"] = flops / (t / 1e3) / 1e12
+                row[k + "_frac"] = row[k + "_tflops"] / peak
+        rows.append(row)
+        op.close()
+        del x, w, y, ws
+        torch.cuda.empty_cache()
+    ref = _reference_conv_table(args.batch, args.imgsz)
+    tot = {k: 0.0 for k in ("fwd", "dgrad", "wgrad")}
+    rtot = dict(tot)
+    print(f"{'layer':26s} {'shape':28s} {'fwd ms':>8s} {'TF':>6s} {'frac':>5s} {'dgrad':>8s} {'TF':>6s} {'wgrad':>8s} "
+          f"{'TF':>6s}" + (f" | {'ref fwd':>8s} {'dgrad':>8s} {'wgrad':>8s}" if ref else ""))
+    for r in rows:
+        shape = f"{r['H']}x{r['W']} {r['C']}->{r['K']} {r['R']}x{r['R']} s{r['stride']}"
+        cells = []
+        for k in ("fwd", "dgrad", "wgrad"):
+            t = r.get(k + "_ms")
+            cell = f"{t:8.3f} {r[k + '_tflops']:6.0f}" if t else f"{'-':>8s} {'-':>6s}"
+            if k == "fwd":
+                cell += f" {r['fwd_frac']:5.2f}" if t else f" {'-':>5s}"
+            cells.append(cell)
+            if t and (not ref or r["name"] in ref):
+                tot[k] += t
+        line = f"{r['name']:26s} {shape:28s} " + " ".join(cells)
+        if r["name"] in ref:
+            rf = ref[r["name"]]
+            r["ref_ms"] = rf
+            for i, k in enumerate(("fwd", "dgrad", "wgrad")):
+                if r.get(k + "_ms"):
+                    rtot[k] += rf[i]
+            line += f" | {rf[0]:8.3f} {rf[1]:8.3f} {rf[2]:8.3f}"
+        print(line)
+    print("total ms (layers with both sides):", {k: round(v, 3) for k, v in tot.items()})
+    if ref:
+        print("reference total ms (same layers):", {k: round(v, 3) for k, v in rtot.items()})
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump({"batch": args.batch, "imgsz": args.imgsz, "peak_tflops": peak, "rows": rows, "total": tot,
+                       "ref_total": rtot}, f, indent=1)
+
+
+def mode_train_passes(args):
+    """The training-side passes at BASELINE config 4 (batch 16 per GPU, 640²): BatchNorm statistics / apply /
+    backward for every distinct conv+BN+SiLU output shape, the stem weight gradient and the mask loss, each
+    timed alone (a 256 MiB read before every call, so L2 holds none of the inputs) and beside the
+    reference's own kernels on the same shapes (oracle/_ref/ref_bn).  Algorithmic bytes: stats 2·M·C, apply
+    4·M·C, backward 6·M·C, stem wgrad 2·(N·H·W·3 + N·P·Q·32), mask loss 2·(2·B·Hp·Wp·32) + B·G·Hp·Wp/8.
+
+        python bench.py --mode train-passes [--batch 16] [--reps 10] [--json out]"""
+    import numpy as np
+    import torch
+    from objectsam_b200 import bn
+    from objectsam_b200 import loss as mloss
+    from objectsam_b200.conv import ConvGeom, ConvOp, DestSpec
+    from objectsam_b200.model import Model
+    from oracle import fsow, yolo_params
+    dev = "cuda"
+    peak = load_peaks()["hbm_gbs"]
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+
+    def timed(fn):
+        fn()
+        fn()
+        tot = 0.0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(args.reps):
+            flush.sum()
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / args.reps
+
+    m = Model(args.batch, args.imgsz)
+    m.load(yolo_params.make_weights(0))
+    m.sync_weights()
+    shapes = []
+    for n in m.nodes():
+        if n["kind"] == 0:
+            geo = ConvGeom(n["N"], n["H"], n["W"], n["C"], n["K"], n["R"], n["R"], n["stride"], n["R"] // 2)
+            sh = (n["N"], geo.P(), geo.Q(), n["K"])
+            if sh not in shapes:
+                shapes.append(sh)
+    m.close()
+    torch.cuda.empty_cache()
+    gen = torch.Generator(device=dev).manual_seed(0)
+    rows = []
+    for (N, H, W, C) in shapes:
+        M = N * H * W
+        z = (torch.rand(N, H, W, C, generator=gen, device=dev) * 5 - 2).half()
+        dA = ((torch.rand(N, H, W, C, generator=gen, device=dev) - 0.5) * 0.2).half()
+        ones, zeros = torch.ones(C, device=dev), torch.zeros(C, device=dev)
+        rm, rv = zeros.clone(), ones.clone()
+        mean, istd, scale, shift = (torch.empty(C, device=dev) for _ in range(4))
+        out, dz = torch.empty_like(z), torch.empty_like(z)
+        gwg, gwb = torch.empty(C, device=dev), torch.empty(C, device=dev)
+        ws = bn.workspace(C, dev)
+        t_stats = timed(lambda: bn.bn_forward_stats(z, ones, zeros, rm, rv, 0.0, 1e-3, mean, istd, scale, shift, ws=ws))
+        t_apply = timed(lambda: bn.bn_forward_apply(z, scale, shift, None, [DestSpec(out)], True))
+        t_bwd = timed(lambda: bn.bn_backward(z, mean, istd, scale, shift, [DestSpec(dA)], True, dz, gwg, gwb, ws=ws))
+        mc2 = 2.0 * M * C
+        rows.append({"op": "bn", "shape": [N, H, W, C], "ms": [t_stats, t_apply, t_bwd],
+                     "gbs": [mc2 / t_stats / 1e6, 2 * mc2 / t_apply / 1e6, 3 * mc2 / t_bwd / 1e6]})
+        del z, dA, out, dz
+        torch.cuda.empty_cache()
+    N, H, W = args.batch, args.imgsz, args.imgsz
+    op = ConvOp().init(ConvGeom(N, H, W, 3, 32, 3, 3, 2, 1))
+    P, Q = op.geom().P(), op.geom().Q()
+    x = torch.rand(N, H, W, 3, generator=gen, device=dev).half()
+    dzs = (torch.rand(N, P, Q, 32, generator=gen, device=dev) * 2 - 1).half()
+    dw = torch.empty(32, 3, 3, 3, dtype=torch.half, device=dev)
+    wsw = torch.empty(op.workspace_size(), dtype=torch.uint8, device=dev)
+    t_wg = timed(lambda: op.wgrad(x, dzs, dw, ws=wsw))
+    rows.append({"op": "stem_wgrad", "shape": [N, H, W, 3, 32], "ms": [t_wg],
+                 "gbs": [2.0 * (N * H * W * 3 + N * P * Q * 32) / t_wg / 1e6]})
+    op.close()
+    # mask loss: 1–30 boxes per image (sides 8–400 px), 10 positives per box, random mask bits
+    S, B = args.imgsz, args.batch
+    Hp = Wp = S // 4
+    lv = [(S // 8, S // 8), (S // 16, S // 16), (S // 32, S // 32)]
+    A = sum(h * w for h, w in lv)
+    G = 32
+    cg = torch.Generator(device="cpu").manual_seed(1)
+    n_gt = torch.randint(1, 31, (B,), generator=cg)
+    side = torch.rand(B, G, 2, generator=cg) * 392 + 8
+    xy = torch.rand(B, G, 2, generator=cg) * (S - side)
+    gt_box = torch.cat([xy, xy + side], -1).float().contiguous()
+    npos = (n_gt * 10).int()
+    pos = torch.zeros(B, A, dtype=torch.int32)
+    agt = torch.full((B, A), -1, dtype=torch.int32)
+    for b in range(B):
+        sel = torch.randperm(A, generator=cg)[: int(npos[b])].sort().values
+        pos[b, : len(sel)] = sel.int()
+        agt[b, sel] = (torch.arange(len(sel)) // 10).int()
+    words = torch.randint(-2**31, 2**31 - 1, (B, G, Hp * Wp // 32), generator=cg, dtype=torch.int64).int()
+    coef = [((torch.rand(B, h, w, 32, generator=gen, device=dev) * 2 - 1)).half() for h, w in lv]
+    proto = (torch.rand(B, Hp, Wp, 32, generator=gen, device=dev) * 2 - 1).half()
+    dproto = torch.empty_like(proto)
+    dcoef = [torch.empty_like(c) for c in coef]
+    lsum = torch.zeros(1, device=dev)
+    fg = torch.tensor([float(npos.sum())], device=dev)
+    one = torch.ones(1, device=dev)
+    margs = [t.to(dev) for t in (npos.int(), pos, agt, gt_box, words)]
+    t_ml = timed(lambda: mloss.mask_loss(coef, proto, *margs, fg, one, S, 7.5, dproto, dcoef, lsum))
+    mbytes = 2.0 * (B * Hp * Wp * 32 * 2) + B * G * Hp * Wp / 8
+    rows.append({"op": "mask_loss", "shape": [B, Hp, Wp, int(npos.sum())], "ms": [t_ml], "gbs": [mbytes / t_ml / 1e6]})
+    ref_bin = os.path.join(ROOT, "oracle", "_ref", "ref_bn")
+    if os.path.exists(ref_bin):
+        cases = [[10, *r["shape"], args.reps] for r in rows if r["op"] == "bn"] + [[13, N, H, W, args.reps]]
+        ins = {f"c{i}.meta": np.array(c, np.int32) for i, c in enumerate(cases)}
+        with tempfile.TemporaryDirectory() as td:
+            fsow.save(os.path.join(td, "in.fsow"), ins)
+            subprocess.run([ref_bin, os.path.join(td, "in.fsow"), os.path.join(td, "out.fsow")], check=True,
+                           timeout=900, env=child_env())
+            out = fsow.load(os.path.join(td, "out.fsow"))
+        for i, r in enumerate(rows[:len(cases)]):
+            r["ref_ms"] = [float(v) for v in out[f"c{i}.ms"]]
+    print(f"HBM peak {peak:.0f} GB/s")
+    for r in rows:
+        shp = "x".join(map(str, r["shape"]))
+        ms = " ".join(f"{v:8.3f}" for v in r["ms"])
+        gb = " ".join(f"{v:6.0f} ({v / peak:4.2f})" for v in r["gbs"])
+        rs = " ".join(f"{v:8.3f}" for v in r.get("ref_ms", []))
+        print(f"{r['op']:12s} {shp:24s} {ms:27s}  {gb:42s}  ref {rs}")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump({"batch": args.batch, "imgsz": args.imgsz, "peak_gbs": peak, "rows": rows}, f, indent=1)
+
+
+def mode_node(args):
+    """One eager forward of the model, then one node of it `repeat` more times inside the NVTX range
+    "osam_profile" — the target of `ncu --nvtx --nvtx-include osam_profile/ -c <repeat> …`.
+
+        python bench.py --mode node --batch 32 --node model.22.proto.cv2 --repeat 3"""
+    import numpy as np
+    import torch
+    from objectsam_b200.model import Model
+    from oracle import yolo_params
+    m = Model(args.batch, args.imgsz)
+    m.load(yolo_params.make_weights(0))
+    m.sync_weights()
+    rng = np.random.Generator(np.random.PCG64(0))
+    m.input().copy_(torch.from_numpy(rng.random((args.batch, args.imgsz, args.imgsz, 3), dtype=np.float32)).half())
+    idx = {n["name"]: n["index"] for n in m.nodes()}
+    m.forward()
+    torch.cuda.synchronize()
+    i = idx[args.node]
+    torch.cuda.nvtx.range_push("osam_profile")
+    for _ in range(args.repeat):
+        m.forward_nodes(i, 1)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print(f"repeated node {args.node} (index {i}) {args.repeat} times")
+
+
+def train_leg(args, rank, world, dev, barrier, all_max):
+    """BASELINE config 4's conv path: forward in training mode (batch-statistics BN) + the whole backward
+    from fixed seeded head gradients, with the library's data-parallel gradient exchange (osam_dp_*: NCCL
+    ncclAvg all-reduce in buckets, overlapped) when N > 1; K steps after W warm-ups, max over ranks; the same
+    steps without the exchange give its exposed cost.  The loss and the optimizer are outside the path and
+    in neither number.  Beside it, the reference's own training pass (Model::forward(true) + backward,
+    oracle/_ref/ref_train, cuDNN) on every rank's GPU: it has no gradient exchange (single-GPU trainer)."""
+    import torch
+    from objectsam_b200.dp import NcclDataParallel
+    from objectsam_b200.model import Model
+    from oracle import fsow, yolo_params
+    B, S, K = args.train_batch, 640, args.steps  # BASELINE config 4 is 640²
+    weights = yolo_params.make_weights(0)
+    m = Model(B, S)
+    m.load(weights)
+    m.sync_weights()
+    m.train_init()
+    m.input().copy_(torch.from_numpy(yolo_params.make_images(B, S, 1 + rank)).half().to(dev))
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    for n in [f"out.{k}{l}" for k in ("box", "cls", "coef") for l in range(3)] + ["out.proto"]:
+        t = m.act_grad(n)
+        t.copy_((torch.randn(t.shape, generator=g, device=dev) * 0.05).half())
+    dp = NcclDataParallel(m, bucket_mb=args.bucket_mb)
+    stream = torch.cuda.current_stream()
+
+    def run(exchange, steps):
+        for _ in range(steps):
+            m.forward_train(0.03)
+            if exchange:
+                dp.backward()
+            else:
+                m.backward()
+
+    def timed(exchange):
+        run(exchange, max(3, args.warmup))
+        if exchange:
+            dp.wait(120000)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run(exchange, K)
+        e1.record(stream)
+        if exchange:
+            dp.wait(120000)
+        barrier()
+        return e0.elapsed_time(e1) / K
+
+    t_dp, = all_max([timed(True)])
+    t_local, = all_max([timed(False)])
+    nb = dp.num_buckets
+    dp.close()
+    m.close()
+    torch.cuda.synchronize()
+    ref = {}
+    binary = os.path.join(ROOT, "oracle", "_ref", "ref_train")
+    if os.path.exists(binary):
+        with tempfile.TemporaryDirectory() as td:
+            wp = os.path.join(td, "w.fsow")
+            fsow.save(wp, weights)
+            try:
+                r = subprocess.run([binary, wp, "-", "-", str(K), str(B), str(S)], capture_output=True, text=True,
+                                   timeout=900, env=child_env())
+                for line in r.stdout.splitlines():
+                    if line.startswith("{"):
+                        ref = json.loads(line)
+            except subprocess.SubprocessError:
+                ref = {}
+    rms, = all_max([ref.get("ms", float("inf"))])
+    out = {"img_per_s": world * B / (t_dp / 1e3), "ms_per_step": t_dp, "ms_per_step_no_exchange": t_local,
+           "exchange_exposed_ms": t_dp - t_local if world > 1 else 0.0, "buckets": nb, "bucket_mb": args.bucket_mb,
+           "nccl_ranks": world if world > 1 else 0, "batch_per_gpu": B, "imgsz": S,
+           "step": "forward(train) + backward of the conv stack (BN batch statistics, fp32 gradients) + averaged "
+                   "gradient all-reduce (osam_dp, NCCL) when N > 1; no loss, no optimizer"}
+    if rms < float("inf"):
+        out["reference_cudnn"] = {"ms_per_gpu_step": rms, "job_img_per_s": world * B / (rms / 1e3),
+                                  "speedup_per_gpu_step": rms / t_local,
+                                  "note": "reference Model::forward(true) + backward, its cuDNN build, no exchange"}
+    return out
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.mode != "step":
+        import torch
+        torch.cuda.set_device(local)
+        {"sweep": mode_sweep, "train-passes": mode_train_passes, "node": mode_node}[args.mode](args)
         return
     # pin this rank to the CPUs near its GPU before anything allocates pinned host memory (first touch
     # then places the staging buffers in the GPU's NUMA node)
@@ -608,6 +989,9 @@ def main():
             ref_cudnn["speedup_forward_only"] = (world * B * 1e3 / fwd_graph_ms_max) / ref_cudnn["job_img_per_s"]
             ref_cudnn["speedup_step"] = value / ref_cudnn["job_img_per_s"]
             ref_cudnn["ranks"] = world
+    train = None
+    if not args.no_train:
+        train = train_leg(args, rank, world, dev, barrier, all_max)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_forward_sample(S, args.cpu_sample_s)
@@ -629,7 +1013,7 @@ def main():
                 "gpu_launches": K * n_all, "clocks": clocks, "forward_only_img_per_s": world * B * 1e3 / fwd_graph_ms_max,
                 "forward_only_ms": fwd_graph_ms_max,
                 "detections_per_image": n_det_mean, "parity": parity, "roofline": roofline, "cpu_baseline": cpu,
-                "e2e": e2e, "reference_cudnn": ref_cudnn,
+                "e2e": e2e, "reference_cudnn": ref_cudnn, "train": train,
                 "top_kernels": sorted(({"name": nodes[i]["name"], "ms": round(node_ms[i], 4),
                                         "tflops": round(nodes[i]["flops"] / (node_ms[i] / 1e3) / 1e12, 1),
                                         "gbs": round(nodes[i]["bytes"] / (node_ms[i] / 1e3) / 1e9, 0)}
