@@ -580,8 +580,8 @@ def mode_train_passes(args):
 
 
 def mode_node(args):
-    """One eager forward of the model, then one node of it `repeat` more times inside the NVTX range
-    "osam_profile" — the target of `ncu --nvtx --nvtx-include osam_profile/ -c <repeat> …`.
+    """One eager forward of the model, then the listed nodes (comma-separated) `repeat` more times each
+    inside the NVTX range "osam_profile" — the target of `ncu --nvtx --nvtx-include osam_profile/ …`.
 
         python bench.py --mode node --batch 32 --node model.22.proto.cv2 --repeat 3"""
     import numpy as np
@@ -596,13 +596,14 @@ def mode_node(args):
     idx = {n["name"]: n["index"] for n in m.nodes()}
     m.forward()
     torch.cuda.synchronize()
-    i = idx[args.node]
+    names = args.node.split(",")
     torch.cuda.nvtx.range_push("osam_profile")
-    for _ in range(args.repeat):
-        m.forward_nodes(i, 1)
+    for name in names:  # in the listed order, each `repeat` times
+        for _ in range(args.repeat):
+            m.forward_nodes(idx[name], 1)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
-    print(f"repeated node {args.node} (index {i}) {args.repeat} times")
+    print(f"repeated nodes {names} {args.repeat} times each")
 
 
 def train_leg(args, rank, world, dev, barrier, all_max):
