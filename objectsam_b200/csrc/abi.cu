@@ -497,9 +497,32 @@ static bool choose_w3s2(const osam_conv_plan* p) {
   return p->P % 16 == 0 && p->Q % 8 == 0 && g.C == p->BK && p->ntn == 1 && p->BN <= 64;
 }
 
+static int conv_prepare_launch(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep,
+                               float beta, void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready,
+                               int* err_word, int par, int y_ctot, int y_choff);
+
 int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep, float beta, void* y,
                  void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready, int* err_word, int par, int y_ctot,
                  int y_choff) {
+  const int rc = conv_prepare_launch(p, x, w, ep, beta, y, ws, ws_bytes, L, w_gemm_ready, err_word, par, y_ctot,
+                                     y_choff);
+  if (rc == OSAM_OK) {  // the kernels' divisors, once the tile shape is final
+    ConvDev& d = L->d;
+    d.f_ntn.set(d.ntn);
+    d.f_tq.set(d.tiles_q);
+    d.f_tp.set(d.tiles_p);
+    d.f_tw.set(d.tw);
+    d.f_nw.set(d.tn * d.tw);
+    d.f_thw.set(d.th * d.tw);
+    d.f_nkc.set(d.nkc);
+    d.f_S.set(d.S);
+  }
+  return rc;
+}
+
+static int conv_prepare_launch(const osam_conv_plan* p, const void* x, const void* w, const osam_epilogue* ep,
+                               float beta, void* y, void* ws, size_t ws_bytes, ConvLaunch* L, bool w_gemm_ready,
+                               int* err_word, int par, int y_ctot, int y_choff) {
   if (!p || !x || !w) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
   const osam_conv_geom& g = p->g;
   *L = ConvLaunch{};
@@ -676,7 +699,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
     bool rgb = g.R == 3 && g.S == 3 && g.C == 3 && g.stride == 2 && g.pad == 1 && g.K == 32 && p->Q % 64 == 0 &&
                p->P % 2 == 0 && e.coop && !e.res && !e.shuffle && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                ((size_t)g.W * 3 * 2) % 16 == 0;
-    for (int i = 0; i < e.ndest && rgb; i++) rgb = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
+    for (int i = 0; i < e.ndest && rgb; i++) rgb = e.dest[i].c0 % 16 == 0 && e.dest[i].c1 % 16 == 0;
     if (rgb) {
       d.th = 2;
       d.tw = 64;
@@ -689,7 +712,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
       const uint32_t box[3] = {208, 5, 1};
       int rc = make_map(&L->ta, x, 3, dims, str, box, 0);
       if (rc) return rc;
-      const uint32_t sbox[4] = {32, 32, 1, 1};
+      const uint32_t sbox[4] = {16, 32, 1, 1};  // one epilogue warp: 16 channels × 32 pixels, unswizzled
       for (int t = 0; t < e.ndest && rc == OSAM_OK; t++) {
         const DestDev& ds = e.dest[t];
         const uint64_t c = (uint64_t)ds.ctot;
@@ -708,7 +731,7 @@ int conv_prepare(const osam_conv_plan* p, const void* x, const void* w, const os
             ss[1] = (uint64_t)p->Q * c * 2;
             ss[2] = (uint64_t)p->P * p->Q * c * 2;
           }
-          rc = make_map(&L->sm.m[4 * t + v], b, 4, sd, ss, sbox, 64);
+          rc = make_map(&L->sm.m[4 * t + v], b, 4, sd, ss, sbox, 0);
         }
       }
       if (rc) return rc;

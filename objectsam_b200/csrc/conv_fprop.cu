@@ -178,10 +178,11 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
         for (int t = t_first; t < ntiles && ok; t += t_step) {
           // PAIR: this CTA's tile of the unit (past the end for the peer of an odd last unit: zero fill),
           // its half of the weight rows; every load counts on the leader's barriers
-          const int nt = t % d.ntn, mt = PAIR ? (t / d.ntn) * 2 + (int)rank : t / d.ntn;
+          const int tn_q = d.f_ntn.quo(t), nt = d.f_ntn.rem(t, tn_q), mt = PAIR ? tn_q * 2 + (int)rank : tn_q;
           const int n0 = nt * BN + (int)rank * Cfg::B_ROWS;
-          const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-          const int q0 = tq * tw, p0 = (rest % d.tiles_p) * th, b0 = (rest / d.tiles_p) * ni;
+          const int rest = d.f_tq.quo(mt), tq = d.f_tq.rem(mt, rest);
+          const int rp = d.f_tp.quo(rest);
+          const int q0 = tq * tw, p0 = d.f_tp.rem(rest, rp) * th, b0 = rp * ni;
           for (int cc = 0; cc < d.C && ok; cc += BK) {
             for (int c = 0; c < 3 && ok; c++, ait++) {
               const int ws = ait % Cfg::A_STAGES;
@@ -240,16 +241,16 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
       for (int t = t_first; t < ntiles && ok; t += t_step) {
         // PAIR: the peer's tile of a last unit with an odd tile count lies past the end: its boxes read
         // the zero fill (TMA out-of-range), its epilogue stores nothing
-        const int nt = t % d.ntn, mt = PAIR ? (t / d.ntn) * 2 + (int)rank : t / d.ntn;
+        const int tn_q = d.f_ntn.quo(t), nt = d.f_ntn.rem(t, tn_q), mt = PAIR ? tn_q * 2 + (int)rank : tn_q;
         const int n0 = nt * BN + (int)rank * Cfg::B_ROWS;
         int q0 = 0, p0 = 0, b0 = 0, m0 = 0;
         if (MODE == A_GEMM) {
           m0 = mt * 128;
         } else {
-          const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-          q0 = tq * d.tw;
-          p0 = (rest % d.tiles_p) * d.th;
-          b0 = (rest / d.tiles_p) * d.tn;
+          const int rest = d.f_tq.quo(mt), rp = d.f_tp.quo(rest);
+          q0 = d.f_tq.rem(mt, rest) * d.tw;
+          p0 = d.f_tp.rem(rest, rp) * d.th;
+          b0 = rp * d.tn;
         }
         for (int kb = 0; kb < d.nk; kb++, it++) {
           const int s = it % STAGES;
@@ -257,14 +258,14 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
             ok = false;
             break;
           }
-          const int tap = kb / d.nkc, cc = (kb - tap * d.nkc) * BK;  // taps outer, channel chunks inner
+          const int tap = d.f_nkc.quo(kb), cc = d.f_nkc.rem(kb, tap) * BK;  // taps outer, channel chunks inner
           uint8_t* a = sA + s * Cfg::A_BYTES;
           uint8_t* b = sB + s * Cfg::B_BYTES;
           int ca[5] = {cc, 0, 0, 0, 0};  // A box coordinates
           if (MODE == A_GEMM) {
             ca[1] = m0;
           } else {
-            const int r = tap / d.S, c = tap - r * d.S;
+            const int r = d.f_S.quo(tap), c = tap - r * d.S;
             if (MODE == A_S1) {
               ca[1] = q0 + c - d.pad;
               ca[2] = p0 + r - d.pad;
@@ -439,7 +440,8 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
     const uint32_t acce_leader = PAIR ? mapa_shared(acce, 0) : 0;  // drained barriers live in the leader
     uint32_t lt = 0;
     for (int t = t_first; t < ntiles; t += t_step, lt++) {
-      const int nt = t % d.ntn, mt = PAIR ? (t / d.ntn) * 2 + (int)rank : t / d.ntn, n0 = nt * BN;
+      const int tn_q = d.f_ntn.quo(t), nt = d.f_ntn.rem(t, tn_q), mt = PAIR ? tn_q * 2 + (int)rank : tn_q;
+      const int n0 = nt * BN;
       if (PAIR && mt >= d.tiles_m) {  // the peer's tile of an odd last unit: nothing to store
         const uint32_t buf = lt & 1;
         if (!mbar_wait(accf + buf, (lt >> 1) & 1, d.err)) break;
@@ -460,19 +462,18 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
         p = (int)(tt % d.P);
         n = (int)(tt / d.P);
       } else if (W3) {  // GEMM rows in (row, image, column) order
-        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q, nw = d.tn * d.tw;
-        const int i = row / nw, rr = row - i * nw, ni = rr / d.tw, j = rr - ni * d.tw;
-        n = (rest / d.tiles_p) * d.tn + ni;
-        p = (rest % d.tiles_p) * d.th + i;
+        const int rest = d.f_tq.quo(mt), tq = d.f_tq.rem(mt, rest), rp = d.f_tp.quo(rest);
+        const int i = d.f_nw.quo(row), rr = d.f_nw.rem(row, i), ni = d.f_tw.quo(rr), j = d.f_tw.rem(rr, ni);
+        n = rp * d.tn + ni;
+        p = d.f_tp.rem(rest, rp) * d.th + i;
         q = tq * d.tw + j;
         valid = n < d.N && p < d.P && q < d.Q;
         pix = ((long long)n * d.P + p) * d.Q + q;
       } else {
-        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-        const int thw = d.th * d.tw;
-        const int ni = row / thw, rr = row - ni * thw, i = rr / d.tw, j = rr - i * d.tw;
-        n = (rest / d.tiles_p) * d.tn + ni;
-        p = (rest % d.tiles_p) * d.th + i;
+        const int rest = d.f_tq.quo(mt), tq = d.f_tq.rem(mt, rest), rp = d.f_tp.quo(rest);
+        const int ni = d.f_thw.quo(row), rr = d.f_thw.rem(row, ni), i = d.f_tw.quo(rr), j = d.f_tw.rem(rr, i);
+        n = rp * d.tn + ni;
+        p = d.f_tp.rem(rest, rp) * d.th + i;
         q = tq * d.tw + j;
         valid = n < d.N && p < d.P && q < d.Q;
         pix = ((long long)n * d.P + p) * d.Q + q;
@@ -481,16 +482,16 @@ __global__ void __launch_bounds__(FpropCfg<BK, BN, PAIR, MODE>::THREADS, FpropCf
       if (W3) {
         // the store maps are (C, Q, N, P) views, so their 3rd and 4th coordinates are image and row:
         // passed in the (bp, bn) slots.  A warp's 32 rows are 32 / (ni·tw) whole tile rows.
-        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-        bq = tq * d.tw;
-        bp = (rest / d.tiles_p) * d.tn;
-        bn = (rest % d.tiles_p) * d.th + (quad * 32) / (d.tn * d.tw);
+        const int rest = d.f_tq.quo(mt), rp = d.f_tp.quo(rest);
+        bq = d.f_tq.rem(mt, rest) * d.tw;
+        bp = rp * d.tn;
+        bn = d.f_tp.rem(rest, rp) * d.th + d.f_nw.quo(quad * 32);
       } else if (MODE != A_GEMM) {
-        const int tq = mt % d.tiles_q, rest = mt / d.tiles_q;
-        const int w0 = quad * 32, thw = d.th * d.tw;
-        bq = tq * d.tw + w0 % d.tw;
-        bp = (rest % d.tiles_p) * d.th + (w0 / d.tw) % d.th;
-        bn = (rest / d.tiles_p) * d.tn + w0 / thw;
+        const int rest = d.f_tq.quo(mt), rp = d.f_tp.quo(rest);
+        const int w0 = quad * 32, wq = d.f_tw.quo(w0);
+        bq = d.f_tq.rem(mt, rest) * d.tw + d.f_tw.rem(w0, wq);
+        bp = d.f_tp.rem(rest, rp) * d.th + (wq & (d.th - 1));
+        bn = rp * d.tn + d.f_thw.quo(w0);
       }
       const uint32_t buf = lt & 1;
       // the residual of the first 32 columns is loaded before the accumulator is ready; each later pass's

@@ -55,6 +55,29 @@ struct EpiDev {
   int wtw, wth, wtn;  // a warp's 32 rows as a (wtn images × wth rows × wtw cols) box of the tile
 };
 
+// Division by a divisor fixed at launch preparation without the integer-division instruction sequence:
+// q = (umulhi(n, m) + n) >> s for 0 ≤ n < 2³¹, with s = ⌈log₂ d⌉ and m = ⌊2³²·(2ˢ − d)/d⌋ + 1 (the
+// round-up method of Granlund & Montgomery, "Division by invariant integers using multiplication", 1994).
+// A power of two gives m = 1: a shift.  The kernels' per-tile and per-row index math (tile → image, row,
+// column) uses it; with the generic sequence that math cost about as many instructions as the
+// epilogue's arithmetic on the narrow layers.
+struct FastDiv {
+  int d = 1, s = 0;
+  uint32_t m = 1;
+  void set(int dv) {
+    d = dv < 1 ? 1 : dv;
+    s = 0;
+    while ((1LL << s) < d) s++;
+    m = (uint32_t)(((1ULL << 32) * ((1ULL << s) - (unsigned long long)d)) / (unsigned long long)d + 1);
+  }
+#ifdef __CUDACC__
+  __device__ __forceinline__ int quo(int n) const {
+    return (int)((__umulhi((uint32_t)n, m) + (uint32_t)n) >> s);
+  }
+  __device__ __forceinline__ int rem(int n, int q) const { return n - q * d; }
+#endif
+};
+
 struct ConvDev {
   int N, H, W, C, K, P, Q, R, S, stride, pad;
   int gemm_n;                 // GEMM N (= K, or 4·K for the transposed conv)
@@ -71,6 +94,9 @@ struct ConvDev {
   int win_nwb;                // A_WIN: window buffers (2 or 3)
   unsigned win_mul;           // A_WIN: ⌈2³²/pitch⌉ — u / pitch = umulhi(u, win_mul) for the sizes planned
   int* err;                   // device error word
+  // the divisions of the conv kernels' index math (FastDiv): GEMM-N tiles, spatial tiles along Q and P,
+  // tile columns, images × columns of a window-form tile row, rows × columns of a tile, channel chunks, S
+  FastDiv f_ntn, f_tq, f_tp, f_tw, f_nw, f_thw, f_nkc, f_S;
   EpiDev ep;
 };
 
