@@ -8,7 +8,8 @@ One process per GPU (torchrun for N > 1); images are sharded across ranks with n
 scaling: every rank runs its own batch).  A step is the config-2 inference of the rank's batch: the
 forward pass of the fused conv path (stem → backbone → SPPF → neck → Segment head → proto, every conv
 one kernel with its folded-BN/SiLU/residual/concat epilogue), then DFL decode, conf > 0.25, NMS IoU 0.7,
-≤ 300 detections per image and the mask assembly (coef · proto > 0, cropped), masks bit-packed.  Timing:
+≤ 300 detections per image and the mask assembly (coef · proto > 0, cropped), masks bit-packed — all one
+detect step (one CUDA graph; decode and NMS overlap the proto branch).  Timing:
 W untimed warm-up steps, then K steps between a barrier + synchronize on both sides, CUDA events on the
 launching stream, max over ranks.  The inputs (157 MB per step at 640²) and activations (GBs) are larger
 than the 126 MB L2, so no flush is needed.
@@ -21,7 +22,7 @@ Rank 0 prints one JSON line.  Besides the contract keys it carries:
                   one CUDA graph of K steps) against the measured burst peaks in MEASURED_PEAKS.json, plus
                   the whole forward against its tensor and HBM floors;
   e2e             the same metric through the C-ABI model with host buffers: every step's pinned host →
-                  device input copy, forward + post-process, device → host copy of the detections and
+                  device input copy, the detect step, device → host copy of the detections and
                   packed masks, pipelined over two copy streams (double-buffered input staging); each rank
                   runs on the CPUs NVML names as near its GPU, so its pinned buffers are NUMA-local, and
                   its host → device copy rate alone is reported beside it;
@@ -762,29 +763,40 @@ def main():
     nodes[n + 2]["flops"] = 2.0 * B * 384 * 32 * Hp * Hp
     n_all = len(nodes)
 
-    # ---- warm-up (eager + graph)
+    # ---- warm-up (eager + graph): the separate post-process, then the detect step
+    model.detect_init(0.25, 0.7, 300, packed=True)
     for _ in range(args.warmup):
         model.forward()
         post()
-    model.forward(use_graph=True)
-    post()
+        model.forward_detect(use_graph=False)
+    model.forward_detect(use_graph=True)
     barrier()
 
-    # ---- timed region: K steps through the product path — the model's captured CUDA graph of the
-    # forward, then decode / NMS / masks — with a CUDA event on each side
+    # ---- timed region: K detect steps through the product path — one captured CUDA graph of the forward
+    # with decode / NMS / masks in it (decode and NMS overlap the proto branch) — with a CUDA event on each side
     K = args.steps
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
         g0.record(stream)
         for _ in range(K):
-            model.forward(use_graph=True)
-            det = post()
+            model.forward_detect(use_graph=True)
         g1.record(stream)
         barrier()
     ms = g0.elapsed_time(g1)
     clocks = clk.summary()
+    det = model.detections()
     n_det_mean = float(det["n_det"].float().mean().item())
+    # the detect step's outputs equal the separate post-process of the same forward
+    ref_det = post()
+    torch.cuda.synchronize()
+    same = torch.equal(det["n_det"], ref_det["n_det"])
+    nd = det["n_det"].cpu().tolist()
+    for k in ("keep", "score", "masks"):
+        same = same and all(torch.equal(det[k][b, :nd[b]], ref_det[k][b, :nd[b]]) for b in range(B))
+    if not same:
+        print(json.dumps({"error": "the detect step's detections differ from the separate post-process"}))
+        sys.exit(3)
 
     # ---- correctness of the timed batch (outside the timed region): the forward's heads and proto for
     # the batch's first and last image against the reference's cuDNN fp16 build run on those two images
@@ -817,19 +829,14 @@ def main():
         stage = [torch.empty_like(d_in) for _ in range(2)]
         # two result slots on the device (step i writes slot i % 2 while slot (i-1) % 2 drains to the host)
         # and two on the host: nothing is allocated inside the timed loop
-        A_ = sum(t.shape[1] * t.shape[2] for t in box)
-        slots = []
-        for _ in range(2):
-            dd = {k: torch.empty_like(det[k]) for k in ("n_det", "keep", "box", "score", "coef_g", "masks")}
-            dd["xyxy"] = torch.empty(B, A_, 4, dtype=torch.float32, device=dev)
-            dd["conf"] = torch.empty(B, A_, dtype=torch.float32, device=dev)
-            slots.append(dd)
+        slots = [{k: torch.empty_like(det[k]) for k in keys} for _ in range(2)]
         h_out = [{k: torch.empty(det[k].shape, dtype=det[k].dtype, pin_memory=True) for k in keys} for _ in range(2)]
 
-        def post_into(dd):
-            postproc.decode(box, cls, S, out=(dd["xyxy"], dd["conf"]))
-            postproc.nms(dd["xyxy"], dd["conf"], 0.25, 0.7, 300, coef=coef, out=dd)
-            postproc.mask_assemble(dd["coef_g"], proto, dd, S, packed=True, out=dd["masks"])
+        def keep_results(dd):
+            # the detect step's buffers are rewritten by the next step: move this step's results into a slot
+            # with elementwise kernels (×1, exact) on the compute stream, for the same copy-engine reason
+            for k in keys:
+                torch.mul(det[k], 1, out=dd[k])
 
         def e2e_run(steps):
             ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -854,10 +861,10 @@ def main():
                 # host → device copy on that engine, which serialises the copies with the compute
                 torch.mul(stage[s], 1, out=d_in)
                 ev_used[s].record(stream)
-                model.forward(use_graph=True)
+                model.forward_detect(use_graph=True)
                 if i >= 2:
                     stream.wait_event(ev_out[s])  # slot s's results of step i-2 have reached the host
-                post_into(slots[s])
+                keep_results(slots[s])
                 done = torch.cuda.Event()
                 done.record(stream)
                 with torch.cuda.stream(copy_out):
@@ -1008,7 +1015,7 @@ def main():
                                        f"U[0,1] images, He-normal weights",
                            "global_batch": B * world, "imgsz": S, "parallelism": f"dp{world} (image shards, no collective)",
                            "l2": "inputs+activations > 126 MB L2 (no flush needed)",
-                           "timing": "timed region = K steps of the model's CUDA graph (forward) + decode/NMS/mask launches, "
+                           "timing": "timed region = K detect steps (one CUDA graph: forward + decode/NMS/masks), "
                                      "CUDA events on each side, max over ranks; per-kernel durations from a CUDA graph "
                                      "of K steps with a timing event around every kernel"},
                 "gpu_launches": K * n_all, "clocks": clocks, "forward_only_img_per_s": world * B * 1e3 / fwd_graph_ms_max,

@@ -287,6 +287,29 @@ int osam_model_act(const osam_model* m, const char* name, osam_tensor* t);   /* 
 int osam_model_forward(osam_model* m, int use_graph, osam_stream_t stream);
 /* Kernels launched by one forward pass (one per graph node). */
 int osam_model_num_launches(const osam_model* m);
+
+/* The whole inference step of BASELINE config 2 in one graph: the forward, then DFL decode, score threshold +
+ * greedy NMS and the mask assembly (osam_decode / osam_nms / osam_mask_assemble) on the model's own output
+ * buffers.  The post-process launches join the forward's dependency graph: decode and NMS need only the box,
+ * class and coefficient heads, so they run while the proto branch is still computing; the masks wait for
+ * proto.  Replaces the reference's Model::forward(false) followed by archive/tools/ref_detect.py's numpy
+ * steps (:37-81).  osam_model_detect_init fixes the settings and allocates the outputs (once; again only
+ * when max_det or packed change); osam_model_forward_detect runs the step (use_graph: as a captured CUDA
+ * graph, recorded at the first call); osam_model_detections returns the output buffers. */
+typedef struct osam_detections {
+  int batch, anchors, max_det, packed, proto_h, proto_w;
+  float* xyxy;    /* [batch][anchors][4] decoded boxes, input pixels */
+  float* conf;    /* [batch][anchors] sigmoid(class logit) */
+  int* n_det;     /* [batch] */
+  int* keep;      /* [batch][max_det] kept anchors in score order, −1 padded */
+  float* box;     /* [batch][max_det][4] */
+  float* score;   /* [batch][max_det] */
+  void* coef_g;   /* [batch][ceil128(max_det)][32] fp16 mask coefficients of the kept anchors */
+  void* masks;    /* packed: u32 [batch][max_det][ceil(Hp·Wp/32)]; else u8 [batch][max_det][Hp·Wp] */
+} osam_detections;
+int osam_model_detect_init(osam_model* m, float conf_th, float iou_th, int max_det, int forced, int packed);
+int osam_model_forward_detect(osam_model* m, int use_graph, osam_stream_t stream);
+int osam_model_detections(const osam_model* m, osam_detections* d);
 /* Launch nodes [first, first+count) of the forward pass on `stream` (eager), e.g. to bracket one
  * kernel with timing events.  Running every node in order equals osam_model_forward(m, 0, stream). */
 int osam_model_forward_nodes(osam_model* m, int first, int count, osam_stream_t stream);

@@ -43,6 +43,12 @@ class Tensor(ctypes.Structure):
     _fields_ = [("p", c_void_p), ("n", c_int), ("h", c_int), ("w", c_int), ("c", c_int)]
 
 
+class Detections(ctypes.Structure):
+    """osam_detections — the detect step's output buffers (device pointers)."""
+    _fields_ = [(f, c_int) for f in ("batch", "anchors", "max_det", "packed", "proto_h", "proto_w")] + \
+               [(f, c_void_p) for f in ("xyxy", "conf", "n_det", "keep", "box", "score", "coef_g", "masks")]
+
+
 class OsamError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"osam error {code}: {msg}")
@@ -97,6 +103,9 @@ _SIGS = {
     "osam_model_act": (c_int, [c_void_p, ctypes.c_char_p, POINTER(Tensor)]),
     "osam_model_forward": (c_int, [c_void_p, c_int, c_void_p]),
     "osam_model_num_launches": (c_int, [c_void_p]),
+    "osam_model_detect_init": (c_int, [c_void_p, c_float, c_float, c_int, c_int, c_int]),
+    "osam_model_forward_detect": (c_int, [c_void_p, c_int, c_void_p]),
+    "osam_model_detections": (c_int, [c_void_p, POINTER(Detections)]),
     "osam_model_forward_nodes": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "osam_model_node_info": (c_int, [c_void_p, c_int, ctypes.c_char_p, c_int, POINTER(c_int), POINTER(ConvGeom)]),
     "osam_model_train_init": (c_int, [c_void_p, c_void_p]),

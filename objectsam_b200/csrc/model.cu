@@ -108,9 +108,7 @@ struct osam_model {
   float* f32 = nullptr;
   size_t f32_n = 0;
   bool synced = false;
-  cudaGraph_t graph = nullptr;
-  cudaGraphExec_t exec = nullptr;
-  cudaStream_t cap = nullptr;  // private stream the graph is recorded on (the legacy stream cannot capture)
+  cudaStream_t cap = nullptr;  // private stream the step graphs are recorded on (the legacy stream cannot capture)
   // training (osam_model_train_init)
   bool train = false;
   uint8_t* garena = nullptr;   // activation gradients
@@ -141,11 +139,39 @@ struct osam_model {
   // leaves idle in its last wave.  Stream 0 is the caller's; the schedule is fixed at the first forward.
   static constexpr int kFwdStreams = 3;
   cudaStream_t fwd_st[kFwdStreams - 1] = {};
-  std::vector<int> node_order;               // launch order: topological, longest remaining path first
-  std::vector<int> node_stream;              // per node: 0 … kFwdStreams − 1
-  std::vector<std::vector<int>> node_waits;  // per node: producers on other streams (latest per stream)
-  std::vector<cudaEvent_t> node_ev;          // per node: recorded after it when another stream waits on it
   cudaEvent_t ev_fwd_start = nullptr, ev_fwd_end[kFwdStreams - 1] = {};
+  // A task of a scheduled step: a model node (its kernel) or a post-process launch of the detect step.
+  enum TaskKind { T_NODE = 0, T_DECODE = 1, T_NMS = 2, T_MASK = 3 };
+  struct Task {
+    TaskKind kind;
+    int node;  // T_NODE: index into nodes
+    std::vector<const MAct*> reads, writes;
+    double cost;  // FLOPs (the longest-remaining-chain priority)
+  };
+  struct Schedule {
+    std::vector<Task> tasks;
+    std::vector<int> order;               // launch order: topological, longest remaining path first
+    std::vector<int> stream;              // per task: 0 … kFwdStreams − 1
+    std::vector<std::vector<int>> waits;  // per task: producers on other streams (latest per stream)
+    std::vector<cudaEvent_t> ev;          // per task: recorded after it when another stream waits on it
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+  };
+  Schedule fwd_sched, det_sched;  // the forward; the forward with decode / NMS / masks
+
+  // ---- the detect step (osam_model_detect_*): post-process outputs owned by the model
+  bool det_on = false;
+  float det_conf = 0.25f, det_iou = 0.7f;
+  int det_max = 300, det_forced = 0, det_packed = 1;
+  float* det_xyxy = nullptr;   // [N][A][4]
+  float* det_confs = nullptr;  // [N][A]
+  int* det_n = nullptr;        // [N]
+  int* det_keep = nullptr;     // [N][max_det]
+  float* det_box = nullptr;    // [N][max_det][4]
+  float* det_score = nullptr;  // [N][max_det]
+  __half* det_coef = nullptr;  // [N][ceil128(max_det)][32]
+  void* det_masks = nullptr;   // [N][max_det][words or Hp·Wp]
+  MAct det_decoded, det_kept, det_maskt;  // stand-ins for the DAG (read/written by the post-process tasks)
 
   // ------------------------------------------------------------------ graph construction
   // The network is data (kLayers below, one row per model.<i> module) lowered in two steps:
@@ -488,11 +514,14 @@ struct osam_model {
   }
 
   void release() {
-    // the instantiated graph refers to the forward's streams' events: destroy it first
-    if (exec) cudaGraphExecDestroy(exec);
-    if (graph) cudaGraphDestroy(graph);
-    exec = nullptr;
-    graph = nullptr;
+    // the instantiated step graphs refer to the forward's streams' events: destroy them first
+    for (Schedule* sc : {&fwd_sched, &det_sched}) {
+      if (sc->exec) cudaGraphExecDestroy(sc->exec);
+      if (sc->graph) cudaGraphDestroy(sc->graph);
+      for (cudaEvent_t ev : sc->ev)
+        if (ev) cudaEventDestroy(ev);
+      *sc = Schedule{};
+    }
     for (auto& nd : nodes) free_subplans(nd->plan);
     cudaFree(garena);
     cudaFree(zarena);
@@ -518,12 +547,14 @@ struct osam_model {
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
     if (side) cudaStreamDestroy(side);
-    for (cudaEvent_t ev : node_ev)
-      if (ev) cudaEventDestroy(ev);
-    node_ev.clear();
-    node_order.clear();
-    node_stream.clear();
-    node_waits.clear();
+    for (void* p : {(void*)det_xyxy, (void*)det_confs, (void*)det_n, (void*)det_keep, (void*)det_box,
+                    (void*)det_score, (void*)det_coef, det_masks})
+      cudaFree(p);
+    det_xyxy = det_confs = det_box = det_score = nullptr;
+    det_n = det_keep = nullptr;
+    det_coef = nullptr;
+    det_masks = nullptr;
+    det_on = false;
     for (int k = 0; k < kFwdStreams - 1; k++) {
       if (fwd_st[k]) cudaStreamDestroy(fwd_st[k]);
       if (ev_fwd_end[k]) cudaEventDestroy(ev_fwd_end[k]);
@@ -543,11 +574,7 @@ struct osam_model {
     dz = gw16 = wconvt = nullptr;
     ws = bnws = nullptr;
     train = false;
-    if (exec) cudaGraphExecDestroy(exec);
-    if (graph) cudaGraphDestroy(graph);
     if (cap) cudaStreamDestroy(cap);
-    exec = nullptr;
-    graph = nullptr;
     cap = nullptr;
     cudaFree(arena);
     cudaFree(w16);
@@ -632,9 +659,7 @@ struct osam_model {
     if (e != cudaSuccess) return model_fail(OSAM_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
     int rc = prepare_launches();
     if (rc) return rc;
-    synced = true;
-    if (exec) {  // weights changed: the graph's kernel arguments are unchanged (same buffers), keep it
-    }
+    synced = true;  // the step graphs stay valid: new weights, same buffers and kernel arguments
     return OSAM_OK;
   }
 
@@ -681,33 +706,52 @@ struct osam_model {
     return OSAM_OK;
   }
 
-  // Dependency DAG of the forward (a node depends on every earlier writer of an activation it reads;
-  // concat buffers are written by several nodes into disjoint channel slices).  Nodes are launched in a
-  // topological order that puts the longest remaining chain (by FLOPs) first — so the proto branch starts
-  // as soon as its input exists — and assigned greedily to kFwdStreams streams: a node continues the
-  // stream whose last node is its latest producer, else takes the stream idle longest.
-  cudaError_t plan_streams() {
-    if (!node_stream.empty()) return cudaSuccess;
-    const int n = (int)nodes.size();
-    std::map<const MAct*, std::vector<int>> writers;
-    std::vector<std::vector<const MAct*>> rd(n);
-    for (int i = 0; i < n; i++) {
+  // The tasks of a step: every node of the forward (what it reads and writes), and with `detect` the
+  // post-process — decode (the box and class heads), NMS (decoded boxes, the coefficient heads) and the
+  // masks (NMS results, proto) — so that decode and NMS run while the proto branch still computes.
+  std::vector<Task> step_tasks(bool detect) {
+    std::vector<Task> t;
+    for (int i = 0; i < (int)nodes.size(); i++) {
       const MNode& nd = *nodes[i];
+      Task k{T_NODE, i, {}, {}, 1.0};
       if (nd.kind == N_POOL) {
-        rd[i].push_back(nd.cat);
-        writers[nd.cat].push_back(i);
-        continue;
+        k.reads = {nd.cat};
+        k.writes = {nd.cat};
+      } else {
+        k.reads.push_back(nd.in);
+        if (nd.res) k.reads.push_back(nd.res);
+        if (nd.kind == N_CONVBN)
+          for (const MDest& d : nd.dests) k.writes.push_back(d.a);
+        else
+          k.writes.push_back(nd.out);
+        k.cost = 2.0 * (double)nd.plan.M * nd.plan.gemm_n * nd.plan.g.R * nd.plan.g.S * nd.plan.g.C;
       }
-      rd[i].push_back(nd.in);
-      if (nd.res) rd[i].push_back(nd.res);
-      if (nd.kind == N_CONVBN)
-        for (const MDest& d : nd.dests) writers[d.a].push_back(i);
-      else
-        writers[nd.out].push_back(i);
+      t.push_back(std::move(k));
     }
+    if (detect) {
+      t.push_back(Task{T_DECODE, -1, {head[0][0], head[0][1], head[0][2], head[1][0], head[1][1], head[1][2]},
+                       {&det_decoded}, 1.0});
+      t.push_back(Task{T_NMS, -1, {&det_decoded, head[2][0], head[2][1], head[2][2]}, {&det_kept}, 1.0});
+      t.push_back(Task{T_MASK, -1, {&det_kept, proto}, {&det_maskt}, 1.0});
+    }
+    return t;
+  }
+
+  // Dependency DAG of a step (a task depends on every earlier writer of a tensor it reads; concat buffers
+  // are written by several nodes into disjoint channel slices).  Tasks are launched in a topological order
+  // that puts the longest remaining chain (by FLOPs) first — so the proto branch starts as soon as its
+  // input exists — and assigned greedily to kFwdStreams streams: a task continues the stream whose last
+  // task is its latest producer, else takes the stream idle longest.
+  cudaError_t plan(Schedule& sc, bool detect) {
+    if (!sc.stream.empty()) return cudaSuccess;
+    sc.tasks = step_tasks(detect);
+    const int n = (int)sc.tasks.size();
+    std::map<const MAct*, std::vector<int>> writers;
+    for (int i = 0; i < n; i++)
+      for (const MAct* a : sc.tasks[i].writes) writers[a].push_back(i);
     std::vector<std::vector<int>> dep(n), succ(n);
     for (int i = 0; i < n; i++) {
-      for (const MAct* a : rd[i]) {
+      for (const MAct* a : sc.tasks[i].reads) {
         auto it = writers.find(a);
         if (it == writers.end()) continue;
         for (int w : it->second)
@@ -717,17 +761,13 @@ struct osam_model {
       dep[i].erase(std::unique(dep[i].begin(), dep[i].end()), dep[i].end());
       for (int w : dep[i]) succ[w].push_back(i);
     }
-    std::vector<double> bottom(n, 0.0);  // FLOPs of the longest chain from a node to the end
+    std::vector<double> bottom(n, 0.0);  // FLOPs of the longest chain from a task to the end
     for (int i = n - 1; i >= 0; i--) {
-      const MNode& nd = *nodes[i];
-      double c = 1.0;
-      if (nd.kind != N_POOL)
-        c = 2.0 * (double)nd.plan.M * nd.plan.gemm_n * nd.plan.g.R * nd.plan.g.S * nd.plan.g.C;
       double m = 0.0;
       for (int sx : succ[i]) m = std::max(m, bottom[sx]);
-      bottom[i] = c + m;
+      bottom[i] = sc.tasks[i].cost + m;
     }
-    node_order.clear();
+    sc.order.clear();
     std::vector<int> pending(n);
     std::vector<char> ready(n, 0);
     for (int i = 0; i < n; i++) {
@@ -739,79 +779,165 @@ struct osam_model {
       for (int i = 0; i < n; i++)
         if (ready[i] == 1 && (pick < 0 || bottom[i] > bottom[pick])) pick = i;
       ready[pick] = 2;
-      node_order.push_back(pick);
+      sc.order.push_back(pick);
       for (int sx : succ[pick])
         if (--pending[sx] == 0) ready[sx] = 1;
     }
-    node_stream.assign(n, 0);
-    node_waits.assign(n, {});
+    sc.stream.assign(n, 0);
+    sc.waits.assign(n, {});
     std::vector<char> signal(n, 0);
     int tail[kFwdStreams];
     for (int k = 0; k < kFwdStreams; k++) tail[k] = -1;
     std::vector<int> pos(n);
-    for (int q = 0; q < n; q++) pos[node_order[q]] = q;
+    for (int q = 0; q < n; q++) pos[sc.order[q]] = q;
     for (int q = 0; q < n; q++) {
-      const int i = node_order[q];
-      const std::vector<int>& deps = dep[i];  // launched earlier, all of them
-      int st = -1;
-      int best = -1;  // the latest-launched producer that is still the tail of its stream
-      for (int w : deps)
-        if (tail[node_stream[w]] == pos[w] && (best < 0 || pos[w] > pos[best])) best = w;
-      if (best >= 0) st = node_stream[best];
+      const int i = sc.order[q];
+      int st = -1, best = -1;  // the latest-launched producer that is still the tail of its stream
+      for (int w : dep[i])
+        if (tail[sc.stream[w]] == pos[w] && (best < 0 || pos[w] > pos[best])) best = w;
+      if (best >= 0) st = sc.stream[best];
       if (st < 0) {
         st = 0;
         for (int k = 1; k < kFwdStreams; k++)
           if (tail[k] < tail[st]) st = k;
       }
-      node_stream[i] = st;
+      sc.stream[i] = st;
       int latest[kFwdStreams];  // per other stream, the producer launched last there
       for (int k = 0; k < kFwdStreams; k++) latest[k] = -1;
-      for (int w : deps) {
-        const int ks = node_stream[w];
+      for (int w : dep[i]) {
+        const int ks = sc.stream[w];
         if (ks != st && (latest[ks] < 0 || pos[w] > pos[latest[ks]])) latest[ks] = w;
       }
       for (int k = 0; k < kFwdStreams; k++)
         if (latest[k] >= 0) {
-          node_waits[i].push_back(latest[k]);
+          sc.waits[i].push_back(latest[k]);
           signal[latest[k]] = 1;
         }
       tail[st] = q;
     }
     cudaError_t e;
-    node_ev.assign(n, nullptr);
+    sc.ev.assign(n, nullptr);
     for (int i = 0; i < n; i++)
-      if (signal[i] && (e = cudaEventCreateWithFlags(&node_ev[i], cudaEventDisableTiming)) != cudaSuccess) return e;
-    for (int k = 0; k < kFwdStreams - 1; k++) {
-      if ((e = cudaStreamCreateWithFlags(&fwd_st[k], cudaStreamNonBlocking)) != cudaSuccess) return e;
-      if ((e = cudaEventCreateWithFlags(&ev_fwd_end[k], cudaEventDisableTiming)) != cudaSuccess) return e;
+      if (signal[i] && (e = cudaEventCreateWithFlags(&sc.ev[i], cudaEventDisableTiming)) != cudaSuccess) return e;
+    if (!ev_fwd_start) {
+      for (int k = 0; k < kFwdStreams - 1; k++) {
+        if ((e = cudaStreamCreateWithFlags(&fwd_st[k], cudaStreamNonBlocking)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&ev_fwd_end[k], cudaEventDisableTiming)) != cudaSuccess) return e;
+      }
+      if ((e = cudaEventCreateWithFlags(&ev_fwd_start, cudaEventDisableTiming)) != cudaSuccess) return e;
     }
-    return cudaEventCreateWithFlags(&ev_fwd_start, cudaEventDisableTiming);
+    return cudaSuccess;
   }
 
-  cudaError_t run(cudaStream_t st) {
-    cudaError_t e = plan_streams();
-    if (e != cudaSuccess) return e;
+  cudaError_t launch_task(const Task& t, cudaStream_t s) {
+    if (t.kind == T_NODE) {
+      MNode& nd = *nodes[t.node];
+      return nd.kind == N_POOL ? launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, s) : conv_launch(nd.L, s);
+    }
+    const int hw[6] = {head[0][0]->H, head[0][0]->W, head[0][1]->H, head[0][1]->W, head[0][2]->H, head[0][2]->W};
+    const int A = hw[0] * hw[1] + hw[2] * hw[3] + hw[4] * hw[5];
+    const osam_stream_t os = reinterpret_cast<osam_stream_t>(s);
+    int rc = OSAM_OK;
+    if (t.kind == T_DECODE) {
+      const void* box[3] = {head[0][0]->p, head[0][1]->p, head[0][2]->p};
+      const void* cls[3] = {head[1][0]->p, head[1][1]->p, head[1][2]->p};
+      rc = osam_decode(box, cls, hw, N, S, reg_max, det_xyxy, det_confs, os);
+    } else if (t.kind == T_NMS) {
+      const void* coef[3] = {head[2][0]->p, head[2][1]->p, head[2][2]->p};
+      rc = osam_nms(det_xyxy, det_confs, N, A, det_conf, det_iou, det_max, det_forced, coef, hw, det_n, det_keep,
+                    det_box, det_score, det_coef, os);
+    } else {
+      rc = osam_mask_assemble(det_coef, proto->p, det_box, det_n, N, proto->H, proto->W, S, det_max, det_packed,
+                              det_masks, os);
+    }
+    return rc == OSAM_OK ? cudaSuccess : cudaErrorLaunchFailure;
+  }
+
+  cudaError_t run(Schedule& sc, cudaStream_t st) {
     cudaStream_t ss[kFwdStreams] = {st};
     for (int k = 1; k < kFwdStreams; k++) ss[k] = fwd_st[k - 1];
+    cudaError_t e;
     // fork: the internal streams start after the caller's stream has reached this point
     if ((e = cudaEventRecord(ev_fwd_start, st)) != cudaSuccess) return e;
     for (int k = 1; k < kFwdStreams; k++)
       if ((e = cudaStreamWaitEvent(ss[k], ev_fwd_start, 0)) != cudaSuccess) return e;
-    for (int i : node_order) {
-      MNode& nd = *nodes[i];
-      cudaStream_t s = ss[node_stream[i]];
-      for (int w : node_waits[i])
-        if ((e = cudaStreamWaitEvent(s, node_ev[w], 0)) != cudaSuccess) return e;
-      e = nd.kind == N_POOL ? launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, s) : conv_launch(nd.L, s);
-      if (e != cudaSuccess) return e;
-      if (node_ev[i] && (e = cudaEventRecord(node_ev[i], s)) != cudaSuccess) return e;
+    for (int i : sc.order) {
+      cudaStream_t s = ss[sc.stream[i]];
+      for (int w : sc.waits[i])
+        if ((e = cudaStreamWaitEvent(s, sc.ev[w], 0)) != cudaSuccess) return e;
+      if ((e = launch_task(sc.tasks[i], s)) != cudaSuccess) return e;
+      if (sc.ev[i] && (e = cudaEventRecord(sc.ev[i], s)) != cudaSuccess) return e;
     }
-    // join: the caller's stream continues after every node
+    // join: the caller's stream continues after every task
     for (int k = 1; k < kFwdStreams; k++) {
       if ((e = cudaEventRecord(ev_fwd_end[k - 1], ss[k])) != cudaSuccess) return e;
       if ((e = cudaStreamWaitEvent(st, ev_fwd_end[k - 1], 0)) != cudaSuccess) return e;
     }
     return cudaSuccess;
+  }
+
+  // One step (the forward, or the forward with the post-process), eagerly or as this schedule's captured
+  // CUDA graph (recorded at the first call, on the model's own stream, replayed on the caller's).
+  int step(Schedule& sc, bool detect, int use_graph, cudaStream_t st) {
+    cudaError_t e;
+    if ((e = plan(sc, detect)) != cudaSuccess)  // streams and events exist before any capture begins
+      return model_fail(OSAM_ERR_CUDA, "step schedule: %s", cudaGetErrorString(e));
+    if (!use_graph) {
+      e = run(sc, st);
+      return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "step: %s", cudaGetErrorString(e));
+    }
+    if (!sc.exec) {
+      if (!cap && (e = cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking)) != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "capture stream: %s", cudaGetErrorString(e));
+      if ((e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "begin capture: %s", cudaGetErrorString(e));
+      cudaError_t er = run(sc, cap);
+      e = cudaStreamEndCapture(cap, &sc.graph);
+      if (er != cudaSuccess || e != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "capture: %s", cudaGetErrorString(er != cudaSuccess ? er : e));
+      if ((e = cudaGraphInstantiate(&sc.exec, sc.graph, 0)) != cudaSuccess)
+        return model_fail(OSAM_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
+    }
+    e = cudaGraphLaunch(sc.exec, st);
+    return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e));
+  }
+
+  int detect_init(float conf_th, float iou_th, int max_det, int forced, int packed) {
+    if (!synced) return model_fail(OSAM_ERR_INVALID, "detect_init before osam_model_sync_weights");
+    if (max_det < 1 || max_det > 1024) return model_fail(OSAM_ERR_INVALID, "max_det must be in [1, 1024]");
+    // settings change the captured launches: drop the detect step's graph (its buffers stay if sizes match)
+    if (det_sched.exec) cudaGraphExecDestroy(det_sched.exec);
+    if (det_sched.graph) cudaGraphDestroy(det_sched.graph);
+    det_sched.exec = nullptr;
+    det_sched.graph = nullptr;
+    const size_t A = (size_t)head[0][0]->H * head[0][0]->W + (size_t)head[0][1]->H * head[0][1]->W +
+                     (size_t)head[0][2]->H * head[0][2]->W;
+    const size_t pad = ((size_t)max_det + 127) / 128 * 128, hw = (size_t)proto->H * proto->W;
+    const size_t mask_bytes = packed ? 4 * ((hw + 31) / 32) : hw;
+    if (!det_on || max_det != det_max || packed != det_packed) {
+      for (void* q : {(void*)det_xyxy, (void*)det_confs, (void*)det_n, (void*)det_keep, (void*)det_box,
+                      (void*)det_score, (void*)det_coef, det_masks})
+        cudaFree(q);
+      cudaError_t e;
+      if ((e = cudaMalloc(&det_xyxy, (size_t)N * A * 4 * sizeof(float))) != cudaSuccess ||
+          (e = cudaMalloc(&det_confs, (size_t)N * A * sizeof(float))) != cudaSuccess ||
+          (e = cudaMalloc(&det_n, (size_t)N * sizeof(int))) != cudaSuccess ||
+          (e = cudaMalloc(&det_keep, (size_t)N * max_det * sizeof(int))) != cudaSuccess ||
+          (e = cudaMalloc(&det_box, (size_t)N * max_det * 4 * sizeof(float))) != cudaSuccess ||
+          (e = cudaMalloc(&det_score, (size_t)N * max_det * sizeof(float))) != cudaSuccess ||
+          (e = cudaMalloc(&det_coef, (size_t)N * pad * 32 * sizeof(__half))) != cudaSuccess ||
+          (e = cudaMalloc(&det_masks, (size_t)N * max_det * mask_bytes)) != cudaSuccess) {
+        det_on = false;
+        return model_fail(OSAM_ERR_NOMEM, "detection buffers: %s", cudaGetErrorString(e));
+      }
+    }
+    det_conf = conf_th;
+    det_iou = iou_th;
+    det_max = max_det;
+    det_forced = forced ? 1 : 0;
+    det_packed = packed ? 1 : 0;
+    det_on = true;
+    return OSAM_OK;
   }
 
   int plan_gradient_modes() {
@@ -1149,28 +1275,13 @@ struct osam_model {
 
   int forward(int use_graph, cudaStream_t st) {
     if (!synced) return model_fail(OSAM_ERR_INVALID, "forward before osam_model_sync_weights");
-    cudaError_t e;
-    if (!use_graph) {
-      e = run(st);
-      return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
-    }
-    if ((e = plan_streams()) != cudaSuccess)  // streams and events exist before any capture begins
-      return model_fail(OSAM_ERR_CUDA, "forward streams: %s", cudaGetErrorString(e));
-    if (!exec) {
-      // Record on the model's own stream; recording does not execute, so no ordering with `st` is needed.
-      if (!cap && (e = cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking)) != cudaSuccess)
-        return model_fail(OSAM_ERR_CUDA, "capture stream: %s", cudaGetErrorString(e));
-      if ((e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
-        return model_fail(OSAM_ERR_CUDA, "begin capture: %s", cudaGetErrorString(e));
-      cudaError_t er = run(cap);
-      e = cudaStreamEndCapture(cap, &graph);
-      if (er != cudaSuccess || e != cudaSuccess)
-        return model_fail(OSAM_ERR_CUDA, "capture: %s", cudaGetErrorString(er != cudaSuccess ? er : e));
-      if ((e = cudaGraphInstantiate(&exec, graph, 0)) != cudaSuccess)
-        return model_fail(OSAM_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
-    }
-    e = cudaGraphLaunch(exec, st);
-    return e == cudaSuccess ? OSAM_OK : model_fail(OSAM_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e));
+    return step(fwd_sched, false, use_graph, st);
+  }
+
+  int forward_detect(int use_graph, cudaStream_t st) {
+    if (!synced) return model_fail(OSAM_ERR_INVALID, "forward before osam_model_sync_weights");
+    if (!det_on) return model_fail(OSAM_ERR_INVALID, "forward_detect before osam_model_detect_init");
+    return step(det_sched, true, use_graph, st);
   }
 };
 
@@ -1308,6 +1419,37 @@ int osam_model_forward(osam_model* m, int use_graph, osam_stream_t stream) {
 }
 
 int osam_model_num_launches(const osam_model* m) { return m ? (int)m->nodes.size() : 0; }
+
+int osam_model_detect_init(osam_model* m, float conf_th, float iou_th, int max_det, int forced, int packed) {
+  if (!m) return model_fail(OSAM_ERR_INVALID, "NULL model");
+  return m->detect_init(conf_th, iou_th, max_det, forced, packed);
+}
+
+int osam_model_forward_detect(osam_model* m, int use_graph, osam_stream_t stream) {
+  if (!m) return model_fail(OSAM_ERR_INVALID, "NULL model");
+  return m->forward_detect(use_graph, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int osam_model_detections(const osam_model* m, osam_detections* d) {
+  if (!m || !d) return model_fail(OSAM_ERR_INVALID, "NULL argument");
+  if (!m->det_on) return model_fail(OSAM_ERR_INVALID, "no detections before osam_model_detect_init");
+  d->batch = m->N;
+  d->anchors = m->head[0][0]->H * m->head[0][0]->W + m->head[0][1]->H * m->head[0][1]->W +
+               m->head[0][2]->H * m->head[0][2]->W;
+  d->max_det = m->det_max;
+  d->packed = m->det_packed;
+  d->proto_h = m->proto->H;
+  d->proto_w = m->proto->W;
+  d->xyxy = m->det_xyxy;
+  d->conf = m->det_confs;
+  d->n_det = m->det_n;
+  d->keep = m->det_keep;
+  d->box = m->det_box;
+  d->score = m->det_score;
+  d->coef_g = m->det_coef;
+  d->masks = m->det_masks;
+  return OSAM_OK;
+}
 
 int osam_model_forward_nodes(osam_model* m, int first, int count, osam_stream_t stream) {
   if (!m || first < 0 || count < 0 || first + count > (int)m->nodes.size())

@@ -99,6 +99,38 @@ class Model:
     def forward(self, use_graph: bool = False, stream=None) -> None:
         check(lib().osam_model_forward(self._m, int(use_graph), stream_ptr(stream)))
 
+    # ------------------------------------------------------------- the detect step (forward + post-process)
+    def detect_init(self, conf_th: float = 0.25, iou_th: float = 0.7, max_det: int = 300, forced: bool = False,
+                    packed: bool = True) -> None:
+        """Settings and output buffers of forward_detect (the post-process joins the forward's graph)."""
+        check(lib().osam_model_detect_init(self._m, float(conf_th), float(iou_th), int(max_det), int(forced),
+                                           int(packed)))
+
+    def forward_detect(self, use_graph: bool = True, stream=None) -> None:
+        """Forward + decode + NMS + masks as one step; decode and NMS overlap the proto branch."""
+        check(lib().osam_model_forward_detect(self._m, int(use_graph), stream_ptr(stream)))
+
+    def detections(self) -> dict:
+        """The detect step's outputs as torch views of the model's buffers: xyxy, conf, n_det, keep, box,
+        score, coef_g, masks (packed int32 words or u8), in the layouts of objectsam_b200.postproc."""
+        import torch
+        from ._lib import Detections
+        d = Detections()
+        check(lib().osam_model_detections(self._m, ctypes.byref(d)))
+        B, A, M = d.batch, d.anchors, d.max_det
+        pad = (M + 127) // 128 * 128
+        hw = d.proto_h * d.proto_w
+
+        def view(ptr, shape, typestr):
+            return torch.as_tensor(_DeviceArray(ptr, shape, self, typestr), device="cuda")
+        out = dict(xyxy=view(d.xyxy, (B, A, 4), "<f4"), conf=view(d.conf, (B, A), "<f4"),
+                   n_det=view(d.n_det, (B,), "<i4"), keep=view(d.keep, (B, M), "<i4"),
+                   box=view(d.box, (B, M, 4), "<f4"), score=view(d.score, (B, M), "<f4"),
+                   coef_g=view(d.coef_g, (B, pad, 32), "<f2"))
+        out["masks"] = view(d.masks, (B, M, (hw + 31) // 32), "<i4") if d.packed else \
+            view(d.masks, (B, M, d.proto_h, d.proto_w), "|u1")
+        return out
+
     @property
     def handle(self) -> int:
         return self._m.value

@@ -165,3 +165,34 @@ def test_nms_bit_exact_many_candidates(cuda_lib, kind, thr, max_det):
     np.testing.assert_array_equal(det["score"][0, :n].cpu().numpy(), conf[anchors])
     np.testing.assert_array_equal(det["box"][0, :n].cpu().numpy(), boxes[anchors])
     assert (det["keep"][0, n:] == -1).all()
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_detect_step_matches_separate_post_process(cuda_lib, use_graph):
+    """The detect step (forward + decode + NMS + masks in one schedule, the post-process overlapping the proto
+    branch) gives exactly the detections of the forward followed by the separate post-process launches."""
+    w = yolo_ref.calibrated_weights(4, 128)
+    B, S = 3, 192
+    imgs = yolo_params.make_images(B, S, 79)
+    m = Model(B, S)
+    m.load(w)
+    m.sync_weights()
+    m.input().copy_(torch.from_numpy(imgs).half())
+    m.forward()
+    ref = postproc.detect(m, conf_th=0.25, iou_th=0.7, max_det=300, packed=True)
+    torch.cuda.synchronize()
+    ref = {k: v.clone() for k, v in ref.items()}
+    m.detect_init(0.25, 0.7, 300, packed=True)
+    for _ in range(2):  # the graph is recorded at the first call and replayed at the second
+        m.forward_detect(use_graph=use_graph)
+    torch.cuda.synchronize()
+    got = m.detections()
+    assert int(ref["n_det"].sum()) > 0
+    for k in ("xyxy", "conf", "n_det", "keep", "box", "score", "masks"):
+        if k in ("keep", "box", "score", "masks"):
+            n = got["n_det"].cpu()
+            for b in range(B):
+                assert torch.equal(got[k][b, :n[b]].cpu(), ref[k][b, :n[b]].cpu()), f"{k} image {b}"
+        else:
+            assert torch.equal(got[k].cpu(), ref[k].cpu()), k
+    m.close()
