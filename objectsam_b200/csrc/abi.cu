@@ -1063,6 +1063,91 @@ int conv_wgrad_f32(const osam_conv_plan* p, const void* x, const void* dz, float
 
 extern "C" {
 
+// Window form of the weight gradient (conv_wgrad.cu, k_conv_wgrad_win): 3×3 / pad-1 convs with 32 or 64
+// input channels, stride 1 or 2 (even input sizes); returns the dz channels per CTA (GEMM N block), or 0
+// when the per-tap form runs.  OSAM_WGRAD_WIN=0 turns it off.
+static int wgrad_window_nb(const osam_conv_plan* p) {
+  const osam_conv_geom& g = p->g;
+  if (p->transposed || g.R != 3 || g.S != 3 || g.pad != 1 || (g.C != 32 && g.C != 64)) return 0;
+  if (!(p->mode == A_S1 && g.stride == 1) && !(p->mode == A_S2 && g.stride == 2 && g.H % 2 == 0 && g.W % 2 == 0))
+    return 0;
+  if (env_switch("OSAM_WGRAD_WIN") == 0) return 0;
+  for (int nb : {64, 32})
+    if (g.K % nb == 0 && wgrad_win_supported(g.C / 32, nb)) return nb;
+  return 0;
+}
+
+// 128-pixel tile of the stride-1 window form: th rows × ni images × tw columns with ni·tw ∈ {8, 16} (so a
+// row tap is a whole number of 512-byte swizzle atoms), the least padded work and halo.
+static void choose_wgrad_window_tile(int N, int P, int Q, int* tn, int* th, int* tw) {
+  double best = -1.0;
+  for (int rows : {8, 16})
+    for (int w = 16; w >= 2; w /= 2) {
+      if (w > rows || rows / w > N) continue;
+      const int n = rows / w, h = 128 / rows;
+      const double cost = (double)cdivll(Q, w) * cdivll(P, h) * cdivll(N, n) * (h + 2) / h;
+      if (best < 0 || cost < best - 1e-9) {
+        best = cost;
+        *tn = n;
+        *th = h;
+        *tw = w;
+      }
+    }
+}
+
+static int wgrad_window(const osam_conv_plan* p, const void* x, const void* dz, WgradLaunch& L, int NB,
+                        osam_stream_t stream) {
+  const osam_conv_geom& g = p->g;
+  ConvDev& d = L.d;
+  const bool s2 = g.stride == 2;
+  L.win = 1;
+  L.CB = g.C / 32;
+  L.NB = NB;
+  if (s2) {
+    d.tn = 1;
+    d.th = 16;
+    d.tw = 8;
+  } else {
+    choose_wgrad_window_tile(g.N, p->P, p->Q, &d.tn, &d.th, &d.tw);
+  }
+  d.tiles_q = (int)cdivll(p->Q, d.tw);
+  d.tiles_p = (int)cdivll(p->P, d.th);
+  const long long tiles = (long long)d.tiles_q * d.tiles_p * cdivll(g.N, d.tn);
+  if (tiles > 0x7fffffffLL) return fail(OSAM_ERR_UNSUPPORTED, "wgrad: too many tiles");
+  d.tiles_m = (int)tiles;
+  L.win_bytes = s2 ? 32 * 2 * 8 * 2 * 17 : 32 * 2 * d.tw * d.tn * (d.th + 2);
+  const int dz_ch = NB >= 64 ? 64 : 32;
+  int rc;
+  {  // dz as (K, Q, N, P): the tile's pixel rows run (row, image, column)
+    const uint64_t dims[4] = {(uint64_t)g.K, (uint64_t)p->Q, (uint64_t)g.N, (uint64_t)p->P};
+    const uint64_t str[3] = {(uint64_t)g.K * 2, (uint64_t)p->P * p->Q * g.K * 2, (uint64_t)p->Q * g.K * 2};
+    const uint32_t box[4] = {(uint32_t)dz_ch, (uint32_t)d.tw, (uint32_t)d.tn, (uint32_t)d.th};
+    rc = make_map(&L.tdz, dz, 4, dims, str, box, dz_ch * 2);
+  }
+  if (rc == OSAM_OK && !s2) {  // x as (C, W, N, H), a window of th + 2 rows
+    const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.N, (uint64_t)g.H};
+    const uint64_t str[3] = {(uint64_t)g.C * 2, (uint64_t)g.H * g.W * g.C * 2, (uint64_t)g.W * g.C * 2};
+    const uint32_t box[4] = {32u, (uint32_t)d.tw, (uint32_t)d.tn, (uint32_t)d.th + 2};
+    rc = make_map(&L.tx, x, 4, dims, str, box, 64);
+  } else if (rc == OSAM_OK) {  // the parity view (2C, W/2, 2, H/2, N), 17 row pairs × both parities × 8 columns
+    const uint64_t dims[5] = {(uint64_t)2 * g.C, (uint64_t)g.W / 2, 2, (uint64_t)g.H / 2, (uint64_t)g.N};
+    const uint64_t str[4] = {(uint64_t)4 * g.C, (uint64_t)g.W * g.C * 2, (uint64_t)2 * g.W * g.C * 2,
+                             (uint64_t)g.H * g.W * g.C * 2};
+    const uint32_t box[5] = {32u, 8u, 2u, 17u, 1u};
+    rc = make_map(&L.tx, x, 5, dims, str, box, 64);
+  }
+  if (rc) return rc;
+  // one CTA per SM: (GEMM N block, run of consecutive tiles)
+  const int nblk = g.K / NB;
+  long long nsplit = std::max(1, sm_count() / nblk);
+  if (nsplit > tiles) nsplit = tiles;
+  L.tiles_per_split = (int)cdivll(tiles, nsplit);
+  L.nsplit = (int)cdivll(tiles, L.tiles_per_split);
+  L.grid = nblk * L.nsplit;
+  cudaError_t e = launch_conv_wgrad(L, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSAM_OK : cuda_fail(e, "osam_conv_wgrad (window form) launch");
+}
+
 static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, void* dw, float* dw32, float beta,
                       void* ws, size_t ws_bytes, osam_stream_t stream, bool direct) {
   if (!p || !x || !dz || (!dw && !dw32)) return fail(OSAM_ERR_INVALID, "NULL plan or operand");
@@ -1110,6 +1195,7 @@ static int wgrad_impl(const osam_conv_plan* p, const void* x, const void* dz, vo
   L.dw32 = dw32;
   L.n_out = (long long)g.K * g.R * g.S * g.C;
   L.beta = beta;
+  if (int nbw = wgrad_window_nb(p)) return wgrad_window(p, x, dz, L, nbw, stream);
   int rc = OSAM_OK;
   {
     const uint64_t dims[4] = {(uint64_t)g.K, (uint64_t)p->Q, (uint64_t)p->P, (uint64_t)g.N};

@@ -137,8 +137,15 @@ struct WgradLaunch {
   int mode;             // A_S1, A_S2, or A_STEM (R·S·C ≤ 32: patch gather, dz as one 2-D map)
   const __half* xp;     // A_STEM: the input itself (gathered by the producer warps, no tensor map)
   int grid, nsplit, tiles_per_split;
+  // window form (3×3, pad 1, C = 32·CB ∈ {32, 64}): per tile one dz box and, per column tap, one x window per
+  // 32-channel block, the three row taps stacked in the GEMM M dimension (d.th/tw/tn/tiles_* = its tiling)
+  int win;              // 0 = per-tap form; 1 = window form
+  int CB, NB;           // 32-channel blocks of x; dz channels (GEMM N) per CTA
+  int win_bytes;        // bytes of one x window box
 };
 cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st);
+// the (x channel blocks, dz channels per CTA) pairs the window form of the weight gradient is built for
+bool wgrad_win_supported(int CB, int NB);
 // 1×1 conv with one output channel: dx = dy ⊗ w (+ beta·dx); dw = Σ dy·x (fp32 acc[C] scratch, + beta·dw)
 cudaError_t launch_dgrad_k1(const __half* dy, const __half* w, __half* dx, long long npix, int C, float beta,
                             cudaStream_t st);

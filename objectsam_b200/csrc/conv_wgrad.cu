@@ -342,6 +342,217 @@ __global__ void __launch_bounds__(StemWgCfg<K>::THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------------
+// Window form for 3×3 / pad-1 convs with 32 or 64 input channels (the narrow C2f bottlenecks, the narrow
+// head branches and the first stride-2 convs).  Per-tap CTAs reload a tile's dz and its shifted x box
+// nine times and, with K = 32 output channels, fill a quarter of the M = 128 accumulator.  Here the nine
+// taps of a 128-pixel tile come from a few boxes, both GEMM operands MN-major:
+//  * row taps stacked in M: the x window (the tile's rows plus the row halo, 64-byte rows of 32 channels)
+//    has its pixel rows in the tile's (row, image, column) order, so row tap r starts r·ni·tw rows further
+//    on — a constant distance, which is the descriptor's M-block stride: the four 32-row M blocks of one
+//    M = 128 MMA are the row taps 0, 1, 2 and a discarded block;
+//  * column taps stacked in N: with the reduction re-indexed by the column shift (pixel q' = q + s − 1),
+//    tap s pairs the UNSHIFTED x window with dz shifted by 1 − s columns,
+//      dW[k][r][s][c] = Σ_{n,p,q'} x[n][p + r − 1][q'][c] · dz[n][p][q' + 1 − s][k],
+//    every (q, s) term counted once over the tiles of q', with the TMA zero fill outside dz; the three
+//    shifted dz boxes sit one box apart, the descriptor's N-block stride, so one MMA has N = 3·NB.
+// Stride 2 (parity view of x: the two row parities of a row pair side by side, output row i of row tap r
+// at window row 16·i + 8·(r + 1)): column tap 1 reads the even columns (window of parity 0, dz unshifted);
+// taps 2 and 0 read the odd columns (window of parity 1) with dz unshifted and shifted by one column,
+// so per 32-channel block one MMA of N = NB and one of N = 2·NB.
+// One CTA takes a run of tiles and accumulates in TMEM (3·NB columns per channel block) for the whole run;
+// at the end the warps on TMEM quadrants 0–2 (= row taps) add the accumulators into the fp32 KRSC
+// workspace with coalesced atomics (lane = input channel).  Rings: dz stages and x window slots, each
+// released by its own MMA commit.  Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer.  No multicast;
+// every wait is bounded.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw64(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (saddr & 0x3FFFFu) >> 4;
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;  // LBO: next 32-element M block (here: the next row tap)
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;  // SBO: next 8 reduction rows
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(4) << 61;                     // 64-byte swizzle
+  return d;
+}
+
+template <int CB, int NB, bool S2>
+struct WgWinCfg {
+  static constexpr int DZ_ROWB = NB * 2;             // one dz box per column shift: 64- or 128-byte rows
+  static constexpr int DZ_BOX = 128 * DZ_ROWB;
+  static constexpr int NDZ = S2 ? 2 : 3;             // dz boxes per tile (column shifts)
+  static constexpr int DZ_BYTES = NDZ * DZ_BOX;
+  static constexpr int DSTAGES = DZ_BYTES <= 32 * 1024 ? 4 : 2;
+  static constexpr int NWIN = CB * (S2 ? 2 : 1);     // x windows per tile
+  // window rows read, the discarded fourth M block included: stride 1 128 + 3·ni·tw (ni·tw ≤ 16);
+  // stride 2 32·7 + 24 + 3·8 + 8 = 280
+  static constexpr int WIN_ROWS = S2 ? 280 : 128 + 3 * 16;
+  static constexpr int WIN_BYTES = (WIN_ROWS * 64 + 1023) & ~1023;
+  static constexpr int WST_RAW = (210 * 1024 - DSTAGES * DZ_BYTES) / WIN_BYTES;
+  static constexpr int WSTAGES = WST_RAW > 4 * NWIN ? 4 * NWIN : WST_RAW;
+  static constexpr int ACC_COLS = 3 * CB * NB;
+  static constexpr int TMEM_COLS = ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
+                                 : ACC_COLS <= 256 ? 256 : 512;
+  static constexpr int THREADS = 192;
+  static constexpr int BAR_BYTES = ((2 * DSTAGES + 2 * WSTAGES + 1) * 8 + 4 + 15) & ~15;  // barriers + TMEM slot
+  static constexpr int SMEM_BYTES = 1024 + DSTAGES * DZ_BYTES + WSTAGES * WIN_BYTES + BAR_BYTES;
+  static_assert(NB == 32 || NB == 64, "dz block: one 32- or 64-channel box per column shift");
+  static_assert(ACC_COLS <= 512, "accumulators must fit in TMEM");
+  static_assert(WSTAGES >= 2, "window ring too small");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert((228 * 1024 / (SMEM_BYTES + 1024)) * TMEM_COLS <= 512, "co-resident CTAs must fit in TMEM");
+};
+
+template <int CB, int NB, bool S2>
+__global__ void __launch_bounds__(192, 1)
+    k_conv_wgrad_win(const __grid_constant__ CUtensorMap tdz, const __grid_constant__ CUtensorMap tx, const ConvDev d,
+                     float* __restrict__ acc, int nblk, int tiles_per_split, int win_bytes) {
+  using Cfg = WgWinCfg<CB, NB, S2>;
+  constexpr int DST = Cfg::DSTAGES, WST = Cfg::WSTAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* dzb = base;
+  uint8_t* wnb = base + DST * Cfg::DZ_BYTES;
+  uint64_t* dfull = reinterpret_cast<uint64_t*>(wnb + WST * Cfg::WIN_BYTES);
+  uint64_t* dempty = dfull + DST;
+  uint64_t* wfull = dempty + DST;
+  uint64_t* wempty = wfull + WST;
+  uint64_t* accf = wempty + WST;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = blockIdx.x % nblk, split = blockIdx.x / nblk;
+  const int t0 = split * tiles_per_split, t1 = min(d.tiles_m, t0 + tiles_per_split);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < DST; s++) {
+      mbar_init(dfull + s, 1);
+      mbar_init(dempty + s, 1);
+    }
+    for (int s = 0; s < WST; s++) {
+      mbar_init(wfull + s, 1);
+      mbar_init(wempty + s, 1);
+    }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tdz);
+    tma_prefetch_desc(&tx);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t wit = 0;
+      bool ok = true;
+      for (int t = t0, it = 0; t < t1 && ok; t++, it++) {
+        const int tq = t % d.tiles_q, rest = t / d.tiles_q;
+        const int tp = rest % d.tiles_p, tn = rest / d.tiles_p;
+        const int q0 = tq * d.tw, p0 = tp * d.th, n0 = tn * d.tn;
+        const int ds = it % DST;
+        if (it >= DST && !mbar_wait(dempty + ds, ((it / DST) - 1) & 1, d.err)) break;
+        mbar_arrive_expect_tx(dfull + ds, Cfg::DZ_BYTES);
+        // dz boxes: stride 1 shifted by 1 − s for s = 0, 1, 2; stride 2 unshifted and shifted by one column
+#pragma unroll
+        for (int j = 0; j < Cfg::NDZ; j++)
+          tma_load_4d(dzb + ds * Cfg::DZ_BYTES + j * Cfg::DZ_BOX, &tdz, dfull + ds, nb * NB, S2 ? q0 + j : q0 + 1 - j,
+                      n0, p0);
+        for (int w = 0; w < Cfg::NWIN; w++, wit++) {
+          const int ws = wit % WST;
+          if (wit >= WST && !mbar_wait(wempty + ws, ((wit / WST) - 1) & 1, d.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(wfull + ws, win_bytes);
+          uint8_t* dst = wnb + ws * Cfg::WIN_BYTES;
+          if (!S2) {
+            tma_load_4d(dst, &tx, wfull + ws, w * 32, q0, n0, p0 - 1);
+          } else {  // w = 2·cb + column parity
+            tma_load_5d(dst, &tx, wfull + ws, (w & 1) * d.C + (w >> 1) * 32, q0, 0, p0 - 1, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t a_lbo = S2 ? 8 * 64 : (uint32_t)(d.tn * d.tw * 64);  // row-tap distance in the window
+      const uint32_t a_sbo = S2 ? 16 * 64 : 8 * 64;                        // next 8 tile pixels
+      uint32_t wit = 0;
+      bool ok = true;
+      for (int t = t0, it = 0; t < t1 && ok; t++, it++) {
+        const int ds = it % DST;
+        if (!mbar_wait(dfull + ds, (it / DST) & 1, d.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t bz = smem_u32(dzb + ds * Cfg::DZ_BYTES);
+        for (int w = 0; w < Cfg::NWIN; w++, wit++) {
+          const int ws = wit % WST;
+          if (!mbar_wait(wfull + ws, (wit / WST) & 1, d.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(wnb + ws * Cfg::WIN_BYTES);
+          // accumulator slots per channel block: stride 1 (s = 0, 1, 2); stride 2 (s = 1 | s = 2, s = 0)
+          const int cb = S2 ? (w >> 1) : w;
+          const int slot = S2 ? (w & 1) : 0;
+          const uint32_t dcol = tmem + (uint32_t)((cb * 3 + slot) * NB);
+          const uint32_t idesc = S2 ? ((w & 1) ? idesc_f16_f32_mn(128, 2 * NB) : idesc_f16_f32_mn(128, NB))
+                                    : idesc_f16_f32_mn(128, 3 * NB);
+#pragma unroll
+          for (int kk = 0; kk < 8; kk++) {  // 16 tile pixels (reduction rows) per MMA
+            const uint32_t arow = S2 ? (uint32_t)(32 * kk + 8) : (uint32_t)(16 * kk);
+            umma_f16(dcol, smem_desc_mn_sw64(a + arow * 64, a_lbo, a_sbo),
+                     smem_desc_mnmajor(bz + kk * 16 * Cfg::DZ_ROWB, Cfg::DZ_ROWB, Cfg::DZ_BOX), idesc,
+                     (it | kk) != 0);
+          }
+          umma_commit(wempty + ws);
+        }
+        if (ok) umma_commit(dempty + ds);
+      }
+      if (ok && t1 > t0) umma_commit(accf);
+    }
+  } else {
+    // ---------------------------------------------------------------- read-out: quadrant = row tap
+    const int r = warp & 3;  // warps 2–5 → TMEM lane quadrants 2, 3, 0, 1; quadrant 3 (warp 3) is discarded
+    const bool ok = t1 > t0 && mbar_wait(accf, 0, d.err);
+    tc_fence_after();
+    if (ok && r < 3) {
+      const uint32_t lrow = tmem + ((uint32_t)(r * 32) << 16);
+      const long long kstride = 9LL * d.C;
+#pragma unroll 1
+      for (int cb = 0; cb < CB; cb++)
+#pragma unroll 1
+        for (int slot = 0; slot < 3; slot++) {
+          const int s = S2 ? (slot + 1) % 3 : slot;
+          float* dst = acc + ((long long)nb * NB * 9 + r * 3 + s) * d.C + cb * 32 + lane;
+#pragma unroll 1
+          for (int n0 = 0; n0 < NB; n0 += 16) {
+            __syncwarp();
+            float v[16];
+            tmem_ld16(lrow + (uint32_t)((cb * 3 + slot) * NB + n0), v);
+#pragma unroll
+            for (int i = 0; i < 16; i++) atomicAdd(dst + (n0 + i) * kstride, v[i]);
+          }
+        }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
 // dw (fp16) = acc (fp32) + beta · dw, or dw32 (fp32) = acc + beta · dw32
 __global__ void k_wgrad_finish(const float* __restrict__ acc, __half* __restrict__ dw, float* __restrict__ dw32,
                                long long n, float beta) {
@@ -438,11 +649,42 @@ static cudaError_t wgrad_stem_launch(const WgradLaunch& L, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+template <int CB, int NB, bool S2>
+static cudaError_t wgrad_win_launch(const WgradLaunch& L, cudaStream_t st) {
+  using Cfg = WgWinCfg<CB, NB, S2>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv_wgrad_win<CB, NB, S2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  k_conv_wgrad_win<CB, NB, S2><<<L.grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(L.tdz, L.tx, L.d, L.acc, L.nsplit ? L.grid / L.nsplit : 1,
+                                                                             L.tiles_per_split, L.win_bytes);
+  return cudaGetLastError();
+}
+
+template <bool S2>
+static cudaError_t wgrad_win_dispatch(const WgradLaunch& L, cudaStream_t st) {
+  if (L.CB == 1) {
+    if (L.NB == 32) return wgrad_win_launch<1, 32, S2>(L, st);
+    if (L.NB == 64) return wgrad_win_launch<1, 64, S2>(L, st);
+  } else if (L.CB == 2) {
+    if (L.NB == 32) return wgrad_win_launch<2, 32, S2>(L, st);
+    if (L.NB == 64) return wgrad_win_launch<2, 64, S2>(L, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+bool wgrad_win_supported(int CB, int NB) { return (CB == 1 || CB == 2) && (NB == 32 || NB == 64); }
+
 cudaError_t launch_conv_wgrad(const WgradLaunch& L, cudaStream_t st) {
   cudaError_t e = L.direct ? cudaSuccess : cudaMemsetAsync(L.acc, 0, (size_t)L.n_out * 4, st);
   if (e != cudaSuccess) return e;
   const int AB = L.AB, BB = L.BB, BN = L.BN;
-  if (L.mode == A_STEM) {
+  if (L.win) {
+    e = L.mode == A_S2 ? wgrad_win_dispatch<true>(L, st) : wgrad_win_dispatch<false>(L, st);
+  } else if (L.mode == A_STEM) {
     if (L.d.K == 32) e = wgrad_stem_launch<32>(L, st);
     else if (L.d.K == 64) e = wgrad_stem_launch<64>(L, st);
     else return cudaErrorInvalidValue;

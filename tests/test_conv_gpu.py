@@ -9,6 +9,7 @@ import torch
 import torch.nn.functional as F
 
 from objectsam_b200.conv import EPI_BIAS, EPI_BN_ACT, ConvGeom, ConvOp, DestSpec, sppf_pool_bwd, sppf_pool_fwd
+from objectsam_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -551,3 +552,32 @@ def test_conv_wgrad_beta_accumulates(cuda_lib):
     op.wgrad(x, dz, dw, ws=ws, beta=1.0)
     torch.cuda.synchronize()
     assert_close(dw, ref_wgrad(x, dz, (K, 3, 3, C), 1, 1) + dw0.float())
+
+
+# window form of the weight gradient (3×3, pad 1, C ∈ {32, 64}; stride 1, or 2 on even sizes): both channel
+# blocks, every dz block width (32, 64, 128 — and K split over two CTAs), ragged tiles, odd batches, runs of
+# many tiles per CTA; the per-tap form (OSAM_WGRAD_WIN=0) on the same inputs must agree too
+WGRAD_WIN_SHAPES = [(2, 20, 20, 32, 32, 1), (3, 40, 24, 64, 64, 1), (1, 13, 11, 32, 128, 1), (2, 17, 9, 64, 32, 1),
+                    (2, 32, 32, 32, 64, 2), (3, 24, 40, 64, 128, 2), (1, 18, 14, 32, 32, 2), (4, 160, 160, 32, 32, 1),
+                    (2, 320, 320, 32, 64, 2), (5, 80, 80, 64, 64, 1)]
+
+
+@pytest.mark.parametrize("shape", WGRAD_WIN_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_conv_wgrad_window_form_matches_torch(cuda_lib, monkeypatch, shape, beta):
+    N, H, W, C, K, s = shape
+    x, _ = rand_conv(N, H, W, C, K, 3, seed=sum(shape) + 21)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, s, 1))
+    P, Q = op.geom().P(), op.geom().Q()
+    g = torch.Generator(device="cpu").manual_seed(15)
+    dz = (torch.rand(N, P, Q, K, generator=g) * 2 - 1).half().to(DEV)
+    dw0 = (torch.rand(K, 3, 3, C, generator=g) - 0.5).half().to(DEV)
+    ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
+    ref = ref_wgrad(x, dz, (K, 3, 3, C), s, 1) + beta * dw0.float()
+    for form in ("1", "0"):  # window form, then the per-tap form
+        monkeypatch.setenv("OSAM_WGRAD_WIN", form)
+        dw = dw0.clone()
+        op.wgrad(x, dz, dw, ws=ws, beta=beta)
+        torch.cuda.synchronize()
+        assert_close(dw, ref)
+    assert _lib.device_error() == 0
