@@ -152,7 +152,8 @@ int osam_sppf_bwd(const void* cat, void* dcat, int N, int H, int W, int c, osam_
  * src/misc.cuh:13-17).  z, residuals and gradients are NHWC fp16 [N·H·W][C] with C a multiple of 8,
  * C ≤ 2048; per-channel vectors are fp32.  Statistics reduce in fp32 per thread and CTA, then fp64.
  * Workspaces: osam_bn_workspace_size(C) / osam_chan_sum_workspace_size(C) bytes, 16-byte aligned, ZERO-FILLED
- * ONCE before first use (the reference's bn_init, src/bn.cuh:28); every call leaves it zeroed again.  One
+ * ONCE before first use (the reference's bn_init, src/bn.cuh:28); every call leaves its accumulators zeroed
+ * again (osam_bn_backward keeps its per-channel means in the scratch behind them, rewritten each call).  One
  * workspace serves calls issued in order on one stream; calls that may overlap need their own.
  * ------------------------------------------------------------------------------------------------ */
 size_t osam_bn_workspace_size(int C);
@@ -174,6 +175,14 @@ int osam_bn_forward_stats(const void* z, int N, int H, int W, int C, const float
  * (src/bn.cuh:42-44, src/bn.cu:204-238, :324-327). */
 int osam_bn_forward_apply(const void* z, int N, int H, int W, int C, const float* scale, const float* shift,
                           const void* res, const osam_dest* dests, int n_dest, int act, osam_stream_t stream);
+
+/* osam_bn_forward_stats followed by osam_bn_forward_apply with that scale/shift, in one call (the pair the
+ * reference's forward(true) runs for every conv, src/model.cpp:389-400).  Same outputs, arguments and
+ * workspace as the two calls. */
+int osam_bn_forward_train(const void* z, int N, int H, int W, int C, const float* gamma, const float* beta,
+                          float* run_mean, float* run_var, float momentum, float eps, float* mean, float* istd,
+                          float* scale, float* shift, const void* res, const osam_dest* dests, int n_dest, int act,
+                          void* ws, size_t ws_bytes, osam_stream_t stream);
 
 /* Backward of osam_bn_forward_apply ∘ stats.  grad_dests[i].p is the GRADIENT buffer of forward
  * destination i (same ctot/choff/c0/c1/up); dA = their sum (2×2 sum for up = 2).  g = dA·silu'(y) (act),

@@ -76,6 +76,9 @@ _SIGS = {
                                       c_void_p]),
     "osam_bn_forward_apply": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                       POINTER(Dest), c_int, c_int, c_void_p]),
+    "osam_bn_forward_train": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_float, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, POINTER(Dest),
+                                      c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "osam_bn_backward": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                  POINTER(Dest), c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
                                  c_void_p, c_size_t, c_void_p]),

@@ -90,6 +90,22 @@ def bn_forward_apply(z, scale, shift, res, dests: Sequence[DestSpec], act: bool 
                                       len(dests), int(act), stream_ptr(stream)))
 
 
+def bn_forward_train(z, gamma, beta, run_mean, run_var, momentum, eps, mean, istd, scale, shift, res,
+                     dests: Sequence[DestSpec], act: bool = True, ws=None, stream=None) -> None:
+    """bn_forward_stats then bn_forward_apply in one call (the pair the reference's forward(true) runs per
+    conv, src/model.cpp:389-400): same outputs and workspace as the two calls."""
+    N, H, W, C = _nhwc(z)
+    if res is not None:
+        assert res.shape == z.shape and res.dtype == torch.float16 and res.is_contiguous()
+    ws = ws if ws is not None else workspace(C, z.device, stream)
+    d = _dests(dests, C)
+    check(lib().osam_bn_forward_train(z.data_ptr(), N, H, W, C, gamma.data_ptr(), beta.data_ptr(),
+                                      run_mean.data_ptr(), run_var.data_ptr(), float(momentum), float(eps),
+                                      mean.data_ptr(), istd.data_ptr(), scale.data_ptr(), shift.data_ptr(), _p(res),
+                                      d, len(dests), int(act), ws.data_ptr(), ws.numel() * ws.element_size(),
+                                      stream_ptr(stream)))
+
+
 def bn_backward(z, mean, istd, scale, shift, grad_dests: Sequence[DestSpec], act: bool, dz, gw_gamma, gw_beta,
                 accum: bool = False, res_grad=None, res_accum: bool = False, ws=None, stream=None) -> None:
     """dz, dγ, dβ (and the residual's gradient) of BN+SiLU (reference bn_backward, src/bn.cu:329-344)."""

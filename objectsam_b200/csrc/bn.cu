@@ -96,6 +96,15 @@ __device__ __forceinline__ void ld8f_any(const float* p, float (&o)[8]) {
 
 enum RedMode : int { RED_STATS = 0, RED_BWD = 1, RED_SUM = 2 };
 
+// Programmatic dependent launch: the BN passes are launched with the programmatic-serialization attribute,
+// so their CTAs are scheduled while the previous kernel of the stream drains; every thread waits for that
+// kernel (and so for all earlier work) before its first global access, then lets the next kernel of the
+// stream be scheduled in turn (it waits for this one the same way before touching memory).
+__device__ __forceinline__ void bn_pdl_entry() {
+  grid_dep_wait();
+  grid_dep_launch();
+}
+
 // The rows a pass walks: z as [M][C] (W = the map's width, for upsampled destinations); each CTA owns
 // `chunk` consecutive rows and processes `lanes` of them side by side (kBnT / (C/8) threads per row).
 struct Rows {
@@ -151,76 +160,84 @@ struct RedArgs {
 //   RED_BWD:   Σg, Σg·x̂ with g = dA·silu'(y), y = scale·z + shift, x̂ = (z − mean)·istd
 //   RED_SUM:   Σz
 // SIMPLE (RED_BWD): one destination, not upsampled, all channels — dA is one 16-byte load per row, kept raw.
-template <int MODE, int U, bool SIMPLE = false>
-__global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(const RedArgs P) {
-  extern __shared__ float2 bn_red[];  // [rowlanes][C]
-  __shared__ unsigned s_last;
+// The thread's per-channel constants: RED_STATS k0 = K; RED_BWD k0 = scale, k1 = shift, k2 = istd,
+// k3 = −mean·istd (x̂ = z·k2 + k3).
+template <int MODE>
+__device__ __forceinline__ void red_consts(const RedArgs& P, int c, float (&k0)[8], float (&k1)[8], float (&k2)[8],
+                                           float (&k3)[8]) {
+  if (MODE == RED_STATS) ld8f_any(P.st.run_mean + c, k0);
+  if (MODE == RED_BWD) {
+    float mu[8];
+    ld8f_any(P.bw.scale + c, k0);
+    ld8f_any(P.bw.shift + c, k1);
+    ld8f_any(P.bw.istd + c, k2);
+    ld8f_any(P.bw.mean + c, mu);
+#pragma unroll
+    for (int i = 0; i < 8; i++) k3[i] = -mu[i] * k2[i];
+  }
+}
+
+// The thread's partial sums (a, b) over rows r0 + rl, r0 + rl + RL, … of its CTA's chunk [r0, r1).
+template <int MODE, int U, bool SIMPLE>
+__device__ __forceinline__ void red_rows(const RedArgs& P, long long r0, long long r1, int rl, int c,
+                                         const float (&k0)[8], const float (&k1)[8], const float (&k2)[8],
+                                         const float (&k3)[8], float (&a)[8], float (&b)[8]) {
   const Rows R = P.rows;
-  const int C = R.C, V = C >> 3, RL = R.lanes;
-  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
-  const bool active = rl < RL;
-  const long long r0 = (long long)blockIdx.x * R.chunk;
-  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
-  float a[8], b[8];
+  const int C = R.C, RL = R.lanes;
 #pragma unroll
   for (int i = 0; i < 8; i++) a[i] = b[i] = 0.f;
-  if (active) {
-    // RED_STATS: k0 = K.  RED_BWD: k0 = scale, k1 = shift, k2 = istd, k3 = −mean·istd (x̂ = z·k2 + k3).
-    float k0[8], k1[8], k2[8], k3[8];
-    if (MODE == RED_STATS) ld8f_any(P.st.run_mean + c, k0);
-    if (MODE == RED_BWD) {
-      float mu[8];
-      ld8f_any(P.bw.scale + c, k0);
-      ld8f_any(P.bw.shift + c, k1);
-      ld8f_any(P.bw.istd + c, k2);
-      ld8f_any(P.bw.mean + c, mu);
+  for (long long r = r0 + rl; r < r1; r += (long long)U * RL) {
+    uint4 zr[U], gr[SIMPLE ? U : 1];
+    float dA[SIMPLE ? 1 : U][8];
 #pragma unroll
-      for (int i = 0; i < 8; i++) k3[i] = -mu[i] * k2[i];
+    for (int u = 0; u < U; u++) {
+      const long long rr = r + (long long)u * RL;
+      if (rr < r1) {
+        zr[u] = *reinterpret_cast<const uint4*>(R.z + rr * C + c);
+        if (SIMPLE) gr[u] = *reinterpret_cast<const uint4*>(P.bw.src[0].g + rr * P.bw.src[0].ctot + c);
+      }
     }
-    for (long long r = r0 + rl; r < r1; r += (long long)U * RL) {
-      uint4 zr[U], gr[SIMPLE ? U : 1];
-      float dA[SIMPLE ? 1 : U][8];
+    if (MODE == RED_BWD && !SIMPLE) {
 #pragma unroll
       for (int u = 0; u < U; u++) {
         const long long rr = r + (long long)u * RL;
-        if (rr < r1) {
-          zr[u] = *reinterpret_cast<const uint4*>(R.z + rr * C + c);
-          if (SIMPLE) gr[u] = *reinterpret_cast<const uint4*>(P.bw.src[0].g + rr * P.bw.src[0].ctot + c);
-        }
+        if (rr < r1) dest_grad_sum8(P.bw.src, P.bw.nsrc, rr, c, R.W, dA[SIMPLE ? 0 : u]);
       }
-      if (MODE == RED_BWD && !SIMPLE) {
+    }
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-          const long long rr = r + (long long)u * RL;
-          if (rr < r1) dest_grad_sum8(P.bw.src, P.bw.nsrc, rr, c, R.W, dA[SIMPLE ? 0 : u]);
-        }
-      }
+    for (int u = 0; u < U; u++) {
+      if (r + (long long)u * RL >= r1) break;
+      float v[8];
+      unpack8h(zr[u], v);
+      if (SIMPLE) unpack8h(gr[u], dA[0]);
 #pragma unroll
-      for (int u = 0; u < U; u++) {
-        if (r + (long long)u * RL >= r1) break;
-        float v[8];
-        unpack8h(zr[u], v);
-        if (SIMPLE) unpack8h(gr[u], dA[0]);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          if (MODE == RED_STATS) {
-            const float d = v[i] - k0[i];
-            a[i] += d;
-            b[i] = fmaf(d, d, b[i]);
-          } else if (MODE == RED_BWD) {
-            float g = dA[SIMPLE ? 0 : u][i];
-            if (P.bw.silu) {
-              const float y = fmaf(k0[i], v[i], k1[i]), s = sigmoid_fast(y);
-              g *= s * fmaf(y, 1.f - s, 1.f);
-            }
-            a[i] += g;
-            b[i] = fmaf(g, fmaf(v[i], k2[i], k3[i]), b[i]);
-          } else {
-            a[i] += v[i];
+      for (int i = 0; i < 8; i++) {
+        if (MODE == RED_STATS) {
+          const float d = v[i] - k0[i];
+          a[i] += d;
+          b[i] = fmaf(d, d, b[i]);
+        } else if (MODE == RED_BWD) {
+          float g = dA[SIMPLE ? 0 : u][i];
+          if (P.bw.silu) {
+            const float y = fmaf(k0[i], v[i], k1[i]), s = sigmoid_fast(y);
+            g *= s * fmaf(y, 1.f - s, 1.f);
           }
+          a[i] += g;
+          b[i] = fmaf(g, fmaf(v[i], k2[i], k3[i]), b[i]);
+        } else {
+          a[i] += v[i];
         }
       }
     }
+  }
+}
+
+// The CTA's sums of (a, b) per channel (shared memory, [row lanes][C]) added into the fp64 accumulators.
+template <int MODE>
+__device__ __forceinline__ void red_flush(const RedArgs& P, float2* bn_red, int rl, int c, bool active,
+                                          const float (&a)[8], const float (&b)[8]) {
+  const int C = P.rows.C, RL = P.rows.lanes;
+  if (active) {
 #pragma unroll
     for (int i = 0; i < 8; i++) bn_red[rl * C + c + i] = make_float2(a[i], b[i]);
   }
@@ -235,6 +252,56 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
     atomicAdd(&P.red.acc[ch], double(sa));
     if (MODE != RED_SUM) atomicAdd(&P.red.acc[C + ch], double(sb));
   }
+}
+
+// Batch statistics of one channel from its shifted sums: mean = K + E[z−K]; biased variance
+// E[(z−K)²] − E[z−K]² (clamped at 0) for normalising; the running variance takes the unbiased M/(M−1)
+// form (reference src/bn.cu:176-191).
+struct ChanStats {
+  float mean, istd, var, scale, shift;
+};
+__device__ __forceinline__ ChanStats stats_from_sums(double sx, double sy, double Md, float K, float gamma,
+                                                     float beta, float eps) {
+  ChanStats s;
+  const float dm = float(sx / Md);
+  float var = float(sy / Md - double(dm) * double(dm));
+  var = var < 0.f ? 0.f : var;
+  s.var = var;
+  s.mean = K + dm;
+  s.istd = rsqrtf(var + eps);
+  s.scale = gamma * s.istd;
+  s.shift = beta - s.mean * s.scale;
+  return s;
+}
+__device__ __forceinline__ void stats_store(const StatsIO& S, int ch, float K, const ChanStats& s, double Md) {
+  S.mean[ch] = s.mean;
+  S.istd[ch] = s.istd;
+  S.scale[ch] = s.scale;
+  S.shift[ch] = s.shift;
+  if (S.momentum > 0.f) {
+    S.run_mean[ch] = (1.f - S.momentum) * K + S.momentum * s.mean;
+    S.run_var[ch] = (1.f - S.momentum) * S.run_var[ch] + S.momentum * float(double(s.var) * Md / (Md - 1.0));
+  }
+}
+
+template <int MODE, int U, bool SIMPLE = false>
+__global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(const RedArgs P) {
+  extern __shared__ float2 bn_red[];  // [rowlanes][C]
+  __shared__ unsigned s_last;
+  bn_pdl_entry();
+  const Rows R = P.rows;
+  const int C = R.C, V = C >> 3, RL = R.lanes;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  const bool active = rl < RL;
+  const long long r0 = (long long)blockIdx.x * R.chunk;
+  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
+  float a[8], b[8];
+  if (active) {
+    float k0[8], k1[8], k2[8], k3[8];
+    red_consts<MODE>(P, c, k0, k1, k2, k3);
+    red_rows<MODE, U, SIMPLE>(P, r0, r1, rl, c, k0, k1, k2, k3, a, b);
+  }
+  red_flush<MODE>(P, bn_red, rl, c, active, a, b);
   // The last CTA to arrive finalises (threadfence reduction: every CTA's atomics are visible before its
   // arrival on the counter).
   __threadfence();
@@ -250,23 +317,9 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
     P.red.acc[ch] = 0.0;
     if (MODE != RED_SUM) P.red.acc[C + ch] = 0.0;
     if (MODE == RED_STATS) {
-      // mean = K + E[z−K]; biased variance E[(z−K)²] − E[z−K]² (clamped at 0) for normalising; the
-      // running variance takes the unbiased M/(M−1) form (reference src/bn.cu:176-191).
       const StatsIO S = P.st;
       const float K = S.run_mean[ch];
-      const float dm = float(sx / Md);
-      float var = float(sy / Md - double(dm) * double(dm));
-      var = var < 0.f ? 0.f : var;
-      const float m = K + dm, is = rsqrtf(var + S.eps);
-      S.mean[ch] = m;
-      S.istd[ch] = is;
-      const float sc = S.gamma[ch] * is;
-      S.scale[ch] = sc;
-      S.shift[ch] = S.beta[ch] - m * sc;
-      if (S.momentum > 0.f) {
-        S.run_mean[ch] = (1.f - S.momentum) * K + S.momentum * m;
-        S.run_var[ch] = (1.f - S.momentum) * S.run_var[ch] + S.momentum * float(double(var) * Md / (Md - 1.0));
-      }
+      stats_store(S, ch, K, stats_from_sums(sx, sy, Md, K, S.gamma[ch], S.beta[ch], S.eps), Md);
     } else if (MODE == RED_BWD) {
       const BwdIO G = P.bw;
       G.gmean[ch] = float(sx / Md);
@@ -289,18 +342,13 @@ struct ApplyArgs {
   int ndest, silu;
 };
 
-// a = act(scale·z + shift) (+ res) → every destination (reference k_apply, src/bn.cu:204-238).
+// a = act(scale·z + shift) (+ res) → every destination, for the thread's rows of [r0, r1), walked from
+// the chunk's end (reference k_apply, src/bn.cu:204-238).
 template <int U>
-__global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
+__device__ __forceinline__ void apply_rows(const ApplyArgs& P, long long r0, long long r1, int rl, int c,
+                                           const float (&sc)[8], const float (&sh)[8]) {
   const Rows R = P.rows;
-  const int C = R.C, V = C >> 3, RL = R.lanes;
-  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
-  if (rl >= RL) return;
-  const long long r0 = (long long)blockIdx.x * R.chunk;
-  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
-  float sc[8], sh[8];
-  ld8f_any(P.scale + c, sc);
-  ld8f_any(P.shift + c, sh);
+  const int C = R.C, RL = R.lanes;
   for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
     uint4 zr[U], rr4[U];
 #pragma unroll
@@ -344,6 +392,21 @@ __global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
   }
 }
 
+template <int U>
+__global__ void __launch_bounds__(kBnT, 3) k_bn_apply(const ApplyArgs P) {
+  bn_pdl_entry();
+  const Rows R = P.rows;
+  const int V = R.C >> 3;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  if (rl >= R.lanes) return;
+  const long long r0 = (long long)blockIdx.x * R.chunk;
+  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
+  float sc[8], sh[8];
+  ld8f_any(P.scale + c, sc);
+  ld8f_any(P.shift + c, sh);
+  apply_rows<U>(P, r0, r1, rl, c, sc, sh);
+}
+
 struct BwdArgs {
   Rows rows;
   const float* mean;
@@ -358,31 +421,29 @@ struct BwdArgs {
   int res_accum;
 };
 
-// dz = scale·(g − mean(g) − x̂·mean(g·x̂)); res_grad (=|+=) dA (reference k_bwd_apply, src/bn.cu:240-270).
-template <int U, bool SIMPLE = false>
-__global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
-  const Rows R = P.rows;
-  const int C = R.C, V = C >> 3, RL = R.lanes;
-  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
-  if (rl >= RL) return;
-  const long long r0 = (long long)blockIdx.x * R.chunk;
-  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
-  // dz = scale·g + ka·z + kb with ka = −scale·istd·m2, kb = scale·(istd·m2·mean − m1)
-  float sc[8], sh[8], ka[8], kb[8];
-  {
-    float mu[8], is[8], m1[8], m2[8];
-    ld8f_any(P.scale + c, sc);
-    ld8f_any(P.shift + c, sh);
-    ld8f_any(P.mean + c, mu);
-    ld8f_any(P.istd + c, is);
-    ld8f(P.gmean + c, m1);
-    ld8f(P.gmean + C + c, m2);
+// dz = scale·g + ka·z + kb with ka = −scale·istd·m2, kb = scale·(istd·m2·mean − m1), m1 = Σg/M, m2 = Σg·x̂/M.
+__device__ __forceinline__ void bwd_consts(const BwdArgs& P, int c, const float (&m1)[8], const float (&m2)[8],
+                                           float (&sc)[8], float (&sh)[8], float (&ka)[8], float (&kb)[8]) {
+  float mu[8], is[8];
+  ld8f_any(P.scale + c, sc);
+  ld8f_any(P.shift + c, sh);
+  ld8f_any(P.mean + c, mu);
+  ld8f_any(P.istd + c, is);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      ka[i] = -sc[i] * is[i] * m2[i];
-      kb[i] = sc[i] * (is[i] * m2[i] * mu[i] - m1[i]);
-    }
+  for (int i = 0; i < 8; i++) {
+    ka[i] = -sc[i] * is[i] * m2[i];
+    kb[i] = sc[i] * (is[i] * m2[i] * mu[i] - m1[i]);
   }
+}
+
+// dz = scale·(g − mean(g) − x̂·mean(g·x̂)); res_grad (=|+=) dA, for the thread's rows of [r0, r1) walked
+// from the chunk's end (reference k_bwd_apply, src/bn.cu:240-270).
+template <int U, bool SIMPLE>
+__device__ __forceinline__ void bwd_apply_rows(const BwdArgs& P, long long r0, long long r1, int rl, int c,
+                                               const float (&sc)[8], const float (&sh)[8], const float (&ka)[8],
+                                               const float (&kb)[8]) {
+  const Rows R = P.rows;
+  const int C = R.C, RL = R.lanes;
   for (long long r = r1 - 1 - rl; r >= r0; r -= (long long)U * RL) {
     uint4 zr[U], gr[SIMPLE ? U : 1];
     float dAf[SIMPLE ? 1 : U][8];
@@ -430,6 +491,22 @@ __global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
       st8h(P.dz + off, v);
     }
   }
+}
+
+template <int U, bool SIMPLE = false>
+__global__ void __launch_bounds__(kBnT, 2) k_bn_bwd_apply(const BwdArgs P) {
+  bn_pdl_entry();
+  const Rows R = P.rows;
+  const int C = R.C, V = C >> 3;
+  const int rl = threadIdx.x / V, c = (threadIdx.x - rl * V) * 8;
+  if (rl >= R.lanes) return;
+  const long long r0 = (long long)blockIdx.x * R.chunk;
+  const long long r1 = r0 + R.chunk < R.M ? r0 + R.chunk : R.M;
+  float m1[8], m2[8], sc[8], sh[8], ka[8], kb[8];
+  ld8f(P.gmean + c, m1);
+  ld8f(P.gmean + C + c, m2);
+  bwd_consts(P, c, m1, m2, sc, sh, ka, kb);
+  bwd_apply_rows<U, SIMPLE>(P, r0, r1, rl, c, sc, sh, ka, kb);
 }
 
 // Σ over rows of x for channel counts that are not a multiple of 8 (the 1-channel class head): every
@@ -592,6 +669,22 @@ int check_shape(const void* z, int N, int H, int W, int C) {
   return OSAM_OK;
 }
 
+// Launch with the programmatic-serialization attribute (the kernels call bn_pdl_entry first).
+template <typename... KArgs, typename... Args>
+void pdl_launch(void (*kernel)(KArgs...), int grid, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kBnT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int launched(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -636,7 +729,7 @@ int osam_bn_forward_stats(const void* z, int N, int H, int W, int C, const float
   P.red = Accum{w.acc, w.counter};
   P.st = StatsIO{gamma, beta, momentum, eps, run_mean, run_var, mean, istd, scale, shift};
   const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
-  k_bn_reduce<RED_STATS, kUStats><<<k.nblk, kBnT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  pdl_launch(k_bn_reduce<RED_STATS, kUStats>, k.nblk, smem, reinterpret_cast<cudaStream_t>(stream), P);
   return launched("osam_bn_forward_stats");
 }
 
@@ -664,8 +757,18 @@ int osam_bn_forward_apply(const void* z, int N, int H, int W, int C, const float
       return bad(OSAM_ERR_INVALID, "bn_forward_apply: destination (16-byte aligned, channels multiple of 8)");
     P.dest[i] = DestDev{static_cast<__half*>(d.p), d.ctot, d.choff, d.c0, c1, d.up, 1};
   }
-  k_bn_apply<kUApply><<<k.nblk, kBnT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  pdl_launch(k_bn_apply<kUApply>, k.nblk, 0, reinterpret_cast<cudaStream_t>(stream), P);
   return launched("osam_bn_forward_apply");
+}
+
+int osam_bn_forward_train(const void* z, int N, int H, int W, int C, const float* gamma, const float* beta,
+                          float* run_mean, float* run_var, float momentum, float eps, float* mean, float* istd,
+                          float* scale, float* shift, const void* res, const osam_dest* dests, int n_dest, int act,
+                          void* ws, size_t ws_bytes, osam_stream_t stream) {
+  if (n_dest < 1 || n_dest > OSAM_MAX_DEST || !dests) return bad(OSAM_ERR_INVALID, "bn_forward_train: 1..4 dests");
+  const int rc = osam_bn_forward_stats(z, N, H, W, C, gamma, beta, run_mean, run_var, momentum, eps, mean, istd, scale,
+                                       shift, ws, ws_bytes, stream);
+  return rc ? rc : osam_bn_forward_apply(z, N, H, W, C, scale, shift, res, dests, n_dest, act, stream);
 }
 
 int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mean, const float* istd,
@@ -714,14 +817,14 @@ int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mea
   B.res_accum = res_accum ? 1 : 0;
   const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
   if (simple) {
-    k_bn_reduce<RED_BWD, kUBwdSimple, true><<<k.nblk, kBnT, smem, st>>>(P);
+    pdl_launch(k_bn_reduce<RED_BWD, kUBwdSimple, true>, k.nblk, smem, st, P);
     if ((rc = launched("osam_bn_backward (sums)"))) return rc;
-    k_bn_bwd_apply<kUBwdSimple, true><<<k.nblk, kBnT, 0, st>>>(B);
+    pdl_launch(k_bn_bwd_apply<kUBwdSimple, true>, k.nblk, 0, st, B);
     return launched("osam_bn_backward (apply)");
   }
-  k_bn_reduce<RED_BWD, kUBwd><<<k.nblk, kBnT, smem, st>>>(P);
+  pdl_launch(k_bn_reduce<RED_BWD, kUBwd>, k.nblk, smem, st, P);
   if ((rc = launched("osam_bn_backward (sums)"))) return rc;
-  k_bn_bwd_apply<kUBwdApply><<<k.nblk, kBnT, 0, st>>>(B);
+  pdl_launch(k_bn_bwd_apply<kUBwdApply>, k.nblk, 0, st, B);
   return launched("osam_bn_backward (apply)");
 }
 
@@ -742,7 +845,7 @@ int osam_chan_sum(const void* x, int64_t M, int C, float* out, int accum, void* 
     P.red = Accum{acc, counter};
     P.sum = SumIO{out, accum ? 1 : 0};
     const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
-    k_bn_reduce<RED_SUM, kUStats><<<k.nblk, kBnT, smem, st>>>(P);
+    pdl_launch(k_bn_reduce<RED_SUM, kUStats>, k.nblk, smem, st, P);
   } else {
     const long long n = (long long)M * C;
     long long per = (n + resident_ctas(0) - 1) / resident_ctas(0);

@@ -1121,16 +1121,15 @@ struct osam_model {
         const int P = nd.plan.P, Q = nd.plan.Q, K = nd.K;
         float* T = tarena + nd.t_off;
         rc = osam_conv_fwd(&nd.plan, nd.in->p, w16 + nd.w_off, nd.z, 0.f, ws, ws_bytes, st);
-        if (!rc)
-          rc = osam_bn_forward_stats(nd.z, N, P, Q, K, T, T + K, T + 2 * K, T + 3 * K, momentum, bn_eps, T + 4 * K,
-                                     T + 5 * K, T + 6 * K, T + 7 * K, bnws, bnws_bytes, st);
         osam_dest d[OSAM_MAX_DEST];
         for (size_t i = 0; i < nd.dests.size(); i++)
           d[i] = osam_dest{nd.dests[i].a->p, nd.dests[i].a->C, nd.dests[i].choff, nd.dests[i].c0, nd.dests[i].c1,
                            nd.dests[i].up};
+        // batch statistics and the normalised, activated output in one kernel
         if (!rc)
-          rc = osam_bn_forward_apply(nd.z, N, P, Q, K, T + 6 * K, T + 7 * K, nd.res ? nd.res->p : nullptr, d,
-                                     (int)nd.dests.size(), 1, st);
+          rc = osam_bn_forward_train(nd.z, N, P, Q, K, T, T + K, T + 2 * K, T + 3 * K, momentum, bn_eps, T + 4 * K,
+                                     T + 5 * K, T + 6 * K, T + 7 * K, nd.res ? nd.res->p : nullptr, d,
+                                     (int)nd.dests.size(), 1, bnws, bnws_bytes, st);
       } else if (nd.kind == N_POOL) {
         if (launch_sppf(nd.cat->p, N, nd.cat->H, nd.cat->W, nd.pc, st) != cudaSuccess) rc = OSAM_ERR_CUDA;
       } else {

@@ -71,15 +71,21 @@ def t32(a):
     return torch.from_numpy(np.ascontiguousarray(a)).float().to(DEV)
 
 
-def run_ours(case, d):
+def run_ours(case, d, fused=True):
+    """The node through bn_forward_train (fused = True) or bn_forward_stats + bn_forward_apply, then the
+    backward."""
     N, H, W, C, act, res, dests, accum, res_accum, zm = case
     z = t16(d["z"])
     gamma, beta, rm, rv = t32(d["gamma"]), t32(d["beta"]), t32(d["run_mean"]), t32(d["run_var"])
     mean, istd, scale, shift = (torch.empty(C, device=DEV) for _ in range(4))
-    bn.bn_forward_stats(z, gamma, beta, rm, rv, MOM, EPS, mean, istd, scale, shift)
     outs = [t16(d[f"dest{k}"]) for k in range(len(dests))]
-    bn.bn_forward_apply(z, scale, shift, t16(d["res"]) if res else None,
-                        [DestSpec(o, choff, c0, c1, up) for o, (_, choff, c0, c1, up) in zip(outs, dests)], bool(act))
+    specs = [DestSpec(o, choff, c0, c1, up) for o, (_, choff, c0, c1, up) in zip(outs, dests)]
+    if fused:
+        bn.bn_forward_train(z, gamma, beta, rm, rv, MOM, EPS, mean, istd, scale, shift,
+                            t16(d["res"]) if res else None, specs, bool(act))
+    else:
+        bn.bn_forward_stats(z, gamma, beta, rm, rv, MOM, EPS, mean, istd, scale, shift)
+        bn.bn_forward_apply(z, scale, shift, t16(d["res"]) if res else None, specs, bool(act))
     grads = [t16(d[f"grad{k}"]) for k in range(len(dests))]
     dz = torch.empty_like(z)
     gwg, gwb = t32(d["gw_gamma0"]), t32(d["gw_beta0"])
@@ -119,10 +125,11 @@ def check_dests_untouched(case, d, o):
 
 
 @pytest.mark.parametrize("case", CASES, ids=IDS)
-def test_bn_train_node_matches_oracle(cuda_lib, case):
+@pytest.mark.parametrize("fused", [True, False], ids=["forward_train", "stats+apply"])
+def test_bn_train_node_matches_oracle(cuda_lib, case, fused):
     N, H, W, C, act, res, dests, accum, res_accum, zm = case
     d = make_case(case, 7)
-    o = run_ours(case, d)
+    o = run_ours(case, d, fused)
     st = bn_ref.bn_forward_stats(d["z"], d["gamma"], d["beta"], d["run_mean"], d["run_var"], MOM, EPS)
     for k in ("mean", "istd", "scale", "shift", "run_mean", "run_var"):
         close_stats(o[k], st[k], k)
@@ -198,10 +205,27 @@ def test_bn_workspace_returns_zeroed(cuda_lib):
             first = [o.clone() for o in outs]
         for a, b in zip(first, outs):
             assert torch.equal(a, b)
+    # bn_forward_train and the backward
+    dests = case[6]
+    bufs = [t16(d[f"dest{k}"]) for k in range(len(dests))]
+    specs = [DestSpec(o, choff, c0, c1, up) for o, (_, choff, c0, c1, up) in zip(bufs, dests)]
+    grads = [DestSpec(t16(d[f"grad{k}"]), choff, c0, c1, up) for k, (_, choff, c0, c1, up) in enumerate(dests)]
+    dz = torch.empty_like(z)
+    gg, gb = torch.zeros(C, device=DEV), torch.zeros(C, device=DEV)
+    for _ in range(3):
+        bn.bn_forward_train(z, *args, 0.0, EPS, *outs, t16(d["res"]), specs, True, ws=ws)
+        bn.bn_backward(z, *outs, grads, True, dz, gg, gb, ws=ws)
+        torch.cuda.synchronize()
+        # the fp64 accumulators and the counter (16·C + 16 bytes) are zeroed again; the backward leaves its
+        # per-channel means in the scratch behind them (rewritten before every read)
+        assert int(ws[:16 * C + 16].count_nonzero()) == 0, "accumulators not returned zeroed"
+        for a, b in zip(first, outs):
+            close_stats(b.cpu().numpy(), a.cpu().numpy(), "fused statistics")
 
 
 def test_bn_train_node_in_cuda_graph(cuda_lib):
-    """stats → apply → backward captured once and replayed: same results as eager (no allocation, no host sync)."""
+    """forward_train → backward captured once and replayed: same results as eager (no allocation, no host
+    sync)."""
     case = CASES[2]
     N, H, W, C, act, res, dests, accum, res_accum, zm = case
     d = make_case(case, 5)
@@ -218,10 +242,9 @@ def test_bn_train_node_in_cuda_graph(cuda_lib):
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
-        bn.bn_forward_stats(z, gamma, beta, rm, rv, MOM, EPS, mean, istd, scale, shift, ws=ws, stream=s)
-        bn.bn_forward_apply(z, scale, shift, None,
+        bn.bn_forward_train(z, gamma, beta, rm, rv, MOM, EPS, mean, istd, scale, shift, None,
                             [DestSpec(o, choff, c0, c1, up) for o, (_, choff, c0, c1, up) in zip(outs, dests)],
-                            bool(act), stream=s)
+                            bool(act), ws=ws, stream=s)
         bn.bn_backward(z, mean, istd, scale, shift,
                        [DestSpec(t, choff, c0, c1, up) for t, (_, choff, c0, c1, up) in zip(grads, dests)],
                        bool(act), dz, gwg, gwb, False, ws=ws, stream=s)
