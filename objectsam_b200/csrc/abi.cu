@@ -132,8 +132,10 @@ static int make_map(CUtensorMap* tm, const void* base, int rank, const uint64_t*
 }
 
 // ------------------------------------------------------------------ planning
+// GEMM N tile: the narrowest that covers GEMM N (96 and 192: the input gradients of the C2f output convs,
+// whose GEMM N is 3·c_; a 128 / 224 tile would not divide it and force the scalar epilogue).
 static int choose_bn(int gemm_n) {
-  static const int opts[] = {16, 32, 64, 128, 224, 256};
+  static const int opts[] = {16, 32, 64, 96, 128, 192, 224, 256};
   if (gemm_n <= 256)
     for (int o : opts)
       if (o >= gemm_n) return o;
@@ -587,7 +589,10 @@ static int conv_prepare_launch(const osam_conv_plan* p, const void* x, const voi
 
   // ---- warp-cooperative epilogue: every destination 8-channel aligned, tiles fully inside the GEMM N
   {
-    bool coop = (p->gemm_n % p->BN == 0) && (p->BN % 16 == 0) && e.beta == 0.f;
+    // beta ≠ 0 (an input gradient added to what is there): one plain destination, its old rows read
+    // coalesced through the stage like a residual (not with the TMA-store epilogue)
+    bool coop = (p->gemm_n % p->BN == 0) && (p->BN % 16 == 0) &&
+                (e.beta == 0.f || (e.ndest == 1 && e.dest[0].up == 1 && !e.shuffle));
     for (int i = 0; i < e.ndest; i++) coop = coop && e.dest[i].vec;
     if (e.shuffle) coop = coop && (e.kout % 32 == 0);
     if (e.res) coop = coop && (g.K % 8 == 0);
@@ -599,7 +604,8 @@ static int conv_prepare_launch(const osam_conv_plan* p, const void* x, const voi
   // the window form of the tensor-map kernel (A_W3) is faster than conv_win.cu where both apply (measured:
   // 160² 32 → 32 0.117 vs 0.143 ms, 80² 0.033 vs 0.037 ms at batch 64)
   W3Tile w3t{};
-  bool win = p->win && e.coop && !e.shuffle && !e.par && env_switch("OSAM_FPROP_WIN") != 0 && !choose_w3(p, &w3t);
+  bool win = p->win && e.coop && e.beta == 0.f && !e.shuffle && !e.par && env_switch("OSAM_FPROP_WIN") != 0 &&
+             !choose_w3(p, &w3t);
   for (int i = 0; i < e.ndest && win; i++) win = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
   if (win) {
     L->mode = A_WIN;
@@ -641,7 +647,7 @@ static int conv_prepare_launch(const osam_conv_plan* p, const void* x, const voi
   }
   // ---- TMA-store epilogue: spatial tiles, 32-column passes, destinations on 32-column boundaries
   {
-    bool ts = e.coop && (L->mode == A_WIN || p->mode == A_S1 || p->mode == A_S2) && p->BN % 32 == 0;
+    bool ts = e.coop && e.beta == 0.f && (L->mode == A_WIN || p->mode == A_S1 || p->mode == A_S2) && p->BN % 32 == 0;
     for (int i = 0; i < e.ndest && ts; i++) ts = e.dest[i].c0 % 32 == 0 && e.dest[i].c1 % 32 == 0;
     if (e.shuffle) ts = ts && e.ndest == 1 && e.kout % 32 == 0;
     if (e.par) ts = ts && e.ndest == 1;

@@ -253,6 +253,29 @@ __device__ __forceinline__ void epilogue_warp(const EpiDev& e, int K, int P, int
   } else {
 #pragma unroll
     for (int i = 0; i < W; i++) y[i] = v[i];
+    // beta ≠ 0 (one plain destination): y += beta·(its current values), the rows read coalesced into the
+    // stage and each lane taking its own, the same way as the residual below
+    if (e.beta != 0.f) {
+      const DestDev& ds = e.dest[0];
+      const __half* ob = ds.p + (ds.choff - ds.c0);
+#pragma unroll
+      for (int it = 0; it < CPR; it++) {
+        const int rr = it * RPI + lane / CPR, ch = lane % CPR, k = k0 + ch * 8;
+        const int ro = __shfl_sync(0xffffffffu, my_o, rr);
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (ro >= 0 && k >= ds.c0 && k < ds.c1) val = *reinterpret_cast<const uint4*>(ob + (long long)ro * ds.ctot + k);
+        *reinterpret_cast<uint4*>(stage + stage_off(rr, ch)) = val;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int ch = 0; ch < CPR; ch++) {
+        float o8[8];
+        unpack8h(*reinterpret_cast<const uint4*>(stage + stage_off(lane, ch)), o8);
+#pragma unroll
+        for (int i = 0; i < 8; i++) y[ch * 8 + i] += e.beta * o8[i];
+      }
+      __syncwarp();
+    }
   }
 
   // ---- residual: coalesced rows into the stage, then each lane reads its own row

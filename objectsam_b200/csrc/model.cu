@@ -124,16 +124,18 @@ struct osam_model {
   void* bnws = nullptr;        // zero-filled BN / channel-sum accumulators
   size_t bnws_bytes = 0;
   // backward: weight gradients run on a side stream, overlapping the next node's BN backward and input
-  // gradient on the caller's stream (the reference's wgrad_side, src/model.cpp:416-428); two dz buffers
-  // alternate so a node's BN backward never overwrites the dz a pending weight gradient still reads
-  __half* dz2 = nullptr;
+  // gradient on the caller's stream (the reference's wgrad_side, src/model.cpp:416-428); kDzBufs dz buffers
+  // rotate so a node's BN backward never overwrites the dz a pending weight gradient still reads, and the
+  // caller's stream runs up to kDzBufs − 1 nodes ahead of the side stream
+  static constexpr int kDzBufs = 4;
+  __half* dzx[kDzBufs - 1] = {};  // buffers 1.. (buffer 0 is dz)
   void* ws_side = nullptr;
   // the input-gradient convs' re-laid-out weights, all nodes, refreshed by one batched launch per step
   __half* prelaid = nullptr;
   DgradJob* jobs = nullptr;
   int njobs = 0;
   cudaStream_t side = nullptr;
-  cudaEvent_t ev_dz[2] = {}, ev_wg[2] = {}, ev_fork = nullptr, ev_join = nullptr;
+  cudaEvent_t ev_dz[kDzBufs] = {}, ev_wg[kDzBufs] = {}, ev_fork = nullptr, ev_join = nullptr;
   // forward on several streams: nodes that do not depend on each other (the neck's PAN path, the three
   // head levels and their branches, the proto chain) overlap, so small layers fill the SMs that a big one
   // leaves idle in its last wave.  Stream 0 is the caller's; the schedule is fixed at the first forward.
@@ -532,14 +534,17 @@ struct osam_model {
     cudaFree(wconvt);
     cudaFree(ws);
     cudaFree(bnws);
-    cudaFree(dz2);
+    for (auto& p : dzx) {
+      cudaFree(p);
+      p = nullptr;
+    }
     cudaFree(ws_side);
     cudaFree(prelaid);
     cudaFree(jobs);
     prelaid = nullptr;
     jobs = nullptr;
     njobs = 0;
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kDzBufs; i++) {
       if (ev_dz[i]) cudaEventDestroy(ev_dz[i]);
       if (ev_wg[i]) cudaEventDestroy(ev_wg[i]);
       ev_dz[i] = ev_wg[i] = nullptr;
@@ -565,7 +570,6 @@ struct osam_model {
     ev_fwd_start = nullptr;
     ev_fork = ev_join = nullptr;
     side = nullptr;
-    dz2 = nullptr;
     ws_side = nullptr;
     garena = nullptr;
     zarena = nullptr;
@@ -1025,14 +1029,16 @@ struct osam_model {
         (e = cudaMalloc(&dz, std::max<size_t>(dzn, 1) * sizeof(__half))) != cudaSuccess ||
         (e = cudaMalloc(&gw16, std::max<size_t>(gwn, 1) * sizeof(__half))) != cudaSuccess ||
         (e = cudaMalloc(&ws, wsb)) != cudaSuccess || (e = cudaMalloc(&bnws, bnb)) != cudaSuccess ||
-        (e = cudaMalloc(&dz2, std::max<size_t>(dzn, 1) * sizeof(__half))) != cudaSuccess ||
         (e = cudaMalloc(&ws_side, wsb)) != cudaSuccess)
       return model_fail(OSAM_ERR_NOMEM, "training buffers: %s", cudaGetErrorString(e));
+    for (auto& p : dzx)
+      if ((e = cudaMalloc(&p, std::max<size_t>(dzn, 1) * sizeof(__half))) != cudaSuccess)
+        return model_fail(OSAM_ERR_NOMEM, "dz buffers: %s", cudaGetErrorString(e));
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
     if ((e = cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, lo)) != cudaSuccess)
       return model_fail(OSAM_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kDzBufs; i++) {
       cudaEventCreateWithFlags(&ev_dz[i], cudaEventDisableTiming);
       cudaEventCreateWithFlags(&ev_wg[i], cudaEventDisableTiming);
     }
@@ -1159,7 +1165,7 @@ struct osam_model {
     // the side stream starts after everything issued so far on the caller's stream
     cudaEventRecord(ev_fork, st);
     cudaStreamWaitEvent(side, ev_fork, 0);
-    bool busy[2] = {false, false};
+    bool busy[kDzBufs] = {};
     int buf = 0;
     for (int i = first + count - 1; i >= first; i--) {
       MNode& nd = *nodes[i];
@@ -1167,7 +1173,7 @@ struct osam_model {
       if (nd.kind == N_CONVBN) {
         const int P = nd.plan.P, Q = nd.plan.Q, K = nd.K;
         float* T = tarena + nd.t_off;
-        __half* d = buf ? dz2 : dz;
+        __half* d = buf ? dzx[buf - 1] : dz;
         if (busy[buf]) cudaStreamWaitEvent(st, ev_wg[buf], 0);  // its last weight gradient has read it
         osam_dest gd[OSAM_MAX_DEST];
         for (size_t k = 0; k < nd.dests.size(); k++)
@@ -1187,7 +1193,7 @@ struct osam_model {
         if (!rc && nd.in != in)
           rc = conv_dgrad_ex(&nd.plan, d, w16 + nd.w_off, nd.in->g, nd.dgrad_accum ? 1.f : 0.f, ws, ws_bytes, st,
                              nd.pre_w);
-        buf ^= 1;
+        buf = (buf + 1) % kDzBufs;
       } else if (nd.kind == N_POOL) {
         rc = osam_sppf_bwd(nd.cat->p, nd.cat->g, N, nd.cat->H, nd.cat->W, nd.pc, st);
       } else {

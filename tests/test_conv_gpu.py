@@ -459,6 +459,9 @@ DGRAD_SHAPES = [
     (2, 40, 40, 128, 256, 3, 2),
     (1, 20, 28, 256, 512, 3, 2),
     (1, 80, 80, 64, 128, 3, 2),
+    (2, 20, 20, 192, 128, 1, 1),   # GEMM N 192 and 96 (the C2f output convs' input gradients)
+    (3, 17, 9, 96, 64, 1, 1),
+    (1, 30, 22, 96, 32, 3, 1),
 ]
 
 
@@ -477,12 +480,14 @@ def test_conv_dgrad_matches_torch(cuda_lib, shape):
     assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), s, R // 2))
 
 
-@pytest.mark.parametrize("stride", [1, 2])
-def test_conv_dgrad_beta_accumulates(cuda_lib, stride):
-    """beta = 1 adds the gradient to dx (the reference's dgrad_accum for inputs with several consumers)."""
-    N, H, W, C, K = 2, 24, 24, 64, 64
-    x, w = rand_conv(N, H, W, C, K, 3, seed=17)
-    op = ConvOp().init(ConvGeom(N, H, W, C, K, 3, 3, stride, 1))
+@pytest.mark.parametrize("stride,R,C,K", [(1, 3, 64, 64), (2, 3, 64, 64), (1, 1, 96, 64), (1, 1, 192, 128),
+                                          (1, 3, 128, 256), (2, 3, 32, 64), (1, 1, 64, 32)])
+def test_conv_dgrad_beta_accumulates(cuda_lib, stride, R, C, K):
+    """beta = 1 adds the gradient to dx (the reference's dgrad_accum for inputs with several consumers):
+    the coalesced epilogue reads the old rows through its stage, for 3×3 / 1×1, both strides, GEMM N 96/192."""
+    N, H, W = 2, 24, 24
+    x, w = rand_conv(N, H, W, C, K, R, seed=17)
+    op = ConvOp().init(ConvGeom(N, H, W, C, K, R, R, stride, R // 2))
     P, Q = op.geom().P(), op.geom().Q()
     g = torch.Generator(device="cpu").manual_seed(10)
     dz = (torch.rand(N, P, Q, K, generator=g) - 0.5).half().to(DEV)
@@ -491,7 +496,7 @@ def test_conv_dgrad_beta_accumulates(cuda_lib, stride):
     ws = torch.empty(op.workspace_size(), dtype=torch.uint8, device=DEV)
     op.dgrad(dz, w, dx, ws=ws, beta=1.0)
     torch.cuda.synchronize()
-    assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), stride, 1) + dx0.float())
+    assert_close(dx, ref_dgrad(dz, w, (N, H, W, C), stride, R // 2) + dx0.float())
 
 
 def ref_wgrad(x, dz, w_shape, stride, pad):
