@@ -113,9 +113,12 @@ struct Rows {
   int W, C, lanes;
 };
 // Cross-CTA reduction state: fp64 sums [2C] and an arrival count, zero between calls.
+// `copies` interleaved copies of the sums, [copies][2C] (CTA b adds into copy b % copies), so that fewer
+// CTAs' atomics meet at one address; the finalising CTA adds the copies in a fixed order.
 struct Accum {
   double* acc;
   unsigned* arrivals;
+  int copies;
 };
 // RED_STATS: batch statistics in, the normalisation and the running statistics out.
 struct StatsIO {
@@ -242,6 +245,7 @@ __device__ __forceinline__ void red_flush(const RedArgs& P, float2* bn_red, int 
     for (int i = 0; i < 8; i++) bn_red[rl * C + c + i] = make_float2(a[i], b[i]);
   }
   __syncthreads();
+  double* acc = P.red.acc + (size_t)(blockIdx.x % P.red.copies) * (MODE == RED_SUM ? C : 2 * C);
   for (int ch = threadIdx.x; ch < C; ch += kBnT) {
     float sa = 0.f, sb = 0.f;
     for (int k = 0; k < RL; k++) {
@@ -249,8 +253,8 @@ __device__ __forceinline__ void red_flush(const RedArgs& P, float2* bn_red, int 
       sa += t.x;
       sb += t.y;
     }
-    atomicAdd(&P.red.acc[ch], double(sa));
-    if (MODE != RED_SUM) atomicAdd(&P.red.acc[C + ch], double(sb));
+    atomicAdd(&acc[ch], double(sa));
+    if (MODE != RED_SUM) atomicAdd(&acc[C + ch], double(sb));
   }
 }
 
@@ -311,11 +315,18 @@ __global__ void __launch_bounds__(kBnT, MODE == RED_BWD ? 2 : 3) k_bn_reduce(con
   if (!s_last) return;
   __threadfence();
   const double Md = double(R.M);
+  const int stride = MODE == RED_SUM ? C : 2 * C;
   for (int ch = threadIdx.x; ch < C; ch += kBnT) {
-    const double sx = __ldcg(&P.red.acc[ch]);
-    const double sy = MODE != RED_SUM ? __ldcg(&P.red.acc[C + ch]) : 0.0;
-    P.red.acc[ch] = 0.0;
-    if (MODE != RED_SUM) P.red.acc[C + ch] = 0.0;
+    double sx = 0.0, sy = 0.0;
+    for (int g = 0; g < P.red.copies; g++) {
+      double* acc = P.red.acc + (size_t)g * stride;
+      sx += __ldcg(&acc[ch]);
+      acc[ch] = 0.0;
+      if (MODE != RED_SUM) {
+        sy += __ldcg(&acc[C + ch]);
+        acc[C + ch] = 0.0;
+      }
+    }
     if (MODE == RED_STATS) {
       const StatsIO S = P.st;
       const float K = S.run_mean[ch];
@@ -651,13 +662,15 @@ struct BnWs {
   unsigned* counter;
   float* sums;
 };
-size_t bn_ws_bytes(int C) { return ((size_t(C) * 24 + 16) + 255) / 256 * 256; }
+// BN workspace: kBnCopies × [2C] fp64 sums, the arrival counter (16 bytes), the backward's [2C] fp32 means.
+constexpr int kBnCopies = 8;
+size_t bn_ws_bytes(int C) { return ((size_t(C) * (16 * kBnCopies + 8) + 16) + 255) / 256 * 256; }
 BnWs bn_ws(void* ws, int C) {
   char* p = static_cast<char*>(ws);
   BnWs w;
   w.acc = reinterpret_cast<double*>(p);
-  w.counter = reinterpret_cast<unsigned*>(p + size_t(C) * 16);
-  w.sums = reinterpret_cast<float*>(p + size_t(C) * 16 + 16);
+  w.counter = reinterpret_cast<unsigned*>(p + size_t(C) * 16 * kBnCopies);
+  w.sums = reinterpret_cast<float*>(p + size_t(C) * 16 * kBnCopies + 16);
   return w;
 }
 
@@ -726,7 +739,7 @@ int osam_bn_forward_stats(const void* z, int N, int H, int W, int C, const float
   const BnWs w = bn_ws(ws, C);
   RedArgs P{};
   P.rows = Rows{static_cast<const __half*>(z), M, k.rows, W, C, k.rowlanes};
-  P.red = Accum{w.acc, w.counter};
+  P.red = Accum{w.acc, w.counter, kBnCopies};
   P.st = StatsIO{gamma, beta, momentum, eps, run_mean, run_var, mean, istd, scale, shift};
   const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
   pdl_launch(k_bn_reduce<RED_STATS, kUStats>, k.nblk, smem, reinterpret_cast<cudaStream_t>(stream), P);
@@ -800,7 +813,7 @@ int osam_bn_backward(const void* z, int N, int H, int W, int C, const float* mea
   }
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   P.rows = B.rows = Rows{static_cast<const __half*>(z), M, k.rows, W, C, k.rowlanes};
-  P.red = Accum{w.acc, w.counter};
+  P.red = Accum{w.acc, w.counter, kBnCopies};
   P.bw.nsrc = B.nsrc = n_dest;
   P.bw.silu = B.silu = act ? 1 : 0;
   P.bw.mean = B.mean = mean;
@@ -842,7 +855,7 @@ int osam_chan_sum(const void* x, int64_t M, int C, float* out, int accum, void* 
     const Chunking k = chunking(M, C, 0);
     RedArgs P{};
     P.rows = Rows{static_cast<const __half*>(x), M, k.rows, 1, C, k.rowlanes};
-    P.red = Accum{acc, counter};
+    P.red = Accum{acc, counter, 1};
     P.sum = SumIO{out, accum ? 1 : 0};
     const size_t smem = size_t(k.rowlanes) * C * sizeof(float2);
     pdl_launch(k_bn_reduce<RED_SUM, kUStats>, k.nblk, smem, st, P);

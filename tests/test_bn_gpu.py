@@ -216,9 +216,10 @@ def test_bn_workspace_returns_zeroed(cuda_lib):
         bn.bn_forward_train(z, *args, 0.0, EPS, *outs, t16(d["res"]), specs, True, ws=ws)
         bn.bn_backward(z, *outs, grads, True, dz, gg, gb, ws=ws)
         torch.cuda.synchronize()
-        # the fp64 accumulators and the counter (16·C + 16 bytes) are zeroed again; the backward leaves its
-        # per-channel means in the scratch behind them (rewritten before every read)
-        assert int(ws[:16 * C + 16].count_nonzero()) == 0, "accumulators not returned zeroed"
+        # the fp64 accumulators and the counter are zeroed again; the backward leaves its per-channel means
+        # (2·C fp32) in the scratch at the end of the workspace (rewritten before every read)
+        nz = torch.nonzero(ws).flatten()
+        assert nz.numel() == 0 or int(nz.min()) >= ws.numel() - 8 * C - 256, "accumulators not returned zeroed"
         for a, b in zip(first, outs):
             close_stats(b.cpu().numpy(), a.cpu().numpy(), "fused statistics")
 
