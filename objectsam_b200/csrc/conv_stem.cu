@@ -344,6 +344,9 @@ __global__ void __launch_bounds__(kS2Threads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  // the next conv (launched with programmatic dependent launch; it waits for this grid before it reads)
+  // may be scheduled as soon as this grid's CTAs retire, instead of after the launch gap
+  grid_dep_launch();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- window producer

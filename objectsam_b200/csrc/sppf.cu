@@ -14,6 +14,9 @@ namespace osam {
 constexpr int kSppfCG = 32;  // channels per CTA (4 × 16-byte vectors per pixel)
 
 __global__ void __launch_bounds__(256) k_sppf(__half* __restrict__ cat, int H, int W, int c) {
+  // programmatic dependent launch: wait for the conv that wrote slice 0, let the next conv be scheduled
+  grid_dep_wait();
+  grid_dep_launch();
   extern __shared__ uint4 sppf_smem[];
   const int HW = H * W, V = kSppfCG / 8;  // 16-byte vectors per pixel in the group
   uint4* cur = sppf_smem;                  // [HW][V]
@@ -175,9 +178,17 @@ cudaError_t launch_sppf(__half* cat, int N, int H, int W, int c, cudaStream_t st
   const size_t smem = size_t(2) * H * W * kSppfCG * sizeof(__half);
   cudaError_t e = sppf_prime();
   if (e != cudaSuccess) return e;
-  dim3 grid(c / kSppfCG, N);
-  k_sppf<<<grid, 256, smem, st>>>(cat, H, W, c);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(c / kSppfCG, N);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_sppf, cat, H, W, c);
 }
 
 }  // namespace osam
