@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--no-train", action="store_true", help="skip the training-step leg")
     ap.add_argument("--train-batch", type=int, default=16, help="training leg: images per GPU (BASELINE config 4)")
     ap.add_argument("--bucket-mb", type=float, default=4.0, help="training leg: gradient bucket size")
-    ap.add_argument("--mode", choices=["step", "sweep", "train-passes", "node"], default="step",
+    ap.add_argument("--mode", choices=["step", "sweep", "train-passes", "node", "train-step"], default="step",
                     help="step: the bench line (default); sweep: per-layer fwd/dgrad/wgrad table (config 3); "
                          "train-passes: BN / stem-wgrad / mask-loss passes against the reference's kernels; "
                          "node: one node of the forward repeated (an ncu target)")
@@ -607,6 +607,39 @@ def mode_node(args):
     print(f"repeated nodes {names} {args.repeat} times each")
 
 
+def mode_train_step(args):
+    """One warm-up training step, then one training step (forward(train) + backward, no exchange) at
+    --train-batch × 640² inside the NVTX range "osam_profile": the target of an ncu launch list of the
+    training pass (`ncu --nvtx --nvtx-include osam_profile/ …`).
+
+        python bench.py --mode train-step [--train-batch 16]"""
+    import torch
+    from objectsam_b200.model import Model
+    from oracle import yolo_params
+    B, S = args.train_batch, 640
+    m = Model(B, S)
+    m.load(yolo_params.make_weights(0))
+    m.sync_weights()
+    m.train_init()
+    m.input().copy_(torch.from_numpy(yolo_params.make_images(B, S, 1)).half().cuda())
+    g = torch.Generator(device="cuda").manual_seed(100)
+    for n in [f"out.{k}{l}" for k in ("box", "cls", "coef") for l in range(3)] + ["out.proto"]:
+        t = m.act_grad(n)
+        t.copy_((torch.randn(t.shape, generator=g, device="cuda") * 0.05).half())
+    m.forward_train(0.03)
+    m.backward()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("osam_profile")
+    e0.record()
+    m.forward_train(0.03)
+    m.backward()
+    e1.record()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print(json.dumps({"mode": "train-step", "batch": B, "imgsz": S, "ms": e0.elapsed_time(e1)}))
+
+
 def train_leg(args, rank, world, dev, barrier, all_max):
     """BASELINE config 4's conv path: forward in training mode (batch-statistics BN) + the whole backward
     from fixed seeded head gradients, with the library's data-parallel gradient exchange (osam_dp_*: NCCL
@@ -696,7 +729,8 @@ def main():
     if args.mode != "step":
         import torch
         torch.cuda.set_device(local)
-        {"sweep": mode_sweep, "train-passes": mode_train_passes, "node": mode_node}[args.mode](args)
+        {"sweep": mode_sweep, "train-passes": mode_train_passes, "node": mode_node,
+         "train-step": mode_train_step}[args.mode](args)
         return
     # pin this rank to the CPUs near its GPU before anything allocates pinned host memory (first touch
     # then places the staging buffers in the GPU's NUMA node)
