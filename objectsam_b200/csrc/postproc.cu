@@ -628,9 +628,13 @@ __global__ void __launch_bounds__(128, 4) k_mask(const MaskArgs a) {
           const int c0 = p0 + 32 * w + 16 * h;  // first pixel of this chunk
           uint32_t m16 = 0u;
           if (fast) {  // the 16 pixels lie in image row y, columns [x, x + 16)
-            uint32_t pos = 0u;
+            // the sign bits of the 16 logits, pixel k at bit k, one funnel shift each (pixel 15 first); a
+            // logit counts when its sign bit is clear — logit > 0 except for an exact +0.0, which a sum of
+            // 32 products only reaches with a zero coefficient row (dead rows are masked by `live`)
+            uint32_t neg = 0u;
 #pragma unroll
-            for (int k = 0; k < 16; k++) pos |= (__uint_as_float(r[k]) > 0.f ? 1u : 0u) << k;
+            for (int k = 15; k >= 0; k--) neg = __funnelshift_l(r[k], neg, 1);
+            const uint32_t pos = ~neg & 0xFFFFu;
             const int lo = min(max(xlo - x, 0), 16), hi = min(max(xhi - x, 0), 16);
             const uint32_t cols = hi > lo ? (0xFFFFu >> (16 - hi)) & ~((1u << lo) - 1u) : 0u;
             m16 = (live && y >= ylo && y < yhi && c0 < npix) ? (pos & cols) : 0u;
