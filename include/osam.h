@@ -227,6 +227,32 @@ int osam_mask_loss(const void* const* coef, const int* level_hw, const void* pro
                    void* const* dcoef, float* loss_sum, void* ws, size_t ws_bytes, osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Detection part of the training loss (SegLoss::run before its mask part: src/loss.cuh:53-64,
+ * src/loss.cu:123-390, :590-612; Ultralytics 8.4 v8SegmentationLoss, one class, reg_max 16, top-10 TAL).
+ *   box[l] / cls[l]: NHWC fp16 heads [batch][h_l][w_l][64] / [..][1], level_hw = {h0, w0, h1, w1, h2, w2};
+ *   n_gt[batch], gt_box [batch][max_gt][4] xyxy input pixels, ignore [batch][proto_h·proto_w/32] bits or NULL
+ *   (a negative anchor whose centre lies in it gets no class loss); scale: device float (gradients only).
+ * DFL decode → per gt the 10 in-box anchors (box enlarged to ≥ 16 px) of highest √score·CIoU⁶ (ties: lower
+ * anchor) → per anchor its gt (most overlap when several chose it) → target scores → BCE on every anchor,
+ * CIoU and DFL on the positives, with their gradients.  Writes dbox[l] and dcls[l] for every anchor, zeroes
+ * the dcoef[l] rows of negatives (osam_mask_loss writes the positives'), agt [batch][A] (−1: negative), tsc
+ * [batch][A] target scores, npos[batch] and pos [batch][A] (positives in anchor order), items[16]: [4]
+ * positives, [5] target-score sum, [8] Σ (1 − CIoU)·t, [10] Σ BCE, [11] Σ DFL·t (the reference's layout; [9]
+ * is the mask loss's: pass items + 9 as its loss_sum and items + 4 as its fg).  Workspace
+ * osam_det_loss_workspace_size(batch, A, max_gt) bytes, 256-byte aligned, any contents (the call zeroes the
+ * part it accumulates into). */
+size_t osam_det_loss_workspace_size(int batch, int anchors, int max_gt);
+int osam_det_loss(const void* const* box, const void* const* cls, const int* level_hw, int batch, int imgsz,
+                  int reg_max, const int* n_gt, const float* gt_box, int max_gt, const uint32_t* ignore, int proto_h,
+                  int proto_w, const float* scale, float box_gain, float cls_gain, float dfl_gain, void* const* dbox,
+                  void* const* dcls, void* const* dcoef, int* agt, float* tsc, int* npos, int* pos, float* items,
+                  void* ws, size_t ws_bytes, osam_stream_t stream);
+/* items[0..3] = [box, seg, cls, dfl] from the sums (the reference's k_final): box = items[8]/T·box_gain,
+ * seg = items[9]/fg·box_gain (0 without positives), cls = items[10]/T·cls_gain, dfl = items[11]/T·dfl_gain,
+ * T = max(items[5], 1), fg = items[4]. */
+int osam_seg_loss_items(float* items, float box_gain, float cls_gain, float dfl_gain, osam_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Inference post-process (the reference has it only in numpy: archive/tools/ref_detect.py:37-81).
  * level_hw = {h0, w0, h1, w1, h2, w2} of the three head levels; anchors = Σ h·w, level-major, row-major.
  * ------------------------------------------------------------------------------------------------ */

@@ -89,6 +89,12 @@ _SIGS = {
     "osam_mask_loss": (c_int, [POINTER(c_void_p), POINTER(c_int), c_void_p, c_int, c_int, c_int, c_int, c_int,
                                c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float,
                                c_void_p, POINTER(c_void_p), c_void_p, c_void_p, c_size_t, c_void_p]),
+    "osam_det_loss_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "osam_det_loss": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,
+                              c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_float, c_float, c_float,
+                              POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_void_p, c_void_p,
+                              c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "osam_seg_loss_items": (c_int, [c_void_p, c_float, c_float, c_float, c_void_p]),
     "osam_decode": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,
                             c_void_p, c_void_p]),
     "osam_nms": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_int, c_int, POINTER(c_void_p),

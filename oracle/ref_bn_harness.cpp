@@ -19,6 +19,7 @@
 //   op 4  sppf_pool_bwd: meta = {4, N, H, W, c}; cat, dcat (N, H, W, 4c) → dcat.
 //   op 5  SegLoss::run (src/loss.cu:590-621): meta = {5, B, imgsz, G}; box<l>, cls<l>, coef<l> heads, proto,
 //         n_gt (int32 [B]), gt_box (B, G, 4), gt_mask (int32 [B, G, Hp·Wp/32]), scale (1) → dproto, dcoef<l>,
+//         dbox<l>, dcls<l>, tsc (target scores),
 //         items (16), agt (int32 [B, A]).
 // Timing ops (device time with CUDA events per call, L2 flushed by reading 256 MiB before each call; inputs
 // are seeded pseudo-random fp16 made on the host):
@@ -275,6 +276,12 @@ int main(int argc, char** argv) {
       for (int l = 0; l < 3; l++) out[p + "dcoef" + std::to_string(l)] = down_act(io.dcoef[l], cshape[l]);
       out[p + "items"] = down_f32(L.items(), 16);
       out[p + "agt"] = down_i32(L.assigned_gt(), {B, c.A()});
+      out[p + "tsc"] = down_f32(L.target_score(), int64_t(B) * c.A());  // [B·A]; entries of negatives are stale
+      for (int l = 0; l < 3; l++) {
+        const std::string k = std::to_string(l);
+        out[p + "dbox" + k] = down_act(io.dbox[l], {B, c.lvl_h[l], c.lvl_w[l], 64});
+        out[p + "dcls" + k] = down_act(io.dcls[l], {B, c.lvl_h[l], c.lvl_w[l], 1});
+      }
     } else if (op == 10 || op == 13) {
       static void* flush = nullptr;
       const size_t flush_bytes = size_t(256) << 20;
