@@ -453,7 +453,8 @@ def mode_sweep(args):
 
 def mode_train_passes(args):
     """The training-side passes at BASELINE config 4 (batch 16 per GPU, 640²): BatchNorm statistics / apply /
-    backward for every distinct conv+BN+SiLU output shape, the stem weight gradient and the mask loss, each
+    backward for every distinct conv+BN+SiLU output shape, the stem weight gradient, the mask loss and the
+    whole segment-head loss (detection part + mask part, SegLoss::run), each
     timed alone (a 256 MiB read before every call, so L2 holds none of the inputs) and beside the
     reference's own kernels on the same shapes (oracle/_ref/ref_bn).  Algorithmic bytes: stats 2·M·C, apply
     4·M·C, backward 6·M·C, stem wgrad 2·(N·H·W·3 + N·P·Q·32), mask loss 2·(2·B·Hp·Wp·32) + B·G·Hp·Wp/8.
@@ -557,10 +558,30 @@ def mode_train_passes(args):
     t_ml = timed(lambda: mloss.mask_loss(coef, proto, *margs, fg, one, S, 7.5, dproto, dcoef, lsum))
     mbytes = 2.0 * (B * Hp * Wp * 32 * 2) + B * G * Hp * Wp / 8
     rows.append({"op": "mask_loss", "shape": [B, Hp, Wp, int(npos.sum())], "ms": [t_ml], "gbs": [mbytes / t_ml / 1e6]})
+    # the whole segment-head loss (SegLoss::run): detection part (decode, assignment, CIoU/DFL/BCE) + mask part
+    sg = torch.Generator(device="cpu").manual_seed(2)
+    box_h = [(torch.randn(B, h, w, 64, generator=sg)).half() for h, w in lv]
+    cls_h = [(torch.randn(B, h, w, 1, generator=sg)).half() for h, w in lv]
+    coef_c = [c.cpu() for c in coef]
+    box_d, cls_d = [t.to(dev) for t in box_h], [t.to(dev) for t in cls_h]
+    dbox, dcls = [torch.empty_like(t) for t in box_d], [torch.empty_like(t) for t in cls_d]
+    n_gt_d, gt_box_d, words_d = n_gt.int().to(dev), gt_box.to(dev), words.to(dev)
+    t_sl = timed(lambda: mloss.seg_loss(box_d, cls_d, coef, proto, n_gt_d, gt_box_d, words_d, one, S, dbox, dcls,
+                                        dcoef, dproto))
+    sbytes = mbytes + 2.0 * B * A * (65 + 65 + 32)  # + the box/class heads read and their gradients written
+    rows.append({"op": "seg_loss", "shape": [B, S, G, int(n_gt.sum())], "ms": [t_sl], "gbs": [sbytes / t_sl / 1e6]})
     ref_bin = os.path.join(ROOT, "oracle", "_ref", "ref_bn")
     if os.path.exists(ref_bin):
         cases = [[10, *r["shape"], args.reps] for r in rows if r["op"] == "bn"] + [[13, N, H, W, args.reps]]
         ins = {f"c{i}.meta": np.array(c, np.int32) for i, c in enumerate(cases)}
+        k5 = f"c{len(cases)}."  # the reference's SegLoss::run on the same heads and ground truth, timed
+        ins[k5 + "meta"] = np.array([5, B, S, G, args.reps], np.int32)
+        ins.update({k5 + "n_gt": n_gt.int().numpy(), k5 + "gt_box": gt_box.numpy(), k5 + "gt_mask": words.numpy(),
+                    k5 + "scale": np.ones(1, np.float32), k5 + "proto": proto.float().cpu().numpy()})
+        for l in range(3):
+            ins[f"{k5}box{l}"] = box_h[l].float().numpy()
+            ins[f"{k5}cls{l}"] = cls_h[l].float().numpy()
+            ins[f"{k5}coef{l}"] = coef_c[l].float().numpy()
         with tempfile.TemporaryDirectory() as td:
             fsow.save(os.path.join(td, "in.fsow"), ins)
             subprocess.run([ref_bin, os.path.join(td, "in.fsow"), os.path.join(td, "out.fsow")], check=True,
@@ -568,6 +589,7 @@ def mode_train_passes(args):
             out = fsow.load(os.path.join(td, "out.fsow"))
         for i, r in enumerate(rows[:len(cases)]):
             r["ref_ms"] = [float(v) for v in out[f"c{i}.ms"]]
+        rows[-1]["ref_ms"] = [float(out[k5 + "ms"][0])]
     print(f"HBM peak {peak:.0f} GB/s")
     for r in rows:
         shp = "x".join(map(str, r["shape"]))

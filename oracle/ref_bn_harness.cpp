@@ -19,7 +19,7 @@
 //   op 4  sppf_pool_bwd: meta = {4, N, H, W, c}; cat, dcat (N, H, W, 4c) → dcat.
 //   op 5  SegLoss::run (src/loss.cu:590-621): meta = {5, B, imgsz, G}; box<l>, cls<l>, coef<l> heads, proto,
 //         n_gt (int32 [B]), gt_box (B, G, 4), gt_mask (int32 [B, G, Hp·Wp/32]), scale (1) → dproto, dcoef<l>,
-//         dbox<l>, dcls<l>, tsc (target scores),
+//         dbox<l>, dcls<l>, tsc (target scores),  (meta[4] = iters > 0: also ms, the mean time of run)
 //         items (16), agt (int32 [B, A]).
 // Timing ops (device time with CUDA events per call, L2 flushed by reading 256 MiB before each call; inputs
 // are seeded pseudo-random fp16 made on the host):
@@ -151,6 +151,7 @@ int main(int argc, char** argv) {
     const std::string p = "c" + std::to_string(ci) + ".";
     if (!has(in, p + "meta")) break;
     const int32_t* m = need(in, p + "meta").i32();
+    const int64_t m_len = need(in, p + "meta").numel();
     const int op = m[0];
     if (op == 0) {
       const int N = m[1], H = m[2], W = m[3], C = m[4], act = m[5], has_res = m[6], nd = m[7];
@@ -276,6 +277,16 @@ int main(int argc, char** argv) {
       for (int l = 0; l < 3; l++) out[p + "dcoef" + std::to_string(l)] = down_act(io.dcoef[l], cshape[l]);
       out[p + "items"] = down_f32(L.items(), 16);
       out[p + "agt"] = down_i32(L.assigned_gt(), {B, c.A()});
+      if (m_len > 4 && m[4] > 0) {  // timing: mean device time of SegLoss::run, L2 flushed before each call
+        static void* flush5 = nullptr;
+        const size_t fb = size_t(256) << 20;
+        if (!flush5) {
+          flush5 = DevMem::alloc(fb);
+          CUDA_CHECK(cudaMemset(flush5, 1, fb));
+        }
+        const float ms = time_flushed([&] { L.run(io, gt, scale, st); }, m[4], flush5, fb, st);
+        out[p + "ms"] = HostTensor::make_f32({1}, &ms);
+      }
       out[p + "tsc"] = down_f32(L.target_score(), int64_t(B) * c.A());  // [B·A]; entries of negatives are stale
       for (int l = 0; l < 3; l++) {
         const std::string k = std::to_string(l);
