@@ -144,7 +144,7 @@ int osam_sppf_fwd(void* cat, int N, int H, int W, int c, osam_stream_t stream);
  * maximum of its clipped 5×5 window, row-major, as PyTorch) and ADDS the result to dcat slice 0; slices 1–3
  * of dcat are left as they are.  Needs no workspace (the reference's two fp32 scratch buffers stay on chip).
  * Replaces sppf_pool_bwd (src/misc.cuh:9-10, src/misc.cu:48-73, :155-166).  c % 8 == 0;
- * OSAM_ERR_UNSUPPORTED when H·W > 1937 (the per-CTA shared memory). */
+ * OSAM_ERR_UNSUPPORTED when H·W > 1816 (the per-CTA shared memory). */
 int osam_sppf_bwd(const void* cat, void* dcat, int N, int H, int W, int c, osam_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------

@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(256) k_sppf(__half* __restrict__ cat, int H, i
 // fp32 scratch goes through HBM.
 constexpr int kSppfBwdCG = 8;
 
-size_t sppf_bwd_smem_bytes(int H, int W) { return (size_t)H * W * (3 * 16 + 2 * kSppfBwdCG * 4 + kSppfBwdCG); }
+size_t sppf_bwd_smem_bytes(int H, int W) { return (size_t)H * W * (3 * 16 + 2 * kSppfBwdCG * 4 + 2 * kSppfBwdCG); }
 
 __global__ void __launch_bounds__(256) k_sppf_bwd(const __half* __restrict__ cat, __half* __restrict__ dcat, int H,
                                                   int W, int c) {
@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(256) k_sppf_bwd(const __half* __restrict__ cat
   float* G = reinterpret_cast<float*>(sppfb_smem + 3 * HW);      // [HW][8] gradient of the pool output
   float* Acc = G + HW * kSppfBwdCG;                              // [HW][8] gradient routed to the pool input
   uint8_t* arg = reinterpret_cast<uint8_t*>(Acc + HW * kSppfBwdCG);  // [HW][8] argmax code (dy+2)·5 + (dx+2)
+  uint8_t* rx = arg + HW * kSppfBwdCG;                                   // [HW][8] first column of a row maximum
   const int n = blockIdx.y, g0 = blockIdx.x * kSppfBwdCG;
   const long long ctot = 4LL * c;
   const __half* img = cat + (long long)n * HW * ctot;
@@ -103,20 +104,39 @@ __global__ void __launch_bounds__(256) k_sppf_bwd(const __half* __restrict__ cat
   __syncthreads();
   for (int L = 2; L >= 0; L--) {
     const __half* SL = reinterpret_cast<const __half*>(S + L * HW);
+    // First maximum of each clipped 5×5 window in row-major order, separably: per (row, column) the row
+    // segment's maximum and its first column (strict >), then per output the first row whose segment
+    // maximum is the largest (strict > again) — the same position as the row-major scan.  The row maxima
+    // use Acc, which holds nothing live until this level's gather below.
+    float* rmax = Acc;
     for (int i = threadIdx.x; i < HW * 8; i += blockDim.x) {
       const int o = i >> 3, ch = i & 7, h = o / W, w = o - h * W;
+      const int x0 = w - 2 < 0 ? 0 : w - 2, x1 = w + 2 >= W ? W - 1 : w + 2;
+      float best = -INFINITY;
+      int bx = 255;
+      for (int x = x0; x <= x1; x++) {
+        const float v = __half2float(SL[(h * W + x) * 8 + ch]);
+        if (v > best) {
+          best = v;
+          bx = x;
+        }
+      }
+      rmax[i] = best;
+      rx[i] = (uint8_t)(bx == 255 ? 255 : bx - w + 2);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < HW * 8; i += blockDim.x) {
+      const int o = i >> 3, ch = i & 7, h = o / W, w = o - h * W;
+      const int y0 = h - 2 < 0 ? 0 : h - 2, y1 = h + 2 >= H ? H - 1 : h + 2;
       float best = -INFINITY;
       int a = 255;
-      const int y0 = h - 2 < 0 ? 0 : h - 2, y1 = h + 2 >= H ? H - 1 : h + 2;
-      const int x0 = w - 2 < 0 ? 0 : w - 2, x1 = w + 2 >= W ? W - 1 : w + 2;
-      for (int y = y0; y <= y1; y++)
-        for (int x = x0; x <= x1; x++) {
-          const float v = __half2float(SL[(y * W + x) * 8 + ch]);
-          if (v > best) {
-            best = v;
-            a = (y - h + 2) * 5 + (x - w + 2);
-          }
+      for (int y = y0; y <= y1; y++) {
+        const int j = (y * W + w) * 8 + ch;
+        if (rmax[j] > best) {
+          best = rmax[j];
+          a = (y - h + 2) * 5 + rx[j];
         }
+      }
       arg[i] = (uint8_t)a;
     }
     __syncthreads();

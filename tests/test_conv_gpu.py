@@ -400,7 +400,8 @@ def test_conv_transpose_2x2_dgrad_wgrad(cuda_lib, shape, beta):
     assert_close(dw, wt.grad.permute(0, 2, 3, 1) + beta * dw0.float())
 
 
-SPPF_BWD_SHAPES = [(3, 20, 20, 256, False), (2, 9, 11, 64, False), (2, 20, 20, 64, True), (1, 40, 40, 32, False)]
+SPPF_BWD_SHAPES = [(3, 20, 20, 256, False), (2, 9, 11, 64, False), (2, 20, 20, 64, True), (1, 40, 40, 32, False),
+                   (1, 40, 40, 32, True)]
 
 
 @pytest.mark.parametrize("shape", SPPF_BWD_SHAPES, ids=lambda s: "x".join(map(str, s)))
