@@ -111,6 +111,10 @@ FORM_SHAPES = [
     (4, 20, 20, 32, 64, 3, 1),    # window form: 8 × 4 × 4-image tiles, ragged rows
     (6, 40, 40, 128, 128, 3, 1),
     (5, 12, 20, 64, 128, 3, 1),   # odd batch: the last tile's second image is zero fill
+    (2, 80, 80, 64, 64, 3, 1),    # window form on 16 × 8 tiles (the network's 80² 64 → 64 layers)
+    (1, 34, 20, 32, 32, 3, 1),    # 16 × 8 tiles, ragged rows and columns, BK 32
+    (3, 32, 24, 32, 32, 3, 1),    # 16 × 8 tiles, BK 32, several images
+    (1, 48, 24, 64, 32, 3, 1),    # 16 × 8 tiles, BN 32 over 64 channels
 ]
 
 
