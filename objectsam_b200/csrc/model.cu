@@ -733,18 +733,28 @@ struct osam_model {
       t.push_back(std::move(k));
     }
     if (detect) {
+      // Priorities of the post-process (FLOP-equivalents).  k_nms runs one latency-bound CTA per image for
+      // ≈ 0.2 ms whatever the batch; it needs only the detection heads, so it should start as soon as they
+      // are done and overlap the prototype branch, which only the mask assembly needs.  Weighting it at half
+      // the step's conv FLOPs puts the head → decode → NMS chain ahead of the prototype chain (measured at
+      // batch 64: detect step 4.19–4.21 → 4.08–4.10 ms; with the NMS at its time-equivalent weight, or
+      // weightless, the prototype chain went first and the NMS ran after it).  Decode and mask assembly
+      // count at their time-equivalents at the forward's rate of ≈ 0.67 PFLOP/s (≈ 0.15 µs and ≈ 3 µs per image).
+      double conv_flops = 0.0;
+      for (const Task& k : t) conv_flops += k.cost;
+      const double cd = 1.0e8 * N, cn = 0.5 * conv_flops, cm = 2.0e9 * N;
       t.push_back(Task{T_DECODE, -1, {head[0][0], head[0][1], head[0][2], head[1][0], head[1][1], head[1][2]},
-                       {&det_decoded}, 1.0});
-      t.push_back(Task{T_NMS, -1, {&det_decoded, head[2][0], head[2][1], head[2][2]}, {&det_kept}, 1.0});
-      t.push_back(Task{T_MASK, -1, {&det_kept, proto}, {&det_maskt}, 1.0});
+                       {&det_decoded}, cd});
+      t.push_back(Task{T_NMS, -1, {&det_decoded, head[2][0], head[2][1], head[2][2]}, {&det_kept}, cn});
+      t.push_back(Task{T_MASK, -1, {&det_kept, proto}, {&det_maskt}, cm});
     }
     return t;
   }
 
   // Dependency DAG of a step (a task depends on every earlier writer of a tensor it reads; concat buffers
   // are written by several nodes into disjoint channel slices).  Tasks are launched in a topological order
-  // that puts the longest remaining chain (by FLOPs) first — so the proto branch starts as soon as its
-  // input exists — and assigned greedily to kFwdStreams streams: a task continues the stream whose last
+  // that puts the longest remaining chain (by FLOPs; the post-process by the weights above) first — so the
+  // detection heads and the NMS go ahead of the proto branch, which then overlaps the NMS — and assigned greedily to kFwdStreams streams: a task continues the stream whose last
   // task is its latest producer, else takes the stream idle longest.
   cudaError_t plan(Schedule& sc, bool detect) {
     if (!sc.stream.empty()) return cudaSuccess;
