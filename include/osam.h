@@ -426,6 +426,69 @@ int osam_device_error_peek(void);
  * reference. */
 int osam_selftest_wait_timeout(unsigned long long budget_ns, osam_stream_t stream);
 
+/* ---- training-batch augmentation (reference src/augment.cuh:19 `augment`, kernels src/augment.cu) ----
+ * The loader's batch description, field for field the reference's (src/dataset.h:19-47): its loader fills
+ * these structs on the host and copies them to the device unchanged, so the layouts must agree. */
+typedef struct osam_aug_src {   /* ≙ SrcInfo: one source image */
+  int64_t img_off;              /* byte offset of its RGB u8 pixels (rows of iw·3) in the image block */
+  int iw, ih;                   /* image size */
+  int mw, mh;                   /* instance-mask resolution */
+} osam_aug_src;
+typedef struct osam_aug_inst {  /* ≙ InstInfo: one instance, in source-image coordinates */
+  int src;                      /* osam_aug_src index */
+  int sample;                   /* output image */
+  int tile;                     /* mosaic tile 0..3 */
+  float box[4];                 /* xyxy, source pixels */
+  int mx0, my0, mcw, mch;       /* its mask window (mask pixels): origin and size */
+  int wpr;                      /* u32 words per mask-bitmap row */
+  int64_t mask_off;             /* u32 offset of its bitmap in the mask block */
+  int ignore;                   /* 1 = an ignore region (excluded from the loss), not a target */
+} osam_aug_inst;
+typedef struct osam_aug_sample {  /* ≙ SampleInfo: one output image */
+  int src[4];                     /* source of each tile (−1: none) */
+  int ta[4][4];                   /* tile rectangle on the 2S × 2S canvas: x1, y1, x2, y2 */
+  int tb[4][2];                   /* where the tile starts in its source: x, y */
+  float s, tx, ty;                /* canvas → output: out = s·u + t */
+  float hsv[3];                   /* hue, saturation, value gains */
+  int flip;                       /* mirror left-right */
+  int inst0, ninst;               /* carried, not read (instances are matched by their `sample`) */
+} osam_aug_sample;
+typedef struct osam_aug_header {  /* ≙ BatchHeader */
+  int B, S;
+  int nsrc, ninst;
+  int64_t img_bytes, mask_words;
+} osam_aug_header;
+/* Device pointers of one batch (≙ the device BatchBuf): hdr → smp[B] → src[4B] → inst[...] may be one
+ * block, as the reference lays them out, or separate arrays. */
+typedef struct osam_aug_batch {
+  const osam_aug_header* hdr;  /* reads hdr->ninst */
+  const osam_aug_sample* smp;
+  const osam_aug_src* src;
+  const osam_aug_inst* inst;
+  const uint8_t* img;
+  const uint32_t* mask;
+} osam_aug_batch;
+/* Outputs (≙ AugOut + GtBatch, src/augment.cuh:11-17, src/loss.cuh:25-30). */
+typedef struct osam_aug_out {
+  void* img;          /* fp16 [B][S][S][3] NHWC in 0..1: the model input */
+  int* n_gt;          /* [B] */
+  float* box;         /* [B][G][4] xyxy output pixels */
+  uint32_t* mask;     /* [B][G][Hp·Wp/32] bits, cell r·Wp + c in bit (r·Wp + c) % 32 of word (r·Wp + c) / 32 */
+  uint32_t* ignore;   /* [B][Hp·Wp/32] or NULL */
+  int* gt_inst;       /* [B][G] instance index of each target */
+  int G, Hp, Wp;      /* Wp % 32 == 0 */
+} osam_aug_out;
+
+/* ≙ augment(dev, B, S, out, stream) (src/augment.cuh:19): mosaic canvas (2S × 2S, fill 114) → affine
+ * (scale + translate, bilinear) → HSV gains → left-right flip → fp16 image; targets (boxes clipped to their
+ * tile, mapped, clipped to the image, flipped, kept when w, h > 2 px, area ratio > 0.1 and aspect < 100, in
+ * instance order, at most G per image), their mask bits on the Hp × Wp grid and the ignore bits.  Every
+ * output word is written, so the outputs need no prior zeroing.  A mask cell is S / Wp output pixels wide.
+ * Requires S % 8 == 0, Wp % 32 == 0, G ≥ 1, hdr / src / inst 8-byte and smp 4-byte aligned (in the
+ * reference's one-block layout: an even B) — OSAM_ERR_INVALID otherwise.  Pixel values, boxes and bits
+ * follow the reference kernels' float steps in their order, under the same fast-math arithmetic. */
+int osam_augment(const osam_aug_batch* batch, int B, int S, const osam_aug_out* out, osam_stream_t stream);
+
 /* Human-readable description of the last error returned on this host thread. */
 const char* osam_last_error(void);
 

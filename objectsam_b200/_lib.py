@@ -55,6 +55,17 @@ class OsamError(RuntimeError):
         self.code = code
 
 
+class AugBatch(ctypes.Structure):
+    """osam_aug_batch — device pointers of one training batch (≙ the reference's device BatchBuf)."""
+    _fields_ = [(n, c_void_p) for n in ("hdr", "smp", "src", "inst", "img", "mask")]
+
+
+class AugOut(ctypes.Structure):
+    """osam_aug_out — ≙ AugOut + GtBatch (reference src/augment.cuh:11-17, src/loss.cuh:25-30)."""
+    _fields_ = [("img", c_void_p), ("n_gt", c_void_p), ("box", c_void_p), ("mask", c_void_p), ("ignore", c_void_p),
+                ("gt_inst", c_void_p), ("G", c_int), ("Hp", c_int), ("Wp", c_int)]
+
+
 # symbol → (restype, argtypes); every entry point of include/osam.h
 _SIGS = {
     "osam_conv_plan_create": (c_int, [POINTER(ConvGeom), c_int, POINTER(c_void_p)]),
@@ -95,6 +106,7 @@ _SIGS = {
                               POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "osam_seg_loss_items": (c_int, [c_void_p, c_float, c_float, c_float, c_void_p]),
+    "osam_augment": (c_int, [POINTER(AugBatch), c_int, c_int, POINTER(AugOut), c_void_p]),
     "osam_decode": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int), c_int, c_int, c_int, c_void_p,
                             c_void_p, c_void_p]),
     "osam_nms": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_int, c_int, POINTER(c_void_p),

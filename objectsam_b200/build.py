@@ -25,6 +25,11 @@ NVCC_FLAGS = ARCH + [
     "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC,
 ]
 
+# Files compiled under extra flags.  augment.cu restates the reference's augmentation float steps, which
+# the reference compiles with --use_fast_math (its Release flags): the same flags make the same roundings
+# (division, flush-to-zero), so pixels, boxes and mask bits agree bit for bit.
+FILE_FLAGS = {"augment.cu": ["--use_fast_math"]}
+
 
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
@@ -55,7 +60,7 @@ def _compile(src: str, newest_header: float, verbose: bool) -> str:
     obj = os.path.join(BUILD_DIR, rel + ".o")
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header):
         return obj
-    cmd = [nvcc()] + NVCC_FLAGS + ["-x", "cu", "-c", src, "-o", obj]
+    cmd = [nvcc()] + NVCC_FLAGS + FILE_FLAGS.get(os.path.basename(src), []) + ["-x", "cu", "-c", src, "-o", obj]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -17,6 +17,11 @@
 //   op 3  wgrad_rgb_s2: meta = {3, N, H, W, K}; x (N, H, W, 3), dz (N, P, Q, K) → dw (K, 3, 3, 3) and
 //         ran (1 if the reference took its own kernel, 0 if it declined the shape).
 //   op 4  sppf_pool_bwd: meta = {4, N, H, W, c}; cat, dcat (N, H, W, 4c) → dcat.
+//   op 6  augment (src/augment.cuh:19): meta = {6, B, S, G, Hp, Wp, with_ignore, iters}; blob (u8: the
+//         batch's header, B sample records, 4B source records and its instance records, laid out as
+//         BatchBuf::alloc_dev lays them out), img (u8 source pixels), mask (int32 instance bitmaps) →
+//         img (fp16 values as f32 [B, S, S, 3]), n_gt, box [B, G, 4], gt_inst [B, G], mask (int32
+//         [B, G, Hp·Wp/32]), [ignore (int32 [B, Hp·Wp/32])], (iters > 0: ms, the mean time of augment).
 //   op 5  SegLoss::run (src/loss.cu:590-621): meta = {5, B, imgsz, G}; box<l>, cls<l>, coef<l> heads, proto,
 //         n_gt (int32 [B]), gt_box (B, G, 4), gt_mask (int32 [B, G, Hp·Wp/32]), scale (1) → dproto, dcoef<l>,
 //         dbox<l>, dcls<l>, tsc (target scores),  (meta[4] = iters > 0: also ms, the mean time of run)
@@ -32,8 +37,12 @@
 #include <string>
 #include <vector>
 
+#include <cstddef>
+
+#include "augment.cuh"
 #include "bn.cuh"
 #include "fsow.h"
+#include "osam.h"
 #include "loss.cuh"
 #include "misc.cuh"
 
@@ -137,6 +146,21 @@ HostTensor down_f32(const float* d, int64_t n) {
   CUDA_CHECK(cudaMemcpy(t.data.data(), d, n * sizeof(float), cudaMemcpyDeviceToHost));
   return t;
 }
+
+// The C ABI's batch records must be the reference's, byte for byte (its loader fills them).
+#define SAME_FIELD(A, B, f) static_assert(offsetof(A, f) == offsetof(B, f), #A "." #f)
+static_assert(sizeof(osam_aug_src) == sizeof(SrcInfo), "SrcInfo size");
+SAME_FIELD(osam_aug_src, SrcInfo, img_off); SAME_FIELD(osam_aug_src, SrcInfo, iw); SAME_FIELD(osam_aug_src, SrcInfo, mh);
+static_assert(sizeof(osam_aug_inst) == sizeof(InstInfo), "InstInfo size");
+SAME_FIELD(osam_aug_inst, InstInfo, src); SAME_FIELD(osam_aug_inst, InstInfo, box);
+SAME_FIELD(osam_aug_inst, InstInfo, mx0); SAME_FIELD(osam_aug_inst, InstInfo, wpr);
+SAME_FIELD(osam_aug_inst, InstInfo, mask_off); SAME_FIELD(osam_aug_inst, InstInfo, ignore);
+static_assert(sizeof(osam_aug_sample) == sizeof(SampleInfo), "SampleInfo size");
+SAME_FIELD(osam_aug_sample, SampleInfo, ta); SAME_FIELD(osam_aug_sample, SampleInfo, tb);
+SAME_FIELD(osam_aug_sample, SampleInfo, s); SAME_FIELD(osam_aug_sample, SampleInfo, hsv);
+SAME_FIELD(osam_aug_sample, SampleInfo, flip); SAME_FIELD(osam_aug_sample, SampleInfo, ninst);
+static_assert(sizeof(osam_aug_header) == sizeof(BatchHeader), "BatchHeader size");
+SAME_FIELD(osam_aug_header, BatchHeader, ninst); SAME_FIELD(osam_aug_header, BatchHeader, mask_words);
 
 }  // namespace
 
@@ -292,6 +316,47 @@ int main(int argc, char** argv) {
         const std::string k = std::to_string(l);
         out[p + "dbox" + k] = down_act(io.dbox[l], {B, c.lvl_h[l], c.lvl_w[l], 64});
         out[p + "dcls" + k] = down_act(io.dcls[l], {B, c.lvl_h[l], c.lvl_w[l], 1});
+      }
+    } else if (op == 6) {
+      const int B = m[1], S = m[2], G = m[3], Hp = m[4], Wp = m[5], with_ignore = m[6], iters = m[7];
+      const HostTensor& blob = need(in, p + "blob");
+      const HostTensor& img = need(in, p + "img");
+      const HostTensor& mask = need(in, p + "mask");
+      BatchBuf db;
+      db.hdr = static_cast<BatchHeader*>(DevMem::alloc(blob.numel()));
+      CUDA_CHECK(cudaMemcpy(db.hdr, blob.u8(), blob.numel(), cudaMemcpyHostToDevice));
+      db.smp = reinterpret_cast<SampleInfo*>(db.hdr + 1);
+      db.src = reinterpret_cast<SrcInfo*>(db.smp + B);
+      db.inst = reinterpret_cast<InstInfo*>(db.src + 4 * B);
+      db.img = dalloc<uint8_t>(img.numel());
+      CUDA_CHECK(cudaMemcpy(db.img, img.u8(), img.numel(), cudaMemcpyHostToDevice));
+      db.mask = reinterpret_cast<uint32_t*>(up_i32(mask));
+      const int words = Hp * Wp / 32;
+      AugOut o;
+      o.G = G; o.Hp = Hp; o.Wp = Wp;
+      o.img = dalloc<act_t>(int64_t(B) * S * S * 3);
+      o.gt.n_gt = dalloc<int>(B);
+      o.gt.box = dalloc<float4>(int64_t(B) * G);
+      o.gt.mask = dalloc<uint32_t>(int64_t(B) * G * words);
+      o.gt.ignore = with_ignore ? dalloc<uint32_t>(int64_t(B) * words) : nullptr;
+      o.gt_inst = dalloc<int>(int64_t(B) * G);
+      augment(db, B, S, o, st);
+      CUDA_CHECK(cudaStreamSynchronize(st));
+      out[p + "img"] = down_act(o.img, {B, S, S, 3});
+      out[p + "n_gt"] = down_i32(o.gt.n_gt, {B});
+      out[p + "box"] = down_f32(reinterpret_cast<const float*>(o.gt.box), int64_t(B) * G * 4);
+      out[p + "gt_inst"] = down_i32(o.gt_inst, {B, G});
+      out[p + "mask"] = down_i32(reinterpret_cast<const int32_t*>(o.gt.mask), {B, G, words});
+      if (with_ignore) out[p + "ignore"] = down_i32(reinterpret_cast<const int32_t*>(o.gt.ignore), {B, words});
+      if (iters > 0) {
+        static void* flush6 = nullptr;
+        const size_t fb = size_t(256) << 20;
+        if (!flush6) {
+          flush6 = DevMem::alloc(fb);
+          CUDA_CHECK(cudaMemset(flush6, 1, fb));
+        }
+        const float ms = time_flushed([&] { augment(db, B, S, o, st); }, iters, flush6, fb, st);
+        out[p + "ms"] = HostTensor::make_f32({1}, &ms);
       }
     } else if (op == 10 || op == 13) {
       static void* flush = nullptr;
