@@ -453,11 +453,12 @@ def mode_sweep(args):
 
 def mode_train_passes(args):
     """The training-side passes at BASELINE config 4 (batch 16 per GPU, 640²): BatchNorm statistics / apply /
-    backward for every distinct conv+BN+SiLU output shape, the stem weight gradient, the mask loss and the
-    whole segment-head loss (detection part + mask part, SegLoss::run), each
+    backward for every distinct conv+BN+SiLU output shape, the stem weight gradient, the mask loss, the
+    whole segment-head loss (detection part + mask part, SegLoss::run) and the batch augmentation, each
     timed alone (a 256 MiB read before every call, so L2 holds none of the inputs) and beside the
     reference's own kernels on the same shapes (oracle/_ref/ref_bn).  Algorithmic bytes: stats 2·M·C, apply
-    4·M·C, backward 6·M·C, stem wgrad 2·(N·H·W·3 + N·P·Q·32), mask loss 2·(2·B·Hp·Wp·32) + B·G·Hp·Wp/8.
+    4·M·C, backward 6·M·C, stem wgrad 2·(N·H·W·3 + N·P·Q·32), mask loss 2·(2·B·Hp·Wp·32) + B·G·Hp·Wp/8,
+    augment: source bytes + 2·B·S²·3 + (B·G + B)·Hp·Wp/8.
 
         python bench.py --mode train-passes [--batch 16] [--reps 10] [--json out]"""
     import numpy as np
@@ -570,6 +571,19 @@ def mode_train_passes(args):
                                         dcoef, dproto))
     sbytes = mbytes + 2.0 * B * A * (65 + 65 + 32)  # + the box/class heads read and their gradients written
     rows.append({"op": "seg_loss", "shape": [B, S, G, int(n_gt.sum())], "ms": [t_sl], "gbs": [sbytes / t_sl / 1e6]})
+    # the training-batch augmentation (augment(): mosaic, affine, HSV, flip, targets, mask and ignore bits) on a
+    # seeded synthetic batch of the loader's layout (tests/aug_batch.py), at the trainer's 256 targets per image
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from aug_batch import make_batch
+    from objectsam_b200 import augment as maug
+    GA = 256
+    ab = make_batch(7, B, S, max_inst=12)
+    a_meta, a_img = torch.from_numpy(ab["meta"]).to(dev), torch.from_numpy(ab["img"]).to(dev)
+    a_mask = torch.from_numpy(ab["mask"].view(np.int32)).to(dev)
+    a_out = maug.augment(a_meta, a_img, a_mask, B, S, GA, Hp, Wp)
+    t_au = timed(lambda: maug.augment(a_meta, a_img, a_mask, B, S, GA, Hp, Wp, out=a_out))
+    abytes = ab["img"].size + 2.0 * B * S * S * 3 + B * GA * Hp * Wp / 8 + B * Hp * Wp / 8
+    rows.append({"op": "augment", "shape": [B, S, GA, len(ab["insts"])], "ms": [t_au], "gbs": [abytes / t_au / 1e6]})
     ref_bin = os.path.join(ROOT, "oracle", "_ref", "ref_bn")
     if os.path.exists(ref_bin):
         cases = [[10, *r["shape"], args.reps] for r in rows if r["op"] == "bn"] + [[13, N, H, W, args.reps]]
@@ -582,6 +596,9 @@ def mode_train_passes(args):
             ins[f"{k5}box{l}"] = box_h[l].float().numpy()
             ins[f"{k5}cls{l}"] = cls_h[l].float().numpy()
             ins[f"{k5}coef{l}"] = coef_c[l].float().numpy()
+        k6 = f"c{len(cases) + 1}."  # the reference's augment() on the same batch, timed
+        ins[k6 + "meta"] = np.array([6, B, S, GA, Hp, Wp, 1, args.reps], np.int32)
+        ins.update({k6 + "blob": ab["meta"], k6 + "img": ab["img"], k6 + "mask": ab["mask"].view(np.int32)})
         with tempfile.TemporaryDirectory() as td:
             fsow.save(os.path.join(td, "in.fsow"), ins)
             subprocess.run([ref_bin, os.path.join(td, "in.fsow"), os.path.join(td, "out.fsow")], check=True,
@@ -589,7 +606,8 @@ def mode_train_passes(args):
             out = fsow.load(os.path.join(td, "out.fsow"))
         for i, r in enumerate(rows[:len(cases)]):
             r["ref_ms"] = [float(v) for v in out[f"c{i}.ms"]]
-        rows[-1]["ref_ms"] = [float(out[k5 + "ms"][0])]
+        rows[-2]["ref_ms"] = [float(out[k5 + "ms"][0])]
+        rows[-1]["ref_ms"] = [float(out[k6 + "ms"][0])]
     print(f"HBM peak {peak:.0f} GB/s")
     for r in rows:
         shp = "x".join(map(str, r["shape"]))

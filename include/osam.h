@@ -484,7 +484,7 @@ typedef struct osam_aug_out {
  * tile, mapped, clipped to the image, flipped, kept when w, h > 2 px, area ratio > 0.1 and aspect < 100, in
  * instance order, at most G per image), their mask bits on the Hp × Wp grid and the ignore bits.  Every
  * output word is written, so the outputs need no prior zeroing.  A mask cell is S / Wp output pixels wide.
- * Requires S % 8 == 0, Wp % 32 == 0, G ≥ 1, hdr / src / inst 8-byte and smp 4-byte aligned (in the
+ * Requires S % 8 == 0 (S ≤ 16384), Wp % 32 == 0, G ≥ 1, hdr / src / inst 8-byte and smp 4-byte aligned (in the
  * reference's one-block layout: an even B) — OSAM_ERR_INVALID otherwise.  Pixel values, boxes and bits
  * follow the reference kernels' float steps in their order, under the same fast-math arithmetic. */
 int osam_augment(const osam_aug_batch* batch, int B, int S, const osam_aug_out* out, osam_stream_t stream);

@@ -13,17 +13,19 @@
 // agrees bit for bit (tests/test_augment_gpu.py checks it against the reference's own kernels).
 //
 // Layout of the work (B200: HBM-bound byte work, no tensor cores):
-//   k_aug_image    one thread per 8 consecutive output pixels of a row: the image's sample record and its
-//                  tiles' source records are staged in shared memory once per block; the 8 pixels leave as
-//                  three 16-byte stores (48 B = 8 × 3 fp16);
+//   k_aug_image    one thread per output pixel (the canvas gathers are latency-bound: all the threads the SM
+//                  holds are needed): the image's sample record and its tiles' source records are staged in
+//                  shared memory once per block, and the block's 256 pixels (1536 B of fp16) are staged there
+//                  too and leave as 16-byte stores;
 //   k_aug_targets  one block per image: an ordered compaction of its instances (warp ballots + a block
 //                  scan), writing boxes, instance indices and n_gt; slots past n_gt are zeroed;
-//   k_aug_gtmask   one block per (image, target slot), one thread per 32-cell word: every word of every
+//   k_aug_gtmask   one block per (image, target slot), one lane per cell and one warp per 32-cell word (the
+//                  word is a ballot: no per-thread chain of dependent bitmap loads): every word of every
 //                  slot is written once (zeros outside the target's window and in empty slots), so the
 //                  bitmaps need no separate clearing pass;
-//   k_aug_ignore   one block per image: its ignore instances' windows are gathered into shared memory and
-//                  each thread ORs the bits of the words it owns into a shared bitmap (no atomics), which
-//                  is written out once.
+//   k_aug_ignore   blocks of 64 words per image: each gathers its image's ignore instances and their cell
+//                  windows into shared memory, and each warp ORs the instances' ballots into its 8 words in
+//                  registers (no atomics), written once.
 #include "conv_internal.h"
 
 #include <cuda_fp16.h>
@@ -70,6 +72,50 @@ __device__ __forceinline__ void canvas_rgb(const AugShared& sh, const uint8_t* _
   }
 }
 
+// The four canvas pixels of a bilinear quad (cx, cy) … (cx + 1, cy + 1), as canvas_rgb gives them.  The
+// first present tile whose rectangle touches the quad decides: when it holds all four corners (and the quad
+// is on the canvas) they are read from it together — no earlier tile touches the quad, so it is every
+// corner's first holder; when no tile touches the quad all four are the fill value; otherwise (a tile or
+// canvas edge through the quad) corner by corner.
+__device__ __forceinline__ void canvas_quad(const AugShared& sh, const uint8_t* __restrict__ img, int S, int cx,
+                                            int cy, float p00[3], float p10[3], float p01[3], float p11[3]) {
+  int first = -1;
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    if (sh.sm.src[t] < 0) continue;
+    const int* r = sh.sm.ta[t];
+    if (r[0] <= cx + 1 && r[2] > cx && r[1] <= cy + 1 && r[3] > cy) {
+      first = t;
+      break;
+    }
+  }
+  if (first < 0) {
+#pragma unroll
+    for (int c = 0; c < 3; c++) p00[c] = p10[c] = p01[c] = p11[c] = (float)kFill;
+    return;
+  }
+  const int* r = sh.sm.ta[first];
+  if (cx >= r[0] && cx + 1 < r[2] && cy >= r[1] && cy + 1 < r[3] && cx >= 0 && cy >= 0 && cx + 1 < 2 * S &&
+      cy + 1 < 2 * S) {
+    const osam_aug_src& si = sh.src[first];
+    const uint8_t* q = img + si.img_off + ((int64_t)(cy - r[1] + sh.sm.tb[first][1]) * si.iw +
+                                           (cx - r[0] + sh.sm.tb[first][0])) * 3;
+    const uint8_t* q1 = q + (int64_t)si.iw * 3;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+      p00[c] = q[c];
+      p10[c] = q[3 + c];
+      p01[c] = q1[c];
+      p11[c] = q1[3 + c];
+    }
+    return;
+  }
+  canvas_rgb(sh, img, S, cx, cy, p00);
+  canvas_rgb(sh, img, S, cx + 1, cy, p10);
+  canvas_rgb(sh, img, S, cx, cy + 1, p01);
+  canvas_rgb(sh, img, S, cx + 1, cy + 1, p11);
+}
+
 __device__ __forceinline__ int clamp_u8(float v) { return min(255, max(0, __float2int_rn(v))); }
 
 // u8 RGB → u8 HSV with H in 0..179 (OpenCV's convention): V = max, S = 255·(max − min)/max, H from the
@@ -109,28 +155,30 @@ __device__ __forceinline__ void from_hsv(int h, int s, int v, int& r, int& g, in
   b = clamp_u8(B);
 }
 
+// fmodf(x, 180) for the hue: for 0 ≤ x < 360 it is x or x − 180, and that difference is exact (Sterbenz:
+// 180 ≤ x < 360), so the single subtraction equals the exactly-defined fmod; elsewhere fmodf itself.
+__device__ __forceinline__ float hue_mod180(float x) {
+  if (x >= 0.f && x < 360.f) return x >= 180.f ? x - 180.f : x;
+  return fmodf(x, 180.f);
+}
+
 __global__ void __launch_bounds__(kAugThreads) k_aug_image(const osam_aug_batch bt, int S, __half* __restrict__ out) {
   __shared__ AugShared sh;
+  __shared__ __align__(16) __half stage[kAugThreads * 3];  // the block's pixels, written out as 16-byte rows
   const int i = blockIdx.y;
   stage_sample(sh, bt, i);
-  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // group of 8 pixels
-  if (g >= (int64_t)S * S / 8) return;
-  const int y = (int)(g * 8 / S), x0 = (int)(g * 8 - (int64_t)y * S);
+  const int64_t npix = (int64_t)S * S, p0 = (int64_t)blockIdx.x * kAugThreads;
+  const int64_t pix = p0 + threadIdx.x;
   const osam_aug_sample& sm = sh.sm;
-  __align__(16) __half o[24];
-#pragma unroll 1
-  for (int k = 0; k < 8; k++) {
-    const int x = x0 + k;
+  if (pix < npix) {
+    const int y = (int)pix / S, x = (int)pix - y * S;  // S ≤ 16384: S² fits 31 bits
     const int xs = sm.flip ? S - 1 - x : x;
     // output → canvas: (x, y) = s·(u, v) + t, sampled bilinearly around (u, v)
     const float u = (xs - sm.tx) / sm.s, v = (y - sm.ty) / sm.s;
     const int cx = int(floorf(u)), cy = int(floorf(v));
     const float fx = u - cx, fy = v - cy;
     float p00[3], p10[3], p01[3], p11[3];
-    canvas_rgb(sh, bt.img, S, cx, cy, p00);
-    canvas_rgb(sh, bt.img, S, cx + 1, cy, p10);
-    canvas_rgb(sh, bt.img, S, cx, cy + 1, p01);
-    canvas_rgb(sh, bt.img, S, cx + 1, cy + 1, p11);
+    canvas_quad(sh, bt.img, S, cx, cy, p00, p10, p01, p11);
     int rgb[3];
 #pragma unroll
     for (int c = 0; c < 3; c++)
@@ -138,18 +186,20 @@ __global__ void __launch_bounds__(kAugThreads) k_aug_image(const osam_aug_batch 
     // HSV gains as a lookup of the u8 levels: hue (H·g₀) mod 180, saturation and value clipped to 0..255
     int h, s, vv;
     to_hsv(rgb[0], rgb[1], rgb[2], h, s, vv);
-    h = int(fmodf(h * sm.hsv[0], 180.f));
+    h = int(hue_mod180(h * sm.hsv[0]));
     s = int(fminf(fmaxf(s * sm.hsv[1], 0.f), 255.f));
     vv = int(fminf(fmaxf(vv * sm.hsv[2], 0.f), 255.f));
     from_hsv(h, s, vv, rgb[0], rgb[1], rgb[2]);
 #pragma unroll
-    for (int c = 0; c < 3; c++) o[3 * k + c] = __float2half(rgb[c] / 255.f);
+    for (int c = 0; c < 3; c++) stage[3 * threadIdx.x + c] = __float2half(rgb[c] / 255.f);
   }
-  uint4* dst = reinterpret_cast<uint4*>(out + (((int64_t)i * S + y) * S + x0) * 3);
-  const uint4* src = reinterpret_cast<const uint4*>(o);
-  dst[0] = src[0];
-  dst[1] = src[1];
-  dst[2] = src[2];
+  __syncthreads();
+  // the block's pixels are contiguous in the output: 6 bytes each, 16-byte rows (S² is a multiple of 64,
+  // so every block's byte count is a multiple of 16 and its start is 16-byte aligned)
+  const int nb = (int)((npix - p0 < kAugThreads ? npix - p0 : kAugThreads) * 6 / 16);
+  uint4* dst = reinterpret_cast<uint4*>(out + ((int64_t)i * npix + p0) * 3);
+  const uint4* src = reinterpret_cast<const uint4*>(stage);
+  for (int q = threadIdx.x; q < nb; q += kAugThreads) dst[q] = src[q];
 }
 
 // Exclusive rank of `flag` among the block's threads in thread order, and the block's total.
@@ -239,30 +289,28 @@ __device__ __forceinline__ void box_cells(float x1, float y1, float x2, float y2
   r1 = min(Hp, int(ceilf(y2 / cs)) + 1);
 }
 
-// Bits [c_lo, c_hi) (cells of row r, all within one 32-cell word starting at cell wc) of an instance's
-// mask followed back through flip, affine and tile to its bitmap.
-__device__ __forceinline__ uint32_t cell_bits(const osam_aug_sample& sm, const osam_aug_inst& in, float kx, float ky,
-                                              const uint32_t* __restrict__ mask, int S, float cs, int r, int wc,
-                                              int c_lo, int c_hi) {
+// Mask bit of cell (r, c): the cell centre followed back through flip, affine and tile to the instance's
+// bitmap.
+__device__ __forceinline__ bool cell_bit(const osam_aug_sample& sm, const osam_aug_inst& in, float kx, float ky,
+                                         const uint32_t* __restrict__ mask, int S, float cs, int r, int c) {
   const int t = in.tile;
-  uint32_t bits = 0u;
-  for (int c = c_lo; c < c_hi; c++) {
-    const float x = (c + 0.5f) * cs - 0.5f, y = (r + 0.5f) * cs - 0.5f;  // cell centre, output pixels
-    const float xs = sm.flip ? S - 1 - x : x;
-    const float u = (xs - sm.tx) / sm.s, v = (y - sm.ty) / sm.s;        // canvas
-    if (u < sm.ta[t][0] || u >= sm.ta[t][2] || v < sm.ta[t][1] || v >= sm.ta[t][3]) continue;
-    const float sx = u - sm.ta[t][0] + sm.tb[t][0], sy = v - sm.ta[t][1] + sm.tb[t][1];  // source pixels
-    const int mx = int(floorf((sx + 0.5f) * kx)) - in.mx0, my = int(floorf((sy + 0.5f) * ky)) - in.my0;
-    if (mx < 0 || my < 0 || mx >= in.mcw || my >= in.mch) continue;
-    const uint32_t wd = mask[in.mask_off + (int64_t)my * in.wpr + (mx >> 5)];
-    bits |= ((wd >> (mx & 31)) & 1u) << (c - wc);
-  }
-  return bits;
+  const float x = (c + 0.5f) * cs - 0.5f, y = (r + 0.5f) * cs - 0.5f;  // cell centre, output pixels
+  const float xs = sm.flip ? S - 1 - x : x;
+  const float u = (xs - sm.tx) / sm.s, v = (y - sm.ty) / sm.s;        // canvas
+  if (u < sm.ta[t][0] || u >= sm.ta[t][2] || v < sm.ta[t][1] || v >= sm.ta[t][3]) return false;
+  const float sx = u - sm.ta[t][0] + sm.tb[t][0], sy = v - sm.ta[t][1] + sm.tb[t][1];  // source pixels
+  const int mx = int(floorf((sx + 0.5f) * kx)) - in.mx0, my = int(floorf((sy + 0.5f) * ky)) - in.my0;
+  if (mx < 0 || my < 0 || mx >= in.mcw || my >= in.mch) return false;
+  return (mask[in.mask_off + (int64_t)my * in.wpr + (mx >> 5)] >> (mx & 31)) & 1u;
 }
 
-__global__ void __launch_bounds__(128) k_aug_gtmask(const osam_aug_batch bt, int S, const osam_aug_out o) {
+// One lane per cell, one warp per 32-cell word (a word is 32 cells of one row: Wp % 32 == 0), the word
+// formed by a ballot: no per-thread chain of dependent bitmap loads.
+constexpr int kMaskThreads = 256;
+
+__global__ void __launch_bounds__(kMaskThreads) k_aug_gtmask(const osam_aug_batch bt, int S, const osam_aug_out o) {
   __shared__ AugShared sh;
-  const int i = blockIdx.y, j = blockIdx.x;
+  const int i = blockIdx.y, j = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int words = o.Hp * o.Wp / 32, wpr = o.Wp / 32;
   uint32_t* dst = o.mask + ((int64_t)i * o.G + j) * words;
   const int ng = o.n_gt[i];
@@ -279,37 +327,44 @@ __global__ void __launch_bounds__(128) k_aug_gtmask(const osam_aug_batch bt, int
   int c0, c1, r0, r1;
   box_cells(bx.x, bx.y, bx.z, bx.w, cs, o.Hp, o.Wp, c0, c1, r0, r1);
   const float kx = float(si.mw) / si.iw, ky = float(si.mh) / si.ih;
-  for (int q = threadIdx.x; q < words; q += blockDim.x) {
-    const int r = q / wpr, wc = (q - r * wpr) * 32;
-    uint32_t bits = 0u;
-    if (r >= r0 && r < r1) {
-      const int lo = max(c0, wc), hi = min(c1, wc + 32);
-      if (lo < hi) bits = cell_bits(sm, in, kx, ky, bt.mask, S, cs, r, wc, lo, hi);
-    }
-    dst[q] = bits;
+  const int w0 = c0 >> 5, w1 = (c1 + 31) >> 5, nww = w1 > w0 ? w1 - w0 : 0, nwr = r1 > r0 ? r1 - r0 : 0;
+  // words outside the window: zero, all threads, coalesced
+  for (int q = threadIdx.x; q < words; q += kMaskThreads) {
+    const int r = q / wpr, w = q - r * wpr;
+    if (r < r0 || r >= r1 || w < w0 || w >= w1) dst[q] = 0u;
+  }
+  // the window's words: a warp each
+  for (int k = warp; k < nwr * nww; k += kMaskThreads / 32) {
+    const int r = r0 + k / nww, w = w0 + k % nww, c = w * 32 + lane;
+    const bool in_win = c >= c0 && c < c1;
+    const unsigned bits = __ballot_sync(0xffffffffu, in_win && cell_bit(sm, in, kx, ky, bt.mask, S, cs, r, c));
+    if (lane == 0) dst[r * wpr + w] = bits;
   }
 }
 
-// Shared-memory plan of k_aug_ignore: the bitmap of one image, then per instance of a chunk its record
-// index and cell window.
+// Per image, its ignore instances that reach into their tile, with their cell windows: gathered by each
+// block of k_aug_ignore (a scan over the batch's instances, in order).
 struct IgnWin {
   int k, c0, c1, r0, r1;
 };
+constexpr int kIgnoreWords = 8;  // words per warp of k_aug_ignore (a block covers 8 warps × 8 words)
 
+// Grid (word blocks, B): each warp ORs, word by word, the ballots of every ignore instance of its image.
 __global__ void __launch_bounds__(kAugThreads) k_aug_ignore(const osam_aug_batch bt, int S, const osam_aug_out o) {
-  extern __shared__ uint32_t ign_bits[];  // [Hp·Wp/32]
   __shared__ AugShared sh;
   __shared__ IgnWin win[kAugThreads];
   __shared__ int warp_tot[kAugThreads / 32];
-  const int i = blockIdx.x;
+  const int i = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int words = o.Hp * o.Wp / 32, wpr = o.Wp / 32;
-  for (int q = threadIdx.x; q < words; q += blockDim.x) ign_bits[q] = 0u;
-  stage_sample(sh, bt, i);  // (its barrier also orders the clearing above)
+  const int q0 = (blockIdx.x * (kAugThreads / 32) + warp) * kIgnoreWords;  // this warp's first word
+  stage_sample(sh, bt, i);
   const osam_aug_sample& sm = sh.sm;
   const int ninst = bt.hdr->ninst;
   const float cs = float(S) / o.Wp;
+  uint32_t acc[kIgnoreWords];
+#pragma unroll
+  for (int w = 0; w < kIgnoreWords; w++) acc[w] = 0u;
   for (int k0 = 0; k0 < ninst; k0 += blockDim.x) {
-    // (1) this chunk's ignore instances of image i that reach into their tile, in order, with windows
     const int k = k0 + threadIdx.x;
     bool hit = false;
     IgnWin wv{};
@@ -326,26 +381,28 @@ __global__ void __launch_bounds__(kAugThreads) k_aug_ignore(const osam_aug_batch
     const int slot = block_rank_of(hit, warp_tot, nl);
     if (hit) win[slot] = wv;
     __syncthreads();
-    // (2) each thread ORs the bits of its own words
     for (int l = 0; l < nl; l++) {
       const IgnWin w = win[l];
       const osam_aug_inst in = bt.inst[w.k];
       const osam_aug_src si = bt.src[in.src];
       const float kx = float(si.mw) / si.iw, ky = float(si.mh) / si.ih;
-      for (int q = threadIdx.x; q < words; q += blockDim.x) {
-        const int r = q / wpr, wc = (q - r * wpr) * 32;
-        if (r < w.r0 || r >= w.r1) continue;
-        const int lo = max(w.c0, wc), hi = min(w.c1, wc + 32);
-        if (lo < hi) ign_bits[q] |= cell_bits(sm, in, kx, ky, bt.mask, S, cs, r, wc, lo, hi);
+#pragma unroll
+      for (int u = 0; u < kIgnoreWords; u++) {
+        const int q = q0 + u;
+        if (q >= words) break;
+        const int r = q / wpr, c = (q - r * wpr) * 32 + lane;
+        const bool in_win = r >= w.r0 && r < w.r1 && c >= w.c0 && c < w.c1;
+        if (__ballot_sync(0xffffffffu, in_win))
+          acc[u] |= __ballot_sync(0xffffffffu, in_win && cell_bit(sm, in, kx, ky, bt.mask, S, cs, r, c));
       }
     }
     __syncthreads();
   }
   uint32_t* dst = o.ignore + (int64_t)i * words;
-  for (int q = threadIdx.x; q < words; q += blockDim.x) dst[q] = ign_bits[q];
+#pragma unroll
+  for (int u = 0; u < kIgnoreWords; u++)
+    if (lane == 0 && q0 + u < words) dst[q0 + u] = acc[u];
 }
-
-constexpr size_t kIgnoreSmemMax = 160 * 1024;
 
 }  // namespace
 }  // namespace osam
@@ -354,8 +411,9 @@ using namespace osam;
 
 extern "C" int osam_augment(const osam_aug_batch* batch, int B, int S, const osam_aug_out* out,
                             osam_stream_t stream) {
-  if (!batch || !out || B < 1 || S < 8 || S % 8 || out->G < 1 || out->Hp < 1 || out->Wp < 32 || out->Wp % 32) {
-    set_last_error("osam_augment: invalid arguments (need B ≥ 1, S % 8 == 0, G ≥ 1, Wp % 32 == 0)");
+  if (!batch || !out || B < 1 || S < 8 || S > 16384 || S % 8 || out->G < 1 || out->Hp < 1 || out->Wp < 32 ||
+      out->Wp % 32) {
+    set_last_error("osam_augment: invalid arguments (need B ≥ 1, 8 ≤ S ≤ 16384, S % 8 == 0, G ≥ 1, Wp % 32 == 0)");
     return OSAM_ERR_INVALID;
   }
   if (!batch->hdr || !batch->smp || !batch->src || !batch->inst || !batch->img || !batch->mask || !out->img ||
@@ -374,31 +432,17 @@ extern "C" int osam_augment(const osam_aug_batch* batch, int B, int S, const osa
     set_last_error("osam_augment: header, source and instance records must be 8-byte aligned");
     return OSAM_ERR_INVALID;
   }
-  const size_t ign_smem = (size_t)out->Hp * out->Wp / 8;
-  if (out->ignore && ign_smem > kIgnoreSmemMax) {
-    set_last_error("osam_augment: ignore bitmap of %d x %d cells exceeds shared memory", out->Hp, out->Wp);
-    return OSAM_ERR_UNSUPPORTED;
-  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const osam_aug_batch bt = *batch;
   const osam_aug_out o = *out;
-  const int64_t groups = (int64_t)S * S / 8;
-  k_aug_image<<<dim3((unsigned)((groups + kAugThreads - 1) / kAugThreads), B), kAugThreads, 0, st>>>(
+  const int64_t npix = (int64_t)S * S;
+  k_aug_image<<<dim3((unsigned)((npix + kAugThreads - 1) / kAugThreads), B), kAugThreads, 0, st>>>(
       bt, S, static_cast<__half*>(o.img));
   k_aug_targets<<<B, kAugThreads, 0, st>>>(bt, S, o);
-  k_aug_gtmask<<<dim3(o.G, B), 128, 0, st>>>(bt, S, o);
+  k_aug_gtmask<<<dim3(o.G, B), kMaskThreads, 0, st>>>(bt, S, o);
   if (o.ignore) {
-    static bool attr = false;
-    if (!attr) {
-      const cudaError_t e = cudaFuncSetAttribute(k_aug_ignore, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)kIgnoreSmemMax);
-      if (e != cudaSuccess) {
-        set_last_error("osam_augment: %s", cudaGetErrorString(e));
-        return OSAM_ERR_CUDA;
-      }
-      attr = true;
-    }
-    k_aug_ignore<<<B, kAugThreads, ign_smem, st>>>(bt, S, o);
+    const int words = o.Hp * o.Wp / 32, per_block = (kAugThreads / 32) * kIgnoreWords;
+    k_aug_ignore<<<dim3((words + per_block - 1) / per_block, B), kAugThreads, 0, st>>>(bt, S, o);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

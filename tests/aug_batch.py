@@ -14,7 +14,10 @@ import numpy as np
 from objectsam_b200.augment import INST_DT, SAMPLE_DT, SRC_DT, pack_meta
 
 
-def make_batch(seed: int, B: int, S: int, max_inst: int = 6, p_missing: float = 0.15, p_ignore: float = 0.15):
+def make_batch(seed: int, B: int, S: int, max_inst: int = 6, p_missing: float = 0.15, p_ignore: float = 0.15,
+               overlap: int = 0):
+    """overlap > 0 starts tiles 1 and 3 that many pixels left of the centre, over tiles 0 and 2 (the first
+    tile holding a canvas pixel wins)."""
     r = np.random.default_rng(seed)
     samples = np.zeros(B, SAMPLE_DT)
     sources, insts, imgs, masks = [], [], [], []
@@ -34,13 +37,13 @@ def make_batch(seed: int, B: int, S: int, max_inst: int = 6, p_missing: float = 
                 a = (max(xc - w, 0), max(yc - h, 0), xc, yc)
                 b = (w - (a[2] - a[0]), h - (a[3] - a[1]))
             elif t == 1:
-                a = (xc, max(yc - h, 0), min(xc + w, 2 * S), yc)
+                a = (xc - overlap, max(yc - h, 0), min(xc - overlap + w, 2 * S), yc)
                 b = (0, h - (a[3] - a[1]))
             elif t == 2:
                 a = (max(xc - w, 0), yc, xc, min(2 * S, yc + h))
                 b = (w - (a[2] - a[0]), 0)
             else:
-                a = (xc, yc, min(xc + w, 2 * S), min(2 * S, yc + h))
+                a = (xc - overlap, yc, min(xc - overlap + w, 2 * S), min(2 * S, yc + h))
                 b = (0, 0)
             si = len(sources)
             sm["src"][t] = si

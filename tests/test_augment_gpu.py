@@ -28,11 +28,12 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_BN = os.path.join(ROOT, "oracle", "_ref", "ref_bn")
 need_ref = pytest.mark.skipif(not os.path.exists(REF_BN), reason="oracle/_ref/ref_bn not built (make -C oracle)")
 
-# seed, B (even: the reference's one-block record layout needs it), S, G, Hp, Wp
+# seed, B (even: the reference's one-block record layout needs it), S, G, Hp, Wp, tile overlap (px)
 CASES = {
-    "b4_256_g16": (1, 4, 256, 16, 64, 64),
-    "b2_640_g256_train_grid": (2, 2, 640, 256, 160, 160),
-    "b6_320_g8_cap": (3, 6, 320, 8, 64, 64),
+    "b4_256_g16": (1, 4, 256, 16, 64, 64, 0),
+    "b2_640_g256_train_grid": (2, 2, 640, 256, 160, 160, 0),
+    "b6_320_g8_cap": (3, 6, 320, 8, 64, 64, 0),
+    "b4_256_overlapping_tiles": (4, 4, 256, 16, 64, 64, 37),
 }
 
 
@@ -60,8 +61,8 @@ def run_ours(bt, G, Hp, Wp, ignore=True, out=None):
 @need_ref
 @pytest.mark.parametrize("name", list(CASES))
 def test_augment_matches_reference_kernels(cuda_lib, name):
-    seed, B, S, G, Hp, Wp = CASES[name]
-    bt = make_batch(seed, B, S)
+    seed, B, S, G, Hp, Wp, ov = CASES[name]
+    bt = make_batch(seed, B, S, overlap=ov)
     ref = run_reference(bt, G, Hp, Wp)
     got = run_ours(bt, G, Hp, Wp)
     np.testing.assert_array_equal(got["img"].astype(np.float32), ref["c0.img"])
@@ -81,10 +82,24 @@ def test_augment_matches_reference_kernels(cuda_lib, name):
         assert (n == G).any(), "the case should reach the per-image target cap"
 
 
+@need_ref
+def test_augment_extreme_hsv_gains_match_reference(cuda_lib):
+    """Gains outside the training range: a negative hue gain (negative H), hue products of 360 and more, zero
+    and saturating saturation/value gains."""
+    from objectsam_b200.augment import pack_meta
+    B, S, G, Hp, Wp = 4, 128, 8, 32, 32
+    bt = make_batch(31, B, S)
+    bt["samples"]["hsv"] = [[-0.7, 1.9, 0.2], [2.6, 0.0, 1.9], [7.3, 3.0, 0.0], [1.0, 1.0, 1.0]]
+    bt["meta"] = pack_meta(B, S, bt["samples"], bt["sources"], bt["insts"], bt["img"].size, bt["mask"].size)
+    ref = run_reference(bt, G, Hp, Wp)
+    got = run_ours(bt, G, Hp, Wp)
+    np.testing.assert_array_equal(got["img"].astype(np.float32), ref["c0.img"])
+
+
 def test_augment_writes_every_output_word(cuda_lib):
     """Outputs filled with 0xFF bytes beforehand (and a second call on the same buffers) give the same
     result: nothing depends on prior zeroing."""
-    seed, B, S, G, Hp, Wp = CASES["b4_256_g16"]
+    seed, B, S, G, Hp, Wp, _ = CASES["b4_256_g16"]
     bt = make_batch(seed, B, S)
     first = run_ours(bt, G, Hp, Wp)
     out = {"img": torch.full((B, S, S, 3), float("nan"), dtype=torch.half, device=DEV),
@@ -100,7 +115,7 @@ def test_augment_writes_every_output_word(cuda_lib):
 
 
 def test_augment_without_ignore_output(cuda_lib):
-    seed, B, S, G, Hp, Wp = CASES["b4_256_g16"]
+    seed, B, S, G, Hp, Wp, _ = CASES["b4_256_g16"]
     bt = make_batch(seed, B, S)
     a = run_ours(bt, G, Hp, Wp, ignore=True)
     b = run_ours(bt, G, Hp, Wp, ignore=False)
