@@ -141,15 +141,19 @@ __global__ void __launch_bounds__(256) k_sppf_bwd(const __half* __restrict__ cat
     }
     __syncthreads();
     for (int i = threadIdx.x; i < HW * 8; i += blockDim.x) {
-      const int p = i >> 3, ch = i & 7, h = p / W, w = p - h * W;
-      const int y0 = h - 2 < 0 ? 0 : h - 2, y1 = h + 2 >= H ? H - 1 : h + 2;
-      const int x0 = w - 2 < 0 ? 0 : w - 2, x1 = w + 2 >= W ? W - 1 : w + 2;
+      const int p = i >> 3, h = p / W, w = p - h * W;
+      // the 5 × 5 neighbours o = p + (dy, dx) in row-major order; o sends its gradient here when its argmax
+      // code is that of offset (−dy, −dx): a constant per unrolled step
       float acc = 0.f;
-      for (int y = y0; y <= y1; y++)
-        for (int x = x0; x <= x1; x++) {
-          const int o = y * W + x;
-          if (arg[o * 8 + ch] == (h - y + 2) * 5 + (w - x + 2)) acc += G[o * 8 + ch];
+#pragma unroll
+      for (int dy = -2; dy <= 2; dy++) {
+        const bool row_in = h + dy >= 0 && h + dy < H;
+#pragma unroll
+        for (int dx = -2; dx <= 2; dx++) {
+          const int j = i + (dy * W + dx) * 8;
+          if (row_in && w + dx >= 0 && w + dx < W && arg[j] == (2 - dy) * 5 + (2 - dx)) acc += G[j];
         }
+      }
       Acc[i] = acc;
     }
     __syncthreads();
