@@ -37,6 +37,18 @@ namespace {
 constexpr int kAugThreads = 256;
 constexpr int kFill = 114;  // canvas value outside every tile (the mosaic fill and the affine border)
 
+// Exact small-integer ↔ float conversions on the FP32 / integer pipes instead of the conversion unit, which
+// the image kernel's ~38 conversions per pixel would otherwise queue on.  For |x| < 2²², the float whose bits
+// are 0x4B400000 + x is 1.5·2²³ + x, so subtracting 1.5·2²³ leaves x exactly; and for |v| < 2²², v + 1.5·2²³
+// lies in [2²³, 2²⁴), where the float spacing is 1, so the rounded sum holds v rounded to the nearest integer
+// (ties to even) in its low bits, as __float2int_rn gives.  The explicitly rounded intrinsics keep the
+// compiler from fusing the magic add into a preceding multiply.
+constexpr float kMagic = 12582912.f;  // 1.5·2²³, bits 0x4B400000
+__device__ __forceinline__ float small_i2f(int x) { return __fsub_rn(__int_as_float(0x4B400000 + x), kMagic); }
+__device__ __forceinline__ int small_f2i_rn(float v) {
+  return fabsf(v) < 4194304.f ? __float_as_int(__fadd_rn(v, kMagic)) - 0x4B400000 : __float2int_rn(v);
+}
+
 // The sample record and its tiles' source records, staged per block.
 struct AugShared {
   osam_aug_sample sm;
@@ -65,9 +77,9 @@ __device__ __forceinline__ void canvas_rgb(const AugShared& sh, const uint8_t* _
     if (px < r[0] || px >= r[2] || py < r[1] || py >= r[3]) continue;
     const int xs = px - r[0] + sh.sm.tb[t][0], ys = py - r[1] + sh.sm.tb[t][1];
     const uint8_t* p = img + sh.src[t].img_off + ((int64_t)ys * sh.src[t].iw + xs) * 3;
-    c[0] = p[0];
-    c[1] = p[1];
-    c[2] = p[2];
+    c[0] = small_i2f(p[0]);
+    c[1] = small_i2f(p[1]);
+    c[2] = small_i2f(p[2]);
     return;
   }
 }
@@ -103,10 +115,10 @@ __device__ __forceinline__ void canvas_quad(const AugShared& sh, const uint8_t* 
     const uint8_t* q1 = q + (int64_t)si.iw * 3;
 #pragma unroll
     for (int c = 0; c < 3; c++) {
-      p00[c] = q[c];
-      p10[c] = q[3 + c];
-      p01[c] = q1[c];
-      p11[c] = q1[3 + c];
+      p00[c] = small_i2f(q[c]);
+      p10[c] = small_i2f(q[3 + c]);
+      p01[c] = small_i2f(q1[c]);
+      p11[c] = small_i2f(q1[3 + c]);
     }
     return;
   }
@@ -116,31 +128,32 @@ __device__ __forceinline__ void canvas_quad(const AugShared& sh, const uint8_t* 
   canvas_rgb(sh, img, S, cx + 1, cy + 1, p11);
 }
 
-__device__ __forceinline__ int clamp_u8(float v) { return min(255, max(0, __float2int_rn(v))); }
+__device__ __forceinline__ int clamp_u8(float v) { return min(255, max(0, small_f2i_rn(v))); }
 
 // u8 RGB → u8 HSV with H in 0..179 (OpenCV's convention): V = max, S = 255·(max − min)/max, H from the
 // sector of the largest channel, halved.
 __device__ __forceinline__ void to_hsv(int r, int g, int b, int& h, int& s, int& v) {
   const int hi = max(r, max(g, b)), lo = min(r, min(g, b)), span = hi - lo;
   v = hi;
-  s = hi ? __float2int_rn(255.f * span / hi) : 0;
+  const float fspan = small_i2f(span);
+  s = hi ? small_f2i_rn(255.f * fspan / small_i2f(hi)) : 0;
   float deg = 0.f;
   if (span) {
     if (hi == r)
-      deg = 60.f * (g - b) / span;
+      deg = 60.f * small_i2f(g - b) / fspan;
     else if (hi == g)
-      deg = 120.f + 60.f * (b - r) / span;
+      deg = 120.f + 60.f * small_i2f(b - r) / fspan;
     else
-      deg = 240.f + 60.f * (r - g) / span;
+      deg = 240.f + 60.f * small_i2f(r - g) / fspan;
     if (deg < 0) deg += 360.f;
   }
-  h = __float2int_rn(deg * 0.5f);
+  h = small_f2i_rn(deg * 0.5f);
   if (h >= 180) h -= 180;
 }
 
 // u8 HSV (H 0..179) → u8 RGB: sector i = ⌊H/60°⌋, fraction f, and the three intermediate levels.
 __device__ __forceinline__ void from_hsv(int h, int s, int v, int& r, int& g, int& b) {
-  const float hs = h * 2.f / 60.f, sat = s / 255.f, val = float(v);
+  const float hs = small_i2f(h) * 2.f / 60.f, sat = small_i2f(s) / 255.f, val = small_i2f(v);
   const int sector = int(floorf(hs)) % 6;
   const float f = hs - floorf(hs);
   const float p = val * (1 - sat), q = val * (1 - sat * f), t = val * (1 - sat * (1 - f));
@@ -186,12 +199,12 @@ __global__ void __launch_bounds__(kAugThreads) k_aug_image(const osam_aug_batch 
     // HSV gains as a lookup of the u8 levels: hue (H·g₀) mod 180, saturation and value clipped to 0..255
     int h, s, vv;
     to_hsv(rgb[0], rgb[1], rgb[2], h, s, vv);
-    h = int(hue_mod180(h * sm.hsv[0]));
-    s = int(fminf(fmaxf(s * sm.hsv[1], 0.f), 255.f));
-    vv = int(fminf(fmaxf(vv * sm.hsv[2], 0.f), 255.f));
+    h = int(hue_mod180(small_i2f(h) * sm.hsv[0]));
+    s = int(fminf(fmaxf(small_i2f(s) * sm.hsv[1], 0.f), 255.f));
+    vv = int(fminf(fmaxf(small_i2f(vv) * sm.hsv[2], 0.f), 255.f));
     from_hsv(h, s, vv, rgb[0], rgb[1], rgb[2]);
 #pragma unroll
-    for (int c = 0; c < 3; c++) stage[3 * threadIdx.x + c] = __float2half(rgb[c] / 255.f);
+    for (int c = 0; c < 3; c++) stage[3 * threadIdx.x + c] = __float2half(small_i2f(rgb[c]) / 255.f);
   }
   __syncthreads();
   // the block's pixels are contiguous in the output: 6 bytes each, 16-byte rows (S² is a multiple of 64,
