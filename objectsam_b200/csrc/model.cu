@@ -754,8 +754,9 @@ struct osam_model {
   // Dependency DAG of a step (a task depends on every earlier writer of a tensor it reads; concat buffers
   // are written by several nodes into disjoint channel slices).  Tasks are launched in a topological order
   // that puts the longest remaining chain (by FLOPs; the post-process by the weights above) first — so the
-  // detection heads and the NMS go ahead of the proto branch, which then overlaps the NMS — and assigned greedily to kFwdStreams streams: a task continues the stream whose last
-  // task is its latest producer, else takes the stream idle longest.
+  // detection heads and the NMS go ahead of the proto branch, which then overlaps the NMS — and assigned
+  // greedily to kFwdStreams streams: a task continues the stream whose last task is its latest producer,
+  // else takes the stream idle longest.
   cudaError_t plan(Schedule& sc, bool detect) {
     if (!sc.stream.empty()) return cudaSuccess;
     sc.tasks = step_tasks(detect);
