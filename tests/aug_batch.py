@@ -91,11 +91,10 @@ def make_batch(seed: int, B: int, S: int, max_inst: int = 6, p_missing: float = 
         sm["ty"] = S / 2 - s * S + r.uniform(-0.1, 0.1) * S
         sm["hsv"] = 1.0 + r.uniform(-1, 1, 3) * np.array([0.015, 0.7, 0.4])
         sm["flip"] = int(r.random() < 0.5)
-    # the loader lists instances sample by sample; shuffle a little across samples to exercise the filter
+    # the loader lists instances sample by sample; shuffle within runs of three to exercise the filter
     insts = np.array(insts, INST_DT) if insts else np.zeros(0, INST_DT)
     if len(insts) > 1:
-        perm = np.argsort(r.random(len(insts)) + np.repeat(np.arange(len(insts)) // 3, 1))
-        insts = insts[perm]
+        insts = insts[np.argsort(r.random(len(insts)) + np.arange(len(insts)) // 3)]
     img = np.concatenate(imgs) if imgs else np.zeros(16, np.uint8)
     mask = np.concatenate(masks) if masks else np.zeros(4, np.uint32)
     srcs = np.array(sources, SRC_DT)
