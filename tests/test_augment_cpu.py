@@ -15,7 +15,7 @@ import pytest
 
 from aug_batch import make_batch
 from objectsam_b200 import _lib
-from objectsam_b200.augment import INST_DT, SAMPLE_DT, SRC_DT, pack_meta
+from objectsam_b200.augment import HEADER_DT, INST_DT, SAMPLE_DT, SRC_DT, pack_meta
 from oracle import augment_ref as R
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -143,3 +143,34 @@ def test_pack_meta_layout():
     assert SAMPLE_DT.itemsize == 148 and SRC_DT.itemsize == 24 and INST_DT.itemsize == 64
     with pytest.raises(AssertionError):
         pack_meta(3, 64, bt["samples"], bt["sources"], bt["insts"], 0, 0)
+
+
+def test_record_dtypes_match_the_c_header(tmp_path):
+    """The numpy record layouts of objectsam_b200.augment against include/osam.h itself: a C program built
+    with gcc prints every field's offset and each record's size (the reference harness asserts the header
+    against the reference's own structs at compile time)."""
+    import shutil
+    import subprocess
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    fields = {"osam_aug_src": SRC_DT, "osam_aug_inst": INST_DT, "osam_aug_sample": SAMPLE_DT,
+              "osam_aug_header": HEADER_DT}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "osam.h"', "int main(void) {"]
+    for st, dt in fields.items():
+        lines.append(f'  printf("{st} size %zu\\n", sizeof({st}));')
+        for name in dt.names:
+            lines.append(f'  printf("{st} {name} %zu\\n", offsetof({st}, {name}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(HERE), "include")
+    subprocess.run(["gcc", "-std=c11", "-I", inc, str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        st, name, v = line.split()
+        got[(st, name)] = int(v)
+    for st, dt in fields.items():
+        assert got[(st, "size")] == dt.itemsize, st
+        for name in dt.names:
+            assert got[(st, name)] == dt.fields[name][1], (st, name)
